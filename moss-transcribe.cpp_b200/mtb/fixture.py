@@ -1,0 +1,197 @@
+"""Seeded random-init GGUF fixtures and synthetic prompts.
+
+The real MOSS checkpoint, its audio and the reference's golden GGUFs are not
+available, so every parity case and benchmark runs on a random-init model of
+the Qwen3 decoder shape that the reference loads (src/qwen3_decoder.cpp:20-85,
+src/model_loader.cpp:116-128).  Tensor names, layouts and quantisation follow
+the reference converter (scripts/convert_moss_transcribe_to_gguf.py:46-53,
+:340-365): q8_0 for token_embd and the seven projection matrices of every
+layer, F32 for norms, the q8_0 bytes produced by the same `gguf.quantize`
+call the converter makes.
+
+Prompts follow the verify-microbench / config-1 recipe: N(0,1) audio rows
+(one 30 s chunk = 375 rows) between two halves of LCG text ids.  The LCG is
+the one the reference's speculative gate uses for its prefixes
+(cpu-lab/moss_speculative_gate.cpp:165-166).
+"""
+from __future__ import annotations
+
+import os
+from dataclasses import dataclass, asdict
+
+import numpy as np
+
+GGML_F32 = 0
+GGML_F16 = 1
+GGML_Q8_0 = 8
+
+
+@dataclass(frozen=True)
+class DecoderShape:
+    hidden: int
+    n_layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    eos_token_id: int = 151645
+    audio_token_id: int = 151671
+
+
+# Qwen3-0.6B, the decoder of MOSS-Transcribe (src/model_loader.cpp:118-128).
+QWEN3_0_6B = DecoderShape(hidden=1024, n_layers=28, n_heads=16, n_kv_heads=8, head_dim=128,
+                          ffn=3072, vocab=151936)
+# A small model of the same structure for fast parity cases.
+TINY = DecoderShape(hidden=256, n_layers=2, n_heads=4, n_kv_heads=2, head_dim=128, ffn=512,
+                    vocab=2048, eos_token_id=2047, audio_token_id=2046)
+
+
+def tensor_specs(shape: DecoderShape):
+    """(name, numpy shape, kind) in a fixed order; kind is 'q' (linear) or 'n' (norm)."""
+    H, hd = shape.hidden, shape.head_dim
+    specs = [("token_embd.weight", (shape.vocab, H), "q")]
+    for i in range(shape.n_layers):
+        b = f"qwen3.blk.{i}."
+        specs += [
+            (b + "attn_norm.weight", (H,), "n"),
+            (b + "attn_q.weight", (shape.n_heads * hd, H), "q"),
+            (b + "attn_k.weight", (shape.n_kv_heads * hd, H), "q"),
+            (b + "attn_v.weight", (shape.n_kv_heads * hd, H), "q"),
+            (b + "attn_q_norm.weight", (hd,), "n"),
+            (b + "attn_k_norm.weight", (hd,), "n"),
+            (b + "attn_o.weight", (H, shape.n_heads * hd), "q"),
+            (b + "ffn_norm.weight", (H,), "n"),
+            (b + "ffn_gate.weight", (shape.ffn, H), "q"),
+            (b + "ffn_up.weight", (shape.ffn, H), "q"),
+            (b + "ffn_down.weight", (H, shape.ffn), "q"),
+        ]
+    specs.append(("qwen3.output_norm.weight", (H,), "n"))
+    return specs
+
+
+def _quantize_q8_0(arr: np.ndarray) -> np.ndarray:
+    import gguf
+    rows = arr.shape[0]
+    out = np.empty((rows, arr.shape[1] // 32 * 34), dtype=np.uint8)
+    step = max(1, (1 << 22) // arr.shape[1])
+    for r in range(0, rows, step):
+        out[r:r + step] = gguf.quantize(arr[r:r + step], gguf.GGMLQuantizationType.Q8_0)
+    return out
+
+
+def write_fixture(path: str, shape: DecoderShape = QWEN3_0_6B, seed: int = 0,
+                  weight_std: float = 0.02, norm_std: float = 0.05, dtype: str = "q8_0",
+                  embd_std: float | None = None) -> str:
+    """Write a random-init decoder GGUF: N(0, weight_std) linear weights from
+    `seed` (token_embd uses embd_std when given), norms 1 + N(0, norm_std) in
+    F32.  Returns `path`.
+
+    The benchmark fixture is the configured N(0, 0.02) model.  Its greedy
+    output settles on one repeated token, which accepts every draft, so parity
+    cases also use PARITY_SCALES (weights 0.06, embeddings 0.2): a model whose
+    greedy stream mixes repeats with new tokens and so exercises rejection,
+    rewind and acceptance alike."""
+    import gguf
+    rng = np.random.default_rng(seed)
+    w = gguf.GGUFWriter(path, "moss_transcribe")
+    w.add_uint32("mtd.text.vocab_size", shape.vocab)
+    w.add_uint32("mtd.text.hidden", shape.hidden)
+    w.add_uint32("mtd.text.ffn", shape.ffn)
+    w.add_uint32("mtd.text.n_layers", shape.n_layers)
+    w.add_uint32("mtd.text.n_heads", shape.n_heads)
+    w.add_uint32("mtd.text.n_kv_heads", shape.n_kv_heads)
+    w.add_uint32("mtd.text.head_dim", shape.head_dim)
+    w.add_float32("mtd.text.rms_eps", shape.rms_eps)
+    w.add_float32("mtd.text.rope_theta", shape.rope_theta)
+    w.add_bool("mtd.text.tied", True)
+    w.add_uint32("mtd.eos_token_id", shape.eos_token_id)
+    w.add_uint32("mtd.audio_token_id", shape.audio_token_id)
+    w.add_uint32("mtd.default_max_new_tokens", 5120)
+    for name, shp, kind in tensor_specs(shape):
+        if kind == "n":
+            arr = (1.0 + norm_std * rng.standard_normal(shp, dtype=np.float32)).astype(np.float32)
+            w.add_tensor(name, arr)
+            continue
+        arr = rng.standard_normal(shp, dtype=np.float32)
+        std = embd_std if (embd_std is not None and name == "token_embd.weight") else weight_std
+        arr *= np.float32(std)
+        if dtype == "q8_0":
+            raw = _quantize_q8_0(arr)
+            w.add_tensor(name, raw, raw_shape=raw.shape, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        elif dtype == "f16":
+            w.add_tensor(name, arr.astype(np.float16))
+        else:
+            raise ValueError(f"unsupported fixture dtype {dtype}")
+        del arr
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return path
+
+
+PARITY_SCALES = {"weight_std": 0.06, "embd_std": 0.2}
+
+
+def cached_fixture(shape: DecoderShape = QWEN3_0_6B, seed: int = 0, directory: str | None = None,
+                   parity: bool = False) -> str:
+    """Path of the fixture for (shape, seed[, parity scales]), writing it on first use."""
+    directory = directory or os.environ.get("MTB_FIXTURE_DIR", "/tmp/mtb_fixtures")
+    os.makedirs(directory, exist_ok=True)
+    tag = "qwen3_0_6b" if shape == QWEN3_0_6B else "tiny" if shape == TINY else \
+        "x".join(str(v) for v in asdict(shape).values())
+    path = os.path.join(directory, f"{tag}_seed{seed}{'_parity' if parity else ''}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_fixture(tmp, shape, seed, **(PARITY_SCALES if parity else {}))
+        os.replace(tmp, path)
+    return path
+
+
+def lcg_ids(n: int, vocab: int, seed: int = 0x12345678) -> np.ndarray:
+    """Prefix ids of cpu-lab/moss_speculative_gate.cpp:165-166."""
+    out = np.empty(n, dtype=np.int32)
+    s = seed & 0xFFFFFFFF
+    for i in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        out[i] = s % vocab
+    return out
+
+
+def dequant_q8_0_rows(raw: np.ndarray, ids: np.ndarray, hidden: int) -> np.ndarray:
+    """q8_0 rows -> f32 (d * q), the embedding lookup of src/generate.cpp:33-66."""
+    nb = hidden // 32
+    rows = raw.reshape(-1, nb, 34)[ids]
+    d = rows[:, :, :2].copy().view(np.float16).astype(np.float32)
+    q = rows[:, :, 2:].view(np.int8).astype(np.float32)
+    return (q * d).reshape(len(ids), hidden)
+
+
+def synthetic_prompt(token_embd_raw: np.ndarray, shape: DecoderShape, n_audio: int = 375,
+                     n_text: int = 32, seed: int = 1) -> np.ndarray:
+    """Fused prompt rows [n_text + n_audio, hidden]: text[0:n/2] + audio + text[n/2:]."""
+    rng = np.random.default_rng(seed)
+    audio = rng.standard_normal((n_audio, shape.hidden), dtype=np.float32)
+    ids = lcg_ids(n_text, shape.vocab)
+    text = dequant_q8_0_rows(token_embd_raw, ids, shape.hidden)
+    half = n_text // 2
+    return np.ascontiguousarray(np.concatenate([text[:half], audio, text[half:]], axis=0))
+
+
+def read_shape(reader) -> DecoderShape:
+    """DecoderShape from a GGUFReader's mtd.* metadata (src/model_loader.cpp:116-128)."""
+    def get(key, default):
+        f = reader.fields.get(key)
+        if f is None:
+            return default
+        return f.parts[f.data[0]][0].item()
+    return DecoderShape(hidden=int(get("mtd.text.hidden", 1024)), n_layers=int(get("mtd.text.n_layers", 28)),
+                        n_heads=int(get("mtd.text.n_heads", 16)), n_kv_heads=int(get("mtd.text.n_kv_heads", 8)),
+                        head_dim=int(get("mtd.text.head_dim", 128)), ffn=int(get("mtd.text.ffn", 3072)),
+                        vocab=int(get("mtd.text.vocab_size", 151936)),
+                        rms_eps=float(get("mtd.text.rms_eps", 1e-6)), rope_theta=float(get("mtd.text.rope_theta", 1e6)),
+                        eos_token_id=int(get("mtd.eos_token_id", 151645)),
+                        audio_token_id=int(get("mtd.audio_token_id", 151671)))

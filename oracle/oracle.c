@@ -1,0 +1,598 @@
+/*
+ * CPU oracle for the strict speculative decode path.  TEST INFRASTRUCTURE
+ * ONLY: see oracle.h for what is restated from where, and for the parity
+ * status of each part.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef struct __attribute__((packed)) {
+    uint16_t d;
+    int8_t qs[32];
+} blk_q8;
+
+_Static_assert(sizeof(blk_q8) == 34, "q8_0 block is 34 bytes");
+
+static inline float h2f(uint16_t h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float)v;
+}
+static inline uint16_t f2h(float f) {
+    _Float16 v = (_Float16)f; /* IEEE round to nearest even */
+    uint16_t h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+static inline float round_f16(float f) { return h2f(f2h(f)); }
+
+void orc_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+/* ------------------------------------------------------------------ q8_0 */
+
+/* ggml x86 SIMD from_float for Q8_0 (the activation conversion that ggml's CPU
+ * mul_mat applies to src1 before every q8_0 dot, called by the reference at
+ * src/cpu_projection.cpp:25 and src/cpu_activation.cpp:30). */
+void orc_quantize_act_q8(const float* x, int64_t k, void* out_blocks) {
+    blk_q8* y = (blk_q8*)out_blocks;
+    for (int64_t i = 0; i < k / 32; ++i) {
+        const float* v = x + i * 32;
+        float amax = 0.0f;
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        const float d = amax / 127.f;
+        y[i].d = f2h(d);
+        const float id = (amax != 0.0f) ? 127.f / amax : 0.0f;
+        for (int j = 0; j < 32; ++j) y[i].qs[j] = (int8_t)nearbyintf(v[j] * id);
+    }
+}
+
+/* quantize_row_q8_0_ref: the weight quantiser (gguf.quantize in the
+ * reference converter, scripts/convert_moss_transcribe_to_gguf.py:360). */
+void orc_quantize_ref_q8(const float* x, int64_t k, void* out_blocks) {
+    blk_q8* y = (blk_q8*)out_blocks;
+    for (int64_t i = 0; i < k / 32; ++i) {
+        const float* v = x + i * 32;
+        float amax = 0.0f;
+        for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
+        const float d = amax / 127.f;
+        const float id = d != 0.0f ? 1.0f / d : 0.0f;
+        y[i].d = f2h(d);
+        for (int j = 0; j < 32; ++j) y[i].qs[j] = (int8_t)roundf(v[j] * id);
+    }
+}
+
+/* ggml_vec_dot_q8_0_q8_0, x86 path: eight fp32 lanes, each fed by an exact
+ * 4-element integer sum per block, then the 8->4->2->1 horizontal add. */
+static inline float dot_q8(const blk_q8* w, const blk_q8* x, int nb) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int b = 0; b < nb; ++b) {
+        const float d = h2f(w[b].d) * h2f(x[b].d);
+        const int8_t* a = w[b].qs;
+        const int8_t* c = x[b].qs;
+        for (int l = 0; l < 8; ++l) {
+            const int s = a[4 * l] * c[4 * l] + a[4 * l + 1] * c[4 * l + 1] +
+                          a[4 * l + 2] * c[4 * l + 2] + a[4 * l + 3] * c[4 * l + 3];
+            acc[l] = fmaf(d, (float)s, acc[l]);
+        }
+    }
+    float r0 = acc[4] + acc[0], r1 = acc[5] + acc[1], r2 = acc[6] + acc[2], r3 = acc[7] + acc[3];
+    r0 = r0 + r2;
+    r1 = r1 + r3;
+    return r0 + r1;
+}
+
+/* ggml_mul_mat(W q8_0 [n_rows x k], x f32 [T x k]) -> y [T x n_rows]. */
+void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int T, float* y) {
+    const int nb = k / 32;
+    blk_q8* xq = (blk_q8*)malloc(sizeof(blk_q8) * (size_t)nb * (size_t)T);
+    for (int t = 0; t < T; ++t) orc_quantize_act_q8(x + (size_t)t * k, k, xq + (size_t)t * nb);
+    const blk_q8* w = (const blk_q8*)w_blocks;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < n_rows; ++n) {
+        const blk_q8* row = w + (size_t)n * nb;
+        for (int t = 0; t < T; ++t) y[(size_t)t * n_rows + n] = dot_q8(row, xq + (size_t)t * nb, nb);
+    }
+    free(xq);
+}
+
+/* ------------------------------------------------------------- model */
+
+typedef struct {
+    const void *wq, *wk, *wv, *wo, *wgate, *wup, *wdown;
+    const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+} orc_layer;
+
+struct orc_model {
+    int hidden, n_layers, n_heads, n_kv, head_dim, ffn, vocab;
+    float eps, theta;
+    const void* token_embd;
+    const float* output_norm;
+    orc_layer* layers;
+};
+
+orc_model* orc_model_create(int hidden, int n_layers, int n_heads, int n_kv_heads, int head_dim,
+                            int ffn, int vocab, float rms_eps, float rope_theta) {
+    if (hidden <= 0 || hidden % 32 || n_layers <= 0 || n_heads <= 0 || n_kv_heads <= 0 ||
+        n_heads % n_kv_heads || head_dim <= 0 || head_dim % 2 || ffn <= 0 || ffn % 32 || vocab <= 0)
+        return NULL;
+    orc_model* m = (orc_model*)calloc(1, sizeof(orc_model));
+    m->hidden = hidden;
+    m->n_layers = n_layers;
+    m->n_heads = n_heads;
+    m->n_kv = n_kv_heads;
+    m->head_dim = head_dim;
+    m->ffn = ffn;
+    m->vocab = vocab;
+    m->eps = rms_eps;
+    m->theta = rope_theta;
+    m->layers = (orc_layer*)calloc((size_t)n_layers, sizeof(orc_layer));
+    return m;
+}
+
+void orc_model_free(orc_model* m) {
+    if (!m) return;
+    free(m->layers);
+    free(m);
+}
+
+int orc_model_set_tensor(orc_model* m, const char* name, const void* data, int type) {
+    if (!m || !name || !data) return -1;
+    if (!strcmp(name, "token_embd.weight")) {
+        if (type != ORC_Q8_0) return -2;
+        m->token_embd = data;
+        return 0;
+    }
+    if (!strcmp(name, "qwen3.output_norm.weight")) {
+        if (type != ORC_F32) return -2;
+        m->output_norm = (const float*)data;
+        return 0;
+    }
+    int layer = -1, used = 0;
+    char field[64];
+    if (sscanf(name, "qwen3.blk.%d.%63s%n", &layer, field, &used) != 2 || layer < 0 ||
+        layer >= m->n_layers)
+        return -3;
+    orc_layer* L = &m->layers[layer];
+    struct { const char* n; const void** q; const float** f; } map[] = {
+        {"attn_q.weight", &L->wq, NULL},       {"attn_k.weight", &L->wk, NULL},
+        {"attn_v.weight", &L->wv, NULL},       {"attn_o.weight", &L->wo, NULL},
+        {"ffn_gate.weight", &L->wgate, NULL},  {"ffn_up.weight", &L->wup, NULL},
+        {"ffn_down.weight", &L->wdown, NULL},  {"attn_norm.weight", NULL, &L->attn_norm},
+        {"attn_q_norm.weight", NULL, &L->q_norm}, {"attn_k_norm.weight", NULL, &L->k_norm},
+        {"ffn_norm.weight", NULL, &L->ffn_norm},
+    };
+    for (size_t i = 0; i < sizeof(map) / sizeof(map[0]); ++i) {
+        if (strcmp(field, map[i].n)) continue;
+        if (map[i].q) {
+            if (type != ORC_Q8_0) return -2;
+            *map[i].q = data;
+        } else {
+            if (type != ORC_F32) return -2;
+            *map[i].f = (const float*)data;
+        }
+        return 0;
+    }
+    return -3;
+}
+
+int orc_model_check(const orc_model* m) {
+    if (!m || !m->token_embd || !m->output_norm) return -1;
+    for (int l = 0; l < m->n_layers; ++l) {
+        const orc_layer* L = &m->layers[l];
+        if (!L->wq || !L->wk || !L->wv || !L->wo || !L->wgate || !L->wup || !L->wdown ||
+            !L->attn_norm || !L->q_norm || !L->k_norm || !L->ffn_norm)
+            return -2 - l;
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------- decoder */
+
+struct orc_decoder {
+    const orc_model* m;
+    int max_seq, past, kv_fp16;
+    float* k; /* [layer][pos][n_kv][hd] */
+    float* v;
+};
+
+orc_decoder* orc_decoder_create(const orc_model* m, int max_seq, int kv_fp16) {
+    if (!m || orc_model_check(m) || max_seq <= 0) return NULL;
+    orc_decoder* d = (orc_decoder*)calloc(1, sizeof(orc_decoder));
+    d->m = m;
+    d->max_seq = max_seq;
+    d->kv_fp16 = kv_fp16;
+    const size_t n = (size_t)m->n_layers * (size_t)max_seq * (size_t)m->n_kv * (size_t)m->head_dim;
+    d->k = (float*)calloc(n, sizeof(float));
+    d->v = (float*)calloc(n, sizeof(float));
+    if (!d->k || !d->v) {
+        orc_decoder_free(d);
+        return NULL;
+    }
+    return d;
+}
+
+void orc_decoder_free(orc_decoder* d) {
+    if (!d) return;
+    free(d->k);
+    free(d->v);
+    free(d);
+}
+
+int orc_decoder_past_len(const orc_decoder* d) { return d ? d->past : -1; }
+/* src/qwen3_decoder.cpp:87-89: stale cache bytes beyond past_len are never read. */
+void orc_decoder_reset(orc_decoder* d) {
+    if (d) d->past = 0;
+}
+/* src/cpu_speculative.cpp:40-42 */
+int orc_decoder_rewind(orc_decoder* d, int position) {
+    if (!d || position < 0 || position > d->past) return -1;
+    d->past = position;
+    return 0;
+}
+
+static inline size_t kv_index(const orc_decoder* d, int layer, int pos) {
+    const orc_model* m = d->m;
+    return (((size_t)layer * d->max_seq + pos) * m->n_kv) * m->head_dim;
+}
+
+int orc_decoder_kv_read(const orc_decoder* d, int layer, int which, int pos0, int n_pos, float* out) {
+    if (!d || layer < 0 || layer >= d->m->n_layers || pos0 < 0 || n_pos < 0 || pos0 + n_pos > d->max_seq)
+        return -1;
+    const float* src = (which ? d->v : d->k) + kv_index(d, layer, pos0);
+    memcpy(out, src, sizeof(float) * (size_t)n_pos * d->m->n_kv * d->m->head_dim);
+    return 0;
+}
+
+int orc_decoder_kv_write(orc_decoder* d, int layer, int which, int pos0, int n_pos, const float* in) {
+    if (!d || layer < 0 || layer >= d->m->n_layers || pos0 < 0 || n_pos < 0 || pos0 + n_pos > d->max_seq)
+        return -1;
+    float* dst = (which ? d->v : d->k) + kv_index(d, layer, pos0);
+    const size_t n = (size_t)n_pos * d->m->n_kv * d->m->head_dim;
+    for (size_t i = 0; i < n; ++i) dst[i] = d->kv_fp16 ? round_f16(in[i]) : in[i];
+    return 0;
+}
+
+static inline uint32_t mix32(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+float orc_synthetic_kv_value(uint32_t seed, int layer, int which, int pos, int head, int dim) {
+    uint32_t h = mix32(seed + 0x9E3779B9u * (uint32_t)(layer * 2 + which + 1));
+    h = mix32(h ^ ((uint32_t)pos * 0x85EBCA6Bu));
+    h = mix32(h ^ ((uint32_t)(head * 1024 + dim) * 0xC2B2AE35u));
+    const uint32_t g = mix32(h ^ 0x68E31DA4u);
+    const int s = (int)(h & 0xffffu) + (int)(h >> 16) + (int)(g & 0xffffu) + (int)(g >> 16) - 131070;
+    return round_f16((float)s * 2.642912e-05f);
+}
+
+int orc_decoder_fill_synthetic_kv(orc_decoder* d, int n_pos, uint32_t seed) {
+    if (!d || n_pos < 0 || n_pos > d->max_seq) return -1;
+    const orc_model* m = d->m;
+#pragma omp parallel for schedule(static)
+    for (int l = 0; l < m->n_layers; ++l)
+        for (int p = 0; p < n_pos; ++p)
+            for (int h = 0; h < m->n_kv; ++h)
+                for (int e = 0; e < m->head_dim; ++e) {
+                    const size_t i = kv_index(d, l, p) + (size_t)h * m->head_dim + e;
+                    d->k[i] = orc_synthetic_kv_value(seed, l, 0, p, h, e);
+                    d->v[i] = orc_synthetic_kv_value(seed, l, 1, p, h, e);
+                }
+    d->past = n_pos;
+    return 0;
+}
+
+/* ggml rms_norm followed by ggml_mul with the weight (src/qwen3.cpp:27-30). */
+static void rms_norm_mul(const float* x, const float* w, int n, float eps, float* y) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / n);
+    const float scale = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; ++i) y[i] = (x[i] * scale) * w[i];
+}
+
+/* ggml_rope_ext NEOX with freq_scale 1, ext_factor 0, attn_factor 1
+ * (src/qwen3.cpp:109-118). */
+static void rope_neox(float* x, int n_dims, int pos, float base) {
+    const float theta_scale = powf(base, -2.0f / (float)n_dims);
+    float theta = (float)pos;
+    const int half = n_dims / 2;
+    for (int i = 0; i < half; ++i) {
+        const float c = cosf(theta), s = sinf(theta);
+        const float x0 = x[i], x1 = x[i + half];
+        x[i] = x0 * c - x1 * s;
+        x[i + half] = x0 * s + x1 * c;
+        theta *= theta_scale;
+    }
+}
+
+static inline float silu(float x) { return x / (1.0f + expf(-x)); }
+
+int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidden) {
+    if (!d || !embeds || T <= 0 || d->past + T > d->max_seq) return -1;
+    const orc_model* m = d->m;
+    const int H = m->hidden, hd = m->head_dim, nh = m->n_heads, nkv = m->n_kv, F = m->ffn;
+    const int past = d->past, kv = past + T, group = nh / nkv;
+    const int qd = nh * hd, kd = nkv * hd;
+    float* x = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* xn = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* q = (float*)malloc(sizeof(float) * (size_t)T * qd);
+    float* k = (float*)malloc(sizeof(float) * (size_t)T * kd);
+    float* v = (float*)malloc(sizeof(float) * (size_t)T * kd);
+    float* o = (float*)malloc(sizeof(float) * (size_t)T * qd);
+    float* proj = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* g = (float*)malloc(sizeof(float) * (size_t)T * F);
+    float* u = (float*)malloc(sizeof(float) * (size_t)T * F);
+    memcpy(x, embeds, sizeof(float) * (size_t)T * H);
+    const float scale = 1.0f / sqrtf((float)hd);
+
+    for (int l = 0; l < m->n_layers; ++l) {
+        const orc_layer* L = &m->layers[l];
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H);
+        orc_mul_mat_q8(L->wq, qd, H, xn, T, q);
+        orc_mul_mat_q8(L->wk, kd, H, xn, T, k);
+        orc_mul_mat_q8(L->wv, kd, H, xn, T, v);
+        for (int t = 0; t < T; ++t) {
+            for (int h = 0; h < nh; ++h) {
+                float* qh = q + (size_t)t * qd + (size_t)h * hd;
+                rms_norm_mul(qh, L->q_norm, hd, m->eps, qh);
+                rope_neox(qh, hd, past + t, m->theta);
+            }
+            for (int h = 0; h < nkv; ++h) {
+                float* kh = k + (size_t)t * kd + (size_t)h * hd;
+                rms_norm_mul(kh, L->k_norm, hd, m->eps, kh);
+                rope_neox(kh, hd, past + t, m->theta);
+            }
+            /* KV store at past+t (src/qwen3.cpp:123-140). */
+            float* kdst = d->k + kv_index(d, l, past + t);
+            float* vdst = d->v + kv_index(d, l, past + t);
+            for (int i = 0; i < kd; ++i) {
+                kdst[i] = d->kv_fp16 ? round_f16(k[(size_t)t * kd + i]) : k[(size_t)t * kd + i];
+                vdst[i] = d->kv_fp16 ? round_f16(v[(size_t)t * kd + i]) : v[(size_t)t * kd + i];
+            }
+        }
+        /* GQA attention with a causal mask when T > 1 (src/qwen3.cpp:158-189,
+         * src/qwen3_decoder.cpp:142-148, src/cpu_context.cpp:13-33). */
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int t = 0; t < T; ++t) {
+            for (int h = 0; h < nh; ++h) {
+                const int kvh = h / group;
+                const float* qh = q + (size_t)t * qd + (size_t)h * hd;
+                const int valid = past + t + 1;
+                float* w = (float*)malloc(sizeof(float) * (size_t)kv);
+                float mx = -INFINITY;
+                for (int j = 0; j < kv; ++j) {
+                    const float* kj = d->k + kv_index(d, l, j) + (size_t)kvh * hd;
+                    float s = 0.0f;
+                    for (int e = 0; e < hd; ++e) s += kj[e] * qh[e];
+                    w[j] = j < valid ? s * scale : -INFINITY;
+                    mx = fmaxf(mx, w[j]);
+                }
+                double sum = 0.0;
+                for (int j = 0; j < kv; ++j) {
+                    const float e = j < valid ? expf(w[j] - mx) : 0.0f;
+                    w[j] = e;
+                    sum += (double)e;
+                }
+                const float inv = (float)(1.0 / sum);
+                for (int j = 0; j < kv; ++j) w[j] *= inv;
+                float* oh = o + (size_t)t * qd + (size_t)h * hd;
+                for (int e = 0; e < hd; ++e) {
+                    float acc = 0.0f;
+                    for (int j = 0; j < valid; ++j) acc += (d->v + kv_index(d, l, j) + (size_t)kvh * hd)[e] * w[j];
+                    oh[e] = acc;
+                }
+                free(w);
+            }
+        }
+        orc_mul_mat_q8(L->wo, H, qd, o, T, proj);
+        for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H);
+        orc_mul_mat_q8(L->wgate, F, H, xn, T, g);
+        orc_mul_mat_q8(L->wup, F, H, xn, T, u);
+        for (size_t i = 0; i < (size_t)T * F; ++i) g[i] = silu(g[i]) * u[i];
+        orc_mul_mat_q8(L->wdown, H, F, g, T, proj);
+        for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
+    }
+    for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H);
+    d->past = kv;
+    free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u);
+    return 0;
+}
+
+/* src/qwen3_decoder.cpp:174-206: token_embd (q8_0) @ hidden, one row. */
+void orc_decoder_logits(const orc_decoder* d, const float* hidden_row, float* logits) {
+    orc_mul_mat_q8(d->m->token_embd, d->m->vocab, d->m->hidden, hidden_row, 1, logits);
+}
+
+/* src/generate.cpp:33-66: get_rows / to_float of q8_0 rows: y = d * q. */
+int orc_embed_rows(const orc_model* m, const int32_t* ids, int n, float* out) {
+    if (!m || !ids || n <= 0) return -1;
+    const int nb = m->hidden / 32;
+    const blk_q8* tok = (const blk_q8*)m->token_embd;
+    for (int p = 0; p < n; ++p) {
+        if (ids[p] < 0 || ids[p] >= m->vocab) return -2;
+        const blk_q8* row = tok + (size_t)ids[p] * nb;
+        for (int b = 0; b < nb; ++b) {
+            const float dd = h2f(row[b].d);
+            for (int j = 0; j < 32; ++j) out[(size_t)p * m->hidden + b * 32 + j] = (float)row[b].qs[j] * dd;
+        }
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------- controller */
+
+/* src/cpu_speculative.cpp:45-56 with the n-gram range made explicit. */
+int orc_ngram_draft(const int32_t* h, int n, int maximum, int n_min, int n_max, int32_t* out) {
+    /* n < 3 is the reference's guard for its fixed n_min = 2; n_min + 1 is its
+     * generalisation (the loop below needs a suffix plus one earlier token). */
+    if (maximum <= 0 || n < 2 || n < n_min + 1) return 0;
+    int top = n_max < n - 1 ? n_max : n - 1;
+    for (int size = top; size >= n_min; --size) {
+        for (int start = n - size - 1; start >= 0; --start) {
+            if (!memcmp(h + n - size, h + start, sizeof(int32_t) * (size_t)size)) {
+                const int begin = start + size;
+                int count = n - begin;
+                if (count > maximum) count = maximum;
+                memcpy(out, h + begin, sizeof(int32_t) * (size_t)count);
+                return count;
+            }
+        }
+    }
+    return 0;
+}
+
+/* src/cpu_speculative.cpp:57-68: first max with strict >, optional penalty
+ * over the set of the last 100 ids. */
+int orc_greedy_choice(const float* raw, int vocab, const int32_t* h, int n, float penalty) {
+    if (vocab <= 0) return -1;
+    if (penalty <= 1.f) {
+        int best = 0;
+        for (int i = 1; i < vocab; ++i)
+            if (raw[i] > raw[best]) best = i;
+        return best;
+    }
+    float* adj = (float*)malloc(sizeof(float) * (size_t)vocab);
+    memcpy(adj, raw, sizeof(float) * (size_t)vocab);
+    unsigned char* seen = (unsigned char*)calloc((size_t)vocab, 1);
+    for (int i = n > 100 ? n - 100 : 0; i < n; ++i) {
+        const int32_t id = h[i];
+        if (id < 0 || id >= vocab || seen[id]) continue;
+        seen[id] = 1;
+        adj[id] = adj[id] > 0 ? adj[id] / penalty : adj[id] * penalty;
+    }
+    int best = 0;
+    for (int i = 1; i < vocab; ++i)
+        if (adj[i] > adj[best]) best = i;
+    free(adj);
+    free(seen);
+    return best;
+}
+
+static float clamp_penalty(float p) { return p < 1.f ? 1.f : (p > 1.5f ? 1.5f : p); }
+
+/* src/cpu_speculative.cpp:86-165 */
+int orc_spec_generate(orc_decoder* d, const float* fused, int seq, int max_new, int eos,
+                      int k_max, int n_min, int n_max, float penalty,
+                      int32_t* out_ids, orc_counters* c,
+                      orc_draft_fn draft, orc_commit_fn commit, void* user) {
+    orc_counters local;
+    if (!c) c = &local;
+    memset(c, 0, sizeof(*c));
+    if (!d || !fused || seq <= 0 || max_new <= 0 || !out_ids || k_max < 0 || n_min < 1 || n_max < n_min) return -1;
+    const orc_model* m = d->m;
+    const int H = m->hidden, V = m->vocab;
+    penalty = clamp_penalty(penalty);
+    d->past = 0;
+    float* hid = (float*)malloc(sizeof(float) * (size_t)seq * H);
+    if (orc_decoder_run(d, fused, seq, hid)) { free(hid); return -1; }
+    float* raw = (float*)malloc(sizeof(float) * (size_t)V);
+    orc_decoder_logits(d, hid + (size_t)(seq - 1) * H, raw);
+    free(hid);
+    int n = 0, stop = 0;
+    int32_t* proposal = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k_max > 0 ? k_max : 1));
+    int32_t* inputs = (int32_t*)malloc(sizeof(int32_t) * (size_t)(k_max + 1));
+    float* emb = (float*)malloc(sizeof(float) * (size_t)(k_max + 1) * H);
+    float* h = (float*)malloc(sizeof(float) * (size_t)(k_max + 1) * H);
+#define EMIT(id)                                   \
+    do {                                           \
+        out_ids[n++] = (id);                       \
+        if ((id) == eos) stop = 1;                 \
+        else if (n >= max_new) stop = 2;           \
+    } while (0)
+    int err = 0;
+    while (!stop) {
+        const int seed = orc_greedy_choice(raw, V, out_ids, n, penalty);
+        EMIT(seed);
+        if (stop) {
+            if (commit) commit(user, out_ids, n, d->past, 1);
+            break;
+        }
+        const int before = d->past;
+        int budget = k_max;
+        if (max_new - n < budget) budget = max_new - n;
+        if (d->max_seq - d->past - 1 < budget) budget = d->max_seq - d->past - 1;
+        if (budget < 0) budget = 0;
+        int np = draft ? draft(user, out_ids, n, budget, proposal)
+                       : orc_ngram_draft(out_ids, n, budget, n_min, n_max, proposal);
+        if (np > budget) np = budget;
+        if (np < 0) np = 0;
+        for (int i = 0; i < np; ++i)
+            if (proposal[i] < 0 || proposal[i] >= V) { err = 1; break; }
+        if (err) break;
+        inputs[0] = seed;
+        memcpy(inputs + 1, proposal, sizeof(int32_t) * (size_t)np);
+        const int T = 1 + np;
+        if (orc_embed_rows(m, inputs, T, emb)) { err = 1; break; }
+        if (T > d->max_seq - d->past || orc_decoder_run(d, emb, T, h)) { err = 1; break; }
+        c->target_calls++;
+        c->drafted_calls += np > 0;
+        c->proposed += np;
+        c->target_input_tokens += T;
+        orc_decoder_logits(d, h, raw);
+        int keep = 1;
+        for (int i = 0; i < np; ++i) {
+            if (proposal[i] != orc_greedy_choice(raw, V, out_ids, n, penalty)) break;
+            c->accepted++;
+            EMIT(proposal[i]);
+            if (stop) break; /* the terminating token is not evaluated */
+            ++keep;
+            orc_decoder_logits(d, h + (size_t)(i + 1) * H, raw);
+        }
+        const int position = before + keep;
+        if (d->past != position) {
+            if (orc_decoder_rewind(d, position)) { err = 1; break; }
+            c->rewinds++;
+        }
+        if (commit) commit(user, out_ids, n, d->past, stop != 0);
+    }
+#undef EMIT
+    c->stop_reason = err ? 0 : stop;
+    free(raw); free(proposal); free(inputs); free(emb); free(h);
+    return err ? -1 : n;
+}
+
+/* src/generate.cpp:235-326 (serial greedy path). */
+int orc_greedy_generate(orc_decoder* d, const float* fused, int seq, int max_new, int eos,
+                        float penalty, int32_t* out_ids) {
+    if (!d || !fused || seq <= 0 || max_new <= 0 || !out_ids) return -1;
+    const orc_model* m = d->m;
+    const int H = m->hidden, V = m->vocab;
+    penalty = clamp_penalty(penalty);
+    d->past = 0;
+    float* hid = (float*)malloc(sizeof(float) * (size_t)seq * H);
+    if (orc_decoder_run(d, fused, seq, hid)) { free(hid); return -1; }
+    float* raw = (float*)malloc(sizeof(float) * (size_t)V);
+    orc_decoder_logits(d, hid + (size_t)(seq - 1) * H, raw);
+    free(hid);
+    float* emb = (float*)malloc(sizeof(float) * (size_t)H);
+    float* h = (float*)malloc(sizeof(float) * (size_t)H);
+    int n = 0, rc = 0;
+    for (;;) {
+        const int t = orc_greedy_choice(raw, V, out_ids, n, penalty);
+        out_ids[n++] = t;
+        if (t == eos || n >= max_new) break;
+        if (orc_embed_rows(m, &t, 1, emb) || orc_decoder_run(d, emb, 1, h)) { rc = -1; break; }
+        orc_decoder_logits(d, h, raw);
+    }
+    free(raw); free(emb); free(h);
+    return rc ? -1 : n;
+}
