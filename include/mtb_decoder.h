@@ -1,0 +1,141 @@
+/*
+ * B200 strict speculative decoder: C ABI of the generate layer.
+ *
+ * This is the boundary the reference's generation layer would call instead of
+ * its CPU path.  Each entry replaces one reference interface (paths relative
+ * to the moss-transcribe.cpp project root):
+ *
+ *   mtb_model_load / mtb_model_free      ModelLoader::load (src/model_loader.cpp:21)
+ *                                        + Qwen3Decoder::load weight part
+ *                                        (src/qwen3_decoder.cpp:20-57)
+ *   mtb_decoder_create / _free           Qwen3Decoder::load KV part
+ *                                        (src/qwen3_decoder.cpp:59-85)
+ *   mtb_decoder_run                      Qwen3Decoder::run / prefill / decode_one
+ *                                        (src/qwen3_decoder.cpp:91-172)
+ *   mtb_decoder_logits                   Qwen3Decoder::logits_from_hidden (:174-206)
+ *   mtb_decoder_rewind / _past_len       CpuSpeculativeDecoder::rewind (src/cpu_speculative.cpp:40-42),
+ *                                        Qwen3Decoder::past_len (src/qwen3_decoder.hpp:55)
+ *   mtb_greedy_generate                  greedy_generate serial path (src/generate.cpp:235-326)
+ *   mtb_spec_generate                    cpu_speculative_generate (src/cpu_speculative.cpp:86-165)
+ *                                        with CpuSpeculativeHooks draft/committed
+ *                                        (src/cpu_speculative.hpp:9-15)
+ *   mtb_ngram_draft                      cpu_ngram_draft (src/cpu_speculative.cpp:45-56),
+ *                                        evaluated by the device draft kernel
+ *   mtb_greedy_choice                    cpu_greedy_choice (src/cpu_speculative.cpp:57-68),
+ *                                        evaluated by the device choice kernel
+ *   mtb_spec_step / _async, mtb_resume,  one verify step of the loop body
+ *   mtb_snapshot_save / _restore         (src/cpu_speculative.cpp:118-155)
+ *
+ * Conventions: every function returns 0 on success or a negative code and
+ * sets a per-object error string; no C++ exception crosses the boundary.  One
+ * decoder is one CUDA device and one stream; decoders on different devices
+ * may be driven from different host threads.  There is no CPU fallback: on a
+ * host without a usable GPU, mtb_model_load fails with an error.
+ */
+#ifndef MTB_DECODER_H
+#define MTB_DECODER_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mtb_model mtb_model;
+typedef struct mtb_decoder mtb_decoder;
+
+enum { MTB_KV_F32 = 0, MTB_KV_F16 = 1 };
+enum { MTB_STOP_NONE = 0, MTB_STOP_EOS = 1, MTB_STOP_LIMIT = 2, MTB_STOP_ERROR = 3 };
+
+/* Draft policy.  The reference policy is k_max 4, n-gram sizes 16..2
+ * (src/cpu_speculative.cpp:47,122); penalty is MTD_REPETITION_PENALTY clamped
+ * to [1, 1.5] (:103-104). */
+typedef struct mtb_spec_params {
+    int32_t k_max;   /* proposals per step, 0..15 */
+    int32_t n_min;   /* smallest n-gram size, >= 1 */
+    int32_t n_max;   /* largest n-gram size */
+    float penalty;   /* repetition penalty over the last 100 ids */
+} mtb_spec_params;
+
+/* Counters of the CPU_SPECULATIVE log line (src/cpu_speculative.cpp:158). */
+typedef struct mtb_counters {
+    int64_t target_calls, drafted_calls, proposed, accepted, target_input_tokens, rewinds;
+    int32_t stop_reason; /* MTB_STOP_* */
+    int32_t past_len;
+} mtb_counters;
+
+/* Mirrors CpuSpeculativeHooks::draft: write at most `budget` ids, return count. */
+typedef int (*mtb_draft_fn)(void* user, const int32_t* ids, int n_ids, int budget, int32_t* out);
+/* Mirrors CpuSpeculativeHooks::committed: after every commit. */
+typedef void (*mtb_commit_fn)(void* user, const int32_t* ids, int n_ids, int past_len, int stopped);
+
+int mtb_abi_version(void);
+/* Returns the error of the last failed call on this thread that had no object. */
+const char* mtb_global_error(void);
+
+/* ---- model: decoder weights resident on one device ---- */
+int mtb_model_load(const char* gguf_path, int device, mtb_model** out);
+void mtb_model_free(mtb_model* m);
+const char* mtb_model_error(const mtb_model* m);
+/* hidden, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab, eos */
+int mtb_model_dims(const mtb_model* m, int32_t* out8);
+
+/* ---- decoder: KV cache (paged, 64 positions per page) and step state ---- */
+int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_decoder** out);
+void mtb_decoder_free(mtb_decoder* d);
+const char* mtb_decoder_error(const mtb_decoder* d);
+int mtb_decoder_past_len(const mtb_decoder* d);
+int mtb_decoder_reset(mtb_decoder* d);
+int mtb_decoder_rewind(mtb_decoder* d, int position);
+/* Append T host rows [T][hidden] at past..past+T-1 (any T; chunks of 16),
+ * writing the final-RMSNorm'd hidden rows to hidden_out [T][hidden] (may be NULL). */
+int mtb_decoder_run(mtb_decoder* d, const float* embeds, int T, float* hidden_out);
+/* Tied LM head on one host hidden row -> logits[vocab]. */
+int mtb_decoder_logits(mtb_decoder* d, const float* hidden_row, float* logits);
+/* KV rows of one layer (which 0 = K, 1 = V) as f32 [n_pos][n_kv][128]. */
+int mtb_decoder_kv_read(mtb_decoder* d, int layer, int which, int pos0, int n_pos, float* out);
+/* Synthetic fp16-valued KV at positions [0, n_pos) of every layer; sets past_len. */
+int mtb_decoder_fill_synthetic_kv(mtb_decoder* d, int n_pos, uint32_t seed);
+
+/* ---- generation ---- */
+int mtb_greedy_generate(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, float penalty,
+                        int32_t* out_ids, int* n_out);
+int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, int eos,
+                      const mtb_spec_params* params, int32_t* out_ids, int* n_out, mtb_counters* counters,
+                      mtb_draft_fn draft, mtb_commit_fn commit, void* user);
+
+/* Continue from an existing cache: ids[0:n_ids] are the generated ids (the
+ * last is the pending seed, not yet in the cache), past the cache length. */
+int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_new, int eos,
+               const mtb_spec_params* params);
+/* One verify step.  draft == NULL -> on-device n-gram draft; otherwise the
+ * n_draft host ids are the proposal.  Synchronous; new ids via mtb_read_ids. */
+int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counters* counters);
+/* Same, asynchronous on the decoder's stream, proposal from DEVICE memory
+ * (NULL -> on-device draft).  Nothing is copied to or from the host. */
+int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft);
+/* Device-side copy of the step state and ids (save) and back (restore),
+ * asynchronous on the decoder's stream. */
+int mtb_snapshot_save(mtb_decoder* d);
+int mtb_snapshot_restore_async(mtb_decoder* d);
+int mtb_read_ids(mtb_decoder* d, int32_t* out, int max_out, int* n_out, mtb_counters* counters);
+
+/* ---- timing on the decoder's stream ---- */
+int mtb_sync(mtb_decoder* d);
+int mtb_event_record(mtb_decoder* d, int slot);          /* slot 0..15 */
+int mtb_event_elapsed_ms(mtb_decoder* d, int a, int b, float* ms);
+/* Kernel launches per verify step (counted when the step graph is built). */
+int mtb_step_kernel_launches(mtb_decoder* d);
+
+/* ---- controller pieces, run by the same device kernels the loop uses ---- */
+/* history: n host ids (n <= the decoder's max_new); out: up to `maximum` ids. */
+int mtb_ngram_draft(mtb_decoder* d, const int32_t* history, int n, int maximum, int n_min, int n_max,
+                    int32_t* out, int* n_out);
+/* raw: n_raw host logits (n_raw <= vocab); history: n host ids. */
+int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t* history, int n, float penalty,
+                      int32_t* choice);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,791 @@
+// Host runtime of the B200 strict speculative decoder (C ABI in
+// include/mtb_decoder.h).
+//
+// Model: GGUF -> q8_0 tiles in HBM (ModelLoader::load + Qwen3Decoder::load,
+// src/model_loader.cpp:21-114, src/qwen3_decoder.cpp:20-85).  Decoder: paged
+// KV cache, device StepState, step buffers and the CUDA graphs of the verify
+// step.  The generation loop (src/cpu_speculative.cpp:86-165) runs on the
+// device: drafting, the verify forward, the LM-head first max, acceptance and
+// rollback are kernels of one captured graph, and the host only watches the
+// stop flag.  With draft/commit hooks the loop runs one step per host round
+// trip so the hooks see every proposal and commit.
+#include "../../include/mtb_decoder.h"
+#include "gguf.hpp"
+#include "kernels.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+using namespace mtb;
+
+namespace {
+thread_local std::string g_error;
+
+constexpr int kAbiVersion = 1;
+}  // namespace
+
+struct mtb_model {
+    int device = 0;
+    DeviceModel dm{};
+    std::vector<LayerWeights> layers;
+    std::vector<void*> allocs;
+    std::string error;
+    int eos = -1;
+    ~mtb_model() {
+        cudaSetDevice(device);
+        for (void* p : allocs) cudaFree(p);
+    }
+};
+
+struct mtb_decoder {
+    mtb_model* model = nullptr;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int max_seq = 0, kv_type = 0, max_new = 0;
+    KvCache kv{};
+    StepBuffers b{};
+    StepState* h_state = nullptr;  // pinned mirror
+    float* h_rows = nullptr;       // pinned staging [kTMax][hidden]
+    int32_t* h_ids = nullptr;      // pinned [max_new]
+    int* h_flag = nullptr;         // pinned [2]
+    StepState* snap_state = nullptr;
+    int32_t* snap_ids = nullptr;
+    int32_t* scratch_i = nullptr;  // [max_new + 16]
+    int* scratch_n = nullptr;
+    float* row_buf = nullptr;      // [hidden]
+    cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+    int launches = 0;
+    cudaEvent_t ev[16] = {};
+    std::vector<void*> allocs;
+    std::string error;
+    ~mtb_decoder() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto& row : graphs)
+            for (auto& g : row)
+                if (g) cudaGraphExecDestroy(g);
+        for (auto& e : ev)
+            if (e) cudaEventDestroy(e);
+        for (void* p : allocs) cudaFree(p);
+        if (h_state) cudaFreeHost(h_state);
+        if (h_rows) cudaFreeHost(h_rows);
+        if (h_ids) cudaFreeHost(h_ids);
+        if (h_flag) cudaFreeHost(h_flag);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+#define MTB_CK(obj, call)                                                                          \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) {                                                                   \
+            (obj)->error = std::string(#call) + ": " + cudaGetErrorString(e_);                      \
+            return -1;                                                                             \
+        }                                                                                          \
+    } while (0)
+
+namespace {
+
+template <class T>
+int dalloc(std::vector<void*>& allocs, std::string& err, T** p, size_t bytes) {
+    void* q = nullptr;
+    const cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess) {
+        err = "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e);
+        return -1;
+    }
+    allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return 0;
+}
+
+int fail(std::string& err, const std::string& msg) {
+    err = msg;
+    return -1;
+}
+
+// Upload one q8_0 matrix (ne = [k, n]) through `staging` and repack it into
+// tiles at destination row groups r * stride + offset.
+int upload_q8(mtb_model* m, const GgufFile& f, const std::string& name, int64_t k, int64_t n, uint8_t* staging,
+              uint8_t* dst, int stride, int offset) {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) return fail(m->error, "missing tensor " + name);
+    if (t->type != GGML_Q8_0)
+        return fail(m->error, name + ": only q8_0 decoder weights are supported (type " + std::to_string(t->type) + ")");
+    if (t->ne.size() != 2 || t->ne[0] != k || t->ne[1] != n)
+        return fail(m->error, name + ": unexpected shape");
+    MTB_CK(m, cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
+    launch_repack_q8(staging, int(n), int(k), dst, stride, offset, nullptr);
+    MTB_CK(m, cudaGetLastError());
+    MTB_CK(m, cudaDeviceSynchronize());
+    return 0;
+}
+
+int upload_f32(mtb_model* m, const GgufFile& f, const std::string& name, int64_t n, const float** out) {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) return fail(m->error, "missing tensor " + name);
+    if (t->type != GGML_F32 || t->ne.size() != 1 || t->ne[0] != n) return fail(m->error, name + ": expected F32 [" + std::to_string(n) + "]");
+    float* p = nullptr;
+    if (dalloc(m->allocs, m->error, &p, size_t(n) * 4)) return -1;
+    MTB_CK(m, cudaMemcpy(p, t->data, size_t(n) * 4, cudaMemcpyHostToDevice));
+    *out = p;
+    return 0;
+}
+
+size_t tiles_bytes(int64_t n_rows, int64_t k) { return size_t(n_rows / kTileRows) * size_t(k / kTileK) * kTileBytes; }
+
+int load_model(mtb_model* m, const char* path) {
+    GgufFile f;
+    if (!f.open(path)) return fail(m->error, f.error());
+    ModelDims& d = m->dm.dims;
+    d.hidden = int(f.get_u32("mtd.text.hidden", 1024));
+    d.n_layers = int(f.get_u32("mtd.text.n_layers", 28));
+    d.n_heads = int(f.get_u32("mtd.text.n_heads", 16));
+    d.n_kv = int(f.get_u32("mtd.text.n_kv_heads", 8));
+    d.ffn = int(f.get_u32("mtd.text.ffn", 3072));
+    d.vocab = int(f.get_u32("mtd.text.vocab_size", 151936));
+    d.eps = f.get_f32("mtd.text.rms_eps", 1e-6f);
+    d.theta = f.get_f32("mtd.text.rope_theta", 1e6f);
+    m->eos = int(f.get_u32("mtd.eos_token_id", 151645));
+    const int head_dim = int(f.get_u32("mtd.text.head_dim", 128));
+    if (head_dim != kHeadDim) return fail(m->error, "head_dim must be 128");
+    if (d.hidden <= 0 || d.hidden % kTileK || d.hidden > 8192) return fail(m->error, "hidden must be a multiple of 64 (<= 8192)");
+    if (d.ffn <= 0 || d.ffn % kTileK || d.ffn > 16384) return fail(m->error, "ffn must be a multiple of 64 (<= 16384)");
+    if (d.n_heads <= 0 || d.n_kv <= 0 || d.n_heads % d.n_kv || d.n_heads / d.n_kv > 4)
+        return fail(m->error, "n_heads must be 1..4 times n_kv_heads");
+    if (d.vocab <= 0 || d.vocab % kTileRows) return fail(m->error, "vocab must be a multiple of 8");
+    if (d.n_layers <= 0) return fail(m->error, "n_layers must be positive");
+    const int64_t H = d.hidden, F = d.ffn, qd = int64_t(d.n_heads) * kHeadDim, kd = int64_t(d.n_kv) * kHeadDim;
+    const GgufTensor* te = f.tensor("token_embd.weight");
+    if (!te) return fail(m->error, "missing token_embd.weight");
+    size_t staging_bytes = te->nbytes;
+    for (int l = 0; l < d.n_layers; ++l) {
+        for (const char* nm : {"attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down"}) {
+            const GgufTensor* t = f.tensor("qwen3.blk." + std::to_string(l) + "." + nm + ".weight");
+            if (!t) return fail(m->error, "missing qwen3.blk." + std::to_string(l) + "." + nm + ".weight");
+            staging_bytes = std::max<size_t>(staging_bytes, t->nbytes);
+        }
+    }
+    uint8_t* staging = nullptr;
+    std::vector<void*> tmp;
+    if (dalloc(tmp, m->error, &staging, staging_bytes)) return -1;
+    struct Guard { std::vector<void*>& v; ~Guard() { for (void* p : v) cudaFree(p); } } guard{tmp};
+
+    uint8_t* embd = nullptr;
+    if (dalloc(m->allocs, m->error, &embd, tiles_bytes(d.vocab, H))) return -1;
+    if (upload_q8(m, f, "token_embd.weight", H, d.vocab, staging, embd, 1, 0)) return -1;
+    m->dm.embd = embd;
+    if (upload_f32(m, f, "qwen3.output_norm.weight", H, &m->dm.output_norm)) return -1;
+    m->layers.resize(size_t(d.n_layers));
+    for (int l = 0; l < d.n_layers; ++l) {
+        const std::string p = "qwen3.blk." + std::to_string(l) + ".";
+        LayerWeights& w = m->layers[size_t(l)];
+        uint8_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+        if (dalloc(m->allocs, m->error, &qkv, tiles_bytes(qd + 2 * kd, H)) ||
+            dalloc(m->allocs, m->error, &o, tiles_bytes(H, qd)) ||
+            dalloc(m->allocs, m->error, &gu, tiles_bytes(2 * F, H)) ||
+            dalloc(m->allocs, m->error, &down, tiles_bytes(H, F)))
+            return -1;
+        if (upload_q8(m, f, p + "attn_q.weight", H, qd, staging, qkv, 1, 0) ||
+            upload_q8(m, f, p + "attn_k.weight", H, kd, staging, qkv, 1, int(qd / kTileRows)) ||
+            upload_q8(m, f, p + "attn_v.weight", H, kd, staging, qkv, 1, int((qd + kd) / kTileRows)) ||
+            upload_q8(m, f, p + "attn_o.weight", qd, H, staging, o, 1, 0) ||
+            upload_q8(m, f, p + "ffn_gate.weight", H, F, staging, gu, 2, 0) ||
+            upload_q8(m, f, p + "ffn_up.weight", H, F, staging, gu, 2, 1) ||
+            upload_q8(m, f, p + "ffn_down.weight", F, H, staging, down, 1, 0))
+            return -1;
+        w.qkv = qkv;
+        w.o = o;
+        w.gu = gu;
+        w.down = down;
+        if (upload_f32(m, f, p + "attn_norm.weight", H, &w.attn_norm) ||
+            upload_f32(m, f, p + "attn_q_norm.weight", kHeadDim, &w.q_norm) ||
+            upload_f32(m, f, p + "attn_k_norm.weight", kHeadDim, &w.k_norm) ||
+            upload_f32(m, f, p + "ffn_norm.weight", H, &w.ffn_norm))
+            return -1;
+    }
+    m->dm.layers = m->layers.data();
+    // Same powf as the CPU path so the RoPE angles advance identically.
+    m->dm.theta_scale = std::pow(d.theta, -2.0f / float(kHeadDim));
+    MTB_CK(m, configure_kernels());
+    MTB_CK(m, cudaDeviceSynchronize());
+    return 0;
+}
+
+int refresh(mtb_decoder* d) {
+    MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    if (d->h_state->error) {
+        d->error = "device reported an out-of-range token id";
+        return -1;
+    }
+    return 0;
+}
+
+int push_state(mtb_decoder* d) {
+    MTB_CK(d, cudaMemcpyAsync(d->b.state, d->h_state, sizeof(StepState), cudaMemcpyHostToDevice, d->stream));
+    return 0;
+}
+
+cudaGraphExec_t step_graph(mtb_decoder* d, int mode, bool penalty) {
+    cudaGraphExec_t& g = d->graphs[mode][penalty ? 1 : 0];
+    if (g) return g;
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return nullptr;
+    launch_step(d->model->dm, d->kv, d->b, mode, penalty, d->stream);
+    if (cudaStreamEndCapture(d->stream, &graph) != cudaSuccess || !graph) return nullptr;
+    size_t n = 0;
+    cudaGraphGetNodes(graph, nullptr, &n);
+    d->launches = int(n);
+    if (cudaGraphInstantiate(&g, graph, 0) != cudaSuccess) g = nullptr;
+    cudaGraphDestroy(graph);
+    return g;
+}
+
+int run_step(mtb_decoder* d, int mode) {
+    cudaGraphExec_t g = step_graph(d, mode, d->h_state->penalty > 1.f);
+    if (!g) return fail(d->error, "could not build the verify-step graph: " + std::string(cudaGetErrorString(cudaGetLastError())));
+    MTB_CK(d, cudaGraphLaunch(g, d->stream));
+    return 0;
+}
+
+// Rows [T][hidden] from the host at past..past+T-1 in chunks of kTMax.
+int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last) {
+    const int H = d->model->dm.dims.hidden;
+    for (int r0 = 0; r0 < T; r0 += kTMax) {
+        const int n = std::min(kTMax, T - r0);
+        std::memcpy(d->h_rows, rows + size_t(r0) * H, size_t(n) * H * sizeof(float));
+        MTB_CK(d, cudaMemcpyAsync(d->b.x, d->h_rows, size_t(n) * H * sizeof(float), cudaMemcpyHostToDevice, d->stream));
+        launch_rows_begin(d->b, n, d->stream);
+        const bool last = r0 + n >= T;
+        launch_forward_rows(d->model->dm, d->kv, d->b, lm_on_last && last, false, d->stream);
+        launch_rows_end(d->b, d->stream);
+        MTB_CK(d, cudaGetLastError());
+        if (hidden_out) {
+            MTB_CK(d, cudaMemcpyAsync(hidden_out + size_t(r0) * H, d->b.hid, size_t(n) * H * sizeof(float),
+                                      cudaMemcpyDeviceToHost, d->stream));
+        }
+        MTB_CK(d, cudaStreamSynchronize(d->stream));  // h_rows is reused by the next chunk
+    }
+    return 0;
+}
+
+void fill_counters(const StepState& s, mtb_counters* c) {
+    if (!c) return;
+    c->target_calls = s.target_calls;
+    c->drafted_calls = s.drafted_calls;
+    c->proposed = s.proposed;
+    c->accepted = s.accepted;
+    c->target_input_tokens = s.target_input_tokens;
+    c->rewinds = s.rewinds;
+    c->stop_reason = s.stop;
+    c->past_len = s.past;
+}
+
+int set_params(mtb_decoder* d, int max_new, int eos, const mtb_spec_params* p) {
+    StepState& s = *d->h_state;
+    if (max_new <= 0 || max_new > d->max_new) return fail(d->error, "max_new must be in [1, " + std::to_string(d->max_new) + "]");
+    const int k = p ? p->k_max : 4;
+    if (k < 0 || k > kTMax - 1) return fail(d->error, "k_max must be in [0, 15]");
+    const int nmin = p ? p->n_min : 2, nmax = p ? p->n_max : 16;
+    if (nmin < 1 || nmax < nmin) return fail(d->error, "need 1 <= n_min <= n_max");
+    float pen = p ? p->penalty : 1.f;
+    pen = std::max(1.f, std::min(1.5f, pen));  // src/cpu_speculative.cpp:104
+    s.max_new = max_new;
+    s.eos = eos;
+    s.k_max = k;
+    s.n_min = nmin;
+    s.n_max = nmax;
+    s.penalty = pen;
+    s.max_seq = d->max_seq;
+    return 0;
+}
+
+void clear_progress(StepState& s) {
+    s.stop = STOP_NONE;
+    s.error = 0;
+    s.n_ids = 0;
+    s.T = 0;
+    s.n_prop = 0;
+    s.forced = 0;
+    s.target_calls = s.drafted_calls = s.proposed = s.accepted = s.target_input_tokens = s.rewinds = 0;
+}
+
+int prefill(mtb_decoder* d, const float* fused, int seq) {
+    if (!fused || seq <= 0) return fail(d->error, "empty prompt");
+    if (seq + 1 > d->max_seq) return fail(d->error, "prompt exceeds max_seq");
+    d->h_state->past = 0;
+    clear_progress(*d->h_state);
+    if (push_state(d)) return -1;
+    if (forward_host_rows(d, fused, seq, nullptr, true)) return -1;
+    launch_prefill_seed(d->b, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    return 0;
+}
+
+}  // namespace
+
+// ================================================================= C ABI
+
+extern "C" {
+
+int mtb_abi_version(void) { return kAbiVersion; }
+const char* mtb_global_error(void) { return g_error.c_str(); }
+
+int mtb_model_load(const char* path, int device, mtb_model** out) {
+    if (!out || !path) { g_error = "null argument"; return -1; }
+    *out = nullptr;
+    try {
+        int n_dev = 0;
+        if (cudaGetDeviceCount(&n_dev) != cudaSuccess || n_dev <= 0) {
+            g_error = "no CUDA device: this library has no CPU path";
+            cudaGetLastError();
+            return -2;
+        }
+        if (device < 0 || device >= n_dev) { g_error = "device index out of range"; return -2; }
+        if (cudaSetDevice(device) != cudaSuccess) { g_error = "cudaSetDevice failed"; return -2; }
+        cudaDeviceProp prop{};
+        cudaGetDeviceProperties(&prop, device);
+        if (prop.major != 10) {
+            g_error = "this library is built for sm_100a (B200); device is sm_" + std::to_string(prop.major * 10 + prop.minor);
+            return -2;
+        }
+        auto* m = new mtb_model();
+        m->device = device;
+        if (load_model(m, path)) {
+            g_error = m->error;
+            delete m;
+            return -1;
+        }
+        *out = m;
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    } catch (...) {
+        g_error = "unknown error";
+        return -1;
+    }
+}
+
+void mtb_model_free(mtb_model* m) { delete m; }
+const char* mtb_model_error(const mtb_model* m) { return m ? m->error.c_str() : ""; }
+
+int mtb_model_dims(const mtb_model* m, int32_t* o) {
+    if (!m || !o) return -1;
+    const ModelDims& d = m->dm.dims;
+    o[0] = d.hidden; o[1] = d.n_layers; o[2] = d.n_heads; o[3] = d.n_kv; o[4] = kHeadDim; o[5] = d.ffn;
+    o[6] = d.vocab; o[7] = m->eos;
+    return 0;
+}
+
+int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_decoder** out) {
+    if (!m || !out) { g_error = "null argument"; return -1; }
+    *out = nullptr;
+    if (max_seq <= 0 || max_new <= 0 || (kv_type != KV_F32 && kv_type != KV_F16)) {
+        g_error = "invalid decoder arguments";
+        return -1;
+    }
+    try {
+        auto* d = new mtb_decoder();
+        d->model = m;
+        d->device = m->device;
+        d->max_seq = max_seq;
+        d->kv_type = kv_type;
+        d->max_new = max_new;
+        auto bail = [&](void) { g_error = d->error; delete d; return -1; };
+        if (cudaSetDevice(d->device) != cudaSuccess) { d->error = "cudaSetDevice failed"; return bail(); }
+        if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) { d->error = "stream"; return bail(); }
+        const ModelDims& dm = m->dm.dims;
+        const int H = dm.hidden, F = dm.ffn, qd = dm.n_heads * kHeadDim, kd = dm.n_kv * kHeadDim;
+        const int kmax = std::max(std::max(H, qd), F);
+        const int n_pages = (max_seq + kPage - 1) / kPage;
+        d->kv.type = kv_type;
+        d->kv.page_elems = (long long)dm.n_layers * 2 * dm.n_kv * kPage * kHeadDim;
+        const size_t esz = kv_type == KV_F16 ? 2 : 4;
+        void* kvb = nullptr;
+        int32_t* pages = nullptr;
+        StepBuffers& b = d->b;
+        b.max_chunks = n_pages;
+        b.lm_blocks = lm_head_blocks(dm.vocab);
+        auto& A = d->allocs;
+        auto& E = d->error;
+        if (dalloc(A, E, &kvb, size_t(n_pages) * d->kv.page_elems * esz) || dalloc(A, E, &pages, size_t(n_pages) * 4) ||
+            dalloc(A, E, &b.state, sizeof(StepState)) || dalloc(A, E, &b.ids, size_t(max_new) * 4) ||
+            dalloc(A, E, &b.x, size_t(kTMax) * H * 4) || dalloc(A, E, &b.qkv, size_t(kTMax) * (qd + 2 * kd) * 4) ||
+            dalloc(A, E, &b.attn_out, size_t(kTMax) * qd * 4) || dalloc(A, E, &b.gu, size_t(kTMax) * F * 4) ||
+            dalloc(A, E, &b.hid, size_t(kTMax) * H * 4) || dalloc(A, E, &b.act_q, size_t(kmax / 32) * 512) ||
+            dalloc(A, E, &b.act_d, size_t(kmax / 32) * 16 * 4) ||
+            dalloc(A, E, &b.part_o, size_t(dm.n_kv) * n_pages * kTMax * 4 * kHeadDim * 4) ||
+            dalloc(A, E, &b.part_ml, size_t(dm.n_kv) * n_pages * kTMax * 4 * sizeof(float2)) ||
+            dalloc(A, E, &b.lm_val, size_t(b.lm_blocks) * 16 * sizeof(float2)) ||
+            dalloc(A, E, &b.logits, size_t(kTMax) * dm.vocab * 4) || dalloc(A, E, &d->snap_state, sizeof(StepState)) ||
+            dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
+            dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
+            return bail();
+        d->kv.base = kvb;
+        d->kv.pages = pages;
+        std::vector<int32_t> ident(static_cast<size_t>(n_pages));
+        for (int i = 0; i < n_pages; ++i) ident[size_t(i)] = i;
+        if (cudaMemcpy(pages, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(kvb, 0, size_t(n_pages) * d->kv.page_elems * esz) != cudaSuccess ||
+            cudaMemset(b.state, 0, sizeof(StepState)) != cudaSuccess) {
+            d->error = "device initialisation failed";
+            return bail();
+        }
+        if (cudaMallocHost(&d->h_state, sizeof(StepState)) != cudaSuccess ||
+            cudaMallocHost(&d->h_rows, size_t(kTMax) * H * 4) != cudaSuccess ||
+            cudaMallocHost(&d->h_ids, size_t(max_new) * 4) != cudaSuccess ||
+            cudaMallocHost(&d->h_flag, 2 * sizeof(int)) != cudaSuccess) {
+            d->error = "pinned host allocation failed";
+            return bail();
+        }
+        std::memset(d->h_state, 0, sizeof(StepState));
+        for (auto& e : d->ev)
+            if (cudaEventCreate(&e) != cudaSuccess) { d->error = "event"; return bail(); }
+        d->h_state->max_seq = max_seq;
+        d->h_state->max_new = max_new;
+        d->h_state->eos = m->eos;
+        d->h_state->k_max = 4;
+        d->h_state->n_min = 2;
+        d->h_state->n_max = 16;
+        d->h_state->penalty = 1.f;
+        if (push_state(d) || cudaStreamSynchronize(d->stream) != cudaSuccess) return bail();
+        *out = d;
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
+}
+
+void mtb_decoder_free(mtb_decoder* d) { delete d; }
+const char* mtb_decoder_error(const mtb_decoder* d) { return d ? d->error.c_str() : ""; }
+
+int mtb_decoder_past_len(const mtb_decoder* dc) {
+    auto* d = const_cast<mtb_decoder*>(dc);
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    return d->h_state->past;
+}
+
+int mtb_decoder_reset(mtb_decoder* d) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    d->h_state->past = 0;  // src/qwen3_decoder.cpp:87-89
+    clear_progress(*d->h_state);
+    if (push_state(d)) return -1;
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_decoder_rewind(mtb_decoder* d, int position) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    if (position < 0 || position > d->h_state->past) return fail(d->error, "invalid rewind");  // cpu_speculative.cpp:40-42
+    d->h_state->past = position;
+    if (push_state(d)) return -1;
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_decoder_run(mtb_decoder* d, const float* embeds, int T, float* hidden_out) {
+    if (!d || !embeds || T <= 0) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    if (d->h_state->past + T > d->max_seq) return fail(d->error, "sequence exceeds max_seq");  // qwen3_decoder.cpp:102
+    return forward_host_rows(d, embeds, T, hidden_out, false);
+}
+
+int mtb_decoder_logits(mtb_decoder* d, const float* hidden_row, float* logits) {
+    if (!d || !hidden_row || !logits) return -1;
+    cudaSetDevice(d->device);
+    const ModelDims& dm = d->model->dm.dims;
+    if (refresh(d)) return -1;
+    const int saved_T = d->h_state->T;
+    MTB_CK(d, cudaMemcpyAsync(d->row_buf, hidden_row, size_t(dm.hidden) * 4, cudaMemcpyHostToDevice, d->stream));
+    const int one = 1;
+    MTB_CK(d, cudaMemcpyAsync(&d->b.state->T, &one, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    launch_logits_row(d->model->dm, d->b, d->row_buf, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    MTB_CK(d, cudaMemcpyAsync(logits, d->b.logits, size_t(dm.vocab) * 4, cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaMemcpyAsync(&d->b.state->T, &saved_T, sizeof(int), cudaMemcpyHostToDevice, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_decoder_kv_read(mtb_decoder* d, int layer, int which, int pos0, int n_pos, float* out) {
+    if (!d || !out) return -1;
+    const ModelDims& dm = d->model->dm.dims;
+    if (layer < 0 || layer >= dm.n_layers || which < 0 || which > 1 || pos0 < 0 || n_pos < 0 || pos0 + n_pos > d->max_seq)
+        return fail(d->error, "kv range");
+    cudaSetDevice(d->device);
+    float* tmp = nullptr;
+    const size_t bytes = size_t(n_pos) * dm.n_kv * kHeadDim * 4;
+    MTB_CK(d, cudaMalloc(&tmp, bytes ? bytes : 4));
+    launch_kv_gather(d->model->dm, d->kv, layer, which, pos0, n_pos, tmp, d->stream);
+    cudaError_t e = cudaMemcpyAsync(out, tmp, bytes, cudaMemcpyDeviceToHost, d->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(d->error, cudaGetErrorString(e));
+    return 0;
+}
+
+int mtb_decoder_fill_synthetic_kv(mtb_decoder* d, int n_pos, uint32_t seed) {
+    if (!d || n_pos < 0 || n_pos > d->max_seq) return -1;
+    cudaSetDevice(d->device);
+    launch_fill_synthetic_kv(d->model->dm, d->kv, n_pos, seed, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    if (refresh(d)) return -1;
+    d->h_state->past = n_pos;
+    if (push_state(d)) return -1;
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params,
+                      int32_t* out_ids, int* n_out, mtb_counters* counters, mtb_draft_fn draft, mtb_commit_fn commit,
+                      void* user) {
+    if (!d || !out_ids || !n_out) return -1;
+    *n_out = 0;
+    try {
+        cudaSetDevice(d->device);
+        if (refresh(d)) return -1;
+        if (set_params(d, max_new, eos, params)) return -1;
+        if (prefill(d, fused, seq)) return -1;
+        StepState& s = *d->h_state;
+        const int vocab = d->model->dm.dims.vocab;
+        if (draft || commit) {
+            // One step per host round trip: the hooks see every proposal and commit.
+            std::vector<int32_t> prop(static_cast<size_t>(kTMax));
+            for (;;) {
+                if (refresh(d)) return -1;
+                MTB_CK(d, cudaMemcpyAsync(d->h_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
+                MTB_CK(d, cudaStreamSynchronize(d->stream));
+                if (s.stop != STOP_NONE) {
+                    if (commit) commit(user, d->h_ids, s.n_ids, s.past, 1);
+                    break;
+                }
+                int budget = std::min(s.k_max, s.max_new - s.n_ids);
+                budget = std::max(0, std::min(budget, s.max_seq - s.past - 1));
+                int mode = 0;
+                if (draft) {
+                    int np = draft(user, d->h_ids, s.n_ids, budget, prop.data());
+                    np = std::max(0, std::min(np, budget));
+                    for (int i = 0; i < np; ++i)
+                        if (prop[size_t(i)] < 0 || prop[size_t(i)] >= vocab) return fail(d->error, "invalid draft token");
+                    for (int i = 0; i < np; ++i) s.tokens[1 + i] = prop[size_t(i)];
+                    s.n_prop = np;
+                    if (push_state(d)) return -1;
+                    mode = 1;
+                }
+                if (run_step(d, mode)) return -1;
+                if (refresh(d)) return -1;
+                // The commit point precedes the next seed (src/cpu_speculative.cpp:154 then :119).
+                if (commit) {
+                    MTB_CK(d, cudaMemcpyAsync(d->h_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
+                    MTB_CK(d, cudaStreamSynchronize(d->stream));
+                    commit(user, d->h_ids, s.commit_n, s.past, s.commit_stop ? 1 : 0);
+                }
+                if (s.stop != STOP_NONE) break;
+            }
+        } else {
+            // Device-driven loop: the host only watches the stop flag, one step behind.
+            int i = 0;
+            for (;;) {
+                if (run_step(d, 0)) return -1;
+                MTB_CK(d, cudaMemcpyAsync(&d->h_flag[i & 1], &d->b.state->stop, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+                MTB_CK(d, cudaEventRecord(d->ev[i & 1], d->stream));
+                if (i > 0) {
+                    MTB_CK(d, cudaEventSynchronize(d->ev[(i - 1) & 1]));
+                    if (d->h_flag[(i - 1) & 1] != STOP_NONE) break;
+                }
+                ++i;
+            }
+            if (refresh(d)) return -1;
+        }
+        MTB_CK(d, cudaMemcpyAsync(out_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+        *n_out = s.n_ids;
+        fill_counters(s, counters);
+        return 0;
+    } catch (const std::exception& e) {
+        d->error = e.what();
+        return -1;
+    }
+}
+
+int mtb_greedy_generate(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, float penalty,
+                        int32_t* out_ids, int* n_out) {
+    const mtb_spec_params p{0, 2, 16, penalty};
+    mtb_counters c{};
+    return mtb_spec_generate(d, fused, seq, max_new, eos, &p, out_ids, n_out, &c, nullptr, nullptr, nullptr);
+}
+
+int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_new, int eos,
+               const mtb_spec_params* params) {
+    if (!d || !ids || n_ids <= 0) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    if (set_params(d, max_new, eos, params)) return -1;
+    if (n_ids > max_new) return fail(d->error, "n_ids exceeds max_new");
+    if (past < 0 || past + 1 > d->max_seq) return fail(d->error, "past out of range");
+    const int vocab = d->model->dm.dims.vocab;
+    for (int i = 0; i < n_ids; ++i)
+        if (ids[i] < 0 || ids[i] >= vocab) return fail(d->error, "invalid token id");
+    StepState& s = *d->h_state;
+    clear_progress(s);
+    s.past = past;
+    s.n_ids = n_ids;
+    s.seed = ids[n_ids - 1];
+    std::memcpy(d->h_ids, ids, size_t(n_ids) * 4);
+    MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->h_ids, size_t(n_ids) * 4, cudaMemcpyHostToDevice, d->stream));
+    if (push_state(d)) return -1;
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counters* counters) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    StepState& s = *d->h_state;
+    int mode = 0;
+    if (draft) {
+        if (n_draft < 0 || n_draft > kTMax - 1) return fail(d->error, "n_draft must be in [0, 15]");
+        const int vocab = d->model->dm.dims.vocab;
+        for (int i = 0; i < n_draft; ++i) {
+            if (draft[i] < 0 || draft[i] >= vocab) return fail(d->error, "invalid draft token");
+            s.tokens[1 + i] = draft[i];
+        }
+        s.n_prop = n_draft;
+        if (push_state(d)) return -1;
+        mode = 1;
+    }
+    if (run_step(d, mode)) return -1;
+    if (refresh(d)) return -1;
+    fill_counters(s, counters);
+    return 0;
+}
+
+int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    int mode = 0;
+    if (draft_device) {
+        if (n_draft < 0 || n_draft > kTMax - 1) return fail(d->error, "n_draft must be in [0, 15]");
+        launch_set_forced(d->b, draft_device, n_draft, d->model->dm.dims.vocab, d->stream);
+        MTB_CK(d, cudaGetLastError());
+        mode = 1;
+    }
+    cudaGraphExec_t g = step_graph(d, mode, d->h_state->penalty > 1.f);
+    if (!g) return fail(d->error, "could not build the verify-step graph");
+    MTB_CK(d, cudaGraphLaunch(g, d->stream));
+    return 0;
+}
+
+int mtb_snapshot_save(mtb_decoder* d) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaMemcpyAsync(d->snap_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToDevice, d->stream));
+    MTB_CK(d, cudaMemcpyAsync(d->snap_ids, d->b.ids, size_t(d->max_new) * 4, cudaMemcpyDeviceToDevice, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_snapshot_restore_async(mtb_decoder* d) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaMemcpyAsync(d->b.state, d->snap_state, sizeof(StepState), cudaMemcpyDeviceToDevice, d->stream));
+    MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->snap_ids, size_t(d->max_new) * 4, cudaMemcpyDeviceToDevice, d->stream));
+    return 0;
+}
+
+int mtb_read_ids(mtb_decoder* d, int32_t* out, int max_out, int* n_out, mtb_counters* counters) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (refresh(d)) return -1;
+    const int n = std::min(d->h_state->n_ids, std::max(0, max_out));
+    if (out && n > 0) {
+        MTB_CK(d, cudaMemcpyAsync(out, d->b.ids, size_t(n) * 4, cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+    }
+    if (n_out) *n_out = d->h_state->n_ids;
+    fill_counters(*d->h_state, counters);
+    return 0;
+}
+
+int mtb_sync(mtb_decoder* d) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    return 0;
+}
+
+int mtb_event_record(mtb_decoder* d, int slot) {
+    if (!d || slot < 2 || slot > 15) return -1;  // slots 0-1 are used by the generate loop
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaEventRecord(d->ev[slot], d->stream));
+    return 0;
+}
+
+int mtb_event_elapsed_ms(mtb_decoder* d, int a, int b, float* ms) {
+    if (!d || !ms || a < 2 || a > 15 || b < 2 || b > 15) return -1;
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaEventSynchronize(d->ev[b]));
+    MTB_CK(d, cudaEventElapsedTime(ms, d->ev[a], d->ev[b]));
+    return 0;
+}
+
+int mtb_step_kernel_launches(mtb_decoder* d) {
+    if (!d) return -1;
+    cudaSetDevice(d->device);
+    if (!step_graph(d, 1, d->h_state->penalty > 1.f)) return -1;
+    return d->launches;
+}
+
+int mtb_ngram_draft(mtb_decoder* d, const int32_t* history, int n, int maximum, int n_min, int n_max, int32_t* out,
+                    int* n_out) {
+    if (!d || !out || !n_out || n < 0 || n > d->max_new || (n > 0 && !history)) return -1;
+    if (n_min < 1 || n_max < n_min) return fail(d->error, "need 1 <= n_min <= n_max");
+    cudaSetDevice(d->device);
+    if (n > 0) MTB_CK(d, cudaMemcpyAsync(d->scratch_i, history, size_t(n) * 4, cudaMemcpyHostToDevice, d->stream));
+    int32_t* dev_out = d->scratch_i + n;  // the proposal never exceeds n ids; scratch holds max_new + 16
+    if (maximum > 16 && n + std::min(maximum, n) > d->max_new + 16) return fail(d->error, "history too long");
+    launch_draft_args(d->scratch_i, n, maximum, n_min, n_max, dev_out, d->scratch_n, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    int cnt = 0;
+    MTB_CK(d, cudaMemcpyAsync(&cnt, d->scratch_n, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    if (cnt > 0) {
+        MTB_CK(d, cudaMemcpyAsync(out, dev_out, size_t(cnt) * 4, cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+    }
+    *n_out = cnt;
+    return 0;
+}
+
+int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t* history, int n, float penalty,
+                      int32_t* choice) {
+    if (!d || !raw || !choice || n_raw <= 0 || n < 0 || n > d->max_new || (n > 0 && !history)) return -1;
+    if (n_raw > d->model->dm.dims.vocab) return fail(d->error, "more logits than the vocabulary");
+    cudaSetDevice(d->device);
+    MTB_CK(d, cudaMemcpyAsync(d->b.logits, raw, size_t(n_raw) * 4, cudaMemcpyHostToDevice, d->stream));
+    if (n > 0) MTB_CK(d, cudaMemcpyAsync(d->scratch_i, history, size_t(n) * 4, cudaMemcpyHostToDevice, d->stream));
+    launch_choice_args(d->b.logits, n_raw, d->scratch_i, n, penalty, d->scratch_n, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    int c = 0;
+    MTB_CK(d, cudaMemcpyAsync(&c, d->scratch_n, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    *choice = c;
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,957 @@
+// sm_100a kernels of the strict speculative verify step.
+//
+// One verify step = draft -> embed -> 28 x (norm+quantise, QKV, QK-norm+RoPE+
+// KV store, attention, O+residual, norm+quantise, gate/up+SwiGLU, quantise,
+// down+residual) -> final norm -> LM head with fused first-max -> accept and
+// rollback.  Every kernel reads the step's row count and positions from the
+// device StepState, so the whole step is one fixed launch sequence that is
+// captured once in a CUDA graph and replayed without host round trips.
+//
+// The layer arithmetic follows src/qwen3.cpp:62-218 of the reference; the
+// q8_0 contract (activation quantised to q8_0 before every q8_0 dot, exact
+// integer block sums, fp32 d_w*d_x scaling) follows ggml's CPU mul_mat as used
+// by src/cpu_projection.cpp:16-37.
+#include "kernels.hpp"
+
+#include <cuda_fp16.h>
+#include <cfloat>
+#include <cstdio>
+
+namespace mtb {
+
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    // D[16 tokens x 8 weight rows] = A[16 x 32] * B[32 x 8], int8 -> int32.
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint4 ld_stream_u4(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint2 ld_nc_u2(const uint8_t* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float h2f_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+__device__ __forceinline__ float h2f_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Byte offset of activation element (row r in 0..15, column c in 0..31) inside
+// one 512-byte block of the m16n8k32 A-fragment order: lane (g, t) holds
+// {A[g][4t..], A[g+8][4t..], A[g][16+4t..], A[g+8][16+4t..]}.
+__device__ __forceinline__ int frag_offset(int r, int c) {
+    const int g = r & 7, hi = r >> 3, t4 = (c & 15) >> 2, part = c >> 4;
+    return (g * 4 + t4) * 16 + (part * 2 + hi) * 4 + (c & 3);
+}
+
+// q8_0 quantisation of one 32-element block held one element per lane, as
+// ggml's x86 from_float: d = amax/127 (stored fp16), code = rint(x * 127/amax).
+__device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, uint8_t* act_q, float* act_d) {
+    const int lane = threadIdx.x & 31;
+    const float amax = warp_max(fabsf(v));
+    const float d = amax / 127.f;
+    const float id = amax != 0.0f ? 127.f / amax : 0.0f;
+    const int q = __float2int_rn(__fmul_rn(v, id));
+    act_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)q;
+    if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
+}
+
+__device__ __forceinline__ long long kv_offset(const KvCache& kv, int n_kv, int layer, int which, int head, int pos) {
+    const int page = kv.pages[pos / kPage];
+    return (long long)page * kv.page_elems +
+           ((((long long)layer * 2 + which) * n_kv + head) * kPage + (pos % kPage)) * kHeadDim;
+}
+
+__device__ __forceinline__ float kv_load(const KvCache& kv, long long off) {
+    return kv.type == KV_F16 ? __half2float(reinterpret_cast<const __half*>(kv.base)[off])
+                             : reinterpret_cast<const float*>(kv.base)[off];
+}
+
+__device__ __forceinline__ void kv_store(const KvCache& kv, long long off, float v) {
+    if (kv.type == KV_F16) reinterpret_cast<__half*>(kv.base)[off] = __float2half_rn(v);
+    else reinterpret_cast<float*>(kv.base)[off] = v;
+}
+
+// ------------------------------------------------------------------ repack
+
+// Raw ggml q8_0 rows (34-byte blocks) -> 544-byte tiles of 8 rows x 64 k:
+// lane (g, t) of a tile holds row g's bytes {4t, 16+4t} of both blocks, the
+// B fragment of m16n8k32; the 16 fp16 scales follow as [t][block][row&1].
+__global__ void k_repack_q8(const uint8_t* __restrict__ src, int n_rows, int k, uint8_t* __restrict__ dst,
+                            int rg_stride, int rg_offset) {
+    const int kt_n = k / kTileK;
+    const long long tiles = (long long)(n_rows / kTileRows) * kt_n;
+    const int blocks_per_row = k / kQ8Block;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < tiles * 32; i += (long long)gridDim.x * blockDim.x) {
+        const long long tile = i / 32;
+        const int lane = int(i % 32);
+        const int rg = int(tile / kt_n), kt = int(tile % kt_n);
+        const int g = lane >> 2, t = lane & 3;
+        const int row = rg * kTileRows + g;
+        uint8_t* out = dst + ((long long)(rg * rg_stride + rg_offset) * kt_n + kt) * kTileBytes;
+        uint8_t bytes[16];
+        for (int blk = 0; blk < 2; ++blk) {
+            const uint8_t* b = src + ((long long)row * blocks_per_row + kt * 2 + blk) * 34;
+            for (int j = 0; j < 4; ++j) {
+                bytes[blk * 8 + j] = b[2 + 4 * t + j];
+                bytes[blk * 8 + 4 + j] = b[2 + 16 + 4 * t + j];
+            }
+        }
+        for (int j = 0; j < 16; ++j) out[lane * 16 + j] = bytes[j];
+        if (lane < 16) {  // scales: lane -> (t', blk, j) = (lane>>2, (lane>>1)&1, lane&1)
+            const int tt = lane >> 2, blk = (lane >> 1) & 1, j = lane & 1;
+            const int srow = rg * kTileRows + 2 * tt + j;
+            const uint8_t* b = src + ((long long)srow * blocks_per_row + kt * 2 + blk) * 34;
+            out[512 + lane * 2] = b[0];
+            out[512 + lane * 2 + 1] = b[1];
+        }
+    }
+}
+
+// ------------------------------------------------------------------ GEMV
+
+enum Epi { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+
+struct GemvArgs {
+    const uint8_t* w;     // tiles
+    int n_rg;             // row groups of 8
+    int kt_n;             // K / 64
+    const uint8_t* act_q; // fragment-order activation, K/32 blocks of 512 bytes
+    const float* act_d;   // [K/32][16]
+    float* out;           // EPI_STORE / EPI_SWIGLU: [16][ld]; EPI_RESID: x [16][ld]
+    int ld;               // output row stride (floats)
+    const StepState* state;
+    float2* lm_val;       // EPI_ARGMAX partials [gridDim.x][16]
+    float* logits;        // EPI_ARGMAX: optional full logits [16][ld]
+};
+
+// Skinny q8_0 GEMM: y[t][n] = sum_blocks dw[n,b] * dx[t,b] * sum_32 qw * qx for
+// up to 16 rows t.  RPB row groups per CTA iteration; the 8 warps split as
+// RPB groups x (8/RPB) K-slices, reduced in a fixed order (deterministic).
+template <int EPI, int RPB>
+__global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int kb_n = a.kt_n * 2;
+    uint4* s_act = reinterpret_cast<uint4*>(smem);                       // [kb_n][32]
+    float* s_d = reinterpret_cast<float*>(s_act + kb_n * 32);            // [kb_n][16]
+    float* s_red = s_d + kb_n * 16;                                      // [8][32][4]
+    const int T = a.state->T;
+    if (T <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(a.act_q);
+        for (int i = threadIdx.x; i < kb_n * 32; i += kThreads) s_act[i] = src[i];
+        for (int i = threadIdx.x; i < kb_n * 16; i += kThreads) s_d[i] = a.act_d[i];
+    }
+    __syncthreads();
+    constexpr int WPR = kWarps / RPB;   // warps per row group
+    const int r = warp % RPB, slice = warp / RPB;
+    float best_v[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0x7fffffff, 0x7fffffff};
+
+    for (int rg0 = blockIdx.x * RPB; rg0 < a.n_rg; rg0 += gridDim.x * RPB) {
+        const int rg = rg0 + r;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (rg < a.n_rg) {
+            const uint8_t* wrow = a.w + (size_t)rg * a.kt_n * kTileBytes;
+            constexpr int U = 4;
+            for (int kt0 = slice; kt0 < a.kt_n; kt0 += WPR * U) {
+                uint4 wv[U];
+                uint2 sv[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int kt = kt0 + u * WPR;
+                    if (kt < a.kt_n) {
+                        wv[u] = ld_stream_u4(wrow + (size_t)kt * kTileBytes + lane * 16);
+                        sv[u] = ld_nc_u2(wrow + (size_t)kt * kTileBytes + 512 + t * 8);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int kt = kt0 + u * WPR;
+                    if (kt < a.kt_n) {
+                        int c0[4], c1[4];
+                        mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv[u].x, wv[u].y);
+                        mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv[u].z, wv[u].w);
+                        const float x0g = s_d[(2 * kt) * 16 + g], x0h = s_d[(2 * kt) * 16 + g + 8];
+                        const float x1g = s_d[(2 * kt + 1) * 16 + g], x1h = s_d[(2 * kt + 1) * 16 + g + 8];
+                        const float w00 = h2f_lo(sv[u].x), w01 = h2f_hi(sv[u].x);  // block 0, rows 2t, 2t+1
+                        const float w10 = h2f_lo(sv[u].y), w11 = h2f_hi(sv[u].y);  // block 1
+                        acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
+                        acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
+                        acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
+                        acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+                        acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
+                        acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
+                        acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
+                        acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+                    }
+                }
+            }
+        }
+        if (WPR > 1) {
+            float4* red = reinterpret_cast<float4*>(s_red);
+            red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (slice == 0) {
+                for (int s2 = 1; s2 < WPR; ++s2) {
+                    const float4 o = red[(s2 * RPB + r) * 32 + lane];
+                    acc[0] += o.x; acc[1] += o.y; acc[2] += o.z; acc[3] += o.w;
+                }
+            }
+        }
+        if (EPI == EPI_SWIGLU) {
+            // Row groups alternate gate (even) / up (odd): the gate warp pairs
+            // with the up warp r + 1 through shared memory.
+            float4* ys = reinterpret_cast<float4*>(s_red) + kWarps * 32;
+            if (slice == 0 && (r & 1)) ys[r * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            __syncthreads();
+            if (slice == 0 && !(r & 1) && rg < a.n_rg) {
+                const float4 u = ys[(r + 1) * 32 + lane];
+                const float uu[4] = {u.x, u.y, u.z, u.w};
+                const int feat = (rg >> 1) * kTileRows + 2 * t;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int row = g + (j >> 1) * 8;
+                    if (row < T) {
+                        const float gv = acc[j];
+                        const float sl = gv / (1.0f + expf(-gv));
+                        a.out[(size_t)row * a.ld + feat + (j & 1)] = sl * uu[j];
+                    }
+                }
+            }
+        } else if (slice == 0 && rg < a.n_rg) {
+            const int n0 = rg * kTileRows + 2 * t;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int row = g + (j >> 1) * 8;
+                const int col = n0 + (j & 1);
+                if (row >= T) continue;
+                float* o = a.out + (size_t)row * a.ld + col;
+                if (EPI == EPI_STORE) *o = acc[j];
+                if (EPI == EPI_RESID) *o = *o + acc[j];
+                if (EPI == EPI_ARGMAX) {
+                    if (a.logits) a.logits[(size_t)row * a.ld + col] = acc[j];
+                    const int slot = j >> 1;
+                    if (acc[j] > best_v[slot] || (acc[j] == best_v[slot] && col < best_i[slot])) {
+                        best_v[slot] = acc[j];
+                        best_i[slot] = col;
+                    }
+                }
+            }
+        }
+        if (WPR > 1 || EPI == EPI_SWIGLU) __syncthreads();
+    }
+    if (EPI == EPI_ARGMAX) {
+        // Reduce (value, first index) over the 4 lanes of a row group, then
+        // over the RPB leader warps, then write this CTA's partial per row.
+#pragma unroll
+        for (int slot = 0; slot < 2; ++slot) {
+#pragma unroll
+            for (int o = 1; o < 4; o <<= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, best_v[slot], o);
+                const int oi = __shfl_xor_sync(0xffffffffu, best_i[slot], o);
+                if (ov > best_v[slot] || (ov == best_v[slot] && oi < best_i[slot])) {
+                    best_v[slot] = ov;
+                    best_i[slot] = oi;
+                }
+            }
+        }
+        float2* cand = reinterpret_cast<float2*>(s_red);  // [RPB][16]
+        if (slice == 0 && t == 0) {
+            cand[r * 16 + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
+            cand[r * 16 + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
+        }
+        __syncthreads();
+        if (threadIdx.x < 16) {
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int rr = 0; rr < RPB; ++rr) {
+                const float2 c = cand[rr * 16 + threadIdx.x];
+                const int ci = __float_as_int(c.y);
+                if (c.x > bv || (c.x == bv && ci < bi)) { bv = c.x; bi = ci; }
+            }
+            a.lm_val[blockIdx.x * 16 + threadIdx.x] = make_float2(bv, __int_as_float(bi));
+        }
+    }
+}
+
+template <int EPI, int RPB>
+void gemv(const GemvArgs& a, int grid, cudaStream_t s) {
+    const int kb_n = a.kt_n * 2;
+    const size_t smem = (size_t)kb_n * 32 * 16 + (size_t)kb_n * 16 * 4 + (size_t)kWarps * 32 * 16 * 2;
+    k_gemv<EPI, RPB><<<grid, kThreads, smem, s>>>(a);
+}
+
+// ------------------------------------------------------------ norms, quant
+
+// RMSNorm (double sum of float squares, 1/sqrtf(mean+eps), (x*s)*w) of each
+// of the 16 rows, quantised to the fragment order; rows >= T become zero.
+// Optionally stores the normed f32 rows (final norm -> hidden).
+__global__ void __launch_bounds__(kThreads) k_rmsnorm_quant(const StepState* st, const float* __restrict__ x, int K,
+                                                            const float* __restrict__ w, float eps,
+                                                            uint8_t* act_q, float* act_d, float* normed) {
+    const int row = blockIdx.x;
+    const int T = st->T;
+    if (T <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ double s_part[kWarps];
+    __shared__ float s_scale;
+    const bool live = row < T;
+    if (live) {
+        double sum = 0.0;
+        for (int i = threadIdx.x; i < K; i += kThreads) {
+            const float v = x[(size_t)row * K + i];
+            sum += (double)(v * v);
+        }
+        sum = warp_sum_d(sum);
+        if (lane == 0) s_part[warp] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double tot = 0.0;
+            for (int i = 0; i < kWarps; ++i) tot += s_part[i];
+            const float mean = (float)(tot / K);
+            s_scale = 1.0f / sqrtf(mean + eps);
+        }
+        __syncthreads();
+    }
+    const float scale = live ? s_scale : 0.f;
+    for (int blk = warp; blk < K / 32; blk += kWarps) {
+        const int i = blk * 32 + lane;
+        float v = 0.f;
+        if (live) {
+            v = __fmul_rn(__fmul_rn(x[(size_t)row * K + i], scale), w[i]);
+            if (normed) normed[(size_t)row * K + i] = v;
+        }
+        quantize_block_lane(v, row, blk, act_q, act_d);
+    }
+}
+
+// Plain quantisation of f32 rows [16][K] (rows >= T -> zero).
+__global__ void __launch_bounds__(kThreads) k_quant_rows(const StepState* st, const float* __restrict__ x, int K,
+                                                         uint8_t* act_q, float* act_d) {
+    const int T = st->T;
+    if (T <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = K / 32;
+    for (int item = blockIdx.x * kWarps + warp; item < nb * kTMax; item += gridDim.x * kWarps) {
+        const int row = item / nb, blk = item % nb;
+        const float v = row < T ? x[(size_t)row * K + blk * 32 + lane] : 0.f;
+        quantize_block_lane(v, row, blk, act_q, act_d);
+    }
+}
+
+// Per-head RMSNorm + NEOX RoPE of q and k (src/qwen3.cpp:104-118), then the
+// KV store of k and v at positions before+t (src/qwen3.cpp:123-140).
+// grid (kTMax, n_heads + n_kv), block 128.
+__global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st, float* qkv, int n_heads, int n_kv,
+                                                            const float* __restrict__ q_norm,
+                                                            const float* __restrict__ k_norm, float eps,
+                                                            float theta_scale, KvCache kv, int layer) {
+    const int T = st->T;
+    const int row = blockIdx.x, hh = blockIdx.y;
+    if (row >= T) return;
+    const int pos = st->before + row;
+    const int ld = (n_heads + 2 * n_kv) * kHeadDim;
+    const bool is_q = hh < n_heads;
+    float* src = qkv + (size_t)row * ld + (size_t)hh * kHeadDim;
+    const float* w = is_q ? q_norm : k_norm;
+    const int d = threadIdx.x;
+    __shared__ double s_part[4];
+    __shared__ float s_y[kHeadDim];
+    const float xv = src[d];
+    double sq = warp_sum_d((double)(xv * xv));
+    if ((d & 31) == 0) s_part[d >> 5] = sq;
+    __syncthreads();
+    const double tot = s_part[0] + s_part[1] + s_part[2] + s_part[3];
+    const float mean = (float)(tot / kHeadDim);
+    const float scale = 1.0f / sqrtf(mean + eps);
+    s_y[d] = __fmul_rn(__fmul_rn(xv, scale), w[d]);
+    __syncthreads();
+    if (d < kHeadDim / 2) {
+        float theta = (float)pos;
+        for (int i = 0; i < d; ++i) theta = __fmul_rn(theta, theta_scale);
+        const float c = cosf(theta), s = sinf(theta);
+        const float x0 = s_y[d], x1 = s_y[d + kHeadDim / 2];
+        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+        const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+        if (is_q) {
+            src[d] = y0;
+            src[d + kHeadDim / 2] = y1;
+        } else {
+            const int head = hh - n_heads;
+            const long long off = kv_offset(kv, n_kv, layer, 0, head, pos);
+            kv_store(kv, off + d, y0);
+            kv_store(kv, off + d + kHeadDim / 2, y1);
+        }
+    }
+    if (!is_q) {
+        const int head = hh - n_heads;
+        const float vv = qkv[(size_t)row * ld + (size_t)(n_heads + n_kv + head) * kHeadDim + d];
+        kv_store(kv, kv_offset(kv, n_kv, layer, 1, head, pos) + d, vv);
+    }
+}
+
+// ------------------------------------------------------------ attention
+
+// Split-KV causal GQA attention, one CTA per (64-position chunk, kv head):
+// scores q.k * 1/sqrt(128), query row t sees positions < before + t + 1
+// (src/qwen3_decoder.cpp:142-148), chunk-local max / exp-sum / P.V partials.
+__global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, const float* __restrict__ qkv, int n_heads,
+                                                         int n_kv, KvCache kv, int layer, float* part_o,
+                                                         float2* part_ml, int max_chunks) {
+    const int T = st->T;
+    if (T <= 0) return;
+    const int before = st->before;
+    const int kv_len = before + T;
+    const int c = blockIdx.x, h = blockIdx.y;
+    if (c * kPage >= kv_len) return;
+    const int G = n_heads / n_kv;
+    const int NQ = T * G;
+    const int ld = (n_heads + 2 * n_kv) * kHeadDim;
+    extern __shared__ __align__(16) float sm[];
+    float* sq = sm;                              // [NQ][128]
+    float* sk = sq + kTMax * 4 * kHeadDim;       // [64][129]  (group <= 4)
+    float* sp = sk + kPage * (kHeadDim + 1);     // [NQ][64]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < NQ * kHeadDim; i += kThreads) {
+        const int q = i / kHeadDim, d = i % kHeadDim;
+        const int t = q / G, j = q % G;
+        sq[i] = qkv[(size_t)t * ld + (size_t)(h * G + j) * kHeadDim + d];
+    }
+    const int p0 = c * kPage;
+    const int n_pos = min(kPage, kv_len - p0);
+    const long long koff = kv_offset(kv, n_kv, layer, 0, h, p0);
+    const long long voff = kv_offset(kv, n_kv, layer, 1, h, p0);
+    for (int i = tid; i < n_pos * kHeadDim; i += kThreads) {
+        const int p = i / kHeadDim, d = i % kHeadDim;
+        sk[p * (kHeadDim + 1) + d] = kv_load(kv, koff + i);
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)kHeadDim);
+    for (int i = tid; i < NQ * kPage; i += kThreads) {
+        const int q = i / kPage, p = i % kPage;
+        const int t = q / G;
+        const int pos = p0 + p;
+        float s = -INFINITY;
+        if (p < n_pos && pos < before + t + 1) {
+            const float* qa = sq + q * kHeadDim;
+            const float* ka = sk + p * (kHeadDim + 1);
+            float acc = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qa[d], ka[d], acc);
+            s = acc * scale;
+        }
+        sp[q * kPage + p] = s;
+    }
+    __syncthreads();
+    for (int q = warp; q < NQ; q += kWarps) {
+        const float a0 = sp[q * kPage + lane], a1 = sp[q * kPage + lane + 32];
+        const float m = warp_max(fmaxf(a0, a1));
+        const float e0 = m == -INFINITY ? 0.f : expf(a0 - m);
+        const float e1 = m == -INFINITY ? 0.f : expf(a1 - m);
+        const float l = warp_sum(e0 + e1);
+        sp[q * kPage + lane] = e0;
+        sp[q * kPage + lane + 32] = e1;
+        if (lane == 0) part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q] = make_float2(m, l);
+    }
+    __syncthreads();
+    for (int i = tid; i < n_pos * kHeadDim; i += kThreads) {
+        const int p = i / kHeadDim, d = i % kHeadDim;
+        sk[p * (kHeadDim + 1) + d] = kv_load(kv, voff + i);
+    }
+    __syncthreads();
+    for (int i = tid; i < NQ * kHeadDim; i += kThreads) {
+        const int q = i / kHeadDim, d = i % kHeadDim;
+        const float* pr = sp + q * kPage;
+        float acc = 0.f;
+        for (int p = 0; p < n_pos; ++p) acc = fmaf(pr[p], sk[p * (kHeadDim + 1) + d], acc);
+        part_o[(((size_t)h * max_chunks + c) * (kTMax * 4) + q) * kHeadDim + d] = acc;
+    }
+}
+
+// Merge the chunk partials of one (row, head): grid (kTMax, n_heads), block 128.
+__global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n_heads, int n_kv,
+                                                      const float* part_o, const float2* part_ml, int max_chunks,
+                                                      float* attn_out) {
+    const int T = st->T;
+    const int t = blockIdx.x, head = blockIdx.y;
+    if (t >= T) return;
+    const int G = n_heads / n_kv;
+    const int h = head / G, q = t * G + head % G;
+    const int kv_len = st->before + T;
+    const int n_chunks = (kv_len + kPage - 1) / kPage;
+    float M = -INFINITY;
+    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q].x);
+    float L = 0.f, o = 0.f;
+    for (int c = 0; c < n_chunks; ++c) {
+        const float2 ml = part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q];
+        if (ml.x == -INFINITY) continue;
+        const float wgt = expf(ml.x - M);
+        L = fmaf(wgt, ml.y, L);
+        o = fmaf(wgt, part_o[(((size_t)h * max_chunks + c) * (kTMax * 4) + q) * kHeadDim + threadIdx.x], o);
+    }
+    attn_out[(size_t)t * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = o / L;
+}
+
+// ------------------------------------------------------------ embed, draft, accept
+
+// q8_0 row dequant (d * q) of the step's tokens from the token_embd tiles
+// (src/generate.cpp:33-66); rows >= T are zeroed.
+__global__ void k_embed(StepState* st, const uint8_t* __restrict__ embd, int hidden, int vocab, float* x) {
+    const int row = blockIdx.x;
+    const int T = st->T;
+    if (T <= 0) return;
+    const int kt_n = hidden / kTileK;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v = 0.f;
+        if (row < T) {
+            int id = st->tokens[row];
+            if (id < 0 || id >= vocab) {  // ids are validated on the host; never read out of bounds
+                if (i == 0) st->error = 1;
+                id = 0;
+            }
+            const int rg = id / kTileRows, g = id % kTileRows;
+            const int kt = i / kTileK, blk = (i % kTileK) / 32, cc = i % 32;
+            const uint8_t* tile = embd + ((size_t)rg * kt_n + kt) * kTileBytes;
+            const int t4 = (cc & 15) >> 2, part = cc >> 4;
+            const int8_t q = (int8_t)tile[(g * 4 + t4) * 16 + blk * 8 + part * 4 + (cc & 3)];
+            const unsigned short hb = *reinterpret_cast<const unsigned short*>(tile + 512 + ((g >> 1) * 4 + blk * 2 + (g & 1)) * 2);
+            v = (float)q * __half2float(__ushort_as_half(hb));
+        }
+        x[(size_t)row * hidden + i] = v;
+    }
+}
+
+// Emit one id into the generated stream (src/cpu_speculative.cpp:108-116).
+__device__ void emit_id(StepState* st, int32_t* ids, int id) {
+    ids[st->n_ids++] = id;
+    if (id == st->eos) st->stop = STOP_EOS;
+    else if (st->n_ids >= st->max_new) st->stop = STOP_LIMIT;
+}
+
+// n-gram draft over the generated ids (src/cpu_speculative.cpp:45-56): the
+// longest suffix size in [n_min, n_max] with an earlier occurrence, latest
+// occurrence first.  For each end position e < n the common suffix length
+// c(e) of ids[0:e] and ids[0:n] (capped at n_max) is computed; the answer is
+// the largest c >= n_min, then the largest e with that c.  The proposal is
+// ids[e : e + min(budget, n - e)].  Called by a whole CTA (blockDim % 32 == 0,
+// <= 1024 threads); returns e (or -1) in every thread.
+__device__ int draft_search(const int32_t* __restrict__ ids, int n, int budget, int n_min, int n_max) {
+    __shared__ unsigned long long s_best[32];
+    const int top = min(n_max, n - 1);
+    unsigned long long best = 0;
+    if (budget > 0 && n >= 2 && n >= n_min + 1 && top >= n_min) {
+        for (int e = threadIdx.x + 1; e < n; e += blockDim.x) {
+            int c = 0;
+            while (c < top && c < e && ids[e - 1 - c] == ids[n - 1 - c]) ++c;
+            if (c >= n_min) {
+                const unsigned long long key = ((unsigned long long)c << 32) | (unsigned)e;
+                best = key > best ? key : best;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+    }
+    if ((threadIdx.x & 31) == 0) s_best[threadIdx.x >> 5] = best;
+    __syncthreads();
+    best = 0;
+    for (int i = 0; i < (int)(blockDim.x / 32); ++i) best = s_best[i] > best ? s_best[i] : best;
+    __syncthreads();
+    return best ? (int)(best & 0xffffffffu) : -1;
+}
+
+__global__ void __launch_bounds__(256) k_draft(StepState* st, const int32_t* __restrict__ ids) {
+    if (st->stop != STOP_NONE) {
+        if (threadIdx.x == 0) st->T = 0;
+        return;
+    }
+    const int n = st->n_ids;
+    int budget = min(st->k_max, st->max_new - n);
+    budget = max(min(budget, st->max_seq - st->past - 1), 0);
+    const int e = draft_search(ids, n, budget, st->n_min, st->n_max);
+    if (threadIdx.x == 0) {
+        int np = 0;
+        st->tokens[0] = st->seed;
+        if (e >= 0) {
+            np = min(budget, n - e);
+            for (int i = 0; i < np; ++i) st->tokens[1 + i] = ids[e + i];
+        }
+        st->n_prop = np;
+        st->T = 1 + np;
+        st->before = st->past;
+    }
+}
+
+// The same search on explicit arguments (mtb_ngram_draft).
+__global__ void __launch_bounds__(256) k_draft_args(const int32_t* __restrict__ ids, int n, int maximum, int n_min,
+                                                    int n_max, int32_t* out, int* n_out) {
+    const int e = draft_search(ids, n, maximum, n_min, n_max);
+    if (threadIdx.x == 0) {
+        const int np = e >= 0 ? min(maximum, n - e) : 0;
+        for (int i = 0; i < np; ++i) out[i] = ids[e + i];
+        *n_out = np;
+    }
+}
+
+// Host-forced proposal already in tokens[1..n_prop]: clamp to the budget.
+__global__ void k_draft_forced(StepState* st) {
+    if (st->stop != STOP_NONE) { st->T = 0; return; }
+    int budget = min(st->k_max, st->max_new - st->n_ids);
+    budget = max(min(budget, st->max_seq - st->past - 1), 0);
+    st->n_prop = max(0, min(st->n_prop, budget));
+    st->tokens[0] = st->seed;
+    st->T = 1 + st->n_prop;
+    st->before = st->past;
+}
+
+// First max over the CTA partials of the fused LM head, for rows < T.
+__device__ void reduce_choices(StepState* st, const float2* lm_val, int lm_blocks) {
+    const int T = st->T;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int row = warp; row < T; row += blockDim.x / 32) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int b = lane; b < lm_blocks; b += 32) {
+            const float2 c = lm_val[b * 16 + row];
+            const int ci = __float_as_int(c.y);
+            if (c.x > bv || (c.x == bv && ci < bi)) { bv = c.x; bi = ci; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) st->choice[row] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+// Strict acceptance and logical rollback (src/cpu_speculative.cpp:142-153),
+// then the next seed (the choice of the last kept row, :119).
+__global__ void k_accept(StepState* st, int32_t* ids, const float2* lm_val, int lm_blocks, int choices_ready) {
+    if (st->T <= 0) return;
+    if (!choices_ready) reduce_choices(st, lm_val, lm_blocks);
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    const int np = st->n_prop;
+    st->target_calls += 1;
+    st->drafted_calls += np > 0;
+    st->proposed += np;
+    st->target_input_tokens += st->T;
+    int keep = 1;
+    for (int i = 0; i < np; ++i) {
+        const int prop = st->tokens[1 + i];
+        if (prop != st->choice[i]) break;
+        st->accepted += 1;
+        emit_id(st, ids, prop);
+        if (st->stop) break;  // the terminating token is not kept in the cache
+        ++keep;
+    }
+    const int position = st->before + keep;
+    if (st->before + st->T != position) st->rewinds += 1;
+    st->past = position;
+    st->commit_n = st->n_ids;
+    st->commit_stop = st->stop != STOP_NONE;
+    if (!st->stop) {
+        st->seed = st->choice[keep - 1];
+        emit_id(st, ids, st->seed);
+    }
+}
+
+// Seed after prefill: the choice of the last prefilled row, emitted.
+__global__ void k_prefill_seed(StepState* st, int32_t* ids, const float2* lm_val, int lm_blocks, int choices_ready) {
+    if (!choices_ready) reduce_choices(st, lm_val, lm_blocks);
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    st->seed = st->choice[st->T - 1];
+    emit_id(st, ids, st->seed);
+}
+
+// Penalised first max (src/cpu_speculative.cpp:57-68) of one logits row by a
+// CTA of 1024 threads: the recent set is the last 100 of hist[0:n_hist] +
+// extra[0:n_extra]; adjusted values x>0 ? x/p : x*p; the lowest index wins a
+// tie (NaN entries never win).  `bits` is a dynamic shared bitmap of vocab bits.
+__device__ int choice_block(const float* __restrict__ lr, int vocab, const int32_t* hist, int n_hist,
+                            const int* extra, int n_extra, float p, unsigned int* bits) {
+    const int words = (vocab + 31) / 32;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) bits[i] = 0;
+    __syncthreads();
+    const int len = n_hist + n_extra;
+    if (p > 1.f)
+        for (int i = max(0, len - 100) + threadIdx.x; i < len; i += blockDim.x) {
+            const int id = i < n_hist ? hist[i] : extra[i - n_hist];
+            if (id >= 0 && id < vocab) atomicOr(&bits[id >> 5], 1u << (id & 31));
+        }
+    __syncthreads();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        float v = lr[i];
+        if ((bits[i >> 5] >> (i & 31)) & 1u) v = v > 0 ? v / p : v * p;
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    __shared__ float s_v[32];
+    __shared__ int s_i[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { s_v[threadIdx.x >> 5] = bv; s_i[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    for (int w = 0; w < (int)(blockDim.x / 32); ++w) {
+        const float ov = s_v[w];
+        const int oi = s_i[w];
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    __syncthreads();
+    // NaN never wins a strict '>' comparison; a NaN at index 0 keeps index 0.
+    if (isnan(lr[0]) || bi == 0x7fffffff) return 0;
+    return bi;
+}
+
+// Per verify row i: history = ids[0:n_ids] + proposals[0:i].  grid (kTMax).
+__global__ void __launch_bounds__(1024) k_choice_penalty(StepState* st, const int32_t* ids, const float* logits,
+                                                          int vocab) {
+    extern __shared__ unsigned int bits[];
+    const int T = st->T;
+    const int row = blockIdx.x;
+    if (row >= T) return;
+    const int c = choice_block(logits + (size_t)row * vocab, vocab, ids, st->n_ids, st->tokens + 1, row,
+                               st->penalty, bits);
+    if (threadIdx.x == 0) st->choice[row] = c;
+}
+
+// mtb_greedy_choice on explicit arguments.
+__global__ void __launch_bounds__(1024) k_choice_args(const float* logits, int n_raw, const int32_t* hist, int n_hist,
+                                                      float p, int* out) {
+    extern __shared__ unsigned int bits[];
+    const int c = choice_block(logits, n_raw, hist, n_hist, nullptr, 0, p, bits);
+    if (threadIdx.x == 0) *out = c;
+}
+
+// Proposal from device memory (asynchronous step API); ids are range-checked.
+__global__ void k_set_forced(StepState* st, const int32_t* src, int n, int vocab) {
+    for (int i = 0; i < n; ++i) {
+        int id = src[i];
+        if (id < 0 || id >= vocab) { st->error = 1; id = 0; }
+        st->tokens[1 + i] = id;
+    }
+    st->n_prop = n;
+}
+
+// Host-supplied rows (prefill chunks, run()): positions before..before+T-1.
+__global__ void k_rows_begin(StepState* st, int T) {
+    st->before = st->past;
+    st->T = T;
+}
+__global__ void k_rows_end(StepState* st) { st->past = st->before + st->T; }
+
+// ------------------------------------------------------------ synthetic KV
+
+__device__ __forceinline__ uint32_t mix32(uint32_t x) {
+    x ^= x >> 16; x *= 0x7feb352du; x ^= x >> 15; x *= 0x846ca68bu; x ^= x >> 16;
+    return x;
+}
+
+// Same values as the oracle's orc_synthetic_kv_value: Irwin-Hall(4) of a
+// 32-bit hash, scaled to unit variance and rounded to fp16.
+__device__ __forceinline__ float synthetic_kv_value(uint32_t seed, int layer, int which, int pos, int head, int dim) {
+    uint32_t h = mix32(seed + 0x9E3779B9u * (uint32_t)(layer * 2 + which + 1));
+    h = mix32(h ^ ((uint32_t)pos * 0x85EBCA6Bu));
+    h = mix32(h ^ ((uint32_t)(head * 1024 + dim) * 0xC2B2AE35u));
+    const uint32_t g = mix32(h ^ 0x68E31DA4u);
+    const int s = (int)(h & 0xffffu) + (int)(h >> 16) + (int)(g & 0xffffu) + (int)(g >> 16) - 131070;
+    return __half2float(__float2half_rn(__fmul_rn((float)s, 2.642912e-05f)));
+}
+
+__global__ void k_fill_synthetic_kv(KvCache kv, int n_layers, int n_kv, int n_pos, uint32_t seed) {
+    const long long total = (long long)n_layers * 2 * n_kv * n_pos * kHeadDim;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int d = int(i % kHeadDim);
+        long long r = i / kHeadDim;
+        const int pos = int(r % n_pos); r /= n_pos;
+        const int head = int(r % n_kv); r /= n_kv;
+        const int which = int(r % 2);
+        const int layer = int(r / 2);
+        kv_store(kv, kv_offset(kv, n_kv, layer, which, head, pos) + d, synthetic_kv_value(seed, layer, which, pos, head, d));
+    }
+}
+
+__global__ void k_kv_gather(KvCache kv, int n_kv, int layer, int which, int pos0, int n_pos, float* out) {
+    const long long total = (long long)n_pos * n_kv * kHeadDim;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int d = int(i % kHeadDim);
+        const int head = int((i / kHeadDim) % n_kv);
+        const int p = int(i / ((long long)kHeadDim * n_kv));
+        out[i] = kv_load(kv, kv_offset(kv, n_kv, layer, which, head, pos0 + p) + d);
+    }
+}
+
+}  // namespace
+
+// ============================================================ launchers
+
+void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int rg_stride, int rg_offset,
+                      cudaStream_t s) {
+    const long long work = (long long)(n_rows / kTileRows) * (k / kTileK) * 32;
+    const int grid = (int)std::min<long long>((work + 255) / 256, 148LL * 16);
+    k_repack_q8<<<grid, 256, 0, s>>>(src, n_rows, k, dst, rg_stride, rg_offset);
+}
+
+int lm_head_blocks(int vocab) {
+    const int n_rg = vocab / kTileRows;
+    return std::min(148 * 4, (n_rg + 7) / 8);
+}
+
+cudaError_t configure_kernels() {
+    // Dynamic shared memory above 48 KB is opt-in per kernel (current device).
+    cudaFuncSetAttribute(k_gemv<EPI_STORE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_gemv<EPI_RESID, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_gemv<EPI_SWIGLU, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_gemv<EPI_ARGMAX, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    return cudaGetLastError();
+}
+
+// Layers, final norm and (optionally) the LM head for the rows in b.x.
+static void forward_layers(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, cudaStream_t s) {
+    const ModelDims& d = m.dims;
+    const int H = d.hidden, F = d.ffn;
+    const int qd = d.n_heads * kHeadDim, kd = d.n_kv * kHeadDim;
+    const int G = d.n_heads / d.n_kv;
+    const size_t attn_smem = (size_t)(kTMax * 4 * kHeadDim + kPage * (kHeadDim + 1) + kTMax * 4 * kPage) * sizeof(float);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const LayerWeights& w = m.layers[l];
+        k_rmsnorm_quant<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.attn_norm, d.eps, b.act_q, b.act_d, nullptr);
+        {
+            GemvArgs a{w.qkv, (qd + 2 * kd) / kTileRows, H / kTileK, b.act_q, b.act_d, b.qkv, qd + 2 * kd, b.state, nullptr, nullptr};
+            gemv<EPI_STORE, 2>(a, (a.n_rg + 1) / 2, s);
+        }
+        k_qk_norm_rope_store<<<dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, w.q_norm,
+                                                                             w.k_norm, d.eps, m.theta_scale, kv, l);
+        k_attn_chunk<<<dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, kv, l,
+                                                                              b.part_o, b.part_ml, b.max_chunks);
+        k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
+                                                              b.max_chunks, b.attn_out);
+        k_quant_rows<<<(qd / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, b.attn_out, qd, b.act_q, b.act_d);
+        {
+            GemvArgs a{w.o, H / kTileRows, qd / kTileK, b.act_q, b.act_d, b.x, H, b.state, nullptr, nullptr};
+            gemv<EPI_RESID, 1>(a, a.n_rg, s);
+        }
+        k_rmsnorm_quant<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.ffn_norm, d.eps, b.act_q, b.act_d, nullptr);
+        {
+            GemvArgs a{w.gu, 2 * F / kTileRows, H / kTileK, b.act_q, b.act_d, b.gu, F, b.state, nullptr, nullptr};
+            gemv<EPI_SWIGLU, 2>(a, a.n_rg / 2, s);
+        }
+        k_quant_rows<<<(F / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, b.gu, F, b.act_q, b.act_d);
+        {
+            GemvArgs a{w.down, H / kTileRows, F / kTileK, b.act_q, b.act_d, b.x, H, b.state, nullptr, nullptr};
+            gemv<EPI_RESID, 1>(a, a.n_rg, s);
+        }
+    }
+    (void)G;
+    k_rmsnorm_quant<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, b.act_q, b.act_d, b.hid);
+}
+
+static void lm_head(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {
+    GemvArgs a{m.embd, m.dims.vocab / kTileRows, m.dims.hidden / kTileK, b.act_q, b.act_d,
+               nullptr, m.dims.vocab, b.state, b.lm_val, want_logits ? b.logits : nullptr};
+    gemv<EPI_ARGMAX, 8>(a, b.lm_blocks, s);
+}
+
+void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, int draft_mode, bool want_logits,
+                 cudaStream_t s) {
+    if (draft_mode == 0) k_draft<<<1, 256, 0, s>>>(b.state, b.ids);
+    else if (draft_mode == 1) k_draft_forced<<<1, 1, 0, s>>>(b.state);
+    k_embed<<<kTMax, 256, 0, s>>>(b.state, m.embd, m.dims.hidden, m.dims.vocab, b.x);
+    forward_layers(m, kv, b, s);
+    const bool penalty_path = want_logits;
+    lm_head(m, b, penalty_path, s);
+    if (penalty_path) {
+        const size_t bits = (size_t)((m.dims.vocab + 31) / 32) * 4;
+        k_choice_penalty<<<kTMax, 1024, bits, s>>>(b.state, b.ids, b.logits, m.dims.vocab);
+    }
+    k_accept<<<1, 512, 0, s>>>(b.state, b.ids, b.lm_val, b.lm_blocks, penalty_path ? 1 : 0);
+}
+
+void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, bool lm, bool want_logits,
+                         cudaStream_t s) {
+    forward_layers(m, kv, b, s);
+    if (lm) lm_head(m, b, want_logits, s);
+}
+
+void launch_draft_args(const int32_t* ids, int n, int maximum, int n_min, int n_max, int32_t* out, int* n_out,
+                       cudaStream_t s) {
+    k_draft_args<<<1, 256, 0, s>>>(ids, n, maximum, n_min, n_max, out, n_out);
+}
+
+void launch_choice_args(const float* logits, int n_raw, const int32_t* hist, int n_hist, float p, int* out,
+                        cudaStream_t s) {
+    k_choice_args<<<1, 1024, (size_t)((n_raw + 31) / 32) * 4, s>>>(logits, n_raw, hist, n_hist, p, out);
+}
+
+void launch_set_forced(const StepBuffers& b, const int32_t* src, int n, int vocab, cudaStream_t s) {
+    k_set_forced<<<1, 1, 0, s>>>(b.state, src, n, vocab);
+}
+
+void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s) { k_rows_begin<<<1, 1, 0, s>>>(b.state, T); }
+void launch_rows_end(const StepBuffers& b, cudaStream_t s) { k_rows_end<<<1, 1, 0, s>>>(b.state); }
+
+void launch_prefill_seed(const StepBuffers& b, cudaStream_t s) {
+    k_prefill_seed<<<1, 512, 0, s>>>(b.state, b.ids, b.lm_val, b.lm_blocks, 0);
+}
+
+void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s) {
+    // hidden_row is device memory holding one row; quantise it as row 0 (T is 1 in state).
+    k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, hidden_row,
+                                                                                        m.dims.hidden, b.act_q, b.act_d);
+    lm_head(m, b, true, s);
+}
+
+void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s) {
+    k_fill_synthetic_kv<<<148 * 8, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, n_pos, seed);
+}
+
+void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos, float* out,
+                      cudaStream_t s) {
+    k_kv_gather<<<148, 256, 0, s>>>(kv, m.dims.n_kv, layer, which, pos0, n_pos, out);
+}
+
+}  // namespace mtb

@@ -1,0 +1,75 @@
+// Launch wrappers for the sm_100a kernels of the verify step (kernels.cu).
+#pragma once
+
+#include "mtb_internal.hpp"
+
+namespace mtb {
+
+// Everything one verify step needs, as device pointers.  Dynamic sizes
+// (rows, positions) are read by the kernels from `state`.
+struct StepBuffers {
+    StepState* state;
+    int32_t* ids;           // generated ids [max_new]
+    float* x;               // residual [kTMax][hidden]
+    float* qkv;             // raw projections [kTMax][(n_heads + 2 n_kv) * 128]
+    float* attn_out;        // combined attention [kTMax][n_heads * 128]
+    float* gu;              // silu(gate) * up [kTMax][ffn]
+    float* hid;             // final-normed hidden [kTMax][hidden]
+    uint8_t* act_q;         // quantised activation in mma fragment order [K/32][512]
+    float* act_d;           // its block scales [K/32][16]
+    float* part_o;          // attention partials [n_kv][max_chunks][kTMax*group][128]
+    float2* part_ml;        // (max, sum) per partial
+    float2* lm_val;         // LM-head argmax partials (value, index-as-float bits)
+    float* logits;          // [kTMax][vocab] (penalty path and tests), may be null
+    int max_chunks;
+    int lm_blocks;
+};
+
+struct KvCache {
+    void* base;              // pages of [n_layers][2][n_kv][kPage][128] elements
+    const int32_t* pages;    // logical page -> physical page
+    int type;                // KvType
+    long long page_elems;    // elements per page
+};
+
+struct DeviceModel {
+    ModelDims dims;
+    LayerWeights* layers;    // host array of device pointers
+    const uint8_t* embd;     // token_embd tiles (also the tied LM head)
+    const float* output_norm;
+    float theta_scale;       // powf(rope_theta, -2/128), computed on the host
+};
+
+// q8_0 rows -> tiles (src: raw ggml blocks, n_rows x k).  Destination row group
+// for source row group r is r * rg_stride + rg_offset.
+void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int rg_stride, int rg_offset,
+                      cudaStream_t s);
+
+// One full verify step for the rows in state->tokens (see decoder.cu).
+// `mode`: 0 = draft on device, 1 = host-forced draft already in state,
+//         2 = no draft (rows given by the host: prefill chunk or explicit run).
+void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, int draft_mode,
+                 bool want_logits, cudaStream_t s);
+
+// Embedding rows from host-provided float rows instead of token ids
+// (prefill and the run() test entry): copies `rows` into x.
+void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, bool lm_head,
+                         bool want_logits, cudaStream_t s);
+
+void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s);
+void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos,
+                      float* out, cudaStream_t s);
+void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s);
+void launch_prefill_seed(const StepBuffers& b, cudaStream_t s);
+
+int lm_head_blocks(int vocab);
+cudaError_t configure_kernels();
+void launch_draft_args(const int32_t* ids, int n, int maximum, int n_min, int n_max, int32_t* out, int* n_out,
+                       cudaStream_t s);
+void launch_choice_args(const float* logits, int n_raw, const int32_t* hist, int n_hist, float p, int* out,
+                        cudaStream_t s);
+void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s);
+void launch_set_forced(const StepBuffers& b, const int32_t* src, int n, int vocab, cudaStream_t s);
+void launch_rows_end(const StepBuffers& b, cudaStream_t s);
+
+}  // namespace mtb

@@ -1,0 +1,292 @@
+"""ctypes binding of libmoss_transcribe_b200.so (include/mtb_decoder.h).
+
+The Python names mirror the reference's generation interface so callers and
+tests read like the reference's own:
+  - Decoder.run / prefill / decode_one / logits_from_hidden / rewind / past_len
+    -> Qwen3Decoder (src/qwen3_decoder.hpp:37-60)
+  - greedy_generate          -> src/generate.cpp:235
+  - cpu_speculative_generate -> src/cpu_speculative.cpp:86 (hooks: draft, committed)
+  - cpu_ngram_draft / cpu_greedy_choice -> src/cpu_speculative.cpp:45,57
+Every call goes to the CUDA library; there is no Python or CPU fallback, and
+loading fails loudly when the library or a GPU is missing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libmoss_transcribe_b200.so")
+_LIB = None
+
+KV_F32, KV_F16 = 0, 1
+STOP_NONE, STOP_EOS, STOP_LIMIT, STOP_ERROR = 0, 1, 2, 3
+
+
+class SpecParams(C.Structure):
+    _fields_ = [("k_max", C.c_int32), ("n_min", C.c_int32), ("n_max", C.c_int32), ("penalty", C.c_float)]
+
+
+class Counters(C.Structure):
+    _fields_ = [("target_calls", C.c_int64), ("drafted_calls", C.c_int64), ("proposed", C.c_int64),
+                ("accepted", C.c_int64), ("target_input_tokens", C.c_int64), ("rewinds", C.c_int64),
+                ("stop_reason", C.c_int32), ("past_len", C.c_int32)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+DRAFT_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, C.POINTER(C.c_int32))
+COMMIT_FN = C.CFUNCTYPE(None, C.c_void_p, C.POINTER(C.c_int32), C.c_int, C.c_int, C.c_int)
+
+# Every exported function with (restype, argtypes); used for binding and for
+# the export check of the boundary test.
+_vp, _i32p, _f32p, _ip = C.c_void_p, C.POINTER(C.c_int32), C.POINTER(C.c_float), C.POINTER(C.c_int)
+SIGNATURES = {
+    "moss_transcribe_capi_abi_version": (C.c_int, []),
+    "moss_transcribe_capi_load": (_vp, [C.c_char_p]),
+    "moss_transcribe_capi_free": (None, [_vp]),
+    "moss_transcribe_capi_transcribe_path": (_vp, [_vp, C.c_char_p, C.c_int]),
+    "moss_transcribe_capi_transcribe_pcm": (_vp, [_vp, _f32p, C.c_int, C.c_int, C.c_int]),
+    "moss_transcribe_capi_free_string": (None, [_vp]),
+    "moss_transcribe_capi_last_error": (C.c_char_p, [_vp]),
+    "mtb_abi_version": (C.c_int, []),
+    "mtb_global_error": (C.c_char_p, []),
+    "mtb_model_load": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_vp)]),
+    "mtb_model_free": (None, [_vp]),
+    "mtb_model_error": (C.c_char_p, [_vp]),
+    "mtb_model_dims": (C.c_int, [_vp, _i32p]),
+    "mtb_decoder_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
+    "mtb_decoder_free": (None, [_vp]),
+    "mtb_decoder_error": (C.c_char_p, [_vp]),
+    "mtb_decoder_past_len": (C.c_int, [_vp]),
+    "mtb_decoder_reset": (C.c_int, [_vp]),
+    "mtb_decoder_rewind": (C.c_int, [_vp, C.c_int]),
+    "mtb_decoder_run": (C.c_int, [_vp, _f32p, C.c_int, _f32p]),
+    "mtb_decoder_logits": (C.c_int, [_vp, _f32p, _f32p]),
+    "mtb_decoder_kv_read": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]),
+    "mtb_decoder_fill_synthetic_kv": (C.c_int, [_vp, C.c_int, C.c_uint32]),
+    "mtb_greedy_generate": (C.c_int, [_vp, _f32p, C.c_int, C.c_int, C.c_int, C.c_float, _i32p, _ip]),
+    "mtb_spec_generate": (C.c_int, [_vp, _f32p, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams), _i32p, _ip,
+                                    C.POINTER(Counters), DRAFT_FN, COMMIT_FN, _vp]),
+    "mtb_resume": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams)]),
+    "mtb_spec_step": (C.c_int, [_vp, _i32p, C.c_int, C.POINTER(Counters)]),
+    "mtb_spec_step_async": (C.c_int, [_vp, _vp, C.c_int]),
+    "mtb_snapshot_save": (C.c_int, [_vp]),
+    "mtb_snapshot_restore_async": (C.c_int, [_vp]),
+    "mtb_read_ids": (C.c_int, [_vp, _i32p, C.c_int, _ip, C.POINTER(Counters)]),
+    "mtb_sync": (C.c_int, [_vp]),
+    "mtb_event_record": (C.c_int, [_vp, C.c_int]),
+    "mtb_event_elapsed_ms": (C.c_int, [_vp, C.c_int, C.c_int, _f32p]),
+    "mtb_step_kernel_launches": (C.c_int, [_vp]),
+    "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
+    "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
+}
+
+
+class MtbError(RuntimeError):
+    pass
+
+
+def lib():
+    """The loaded CUDA library; raises if it has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise MtbError(f"{LIB_PATH} is missing: build it with __graft_entry__.build() or `make -C "
+                           f"{os.path.dirname(LIB_PATH)}`")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def _f32(a):
+    return a.ctypes.data_as(_f32p)
+
+
+def _i32(a):
+    return a.ctypes.data_as(_i32p)
+
+
+def _arr_i32(x):
+    return np.ascontiguousarray(np.asarray(x, dtype=np.int32))
+
+
+class Model:
+    """Decoder weights of a GGUF file resident on one CUDA device."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        L = lib()
+        p = C.c_void_p()
+        rc = L.mtb_model_load(gguf_path.encode(), int(device), C.byref(p))
+        if rc != 0:
+            raise MtbError(f"mtb_model_load: {L.mtb_global_error().decode()}")
+        self.ptr = p
+        self.device = device
+        dims = (C.c_int32 * 8)()
+        L.mtb_model_dims(self.ptr, dims)
+        (self.hidden, self.n_layers, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.vocab,
+         self.eos) = list(dims)
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            lib().mtb_model_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        self.close()
+
+
+class Decoder:
+    """Qwen3Decoder on the GPU: paged KV cache plus the device step state."""
+
+    def __init__(self, model: Model, max_seq: int, kv_type: int = KV_F32, max_new: int = 4096):
+        L = lib()
+        p = C.c_void_p()
+        if L.mtb_decoder_create(model.ptr, int(max_seq), int(kv_type), int(max_new), C.byref(p)) != 0:
+            raise MtbError(f"mtb_decoder_create: {L.mtb_global_error().decode()}")
+        self.ptr = p
+        self.model = model
+        self.max_seq = max_seq
+        self.max_new = max_new
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            lib().mtb_decoder_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise MtbError(f"{what}: {lib().mtb_decoder_error(self.ptr).decode()}")
+
+    # -- Qwen3Decoder surface ------------------------------------------------
+    @property
+    def past_len(self) -> int:
+        v = lib().mtb_decoder_past_len(self.ptr)
+        if v < 0:
+            self._check(-1, "past_len")
+        return v
+
+    def reset(self):
+        self._check(lib().mtb_decoder_reset(self.ptr), "reset")
+
+    def rewind(self, position: int) -> bool:
+        return lib().mtb_decoder_rewind(self.ptr, int(position)) == 0
+
+    def run(self, embeds: np.ndarray) -> np.ndarray:
+        e = np.ascontiguousarray(embeds, dtype=np.float32).reshape(-1, self.model.hidden)
+        out = np.zeros_like(e)
+        self._check(lib().mtb_decoder_run(self.ptr, _f32(e), e.shape[0], _f32(out)), "run")
+        return out
+
+    def prefill(self, embeds: np.ndarray) -> np.ndarray:
+        self.reset()
+        return self.run(embeds)
+
+    def decode_one(self, embed: np.ndarray) -> np.ndarray:
+        return self.run(np.asarray(embed, dtype=np.float32).reshape(1, -1))[0]
+
+    def logits_from_hidden(self, hidden_row: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(hidden_row, dtype=np.float32).ravel()
+        out = np.zeros(self.model.vocab, dtype=np.float32)
+        self._check(lib().mtb_decoder_logits(self.ptr, _f32(h), _f32(out)), "logits")
+        return out
+
+    def kv(self, layer: int, which: int, pos0: int, n: int) -> np.ndarray:
+        out = np.zeros((n, self.model.n_kv_heads, self.model.head_dim), dtype=np.float32)
+        self._check(lib().mtb_decoder_kv_read(self.ptr, layer, which, pos0, n, _f32(out)), "kv_read")
+        return out
+
+    def fill_synthetic_kv(self, n_pos: int, seed: int):
+        self._check(lib().mtb_decoder_fill_synthetic_kv(self.ptr, int(n_pos), int(seed) & 0xFFFFFFFF), "fill_kv")
+
+    # -- generation ------------------------------------------------------------
+    def greedy_generate(self, fused: np.ndarray, max_new: int, eos: int, penalty: float = 1.0) -> list[int]:
+        f = np.ascontiguousarray(fused, dtype=np.float32).reshape(-1, self.model.hidden)
+        out = np.zeros(max_new, dtype=np.int32)
+        n = C.c_int()
+        self._check(lib().mtb_greedy_generate(self.ptr, _f32(f), f.shape[0], int(max_new), int(eos), float(penalty),
+                                              _i32(out), C.byref(n)), "greedy_generate")
+        return out[:n.value].tolist()
+
+    def cpu_speculative_generate(self, fused: np.ndarray, max_new: int, eos: int, k_max: int = 4, n_min: int = 2,
+                                 n_max: int = 16, penalty: float = 1.0, draft=None, committed=None):
+        """Strict speculative generate; `draft(ids, budget)` and
+        `committed(ids, past_len, stopped)` are the reference's hooks."""
+        f = np.ascontiguousarray(fused, dtype=np.float32).reshape(-1, self.model.hidden)
+        out = np.zeros(max_new, dtype=np.int32)
+        n = C.c_int()
+        counters = Counters()
+        params = SpecParams(k_max, n_min, n_max, penalty)
+
+        def _draft(user, ids, n_ids, budget, dst):
+            got = list(draft([ids[i] for i in range(n_ids)], budget))[:budget]
+            for i, v in enumerate(got):
+                dst[i] = int(v)
+            return len(got)
+
+        def _commit(user, ids, n_ids, past, stopped):
+            committed([ids[i] for i in range(n_ids)], past, bool(stopped))
+
+        dfn = DRAFT_FN(_draft) if draft else DRAFT_FN()
+        cfn = COMMIT_FN(_commit) if committed else COMMIT_FN()
+        self._check(lib().mtb_spec_generate(self.ptr, _f32(f), f.shape[0], int(max_new), int(eos), C.byref(params),
+                                            _i32(out), C.byref(n), C.byref(counters), dfn, cfn, None),
+                    "spec_generate")
+        return out[:n.value].tolist(), counters.as_dict()
+
+    # -- step-level API --------------------------------------------------------
+    def resume(self, ids, past: int, max_new: int, eos: int, k_max=4, n_min=2, n_max=16, penalty=1.0):
+        a = _arr_i32(ids)
+        params = SpecParams(k_max, n_min, n_max, penalty)
+        self._check(lib().mtb_resume(self.ptr, _i32(a), a.size, int(past), int(max_new), int(eos), C.byref(params)),
+                    "resume")
+
+    def spec_step(self, draft=None) -> dict:
+        c = Counters()
+        if draft is None:
+            rc = lib().mtb_spec_step(self.ptr, None, 0, C.byref(c))
+        else:
+            a = _arr_i32(draft)
+            rc = lib().mtb_spec_step(self.ptr, _i32(a) if a.size else _i32(np.zeros(1, np.int32)), a.size, C.byref(c))
+        self._check(rc, "spec_step")
+        return c.as_dict()
+
+    def read_ids(self):
+        out = np.zeros(self.max_new, dtype=np.int32)
+        n = C.c_int()
+        c = Counters()
+        self._check(lib().mtb_read_ids(self.ptr, _i32(out), self.max_new, C.byref(n), C.byref(c)), "read_ids")
+        return out[:n.value].tolist(), c.as_dict()
+
+    def cpu_ngram_draft(self, history, maximum: int, n_min: int = 2, n_max: int = 16) -> list[int]:
+        h = _arr_i32(history)
+        out = np.zeros(max(1, len(h) + 16), dtype=np.int32)
+        n = C.c_int()
+        self._check(lib().mtb_ngram_draft(self.ptr, _i32(h) if h.size else None, h.size, int(maximum), int(n_min),
+                                          int(n_max), _i32(out), C.byref(n)), "ngram_draft")
+        return out[:n.value].tolist()
+
+    def cpu_greedy_choice(self, raw, history, penalty: float) -> int:
+        r = np.ascontiguousarray(np.asarray(raw, dtype=np.float32))
+        h = _arr_i32(history)
+        c = C.c_int32()
+        self._check(lib().mtb_greedy_choice(self.ptr, _f32(r), r.size, _i32(h) if h.size else None, h.size,
+                                            float(penalty), C.byref(c)), "greedy_choice")
+        return c.value
+
+    # -- timing ----------------------------------------------------------------
+    def sync(self):
+        self._check(lib().mtb_sync(self.ptr), "sync")
+
+    def step_kernel_launches(self) -> int:
+        return lib().mtb_step_kernel_launches(self.ptr)
