@@ -153,8 +153,10 @@ int load_model(mtb_model* m, const char* path) {
     m->eos = int(f.get_u32("mtd.eos_token_id", 151645));
     const int head_dim = int(f.get_u32("mtd.text.head_dim", 128));
     if (head_dim != kHeadDim) return fail(m->error, "head_dim must be 128");
-    if (d.hidden <= 0 || d.hidden % kTileK || d.hidden > 8192) return fail(m->error, "hidden must be a multiple of 64 (<= 8192)");
-    if (d.ffn <= 0 || d.ffn % kTileK || d.ffn > 16384) return fail(m->error, "ffn must be a multiple of 64 (<= 16384)");
+    // Every K of a projection is a whole number of 256-element slices.
+    if (d.hidden <= 0 || d.hidden % 256 || d.hidden > 8192) return fail(m->error, "hidden must be a multiple of 256 (<= 8192)");
+    if (d.ffn <= 0 || d.ffn % 256 || d.ffn > 16384) return fail(m->error, "ffn must be a multiple of 256 (<= 16384)");
+    if ((d.n_heads * kHeadDim) % 256) return fail(m->error, "n_heads * 128 must be a multiple of 256");
     if (d.n_heads <= 0 || d.n_kv <= 0 || d.n_heads % d.n_kv || d.n_heads / d.n_kv > 4)
         return fail(m->error, "n_heads must be 1..4 times n_kv_heads");
     if (d.vocab <= 0 || d.vocab % kTileRows) return fail(m->error, "vocab must be a multiple of 8");

@@ -12,6 +12,7 @@
 // integer block sums, fp32 d_w*d_x scaling) follows ggml's CPU mul_mat as used
 // by src/cpu_projection.cpp:16-37.
 #include "kernels.hpp"
+#include "exact_math.cuh"
 
 #include <cuda_fp16.h>
 #include <cfloat>
@@ -156,15 +157,22 @@ struct GemvArgs {
 };
 
 // Skinny q8_0 GEMM: y[t][n] = sum_blocks dw[n,b] * dx[t,b] * sum_32 qw * qx for
-// up to 16 rows t.  RPB row groups per CTA iteration; the 8 warps split as
-// RPB groups x (8/RPB) K-slices, reduced in a fixed order (deterministic).
+// up to 16 rows t.  Evaluation order (shared with the CPU restatement): per
+// output, one fmaf per 32-block in ascending order inside each 256-element
+// slice (4 tiles), then the slice partials added in ascending order.
+// A CTA iteration covers RPB row groups; its RPB * S (row group, slice) items
+// are spread over the 8 warps (the next item's tiles load while the current
+// one computes), and warp r < RPB adds the slices of row group r.
+constexpr int kSliceTiles = 4;
+
 template <int EPI, int RPB>
 __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int kb_n = a.kt_n * 2;
+    const int S = a.kt_n / kSliceTiles;
     uint4* s_act = reinterpret_cast<uint4*>(smem);                       // [kb_n][32]
     float* s_d = reinterpret_cast<float*>(s_act + kb_n * 32);            // [kb_n][16]
-    float* s_red = s_d + kb_n * 16;                                      // [8][32][4]
+    float4* s_part = reinterpret_cast<float4*>(s_d + kb_n * 16);         // [RPB][S][32]
     const int T = a.state->T;
     if (T <= 0) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -175,107 +183,117 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
         for (int i = threadIdx.x; i < kb_n * 16; i += kThreads) s_d[i] = a.act_d[i];
     }
     __syncthreads();
-    constexpr int WPR = kWarps / RPB;   // warps per row group
-    const int r = warp % RPB, slice = warp / RPB;
+    const int n_items = RPB * S;
     float best_v[2] = {-INFINITY, -INFINITY};
     int best_i[2] = {0x7fffffff, 0x7fffffff};
 
     for (int rg0 = blockIdx.x * RPB; rg0 < a.n_rg; rg0 += gridDim.x * RPB) {
-        const int rg = rg0 + r;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (rg < a.n_rg) {
-            const uint8_t* wrow = a.w + (size_t)rg * a.kt_n * kTileBytes;
-            constexpr int U = 4;
-            for (int kt0 = slice; kt0 < a.kt_n; kt0 += WPR * U) {
-                uint4 wv[U];
-                uint2 sv[U];
+        uint4 wv[kSliceTiles];
+        uint2 sv[kSliceTiles];
+        auto load = [&](int it, uint4 (&w)[kSliceTiles], uint2 (&sc)[kSliceTiles]) {
+            const int rg = rg0 + it / S, sl = it % S;
+            if (rg >= a.n_rg) return;
+            const uint8_t* tile = a.w + ((size_t)rg * a.kt_n + (size_t)sl * kSliceTiles) * kTileBytes;
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int kt = kt0 + u * WPR;
-                    if (kt < a.kt_n) {
-                        wv[u] = ld_stream_u4(wrow + (size_t)kt * kTileBytes + lane * 16);
-                        sv[u] = ld_nc_u2(wrow + (size_t)kt * kTileBytes + 512 + t * 8);
-                    }
-                }
+            for (int u = 0; u < kSliceTiles; ++u) {
+                w[u] = ld_stream_u4(tile + (size_t)u * kTileBytes + lane * 16);
+                sc[u] = ld_nc_u2(tile + (size_t)u * kTileBytes + 512 + t * 8);
+            }
+        };
+        int it = warp;
+        if (it < n_items) load(it, wv, sv);
+        while (it < n_items) {
+            const int next = it + kWarps;
+            uint4 wn[kSliceTiles];
+            uint2 sn[kSliceTiles];
+            if (next < n_items) load(next, wn, sn);
+            const int r = it / S, sl = it % S;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (rg0 + r < a.n_rg) {
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int kt = kt0 + u * WPR;
-                    if (kt < a.kt_n) {
-                        int c0[4], c1[4];
-                        mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv[u].x, wv[u].y);
-                        mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv[u].z, wv[u].w);
-                        const float x0g = s_d[(2 * kt) * 16 + g], x0h = s_d[(2 * kt) * 16 + g + 8];
-                        const float x1g = s_d[(2 * kt + 1) * 16 + g], x1h = s_d[(2 * kt + 1) * 16 + g + 8];
-                        const float w00 = h2f_lo(sv[u].x), w01 = h2f_hi(sv[u].x);  // block 0, rows 2t, 2t+1
-                        const float w10 = h2f_lo(sv[u].y), w11 = h2f_hi(sv[u].y);  // block 1
-                        acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
-                        acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
-                        acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
-                        acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
-                        acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
-                        acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
-                        acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
-                        acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
-                    }
+                for (int u = 0; u < kSliceTiles; ++u) {
+                    const int kt = sl * kSliceTiles + u;
+                    int c0[4], c1[4];
+                    mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv[u].x, wv[u].y);
+                    mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv[u].z, wv[u].w);
+                    const float x0g = s_d[(2 * kt) * 16 + g], x0h = s_d[(2 * kt) * 16 + g + 8];
+                    const float x1g = s_d[(2 * kt + 1) * 16 + g], x1h = s_d[(2 * kt + 1) * 16 + g + 8];
+                    const float w00 = h2f_lo(sv[u].x), w01 = h2f_hi(sv[u].x);  // block 0, rows 2t, 2t+1
+                    const float w10 = h2f_lo(sv[u].y), w11 = h2f_hi(sv[u].y);  // block 1
+                    // d = dw * dx is exact (two fp16 values); one fmaf per block.
+                    acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
+                    acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
+                    acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
+                    acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+                    acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
+                    acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
+                    acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
+                    acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
                 }
             }
-        }
-        if (WPR > 1) {
-            float4* red = reinterpret_cast<float4*>(s_red);
-            red[warp * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            __syncthreads();
-            if (slice == 0) {
-                for (int s2 = 1; s2 < WPR; ++s2) {
-                    const float4 o = red[(s2 * RPB + r) * 32 + lane];
-                    acc[0] += o.x; acc[1] += o.y; acc[2] += o.z; acc[3] += o.w;
-                }
+            s_part[(r * S + sl) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            if (next < n_items) {
+#pragma unroll
+                for (int u = 0; u < kSliceTiles; ++u) { wv[u] = wn[u]; sv[u] = sn[u]; }
             }
+            it = next;
         }
-        if (EPI == EPI_SWIGLU) {
-            // Row groups alternate gate (even) / up (odd): the gate warp pairs
-            // with the up warp r + 1 through shared memory.
-            float4* ys = reinterpret_cast<float4*>(s_red) + kWarps * 32;
-            if (slice == 0 && (r & 1)) ys[r * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            __syncthreads();
-            if (slice == 0 && !(r & 1) && rg < a.n_rg) {
-                const float4 u = ys[(r + 1) * 32 + lane];
-                const float uu[4] = {u.x, u.y, u.z, u.w};
-                const int feat = (rg >> 1) * kTileRows + 2 * t;
+        __syncthreads();
+        if (warp < RPB) {
+            const int r = warp, rg = rg0 + r;
+            auto slice_sum = [&](int rr) {
+                float4 y = s_part[(rr * S) * 32 + lane];
+                for (int sl = 1; sl < S; ++sl) {
+                    const float4 o = s_part[(rr * S + sl) * 32 + lane];
+                    y.x = y.x + o.x; y.y = y.y + o.y; y.z = y.z + o.z; y.w = y.w + o.w;
+                }
+                return y;
+            };
+            if (EPI == EPI_SWIGLU) {
+                // Row groups alternate gate (even) / up (odd).
+                if (!(r & 1) && rg < a.n_rg) {
+                    const float4 gq = slice_sum(r), uq = slice_sum(r + 1);
+                    const float gg[4] = {gq.x, gq.y, gq.z, gq.w}, uu[4] = {uq.x, uq.y, uq.z, uq.w};
+                    const int feat = (rg >> 1) * kTileRows + 2 * t;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int row = g + (j >> 1) * 8;
+                        if (row < T) {
+                            const float sl = gg[j] / (1.0f + exact_expf(-gg[j]));
+                            a.out[(size_t)row * a.ld + feat + (j & 1)] = sl * uu[j];
+                        }
+                    }
+                }
+            } else if (rg < a.n_rg) {
+                const float4 yq = slice_sum(r);
+                const float y[4] = {yq.x, yq.y, yq.z, yq.w};
+                const int n0 = rg * kTileRows + 2 * t;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int row = g + (j >> 1) * 8;
-                    if (row < T) {
-                        const float gv = acc[j];
-                        const float sl = gv / (1.0f + expf(-gv));
-                        a.out[(size_t)row * a.ld + feat + (j & 1)] = sl * uu[j];
+                    const int col = n0 + (j & 1);
+                    if (row >= T) continue;
+                    if (EPI == EPI_STORE) a.out[(size_t)row * a.ld + col] = y[j];
+                    if (EPI == EPI_RESID) {
+                        float* o = a.out + (size_t)row * a.ld + col;
+                        *o = *o + y[j];
                     }
-                }
-            }
-        } else if (slice == 0 && rg < a.n_rg) {
-            const int n0 = rg * kTileRows + 2 * t;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int row = g + (j >> 1) * 8;
-                const int col = n0 + (j & 1);
-                if (row >= T) continue;
-                float* o = a.out + (size_t)row * a.ld + col;
-                if (EPI == EPI_STORE) *o = acc[j];
-                if (EPI == EPI_RESID) *o = *o + acc[j];
-                if (EPI == EPI_ARGMAX) {
-                    if (a.logits) a.logits[(size_t)row * a.ld + col] = acc[j];
-                    const int slot = j >> 1;
-                    if (acc[j] > best_v[slot] || (acc[j] == best_v[slot] && col < best_i[slot])) {
-                        best_v[slot] = acc[j];
-                        best_i[slot] = col;
+                    if (EPI == EPI_ARGMAX) {
+                        if (a.logits) a.logits[(size_t)row * a.ld + col] = y[j];
+                        const int slot = j >> 1;
+                        if (y[j] > best_v[slot] || (y[j] == best_v[slot] && col < best_i[slot])) {
+                            best_v[slot] = y[j];
+                            best_i[slot] = col;
+                        }
                     }
                 }
             }
         }
-        if (WPR > 1 || EPI == EPI_SWIGLU) __syncthreads();
+        __syncthreads();
     }
     if (EPI == EPI_ARGMAX) {
-        // Reduce (value, first index) over the 4 lanes of a row group, then
-        // over the RPB leader warps, then write this CTA's partial per row.
+        // (value, first index) over the 4 lanes of a row group, then over the
+        // RPB warps, then this CTA's partial per row.
 #pragma unroll
         for (int slot = 0; slot < 2; ++slot) {
 #pragma unroll
@@ -288,10 +306,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
                 }
             }
         }
-        float2* cand = reinterpret_cast<float2*>(s_red);  // [RPB][16]
-        if (slice == 0 && t == 0) {
-            cand[r * 16 + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
-            cand[r * 16 + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
+        float2* cand = reinterpret_cast<float2*>(s_part);  // [RPB][16]
+        if (warp < RPB && t == 0) {
+            cand[warp * 16 + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
+            cand[warp * 16 + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
         }
         __syncthreads();
         if (threadIdx.x < 16) {
@@ -310,7 +328,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
 template <int EPI, int RPB>
 void gemv(const GemvArgs& a, int grid, cudaStream_t s) {
     const int kb_n = a.kt_n * 2;
-    const size_t smem = (size_t)kb_n * 32 * 16 + (size_t)kb_n * 16 * 4 + (size_t)kWarps * 32 * 16 * 2;
+    const int S = a.kt_n / kSliceTiles;
+    const size_t smem = (size_t)kb_n * 32 * 16 + (size_t)kb_n * 16 * 4 + (size_t)RPB * S * 32 * 16;
     k_gemv<EPI, RPB><<<grid, kThreads, smem, s>>>(a);
 }
 
@@ -402,7 +421,8 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
     if (d < kHeadDim / 2) {
         float theta = (float)pos;
         for (int i = 0; i < d; ++i) theta = __fmul_rn(theta, theta_scale);
-        const float c = cosf(theta), s = sinf(theta);
+        float s, c;
+        exact_sincosf(theta, &s, &c);
         const float x0 = s_y[d], x1 = s_y[d + kHeadDim / 2];
         const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
         const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
@@ -479,8 +499,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
     for (int q = warp; q < NQ; q += kWarps) {
         const float a0 = sp[q * kPage + lane], a1 = sp[q * kPage + lane + 32];
         const float m = warp_max(fmaxf(a0, a1));
-        const float e0 = m == -INFINITY ? 0.f : expf(a0 - m);
-        const float e1 = m == -INFINITY ? 0.f : expf(a1 - m);
+        const float e0 = a0 == -INFINITY ? 0.f : exact_expf(a0 - m);
+        const float e1 = a1 == -INFINITY ? 0.f : exact_expf(a1 - m);
         const float l = warp_sum(e0 + e1);
         sp[q * kPage + lane] = e0;
         sp[q * kPage + lane + 32] = e1;
@@ -518,7 +538,7 @@ __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n
     for (int c = 0; c < n_chunks; ++c) {
         const float2 ml = part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q];
         if (ml.x == -INFINITY) continue;
-        const float wgt = expf(ml.x - M);
+        const float wgt = exact_expf(ml.x - M);
         L = fmaf(wgt, ml.y, L);
         o = fmaf(wgt, part_o[(((size_t)h * max_chunks + c) * (kTMax * 4) + q) * kHeadDim + threadIdx.x], o);
     }

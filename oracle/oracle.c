@@ -33,6 +33,112 @@ static inline uint16_t f2h(float f) {
 }
 static inline float round_f16(float f) { return h2f(f2h(f)); }
 
+/* ------------------------------------------------------------ exp, sin, cos
+ * Own implementations (Cody-Waite range reduction + Taylor series, evaluated
+ * in double with every operation rounded separately; the library is built
+ * with -ffp-contract=off).  The CUDA kernels evaluate the same sequence, so
+ * both sides return identical floats.  Accuracy: the double result is within
+ * a few 1e-16 relative of the true value, so the float result is the
+ * correctly rounded one except in rare near-tie cases. */
+#define MTB_LN2_HI 0.6931471803691238       /* ln 2 to 32 bits */
+#define MTB_LN2_LO 1.9082149292705877e-10   /* ln 2 - MTB_LN2_HI */
+#define MTB_INV_LN2 1.4426950408889634
+#define MTB_PIO2_1 1.5707963267341256       /* pi/2 to 33 bits */
+#define MTB_PIO2_2 6.077100506303966e-11    /* next 33 bits */
+#define MTB_PIO2_3 2.0222662487959506e-21   /* remainder */
+#define MTB_TWO_OVER_PI 0.6366197723675814
+
+float orc_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.8f) return INFINITY;
+    if (x < -104.0f) return 0.0f;
+    const double xd = (double)x;
+    const double n = rint(xd * MTB_INV_LN2);
+    const double r = (xd - n * MTB_LN2_HI) - n * MTB_LN2_LO;
+    /* e^r = sum r^k / k!, k <= 12, |r| <= 0.35 */
+    double p = 1.0 / 479001600.0;
+    p = p * r + 1.0 / 39916800.0;
+    p = p * r + 1.0 / 3628800.0;
+    p = p * r + 1.0 / 362880.0;
+    p = p * r + 1.0 / 40320.0;
+    p = p * r + 1.0 / 5040.0;
+    p = p * r + 1.0 / 720.0;
+    p = p * r + 1.0 / 120.0;
+    p = p * r + 1.0 / 24.0;
+    p = p * r + 1.0 / 6.0;
+    p = p * r + 0.5;
+    p = p * r + 1.0;
+    p = p * r + 1.0;
+    return (float)ldexp(p, (int)n);
+}
+
+void orc_sincosf(float x, float* s_out, float* c_out) {
+    const double xd = (double)x;
+    const double k = rint(xd * MTB_TWO_OVER_PI);
+    const double r = ((xd - k * MTB_PIO2_1) - k * MTB_PIO2_2) - k * MTB_PIO2_3;
+    const double r2 = r * r;
+    /* sin r = r - r^3/3! + ... (to r^19), cos r = 1 - r^2/2! + ... (to r^20) */
+    double ps = -1.0 / 121645100408832000.0;
+    ps = ps * r2 + 1.0 / 355687428096000.0;
+    ps = ps * r2 - 1.0 / 1307674368000.0;
+    ps = ps * r2 + 1.0 / 6227020800.0;
+    ps = ps * r2 - 1.0 / 39916800.0;
+    ps = ps * r2 + 1.0 / 362880.0;
+    ps = ps * r2 - 1.0 / 5040.0;
+    ps = ps * r2 + 1.0 / 120.0;
+    ps = ps * r2 - 1.0 / 6.0;
+    ps = ps * r2 + 1.0;
+    const double sv = ps * r;
+    double pc = 1.0 / 2432902008176640000.0;
+    pc = pc * r2 - 1.0 / 6402373705728000.0;
+    pc = pc * r2 + 1.0 / 20922789888000.0;
+    pc = pc * r2 - 1.0 / 87178291200.0;
+    pc = pc * r2 + 1.0 / 479001600.0;
+    pc = pc * r2 - 1.0 / 3628800.0;
+    pc = pc * r2 + 1.0 / 40320.0;
+    pc = pc * r2 - 1.0 / 720.0;
+    pc = pc * r2 + 1.0 / 24.0;
+    pc = pc * r2 - 0.5;
+    pc = pc * r2 + 1.0;
+    const double cv = pc;
+    const long long q = ((long long)k % 4 + 4) % 4;
+    double so, co;
+    if (q == 0) { so = sv; co = cv; }
+    else if (q == 1) { so = cv; co = -sv; }
+    else if (q == 2) { so = -sv; co = -cv; }
+    else { so = -cv; co = sv; }
+    *s_out = (float)so;
+    *c_out = (float)co;
+}
+
+/* Sum of float squares in double in the CUDA kernels' order: `threads`
+ * strided partial sums (each sequential from 0.0), a xor-butterfly inside
+ * each group of 32 (pairs i, i+16, then i, i+8, ... ), then the group totals
+ * added in order.  Addition is commutative, so only the tree shape matters. */
+static double sum_squares_tree(const float* x, int n, int threads) {
+    double part[1024];
+    for (int i = 0; i < threads; ++i) {
+        double acc = 0.0;
+        for (int j = i; j < n; j += threads) acc += (double)(x[j] * x[j]);
+        part[i] = acc;
+    }
+    double tot = 0.0;
+    for (int w = 0; w < threads / 32; ++w) {
+        double* v = part + 32 * w;
+        for (int off = 16; off > 0; off >>= 1)
+            for (int i = 0; i < off; ++i) v[i] = v[i] + v[i + off];
+        tot += v[0];
+    }
+    return tot;
+}
+
+/* Float xor-butterfly total of 32 values (the kernels' warp sum). */
+static float warp_tree_sum(float* v) {
+    for (int off = 16; off > 0; off >>= 1)
+        for (int i = 0; i < off; ++i) v[i] = v[i] + v[i + off];
+    return v[0];
+}
+
 void orc_set_threads(int n) {
 #ifdef _OPENMP
     if (n > 0) omp_set_num_threads(n);
@@ -74,24 +180,25 @@ void orc_quantize_ref_q8(const float* x, int64_t k, void* out_blocks) {
     }
 }
 
-/* ggml_vec_dot_q8_0_q8_0, x86 path: eight fp32 lanes, each fed by an exact
- * 4-element integer sum per block, then the 8->4->2->1 horizontal add. */
+/* q8_0 x q8_0 dot: exact integer sum per 32-block, times d_w*d_x (an exact
+ * product of two fp16 values), accumulated with one fmaf per block in
+ * ascending block order inside each 256-element slice; the slice partials
+ * are then added in ascending order.  ggml's x86 path spreads each block over
+ * eight lanes instead; the evaluation order here is the one this oracle and
+ * the CUDA kernels share (a difference of float rounding order only). */
 static inline float dot_q8(const blk_q8* w, const blk_q8* x, int nb) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int b = 0; b < nb; ++b) {
-        const float d = h2f(w[b].d) * h2f(x[b].d);
-        const int8_t* a = w[b].qs;
-        const int8_t* c = x[b].qs;
-        for (int l = 0; l < 8; ++l) {
-            const int s = a[4 * l] * c[4 * l] + a[4 * l + 1] * c[4 * l + 1] +
-                          a[4 * l + 2] * c[4 * l + 2] + a[4 * l + 3] * c[4 * l + 3];
-            acc[l] = fmaf(d, (float)s, acc[l]);
+    float total = 0.0f;
+    for (int s0 = 0; s0 < nb; s0 += 8) {
+        float acc = 0.0f;
+        for (int b = s0; b < s0 + 8 && b < nb; ++b) {
+            const float d = h2f(w[b].d) * h2f(x[b].d);
+            int isum = 0;
+            for (int j = 0; j < 32; ++j) isum += w[b].qs[j] * x[b].qs[j];
+            acc = fmaf((float)isum, d, acc);
         }
+        total = total + acc;
     }
-    float r0 = acc[4] + acc[0], r1 = acc[5] + acc[1], r2 = acc[6] + acc[2], r3 = acc[7] + acc[3];
-    r0 = r0 + r2;
-    r1 = r1 + r3;
-    return r0 + r1;
+    return total;
 }
 
 /* ggml_mul_mat(W q8_0 [n_rows x k], x f32 [T x k]) -> y [T x n_rows]. */
@@ -299,10 +406,12 @@ int orc_decoder_fill_synthetic_kv(orc_decoder* d, int n_pos, uint32_t seed) {
     return 0;
 }
 
-/* ggml rms_norm followed by ggml_mul with the weight (src/qwen3.cpp:27-30). */
-static void rms_norm_mul(const float* x, const float* w, int n, float eps, float* y) {
-    double sum = 0.0;
-    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+/* ggml rms_norm followed by ggml_mul with the weight (src/qwen3.cpp:27-30):
+ * float squares summed in double, mean as float, 1/sqrtf(mean + eps), then
+ * (x * scale) * w.  `threads` fixes the summation tree (256 for hidden rows,
+ * 128 for per-head q/k norms). */
+static void rms_norm_mul(const float* x, const float* w, int n, float eps, float* y, int threads) {
+    const double sum = sum_squares_tree(x, n, threads);
     const float mean = (float)(sum / n);
     const float scale = 1.0f / sqrtf(mean + eps);
     for (int i = 0; i < n; ++i) y[i] = (x[i] * scale) * w[i];
@@ -315,7 +424,8 @@ static void rope_neox(float* x, int n_dims, int pos, float base) {
     float theta = (float)pos;
     const int half = n_dims / 2;
     for (int i = 0; i < half; ++i) {
-        const float c = cosf(theta), s = sinf(theta);
+        float s, c;
+        orc_sincosf(theta, &s, &c);
         const float x0 = x[i], x1 = x[i + half];
         x[i] = x0 * c - x1 * s;
         x[i + half] = x0 * s + x1 * c;
@@ -323,7 +433,7 @@ static void rope_neox(float* x, int n_dims, int pos, float base) {
     }
 }
 
-static inline float silu(float x) { return x / (1.0f + expf(-x)); }
+static inline float silu(float x) { return x / (1.0f + orc_expf(-x)); }
 
 int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidden) {
     if (!d || !embeds || T <= 0 || d->past + T > d->max_seq) return -1;
@@ -345,19 +455,19 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
 
     for (int l = 0; l < m->n_layers; ++l) {
         const orc_layer* L = &m->layers[l];
-        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H);
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H, 256);
         orc_mul_mat_q8(L->wq, qd, H, xn, T, q);
         orc_mul_mat_q8(L->wk, kd, H, xn, T, k);
         orc_mul_mat_q8(L->wv, kd, H, xn, T, v);
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 float* qh = q + (size_t)t * qd + (size_t)h * hd;
-                rms_norm_mul(qh, L->q_norm, hd, m->eps, qh);
+                rms_norm_mul(qh, L->q_norm, hd, m->eps, qh, 128);
                 rope_neox(qh, hd, past + t, m->theta);
             }
             for (int h = 0; h < nkv; ++h) {
                 float* kh = k + (size_t)t * kd + (size_t)h * hd;
-                rms_norm_mul(kh, L->k_norm, hd, m->eps, kh);
+                rms_norm_mul(kh, L->k_norm, hd, m->eps, kh, 128);
                 rope_neox(kh, hd, past + t, m->theta);
             }
             /* KV store at past+t (src/qwen3.cpp:123-140). */
@@ -369,49 +479,75 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
             }
         }
         /* GQA attention with a causal mask when T > 1 (src/qwen3.cpp:158-189,
-         * src/qwen3_decoder.cpp:142-148, src/cpu_context.cpp:13-33). */
+         * src/qwen3_decoder.cpp:142-148): query row t sees positions
+         * [0, past + t], context over that valid length only
+         * (src/cpu_context.cpp:13-33).  softmax(s * 1/sqrt(hd)) is evaluated
+         * per 64-position chunk (chunk max m_c, e = exp(s - m_c), chunk sum l_c
+         * and context o_c) and the chunks are merged with weights
+         * exp(m_c - M); the same function as one softmax over the row, in the
+         * evaluation order shared with the CUDA kernels. */
 #pragma omp parallel for collapse(2) schedule(static)
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 const int kvh = h / group;
                 const float* qh = q + (size_t)t * qd + (size_t)h * hd;
                 const int valid = past + t + 1;
-                float* w = (float*)malloc(sizeof(float) * (size_t)kv);
-                float mx = -INFINITY;
-                for (int j = 0; j < kv; ++j) {
-                    const float* kj = d->k + kv_index(d, l, j) + (size_t)kvh * hd;
-                    float s = 0.0f;
-                    for (int e = 0; e < hd; ++e) s += kj[e] * qh[e];
-                    w[j] = j < valid ? s * scale : -INFINITY;
-                    mx = fmaxf(mx, w[j]);
+                const int n_chunks = (valid + 63) / 64;
+                float* cm = (float*)malloc(sizeof(float) * (size_t)n_chunks);
+                float* cl = (float*)malloc(sizeof(float) * (size_t)n_chunks);
+                float* co = (float*)malloc(sizeof(float) * (size_t)n_chunks * hd);
+                for (int c = 0; c < n_chunks; ++c) {
+                    float sc[64], e[64];
+                    float mx = -INFINITY;
+                    for (int p = 0; p < 64; ++p) {
+                        const int j = c * 64 + p;
+                        sc[p] = -INFINITY;
+                        if (j < valid) {
+                            const float* kj = d->k + kv_index(d, l, j) + (size_t)kvh * hd;
+                            float acc = 0.0f;
+                            for (int e2 = 0; e2 < hd; ++e2) acc = fmaf(qh[e2], kj[e2], acc);
+                            sc[p] = acc * scale;
+                        }
+                        mx = fmaxf(mx, sc[p]);
+                    }
+                    float pair[32];
+                    for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : orc_expf(sc[p] - mx);
+                    for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
+                    cm[c] = mx;
+                    cl[c] = warp_tree_sum(pair);
+                    const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
+                    for (int e2 = 0; e2 < hd; ++e2) {
+                        float acc = 0.0f;
+                        for (int p = 0; p < n_pos; ++p)
+                            acc = fmaf(e[p], (d->v + kv_index(d, l, c * 64 + p) + (size_t)kvh * hd)[e2], acc);
+                        co[(size_t)c * hd + e2] = acc;
+                    }
                 }
-                double sum = 0.0;
-                for (int j = 0; j < kv; ++j) {
-                    const float e = j < valid ? expf(w[j] - mx) : 0.0f;
-                    w[j] = e;
-                    sum += (double)e;
-                }
-                const float inv = (float)(1.0 / sum);
-                for (int j = 0; j < kv; ++j) w[j] *= inv;
+                float M = -INFINITY;
+                for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, cm[c]);
                 float* oh = o + (size_t)t * qd + (size_t)h * hd;
-                for (int e = 0; e < hd; ++e) {
-                    float acc = 0.0f;
-                    for (int j = 0; j < valid; ++j) acc += (d->v + kv_index(d, l, j) + (size_t)kvh * hd)[e] * w[j];
-                    oh[e] = acc;
+                for (int e2 = 0; e2 < hd; ++e2) {
+                    float Ls = 0.0f, acc = 0.0f;
+                    for (int c = 0; c < n_chunks; ++c) {
+                        const float wgt = orc_expf(cm[c] - M);
+                        Ls = fmaf(wgt, cl[c], Ls);
+                        acc = fmaf(wgt, co[(size_t)c * hd + e2], acc);
+                    }
+                    oh[e2] = acc / Ls;
                 }
-                free(w);
+                free(cm); free(cl); free(co);
             }
         }
         orc_mul_mat_q8(L->wo, H, qd, o, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
-        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H);
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 256);
         orc_mul_mat_q8(L->wgate, F, H, xn, T, g);
         orc_mul_mat_q8(L->wup, F, H, xn, T, u);
         for (size_t i = 0; i < (size_t)T * F; ++i) g[i] = silu(g[i]) * u[i];
         orc_mul_mat_q8(L->wdown, H, F, g, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
     }
-    for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H);
+    for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 256);
     d->past = kv;
     free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u);
     return 0;

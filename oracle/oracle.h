@@ -23,24 +23,36 @@
  *
  * The arithmetic of the ops above lives in ggml (commit eced84c, an
  * un-vendored submodule that is absent from the reference tree).  The oracle
- * restates ggml's published x86 CPU algorithms:
+ * restates ggml's published CPU algorithms:
  *   - q8_0 activation quantisation (x86 SIMD from_float): d = amax/127 stored as
  *     fp16 (round to nearest even), codes = round_half_even(x * (127/amax));
  *   - q8_0 weight quantisation (quantize_row_q8_0_ref, the algorithm of the
  *     gguf Python package the reference converter calls): codes =
  *     round_half_away(x * (1/d));
- *   - q8_0 x q8_0 dot: per 32-block, eight lanes of 4-element exact integer
- *     sums, scaled by fp32(d_w)*fp32(d_x) and fused-multiply-added into eight
- *     fp32 lanes, then the 8->4->2->1 horizontal add;
+ *   - q8_0 x q8_0 dot: exact integer sum per 32-block scaled by
+ *     fp32(d_w)*fp32(d_x) and accumulated in fp32;
  *   - rms_norm: sum of float squares accumulated in double, scale =
- *     1/sqrtf(mean + eps);
+ *     1/sqrtf(mean + eps), y = (x*scale)*w;
  *   - NEOX rope: theta advanced by repeated float multiplication with
  *     powf(base, -2/n_dims), pairs (i, i + n_dims/2);
- *   - soft_max_ext: x*scale + mask, max, expf(x - max), double sum, x*(1/sum).
+ *   - soft_max_ext: softmax(x*scale + causal mask), then P.V over the valid
+ *     length.
+ *
+ * Evaluation order.  ggml's float summation order differs between its own
+ * ISA paths (x86 lanes, ARM, the llamafile kernels), and a random-init q8_0
+ * network amplifies any reordering: one ulp moves an activation code, which
+ * the next layers carry on.  So this oracle fixes one documented order, and
+ * the CUDA kernels evaluate exactly the same operations in the same order,
+ * which makes the two bit-identical: q8_0 dots in 256-element slices (fmaf
+ * per block, slices added in order); squares summed in the kernels' tree
+ * (sum_squares_tree); softmax per 64-position chunk, merged with
+ * exp(m_c - M); exp/sin/cos are this library's own (orc_expf, orc_sincosf:
+ * Cody-Waite reduction and Taylor series in double).
  *
  * Parity status: the draft and greedy-choice functions are pinned by the 12
  * known-answer controls of tests/test_cpu_speculative.cpp and by vectors made
- * with the reference's own Python replay tool (cpu-lab/moss_ngram_audit.py).
+ * with the reference's own Python replay tool (cpu-lab/moss_ngram_audit.py);
+ * the q8_0 weight bytes by the gguf package the reference converter calls.
  * The decoder's floating-point arithmetic is PARITY UNPINNED against ggml
  * itself: ggml is not on disk and the reference's golden GGUFs are not in the
  * tree, so the float ops above are restated from ggml's published algorithms
@@ -129,6 +141,9 @@ void orc_quantize_act_q8(const float* x, int64_t k, void* out_blocks);
 void orc_quantize_ref_q8(const float* x, int64_t k, void* out_blocks);
 void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int T, float* y);
 void orc_set_threads(int n);
+/* The exp / sin / cos the oracle (and the CUDA kernels) evaluate. */
+float orc_expf(float x);
+void orc_sincosf(float x, float* s, float* c);
 
 #ifdef __cplusplus
 }

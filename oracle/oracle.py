@@ -72,6 +72,9 @@ def lib():
         L.orc_quantize_ref_q8.argtypes = [f32p, C.c_int64, vp]
         L.orc_mul_mat_q8.argtypes = [vp, C.c_int, C.c_int, f32p, C.c_int, f32p]
         L.orc_set_threads.argtypes = [C.c_int]
+        L.orc_expf.restype = C.c_float
+        L.orc_expf.argtypes = [C.c_float]
+        L.orc_sincosf.argtypes = [C.c_float, f32p, f32p]
         _LIB = L
     return _LIB
 
@@ -82,6 +85,16 @@ def _f32(a):
 
 def _i32(a):
     return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def expf(x: float) -> float:
+    return lib().orc_expf(float(x))
+
+
+def sincosf(x: float):
+    s, c = C.c_float(), C.c_float()
+    lib().orc_sincosf(float(x), C.byref(s), C.byref(c))
+    return s.value, c.value
 
 
 def set_threads(n: int):

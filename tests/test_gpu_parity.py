@@ -1,9 +1,17 @@
 """CUDA path vs the CPU oracle, through the C ABI (libmoss_transcribe_b200.so).
 
-Tolerances follow the north-star contract: logits within 2e-3 max-abs of the
-oracle; draft tables, accepted ids, counters and rollback positions exact
-(tokens are compared exactly; every case below has top-1/top-2 margins far
-above 1e-2 at the compared positions, which test_margins_are_decisive checks).
+The CUDA kernels and the oracle evaluate the same operations in the same
+order (q8_0 dots in 256-element slices, the kernels' reduction trees, chunked
+softmax, the library's own exp/sin/cos), so hidden rows, KV entries, logits,
+accepted ids, counters and rollback positions are compared bit for bit.  The
+north-star contract (logits within 2e-3 max-abs; tokens exact where the
+top-1/top-2 margin exceeds 1e-2) is strictly weaker than that.
+
+Why exactness rather than a tolerance: every projection re-quantises its input
+to q8_0, so one ulp of accumulation-order difference can move an activation
+code by a whole step, and a random-init network carries that on; measured on
+the Qwen3-0.6B shape, an order-only difference reached 0.07 max-abs in the
+logits after a 407-row prefill.
 """
 import json
 import os
@@ -36,15 +44,13 @@ def test_run_hidden_logits_and_kv_match_oracle(gpu_tiny, tiny_oracle):
     oh = od.run(prompt)
     gh = gd.run(prompt)
     assert gd.past_len == od.past_len == prompt.shape[0]
-    np.testing.assert_allclose(gh, oh, atol=2e-4, rtol=0)
-    for row in (0, prompt.shape[0] - 1):
-        ol = od.logits(oh[row])
-        assert np.abs(gd.logits_from_hidden(oh[row]) - ol).max() <= 1e-4  # LM head alone
-        assert np.abs(gd.logits_from_hidden(gh[row]) - ol).max() <= LOGIT_ATOL
+    np.testing.assert_array_equal(gh, oh)
+    for row in range(prompt.shape[0]):
+        np.testing.assert_array_equal(gd.logits_from_hidden(gh[row]), od.logits(oh[row]))
     for layer in range(tiny_oracle.shape.n_layers):
         for which in (0, 1):
-            np.testing.assert_allclose(gd.kv(layer, which, 0, prompt.shape[0]),
-                                       od.kv(layer, which, 0, prompt.shape[0]), atol=2e-4, rtol=0)
+            np.testing.assert_array_equal(gd.kv(layer, which, 0, prompt.shape[0]),
+                                          od.kv(layer, which, 0, prompt.shape[0]))
 
 
 @pytest.mark.parametrize("T", [1, 2, 3, 4, 8, 15, 16])
@@ -59,9 +65,9 @@ def test_verify_rows_at_every_width(gpu_tiny, tiny_oracle, T):
     rows = tiny_oracle.embed((np.arange(T) * 101 + 7) % tiny_oracle.shape.vocab)
     oh = od.run(rows)
     gh = gd.run(rows)
-    np.testing.assert_allclose(gh, oh, atol=2e-4, rtol=0)
+    np.testing.assert_array_equal(gh, oh)
     for t in range(T):
-        assert np.abs(gd.logits_from_hidden(gh[t]) - od.logits(oh[t])).max() <= LOGIT_ATOL
+        np.testing.assert_array_equal(gd.logits_from_hidden(gh[t]), od.logits(oh[t]))
 
 
 def test_rewind_then_append_matches_serial(gpu_tiny, tiny_oracle):
@@ -79,7 +85,7 @@ def test_rewind_then_append_matches_serial(gpu_tiny, tiny_oracle):
     od.run(prompt)
     od.run(rows[:2])
     o2 = od.run(tiny_oracle.embed([9]))
-    np.testing.assert_allclose(h2, o2, atol=2e-4, rtol=0)
+    np.testing.assert_array_equal(h2, o2)
 
 
 def test_device_draft_matches_reference_replay_tool(gpu_tiny):
@@ -198,7 +204,7 @@ def test_fp16_kv_matches_oracle_rounding(gpu_tiny, tiny_oracle):
     g_ids, g_c = gd.cpu_speculative_generate(prompt, 64, -1, k_max=8, n_min=3, n_max=3)
     assert g_ids == o_ids
     assert g_c["accepted"] == o_c["accepted"]
-    np.testing.assert_allclose(gd.kv(1, 1, 0, 40), od.kv(1, 1, 0, 40), atol=2e-3, rtol=1e-3)
+    np.testing.assert_array_equal(gd.kv(1, 1, 0, 40), od.kv(1, 1, 0, 40))
 
 
 def test_margins_are_decisive(gpu_tiny, tiny_oracle):

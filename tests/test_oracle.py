@@ -200,3 +200,32 @@ def test_gate_scenarios(tiny_oracle, scenario):
     for n, past, stop in commits:
         assert past == prefix + n - (1 if stop else 0)
     assert commits[-1][2]
+
+
+def _ulp_err(got, exact):
+    got = np.float32(got)
+    ref = np.float32(exact)
+    if ref == got:
+        return 0
+    return abs(int(np.array(got, np.float32).view(np.int32)) - int(np.array(ref, np.float32).view(np.int32)))
+
+
+def test_own_exp_is_correctly_rounded_within_one_ulp():
+    rng = np.random.default_rng(11)
+    xs = np.concatenate([rng.uniform(-100, 88, 4000), rng.uniform(-2, 2, 4000), [0.0, -0.0, 1e-30, -1e-30]])
+    worst = max(_ulp_err(oracle.expf(float(np.float32(x))), np.exp(np.float64(np.float32(x)))) for x in xs)
+    assert worst <= 1
+    assert oracle.expf(float("-inf")) == 0.0 and oracle.expf(200.0) == float("inf")
+    assert oracle.expf(0.0) == 1.0
+
+
+def test_own_sincos_is_correctly_rounded_within_one_ulp():
+    rng = np.random.default_rng(12)
+    # RoPE angles: positions up to 32k times 1e6^(-i/64).
+    xs = np.concatenate([rng.uniform(0, 32768, 3000), rng.uniform(-4, 4, 3000), np.arange(0, 2000, dtype=np.float64)])
+    worst = 0
+    for x in xs:
+        xf = np.float64(np.float32(x))
+        s, c = oracle.sincosf(float(xf))
+        worst = max(worst, _ulp_err(s, np.sin(xf)), _ulp_err(c, np.cos(xf)))
+    assert worst <= 1
