@@ -596,7 +596,9 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
                     MTB_CK(d, cudaStreamSynchronize(d->stream));
                     commit(user, d->h_ids, s.commit_n, s.past, s.commit_stop ? 1 : 0);
                 }
-                if (s.stop != STOP_NONE) break;
+                // Stopped on an accepted proposal: that commit was the last.  Stopped
+                // on the seed emitted after the commit: the loop top commits once more.
+                if (s.commit_stop) break;
             }
         } else {
             // Device-driven loop: the host only watches the stop flag, one step behind.

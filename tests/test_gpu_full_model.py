@@ -48,27 +48,34 @@ def test_config1_prefill_and_speculative_decode_bit_exact(full_oracle, full_gpu)
 
 @pytest.mark.parametrize("T", [1, 8, 16])
 def test_verify_microbench_step_bit_exact(full_oracle, full_gpu, T):
-    """KV prefilled to 2048 positions with synthetic fp16 values, one verify
-    step of T rows: hidden rows, logits choices and acceptance match."""
+    """KV prefilled to 2048 positions with synthetic fp16 values; the draft is
+    the target's own greedy continuation for floor((T-1)/2) tokens, then wrong
+    tokens.  One verify step: hidden rows bit-exact, floor((T-1)/2) accepted,
+    the bonus token is the target's next choice, the cache rolls back."""
+    V = full_oracle.shape.vocab
     od = oracle.OracleDecoder(full_oracle, 2048 + 32, kv_fp16=True)
     gd = capi.Decoder(full_gpu, 2048 + 32, capi.KV_F16, max_new=64)
     od.fill_synthetic_kv(2048, 1234)
     gd.fill_synthetic_kv(2048, 1234)
     for layer in (0, 27):
         np.testing.assert_array_equal(gd.kv(layer, 1, 2000, 48), od.kv(layer, 1, 2000, 48))
-    ids = fixture.lcg_ids(T, full_oracle.shape.vocab, seed=99)
-    rows = full_oracle.embed(ids)
-    oh = od.run(rows)
-    gh = gd.run(rows)
-    np.testing.assert_array_equal(gh, oh)
-    choices = [int(np.argmax(od.logits(oh[t]))) for t in range(T)]
-    # The step API: seed + proposals that match the first floor((T-1)/2) choices.
-    gd.rewind(2048)
+    seed = int(fixture.lcg_ids(1, V, seed=99)[0])
     keep = (T - 1) // 2
-    draft = choices[:keep] + [(c + 1) % full_oracle.shape.vocab for c in choices[keep:T - 1]]
-    gd.resume([int(ids[0])], 2048, 64, -1, k_max=15)
+    chain = [seed]  # serial greedy continuation on the oracle
+    for _ in range(keep + 1):
+        h = od.run(full_oracle.embed([chain[-1]]))
+        chain.append(int(np.argmax(od.logits(h[0]))))
+    draft = chain[1:1 + keep] + [(chain[1 + keep] + 1 + i) % V for i in range(T - 1 - keep)]
+    od.rewind(2048)
+    inputs = [seed] + draft
+    oh = od.run(full_oracle.embed(inputs))
+    gh = gd.run(full_oracle.embed(inputs))
+    np.testing.assert_array_equal(gh, oh)
+    gd.rewind(2048)
+    gd.resume([seed], 2048, 64, -1, k_max=15)
     c = gd.spec_step(draft)
     got, _ = gd.read_ids()
     assert c["accepted"] == keep
-    assert got == [int(ids[0])] + choices[:keep] + [choices[keep]]
+    assert got == chain[:keep + 2]
     assert c["past_len"] == 2048 + keep + 1
+    assert c["rewinds"] == (1 if T > keep + 1 else 0)

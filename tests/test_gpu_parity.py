@@ -137,8 +137,9 @@ def test_greedy_generate_matches_oracle_and_eos_stops(gpu_tiny, tiny_oracle):
     gd = capi.Decoder(gpu_tiny, 256, capi.KV_F32, max_new=128)
     o = od.greedy_generate(prompt, 60, -1)
     assert gd.greedy_generate(prompt, 60, -1) == o
-    eos = next(t for i, t in enumerate(o) if i >= 10 and t not in o[:i])
-    cut = o.index(eos)
+    fresh = [i for i in range(1, len(o)) if o[i] not in o[:i]]
+    cut = fresh[-1]  # the last id that first appears at its own position
+    eos = o[cut]
     assert gd.greedy_generate(prompt, 60, eos) == o[:cut + 1]
     ids, c = gd.cpu_speculative_generate(prompt, 60, eos, k_max=8)
     assert ids == o[:cut + 1] and c["stop_reason"] == capi.STOP_EOS
