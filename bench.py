@@ -1,0 +1,298 @@
+#!/usr/bin/env python3
+"""Benchmark of the strict speculative verify step.
+
+Workload (one "step"): the random-init Qwen3-0.6B q8_0 decoder, KV cache
+prefilled to 2048 positions with synthetic fp16 K/V, one verify step of
+k+1 = 8 rows (seed + 7 proposals), LM-head first max and acceptance.  The
+proposal is the target's own greedy continuation for floor(7/2) = 3 tokens
+followed by wrong tokens, so every step commits 3 accepted + 1 bonus = 4
+tokens and rolls the cache back by 4 rows; the step state is restored on the
+device before each step so every step sees the same 2048-position cache.
+
+  value  decoded tokens/s with inputs resident in HBM (device-to-device state
+         restore + the captured verify-step graph), whole job over N GPUs;
+  e2e    the same metric through the public C ABI with host buffers
+         (mtb_resume + mtb_spec_step + mtb_read_ids: host->device and
+         device->host copies inside the timed region).
+
+`--impl reference` times the CPU restatement of the reference path (the
+oracle: the reference's own ggml build cannot be compiled here) on the same
+workload with all host cores.  Multi-GPU (torchrun): one independent decoder
+replica per GPU, no collective on the data path (weak scaling); rank 0 prints.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "moss-transcribe.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "decoded tokens/s/GPU, strict spec-decode, Qwen3-0.6B q8_0; % of HBM roofline"
+UNIT = "tokens/s"
+KV_LEN = 2048
+T_ROWS = 8
+KV_SEED = 1234
+# Algorithmic bytes of one verify step (q8_0 weights + LM head once, F32 norms,
+# fp16 K+V reads of the cached positions, KV append, embedding rows).
+WEIGHT_BYTES = 633_233_408
+NORM_BYTES = 262_144
+KV_BYTES_PER_POS = 114_688
+EMBED_BYTES_PER_ROW = 1_088
+
+
+def step_bytes(kv_len: int, T: int) -> int:
+    return WEIGHT_BYTES + NORM_BYTES + kv_len * KV_BYTES_PER_POS + T * KV_BYTES_PER_POS + T * EMBED_BYTES_PER_ROW
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/mtb_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        return rank, local, world, dist, torch
+    return rank, local, world, None, None
+
+
+def greedy_draft(model_path: str, dec, kv_len: int, T: int, seed_tok: int, vocab: int):
+    """The target's greedy continuation (floor((T-1)/2) tokens) + wrong tokens."""
+    keep = (T - 1) // 2
+    dec.resume([seed_tok], kv_len, 64, -1, k_max=0)
+    for _ in range(keep + 1):
+        dec.spec_step(None)
+    ids, _ = dec.read_ids()
+    chain = ids[:keep + 2]
+    draft = chain[1:1 + keep] + [(chain[1 + keep] + 1 + i) % vocab for i in range(T - 1 - keep)]
+    return draft, keep
+
+
+def cpu_baseline(path: str, steps: int, sample_s: float = 20.0):
+    """The CPU restatement (oracle) on the same workload, all host cores."""
+    import oracle
+    from mtb import fixture
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    om = oracle.OracleModel(path)
+    V = om.shape.vocab
+    od = oracle.OracleDecoder(om, KV_LEN + 32, kv_fp16=True)
+    od.fill_synthetic_kv(KV_LEN, KV_SEED)
+    seed_tok = int(fixture.lcg_ids(1, V, seed=99)[0])
+    keep = (T_ROWS - 1) // 2
+    draft = [(seed_tok + 1 + i) % V for i in range(T_ROWS - 1)]
+    times = []
+    t_end = time.time() + sample_s
+    while len(times) < max(1, steps) and (time.time() < t_end or not times):
+        od.rewind(KV_LEN)
+        t0 = time.perf_counter()
+        # One verify step as the reference computes it: append T rows, then
+        # lazy per-row logits for the accepted prefix (keep + 1 rows).
+        h = od.run(om.embed([seed_tok] + draft))
+        for r in range(keep + 1):
+            od.logits(h[r])
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    return {"value": (keep + 1) / t, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{len(times)} verify steps of T={T_ROWS} at kv {KV_LEN} (fp16-rounded KV), "
+                      f"append + {keep + 1} lazy LM-head rows each, median {t * 1e3:.1f} ms"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, local, world, dist, torch = dist_setup(args)
+    from mtb import fixture
+    path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0)
+    config = {"workload": "configs[1] verify-step microbench: KV 2048 fp16 synthetic, k+1=8, draft matches 3",
+              "model": "Qwen3-0.6B decoder (random-init N(0,0.02), q8_0)", "kv_len": KV_LEN, "k_plus_1": T_ROWS,
+              "tokens_per_step": 4, "l2": "inputs larger than L2 (633 MB of weights streamed per step)",
+              "parallelism": f"replicas x{world}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(path, max(args.steps, 1))
+        line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32", "data": "synthetic", "config": config,
+                "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                                             "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    from mtb import capi
+    model = capi.Model(path, local)
+    dec = capi.Decoder(model, KV_LEN + 64, capi.KV_F16, max_new=64)
+    dec.fill_synthetic_kv(KV_LEN, KV_SEED)
+    V = model.vocab
+    seed_tok = int(fixture.lcg_ids(1, V, seed=99)[0])
+    draft, keep = greedy_draft(path, dec, KV_LEN, T_ROWS, seed_tok, V)
+    tokens_per_step = keep + 1
+
+    # ---- value: device-resident inputs, captured step graph ----------------
+    dec.resume([seed_tok], KV_LEN, 64, -1, k_max=15)
+    dec.snapshot_save()
+    import ctypes as C
+    draft_arr = np.asarray(draft, dtype=np.int32)
+    # Device copy of the proposal through the library's own upload path.
+    dbuf = _device_ids(dec, draft_arr)
+    for _ in range(max(3, args.warmup)):
+        dec.snapshot_restore_async()
+        dec.spec_step_async(dbuf, len(draft))
+    dec.sync()
+    ids, c = dec.read_ids()
+    assert c["accepted"] == keep and len(ids) == keep + 2, (ids, c)
+    launches = dec.step_kernel_launches() + 1  # + the proposal upload kernel
+    if dist:
+        torch.cuda.synchronize()
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    dec.sync()
+    dec.event_record(2)
+    for _ in range(args.steps):
+        dec.snapshot_restore_async()
+        dec.spec_step_async(dbuf, len(draft))
+    dec.event_record(3)
+    ms = dec.event_elapsed_ms(2, 3)
+    clk = clocks.stop()
+    ids, c = dec.read_ids()
+    assert c["accepted"] == keep, c
+    if dist:
+        t = torch.tensor([ms], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    value = world * args.steps * tokens_per_step / (ms / 1e3)
+
+    # ---- e2e: the public C ABI with host buffers ------------------------------
+    h0 = dec.transfer_bytes()
+    n_e2e = max(10, args.steps // 4)
+    for _ in range(3):
+        dec.resume([seed_tok], KV_LEN, 64, -1, k_max=15)
+        dec.spec_step(draft)
+        dec.read_ids()
+    h0 = dec.transfer_bytes()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        dec.resume([seed_tok], KV_LEN, 64, -1, k_max=15)
+        dec.spec_step(draft)
+        got, _ = dec.read_ids()
+    e2e_s = time.perf_counter() - t0
+    h1 = dec.transfer_bytes()
+    if dist:
+        t = torch.tensor([e2e_s], device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = {"value": world * n_e2e * tokens_per_step / e2e_s, "unit": UNIT,
+           "h2d_bytes_per_step": (h1[0] - h0[0]) // n_e2e + len(draft) * 4,
+           "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
+           "ms_per_step": e2e_s * 1e3 / n_e2e}
+
+    peak, peak_kind = measured_peaks()
+    bytes_step = step_bytes(KV_LEN, T_ROWS)
+    achieved = bytes_step / (ms_step / 1e3) / 1e9
+    roofline = {"bound": "hbm", "kernel": "verify step (one CUDA graph)", "achieved": round(achieved, 1),
+                "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "algorithmic_bytes": bytes_step, "traffic": None}
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32 (fp16 KV)", "data": "synthetic", "config": config,
+            "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(path, 5)
+    if rank == 0:
+        print(json.dumps(line))
+    dec.close()
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _device_ids(dec, arr: np.ndarray) -> int:
+    """Device buffer holding `arr` (int32), allocated with torch (plumbing)."""
+    import torch
+    t = torch.from_numpy(arr.copy()).to(f"cuda:{dec.model.device}")
+    torch.cuda.synchronize()
+    _KEEP.append(t)
+    return t.data_ptr()
+
+
+_KEEP = []
+
+if __name__ == "__main__":
+    main()

@@ -126,6 +126,8 @@ int mtb_event_record(mtb_decoder* d, int slot);          /* slot 0..15 */
 int mtb_event_elapsed_ms(mtb_decoder* d, int a, int b, float* ms);
 /* Kernel launches per verify step (counted when the step graph is built). */
 int mtb_step_kernel_launches(mtb_decoder* d);
+/* Host<->device bytes this decoder has copied so far (both cumulative). */
+int mtb_transfer_bytes(mtb_decoder* d, int64_t* h2d, int64_t* d2h);
 
 /* ---- controller pieces, run by the same device kernels the loop uses ---- */
 /* history: n host ids (n <= the decoder's max_new); out: up to `maximum` ids. */

@@ -59,6 +59,7 @@ struct mtb_decoder {
     float* row_buf = nullptr;      // [hidden]
     cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
     int launches = 0;
+    long long h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes this decoder has issued
     cudaEvent_t ev[16] = {};
     std::vector<void*> allocs;
     std::string error;
@@ -219,6 +220,7 @@ int load_model(mtb_model* m, const char* path) {
 }
 
 int refresh(mtb_decoder* d) {
+    d->d2h_bytes += sizeof(StepState);
     MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
     if (d->h_state->error) {
@@ -229,6 +231,7 @@ int refresh(mtb_decoder* d) {
 }
 
 int push_state(mtb_decoder* d) {
+    d->h2d_bytes += sizeof(StepState);
     MTB_CK(d, cudaMemcpyAsync(d->b.state, d->h_state, sizeof(StepState), cudaMemcpyHostToDevice, d->stream));
     return 0;
 }
@@ -650,6 +653,7 @@ int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_
     s.n_ids = n_ids;
     s.seed = ids[n_ids - 1];
     std::memcpy(d->h_ids, ids, size_t(n_ids) * 4);
+    d->h2d_bytes += size_t(n_ids) * 4;
     MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->h_ids, size_t(n_ids) * 4, cudaMemcpyHostToDevice, d->stream));
     if (push_state(d)) return -1;
     MTB_CK(d, cudaStreamSynchronize(d->stream));
@@ -718,6 +722,7 @@ int mtb_read_ids(mtb_decoder* d, int32_t* out, int max_out, int* n_out, mtb_coun
     if (refresh(d)) return -1;
     const int n = std::min(d->h_state->n_ids, std::max(0, max_out));
     if (out && n > 0) {
+        d->d2h_bytes += size_t(n) * 4;
         MTB_CK(d, cudaMemcpyAsync(out, d->b.ids, size_t(n) * 4, cudaMemcpyDeviceToHost, d->stream));
         MTB_CK(d, cudaStreamSynchronize(d->stream));
     }
@@ -745,6 +750,13 @@ int mtb_event_elapsed_ms(mtb_decoder* d, int a, int b, float* ms) {
     cudaSetDevice(d->device);
     MTB_CK(d, cudaEventSynchronize(d->ev[b]));
     MTB_CK(d, cudaEventElapsedTime(ms, d->ev[a], d->ev[b]));
+    return 0;
+}
+
+int mtb_transfer_bytes(mtb_decoder* d, int64_t* h2d, int64_t* d2h) {
+    if (!d) return -1;
+    if (h2d) *h2d = d->h2d_bytes;
+    if (d2h) *d2h = d->d2h_bytes;
     return 0;
 }
 

@@ -81,6 +81,7 @@ SIGNATURES = {
     "mtb_event_record": (C.c_int, [_vp, C.c_int]),
     "mtb_event_elapsed_ms": (C.c_int, [_vp, C.c_int, C.c_int, _f32p]),
     "mtb_step_kernel_launches": (C.c_int, [_vp]),
+    "mtb_transfer_bytes": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
 }
@@ -290,3 +291,25 @@ class Decoder:
 
     def step_kernel_launches(self) -> int:
         return lib().mtb_step_kernel_launches(self.ptr)
+
+    def transfer_bytes(self):
+        a, b = C.c_int64(), C.c_int64()
+        lib().mtb_transfer_bytes(self.ptr, C.byref(a), C.byref(b))
+        return a.value, b.value
+
+    def spec_step_async(self, draft_device_ptr, n_draft: int):
+        self._check(lib().mtb_spec_step_async(self.ptr, C.c_void_p(draft_device_ptr), int(n_draft)), "spec_step_async")
+
+    def snapshot_save(self):
+        self._check(lib().mtb_snapshot_save(self.ptr), "snapshot_save")
+
+    def snapshot_restore_async(self):
+        self._check(lib().mtb_snapshot_restore_async(self.ptr), "snapshot_restore")
+
+    def event_record(self, slot: int):
+        self._check(lib().mtb_event_record(self.ptr, int(slot)), "event_record")
+
+    def event_elapsed_ms(self, a: int, b: int) -> float:
+        ms = C.c_float()
+        self._check(lib().mtb_event_elapsed_ms(self.ptr, int(a), int(b), C.byref(ms)), "event_elapsed")
+        return ms.value
