@@ -137,6 +137,26 @@ int mtb_ngram_draft(mtb_decoder* d, const int32_t* history, int n, int maximum, 
 int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t* history, int n, float penalty,
                       int32_t* choice);
 
+/* ---- LM head without device allocation ----
+ * No counterpart in the reference (its LM head, Qwen3Decoder::logits_from_hidden,
+ * allocates a ggml graph per call).  For callers that cannot allocate device
+ * memory: serving processes that give all free device memory to their own pool
+ * allocator at start-up and forbid later cudaMalloc, because a late cudaMalloc
+ * can fail for lack of room and cudaMalloc/cudaFree synchronise the device.
+ *
+ * hidden_rows: DEVICE pointer to T final-normed hidden rows [T][hidden];
+ * choices: DEVICE pointer to T int32, receives each row's first-max token id
+ * (mtb_greedy_choice without penalty).  stream: a cudaStream_t, NULL for the
+ * default stream; the call is asynchronous on it.  Limits: T in [1, 16],
+ * hidden <= 4096; larger sizes return -2 with mtb_noalloc_error() set.
+ * Intermediates live in one static device array of about 148 KB that every
+ * device loading this library holds until exit; the first call on a device
+ * looks its address up (call it once before any stream capture).  Calls share
+ * that array: calls that overlap on the GPU race.  Nothing is allocated: no
+ * cudaMalloc, cudaFree or allocating library routine is called. */
+int mtb_lm_head_argmax_noalloc(const mtb_model* m, const float* hidden_rows, int T, int32_t* choices, void* stream);
+const char* mtb_noalloc_error(void);
+
 #ifdef __cplusplus
 }
 #endif

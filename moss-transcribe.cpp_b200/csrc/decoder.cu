@@ -380,6 +380,15 @@ int mtb_model_load(const char* path, int device, mtb_model** out) {
 void mtb_model_free(mtb_model* m) { delete m; }
 const char* mtb_model_error(const mtb_model* m) { return m ? m->error.c_str() : ""; }
 
+// Device-side view of a loaded model for the other translation units (not
+// part of the public ABI).
+__attribute__((visibility("hidden"))) int mtb_model_device_view(const mtb_model* m, const void** view, int* device) {
+    if (!m || !view || !device) return -1;
+    *view = &m->dm;
+    *device = m->device;
+    return 0;
+}
+
 int mtb_model_dims(const mtb_model* m, int32_t* o) {
     if (!m || !o) return -1;
     const ModelDims& d = m->dm.dims;

@@ -796,6 +796,20 @@ __global__ void k_set_forced(StepState* st, const int32_t* src, int n, int vocab
     st->n_prop = n;
 }
 
+// Step state for a standalone launch sequence: only T is read by the kernels.
+__global__ void k_state_rows(StepState* st, int T) {
+    StepState z = {};
+    z.T = T;
+    *st = z;
+}
+
+// First max of each row's LM-head partials, written to `out` (rows < T).
+__global__ void k_reduce_choices_out(StepState* st, const float2* lm_val, int lm_blocks, int32_t* out) {
+    reduce_choices(st, lm_val, lm_blocks);
+    __syncthreads();
+    if ((int)threadIdx.x < st->T) out[threadIdx.x] = st->choice[threadIdx.x];
+}
+
 // Host-supplied rows (prefill chunks, run()): positions before..before+T-1.
 __global__ void k_rows_begin(StepState* st, int T) {
     st->before = st->past;
@@ -949,6 +963,18 @@ void launch_choice_args(const float* logits, int n_raw, const int32_t* hist, int
 
 void launch_set_forced(const StepBuffers& b, const int32_t* src, int n, int vocab, cudaStream_t s) {
     k_set_forced<<<1, 1, 0, s>>>(b.state, src, n, vocab);
+}
+
+void launch_lm_argmax_rows(const DeviceModel& m, StepState* state, const float* rows, int T, uint8_t* act_q,
+                           float* act_d, float2* partials, int32_t* choices, cudaStream_t s) {
+    const int lm_blocks = lm_head_blocks(m.dims.vocab);
+    k_state_rows<<<1, 1, 0, s>>>(state, T);
+    k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(state, rows, m.dims.hidden,
+                                                                                        act_q, act_d);
+    GemvArgs a{m.embd, m.dims.vocab / kTileRows, m.dims.hidden / kTileK, act_q, act_d,
+               nullptr, m.dims.vocab, state, partials, nullptr};
+    gemv<EPI_ARGMAX, 8>(a, lm_blocks, s);
+    k_reduce_choices_out<<<1, 512, 0, s>>>(state, partials, lm_blocks, choices);
 }
 
 void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s) { k_rows_begin<<<1, 1, 0, s>>>(b.state, T); }

@@ -69,6 +69,10 @@ void launch_draft_args(const int32_t* ids, int n, int maximum, int n_min, int n_
 void launch_choice_args(const float* logits, int n_raw, const int32_t* hist, int n_hist, float p, int* out,
                         cudaStream_t s);
 void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s);
+// LM head + first max of T host-independent device rows into `choices`, with
+// every intermediate in caller-provided device scratch (no allocation).
+void launch_lm_argmax_rows(const DeviceModel& m, StepState* state, const float* rows, int T, uint8_t* act_q,
+                           float* act_d, float2* partials, int32_t* choices, cudaStream_t s);
 void launch_set_forced(const StepBuffers& b, const int32_t* src, int n, int vocab, cudaStream_t s);
 void launch_rows_end(const StepBuffers& b, cudaStream_t s);
 

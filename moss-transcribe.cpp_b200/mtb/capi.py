@@ -84,6 +84,8 @@ SIGNATURES = {
     "mtb_transfer_bytes": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
+    "mtb_lm_head_argmax_noalloc": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
+    "mtb_noalloc_error": (C.c_char_p, []),
 }
 
 
