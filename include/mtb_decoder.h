@@ -79,6 +79,10 @@ void mtb_model_free(mtb_model* m);
 const char* mtb_model_error(const mtb_model* m);
 /* hidden, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab, eos */
 int mtb_model_dims(const mtb_model* m, int32_t* out8);
+/* CTAs of the persistent verify-step kernel (one per SM), or 0 when verify
+ * steps run as a graph of separate kernels (unsupported shape, repetition
+ * penalty > 1, or MTB_NO_PERSISTENT set at load). */
+int mtb_model_persistent_grid(const mtb_model* m);
 
 /* ---- decoder: KV cache (paged, 64 positions per page) and step state ---- */
 int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_decoder** out);
@@ -126,6 +130,14 @@ int mtb_event_record(mtb_decoder* d, int slot);          /* slot 0..15 */
 int mtb_event_elapsed_ms(mtb_decoder* d, int a, int b, float* ms);
 /* Kernel launches per verify step (counted when the step graph is built). */
 int mtb_step_kernel_launches(mtb_decoder* d);
+/* Timeline of the last persistent verify step (decoder created with
+ * MTB_PROFILE=1 in the environment): out[2b], out[2b+1] = CTA 0's arrival and
+ * release at grid barrier b, out[2*512], out[2*512+1] = kernel start and end,
+ * out[2*512 + 2 + 4b + k] = sub-phase mark k of phase b (0 when unused),
+ * out[6*512 + 2 + 512 c + b] = CTA c's arrival at barrier b, all in ns of the
+ * GPU global timer; the profile counterpart of the
+ * reference's MTD_PROFILE phase timers (src/cpu_profile.cpp:23-68). */
+int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out);
 /* Host<->device bytes this decoder has copied so far (both cumulative). */
 int mtb_transfer_bytes(mtb_decoder* d, int64_t* h2d, int64_t* d2h);
 

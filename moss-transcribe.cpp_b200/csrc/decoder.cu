@@ -15,6 +15,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -32,6 +33,8 @@ struct mtb_model {
     int device = 0;
     DeviceModel dm{};
     std::vector<LayerWeights> layers;
+    LayerWeights* layers_dev = nullptr;  // device copy for the persistent kernel
+    int mega_grid = 0;                   // 0: the persistent kernel is not used
     std::vector<void*> allocs;
     std::string error;
     int eos = -1;
@@ -48,6 +51,7 @@ struct mtb_decoder {
     int max_seq = 0, kv_type = 0, max_new = 0;
     KvCache kv{};
     StepBuffers b{};
+    MegaBuffers mb{};
     StepState* h_state = nullptr;  // pinned mirror
     float* h_rows = nullptr;       // pinned staging [kTMax][hidden]
     int32_t* h_ids = nullptr;      // pinned [max_new]
@@ -212,9 +216,17 @@ int load_model(mtb_model* m, const char* path) {
             return -1;
     }
     m->dm.layers = m->layers.data();
+    if (dalloc(m->allocs, m->error, &m->layers_dev, sizeof(LayerWeights) * m->layers.size())) return -1;
+    MTB_CK(m, cudaMemcpy(m->layers_dev, m->layers.data(), sizeof(LayerWeights) * m->layers.size(),
+                         cudaMemcpyHostToDevice));
     // Same powf as the CPU path so the RoPE angles advance identically.
     m->dm.theta_scale = std::pow(d.theta, -2.0f / float(kHeadDim));
     MTB_CK(m, configure_kernels());
+    if (!std::getenv("MTB_NO_PERSISTENT")) {
+        int grid = 0;
+        MTB_CK(m, configure_megakernel(m->device, d.hidden, &grid));
+        m->mega_grid = megakernel_supports(d, grid) ? grid : 0;
+    }
     MTB_CK(m, cudaDeviceSynchronize());
     return 0;
 }
@@ -224,7 +236,8 @@ int refresh(mtb_decoder* d) {
     MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
     if (d->h_state->error) {
-        d->error = "device reported an out-of-range token id";
+        d->error = d->h_state->error == 2 ? "verify step gave up waiting (persistent kernel timeout)"
+                                          : "device reported an out-of-range token id";
         return -1;
     }
     return 0;
@@ -241,7 +254,13 @@ cudaGraphExec_t step_graph(mtb_decoder* d, int mode, bool penalty) {
     if (g) return g;
     cudaGraph_t graph = nullptr;
     if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return nullptr;
-    launch_step(d->model->dm, d->kv, d->b, mode, penalty, d->stream);
+    if (d->model->mega_grid > 0 && !penalty) {
+        // Draft, then the whole verify step as one persistent kernel.
+        launch_draft(d->b, mode, d->stream);
+        launch_step_persistent(d->model->dm, d->model->layers_dev, d->kv, d->b, d->mb, d->model->mega_grid, d->stream);
+    } else {
+        launch_step(d->model->dm, d->kv, d->b, mode, penalty, d->stream);
+    }
     if (cudaStreamEndCapture(d->stream, &graph) != cudaSuccess || !graph) return nullptr;
     size_t n = 0;
     cudaGraphGetNodes(graph, nullptr, &n);
@@ -389,6 +408,8 @@ __attribute__((visibility("hidden"))) int mtb_model_device_view(const mtb_model*
     return 0;
 }
 
+int mtb_model_persistent_grid(const mtb_model* m) { return m ? m->mega_grid : -1; }
+
 int mtb_model_dims(const mtb_model* m, int32_t* o) {
     if (!m || !o) return -1;
     const ModelDims& d = m->dm.dims;
@@ -428,6 +449,19 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         b.lm_blocks = lm_head_blocks(dm.vocab);
         auto& A = d->allocs;
         auto& E = d->error;
+        uint8_t* zero_region = nullptr;
+        const size_t n_tickets = size_t(dm.n_layers) * (F / 32), n_head_tickets = size_t(dm.n_layers) * (dm.n_heads + 2 * dm.n_kv);
+        d->mb.zero_bytes = 16 + (n_tickets + n_head_tickets) * 4;
+        if (dalloc(A, E, &d->mb.act2_q, size_t(F / 32) * 512) || dalloc(A, E, &d->mb.act2_d, size_t(F / 32) * 16 * 4) ||
+            dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
+            dalloc(A, E, &zero_region, d->mb.zero_bytes))
+            return bail();
+        if (std::getenv("MTB_PROFILE") && dalloc(A, E, &d->mb.timeline, (6 * kMaxBarriers + 2 + 256 * kMaxBarriers) * 8)) return bail();
+        d->mb.bar = reinterpret_cast<unsigned*>(zero_region);
+        d->mb.abort_flag = reinterpret_cast<int*>(zero_region + 4);
+        d->mb.tickets = reinterpret_cast<unsigned*>(zero_region + 16);
+        d->mb.head_tickets = d->mb.tickets + n_tickets;
+        if (dalloc(A, E, &d->mb.qr, size_t(kTMax) * dm.n_heads * kHeadDim * 4)) return bail();
         if (dalloc(A, E, &kvb, size_t(n_pages) * d->kv.page_elems * esz) || dalloc(A, E, &pages, size_t(n_pages) * 4) ||
             dalloc(A, E, &b.state, sizeof(StepState)) || dalloc(A, E, &b.ids, size_t(max_new) * 4) ||
             dalloc(A, E, &b.x, size_t(kTMax) * H * 4) || dalloc(A, E, &b.qkv, size_t(kTMax) * (qd + 2 * kd) * 4) ||
@@ -766,6 +800,18 @@ int mtb_transfer_bytes(mtb_decoder* d, int64_t* h2d, int64_t* d2h) {
     if (!d) return -1;
     if (h2d) *h2d = d->h2d_bytes;
     if (d2h) *d2h = d->d2h_bytes;
+    return 0;
+}
+
+int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out) {
+    if (!d || !out || !n_out) return -1;
+    *n_out = 0;
+    if (!d->mb.timeline) return fail(d->error, "set MTB_PROFILE=1 before creating the decoder");
+    cudaSetDevice(d->device);
+    const int n = std::min(max_out, 6 * kMaxBarriers + 2 + 256 * kMaxBarriers);
+    MTB_CK(d, cudaMemcpyAsync(out, d->mb.timeline, size_t(n) * 8, cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    *n_out = n;
     return 0;
 }
 

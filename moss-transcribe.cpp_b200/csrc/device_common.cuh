@@ -1,0 +1,160 @@
+// Device helpers shared by the verify-step kernels (kernels.cu) and the
+// persistent verify-step kernel (megakernel.cu).
+#pragma once
+
+#include "mtb_internal.hpp"
+#include "exact_math.cuh"
+#include "kernels.hpp"
+
+#include <cuda_fp16.h>
+
+namespace mtb {
+namespace dev {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+    // D[16 tokens x 8 weight rows] = A[16 x 32] * B[32 x 8], int8 -> int32.
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint4 ld_stream_u4(const uint8_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint2 ld_nc_u2(const uint8_t* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float h2f_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
+__device__ __forceinline__ float h2f_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// amax of |v| over the 32 lanes: non-negative floats order like their bit
+// patterns, so one integer max reduction gives exactly fmaxf's result.
+__device__ __forceinline__ float warp_absmax(float v) {
+    return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v))));
+}
+
+// q8_0 scales of up to 32 blocks at once: amax[i] is uniform across the warp;
+// lane i computes d = amax/127 and 1/d' = 127/amax of block i (correctly
+// rounded divisions, one per lane instead of 2N in sequence), then block i's
+// pair is broadcast back by shuffles.  Results equal the per-block formulas.
+template <int N>
+__device__ __forceinline__ void q8_scales(const float (&amax)[N], float (&d)[N], float (&inv)[N]) {
+    static_assert(N <= 32, "one block per lane");
+    const int lane = threadIdx.x & 31;
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (lane == i) mine = amax[i];
+    const float dl = mine / 127.f;
+    const float il = mine != 0.0f ? 127.f / mine : 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        d[i] = __shfl_sync(0xffffffffu, dl, i);
+        inv[i] = __shfl_sync(0xffffffffu, il, i);
+    }
+}
+
+// Byte offset of activation element (row r in 0..15, column c in 0..31) inside
+// one 512-byte block of the m16n8k32 A-fragment order: lane (g, t) holds
+// {A[g][4t..], A[g+8][4t..], A[g][16+4t..], A[g+8][16+4t..]}.
+__device__ __forceinline__ int frag_offset(int r, int c) {
+    const int g = r & 7, hi = r >> 3, t4 = (c & 15) >> 2, part = c >> 4;
+    return (g * 4 + t4) * 16 + (part * 2 + hi) * 4 + (c & 3);
+}
+
+// q8_0 quantisation of one 32-element block held one element per lane, as
+// ggml's x86 from_float: d = amax/127 (stored fp16), code = rint(x * 127/amax).
+__device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, uint8_t* act_q, float* act_d) {
+    const int lane = threadIdx.x & 31;
+    const float amax = warp_absmax(v);
+    const float d = amax / 127.f;
+    const float id = amax != 0.0f ? 127.f / amax : 0.0f;
+    const int q = __float2int_rn(__fmul_rn(v, id));
+    act_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)q;
+    if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
+}
+
+__device__ __forceinline__ long long kv_offset(const KvCache& kv, int n_kv, int layer, int which, int head, int pos) {
+    const int page = kv.pages[pos / kPage];
+    return (long long)page * kv.page_elems +
+           ((((long long)layer * 2 + which) * n_kv + head) * kPage + (pos % kPage)) * kHeadDim;
+}
+
+__device__ __forceinline__ float kv_load(const KvCache& kv, long long off) {
+    return kv.type == KV_F16 ? __half2float(reinterpret_cast<const __half*>(kv.base)[off])
+                             : reinterpret_cast<const float*>(kv.base)[off];
+}
+
+__device__ __forceinline__ void kv_store(const KvCache& kv, long long off, float v) {
+    if (kv.type == KV_F16) reinterpret_cast<__half*>(kv.base)[off] = __float2half_rn(v);
+    else reinterpret_cast<float*>(kv.base)[off] = v;
+}
+
+
+// Emit one id into the generated stream (src/cpu_speculative.cpp:108-116).
+__device__ __forceinline__ void emit_id(StepState* st, int32_t* ids, int id) {
+    ids[st->n_ids++] = id;
+    if (id == st->eos) st->stop = STOP_EOS;
+    else if (st->n_ids >= st->max_new) st->stop = STOP_LIMIT;
+}
+
+// Strict acceptance and logical rollback (src/cpu_speculative.cpp:142-153)
+// given the per-row choices, then the next seed (the choice of the last kept
+// row, :119).  One thread.
+__device__ __forceinline__ void accept_choices(StepState* st, int32_t* ids) {
+    const int np = st->n_prop;
+    st->target_calls += 1;
+    st->drafted_calls += np > 0;
+    st->proposed += np;
+    st->target_input_tokens += st->T;
+    int keep = 1;
+    for (int i = 0; i < np; ++i) {
+        const int prop = st->tokens[1 + i];
+        if (prop != st->choice[i]) break;
+        st->accepted += 1;
+        emit_id(st, ids, prop);
+        if (st->stop) break;  // the terminating token is not kept in the cache
+        ++keep;
+    }
+    const int position = st->before + keep;
+    if (st->before + st->T != position) st->rewinds += 1;
+    st->past = position;
+    st->commit_n = st->n_ids;
+    st->commit_stop = st->stop != STOP_NONE;
+    if (!st->stop) {
+        st->seed = st->choice[keep - 1];
+        emit_id(st, ids, st->seed);
+    }
+}
+
+}  // namespace dev
+}  // namespace mtb

@@ -11,8 +11,7 @@
 // q8_0 contract (activation quantised to q8_0 before every q8_0 dot, exact
 // integer block sums, fp32 d_w*d_x scaling) follows ggml's CPU mul_mat as used
 // by src/cpu_projection.cpp:16-37.
-#include "kernels.hpp"
-#include "exact_math.cuh"
+#include "device_common.cuh"
 
 #include <cuda_fp16.h>
 #include <cfloat>
@@ -22,86 +21,7 @@ namespace mtb {
 
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
-    // D[16 tokens x 8 weight rows] = A[16 x 32] * B[32 x 8], int8 -> int32.
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};\n"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1), "r"(0));
-}
-
-__device__ __forceinline__ uint4 ld_stream_u4(const uint8_t* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ uint2 ld_nc_u2(const uint8_t* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ float h2f_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
-__device__ __forceinline__ float h2f_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
-
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-    return v;
-}
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-// Byte offset of activation element (row r in 0..15, column c in 0..31) inside
-// one 512-byte block of the m16n8k32 A-fragment order: lane (g, t) holds
-// {A[g][4t..], A[g+8][4t..], A[g][16+4t..], A[g+8][16+4t..]}.
-__device__ __forceinline__ int frag_offset(int r, int c) {
-    const int g = r & 7, hi = r >> 3, t4 = (c & 15) >> 2, part = c >> 4;
-    return (g * 4 + t4) * 16 + (part * 2 + hi) * 4 + (c & 3);
-}
-
-// q8_0 quantisation of one 32-element block held one element per lane, as
-// ggml's x86 from_float: d = amax/127 (stored fp16), code = rint(x * 127/amax).
-__device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, uint8_t* act_q, float* act_d) {
-    const int lane = threadIdx.x & 31;
-    const float amax = warp_max(fabsf(v));
-    const float d = amax / 127.f;
-    const float id = amax != 0.0f ? 127.f / amax : 0.0f;
-    const int q = __float2int_rn(__fmul_rn(v, id));
-    act_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)q;
-    if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
-}
-
-__device__ __forceinline__ long long kv_offset(const KvCache& kv, int n_kv, int layer, int which, int head, int pos) {
-    const int page = kv.pages[pos / kPage];
-    return (long long)page * kv.page_elems +
-           ((((long long)layer * 2 + which) * n_kv + head) * kPage + (pos % kPage)) * kHeadDim;
-}
-
-__device__ __forceinline__ float kv_load(const KvCache& kv, long long off) {
-    return kv.type == KV_F16 ? __half2float(reinterpret_cast<const __half*>(kv.base)[off])
-                             : reinterpret_cast<const float*>(kv.base)[off];
-}
-
-__device__ __forceinline__ void kv_store(const KvCache& kv, long long off, float v) {
-    if (kv.type == KV_F16) reinterpret_cast<__half*>(kv.base)[off] = __float2half_rn(v);
-    else reinterpret_cast<float*>(kv.base)[off] = v;
-}
+using namespace dev;
 
 // ------------------------------------------------------------------ repack
 
@@ -242,8 +162,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
         if (warp < RPB) {
             const int r = warp, rg = rg0 + r;
             auto slice_sum = [&](int rr) {
-                float4 y = s_part[(rr * S) * 32 + lane];
-                for (int sl = 1; sl < S; ++sl) {
+                float4 y = make_float4(0.f, 0.f, 0.f, 0.f);  // 0 + p0 + p1 + ... as on the CPU
+                for (int sl = 0; sl < S; ++sl) {
                     const float4 o = s_part[(rr * S + sl) * 32 + lane];
                     y.x = y.x + o.x; y.y = y.y + o.y; y.z = y.z + o.z; y.w = y.w + o.w;
                 }
@@ -574,13 +494,6 @@ __global__ void k_embed(StepState* st, const uint8_t* __restrict__ embd, int hid
     }
 }
 
-// Emit one id into the generated stream (src/cpu_speculative.cpp:108-116).
-__device__ void emit_id(StepState* st, int32_t* ids, int id) {
-    ids[st->n_ids++] = id;
-    if (id == st->eos) st->stop = STOP_EOS;
-    else if (st->n_ids >= st->max_new) st->stop = STOP_LIMIT;
-}
-
 // n-gram draft over the generated ids (src/cpu_speculative.cpp:45-56): the
 // longest suffix size in [n_min, n_max] with an earlier occurrence, latest
 // occurrence first.  For each end position e < n the common suffix length
@@ -688,29 +601,7 @@ __global__ void k_accept(StepState* st, int32_t* ids, const float2* lm_val, int 
     if (!choices_ready) reduce_choices(st, lm_val, lm_blocks);
     __syncthreads();
     if (threadIdx.x != 0) return;
-    const int np = st->n_prop;
-    st->target_calls += 1;
-    st->drafted_calls += np > 0;
-    st->proposed += np;
-    st->target_input_tokens += st->T;
-    int keep = 1;
-    for (int i = 0; i < np; ++i) {
-        const int prop = st->tokens[1 + i];
-        if (prop != st->choice[i]) break;
-        st->accepted += 1;
-        emit_id(st, ids, prop);
-        if (st->stop) break;  // the terminating token is not kept in the cache
-        ++keep;
-    }
-    const int position = st->before + keep;
-    if (st->before + st->T != position) st->rewinds += 1;
-    st->past = position;
-    st->commit_n = st->n_ids;
-    st->commit_stop = st->stop != STOP_NONE;
-    if (!st->stop) {
-        st->seed = st->choice[keep - 1];
-        emit_id(st, ids, st->seed);
-    }
+    accept_choices(st, ids);
 }
 
 // Seed after prefill: the choice of the last prefilled row, emitted.
@@ -943,6 +834,11 @@ void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, 
         k_choice_penalty<<<kTMax, 1024, bits, s>>>(b.state, b.ids, b.logits, m.dims.vocab);
     }
     k_accept<<<1, 512, 0, s>>>(b.state, b.ids, b.lm_val, b.lm_blocks, penalty_path ? 1 : 0);
+}
+
+void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s) {
+    if (draft_mode == 0) k_draft<<<1, 256, 0, s>>>(b.state, b.ids);
+    else if (draft_mode == 1) k_draft_forced<<<1, 1, 0, s>>>(b.state);
 }
 
 void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, bool lm, bool want_logits,

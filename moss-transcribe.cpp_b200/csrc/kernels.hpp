@@ -25,6 +25,22 @@ struct StepBuffers {
     int lm_blocks;
 };
 
+// Extra buffers of the persistent verify-step kernel.
+struct MegaBuffers {
+    uint8_t* act2_q;     // SwiGLU fragments (K = ffn)
+    float* act2_d;
+    float2* lm_val;      // [grid][16] LM-head partials
+    unsigned* bar;       // zeroed before every launch, together with abort_flag and tickets
+    int* abort_flag;
+    unsigned* tickets;   // [n_layers][ffn / 32]
+    unsigned* head_tickets;  // [n_layers][n_heads + 2 n_kv]
+    float* qr;           // [16][n_heads][128] prepared q rows
+    size_t zero_bytes;
+    unsigned long long* timeline;  // optional [2 * kMaxBarriers + 2] (MTB_PROFILE=1)
+};
+
+constexpr int kMaxBarriers = 512;
+
 struct KvCache {
     void* base;              // pages of [n_layers][2][n_kv][kPage][128] elements
     const int32_t* pages;    // logical page -> physical page
@@ -63,6 +79,15 @@ void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* 
 void launch_prefill_seed(const StepBuffers& b, cudaStream_t s);
 
 int lm_head_blocks(int vocab);
+
+// Persistent verify step (megakernel.cu).
+int megakernel_smem_bytes();
+cudaError_t configure_megakernel(int device, int hidden, int* grid_out);
+bool megakernel_supports(const ModelDims& d, int grid);
+cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
+                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s);
+// The draft part of a step alone (0: on-device n-gram, 1: host-forced proposal).
+void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s);
 cudaError_t configure_kernels();
 void launch_draft_args(const int32_t* ids, int n, int maximum, int n_min, int n_max, int32_t* out, int* n_out,
                        cudaStream_t s);

@@ -1,0 +1,1256 @@
+// The verify step as one persistent kernel (one CTA per SM).
+//
+// Why: a verify step is 28 layers x ~10 dependent operations of a few
+// microseconds each; as separate launches most of the step is launch gaps.
+// Here every operation is a phase of one kernel, phases are separated by grid
+// barriers, and one producer warp per CTA streams every weight tile the CTA
+// will need (all layers, then the LM head) through a ring of shared-memory
+// slots with cp.async.bulk + mbarriers.  Weights do not depend on the step's
+// activations, so HBM keeps streaming while the consumer warps wait at
+// barriers; the consumers find their tiles already in shared memory.
+//
+// Phases per layer (src/qwen3.cpp:62-218):
+//   A  RMSNorm + q8_0 quantise (every CTA, into shared memory); QKV rows
+//   B  attention per (64-position chunk, kv head): per-head RMSNorm + RoPE of
+//      q (and of k for the step's new positions, stored to the KV cache),
+//      scores, chunk softmax, P.V partials
+//   C  chunk merge per (row, q head) and q8_0 quantise of the context
+//   D  O projection + residual
+//   E  RMSNorm + quantise; gate/up + SwiGLU; a ticket per 32-feature block
+//      lets the last of its four producers quantise it for the down projection
+//   F  down projection + residual
+// then the final RMSNorm, the LM head with a fused first max, and the
+// acceptance / rollback of src/cpu_speculative.cpp:142-153 (CTA 0).
+//
+// Every operation evaluates the same arithmetic in the same order as the
+// multi-kernel path (kernels.cu) and the CPU restatement, so the results are
+// identical bit for bit.  All waits (grid barrier, mbarriers) are bounded by
+// a time limit; on expiry the kernel records an error in the step state,
+// raises an abort flag that every other wait watches, drains its own bulk
+// copies and returns.
+#include "device_common.cuh"
+
+#include <algorithm>
+
+namespace mtb {
+namespace {
+
+using namespace dev;
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kMegaThreads = kConsumers + 32;   // + the producer warp
+constexpr int kSlotBytes = 16 * kTileBytes;      // 8704: 16 tiles = 4 slices of 256 K
+constexpr int kRingSlots = 16;
+constexpr int kRegionBytes = 60 * 1024;          // activation fragments / attention scratch
+constexpr int kRopeBytes = kTMax * 64 * 2 * 4;   // cos/sin of the step's positions
+constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr int kTimelineStart = 2 * kMaxBarriers;       // kernel start / end slots
+constexpr int kArrivalBase = 6 * kMaxBarriers + 2;     // [cta][barrier] arrivals after the marks
+
+struct MegaArgs {
+    ModelDims d;
+    const LayerWeights* layers;  // device array
+    const uint8_t* embd;
+    const float* output_norm;
+    float theta_scale;
+    KvCache kv;
+    StepState* state;
+    int32_t* ids;
+    float* x;        // [16][H]
+    float* qkv;      // [16][qd + 2 kd]
+    float* gu;       // [16][F]
+    float* qr;       // [16][n_heads][128] q rows after RMSNorm + RoPE
+    uint8_t* act_q;  // context fragments (K = qd), then reused for K = F below
+    float* act_d;
+    uint8_t* act2_q; // SwiGLU fragments (K = F)
+    float* act2_d;
+    float* part_o;
+    float2* part_ml;
+    int max_chunks;
+    float2* lm_val;  // [grid][16]
+    unsigned* bar;   // grid barrier counter, zero at launch
+    unsigned* tickets;  // [n_layers][ffn/32], zero at launch
+    unsigned* head_tickets;  // [n_layers][n_heads + 2 n_kv], zero at launch
+    int* abort_flag;
+    unsigned long long* timeline;  // optional: CTA 0's [barrier][arrive, release] in ns
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase; false on timeout or abort.
+__device__ bool mbar_wait(uint64_t* b, unsigned parity, const int* abort_flag) {
+    const unsigned long long t0 = global_ns();
+    for (unsigned it = 0;; ++it) {
+        if (mbar_try_wait(b, parity)) return true;
+        if ((it & 63) == 63) {
+            if (*reinterpret_cast<const volatile int*>(abort_flag)) return false;
+            if (global_ns() - t0 > kWaitNs) return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(b)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(b))
+        : "memory");
+}
+
+__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
+
+// Sub-phase mark k (0..3) of phase b in the optional timeline (CTA 0, thread 0).
+__device__ __forceinline__ void mark(unsigned long long* timeline, int b, int k) {
+    if (timeline && blockIdx.x == 0 && threadIdx.x == 0) timeline[2 * kMaxBarriers + 2 + 4 * b + k] = global_ns();
+}
+
+// ------------------------------------------------------------------ schedule
+
+// Weight phases in stream order: per layer A (QKV), D (O), E (gate/up pair),
+// F (down); then G (LM head).  Item i of a phase goes to CTA (i + rot) % grid,
+// where rot is the number of items in all earlier weight phases, so the work
+// rotates over the CTAs from phase to phase.
+enum WPhase { W_QKV = 0, W_O = 1, W_GU = 2, W_DOWN = 3, W_LM = 4 };
+
+struct PhaseInfo {
+    int n_items;    // items in the phase
+    int rot;        // rotation
+    int bytes;      // weight bytes per item
+    int slots;      // ring slots per item
+    int count;      // items of this CTA
+    int first;      // first global item of this CTA
+    long long slot0;  // first ring slot sequence number of this phase for this CTA
+};
+
+struct Schedule {
+    int grid, cta;
+    int qd, kd, H, F, V, L;
+    // sizes per weight phase kind
+    int n[5], bytes[5];
+    __device__ void init(const ModelDims& d, int grid_, int cta_) {
+        grid = grid_;
+        cta = cta_;
+        H = d.hidden;
+        F = d.ffn;
+        V = d.vocab;
+        L = d.n_layers;
+        qd = d.n_heads * kHeadDim;
+        kd = d.n_kv * kHeadDim;
+        n[W_QKV] = (qd + 2 * kd) / kTileRows;
+        bytes[W_QKV] = (H / kTileK) * kTileBytes;
+        n[W_O] = H / kTileRows;
+        bytes[W_O] = (qd / kTileK) * kTileBytes;
+        n[W_GU] = F / kTileRows;  // pairs of row groups (gate, up)
+        bytes[W_GU] = 2 * (H / kTileK) * kTileBytes;
+        n[W_DOWN] = H / kTileRows;
+        bytes[W_DOWN] = (F / kTileK) * kTileBytes;
+        n[W_LM] = V / kTileRows;
+        bytes[W_LM] = (H / kTileK) * kTileBytes;
+    }
+    __device__ int slots_of(int kind) const { return (bytes[kind] + kSlotBytes - 1) / kSlotBytes; }
+    __device__ int count_of(int n_items, int rot, int* first) const {
+        const int f = ((cta - rot) % grid + grid) % grid;
+        *first = f;
+        return f < n_items ? (n_items - 1 - f) / grid + 1 : 0;
+    }
+    // Running position in the phase sequence: both the producer and the
+    // consumers advance it phase by phase, so neither recomputes the prefix.
+    __device__ PhaseInfo take(int kind, long long* items_before, long long* slot_next) const {
+        PhaseInfo pi{};
+        pi.n_items = n[kind];
+        pi.rot = int(*items_before % grid);
+        pi.bytes = bytes[kind];
+        pi.slots = slots_of(kind);
+        pi.count = count_of(pi.n_items, pi.rot, &pi.first);
+        pi.slot0 = *slot_next;
+        *items_before += n[kind];
+        *slot_next += (long long)pi.count * pi.slots;
+        return pi;
+    }
+    __device__ const uint8_t* item_src(const LayerWeights* lw, const uint8_t* embd, int p, int item) const {
+        if (p >= L * 4) return embd + (size_t)item * bytes[W_LM];
+        const LayerWeights& w = lw[p / 4];
+        switch (p % 4) {
+            case W_QKV: return w.qkv + (size_t)item * bytes[W_QKV];
+            case W_O: return w.o + (size_t)item * bytes[W_O];
+            case W_GU: return w.gu + (size_t)item * bytes[W_GU];
+            default: return w.down + (size_t)item * bytes[W_DOWN];
+        }
+    }
+};
+
+// ------------------------------------------------------------------ producer
+
+__device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, uint64_t* full, uint64_t* empty) {
+    long long q = 0;  // ring slot sequence number
+    const int n_phases = sch.L * 4 + 1;
+    bool ok = true;
+    long long items_before = 0;
+    for (int p = 0; p < n_phases && ok; ++p) {
+        const int kind = p < sch.L * 4 ? p % 4 : W_LM;
+        const int rot = int(items_before % sch.grid);
+        int first = 0;
+        const int cnt = sch.count_of(sch.n[kind], rot, &first);
+        const int slots = sch.slots_of(kind);
+        for (int j = 0; j < cnt && ok; ++j) {
+            const int item = first + j * sch.grid;
+            const uint8_t* src = sch.item_src(a.layers, a.embd, p, item);
+            for (int k = 0; k < slots; ++k, ++q) {
+                const int s = int(q % kRingSlots);
+                const long long use = q / kRingSlots;
+                if (use > 0 && !mbar_wait(&empty[s], unsigned((use - 1) & 1), a.abort_flag)) { ok = false; break; }
+                const int off = k * kSlotBytes;
+                const int nbytes = min(kSlotBytes, sch.bytes[kind] - off);
+                mbar_expect_tx(&full[s], unsigned(nbytes));
+                bulk_g2s(ring + (size_t)s * kSlotBytes, src + off, unsigned(nbytes), &full[s]);
+            }
+        }
+        items_before += sch.n[kind];
+    }
+    if (!ok) {
+        atomicExch(a.abort_flag, 1);
+        // Drain this CTA's copies still in flight before the CTA exits.
+        for (long long r = q - 1; r >= 0 && r >= q - kRingSlots; --r) {
+            const int s = int(r % kRingSlots);
+            const unsigned long long t0 = global_ns();
+            while (!mbar_try_wait(&full[s], unsigned((r / kRingSlots) & 1)) && global_ns() - t0 < kWaitNs) {
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ consumer pieces
+
+// Grid barrier over the consumer warps of every CTA (the counter only grows;
+// barrier b completes at (b + 1) * grid arrivals).  Returns false on abort.
+__device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
+    consumer_sync();
+    if (threadIdx.x == 0) {
+        const int b = int(target / gridDim.x) - 1;
+        if (a.timeline && blockIdx.x == 0) a.timeline[2 * b] = global_ns();
+        // Every CTA's arrival, for the skew between CTAs.
+        if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
+        __threadfence();
+        atomicAdd(a.bar, 1u);
+        const unsigned long long t0 = global_ns();
+        int status = 0;
+        for (unsigned it = 0;; ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+            if (v >= target) break;
+            if ((it & 31) == 31) {
+                if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
+                if (global_ns() - t0 > kWaitNs) {
+                    atomicExch(a.abort_flag, 1);
+                    a.state->error = 2;
+                    status = 1;
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        if (a.timeline && blockIdx.x == 0) a.timeline[2 * b + 1] = global_ns();
+        *s_flag = status;
+    }
+    consumer_sync();
+    return *s_flag == 0;
+}
+
+// A consumer wait that gave up: flag the step and let every wait stop.  The
+// warp then carries on to the next grid barrier (never returns alone: the
+// consumer warps of a CTA meet at named barriers), where all warps exit.
+__device__ void consumer_fail(const MegaArgs& a) {
+    if ((threadIdx.x & 31) == 0) {
+        atomicExch(a.abort_flag, 1);
+        a.state->error = 2;
+    }
+}
+
+// Wait for ring slot q (consumer side), lane-0 poll, warp-wide result.
+__device__ __forceinline__ bool slot_wait(uint64_t* full, long long q, const int* abort_flag) {
+    bool ok = true;
+    if ((threadIdx.x & 31) == 0) ok = mbar_wait(&full[q % kRingSlots], unsigned((q / kRingSlots) & 1), abort_flag);
+    return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+__device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[q % kRingSlots]);
+}
+
+// RMSNorm (the 256-thread tree of k_rmsnorm_quant) and q8_0 quantisation of
+// rows [16][K] of global x into shared fragments; rows >= T become zero.
+// Thread 32w + lane owns elements 256k + 32w + lane, i.e. lane `lane` of the
+// blocks b = 8k + w: its partial sum runs over k in order (the same tree), the
+// loads are coalesced per warp and all in flight together, and each warp
+// quantises its own blocks from registers.  K = 256 * NK.
+template <int NK>
+__device__ __noinline__ void norm_quant_smem(const float* x, const float* __restrict__ wn, float eps, int T,
+                                            uint8_t* act_q, float* act_d, double* s_wsum, float* s_scale,
+                                            unsigned long long* timeline = nullptr, int pid = 0) {
+    constexpr int K = 256 * NK;
+    constexpr int RG = 8;  // rows per pass (rows are independent; 8 x NK values per lane)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t* q32 = reinterpret_cast<uint32_t*>(act_q);
+    float wv[NK];
+#pragma unroll
+    for (int k = 0; k < NK; ++k) wv[k] = wn[256 * k + 32 * warp + lane];
+    for (int t0 = 0; t0 < kTMax; t0 += RG) {
+        if (t0 >= T) {
+            // Rows without a token: 32 zero codes per owned block (8 words) and d = 0.
+            if (lane < 8) {
+#pragma unroll
+                for (int r = 0; r < RG; ++r)
+#pragma unroll
+                    for (int k = 0; k < NK; ++k) {
+                        const int blk = 8 * k + warp;
+                        q32[((size_t)blk * 512 + frag_offset(t0 + r, lane * 4)) / 4] = 0u;
+                        if (lane == 0) act_d[blk * 16 + t0 + r] = 0.f;
+                    }
+            }
+            continue;
+        }
+        float v[RG][NK];
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+            for (int k = 0; k < NK; ++k)
+                v[r][k] = t0 + r < T ? ldcg(x + (size_t)(t0 + r) * K + 256 * k + 32 * warp + lane) : 0.f;
+        // Per-row partials, then the rows' butterflies interleaved (independent
+        // chains; each row's tree is the same xor butterfly).
+        double acc[RG];
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+            acc[r] = 0.0;
+#pragma unroll
+            for (int k = 0; k < NK; ++k) acc[r] += (double)(v[r][k] * v[r][k]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int r = 0; r < RG; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
+        if (lane == 0)
+#pragma unroll
+            for (int r = 0; r < RG; ++r)
+                if (t0 + r < T) s_wsum[warp * kTMax + t0 + r] = acc[r];
+        consumer_sync();
+        if (tid < RG && t0 + tid < T) {
+            double tot = 0.0;
+            for (int i = 0; i < kConsumerWarps; ++i) tot += s_wsum[i * kTMax + t0 + tid];
+            const float mean = (float)(tot / K);
+            s_scale[t0 + tid] = 1.0f / sqrtf(mean + eps);
+        }
+        consumer_sync();
+        // amax per (row, block) by one integer max reduction each; the scale
+        // divisions spread over the lanes (q8_scales).
+        constexpr int NB = RG * NK <= 32 ? RG * NK : 32;
+        static_assert(RG * NK <= 32, "one block per lane");
+        float am[NB], dd[NB], id[NB];
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+            const float sc = t0 + r < T ? s_scale[t0 + r] : 0.f;
+#pragma unroll
+            for (int k = 0; k < NK; ++k) {
+                v[r][k] = t0 + r < T ? __fmul_rn(__fmul_rn(v[r][k], sc), wv[k]) : 0.f;
+                am[r * NK + k] = warp_absmax(v[r][k]);
+            }
+        }
+        q8_scales<NB>(am, dd, id);
+#pragma unroll
+        for (int r = 0; r < RG; ++r) {
+#pragma unroll
+            for (int k = 0; k < NK; ++k) {
+                const int blk = 8 * k + warp;
+                act_q[(size_t)blk * 512 + frag_offset(t0 + r, lane)] =
+                    (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[r][k], id[r * NK + k]));
+                if (lane == 0) act_d[blk * 16 + t0 + r] = __half2float(__float2half_rn(dd[r * NK + k]));
+            }
+        }
+    }
+    (void)timeline;
+    (void)pid;
+    consumer_sync();
+}
+
+// Copy fragments [K/32][512] + scales [K/32][16] from global into shared
+// memory, every load of a thread issued before the first store.
+__device__ void load_act_smem(const uint8_t* gq, const float* gd, int K, uint8_t* act_q, float* act_d) {
+    const int nb = K / 32;
+    const uint4* src = reinterpret_cast<const uint4*>(gq);
+    uint4* dst = reinterpret_cast<uint4*>(act_q);
+    const int n16 = nb * 32, nd = nb * 16 / 4;  // uint4 of fragments, float4 of scales
+    constexpr int U = 8;
+    for (int base = threadIdx.x; base < n16; base += kConsumers * U) {
+        uint4 r[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (base + u * kConsumers < n16) r[u] = __ldcg(src + base + u * kConsumers);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (base + u * kConsumers < n16) dst[base + u * kConsumers] = r[u];
+    }
+    const float4* sd = reinterpret_cast<const float4*>(gd);
+    float4* dd = reinterpret_cast<float4*>(act_d);
+    for (int i = threadIdx.x; i < nd; i += kConsumers) dd[i] = __ldcg(sd + i);
+    consumer_sync();
+}
+
+// A chunk's K or V rows held in registers between the load and the store to
+// shared memory (fp16: 4 x 16 bytes per thread; f32: 8 x 16 bytes).
+struct KvRegs {
+    uint4 r[8];
+};
+
+__device__ __forceinline__ void kv_fetch(const KvCache& kv, long long off, int n_pos, KvRegs& v) {
+    const bool f16 = kv.type == KV_F16;
+    const uint4* src = f16 ? reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.base) + off)
+                           : reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(kv.base) + off);
+    const int n = n_pos * (f16 ? 16 : 32);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int i = threadIdx.x + u * kConsumers;
+        if (i < n) v.r[u] = __ldcg(src + i);
+    }
+}
+
+__device__ __forceinline__ void kv_park(const KvCache& kv, const KvRegs& v, int n_pos, float* sk) {
+    if (kv.type == KV_F16) {
+        const int n = n_pos * 16;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = threadIdx.x + u * kConsumers;
+            if (i < n) {
+                const int p = i >> 4, e0 = (i & 15) * 8;
+                const __half2* hv = reinterpret_cast<const __half2*>(&v.r[u]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float2 f = __half22float2(hv[k]);
+                    sk[p * (kHeadDim + 1) + e0 + 2 * k] = f.x;
+                    sk[p * (kHeadDim + 1) + e0 + 2 * k + 1] = f.y;
+                }
+            }
+        }
+    } else {
+        const int n = n_pos * 32;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = threadIdx.x + u * kConsumers;
+            if (i < n) {
+                const int p = i >> 5, e0 = (i & 31) * 4;
+                const float4 f = *reinterpret_cast<const float4*>(&v.r[u]);
+                sk[p * (kHeadDim + 1) + e0] = f.x;
+                sk[p * (kHeadDim + 1) + e0 + 1] = f.y;
+                sk[p * (kHeadDim + 1) + e0 + 2] = f.z;
+                sk[p * (kHeadDim + 1) + e0 + 3] = f.w;
+            }
+        }
+    }
+}
+
+// One 64-position K or V chunk of one head into shared memory as f32 rows of
+// stride 129 (conflict-free column reads), 16-byte loads all in flight.
+__device__ __forceinline__ void load_kv_chunk(const KvCache& kv, long long off, int n_pos, float* sk) {
+    KvRegs r;
+    kv_fetch(kv, off, n_pos, r);
+    kv_park(kv, r, n_pos, sk);
+}
+
+// One 256-K slice of one row group from shared memory: the slice partial of
+// the 16 x 8 outputs this lane holds (one fmaf per block, in block order).
+__device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint4* s_act, const float* s_d, int kt0) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const uint8_t* tile = slice + u * kTileBytes;
+        const uint4 wv = *reinterpret_cast<const uint4*>(tile + lane * 16);
+        const uint2 sv = *reinterpret_cast<const uint2*>(tile + 512 + t * 8);
+        const int kt = kt0 + u;
+        int c0[4], c1[4];
+        mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv.x, wv.y);
+        mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv.z, wv.w);
+        const float x0g = s_d[(2 * kt) * 16 + g], x0h = s_d[(2 * kt) * 16 + g + 8];
+        const float x1g = s_d[(2 * kt + 1) * 16 + g], x1h = s_d[(2 * kt + 1) * 16 + g + 8];
+        const float w00 = h2f_lo(sv.x), w01 = h2f_hi(sv.x), w10 = h2f_lo(sv.y), w11 = h2f_hi(sv.y);
+        acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
+        acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
+        acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
+        acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+        acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
+        acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
+        acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
+        acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+    }
+    return make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// Outputs of row group `rg_local` (0 or 1 for a gate/up pair) of the item whose
+// slots start at sequence number q0: 0 + slice 0 + slice 1 + ... in order.
+// Waits for and releases the item's ring slots (all of them when `release`).
+__device__ __forceinline__ bool item_rows(const uint8_t* ring, uint64_t* full, uint64_t* empty, long long q0, int kt_n, int rg_local,
+                          const uint4* s_act, const float* s_d, const int* abort_flag, float4* out) {
+    const int S = kt_n / 4;
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+        const int off = (rg_local * kt_n + s * 4) * kTileBytes;
+        const long long q = q0 + off / kSlotBytes;
+        if ((off % kSlotBytes) == 0 || s == 0)
+            if (!slot_wait(full, q, abort_flag)) return false;
+        const float4 p = slice_partial(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, s * 4);
+        y.x = y.x + p.x; y.y = y.y + p.y; y.z = y.z + p.z; y.w = y.w + p.w;
+    }
+    *out = y;
+    return true;
+}
+
+__device__ __forceinline__ void release_item(uint64_t* empty, long long q0, int slots) {
+    for (int k = 0; k < slots; ++k) slot_release(empty, q0 + k);
+}
+
+// A weight phase of this CTA split into (item, row group, 256-K slice) units
+// over the 8 consumer warps; each unit's partial goes to shared memory, then
+// `epi(j, part)` runs once per item (item j's units start at part + j*U*32,
+// row group r's slice s at (r*S + s)*32) and adds the slices in order.  The
+// phase's ring slots are all released after the units (at most 8 per CTA).
+template <typename Epi>
+__device__ __forceinline__ bool weight_phase(const PhaseInfo& pi, int rgs, int kt_n, const uint8_t* ring,
+                                             uint64_t* full, uint64_t* empty, const uint4* s_act, const float* s_d,
+                                             float4* s_part, const int* abort_flag, Epi epi) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = kt_n / 4, U = rgs * S;
+    const int n_units = pi.count * U;
+    bool ok = true;
+    for (int u = warp; u < n_units; u += kConsumerWarps) {
+        const int j = u / U, r = (u % U) / S, sl = u % S;
+        const int off = (r * kt_n + sl * 4) * kTileBytes;
+        const long long q = pi.slot0 + (long long)j * pi.slots + off / kSlotBytes;
+        if (!slot_wait(full, q, abort_flag)) { ok = false; break; }
+        s_part[u * 32 + lane] = slice_partial(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, sl * 4);
+    }
+    consumer_sync();
+    const int n_slots = pi.count * pi.slots;
+    for (int k = threadIdx.x; k < n_slots; k += kConsumers) mbar_arrive(&empty[(pi.slot0 + k) % kRingSlots]);
+    for (int j = warp; j < pi.count; j += kConsumerWarps) epi(j, s_part + (size_t)j * U * 32);
+    return ok;
+}
+
+__device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
+    const int lane = threadIdx.x & 31;
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);  // 0 + slice 0 + slice 1 + ... as on the CPU
+    for (int sl = 0; sl < S; ++sl) {
+        const float4 p = part[sl * 32 + lane];
+        y.x = y.x + p.x; y.y = y.y + p.y; y.z = y.z + p.z; y.w = y.w + p.w;
+    }
+    return y;
+}
+
+// The SwiGLU block `blk` (32 features of all 16 rows) quantised for the down
+// projection by the warp that completed its last group (rows >= T are zero).
+__device__ __noinline__ void quantize_ticket_block(const MegaArgs& a, int blk, int T) {
+    const int lane = threadIdx.x & 31;
+    const int F = a.d.ffn;
+    float v[kTMax], m[kTMax], dq[kTMax], iq[kTMax];
+#pragma unroll
+    for (int row = 0; row < kTMax; ++row) v[row] = row < T ? __ldcg(a.gu + (size_t)row * F + blk * 32 + lane) : 0.f;
+#pragma unroll
+    for (int row = 0; row < kTMax; ++row) m[row] = warp_absmax(v[row]);
+    q8_scales<kTMax>(m, dq, iq);
+#pragma unroll
+    for (int row = 0; row < kTMax; ++row) {
+        a.act2_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[row], iq[row]));
+        if (lane == 0) a.act2_d[blk * 16 + row] = __half2float(__float2half_rn(dq[row]));
+    }
+}
+
+// Phase C for one (row t, q head qh) by one warp: merge of the chunk partials
+// in chunk order, then the four q8_0 blocks of that head's context row.
+__device__ __noinline__ void combine_item(const MegaArgs& a, int t, int qh, int T, int n_chunks) {
+    const int lane = threadIdx.x & 31;
+    const int nh = a.d.n_heads, G = nh / a.d.n_kv;
+    constexpr int B = 16;  // chunks per prefetch batch
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (t < T) {
+        const int h = qh / G, qi = t * G + qh % G;
+        const size_t base0 = (size_t)h * a.max_chunks * (kTMax * 4) + qi;
+        auto po_at = [&](int c, int k) {
+            return &a.part_o[(base0 + (size_t)c * (kTMax * 4)) * kHeadDim + k * 32 + lane];
+        };
+        float po[B][4];
+#pragma unroll
+        for (int u = 0; u < B; ++u)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) po[u][k] = u < n_chunks ? __ldcg(po_at(u, k)) : 0.f;
+        float M = -INFINITY;
+        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, __ldcg(&a.part_ml[base0 + (size_t)c * (kTMax * 4)].x));
+        M = warp_max(M);
+        float Ls = 0.f;
+        for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+            float2 ml = make_float2(-INFINITY, 0.f);
+            if (c0 + lane < n_chunks) ml = __ldcg(&a.part_ml[base0 + (size_t)(c0 + lane) * (kTMax * 4)]);
+            const float wl = ml.x == -INFINITY ? 0.f : exact_expf(ml.x - M);
+            const int nc = min(32, n_chunks - c0);
+            for (int cb = 0; cb < nc; cb += B) {
+                float nx[B][4];
+                const int nb = c0 + cb + B;  // first chunk of the next batch
+#pragma unroll
+                for (int u = 0; u < B; ++u)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) nx[u][k] = nb + u < n_chunks ? __ldcg(po_at(nb + u, k)) : 0.f;
+#pragma unroll
+                for (int u = 0; u < B; ++u) {
+                    const float mc = __shfl_sync(0xffffffffu, ml.x, (cb + u) & 31);
+                    const float lc = __shfl_sync(0xffffffffu, ml.y, (cb + u) & 31);
+                    const float wgt = __shfl_sync(0xffffffffu, wl, (cb + u) & 31);
+                    if (cb + u < nc && mc != -INFINITY) {
+                        Ls = fmaf(wgt, lc, Ls);
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) o[k] = fmaf(wgt, po[u][k], o[k]);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < B; ++u)
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) po[u][k] = nx[u][k];
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o[k] = o[k] / Ls;
+    }
+    float am[4], dq[4], iq[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) am[k] = warp_absmax(o[k]);
+    q8_scales<4>(am, dq, iq);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int blk = qh * 4 + k;
+        a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o[k], iq[k]));
+        if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[k]));
+    }
+}
+
+// Preparation of one (head, row) of the step, by one warp (phase A2): q heads
+// get RMSNorm + NEOX RoPE into qr; k heads RMSNorm + RoPE into the KV cache;
+// v heads are copied into the KV cache.  Lane `lane` holds elements lane + 32 q of the
+// head row (q = 0..3): quarter q's square sum is one butterfly, the quarters
+// are added in order (the tree of k_qk_norm_rope_store), and the RoPE pairs
+// (e, e + 64) are (lane, lane + 64) and (lane + 32, lane + 96).
+__device__ __noinline__ void prep_row(const MegaArgs& a, const LayerWeights& w, int l, int hh, int t, int before,
+                                      const float* s_rope) {
+    const int lane = threadIdx.x & 31;
+    const int nh = a.d.n_heads, nkv = a.d.n_kv;
+    const int ldq = (nh + 2 * nkv) * kHeadDim;
+    const bool is_q = hh < nh, is_k = !is_q && hh < nh + nkv;
+    float x[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) x[q] = __ldcg(a.qkv + (size_t)t * ldq + (size_t)hh * kHeadDim + 32 * q + lane);
+    const int pos = before + t;
+    if (!is_q && !is_k) {
+        const long long off = kv_offset(a.kv, nkv, l, 1, hh - nh - nkv, pos);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) kv_store(a.kv, off + 32 * q + lane, x[q]);
+        return;
+    }
+    const float* wn = is_q ? w.q_norm : w.k_norm;
+    double part[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) part[q] = warp_sum_d((double)(x[q] * x[q]));
+    const double tot = part[0] + part[1] + part[2] + part[3];
+    const float mean = (float)(tot / kHeadDim);
+    const float scale = 1.0f / sqrtf(mean + a.d.eps);
+    float y[4], o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) y[q] = __fmul_rn(__fmul_rn(x[q], scale), wn[32 * q + lane]);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int e = 32 * q + lane;
+        const float cs = s_rope[(t * 64 + e) * 2], sn = s_rope[(t * 64 + e) * 2 + 1];
+        o[q] = __fsub_rn(__fmul_rn(y[q], cs), __fmul_rn(y[q + 2], sn));
+        o[q + 2] = __fadd_rn(__fmul_rn(y[q], sn), __fmul_rn(y[q + 2], cs));
+    }
+    if (is_q) {
+        float* dst = a.qr + ((size_t)t * nh + hh) * kHeadDim;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[32 * q + lane] = o[q];
+    } else {
+        const long long off = kv_offset(a.kv, nkv, l, 0, hh - nh, pos);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) kv_store(a.kv, off + 32 * q + lane, o[q]);
+    }
+}
+
+// Attention of one (64-position chunk c, kv head h) item by the whole CTA
+// (phase B): scores of the head's G query heads' rows against the chunk, the
+// chunk softmax and the P.V partials (same order as k_attn_chunk).  The q rows
+// and the step's new k/v rows were prepared in phase A (prep_head).
+__device__ __noinline__ void attention_item(const MegaArgs& a, int l, int c, int h, int T, int before, uint8_t* region,
+                                            int mark_pid) {
+    const ModelDims& d = a.d;
+    const int nh = d.n_heads, nkv = d.n_kv, G = nh / nkv;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int kv_len = before + T, NQ = T * G;
+    const float attn_scale = 1.0f / sqrtf((float)kHeadDim);
+    float* sq = reinterpret_cast<float*>(region);              // [NQ <= 32][128]
+    float* sk = sq + 32 * kHeadDim;                            // [64][129]
+    float* sp = sk + kPage * (kHeadDim + 1);                    // [NQ][64]
+                const int p0 = c * kPage;
+                const int n_pos = min(kPage, kv_len - p0);
+    // q rows of the head's G query heads (normed and rotated in phase A) and
+    // the chunk's K rows; the V rows are loaded into registers now and parked
+    // in shared memory after the scores (the K buffer is reused).
+    for (int i = tid; i < NQ * 32; i += kConsumers) {
+        const int r = i >> 5, c4 = i & 31;
+        const int t = r / G, jh = r % G;
+        reinterpret_cast<float4*>(sq + r * kHeadDim)[c4] =
+            __ldcg(reinterpret_cast<const float4*>(a.qr + ((size_t)t * nh + h * G + jh) * kHeadDim) + c4);
+    }
+                if (mark_pid >= 0) mark(a.timeline, mark_pid, 0);
+                // Scores over the chunk (same order as k_attn_chunk).
+                const long long koff = kv_offset(a.kv, nkv, l, 0, h, p0);
+                const long long voff = kv_offset(a.kv, nkv, l, 1, h, p0);
+                KvRegs vreg;
+                kv_fetch(a.kv, voff, n_pos, vreg);
+                load_kv_chunk(a.kv, koff, n_pos, sk);
+                consumer_sync();
+                // Scores: each thread owns a 2 x 2 tile (2 query rows x 2 positions);
+                // every score is still one sequential fmaf chain over the 128 dims.
+                for (int tile = tid; tile < (NQ / 2) * (kPage / 2); tile += kConsumers) {
+                    const int qi0 = (tile / (kPage / 2)) * 2, pp = tile % (kPage / 2);
+                    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+                    const float* qa0 = sq + qi0 * kHeadDim;
+                    const float* qa1 = qa0 + kHeadDim;
+                    const float* k0 = sk + pp * (kHeadDim + 1);
+                    const float* k1 = sk + (pp + 32) * (kHeadDim + 1);
+#pragma unroll 8
+                    for (int e = 0; e < kHeadDim; ++e) {
+                        const float q0 = qa0[e], q1 = qa1[e], kk0 = k0[e], kk1 = k1[e];
+                        acc[0][0] = fmaf(q0, kk0, acc[0][0]);
+                        acc[0][1] = fmaf(q0, kk1, acc[0][1]);
+                        acc[1][0] = fmaf(q1, kk0, acc[1][0]);
+                        acc[1][1] = fmaf(q1, kk1, acc[1][1]);
+                    }
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        const int t = (qi0 + r) / G;
+#pragma unroll
+                        for (int u = 0; u < 2; ++u) {
+                            const int p = pp + 32 * u;
+                            const bool ok = p < n_pos && p0 + p < before + t + 1;
+                            sp[(qi0 + r) * kPage + p] = ok ? acc[r][u] * attn_scale : -INFINITY;
+                        }
+                    }
+                }
+                consumer_sync();
+                if (mark_pid >= 0) mark(a.timeline, mark_pid, 1);
+                for (int qi = warp; qi < NQ; qi += kConsumerWarps) {
+                    const float a0 = sp[qi * kPage + lane], a1 = sp[qi * kPage + lane + 32];
+                    const float m = warp_max(fmaxf(a0, a1));
+                    const float e0 = a0 == -INFINITY ? 0.f : exact_expf(a0 - m);
+                    const float e1 = a1 == -INFINITY ? 0.f : exact_expf(a1 - m);
+                    const float lsum = warp_sum(e0 + e1);
+                    sp[qi * kPage + lane] = e0;
+                    sp[qi * kPage + lane + 32] = e1;
+                    if (lane == 0) a.part_ml[((size_t)h * a.max_chunks + c) * (kTMax * 4) + qi] = make_float2(m, lsum);
+                }
+                consumer_sync();
+                kv_park(a.kv, vreg, n_pos, sk);
+                consumer_sync();
+                if (mark_pid >= 0) mark(a.timeline, mark_pid, 2);
+                // P.V: each thread owns 2 query rows x 2 dims; each output is one
+                // sequential fmaf chain over the chunk's positions.
+                for (int tile = tid; tile < (NQ / 2) * (kHeadDim / 2); tile += kConsumers) {
+                    const int qi0 = (tile / (kHeadDim / 2)) * 2, e0 = tile % (kHeadDim / 2);
+                    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+                    const float* pr0 = sp + qi0 * kPage;
+                    const float* pr1 = pr0 + kPage;
+                    for (int p = 0; p < n_pos; ++p) {
+                        const float w0 = pr0[p], w1 = pr1[p];
+                        const float v0 = sk[p * (kHeadDim + 1) + e0], v1 = sk[p * (kHeadDim + 1) + e0 + 64];
+                        acc[0][0] = fmaf(w0, v0, acc[0][0]);
+                        acc[0][1] = fmaf(w0, v1, acc[0][1]);
+                        acc[1][0] = fmaf(w1, v0, acc[1][0]);
+                        acc[1][1] = fmaf(w1, v1, acc[1][1]);
+                    }
+#pragma unroll
+                    for (int r = 0; r < 2; ++r) {
+                        float* dst = a.part_o + (((size_t)h * a.max_chunks + c) * (kTMax * 4) + qi0 + r) * kHeadDim;
+                        dst[e0] = acc[r][0];
+                        dst[e0 + 64] = acc[r][1];
+                    }
+                }
+    consumer_sync();
+}
+
+// ------------------------------------------------------------------ the kernel
+
+// Per-CTA context, built once in shared memory by thread 0: the phase
+// functions below read their sizes and pointers from here instead of keeping
+// them live in registers across the whole step.
+struct KCtx {
+    MegaArgs a;
+    Schedule sch;
+    uint8_t* ring;
+    uint8_t* region;   // activation fragments + slice partials / attention scratch
+    float* rope;       // [16][64][cos, sin]
+    uint64_t* full;
+    uint64_t* empty;
+    double* wsum;      // [8][16]
+    float* scale;      // [16]
+    float2* cand;      // [8][16]
+    int* flag;
+    int T, before, kv_len, n_chunks;
+};
+
+__device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
+
+// Grid barrier at the end of a phase; false when the step is being aborted.
+__device__ __noinline__ bool end_phase(const KCtx& c, unsigned* target) {
+    *target += gridDim.x;
+    return grid_barrier(c.a, *target, c.flag);
+}
+
+// RoPE angles of the step's positions (theta advanced by repeated float
+// products, src/qwen3.cpp:109-118), shared by every layer; and the embedding
+// rows of the step's tokens (q8_0 dequant from the token_embd tiles).
+__device__ __noinline__ void phase_embed(const KCtx& c) {
+    const MegaArgs& a = c.a;
+    const int tid = threadIdx.x, H = a.d.hidden;
+    for (int i = tid; i < kTMax * 64; i += kConsumers) {
+        const int t = i / 64, k = i % 64;
+        float theta = (float)(c.before + t);
+        for (int j = 0; j < k; ++j) theta = __fmul_rn(theta, a.theta_scale);
+        float sn, cs;
+        exact_sincosf(theta, &sn, &cs);
+        c.rope[i * 2] = cs;
+        c.rope[i * 2 + 1] = sn;
+    }
+    const int kt_n = H / kTileK;
+    StepState* st = a.state;
+    for (int i = blockIdx.x * kConsumers + tid; i < kTMax * H; i += gridDim.x * kConsumers) {
+        const int row = i / H, col = i % H;
+        float v = 0.f;
+        if (row < c.T) {
+            int id = st->tokens[row];
+            if (id < 0 || id >= a.d.vocab) { st->error = 1; id = 0; }
+            const int rg = id / kTileRows, g = id % kTileRows;
+            const int kt = col / kTileK, blk = (col % kTileK) / 32, cc = col % 32;
+            const uint8_t* tile = a.embd + ((size_t)rg * kt_n + kt) * kTileBytes;
+            const int t4 = (cc & 15) >> 2, part = cc >> 4;
+            const int8_t q = (int8_t)tile[(g * 4 + t4) * 16 + blk * 8 + part * 4 + (cc & 3)];
+            const unsigned short hb =
+                *reinterpret_cast<const unsigned short*>(tile + 512 + ((g >> 1) * 4 + blk * 2 + (g & 1)) * 2);
+            v = (float)q * __half2float(__ushort_as_half(hb));
+        }
+        a.x[i] = v;
+    }
+    consumer_sync();
+}
+
+// Epilogue helper: lane (g, t) holds rows g, g + 8 x columns 2t, 2t + 1 of a row group.
+template <typename F>
+__device__ __forceinline__ void for_outputs(const float4& y, int T, F f) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const float yy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int row = g + (k >> 1) * 8;
+        if (row < T) f(row, 2 * t + (k & 1), yy[k]);
+    }
+}
+
+// A: RMSNorm + quantise (every CTA), QKV rows -> qkv.
+template <int NK>
+__device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int pid) {
+    const MegaArgs& a = c.a;
+    const LayerWeights& w = a.layers[l];
+    constexpr int K = 256 * NK;
+    uint8_t* act_q = c.region;
+    float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    mark(a.timeline, pid, 0);
+    const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
+    float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
+    const int ldq = (a.d.n_heads + 2 * a.d.n_kv) * kHeadDim, T = c.T;
+    return weight_phase(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+                        s_part, a.abort_flag, [&](int j, const float4* part) {
+                            const int item = pi.first + j * gridDim.x;
+                            for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
+                                a.qkv[(size_t)row * ldq + item * kTileRows + col] = v;
+                            });
+                        });
+}
+
+// A2: per-(head, row) RMSNorm + RoPE, KV append (warps numbered across CTAs).
+__device__ __noinline__ void phase_prep(const KCtx& c, int l) {
+    const MegaArgs& a = c.a;
+    const int warp = threadIdx.x >> 5;
+    const int n_tasks = (a.d.n_heads + 2 * a.d.n_kv) * c.T;
+    for (int task = blockIdx.x + gridDim.x * warp; task < n_tasks; task += gridDim.x * kConsumerWarps)
+        prep_row(a, a.layers[l], l, task / c.T, task % c.T, c.before, c.rope);
+}
+
+// B: attention chunks, one (chunk, kv head) item per CTA at a time.
+__device__ __noinline__ void phase_attn(const KCtx& c, int l, int pid) {
+    const int nkv = c.a.d.n_kv;
+    const int n_items = c.n_chunks * nkv;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+        attention_item(c.a, l, it / nkv, it % nkv, c.T, c.before, c.region, it == (int)blockIdx.x ? pid : -1);
+        consumer_sync();
+    }
+}
+
+// C: chunk merge + quantise the context rows (warps numbered across CTAs).
+__device__ __noinline__ void phase_combine(const KCtx& c) {
+    const int nh = c.a.d.n_heads, warp = threadIdx.x >> 5;
+    const int n_items = kTMax * nh;
+    for (int it = blockIdx.x + gridDim.x * warp; it < n_items; it += gridDim.x * kConsumerWarps)
+        combine_item(c.a, it / nh, it % nh, c.T, c.n_chunks);
+}
+
+// D: O projection + residual.  F: down projection + residual.
+__device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* cur, int pid, bool down) {
+    const MegaArgs& a = c.a;
+    const int K = down ? a.d.ffn : a.d.n_heads * kHeadDim, H = a.d.hidden, T = c.T;
+    uint8_t* act_q = c.region;
+    float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    load_act_smem(down ? a.act2_q : a.act_q, down ? a.act2_d : a.act_d, K, act_q, act_d);
+    mark(a.timeline, pid, 0);
+    const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
+    float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
+    return weight_phase(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+                        s_part, a.abort_flag, [&](int j, const float4* part) {
+                            const int item = pi.first + j * gridDim.x;
+                            for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
+                                float* o = a.x + (size_t)row * H + item * kTileRows + col;
+                                *o = __ldcg(o) + v;
+                            });
+                        });
+}
+
+// E: RMSNorm + quantise; gate/up + SwiGLU -> gu; a ticket per 32-feature block
+// lets the last of its four groups quantise it for the down projection.
+template <int NK>
+__device__ __noinline__ bool phase_gu(const KCtx& c, int l, long long* cur, int pid) {
+    const MegaArgs& a = c.a;
+    const LayerWeights& w = a.layers[l];
+    constexpr int K = 256 * NK;
+    const int F = a.d.ffn, T = c.T, lane = threadIdx.x & 31;
+    uint8_t* act_q = c.region;
+    float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T, act_q, act_d, c.wsum, c.scale);
+    mark(a.timeline, pid, 0);
+    const PhaseInfo pi = c.sch.take(W_GU, &cur[0], &cur[1]);
+    float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
+    constexpr int S = K / kTileK / 4;
+    return weight_phase(pi, 2, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+                        s_part, a.abort_flag, [&](int j, const float4* part) {
+                            const int item = pi.first + j * gridDim.x;  // features 8i..8i+7
+                            const float4 gq = sum_slices(part, S), uq = sum_slices(part + S * 32, S);
+                            const float gg[4] = {gq.x, gq.y, gq.z, gq.w}, uu[4] = {uq.x, uq.y, uq.z, uq.w};
+                            const int g = lane >> 2, t = lane & 3;
+                            const int feat = item * kTileRows + 2 * t;
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int row = g + (k >> 1) * 8;
+                                if (row < T) {
+                                    const float sl = gg[k] / (1.0f + exact_expf(-gg[k]));
+                                    a.gu[(size_t)row * F + feat + (k & 1)] = sl * uu[k];
+                                }
+                            }
+                            __threadfence();
+                            __syncwarp();
+                            int last = 0;
+                            if (lane == 0) last = atomicAdd(&a.tickets[l * (F / 32) + item / 4], 1u) == 3u;
+                            if (__shfl_sync(0xffffffffu, last, 0)) {
+                                __threadfence();
+                                quantize_ticket_block(a, item / 4, T);
+                            }
+                        });
+}
+
+// G: final RMSNorm + quantise; LM head with the fused first max -> lm_val[cta].
+template <int NK>
+__device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
+    const MegaArgs& a = c.a;
+    constexpr int K = 256 * NK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    uint8_t* act_q = c.region;
+    float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    mark(a.timeline, pid, 0);
+    const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
+    float best_v[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0x7fffffff, 0x7fffffff};
+    bool ok = true;
+    for (int j = warp; j < pi.count; j += kConsumerWarps) {
+        const int item = pi.first + j * gridDim.x;
+        const long long q0 = pi.slot0 + (long long)j * pi.slots;
+        float4 y;
+        if (!item_rows(c.ring, c.full, c.empty, q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
+                       a.abort_flag, &y)) {
+            ok = false;
+            break;
+        }
+        release_item(c.empty, q0, pi.slots);
+        const float yy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int col = item * kTileRows + 2 * t + (k & 1);
+            const int slot = k >> 1;
+            if (yy[k] > best_v[slot] || (yy[k] == best_v[slot] && col < best_i[slot])) {
+                best_v[slot] = yy[k];
+                best_i[slot] = col;
+            }
+        }
+    }
+#pragma unroll
+    for (int slot = 0; slot < 2; ++slot) {
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v[slot], o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i[slot], o);
+            if (ov > best_v[slot] || (ov == best_v[slot] && oi < best_i[slot])) {
+                best_v[slot] = ov;
+                best_i[slot] = oi;
+            }
+        }
+    }
+    if (t == 0) {
+        c.cand[warp * kTMax + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
+        c.cand[warp * kTMax + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
+    }
+    consumer_sync();
+    if (tid < kTMax) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int r = 0; r < kConsumerWarps; ++r) {
+            const float2 cc = c.cand[r * kTMax + tid];
+            const int ci = __float_as_int(cc.y);
+            if (cc.x > bv || (cc.x == bv && ci < bi)) { bv = cc.x; bi = ci; }
+        }
+        a.lm_val[blockIdx.x * kTMax + tid] = make_float2(bv, __int_as_float(bi));
+    }
+    return ok;
+}
+
+// H (CTA 0): first max over the CTA partials, acceptance and rollback.
+__device__ __noinline__ void phase_accept(const KCtx& c) {
+    const MegaArgs& a = c.a;
+    StepState* st = a.state;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int row = warp; row < c.T; row += kConsumerWarps) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int b = lane; b < (int)gridDim.x; b += 32) {
+            const float2 cc = __ldcg(&a.lm_val[b * kTMax + row]);
+            const int ci = __float_as_int(cc.y);
+            if (cc.x > bv || (cc.x == bv && ci < bi)) { bv = cc.x; bi = ci; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) st->choice[row] = bi == 0x7fffffff ? 0 : bi;
+    }
+    consumer_sync();
+    if (threadIdx.x == 0) accept_choices(st, a.ids);
+    if (a.timeline && threadIdx.x == 0) a.timeline[kTimelineStart + 1] = global_ns();
+}
+
+template <int kNK>
+__global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs args) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ KCtx s_ctx;
+    __shared__ double s_wsum[kConsumerWarps * kTMax];
+    __shared__ float s_scale[kTMax * 4];
+    __shared__ float2 s_cand[kConsumerWarps * kTMax];
+    __shared__ int s_flag;
+    const int T = args.state->T;
+    if (T <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        KCtx& c = s_ctx;
+        c.a = args;
+        c.sch.init(args.d, gridDim.x, blockIdx.x);
+        c.ring = smem;
+        c.region = smem + (size_t)kRingSlots * kSlotBytes;
+        c.rope = reinterpret_cast<float*>(c.region + kRegionBytes);
+        c.full = reinterpret_cast<uint64_t*>(c.rope + kTMax * 64 * 2);
+        c.empty = c.full + kRingSlots;
+        c.wsum = s_wsum;
+        c.scale = s_scale;
+        c.cand = s_cand;
+        c.flag = &s_flag;
+        c.T = T;
+        c.before = args.state->before;
+        c.kv_len = c.before + T;
+        c.n_chunks = (c.kv_len + kPage - 1) / kPage;
+        if (args.timeline && blockIdx.x == 0) args.timeline[kTimelineStart] = global_ns();
+        for (int s = 0; s < kRingSlots; ++s) {
+            mbar_init(&c.full[s], 1);
+            mbar_init(&c.empty[s], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const KCtx& c = s_ctx;
+    if (warp == kConsumerWarps) {
+        if (lane == 0) producer(c.a, c.sch, c.ring, c.full, c.empty);
+        return;
+    }
+    unsigned target = 0;
+    long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
+    phase_embed(c);
+    if (!end_phase(c, &target)) return;
+    for (int l = 0; l < c.a.d.n_layers; ++l) {
+        if (!phase_qkv<kNK>(c, l, cur, phase_index(target) + 1)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        phase_prep(c, l);
+        if (!end_phase(c, &target)) return;
+        phase_attn(c, l, phase_index(target) + 1);
+        if (!end_phase(c, &target)) return;
+        phase_combine(c);
+        if (!end_phase(c, &target)) return;
+        if (!phase_proj_resid(c, l, cur, phase_index(target) + 1, false)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        if (!phase_gu<kNK>(c, l, cur, phase_index(target) + 1)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        if (!phase_proj_resid(c, l, cur, phase_index(target) + 1, true)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+    }
+    if (!phase_lm<kNK>(c, cur, phase_index(target) + 1)) consumer_fail(c.a);
+    if (!end_phase(c, &target)) return;
+    if (blockIdx.x == 0) phase_accept(c);
+}
+
+}  // namespace
+
+int megakernel_smem_bytes() {
+    return kRingSlots * kSlotBytes + kRegionBytes + kRopeBytes + 2 * kRingSlots * 8;
+}
+
+template <int NK>
+cudaError_t configure_one(int device, int* grid_out) {
+    cudaError_t e = cudaFuncSetAttribute(k_verify_persistent<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         megakernel_smem_bytes());
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_verify_persistent<NK>, kMegaThreads,
+                                                      megakernel_smem_bytes());
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    *grid_out = per_sm >= 1 ? sms : 0;
+    return cudaSuccess;
+}
+
+cudaError_t configure_megakernel(int device, int hidden, int* grid_out) {
+    switch (hidden) {
+        case 256: return configure_one<1>(device, grid_out);
+        case 512: return configure_one<2>(device, grid_out);
+        case 1024: return configure_one<4>(device, grid_out);
+        default: *grid_out = 0; return cudaSuccess;
+    }
+}
+
+bool megakernel_supports(const ModelDims& d, int grid) {
+    if (grid <= 0) return false;
+    const bool hidden_ok = d.hidden == 256 || d.hidden == 512 || d.hidden == 1024;
+    // Query rows are tiled in pairs (T * group must be even for every T).
+    if (!hidden_ok || (d.n_heads / d.n_kv) % 2 != 0 || d.n_heads / d.n_kv * kTMax > 32) return false;
+    if (d.ffn % 32 || (d.ffn / kTileRows) % 4) return false;
+    const int qd = d.n_heads * kHeadDim;
+    // Per weight phase: fragments + scales of its K plus 512 bytes per slice
+    // unit of the CTA's items must fit the shared region.
+    auto need = [&](int K, int items, int units_per_item) {
+        return (size_t)(K / 32) * (512 + 64) + (size_t)((items + grid - 1) / grid) * units_per_item * 512;
+    };
+    const size_t worst = std::max(std::max(need(d.hidden, (qd + 2 * d.n_kv * kHeadDim) / kTileRows, d.hidden / 256),
+                                           need(qd, d.hidden / kTileRows, qd / 256)),
+                                  std::max(need(d.hidden, d.ffn / kTileRows, 2 * d.hidden / 256),
+                                           need(d.ffn, d.hidden / kTileRows, d.ffn / 256)));
+    const size_t attn = (size_t)(32 * kHeadDim + kPage * (kHeadDim + 1) + 32 * kPage) * 4;
+    return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
+}
+
+cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
+                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+    MegaArgs a{};
+    a.timeline = mb.timeline;
+    a.d = m.dims;
+    a.layers = layers_dev;
+    a.embd = m.embd;
+    a.output_norm = m.output_norm;
+    a.theta_scale = m.theta_scale;
+    a.kv = kv;
+    a.state = b.state;
+    a.ids = b.ids;
+    a.x = b.x;
+    a.qkv = b.qkv;
+    a.gu = b.gu;
+    a.act_q = b.act_q;
+    a.act_d = b.act_d;
+    a.act2_q = mb.act2_q;
+    a.act2_d = mb.act2_d;
+    a.part_o = b.part_o;
+    a.part_ml = b.part_ml;
+    a.max_chunks = b.max_chunks;
+    a.lm_val = mb.lm_val;
+    a.bar = mb.bar;
+    a.tickets = mb.tickets;
+    a.head_tickets = mb.head_tickets;
+    a.qr = mb.qr;
+    a.abort_flag = mb.abort_flag;
+    cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, tickets, abort flag
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kMegaThreads);
+    cfg.dynamicSmemBytes = megakernel_smem_bytes();
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // all CTAs co-resident, or the launch fails
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    switch (m.dims.hidden) {
+        case 256: return cudaLaunchKernelEx(&cfg, k_verify_persistent<1>, a);
+        case 512: return cudaLaunchKernelEx(&cfg, k_verify_persistent<2>, a);
+        default: return cudaLaunchKernelEx(&cfg, k_verify_persistent<4>, a);
+    }
+}
+
+}  // namespace mtb

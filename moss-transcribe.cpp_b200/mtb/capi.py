@@ -58,6 +58,7 @@ SIGNATURES = {
     "mtb_model_free": (None, [_vp]),
     "mtb_model_error": (C.c_char_p, [_vp]),
     "mtb_model_dims": (C.c_int, [_vp, _i32p]),
+    "mtb_model_persistent_grid": (C.c_int, [_vp]),
     "mtb_decoder_create": (C.c_int, [_vp, C.c_int, C.c_int, C.c_int, C.POINTER(_vp)]),
     "mtb_decoder_free": (None, [_vp]),
     "mtb_decoder_error": (C.c_char_p, [_vp]),
@@ -82,6 +83,7 @@ SIGNATURES = {
     "mtb_event_elapsed_ms": (C.c_int, [_vp, C.c_int, C.c_int, _f32p]),
     "mtb_step_kernel_launches": (C.c_int, [_vp]),
     "mtb_transfer_bytes": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
+    "mtb_step_timeline": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, _ip]),
     "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
     "mtb_lm_head_argmax_noalloc": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
@@ -136,6 +138,7 @@ class Model:
         L.mtb_model_dims(self.ptr, dims)
         (self.hidden, self.n_layers, self.n_heads, self.n_kv_heads, self.head_dim, self.ffn, self.vocab,
          self.eos) = list(dims)
+        self.persistent_grid = L.mtb_model_persistent_grid(self.ptr)
 
     def close(self):
         if getattr(self, "ptr", None):
@@ -293,6 +296,17 @@ class Decoder:
 
     def step_kernel_launches(self) -> int:
         return lib().mtb_step_kernel_launches(self.ptr)
+
+    def step_timeline(self):
+        """(arrive_ns, release_ns) per grid barrier and (start, end) of the last
+        persistent step; needs MTB_PROFILE=1 when the decoder was created."""
+        out = (C.c_int64 * (6 * 512 + 2 + 256 * 512))()
+        n = C.c_int()
+        self._check(lib().mtb_step_timeline(self.ptr, out, len(out), C.byref(n)), "step_timeline")
+        vals = np.frombuffer(out, dtype=np.int64)
+        marks = [tuple(vals[1026 + 4 * b:1030 + 4 * b]) for b in range(512)]
+        self.last_arrivals = vals[6 * 512 + 2:].reshape(256, 512)
+        return [(vals[2 * b], vals[2 * b + 1]) for b in range(512)], (vals[1024], vals[1025]), marks
 
     def transfer_bytes(self):
         a, b = C.c_int64(), C.c_int64()

@@ -29,6 +29,12 @@ def full_gpu(full_path):
     return capi.Model(full_path, 0)
 
 
+def test_persistent_verify_kernel_is_active(full_gpu):
+    """On a B200 the Qwen3-0.6B verify step runs as one persistent kernel per
+    SM (148 CTAs); a silent fall-back to the kernel graph would fail here."""
+    assert full_gpu.persistent_grid >= 132
+
+
 def test_config1_prefill_and_speculative_decode_bit_exact(full_oracle, full_gpu):
     prompt = fixture.synthetic_prompt(full_oracle.arrays["token_embd.weight"], full_oracle.shape, n_audio=375,
                                       n_text=32)
