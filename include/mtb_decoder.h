@@ -134,7 +134,9 @@ int mtb_step_kernel_launches(mtb_decoder* d);
  * MTB_PROFILE=1 in the environment): out[2b], out[2b+1] = CTA 0's arrival and
  * release at grid barrier b, out[2*512], out[2*512+1] = kernel start and end,
  * out[2*512 + 2 + 4b + k] = sub-phase mark k of phase b (0 when unused),
- * out[6*512 + 2 + 512 c + b] = CTA c's arrival at barrier b, all in ns of the
+ * out[6*512 + 2 + 512 c + b] = CTA c's arrival at barrier b,
+ * out[6*512 + 2 + 256*512 + 16 (512 c + b) + k] = CTA c's sub-phase mark k of
+ * phase b (c < 256, k < 16), all in ns of the
  * GPU global timer; the profile counterpart of the
  * reference's MTD_PROFILE phase timers (src/cpu_profile.cpp:23-68). */
 int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out);

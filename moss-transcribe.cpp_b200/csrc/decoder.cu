@@ -105,6 +105,13 @@ int dalloc(std::vector<void*>& allocs, std::string& err, T** p, size_t bytes) {
     }
     allocs.push_back(q);
     *p = static_cast<T*>(q);
+    // Zeroed once so rows a step does not write (rows >= T of the activation
+    // fragments, cache pages past the written positions) hold finite values.
+    const cudaError_t z = cudaMemset(q, 0, bytes ? bytes : 16);
+    if (z != cudaSuccess) {
+        err = std::string("cudaMemset: ") + cudaGetErrorString(z);
+        return -1;
+    }
     return 0;
 }
 
@@ -456,7 +463,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
             return bail();
-        if (std::getenv("MTB_PROFILE") && dalloc(A, E, &d->mb.timeline, (6 * kMaxBarriers + 2 + 256 * kMaxBarriers) * 8)) return bail();
+        if (std::getenv("MTB_PROFILE") && dalloc(A, E, &d->mb.timeline, (6 * kMaxBarriers + 2 + 256 * kMaxBarriers * 17) * 8)) return bail();
         d->mb.bar = reinterpret_cast<unsigned*>(zero_region);
         d->mb.abort_flag = reinterpret_cast<int*>(zero_region + 4);
         d->mb.tickets = reinterpret_cast<unsigned*>(zero_region + 16);
@@ -808,7 +815,7 @@ int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out) {
     *n_out = 0;
     if (!d->mb.timeline) return fail(d->error, "set MTB_PROFILE=1 before creating the decoder");
     cudaSetDevice(d->device);
-    const int n = std::min(max_out, 6 * kMaxBarriers + 2 + 256 * kMaxBarriers);
+    const int n = std::min(max_out, 6 * kMaxBarriers + 2 + 256 * kMaxBarriers * 17);
     MTB_CK(d, cudaMemcpyAsync(out, d->mb.timeline, size_t(n) * 8, cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
     *n_out = n;

@@ -1,44 +1,48 @@
 // exp, sin and cos of the verify step, evaluated exactly as the CPU restatement
-// of the path evaluates them: Cody-Waite range reduction and Taylor series in
-// double, every operation rounded separately (this file is compiled with
-// -fmad=false, so no product and sum are fused unless written as fma).
-// Accuracy: the double result is within a few 1e-16 relative of the true
-// value, so the returned float is the correctly rounded one except in rare
-// near-tie cases.  Constants: ln 2 and pi/2 split into 32/33-bit leading parts
-// so that n * part is exact for every reduction count that can occur.
+// of the path evaluates them (this file is compiled with -fmad=false, so no
+// product and sum are fused unless written as fma).
+// exp: float arithmetic throughout.  n = rint(x log2 e); Cody-Waite reduction
+// r = x - n ln2 with ln2 split into a 16-bit head (0x3F317200) and a tail, each
+// step one fmaf; e^r by the Taylor polynomial to r^7 in Horner form (fmaf per
+// step, coefficients the floats nearest 1/k!); then exact scaling by 2^n (two
+// factors below 2^-126, so a subnormal result is rounded once).  Within 1 ulp
+// of the true value.
+// sin/cos: Cody-Waite reduction by pi/2 and Taylor series in double, every
+// operation rounded separately, so the returned float is the correctly rounded
+// one except in rare near-tie cases.  Constants: pi/2 split into 33-bit
+// leading parts so that k * part is exact for every reduction count that can
+// occur.
 #pragma once
 
 namespace mtb {
 
-constexpr double kLn2Hi = 0.6931471803691238;       // ln 2 to 32 bits
-constexpr double kLn2Lo = 1.9082149292705877e-10;   // ln 2 - kLn2Hi
-constexpr double kInvLn2 = 1.4426950408889634;
 constexpr double kPio2_1 = 1.5707963267341256;      // pi/2 to 33 bits
 constexpr double kPio2_2 = 6.077100506303966e-11;   // next 33 bits
 constexpr double kPio2_3 = 2.0222662487959506e-21;  // remainder
 constexpr double kTwoOverPi = 0.6366197723675814;
 
 __device__ __forceinline__ float exact_expf(float x) {
-    if (x != x) return x;
-    if (x > 88.8f) return INFINITY;
-    if (x < -104.0f) return 0.0f;
-    const double xd = (double)x;
-    const double n = rint(xd * kInvLn2);
-    const double r = (xd - n * kLn2Hi) - n * kLn2Lo;
-    double p = 1.0 / 479001600.0;  // sum r^k / k!, k <= 12
-    p = p * r + 1.0 / 39916800.0;
-    p = p * r + 1.0 / 3628800.0;
-    p = p * r + 1.0 / 362880.0;
-    p = p * r + 1.0 / 40320.0;
-    p = p * r + 1.0 / 5040.0;
-    p = p * r + 1.0 / 720.0;
-    p = p * r + 1.0 / 120.0;
-    p = p * r + 1.0 / 24.0;
-    p = p * r + 1.0 / 6.0;
-    p = p * r + 0.5;
-    p = p * r + 1.0;
-    p = p * r + 1.0;
-    return (float)ldexp(p, (int)n);
+    // Branch-free: x is clamped for the arithmetic and the special cases are
+    // selected at the end; 2^n is applied as (p * 2^a) * 2^b with
+    // (a, b) = (n, 0), (1, 127) for n = 128, (n + 64, -64) for n < -126.
+    const float xc = fminf(fmaxf(x, -103.972084f), 88.7228317f);
+    const float n = rintf(__fmul_rn(xc, 1.44269502f));
+    float r = fmaf(n, -0.693145752f, xc);
+    r = fmaf(n, -1.42860677e-6f, r);
+    float p = 1.98412701e-4f;
+    p = fmaf(p, r, 1.38888892e-3f);
+    p = fmaf(p, r, 8.33333377e-3f);
+    p = fmaf(p, r, 4.16666679e-2f);
+    p = fmaf(p, r, 1.66666672e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int)n;
+    const int ea = ni > 127 ? 1 : (ni < -126 ? ni + 64 : ni);
+    const int eb = ni > 127 ? 127 : (ni < -126 ? -64 : 0);
+    const float y = __fmul_rn(__fmul_rn(p, __uint_as_float((unsigned)(ea + 127) << 23)),
+                              __uint_as_float((unsigned)(eb + 127) << 23));
+    return x != x ? x : (x > 88.7228317f ? INFINITY : (x < -103.972084f ? 0.0f : y));
 }
 
 __device__ __forceinline__ void exact_sincosf(float x, float* s_out, float* c_out) {

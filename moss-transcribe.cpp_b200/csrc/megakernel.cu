@@ -11,10 +11,13 @@
 //
 // Phases per layer (src/qwen3.cpp:62-218):
 //   A  RMSNorm + q8_0 quantise (every CTA, into shared memory); QKV rows
-//   B  attention per (64-position chunk, kv head): per-head RMSNorm + RoPE of
-//      q (and of k for the step's new positions, stored to the KV cache),
-//      scores, chunk softmax, P.V partials
-//   C  chunk merge per (row, q head) and q8_0 quantise of the context
+//   A2 per-head RMSNorm + RoPE of q (and of k for the step's new positions,
+//      stored to the KV cache with the new v rows)
+//   B  attention per (64-position chunk, kv head): scores, chunk softmax,
+//      P.V partials, the chunk's K/V rows streamed into the ring by the
+//      producer like weights
+//   C  chunk merge per (row, q head, 32-dim block) and q8_0 quantise of the
+//      context
 //   D  O projection + residual
 //   E  RMSNorm + quantise; gate/up + SwiGLU; a ticket per 32-feature block
 //      lets the last of its four producers quantise it for the down projection
@@ -42,11 +45,14 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kMegaThreads = kConsumers + 32;   // + the producer warp
 constexpr int kSlotBytes = 16 * kTileBytes;      // 8704: 16 tiles = 4 slices of 256 K
 constexpr int kRingSlots = 16;
-constexpr int kRegionBytes = 60 * 1024;          // activation fragments / attention scratch
+constexpr int kRegionBytes = 64 * 1024;          // activation fragments / attention scratch
 constexpr int kRopeBytes = kTMax * 64 * 2 * 4;   // cos/sin of the step's positions
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s bound on every wait
+constexpr unsigned kSuspendHintNs = 20000;             // longest sleep in one mbarrier try_wait
 constexpr int kTimelineStart = 2 * kMaxBarriers;       // kernel start / end slots
 constexpr int kArrivalBase = 6 * kMaxBarriers + 2;     // [cta][barrier] arrivals after the marks
+constexpr int kCtaMarkBase = kArrivalBase + 256 * kMaxBarriers;  // [cta][barrier][16] sub-phase marks
+constexpr int kCtaMarks = 16;
 
 struct MegaArgs {
     ModelDims d;
@@ -102,15 +108,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, unsigned parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes or the hint (ns) runs out, instead of spinning on the issue slots
+// its warp scheduler shares with the consumer warps.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* b, unsigned parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(b)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase; false on timeout or abort.
 __device__ bool mbar_wait(uint64_t* b, unsigned parity, const int* abort_flag) {
+    if (mbar_try_wait(b, parity)) return true;
     const unsigned long long t0 = global_ns();
-    for (unsigned it = 0;; ++it) {
-        if (mbar_try_wait(b, parity)) return true;
-        if ((it & 63) == 63) {
-            if (*reinterpret_cast<const volatile int*>(abort_flag)) return false;
-            if (global_ns() - t0 > kWaitNs) return false;
-        }
+    for (;;) {
+        if (mbar_try_wait_sleep(b, parity)) return true;
+        if (*reinterpret_cast<const volatile int*>(abort_flag)) return false;
+        if (global_ns() - t0 > kWaitNs) return false;
     }
 }
 
@@ -133,21 +151,38 @@ __device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 
 // Sub-phase mark k (0..3) of phase b in the optional timeline (CTA 0, thread 0).
 __device__ __forceinline__ void mark(unsigned long long* timeline, int b, int k) {
-    if (timeline && blockIdx.x == 0 && threadIdx.x == 0) timeline[2 * kMaxBarriers + 2 + 4 * b + k] = global_ns();
+    if (!timeline || threadIdx.x != 0 || b < 0 || b >= kMaxBarriers || blockIdx.x >= 256) return;
+    const unsigned long long t = global_ns();
+    if (blockIdx.x == 0 && k < 4) timeline[2 * kMaxBarriers + 2 + 4 * b + k] = t;
+    if (k < kCtaMarks) timeline[kCtaMarkBase + ((size_t)blockIdx.x * kMaxBarriers + b) * kCtaMarks + k] = t;
 }
 
 // ------------------------------------------------------------------ schedule
 
-// Weight phases in stream order: per layer A (QKV), D (O), E (gate/up pair),
-// F (down); then G (LM head).  Item i of a phase goes to CTA (i + rot) % grid,
-// where rot is the number of items in all earlier weight phases, so the work
-// rotates over the CTAs from phase to phase.
-enum WPhase { W_QKV = 0, W_O = 1, W_GU = 2, W_DOWN = 3, W_LM = 4 };
+// Streamed phases in ring order: per layer A (QKV rows), B (the K/V rows of
+// the attention items), D (O), E (gate/up pair), F (down); then G (LM head).
+// Item i of a phase goes to CTA (i + rot) % grid, where rot is the number of
+// items in all earlier streamed phases, so the work rotates over the CTAs from
+// phase to phase.
+enum WPhase { W_QKV = 0, W_ATTN = 1, W_O = 2, W_GU = 3, W_DOWN = 4, W_LM = 5 };
+constexpr int kLayerPhases = 5;
+
+// An attention item's K and V chunk rows in the ring: 64 rows each, row stride
+// 272 bytes for fp16 (256 + 16: 16-byte reads of 8 consecutive rows hit 8
+// different bank quads) and 528 for f32; 32 or 16 rows per slot, so one item
+// takes 4 (fp16) or 8 (f32) slots: K rows first, then V rows.
+template <bool F16>
+struct KvSlots {
+    static constexpr int kRowBytes = F16 ? 256 : 512;
+    static constexpr int kRowStride = kRowBytes + 16;
+    static constexpr int kRowsPerSlot = F16 ? 32 : 16;
+    static constexpr int kSlotsPerHalf = kPage / kRowsPerSlot;
+};
 
 struct PhaseInfo {
     int n_items;    // items in the phase
     int rot;        // rotation
-    int bytes;      // weight bytes per item
+    int bytes;      // streamed bytes per item
     int slots;      // ring slots per item
     int count;      // items of this CTA
     int first;      // first global item of this CTA
@@ -156,20 +191,25 @@ struct PhaseInfo {
 
 struct Schedule {
     int grid, cta;
-    int qd, kd, H, F, V, L;
-    // sizes per weight phase kind
-    int n[5], bytes[5];
-    __device__ void init(const ModelDims& d, int grid_, int cta_) {
+    int qd, kd, H, F, V, L, nkv;
+    bool kv_f16;
+    // sizes per streamed phase kind
+    int n[6], bytes[6];
+    __device__ void init(const ModelDims& d, int grid_, int cta_, bool kv_f16_, int n_chunks) {
         grid = grid_;
         cta = cta_;
         H = d.hidden;
         F = d.ffn;
         V = d.vocab;
         L = d.n_layers;
+        nkv = d.n_kv;
+        kv_f16 = kv_f16_;
         qd = d.n_heads * kHeadDim;
         kd = d.n_kv * kHeadDim;
         n[W_QKV] = (qd + 2 * kd) / kTileRows;
         bytes[W_QKV] = (H / kTileK) * kTileBytes;
+        n[W_ATTN] = n_chunks * d.n_kv;  // (chunk, kv head) items
+        bytes[W_ATTN] = 2 * (kv_f16 ? KvSlots<true>::kSlotsPerHalf : KvSlots<false>::kSlotsPerHalf) * kSlotBytes;
         n[W_O] = H / kTileRows;
         bytes[W_O] = (qd / kTileK) * kTileBytes;
         n[W_GU] = F / kTileRows;  // pairs of row groups (gate, up)
@@ -199,10 +239,10 @@ struct Schedule {
         *slot_next += (long long)pi.count * pi.slots;
         return pi;
     }
-    __device__ const uint8_t* item_src(const LayerWeights* lw, const uint8_t* embd, int p, int item) const {
-        if (p >= L * 4) return embd + (size_t)item * bytes[W_LM];
-        const LayerWeights& w = lw[p / 4];
-        switch (p % 4) {
+    __device__ const uint8_t* item_src(const LayerWeights* lw, const uint8_t* embd, int kind, int layer, int item) const {
+        if (kind == W_LM) return embd + (size_t)item * bytes[W_LM];
+        const LayerWeights& w = lw[layer];
+        switch (kind) {
             case W_QKV: return w.qkv + (size_t)item * bytes[W_QKV];
             case W_O: return w.o + (size_t)item * bytes[W_O];
             case W_GU: return w.gu + (size_t)item * bytes[W_GU];
@@ -211,35 +251,67 @@ struct Schedule {
     }
 };
 
+// Row r (0..63) of the K (which = 0) or V (which = 1) rows of the attention
+// item whose slots start at sequence number q0.
+template <bool F16>
+__device__ __forceinline__ uint8_t* kv_row(uint8_t* ring, long long q0, int which, int r) {
+    using KS = KvSlots<F16>;
+    const long long q = q0 + which * KS::kSlotsPerHalf + r / KS::kRowsPerSlot;
+    return ring + (size_t)(q % kRingSlots) * kSlotBytes + (r % KS::kRowsPerSlot) * KS::kRowStride;
+}
+
 // ------------------------------------------------------------------ producer
 
+// The producer warp: lane 0 waits for free slots and posts the expected bytes;
+// a weight item slot is one bulk copy (lane 0), an attention slot one bulk
+// copy per K/V row (one row per lane, the padded row stride above).
 __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, uint64_t* full, uint64_t* empty) {
+    const int lane = threadIdx.x & 31;
     long long q = 0;  // ring slot sequence number
-    const int n_phases = sch.L * 4 + 1;
+    const int n_phases = sch.L * kLayerPhases + 1;
     bool ok = true;
     long long items_before = 0;
+    const int row_bytes = sch.kv_f16 ? KvSlots<true>::kRowBytes : KvSlots<false>::kRowBytes;
+    const int row_stride = sch.kv_f16 ? KvSlots<true>::kRowStride : KvSlots<false>::kRowStride;
+    const int rps = sch.kv_f16 ? KvSlots<true>::kRowsPerSlot : KvSlots<false>::kRowsPerSlot;
     for (int p = 0; p < n_phases && ok; ++p) {
-        const int kind = p < sch.L * 4 ? p % 4 : W_LM;
+        const int kind = p < sch.L * kLayerPhases ? p % kLayerPhases : W_LM;
+        const int layer = p / kLayerPhases;
         const int rot = int(items_before % sch.grid);
         int first = 0;
         const int cnt = sch.count_of(sch.n[kind], rot, &first);
         const int slots = sch.slots_of(kind);
         for (int j = 0; j < cnt && ok; ++j) {
             const int item = first + j * sch.grid;
-            const uint8_t* src = sch.item_src(a.layers, a.embd, p, item);
             for (int k = 0; k < slots; ++k, ++q) {
                 const int s = int(q % kRingSlots);
                 const long long use = q / kRingSlots;
-                if (use > 0 && !mbar_wait(&empty[s], unsigned((use - 1) & 1), a.abort_flag)) { ok = false; break; }
-                const int off = k * kSlotBytes;
-                const int nbytes = min(kSlotBytes, sch.bytes[kind] - off);
-                mbar_expect_tx(&full[s], unsigned(nbytes));
-                bulk_g2s(ring + (size_t)s * kSlotBytes, src + off, unsigned(nbytes), &full[s]);
+                int good = 1;
+                if (lane == 0 && use > 0 && !mbar_wait(&empty[s], unsigned((use - 1) & 1), a.abort_flag)) good = 0;
+                if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
+                uint8_t* dst = ring + (size_t)s * kSlotBytes;
+                if (kind == W_ATTN) {
+                    const int half = slots / 2, which = k / half, r = (k % half) * rps + lane;
+                    const int chunk = item / sch.nkv, h = item % sch.nkv;
+                    if (lane == 0) mbar_expect_tx(&full[s], unsigned(rps * row_bytes));
+                    __syncwarp();
+                    if (lane < rps) {
+                        const long long off = kv_offset(a.kv, sch.nkv, layer, which, h, chunk * kPage + r);
+                        const uint8_t* src = static_cast<const uint8_t*>(a.kv.base) + off * (sch.kv_f16 ? 2 : 4);
+                        bulk_g2s(dst + lane * row_stride, src, unsigned(row_bytes), &full[s]);
+                    }
+                } else if (lane == 0) {
+                    const uint8_t* src = sch.item_src(a.layers, a.embd, kind, layer, item);
+                    const int off = k * kSlotBytes;
+                    const int nbytes = min(kSlotBytes, sch.bytes[kind] - off);
+                    mbar_expect_tx(&full[s], unsigned(nbytes));
+                    bulk_g2s(dst, src + off, unsigned(nbytes), &full[s]);
+                }
             }
         }
         items_before += sch.n[kind];
     }
-    if (!ok) {
+    if (!ok && lane == 0) {
         atomicExch(a.abort_flag, 1);
         // Drain this CTA's copies still in flight before the CTA exits.
         for (long long r = q - 1; r >= 0 && r >= q - kRingSlots; --r) {
@@ -303,6 +375,14 @@ __device__ __forceinline__ bool slot_wait(uint64_t* full, long long q, const int
     bool ok = true;
     if ((threadIdx.x & 31) == 0) ok = mbar_wait(&full[q % kRingSlots], unsigned((q / kRingSlots) & 1), abort_flag);
     return __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+}
+
+// Wait for ring slots q0 .. q0 + n - 1 (n <= 32), one lane per slot.
+__device__ __forceinline__ bool slots_wait(uint64_t* full, long long q0, int n, const int* abort_flag) {
+    const int lane = threadIdx.x & 31;
+    bool ok = true;
+    if (lane < n) ok = mbar_wait(&full[(q0 + lane) % kRingSlots], unsigned(((q0 + lane) / kRingSlots) & 1), abort_flag);
+    return __all_sync(0xffffffffu, ok) != 0;
 }
 
 __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
@@ -427,66 +507,6 @@ __device__ void load_act_smem(const uint8_t* gq, const float* gd, int K, uint8_t
     consumer_sync();
 }
 
-// A chunk's K or V rows held in registers between the load and the store to
-// shared memory (fp16: 4 x 16 bytes per thread; f32: 8 x 16 bytes).
-struct KvRegs {
-    uint4 r[8];
-};
-
-__device__ __forceinline__ void kv_fetch(const KvCache& kv, long long off, int n_pos, KvRegs& v) {
-    const bool f16 = kv.type == KV_F16;
-    const uint4* src = f16 ? reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(kv.base) + off)
-                           : reinterpret_cast<const uint4*>(reinterpret_cast<const float*>(kv.base) + off);
-    const int n = n_pos * (f16 ? 16 : 32);
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-        const int i = threadIdx.x + u * kConsumers;
-        if (i < n) v.r[u] = __ldcg(src + i);
-    }
-}
-
-__device__ __forceinline__ void kv_park(const KvCache& kv, const KvRegs& v, int n_pos, float* sk) {
-    if (kv.type == KV_F16) {
-        const int n = n_pos * 16;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int i = threadIdx.x + u * kConsumers;
-            if (i < n) {
-                const int p = i >> 4, e0 = (i & 15) * 8;
-                const __half2* hv = reinterpret_cast<const __half2*>(&v.r[u]);
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float2 f = __half22float2(hv[k]);
-                    sk[p * (kHeadDim + 1) + e0 + 2 * k] = f.x;
-                    sk[p * (kHeadDim + 1) + e0 + 2 * k + 1] = f.y;
-                }
-            }
-        }
-    } else {
-        const int n = n_pos * 32;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = threadIdx.x + u * kConsumers;
-            if (i < n) {
-                const int p = i >> 5, e0 = (i & 31) * 4;
-                const float4 f = *reinterpret_cast<const float4*>(&v.r[u]);
-                sk[p * (kHeadDim + 1) + e0] = f.x;
-                sk[p * (kHeadDim + 1) + e0 + 1] = f.y;
-                sk[p * (kHeadDim + 1) + e0 + 2] = f.z;
-                sk[p * (kHeadDim + 1) + e0 + 3] = f.w;
-            }
-        }
-    }
-}
-
-// One 64-position K or V chunk of one head into shared memory as f32 rows of
-// stride 129 (conflict-free column reads), 16-byte loads all in flight.
-__device__ __forceinline__ void load_kv_chunk(const KvCache& kv, long long off, int n_pos, float* sk) {
-    KvRegs r;
-    kv_fetch(kv, off, n_pos, r);
-    kv_park(kv, r, n_pos, sk);
-}
-
 // One 256-K slice of one row group from shared memory: the slice partial of
 // the 16 x 8 outputs this lane holds (one fmaf per block, in block order).
 __device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint4* s_act, const float* s_d, int kt0) {
@@ -594,70 +614,59 @@ __device__ __noinline__ void quantize_ticket_block(const MegaArgs& a, int blk, i
     }
 }
 
-// Phase C for one (row t, q head qh) by one warp: merge of the chunk partials
-// in chunk order, then the four q8_0 blocks of that head's context row.
-__device__ __noinline__ void combine_item(const MegaArgs& a, int t, int qh, int T, int n_chunks) {
+// Phase C for one (row t, q head qh, 32-dim block k) by one warp, lane =
+// dim 32 k + lane: merge of the chunk partials in chunk order (M = max m_c;
+// w_c = exp(m_c - M); L = sum w_c l_c; o = sum w_c o_c / L, each sum one
+// sequential fmaf chain), then that q8_0 block of the context row.  All of a
+// batch's loads (32 chunks) are issued together, the next batch's while the
+// current one is summed.
+__device__ __noinline__ void combine_task(const MegaArgs& a, int t, int qh, int k, int n_chunks) {
     const int lane = threadIdx.x & 31;
-    const int nh = a.d.n_heads, G = nh / a.d.n_kv;
-    constexpr int B = 16;  // chunks per prefetch batch
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    if (t < T) {
-        const int h = qh / G, qi = t * G + qh % G;
-        const size_t base0 = (size_t)h * a.max_chunks * (kTMax * 4) + qi;
-        auto po_at = [&](int c, int k) {
-            return &a.part_o[(base0 + (size_t)c * (kTMax * 4)) * kHeadDim + k * 32 + lane];
-        };
-        float po[B][4];
+    const int G = a.d.n_heads / a.d.n_kv, h = qh / G, qi = t * G + qh % G;
+    const size_t base = (size_t)h * a.max_chunks * (kTMax * 4) + qi;  // (h, chunk 0, qi)
+    const float* po = a.part_o + base * kHeadDim + 32 * k + lane;
+    constexpr size_t kStrideO = (size_t)kTMax * 4 * kHeadDim;         // one chunk further
+    float ov[32];
 #pragma unroll
-        for (int u = 0; u < B; ++u)
+    for (int u = 0; u < 32; ++u) ov[u] = u < n_chunks ? __ldcg(po + u * kStrideO) : 0.f;
+    const float2 ml_first = lane < n_chunks ? __ldcg(&a.part_ml[base + (size_t)lane * (kTMax * 4)])
+                                            : make_float2(-INFINITY, 0.f);
+    float M = ml_first.x;
+    for (int c = lane + 32; c < n_chunks; c += 32) M = fmaxf(M, __ldcg(&a.part_ml[base + (size_t)c * (kTMax * 4)].x));
+    M = warp_max(M);
+    float Ls = 0.f, acc = 0.f;
+    for (int c0 = 0; c0 < n_chunks; c0 += 32) {
+        float2 ml = ml_first;
+        if (c0 > 0)
+            ml = c0 + lane < n_chunks ? __ldcg(&a.part_ml[base + (size_t)(c0 + lane) * (kTMax * 4)])
+                                      : make_float2(-INFINITY, 0.f);
+        const float wl = ml.x == -INFINITY ? 0.f : exact_expf(ml.x - M);
+        float nx[32];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) po[u][k] = u < n_chunks ? __ldcg(po_at(u, k)) : 0.f;
-        float M = -INFINITY;
-        for (int c = lane; c < n_chunks; c += 32) M = fmaxf(M, __ldcg(&a.part_ml[base0 + (size_t)c * (kTMax * 4)].x));
-        M = warp_max(M);
-        float Ls = 0.f;
-        for (int c0 = 0; c0 < n_chunks; c0 += 32) {
-            float2 ml = make_float2(-INFINITY, 0.f);
-            if (c0 + lane < n_chunks) ml = __ldcg(&a.part_ml[base0 + (size_t)(c0 + lane) * (kTMax * 4)]);
-            const float wl = ml.x == -INFINITY ? 0.f : exact_expf(ml.x - M);
-            const int nc = min(32, n_chunks - c0);
-            for (int cb = 0; cb < nc; cb += B) {
-                float nx[B][4];
-                const int nb = c0 + cb + B;  // first chunk of the next batch
+        for (int u = 0; u < 32; ++u) {
+            const int c = c0 + 32 + u;
+            nx[u] = c < n_chunks ? __ldcg(po + (size_t)c * kStrideO) : 0.f;
+        }
+        const int nc = min(32, n_chunks - c0);
 #pragma unroll
-                for (int u = 0; u < B; ++u)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) nx[u][k] = nb + u < n_chunks ? __ldcg(po_at(nb + u, k)) : 0.f;
-#pragma unroll
-                for (int u = 0; u < B; ++u) {
-                    const float mc = __shfl_sync(0xffffffffu, ml.x, (cb + u) & 31);
-                    const float lc = __shfl_sync(0xffffffffu, ml.y, (cb + u) & 31);
-                    const float wgt = __shfl_sync(0xffffffffu, wl, (cb + u) & 31);
-                    if (cb + u < nc && mc != -INFINITY) {
-                        Ls = fmaf(wgt, lc, Ls);
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) o[k] = fmaf(wgt, po[u][k], o[k]);
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < B; ++u)
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) po[u][k] = nx[u][k];
+        for (int u = 0; u < 32; ++u) {
+            const float mc = __shfl_sync(0xffffffffu, ml.x, u);
+            const float lc = __shfl_sync(0xffffffffu, ml.y, u);
+            const float wgt = __shfl_sync(0xffffffffu, wl, u);
+            if (u < nc && mc != -INFINITY) {
+                Ls = fmaf(wgt, lc, Ls);
+                acc = fmaf(wgt, ov[u], acc);
             }
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) o[k] = o[k] / Ls;
+        for (int u = 0; u < 32; ++u) ov[u] = nx[u];
     }
-    float am[4], dq[4], iq[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) am[k] = warp_absmax(o[k]);
-    q8_scales<4>(am, dq, iq);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int blk = qh * 4 + k;
-        a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o[k], iq[k]));
-        if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[k]));
-    }
+    const float o = acc / Ls;
+    float am[1] = {warp_absmax(o)}, dq[1], iq[1];
+    q8_scales<1>(am, dq, iq);
+    const int blk = qh * 4 + k;
+    a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o, iq[0]));
+    if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[0]));
 }
 
 // Preparation of one (head, row) of the step, by one warp (phase A2): q heads
@@ -710,106 +719,202 @@ __device__ __noinline__ void prep_row(const MegaArgs& a, const LayerWeights& w, 
     }
 }
 
-// Attention of one (64-position chunk c, kv head h) item by the whole CTA
-// (phase B): scores of the head's G query heads' rows against the chunk, the
-// chunk softmax and the P.V partials (same order as k_attn_chunk).  The q rows
-// and the step's new k/v rows were prepared in phase A (prep_head).
-__device__ __noinline__ void attention_item(const MegaArgs& a, int l, int c, int h, int T, int before, uint8_t* region,
-                                            int mark_pid) {
-    const ModelDims& d = a.d;
-    const int nh = d.n_heads, nkv = d.n_kv, G = nh / nkv;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kv_len = before + T, NQ = T * G;
+// Attention of one (64-position chunk, kv head h) item (phase B) by `wpi`
+// warps (the item's warp wl = 0..wpi-1, named barrier `bar` over them), its K
+// and V rows already in ring slots q0.. (streamed by the producer).  The
+// item's warp wl owns the query rows wl, wl + wpi, ... of the head's G query
+// heads (row = t * G + j): lane `lane` holds positions lane and lane + 32, so
+// each score is one sequential fmaf chain over the 128 dims, the chunk softmax
+// is the warp butterfly (max, then e = exp(s - m) and the pair/butterfly
+// sum), and each P.V output (lane's dims 4 lane .. 4 lane + 3) is one
+// sequential fmaf chain over the chunk's positions; the order of
+// k_attn_chunk and the CPU restatement.
+constexpr int kAttnRegion = 32 * kHeadDim * 4 + 32 * kPage * 8;  // q rows + doubled exp weights
+
+__device__ __forceinline__ void item_sync(int bar, int nthr) {
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthr) : "memory");
+}
+
+// Scores, softmax and P.V of this warp's R rows (R a power of two; rows at or
+// past `nq` are computed on spare query rows and not stored).
+template <bool F16, int R>
+__device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring, long long q0, const float* sq,
+                                          float2* sw, int wl, int wpi, int nq, int G, int p0, int n_pos, int before,
+                                          size_t ml0) {
+    using KS = KvSlots<F16>;
+    const int lane = threadIdx.x & 31;
     const float attn_scale = 1.0f / sqrtf((float)kHeadDim);
-    float* sq = reinterpret_cast<float*>(region);              // [NQ <= 32][128]
-    float* sk = sq + 32 * kHeadDim;                            // [64][129]
-    float* sp = sk + kPage * (kHeadDim + 1);                    // [NQ][64]
-                const int p0 = c * kPage;
-                const int n_pos = min(kPage, kv_len - p0);
-    // q rows of the head's G query heads (normed and rotated in phase A) and
-    // the chunk's K rows; the V rows are loaded into registers now and parked
-    // in shared memory after the scores (the K buffer is reused).
-    for (int i = tid; i < NQ * 32; i += kConsumers) {
+    float acc[R][2];
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
+    {
+        const uint8_t* k0 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane);
+        const uint8_t* k1 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane + 32);
+        constexpr int EB = F16 ? 8 : 4;  // dims per 16-byte read
+#pragma unroll 1
+        for (int eb = 0; eb < kHeadDim / EB; ++eb) {
+            float fa[EB], fb[EB];
+            const uint4 ua = *reinterpret_cast<const uint4*>(k0 + eb * 16);
+            const uint4 ub = *reinterpret_cast<const uint4*>(k1 + eb * 16);
+            if constexpr (F16) {
+                const __half2* ha = reinterpret_cast<const __half2*>(&ua);
+                const __half2* hb = reinterpret_cast<const __half2*>(&ub);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 x = __half22float2(ha[i]), y = __half22float2(hb[i]);
+                    fa[2 * i] = x.x; fa[2 * i + 1] = x.y;
+                    fb[2 * i] = y.x; fb[2 * i + 1] = y.y;
+                }
+            } else {
+                fa[0] = __uint_as_float(ua.x); fa[1] = __uint_as_float(ua.y);
+                fa[2] = __uint_as_float(ua.z); fa[3] = __uint_as_float(ua.w);
+                fb[0] = __uint_as_float(ub.x); fb[1] = __uint_as_float(ub.y);
+                fb[2] = __uint_as_float(ub.z); fb[3] = __uint_as_float(ub.w);
+            }
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const float* qrow = sq + (wl + wpi * rr) * kHeadDim + eb * EB;
+                float qv[EB];
+#pragma unroll
+                for (int i = 0; i < EB; i += 4) {
+                    const float4 q4 = *reinterpret_cast<const float4*>(qrow + i);
+                    qv[i] = q4.x; qv[i + 1] = q4.y; qv[i + 2] = q4.z; qv[i + 3] = q4.w;
+                }
+#pragma unroll
+                for (int i = 0; i < EB; ++i) {
+                    acc[rr][0] = fmaf(qv[i], fa[i], acc[rr][0]);
+                    acc[rr][1] = fmaf(qv[i], fb[i], acc[rr][1]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+        const int r = wl + wpi * rr, t = r / G;
+        const bool ok0 = lane < n_pos && p0 + lane < before + t + 1;
+        const bool ok1 = lane + 32 < n_pos && p0 + lane + 32 < before + t + 1;
+        const float s0 = ok0 ? acc[rr][0] * attn_scale : -INFINITY;
+        const float s1 = ok1 ? acc[rr][1] * attn_scale : -INFINITY;
+        const float m = warp_max(fmaxf(s0, s1));
+        const float x0 = exact_expf(s0 - m), x1 = exact_expf(s1 - m);
+        const float e0 = s0 == -INFINITY ? 0.f : x0;
+        const float e1 = s1 == -INFINITY ? 0.f : x1;
+        const float lsum = warp_sum(e0 + e1);
+        sw[(wl + wpi * rr) * kPage + lane] = make_float2(e0, e0);
+        sw[(wl + wpi * rr) * kPage + lane + 32] = make_float2(e1, e1);
+        if (lane == 0 && r < nq) a.part_ml[ml0 + r] = make_float2(m, lsum);
+    }
+    __syncwarp();
+    // P.V: o[rr] = {dims 4 lane, 4 lane + 1}, {4 lane + 2, 4 lane + 3}; each
+    // component one fmaf chain over the positions (two per __ffma2_rn).
+    float2 o[R][2];
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) o[rr][0] = o[rr][1] = make_float2(0.f, 0.f);
+    auto load_v = [&](const uint8_t* row, float2& v01, float2& v23) {
+        if constexpr (F16) {
+            const uint2 hv = *reinterpret_cast<const uint2*>(row);
+            v01 = __half22float2(*reinterpret_cast<const __half2*>(&hv.x));
+            v23 = __half22float2(*reinterpret_cast<const __half2*>(&hv.y));
+        } else {
+            const float4 f = *reinterpret_cast<const float4*>(row);
+            v01 = make_float2(f.x, f.y);
+            v23 = make_float2(f.z, f.w);
+        }
+    };
+    for (int sidx = 0; sidx < KS::kSlotsPerHalf; ++sidx) {
+        const int pb = sidx * KS::kRowsPerSlot;
+        const uint8_t* vs = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 1, pb) + lane * (F16 ? 8 : 16);
+        const int np = min(KS::kRowsPerSlot, n_pos - pb);
+        int pr = 0;
+#pragma unroll 1
+        for (; pr + 4 <= np; pr += 4) {
+            float2 v[4][2];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) load_v(vs + (pr + i) * KS::kRowStride, v[i][0], v[i][1]);
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const float4* wr = reinterpret_cast<const float4*>(sw + (wl + wpi * rr) * kPage + pb + pr);
+                const float4 w01 = wr[0], w23 = wr[1];
+                const float2 w[4] = {make_float2(w01.x, w01.y), make_float2(w01.z, w01.w),
+                                     make_float2(w23.x, w23.y), make_float2(w23.z, w23.w)};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    o[rr][0] = __ffma2_rn(w[i], v[i][0], o[rr][0]);
+                    o[rr][1] = __ffma2_rn(w[i], v[i][1], o[rr][1]);
+                }
+            }
+        }
+#pragma unroll 1
+        for (; pr < np; ++pr) {
+            float2 v01, v23;
+            load_v(vs + pr * KS::kRowStride, v01, v23);
+#pragma unroll
+            for (int rr = 0; rr < R; ++rr) {
+                const float2 w = sw[(wl + wpi * rr) * kPage + pb + pr];
+                o[rr][0] = __ffma2_rn(w, v01, o[rr][0]);
+                o[rr][1] = __ffma2_rn(w, v23, o[rr][1]);
+            }
+        }
+    }
+#pragma unroll
+    for (int rr = 0; rr < R; ++rr) {
+        const int r = wl + wpi * rr;
+        if (r < nq)
+            reinterpret_cast<float4*>(a.part_o + (ml0 + r) * kHeadDim)[lane] =
+                make_float4(o[rr][0].x, o[rr][0].y, o[rr][1].x, o[rr][1].y);
+    }
+}
+
+// Returns false when a slot wait gave up.
+template <bool F16>
+__device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region, int l,
+                                       int chunk, int h, long long q0, int T, int before, int wl, int wpi, int bar,
+                                       int mark_pid, int mark_k) {
+    using KS = KvSlots<F16>;
+    const int nh = a.d.n_heads, nkv = a.d.n_kv, G = nh / nkv;
+    const int lane = threadIdx.x & 31, it = wl * 32 + lane, nthr = wpi * 32;
+    const int kv_len = before + T, NQ = T * G;
+    const int p0 = chunk * kPage, n_pos = min(kPage, kv_len - p0);
+    float* sq = reinterpret_cast<float*>(region);                         // [32][128] query rows
+    float2* sw = reinterpret_cast<float2*>(region + 32 * kHeadDim * 4);   // [32][64] exp weights, doubled
+    for (int i = it; i < NQ * 32; i += nthr) {
         const int r = i >> 5, c4 = i & 31;
         const int t = r / G, jh = r % G;
         reinterpret_cast<float4*>(sq + r * kHeadDim)[c4] =
             __ldcg(reinterpret_cast<const float4*>(a.qr + ((size_t)t * nh + h * G + jh) * kHeadDim) + c4);
     }
-                if (mark_pid >= 0) mark(a.timeline, mark_pid, 0);
-                // Scores over the chunk (same order as k_attn_chunk).
-                const long long koff = kv_offset(a.kv, nkv, l, 0, h, p0);
-                const long long voff = kv_offset(a.kv, nkv, l, 1, h, p0);
-                KvRegs vreg;
-                kv_fetch(a.kv, voff, n_pos, vreg);
-                load_kv_chunk(a.kv, koff, n_pos, sk);
-                consumer_sync();
-                // Scores: each thread owns a 2 x 2 tile (2 query rows x 2 positions);
-                // every score is still one sequential fmaf chain over the 128 dims.
-                for (int tile = tid; tile < (NQ / 2) * (kPage / 2); tile += kConsumers) {
-                    const int qi0 = (tile / (kPage / 2)) * 2, pp = tile % (kPage / 2);
-                    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-                    const float* qa0 = sq + qi0 * kHeadDim;
-                    const float* qa1 = qa0 + kHeadDim;
-                    const float* k0 = sk + pp * (kHeadDim + 1);
-                    const float* k1 = sk + (pp + 32) * (kHeadDim + 1);
-#pragma unroll 8
-                    for (int e = 0; e < kHeadDim; ++e) {
-                        const float q0 = qa0[e], q1 = qa1[e], kk0 = k0[e], kk1 = k1[e];
-                        acc[0][0] = fmaf(q0, kk0, acc[0][0]);
-                        acc[0][1] = fmaf(q0, kk1, acc[0][1]);
-                        acc[1][0] = fmaf(q1, kk0, acc[1][0]);
-                        acc[1][1] = fmaf(q1, kk1, acc[1][1]);
-                    }
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        const int t = (qi0 + r) / G;
-#pragma unroll
-                        for (int u = 0; u < 2; ++u) {
-                            const int p = pp + 32 * u;
-                            const bool ok = p < n_pos && p0 + p < before + t + 1;
-                            sp[(qi0 + r) * kPage + p] = ok ? acc[r][u] * attn_scale : -INFINITY;
-                        }
-                    }
-                }
-                consumer_sync();
-                if (mark_pid >= 0) mark(a.timeline, mark_pid, 1);
-                for (int qi = warp; qi < NQ; qi += kConsumerWarps) {
-                    const float a0 = sp[qi * kPage + lane], a1 = sp[qi * kPage + lane + 32];
-                    const float m = warp_max(fmaxf(a0, a1));
-                    const float e0 = a0 == -INFINITY ? 0.f : exact_expf(a0 - m);
-                    const float e1 = a1 == -INFINITY ? 0.f : exact_expf(a1 - m);
-                    const float lsum = warp_sum(e0 + e1);
-                    sp[qi * kPage + lane] = e0;
-                    sp[qi * kPage + lane + 32] = e1;
-                    if (lane == 0) a.part_ml[((size_t)h * a.max_chunks + c) * (kTMax * 4) + qi] = make_float2(m, lsum);
-                }
-                consumer_sync();
-                kv_park(a.kv, vreg, n_pos, sk);
-                consumer_sync();
-                if (mark_pid >= 0) mark(a.timeline, mark_pid, 2);
-                // P.V: each thread owns 2 query rows x 2 dims; each output is one
-                // sequential fmaf chain over the chunk's positions.
-                for (int tile = tid; tile < (NQ / 2) * (kHeadDim / 2); tile += kConsumers) {
-                    const int qi0 = (tile / (kHeadDim / 2)) * 2, e0 = tile % (kHeadDim / 2);
-                    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-                    const float* pr0 = sp + qi0 * kPage;
-                    const float* pr1 = pr0 + kPage;
-                    for (int p = 0; p < n_pos; ++p) {
-                        const float w0 = pr0[p], w1 = pr1[p];
-                        const float v0 = sk[p * (kHeadDim + 1) + e0], v1 = sk[p * (kHeadDim + 1) + e0 + 64];
-                        acc[0][0] = fmaf(w0, v0, acc[0][0]);
-                        acc[0][1] = fmaf(w0, v1, acc[0][1]);
-                        acc[1][0] = fmaf(w1, v0, acc[1][0]);
-                        acc[1][1] = fmaf(w1, v1, acc[1][1]);
-                    }
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        float* dst = a.part_o + (((size_t)h * a.max_chunks + c) * (kTMax * 4) + qi0 + r) * kHeadDim;
-                        dst[e0] = acc[r][0];
-                        dst[e0 + 64] = acc[r][1];
-                    }
-                }
-    consumer_sync();
+    const bool ok = slots_wait(full, q0, 2 * KS::kSlotsPerHalf, a.abort_flag);
+    if (wl == 0) mark(a.timeline, mark_pid, mark_k);
+    // The step's own rows were stored to the cache in phase A2, possibly after
+    // the producer copied the page: take them from the cache again.
+    {
+        constexpr int U = KS::kRowBytes / 16;  // 16-byte units per row
+        const int r_lo = max(before - p0, 0), nr = max(n_pos - r_lo, 0);
+        const size_t esz = F16 ? 2 : 4;
+        for (int i = it; i < 2 * nr * U; i += nthr) {
+            const int which = i / (nr * U), rem = i % (nr * U);
+            const int r = r_lo + rem / U, u = rem % U;
+            const long long off = kv_offset(a.kv, nkv, l, which, h, p0 + r);
+            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.kv.base) + off * esz) + u);
+            *reinterpret_cast<uint4*>(kv_row<F16>(ring, q0, which, r) + u * 16) = v;
+        }
+        // Order these generic-proxy stores before the producer's next bulk copies into the slots.
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    item_sync(bar, nthr);
+    if (wl == 0) mark(a.timeline, mark_pid, mark_k + 1);
+    const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // rows of this warp
+    const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4);
+    if (R == 1)
+        attn_rows<F16, 1>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    else if (R == 2)
+        attn_rows<F16, 2>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    else if (R > 2 && R <= 4)
+        attn_rows<F16, 4>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    else if (R > 4)
+        attn_rows<F16, 8>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    if (wl == 0) mark(a.timeline, mark_pid, mark_k + 2);
+    return ok;
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -920,22 +1025,40 @@ __device__ __noinline__ void phase_prep(const KCtx& c, int l) {
         prep_row(a, a.layers[l], l, task / c.T, task % c.T, c.before, c.rope);
 }
 
-// B: attention chunks, one (chunk, kv head) item per CTA at a time.
-__device__ __noinline__ void phase_attn(const KCtx& c, int l, int pid) {
-    const int nkv = c.a.d.n_kv;
-    const int n_items = c.n_chunks * nkv;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-        attention_item(c.a, l, it / nkv, it % nkv, c.T, c.before, c.region, it == (int)blockIdx.x ? pid : -1);
+// B: attention items of this CTA in stream order, two at a time (four warps
+// each, named barriers 2 and 3) while two are left, else one over all eight.
+__device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, int pid) {
+    const MegaArgs& a = c.a;
+    const PhaseInfo pi = c.sch.take(W_ATTN, &cur[0], &cur[1]);
+    const int nkv = a.d.n_kv, warp = threadIdx.x >> 5;
+    bool ok = true;
+    for (int j = 0; j < pi.count; j += 2) {
+        const int n_now = min(2, pi.count - j), wpi = kConsumerWarps / n_now;
+        const int sub = warp / wpi, wl = warp % wpi;
+        const int item = pi.first + (j + sub) * gridDim.x, chunk = item / nkv, h = item % nkv;
+        const long long q0 = pi.slot0 + (long long)(j + sub) * pi.slots;
+        uint8_t* region = c.region + sub * kAttnRegion;
+        const int mp = j == 0 && sub == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
+        const bool good = c.sch.kv_f16
+                              ? attn_item<true>(a, c.ring, c.full, region, l, chunk, h, q0, c.T, c.before, wl, wpi,
+                                                2 + sub, mp, mk)
+                              : attn_item<false>(a, c.ring, c.full, region, l, chunk, h, q0, c.T, c.before, wl, wpi,
+                                                 2 + sub, mp, mk);
+        ok = ok && good;
         consumer_sync();
+        if (threadIdx.x < n_now * pi.slots) mbar_arrive(&c.empty[(pi.slot0 + (long long)j * pi.slots + threadIdx.x) % kRingSlots]);
+        mark(a.timeline, mp, mk + 3);
     }
+    return ok;
 }
 
-// C: chunk merge + quantise the context rows (warps numbered across CTAs).
+// C: chunk merge + quantise, one (row, q head, block) per warp, warps
+// numbered across CTAs.
 __device__ __noinline__ void phase_combine(const KCtx& c) {
     const int nh = c.a.d.n_heads, warp = threadIdx.x >> 5;
-    const int n_items = kTMax * nh;
-    for (int it = blockIdx.x + gridDim.x * warp; it < n_items; it += gridDim.x * kConsumerWarps)
-        combine_item(c.a, it / nh, it % nh, c.T, c.n_chunks);
+    const int n_tasks = c.T * nh * 4;
+    for (int it = blockIdx.x + gridDim.x * warp; it < n_tasks; it += gridDim.x * kConsumerWarps)
+        combine_task(c.a, it / (nh * 4), (it / 4) % nh, it % 4, c.n_chunks);
 }
 
 // D: O projection + residual.  F: down projection + residual.
@@ -1087,7 +1210,10 @@ __device__ __noinline__ void phase_accept(const KCtx& c) {
     }
     consumer_sync();
     if (threadIdx.x == 0) accept_choices(st, a.ids);
-    if (a.timeline && threadIdx.x == 0) a.timeline[kTimelineStart + 1] = global_ns();
+    if (a.timeline && threadIdx.x == 0) {
+        a.timeline[kTimelineStart + 1] = global_ns();
+        a.timeline[kCtaMarkBase + (size_t)(kMaxBarriers - 1) * kCtaMarks + 1] = clock64();
+    }
 }
 
 template <int kNK>
@@ -1100,11 +1226,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     __shared__ int s_flag;
     const int T = args.state->T;
     if (T <= 0) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         KCtx& c = s_ctx;
         c.a = args;
-        c.sch.init(args.d, gridDim.x, blockIdx.x);
+        c.T = T;
+        c.before = args.state->before;
+        c.kv_len = c.before + T;
+        c.n_chunks = (c.kv_len + kPage - 1) / kPage;
+        c.sch.init(args.d, gridDim.x, blockIdx.x, args.kv.type == KV_F16, c.n_chunks);
         c.ring = smem;
         c.region = smem + (size_t)kRingSlots * kSlotBytes;
         c.rope = reinterpret_cast<float*>(c.region + kRegionBytes);
@@ -1114,11 +1244,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
         c.scale = s_scale;
         c.cand = s_cand;
         c.flag = &s_flag;
-        c.T = T;
-        c.before = args.state->before;
-        c.kv_len = c.before + T;
-        c.n_chunks = (c.kv_len + kPage - 1) / kPage;
-        if (args.timeline && blockIdx.x == 0) args.timeline[kTimelineStart] = global_ns();
+        if (args.timeline && blockIdx.x == 0) {
+            args.timeline[kTimelineStart] = global_ns();
+            // SM cycles beside the timer (CTA 0, last barrier slot): the clock the step ran at.
+            args.timeline[kCtaMarkBase + (size_t)(kMaxBarriers - 1) * kCtaMarks] = clock64();
+        }
         for (int s = 0; s < kRingSlots; ++s) {
             mbar_init(&c.full[s], 1);
             mbar_init(&c.empty[s], 1);
@@ -1128,7 +1258,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     __syncthreads();
     const KCtx& c = s_ctx;
     if (warp == kConsumerWarps) {
-        if (lane == 0) producer(c.a, c.sch, c.ring, c.full, c.empty);
+        producer(c.a, c.sch, c.ring, c.full, c.empty);
         return;
     }
     unsigned target = 0;
@@ -1136,22 +1266,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     phase_embed(c);
     if (!end_phase(c, &target)) return;
     for (int l = 0; l < c.a.d.n_layers; ++l) {
-        if (!phase_qkv<kNK>(c, l, cur, phase_index(target) + 1)) consumer_fail(c.a);
+        if (!phase_qkv<kNK>(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
         phase_prep(c, l);
         if (!end_phase(c, &target)) return;
-        phase_attn(c, l, phase_index(target) + 1);
+        if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
         phase_combine(c);
         if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid(c, l, cur, phase_index(target) + 1, false)) consumer_fail(c.a);
+        if (!phase_proj_resid(c, l, cur, phase_index(target), false)) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
-        if (!phase_gu<kNK>(c, l, cur, phase_index(target) + 1)) consumer_fail(c.a);
+        if (!phase_gu<kNK>(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid(c, l, cur, phase_index(target) + 1, true)) consumer_fail(c.a);
+        if (!phase_proj_resid(c, l, cur, phase_index(target), true)) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
     }
-    if (!phase_lm<kNK>(c, cur, phase_index(target) + 1)) consumer_fail(c.a);
+    if (!phase_lm<kNK>(c, cur, phase_index(target))) consumer_fail(c.a);
     if (!end_phase(c, &target)) return;
     if (blockIdx.x == 0) phase_accept(c);
 }
@@ -1202,7 +1332,7 @@ bool megakernel_supports(const ModelDims& d, int grid) {
                                            need(qd, d.hidden / kTileRows, qd / 256)),
                                   std::max(need(d.hidden, d.ffn / kTileRows, 2 * d.hidden / 256),
                                            need(d.ffn, d.hidden / kTileRows, d.ffn / 256)));
-    const size_t attn = (size_t)(32 * kHeadDim + kPage * (kHeadDim + 1) + 32 * kPage) * 4;
+    const size_t attn = (size_t)2 * kAttnRegion;  // two items at a time
     return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
 }
 

@@ -300,12 +300,13 @@ class Decoder:
     def step_timeline(self):
         """(arrive_ns, release_ns) per grid barrier and (start, end) of the last
         persistent step; needs MTB_PROFILE=1 when the decoder was created."""
-        out = (C.c_int64 * (6 * 512 + 2 + 256 * 512))()
+        out = (C.c_int64 * (6 * 512 + 2 + 256 * 512 * 17))()
         n = C.c_int()
         self._check(lib().mtb_step_timeline(self.ptr, out, len(out), C.byref(n)), "step_timeline")
         vals = np.frombuffer(out, dtype=np.int64)
         marks = [tuple(vals[1026 + 4 * b:1030 + 4 * b]) for b in range(512)]
-        self.last_arrivals = vals[6 * 512 + 2:].reshape(256, 512)
+        self.last_arrivals = vals[6 * 512 + 2:6 * 512 + 2 + 256 * 512].reshape(256, 512)
+        self.last_cta_marks = vals[6 * 512 + 2 + 256 * 512:].reshape(256, 512, 16)
         return [(vals[2 * b], vals[2 * b + 1]) for b in range(512)], (vals[1024], vals[1025]), marks
 
     def transfer_bytes(self):

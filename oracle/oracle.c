@@ -34,42 +34,54 @@ static inline uint16_t f2h(float f) {
 static inline float round_f16(float f) { return h2f(f2h(f)); }
 
 /* ------------------------------------------------------------ exp, sin, cos
- * Own implementations (Cody-Waite range reduction + Taylor series, evaluated
- * in double with every operation rounded separately; the library is built
- * with -ffp-contract=off).  The CUDA kernels evaluate the same sequence, so
- * both sides return identical floats.  Accuracy: the double result is within
- * a few 1e-16 relative of the true value, so the float result is the
- * correctly rounded one except in rare near-tie cases. */
-#define MTB_LN2_HI 0.6931471803691238       /* ln 2 to 32 bits */
-#define MTB_LN2_LO 1.9082149292705877e-10   /* ln 2 - MTB_LN2_HI */
-#define MTB_INV_LN2 1.4426950408889634
+ * Own implementations; the library is built with -ffp-contract=off, so only
+ * the fmaf calls written here are fused, and the CUDA kernels evaluate the
+ * same sequence, so both sides return identical floats.
+ * exp: float arithmetic throughout.  n = rint(x log2 e); Cody-Waite reduction
+ * r = x - n ln2 with ln2 split into a 16-bit head (0x3F317200) and a tail,
+ * each step one fmaf; e^r by the Taylor polynomial to r^7 in Horner form
+ * (fmaf per step, coefficients the floats nearest 1/k!); then exact scaling
+ * by 2^n (two factors, so a subnormal result is rounded once).
+ * Within 1 ulp of the true value (|r| <= 0.347: truncation 5e-9 relative).
+ * sin/cos: Cody-Waite reduction by pi/2 and Taylor series in double, every
+ * operation rounded separately; the double result is within a few 1e-16
+ * relative of the true value, so the float result is the correctly rounded
+ * one except in rare near-tie cases. */
 #define MTB_PIO2_1 1.5707963267341256       /* pi/2 to 33 bits */
 #define MTB_PIO2_2 6.077100506303966e-11    /* next 33 bits */
 #define MTB_PIO2_3 2.0222662487959506e-21   /* remainder */
 #define MTB_TWO_OVER_PI 0.6366197723675814
 
+static inline float bits_f32(uint32_t u) {
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
 float orc_expf(float x) {
+    /* x is clamped for the arithmetic and the special cases are selected at
+     * the end; 2^n is applied as (p * 2^a) * 2^b with (a, b) = (n, 0),
+     * (1, 127) for n = 128, (n + 64, -64) for n < -126. */
+    const float xc = fminf(fmaxf(x, -103.972084f), 88.7228317f);
+    const float n = rintf(xc * 1.44269502f);
+    float r = fmaf(n, -0.693145752f, xc);
+    r = fmaf(n, -1.42860677e-6f, r);
+    float p = 1.98412701e-4f;
+    p = fmaf(p, r, 1.38888892e-3f);
+    p = fmaf(p, r, 8.33333377e-3f);
+    p = fmaf(p, r, 4.16666679e-2f);
+    p = fmaf(p, r, 1.66666672e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    const int ni = (int)n;
+    const int ea = ni > 127 ? 1 : (ni < -126 ? ni + 64 : ni);
+    const int eb = ni > 127 ? 127 : (ni < -126 ? -64 : 0);
+    const float y = (p * bits_f32((uint32_t)(ea + 127) << 23)) * bits_f32((uint32_t)(eb + 127) << 23);
     if (x != x) return x;
-    if (x > 88.8f) return INFINITY;
-    if (x < -104.0f) return 0.0f;
-    const double xd = (double)x;
-    const double n = rint(xd * MTB_INV_LN2);
-    const double r = (xd - n * MTB_LN2_HI) - n * MTB_LN2_LO;
-    /* e^r = sum r^k / k!, k <= 12, |r| <= 0.35 */
-    double p = 1.0 / 479001600.0;
-    p = p * r + 1.0 / 39916800.0;
-    p = p * r + 1.0 / 3628800.0;
-    p = p * r + 1.0 / 362880.0;
-    p = p * r + 1.0 / 40320.0;
-    p = p * r + 1.0 / 5040.0;
-    p = p * r + 1.0 / 720.0;
-    p = p * r + 1.0 / 120.0;
-    p = p * r + 1.0 / 24.0;
-    p = p * r + 1.0 / 6.0;
-    p = p * r + 0.5;
-    p = p * r + 1.0;
-    p = p * r + 1.0;
-    return (float)ldexp(p, (int)n);
+    if (x > 88.7228317f) return INFINITY;   /* the largest x with a finite result */
+    if (x < -103.972084f) return 0.0f;      /* e^x below half the smallest subnormal */
+    return y;
 }
 
 void orc_sincosf(float x, float* s_out, float* c_out) {
