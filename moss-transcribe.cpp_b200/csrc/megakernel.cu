@@ -19,8 +19,8 @@
 //   C  chunk merge per (row, q head, 32-dim block) and q8_0 quantise of the
 //      context
 //   D  O projection + residual
-//   E  RMSNorm + quantise; gate/up + SwiGLU; a ticket per 32-feature block
-//      lets the last of its four producers quantise it for the down projection
+//   E  RMSNorm + quantise; gate/up + SwiGLU per 32-feature block, quantised
+//      for the down projection by the CTA that computed it
 //   F  down projection + residual
 // then the final RMSNorm, the LM head with a fused first max, and the
 // acceptance / rollback of src/cpu_speculative.cpp:142-153 (CTA 0).
@@ -212,8 +212,8 @@ struct Schedule {
         bytes[W_ATTN] = 2 * (kv_f16 ? KvSlots<true>::kSlotsPerHalf : KvSlots<false>::kSlotsPerHalf) * kSlotBytes;
         n[W_O] = H / kTileRows;
         bytes[W_O] = (qd / kTileK) * kTileBytes;
-        n[W_GU] = F / kTileRows;  // pairs of row groups (gate, up)
-        bytes[W_GU] = 2 * (H / kTileK) * kTileBytes;
+        n[W_GU] = F / 32;  // 32-feature blocks: four (gate, up) pairs of row groups
+        bytes[W_GU] = 8 * (H / kTileK) * kTileBytes;
         n[W_DOWN] = H / kTileRows;
         bytes[W_DOWN] = (F / kTileK) * kTileBytes;
         n[W_LM] = V / kTileRows;
@@ -509,6 +509,9 @@ __device__ void load_act_smem(const uint8_t* gq, const float* gd, int K, uint8_t
 
 // One 256-K slice of one row group from shared memory: the slice partial of
 // the 16 x 8 outputs this lane holds (one fmaf per block, in block order).
+// kLow: the step has at most 8 rows, so the outputs of rows 8..15 (the .z/.w
+// components) are not formed.
+template <bool kLow>
 __device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint4* s_act, const float* s_d, int kt0) {
     const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -521,17 +524,22 @@ __device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint
         int c0[4], c1[4];
         mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv.x, wv.y);
         mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv.z, wv.w);
-        const float x0g = s_d[(2 * kt) * 16 + g], x0h = s_d[(2 * kt) * 16 + g + 8];
-        const float x1g = s_d[(2 * kt + 1) * 16 + g], x1h = s_d[(2 * kt + 1) * 16 + g + 8];
+        const float x0g = s_d[(2 * kt) * 16 + g], x1g = s_d[(2 * kt + 1) * 16 + g];
         const float w00 = h2f_lo(sv.x), w01 = h2f_hi(sv.x), w10 = h2f_lo(sv.y), w11 = h2f_hi(sv.y);
         acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
         acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
-        acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
-        acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+        if (!kLow) {
+            const float x0h = s_d[(2 * kt) * 16 + g + 8];
+            acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
+            acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+        }
         acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
         acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
-        acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
-        acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+        if (!kLow) {
+            const float x1h = s_d[(2 * kt + 1) * 16 + g + 8];
+            acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
+            acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+        }
     }
     return make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
@@ -539,6 +547,7 @@ __device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint
 // Outputs of row group `rg_local` (0 or 1 for a gate/up pair) of the item whose
 // slots start at sequence number q0: 0 + slice 0 + slice 1 + ... in order.
 // Waits for and releases the item's ring slots (all of them when `release`).
+template <bool kLow>
 __device__ __forceinline__ bool item_rows(const uint8_t* ring, uint64_t* full, uint64_t* empty, long long q0, int kt_n, int rg_local,
                           const uint4* s_act, const float* s_d, const int* abort_flag, float4* out) {
     const int S = kt_n / 4;
@@ -548,7 +557,7 @@ __device__ __forceinline__ bool item_rows(const uint8_t* ring, uint64_t* full, u
         const long long q = q0 + off / kSlotBytes;
         if ((off % kSlotBytes) == 0 || s == 0)
             if (!slot_wait(full, q, abort_flag)) return false;
-        const float4 p = slice_partial(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, s * 4);
+        const float4 p = slice_partial<kLow>(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, s * 4);
         y.x = y.x + p.x; y.y = y.y + p.y; y.z = y.z + p.z; y.w = y.w + p.w;
     }
     *out = y;
@@ -564,7 +573,7 @@ __device__ __forceinline__ void release_item(uint64_t* empty, long long q0, int 
 // `epi(j, part)` runs once per item (item j's units start at part + j*U*32,
 // row group r's slice s at (r*S + s)*32) and adds the slices in order.  The
 // phase's ring slots are all released after the units (at most 8 per CTA).
-template <typename Epi>
+template <bool kLow, typename Epi>
 __device__ __forceinline__ bool weight_phase(const PhaseInfo& pi, int rgs, int kt_n, const uint8_t* ring,
                                              uint64_t* full, uint64_t* empty, const uint4* s_act, const float* s_d,
                                              float4* s_part, const int* abort_flag, Epi epi) {
@@ -577,7 +586,7 @@ __device__ __forceinline__ bool weight_phase(const PhaseInfo& pi, int rgs, int k
         const int off = (r * kt_n + sl * 4) * kTileBytes;
         const long long q = pi.slot0 + (long long)j * pi.slots + off / kSlotBytes;
         if (!slot_wait(full, q, abort_flag)) { ok = false; break; }
-        s_part[u * 32 + lane] = slice_partial(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, sl * 4);
+        s_part[u * 32 + lane] = slice_partial<kLow>(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, sl * 4);
     }
     consumer_sync();
     const int n_slots = pi.count * pi.slots;
@@ -594,24 +603,6 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
         y.x = y.x + p.x; y.y = y.y + p.y; y.z = y.z + p.z; y.w = y.w + p.w;
     }
     return y;
-}
-
-// The SwiGLU block `blk` (32 features of all 16 rows) quantised for the down
-// projection by the warp that completed its last group (rows >= T are zero).
-__device__ __noinline__ void quantize_ticket_block(const MegaArgs& a, int blk, int T) {
-    const int lane = threadIdx.x & 31;
-    const int F = a.d.ffn;
-    float v[kTMax], m[kTMax], dq[kTMax], iq[kTMax];
-#pragma unroll
-    for (int row = 0; row < kTMax; ++row) v[row] = row < T ? __ldcg(a.gu + (size_t)row * F + blk * 32 + lane) : 0.f;
-#pragma unroll
-    for (int row = 0; row < kTMax; ++row) m[row] = warp_absmax(v[row]);
-    q8_scales<kTMax>(m, dq, iq);
-#pragma unroll
-    for (int row = 0; row < kTMax; ++row) {
-        a.act2_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[row], iq[row]));
-        if (lane == 0) a.act2_d[blk * 16 + row] = __half2float(__float2half_rn(dq[row]));
-    }
 }
 
 // Phase C for one (row t, q head qh, 32-dim block k) by one warp, lane =
@@ -995,7 +986,7 @@ __device__ __forceinline__ void for_outputs(const float4& y, int T, F f) {
 }
 
 // A: RMSNorm + quantise (every CTA), QKV rows -> qkv.
-template <int NK>
+template <int NK, bool kLow>
 __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int pid) {
     const MegaArgs& a = c.a;
     const LayerWeights& w = a.layers[l];
@@ -1007,7 +998,7 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
     const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     const int ldq = (a.d.n_heads + 2 * a.d.n_kv) * kHeadDim, T = c.T;
-    return weight_phase(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+    return weight_phase<kLow>(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
                             for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
@@ -1062,6 +1053,7 @@ __device__ __noinline__ void phase_combine(const KCtx& c) {
 }
 
 // D: O projection + residual.  F: down projection + residual.
+template <bool kLow>
 __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* cur, int pid, bool down) {
     const MegaArgs& a = c.a;
     const int K = down ? a.d.ffn : a.d.n_heads * kHeadDim, H = a.d.hidden, T = c.T;
@@ -1071,7 +1063,7 @@ __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* c
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
-    return weight_phase(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+    return weight_phase<kLow>(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
                             for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
@@ -1081,49 +1073,57 @@ __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* c
                         });
 }
 
-// E: RMSNorm + quantise; gate/up + SwiGLU -> gu; a ticket per 32-feature block
-// lets the last of its four groups quantise it for the down projection.
-template <int NK>
+// E: RMSNorm + quantise; gate/up for one 32-feature block per item (four
+// (gate, up) pairs of row groups, 8 ring slots), SwiGLU into shared memory
+// (warp k: pair k), then the block's q8_0 quantisation for the down
+// projection (one row per warp at a time) straight from shared memory.
+template <int NK, bool kLow>
 __device__ __noinline__ bool phase_gu(const KCtx& c, int l, long long* cur, int pid) {
     const MegaArgs& a = c.a;
     const LayerWeights& w = a.layers[l];
     constexpr int K = 256 * NK;
-    const int F = a.d.ffn, T = c.T, lane = threadIdx.x & 31;
+    constexpr int S = K / kTileK / 4;  // slices per row group
+    const int T = c.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* act_q = c.region;
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
     norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T, act_q, act_d, c.wsum, c.scale);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_GU, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
-    constexpr int S = K / kTileK / 4;
-    return weight_phase(pi, 2, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
-                        s_part, a.abort_flag, [&](int j, const float4* part) {
-                            const int item = pi.first + j * gridDim.x;  // features 8i..8i+7
-                            const float4 gq = sum_slices(part, S), uq = sum_slices(part + S * 32, S);
-                            const float gg[4] = {gq.x, gq.y, gq.z, gq.w}, uu[4] = {uq.x, uq.y, uq.z, uq.w};
-                            const int g = lane >> 2, t = lane & 3;
-                            const int feat = item * kTileRows + 2 * t;
+    float* s_gu = reinterpret_cast<float*>(s_part + (size_t)pi.count * 8 * S * 32);  // [16 rows][32 features]
+    const bool ok = weight_phase<kLow>(pi, 8, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q),
+                                       act_d, s_part, a.abort_flag, [](int, const float4*) {});
+    const int g = lane >> 2, t = lane & 3;
+    for (int j = 0; j < pi.count; ++j) {
+        const int blk = pi.first + j * gridDim.x;  // features 32 blk .. 32 blk + 31
+        if (warp < 4) {
+            const float4* part = s_part + (size_t)j * 8 * S * 32;
+            const float4 gq = sum_slices(part + (2 * warp) * S * 32, S), uq = sum_slices(part + (2 * warp + 1) * S * 32, S);
+            const float gg[4] = {gq.x, gq.y, gq.z, gq.w}, uu[4] = {uq.x, uq.y, uq.z, uq.w};
 #pragma unroll
-                            for (int k = 0; k < 4; ++k) {
-                                const int row = g + (k >> 1) * 8;
-                                if (row < T) {
-                                    const float sl = gg[k] / (1.0f + exact_expf(-gg[k]));
-                                    a.gu[(size_t)row * F + feat + (k & 1)] = sl * uu[k];
-                                }
-                            }
-                            __threadfence();
-                            __syncwarp();
-                            int last = 0;
-                            if (lane == 0) last = atomicAdd(&a.tickets[l * (F / 32) + item / 4], 1u) == 3u;
-                            if (__shfl_sync(0xffffffffu, last, 0)) {
-                                __threadfence();
-                                quantize_ticket_block(a, item / 4, T);
-                            }
-                        });
+            for (int k = 0; k < (kLow ? 2 : 4); ++k) {
+                const int row = g + (k >> 1) * 8;
+                if (row < T) {
+                    const float sl = gg[k] / (1.0f + exact_expf(-gg[k]));
+                    s_gu[row * 32 + 8 * warp + 2 * t + (k & 1)] = sl * uu[k];
+                }
+            }
+        }
+        consumer_sync();
+        for (int row = warp; row < T; row += kConsumerWarps) {
+            const float v = s_gu[row * 32 + lane];
+            float am[1] = {warp_absmax(v)}, dq[1], iq[1];
+            q8_scales<1>(am, dq, iq);
+            a.act2_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, iq[0]));
+            if (lane == 0) a.act2_d[blk * 16 + row] = __half2float(__float2half_rn(dq[0]));
+        }
+        consumer_sync();
+    }
+    return ok;
 }
 
 // G: final RMSNorm + quantise; LM head with the fused first max -> lm_val[cta].
-template <int NK>
+template <int NK, bool kLow>
 __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
     const MegaArgs& a = c.a;
     constexpr int K = 256 * NK;
@@ -1139,13 +1139,16 @@ __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
     for (int j = warp; j < pi.count; j += kConsumerWarps) {
         const int item = pi.first + j * gridDim.x;
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
+        const int jw = j / kConsumerWarps;  // this warp's item count so far
+        if (warp == 0 && jw < 7 && slot_wait(c.full, q0, a.abort_flag)) mark(a.timeline, pid, 1 + 2 * jw);
         float4 y;
-        if (!item_rows(c.ring, c.full, c.empty, q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
+        if (!item_rows<kLow>(c.ring, c.full, c.empty, q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
                        a.abort_flag, &y)) {
             ok = false;
             break;
         }
         release_item(c.empty, q0, pi.slots);
+        if (warp == 0 && jw < 7) mark(a.timeline, pid, 2 + 2 * jw);
         const float yy[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -1216,6 +1219,34 @@ __device__ __noinline__ void phase_accept(const KCtx& c) {
     }
 }
 
+// The consumer warps' phase sequence; kLow: the step has at most 8 rows.
+template <int kNK, bool kLow>
+__device__ __noinline__ void run_phases(const KCtx& c) {
+    unsigned target = 0;
+    long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
+    phase_embed(c);
+    if (!end_phase(c, &target)) return;
+    for (int l = 0; l < c.a.d.n_layers; ++l) {
+        if (!phase_qkv<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        phase_prep(c, l);
+        if (!end_phase(c, &target)) return;
+        if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        phase_combine(c);
+        if (!end_phase(c, &target)) return;
+        if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), false)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        if (!phase_gu<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+        if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), true)) consumer_fail(c.a);
+        if (!end_phase(c, &target)) return;
+    }
+    if (!phase_lm<kNK, kLow>(c, cur, phase_index(target))) consumer_fail(c.a);
+    if (!end_phase(c, &target)) return;
+    if (blockIdx.x == 0) phase_accept(c);
+}
+
 template <int kNK>
 __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs args) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1261,30 +1292,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
         producer(c.a, c.sch, c.ring, c.full, c.empty);
         return;
     }
-    unsigned target = 0;
-    long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
-    phase_embed(c);
-    if (!end_phase(c, &target)) return;
-    for (int l = 0; l < c.a.d.n_layers; ++l) {
-        if (!phase_qkv<kNK>(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        phase_prep(c, l);
-        if (!end_phase(c, &target)) return;
-        if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        phase_combine(c);
-        if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid(c, l, cur, phase_index(target), false)) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_gu<kNK>(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid(c, l, cur, phase_index(target), true)) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-    }
-    if (!phase_lm<kNK>(c, cur, phase_index(target))) consumer_fail(c.a);
-    if (!end_phase(c, &target)) return;
-    if (blockIdx.x == 0) phase_accept(c);
+    if (c.T <= 8)
+        run_phases<kNK, true>(c);
+    else
+        run_phases<kNK, false>(c);
 }
+
 
 }  // namespace
 
@@ -1330,7 +1343,7 @@ bool megakernel_supports(const ModelDims& d, int grid) {
     };
     const size_t worst = std::max(std::max(need(d.hidden, (qd + 2 * d.n_kv * kHeadDim) / kTileRows, d.hidden / 256),
                                            need(qd, d.hidden / kTileRows, qd / 256)),
-                                  std::max(need(d.hidden, d.ffn / kTileRows, 2 * d.hidden / 256),
+                                  std::max(need(d.hidden, d.ffn / 32, 8 * d.hidden / 256) + 16 * 32 * 4,
                                            need(d.ffn, d.hidden / kTileRows, d.ffn / 256)));
     const size_t attn = (size_t)2 * kAttnRegion;  // two items at a time
     return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
