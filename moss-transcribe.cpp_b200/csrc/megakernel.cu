@@ -334,13 +334,14 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
         if (a.timeline && blockIdx.x == 0) a.timeline[2 * b] = global_ns();
         // Every CTA's arrival, for the skew between CTAs.
         if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
-        __threadfence();
-        atomicAdd(a.bar, 1u);
+        // Arrive with release semantics (the CTA's writes, ordered before by the
+        // named barrier, become visible with it); poll relaxed; acquire once.
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long t0 = global_ns();
         int status = 0;
         for (unsigned it = 0;; ++it) {
             unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
             if (v >= target) break;
             if ((it & 31) == 31) {
                 if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
@@ -352,7 +353,7 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
                 }
             }
         }
-        __threadfence();
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         if (a.timeline && blockIdx.x == 0) a.timeline[2 * b + 1] = global_ns();
         *s_flag = status;
     }
@@ -391,7 +392,8 @@ __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
 }
 
 // RMSNorm (the 256-thread tree of k_rmsnorm_quant) and q8_0 quantisation of
-// rows [16][K] of global x into shared fragments; rows >= T become zero.
+// rows [T][K] of global x into shared fragments (rows >= T are left as they
+// are: every consumer discards the outputs of those rows).
 // Thread 32w + lane owns elements 256k + 32w + lane, i.e. lane `lane` of the
 // blocks b = 8k + w: its partial sum runs over k in order (the same tree), the
 // loads are coalesced per warp and all in flight together, and each warp
@@ -403,25 +405,11 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
     constexpr int K = 256 * NK;
     constexpr int RG = 8;  // rows per pass (rows are independent; 8 x NK values per lane)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint32_t* q32 = reinterpret_cast<uint32_t*>(act_q);
     float wv[NK];
 #pragma unroll
     for (int k = 0; k < NK; ++k) wv[k] = wn[256 * k + 32 * warp + lane];
     for (int t0 = 0; t0 < kTMax; t0 += RG) {
-        if (t0 >= T) {
-            // Rows without a token: 32 zero codes per owned block (8 words) and d = 0.
-            if (lane < 8) {
-#pragma unroll
-                for (int r = 0; r < RG; ++r)
-#pragma unroll
-                    for (int k = 0; k < NK; ++k) {
-                        const int blk = 8 * k + warp;
-                        q32[((size_t)blk * 512 + frag_offset(t0 + r, lane * 4)) / 4] = 0u;
-                        if (lane == 0) act_d[blk * 16 + t0 + r] = 0.f;
-                    }
-            }
-            continue;
-        }
+        if (t0 >= T) break;  // rows >= T are never read back: the kernels discard their outputs
         float v[RG][NK];
 #pragma unroll
         for (int r = 0; r < RG; ++r)
@@ -437,6 +425,7 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
 #pragma unroll
             for (int k = 0; k < NK; ++k) acc[r] += (double)(v[r][k] * v[r][k]);
         }
+        if (t0 == 0) mark(timeline, pid, 4);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
@@ -449,10 +438,11 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
         if (tid < RG && t0 + tid < T) {
             double tot = 0.0;
             for (int i = 0; i < kConsumerWarps; ++i) tot += s_wsum[i * kTMax + t0 + tid];
-            const float mean = (float)(tot / K);
+            const float mean = (float)(tot * (1.0 / K));  // K a power of two: the same as tot / K
             s_scale[t0 + tid] = 1.0f / sqrtf(mean + eps);
         }
         consumer_sync();
+        if (t0 == 0) mark(timeline, pid, 5);
         // amax per (row, block) by one integer max reduction each; the scale
         // divisions spread over the lanes (q8_scales).
         constexpr int NB = RG * NK <= 32 ? RG * NK : 32;
@@ -479,9 +469,8 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
             }
         }
     }
-    (void)timeline;
-    (void)pid;
     consumer_sync();
+    mark(timeline, pid, 6);
 }
 
 // Copy fragments [K/32][512] + scales [K/32][16] from global into shared
@@ -687,7 +676,7 @@ __device__ __noinline__ void prep_row(const MegaArgs& a, const LayerWeights& w, 
 #pragma unroll
     for (int q = 0; q < 4; ++q) part[q] = warp_sum_d((double)(x[q] * x[q]));
     const double tot = part[0] + part[1] + part[2] + part[3];
-    const float mean = (float)(tot / kHeadDim);
+    const float mean = (float)(tot * (1.0 / kHeadDim));  // exact: 128 is a power of two
     const float scale = 1.0f / sqrtf(mean + a.d.eps);
     float y[4], o[4];
 #pragma unroll
@@ -993,7 +982,7 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
     constexpr int K = 256 * NK;
     uint8_t* act_q = c.region;
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, a.timeline, pid);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
