@@ -11,11 +11,11 @@
 //
 // Phases per layer (src/qwen3.cpp:62-218):
 //   A  RMSNorm + q8_0 quantise (every CTA, into shared memory); QKV rows
-//   A2 per-head RMSNorm + RoPE of q (and of k for the step's new positions,
-//      stored to the KV cache with the new v rows)
-//   B  attention per (64-position chunk, kv head): scores, chunk softmax,
-//      P.V partials, the chunk's K/V rows streamed into the ring by the
-//      producer like weights
+//   B  attention per (64-position chunk, kv head): per-head RMSNorm + RoPE of
+//      the head's q rows (and of k for the step's new positions, stored to
+//      the KV cache with the new v rows by the item holding them), scores,
+//      chunk softmax, P.V partials; the chunk's K/V rows streamed into the
+//      ring by the producer like weights
 //   C  chunk merge per (row, q head, 32-dim block) and q8_0 quantise of the
 //      context
 //   D  O projection + residual
@@ -66,7 +66,6 @@ struct MegaArgs {
     float* x;        // [16][H]
     float* qkv;      // [16][qd + 2 kd]
     float* gu;       // [16][F]
-    float* qr;       // [16][n_heads][128] q rows after RMSNorm + RoPE
     uint8_t* act_q;  // context fragments (K = qd), then reused for K = F below
     float* act_d;
     uint8_t* act2_q; // SwiGLU fragments (K = F)
@@ -649,53 +648,29 @@ __device__ __noinline__ void combine_task(const MegaArgs& a, int t, int qh, int 
     if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[0]));
 }
 
-// Preparation of one (head, row) of the step, by one warp (phase A2): q heads
-// get RMSNorm + NEOX RoPE into qr; k heads RMSNorm + RoPE into the KV cache;
-// v heads are copied into the KV cache.  Lane `lane` holds elements lane + 32 q of the
-// head row (q = 0..3): quarter q's square sum is one butterfly, the quarters
-// are added in order (the tree of k_qk_norm_rope_store), and the RoPE pairs
-// (e, e + 64) are (lane, lane + 64) and (lane + 32, lane + 96).
-__device__ __noinline__ void prep_row(const MegaArgs& a, const LayerWeights& w, int l, int hh, int t, int before,
-                                      const float* s_rope) {
+// Per-head RMSNorm (the 128-thread tree of k_qk_norm_rope_store) and NEOX
+// RoPE of one q or k head row by one warp.  Lane `lane` holds elements
+// lane + 32 q of the row (q = 0..3): quarter q's square sum is one butterfly,
+// the quarters are added in order, and the RoPE pairs (e, e + 64) are
+// (lane, lane + 64) and (lane + 32, lane + 96); `rope` = the row's [64][cos, sin].
+__device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* __restrict__ wn, float eps,
+                                              const float* rope, float (&o)[4]) {
     const int lane = threadIdx.x & 31;
-    const int nh = a.d.n_heads, nkv = a.d.n_kv;
-    const int ldq = (nh + 2 * nkv) * kHeadDim;
-    const bool is_q = hh < nh, is_k = !is_q && hh < nh + nkv;
-    float x[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) x[q] = __ldcg(a.qkv + (size_t)t * ldq + (size_t)hh * kHeadDim + 32 * q + lane);
-    const int pos = before + t;
-    if (!is_q && !is_k) {
-        const long long off = kv_offset(a.kv, nkv, l, 1, hh - nh - nkv, pos);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) kv_store(a.kv, off + 32 * q + lane, x[q]);
-        return;
-    }
-    const float* wn = is_q ? w.q_norm : w.k_norm;
     double part[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) part[q] = warp_sum_d((double)(x[q] * x[q]));
     const double tot = part[0] + part[1] + part[2] + part[3];
     const float mean = (float)(tot * (1.0 / kHeadDim));  // exact: 128 is a power of two
-    const float scale = 1.0f / sqrtf(mean + a.d.eps);
-    float y[4], o[4];
+    const float scale = 1.0f / sqrtf(mean + eps);
+    float y[4];
 #pragma unroll
     for (int q = 0; q < 4; ++q) y[q] = __fmul_rn(__fmul_rn(x[q], scale), wn[32 * q + lane]);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
         const int e = 32 * q + lane;
-        const float cs = s_rope[(t * 64 + e) * 2], sn = s_rope[(t * 64 + e) * 2 + 1];
+        const float cs = rope[e * 2], sn = rope[e * 2 + 1];
         o[q] = __fsub_rn(__fmul_rn(y[q], cs), __fmul_rn(y[q + 2], sn));
         o[q + 2] = __fadd_rn(__fmul_rn(y[q], sn), __fmul_rn(y[q + 2], cs));
-    }
-    if (is_q) {
-        float* dst = a.qr + ((size_t)t * nh + hh) * kHeadDim;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) dst[32 * q + lane] = o[q];
-    } else {
-        const long long off = kv_offset(a.kv, nkv, l, 0, hh - nh, pos);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) kv_store(a.kv, off + 32 * q + lane, o[q]);
     }
 }
 
@@ -847,43 +822,66 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 
 // Returns false when a slot wait gave up.
 template <bool F16>
-__device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region, int l,
-                                       int chunk, int h, long long q0, int T, int before, int wl, int wpi, int bar,
-                                       int mark_pid, int mark_k) {
+__device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
+                                       const float* rope, int l, int chunk, int h, long long q0, int T, int before,
+                                       int wl, int wpi, int bar, int mark_pid, int mark_k) {
     using KS = KvSlots<F16>;
     const int nh = a.d.n_heads, nkv = a.d.n_kv, G = nh / nkv;
-    const int lane = threadIdx.x & 31, it = wl * 32 + lane, nthr = wpi * 32;
+    const int lane = threadIdx.x & 31, nthr = wpi * 32;
     const int kv_len = before + T, NQ = T * G;
     const int p0 = chunk * kPage, n_pos = min(kPage, kv_len - p0);
     float* sq = reinterpret_cast<float*>(region);                         // [32][128] query rows
     float2* sw = reinterpret_cast<float2*>(region + 32 * kHeadDim * 4);   // [32][64] exp weights, doubled
-    for (int i = it; i < NQ * 32; i += nthr) {
-        const int r = i >> 5, c4 = i & 31;
-        const int t = r / G, jh = r % G;
-        reinterpret_cast<float4*>(sq + r * kHeadDim)[c4] =
-            __ldcg(reinterpret_cast<const float4*>(a.qr + ((size_t)t * nh + h * G + jh) * kHeadDim) + c4);
+    const LayerWeights& w = a.layers[l];
+    const int ldq = (nh + 2 * nkv) * kHeadDim;
+    const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // query rows of this warp
+    // This warp's query rows: RMSNorm + RoPE of the raw projections (the
+    // same rows in every chunk item of the head; cheaper than a phase).
+    for (int rr = 0; rr < R; ++rr) {
+        const int r = wl + wpi * rr, t = r / G, jh = r % G;
+        const float* src = a.qkv + (size_t)t * ldq + (size_t)(h * G + jh) * kHeadDim;
+        float x[4], o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) x[q] = __ldcg(src + 32 * q + lane);
+        norm_rope_row(x, w.q_norm, a.d.eps, rope + t * 64 * 2, o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) sq[r * kHeadDim + 32 * q + lane] = o[q];
     }
     const bool ok = slots_wait(full, q0, 2 * KS::kSlotsPerHalf, a.abort_flag);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k);
-    // The step's own rows were stored to the cache in phase A2, possibly after
-    // the producer copied the page: take them from the cache again.
+    // The step's own positions in this chunk: k (RMSNorm + RoPE) and v rows
+    // from the raw projections into the ring rows and the KV cache (the
+    // producer's copy of those rows predates them).  One row per warp.
     {
-        constexpr int U = KS::kRowBytes / 16;  // 16-byte units per row
         const int r_lo = max(before - p0, 0), nr = max(n_pos - r_lo, 0);
-        const size_t esz = F16 ? 2 : 4;
-        for (int i = it; i < 2 * nr * U; i += nthr) {
-            const int which = i / (nr * U), rem = i % (nr * U);
-            const int r = r_lo + rem / U, u = rem % U;
+        for (int i = wl; i < 2 * nr; i += wpi) {
+            const int which = i / nr, r = r_lo + i % nr, t = p0 + r - before;
+            const float* src = a.qkv + (size_t)t * ldq + (size_t)(nh + which * nkv + h) * kHeadDim;
+            float x[4], o[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) x[q] = __ldcg(src + 32 * q + lane);
+            if (which == 0) {
+                norm_rope_row(x, w.k_norm, a.d.eps, rope + t * 64 * 2, o);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) o[q] = x[q];
+            }
             const long long off = kv_offset(a.kv, nkv, l, which, h, p0 + r);
-            const uint4 v = __ldcg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.kv.base) + off * esz) + u);
-            *reinterpret_cast<uint4*>(kv_row<F16>(ring, q0, which, r) + u * 16) = v;
+            uint8_t* row = kv_row<F16>(ring, q0, which, r);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                kv_store(a.kv, off + 32 * q + lane, o[q]);
+                if constexpr (F16)
+                    reinterpret_cast<__half*>(row)[32 * q + lane] = __float2half_rn(o[q]);
+                else
+                    reinterpret_cast<float*>(row)[32 * q + lane] = o[q];
+            }
         }
         // Order these generic-proxy stores before the producer's next bulk copies into the slots.
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     item_sync(bar, nthr);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 1);
-    const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // rows of this warp
     const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4);
     if (R == 1)
         attn_rows<F16, 1>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
@@ -996,15 +994,6 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
                         });
 }
 
-// A2: per-(head, row) RMSNorm + RoPE, KV append (warps numbered across CTAs).
-__device__ __noinline__ void phase_prep(const KCtx& c, int l) {
-    const MegaArgs& a = c.a;
-    const int warp = threadIdx.x >> 5;
-    const int n_tasks = (a.d.n_heads + 2 * a.d.n_kv) * c.T;
-    for (int task = blockIdx.x + gridDim.x * warp; task < n_tasks; task += gridDim.x * kConsumerWarps)
-        prep_row(a, a.layers[l], l, task / c.T, task % c.T, c.before, c.rope);
-}
-
 // B: attention items of this CTA in stream order, two at a time (four warps
 // each, named barriers 2 and 3) while two are left, else one over all eight.
 __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, int pid) {
@@ -1020,10 +1009,10 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
         uint8_t* region = c.region + sub * kAttnRegion;
         const int mp = j == 0 && sub == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
-                              ? attn_item<true>(a, c.ring, c.full, region, l, chunk, h, q0, c.T, c.before, wl, wpi,
-                                                2 + sub, mp, mk)
-                              : attn_item<false>(a, c.ring, c.full, region, l, chunk, h, q0, c.T, c.before, wl, wpi,
-                                                 2 + sub, mp, mk);
+                              ? attn_item<true>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.T, c.before,
+                                                wl, wpi, 2 + sub, mp, mk)
+                              : attn_item<false>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.T, c.before,
+                                                 wl, wpi, 2 + sub, mp, mk);
         ok = ok && good;
         consumer_sync();
         if (threadIdx.x < n_now * pi.slots) mbar_arrive(&c.empty[(pi.slot0 + (long long)j * pi.slots + threadIdx.x) % kRingSlots]);
@@ -1218,8 +1207,6 @@ __device__ __noinline__ void run_phases(const KCtx& c) {
     for (int l = 0; l < c.a.d.n_layers; ++l) {
         if (!phase_qkv<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
-        phase_prep(c, l);
-        if (!end_phase(c, &target)) return;
         if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
         phase_combine(c);
@@ -1364,7 +1351,6 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     a.bar = mb.bar;
     a.tickets = mb.tickets;
     a.head_tickets = mb.head_tickets;
-    a.qr = mb.qr;
     a.abort_flag = mb.abort_flag;
     cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, tickets, abort flag
     if (e != cudaSuccess) return e;
