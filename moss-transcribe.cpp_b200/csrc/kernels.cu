@@ -366,7 +366,7 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
 // ------------------------------------------------------------ attention
 
 // Split-KV causal GQA attention, one CTA per (64-position chunk, kv head):
-// scores q.k * 1/sqrt(128), query row t sees positions < before + t + 1
+// scores q.k * 1/sqrt(128) (q.k = even-dim fmaf chain + odd-dim fmaf chain), query row t sees positions < before + t + 1
 // (src/qwen3_decoder.cpp:142-148), chunk-local max / exp-sum / P.V partials.
 __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, const float* __restrict__ qkv, int n_heads,
                                                          int n_kv, KvCache kv, int layer, float* part_o,
@@ -408,10 +408,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
         if (p < n_pos && pos < before + t + 1) {
             const float* qa = sq + q * kHeadDim;
             const float* ka = sk + p * (kHeadDim + 1);
-            float acc = 0.f;
+            float ae = 0.f, ao = 0.f;  // even and odd dims, then their sum
 #pragma unroll 8
-            for (int d = 0; d < kHeadDim; ++d) acc = fmaf(qa[d], ka[d], acc);
-            s = acc * scale;
+            for (int d = 0; d < kHeadDim; d += 2) {
+                ae = fmaf(qa[d], ka[d], ae);
+                ao = fmaf(qa[d + 1], ka[d + 1], ao);
+            }
+            s = (ae + ao) * scale;
         }
         sp[q * kPage + p] = s;
     }

@@ -679,7 +679,8 @@ __device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* 
 // and V rows already in ring slots q0.. (streamed by the producer).  The
 // item's warp wl owns the query rows wl, wl + wpi, ... of the head's G query
 // heads (row = t * G + j): lane `lane` holds positions lane and lane + 32, so
-// each score is one sequential fmaf chain over the 128 dims, the chunk softmax
+// each score is two sequential fmaf chains (even and odd dims, one __ffma2_rn
+// per dim pair) added, the chunk softmax
 // is the warp butterfly (max, then e = exp(s - m) and the pair/butterfly
 // sum), and each P.V output (lane's dims 4 lane .. 4 lane + 3) is one
 // sequential fmaf chain over the chunk's positions; the order of
@@ -699,16 +700,17 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
     using KS = KvSlots<F16>;
     const int lane = threadIdx.x & 31;
     const float attn_scale = 1.0f / sqrtf((float)kHeadDim);
-    float acc[R][2];
+    // acc[rr][u] = {even-dim chain, odd-dim chain} of row rr, position lane + 32 u.
+    float2 acc[R][2];
 #pragma unroll
-    for (int rr = 0; rr < R; ++rr) acc[rr][0] = acc[rr][1] = 0.f;
+    for (int rr = 0; rr < R; ++rr) acc[rr][0] = acc[rr][1] = make_float2(0.f, 0.f);
     {
         const uint8_t* k0 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane);
         const uint8_t* k1 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane + 32);
         constexpr int EB = F16 ? 8 : 4;  // dims per 16-byte read
 #pragma unroll 1
         for (int eb = 0; eb < kHeadDim / EB; ++eb) {
-            float fa[EB], fb[EB];
+            float2 ka[EB / 2], kb[EB / 2];
             const uint4 ua = *reinterpret_cast<const uint4*>(k0 + eb * 16);
             const uint4 ub = *reinterpret_cast<const uint4*>(k1 + eb * 16);
             if constexpr (F16) {
@@ -716,29 +718,29 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
                 const __half2* hb = reinterpret_cast<const __half2*>(&ub);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const float2 x = __half22float2(ha[i]), y = __half22float2(hb[i]);
-                    fa[2 * i] = x.x; fa[2 * i + 1] = x.y;
-                    fb[2 * i] = y.x; fb[2 * i + 1] = y.y;
+                    ka[i] = __half22float2(ha[i]);
+                    kb[i] = __half22float2(hb[i]);
                 }
             } else {
-                fa[0] = __uint_as_float(ua.x); fa[1] = __uint_as_float(ua.y);
-                fa[2] = __uint_as_float(ua.z); fa[3] = __uint_as_float(ua.w);
-                fb[0] = __uint_as_float(ub.x); fb[1] = __uint_as_float(ub.y);
-                fb[2] = __uint_as_float(ub.z); fb[3] = __uint_as_float(ub.w);
+                ka[0] = make_float2(__uint_as_float(ua.x), __uint_as_float(ua.y));
+                ka[1] = make_float2(__uint_as_float(ua.z), __uint_as_float(ua.w));
+                kb[0] = make_float2(__uint_as_float(ub.x), __uint_as_float(ub.y));
+                kb[1] = make_float2(__uint_as_float(ub.z), __uint_as_float(ub.w));
             }
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) {
                 const float* qrow = sq + (wl + wpi * rr) * kHeadDim + eb * EB;
-                float qv[EB];
+                float2 qv[EB / 2];
 #pragma unroll
                 for (int i = 0; i < EB; i += 4) {
                     const float4 q4 = *reinterpret_cast<const float4*>(qrow + i);
-                    qv[i] = q4.x; qv[i + 1] = q4.y; qv[i + 2] = q4.z; qv[i + 3] = q4.w;
+                    qv[i / 2] = make_float2(q4.x, q4.y);
+                    qv[i / 2 + 1] = make_float2(q4.z, q4.w);
                 }
 #pragma unroll
-                for (int i = 0; i < EB; ++i) {
-                    acc[rr][0] = fmaf(qv[i], fa[i], acc[rr][0]);
-                    acc[rr][1] = fmaf(qv[i], fb[i], acc[rr][1]);
+                for (int i = 0; i < EB / 2; ++i) {
+                    acc[rr][0] = __ffma2_rn(qv[i], ka[i], acc[rr][0]);
+                    acc[rr][1] = __ffma2_rn(qv[i], kb[i], acc[rr][1]);
                 }
             }
         }
@@ -748,8 +750,8 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
         const int r = wl + wpi * rr, t = r / G;
         const bool ok0 = lane < n_pos && p0 + lane < before + t + 1;
         const bool ok1 = lane + 32 < n_pos && p0 + lane + 32 < before + t + 1;
-        const float s0 = ok0 ? acc[rr][0] * attn_scale : -INFINITY;
-        const float s1 = ok1 ? acc[rr][1] * attn_scale : -INFINITY;
+        const float s0 = ok0 ? __fmul_rn(__fadd_rn(acc[rr][0].x, acc[rr][0].y), attn_scale) : -INFINITY;
+        const float s1 = ok1 ? __fmul_rn(__fadd_rn(acc[rr][1].x, acc[rr][1].y), attn_scale) : -INFINITY;
         const float m = warp_max(fmaxf(s0, s1));
         const float x0 = exact_expf(s0 - m), x1 = exact_expf(s1 - m);
         const float e0 = s0 == -INFINITY ? 0.f : x0;

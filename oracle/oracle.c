@@ -493,7 +493,8 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         /* GQA attention with a causal mask when T > 1 (src/qwen3.cpp:158-189,
          * src/qwen3_decoder.cpp:142-148): query row t sees positions
          * [0, past + t], context over that valid length only
-         * (src/cpu_context.cpp:13-33).  softmax(s * 1/sqrt(hd)) is evaluated
+         * (src/cpu_context.cpp:13-33).  Each score q.k is two sequential fmaf
+         * chains (even and odd dims) added.  softmax(s * 1/sqrt(hd)) is evaluated
          * per 64-position chunk (chunk max m_c, e = exp(s - m_c), chunk sum l_c
          * and context o_c) and the chunks are merged with weights
          * exp(m_c - M); the same function as one softmax over the row, in the
@@ -516,9 +517,13 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
                         sc[p] = -INFINITY;
                         if (j < valid) {
                             const float* kj = d->k + kv_index(d, l, j) + (size_t)kvh * hd;
-                            float acc = 0.0f;
-                            for (int e2 = 0; e2 < hd; ++e2) acc = fmaf(qh[e2], kj[e2], acc);
-                            sc[p] = acc * scale;
+                            /* two fmaf chains, even and odd dims, then their sum */
+                            float ae = 0.0f, ao = 0.0f;
+                            for (int e2 = 0; e2 < hd; e2 += 2) {
+                                ae = fmaf(qh[e2], kj[e2], ae);
+                                ao = fmaf(qh[e2 + 1], kj[e2 + 1], ao);
+                            }
+                            sc[p] = (ae + ao) * scale;
                         }
                         mx = fmaxf(mx, sc[p]);
                     }
