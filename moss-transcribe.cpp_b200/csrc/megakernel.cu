@@ -822,9 +822,10 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
     }
 }
 
-// Returns false when a slot wait gave up.
-template <bool F16>
-__device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
+// The item with RP >= this warp's query rows (a power of two).  Returns false
+// when a slot wait gave up.
+template <bool F16, int RP>
+__device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
                                        const float* rope, int l, int chunk, int h, long long q0, int T, int before,
                                        int wl, int wpi, int bar, int mark_pid, int mark_k) {
     using KS = KvSlots<F16>;
@@ -838,16 +839,27 @@ __device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_
     const int ldq = (nh + 2 * nkv) * kHeadDim;
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // query rows of this warp
     // This warp's query rows: RMSNorm + RoPE of the raw projections (the
-    // same rows in every chunk item of the head; cheaper than a phase).
-    for (int rr = 0; rr < R; ++rr) {
-        const int r = wl + wpi * rr, t = r / G, jh = r % G;
-        const float* src = a.qkv + (size_t)t * ldq + (size_t)(h * G + jh) * kHeadDim;
-        float x[4], o[4];
+    // same rows in every chunk item of the head; cheaper than a phase).  All
+    // rows' loads are issued first.
+    {
+        float x[RP][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) x[q] = __ldcg(src + 32 * q + lane);
-        norm_rope_row(x, w.q_norm, a.d.eps, rope + t * 64 * 2, o);
+        for (int rr = 0; rr < RP; ++rr) {
+            const int r = wl + wpi * rr, t = r / G, jh = r % G;
+            const float* src = a.qkv + (size_t)t * ldq + (size_t)(h * G + jh) * kHeadDim;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) sq[r * kHeadDim + 32 * q + lane] = o[q];
+            for (int q = 0; q < 4; ++q) x[rr][q] = rr < R ? __ldcg(src + 32 * q + lane) : 0.f;
+        }
+#pragma unroll
+        for (int rr = 0; rr < RP; ++rr) {
+            if (rr < R) {
+                const int r = wl + wpi * rr, t = r / G;
+                float o[4];
+                norm_rope_row(x[rr], w.q_norm, a.d.eps, rope + t * 64 * 2, o);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) sq[r * kHeadDim + 32 * q + lane] = o[q];
+            }
+        }
     }
     const bool ok = slots_wait(full, q0, 2 * KS::kSlotsPerHalf, a.abort_flag);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k);
@@ -885,16 +897,21 @@ __device__ __noinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_
     item_sync(bar, nthr);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 1);
     const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4);
-    if (R == 1)
-        attn_rows<F16, 1>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
-    else if (R == 2)
-        attn_rows<F16, 2>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
-    else if (R > 2 && R <= 4)
-        attn_rows<F16, 4>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
-    else if (R > 4)
-        attn_rows<F16, 8>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    if (R > 0) attn_rows<F16, RP>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 2);
     return ok;
+}
+
+template <bool F16>
+__device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
+                                          const float* rope, int l, int chunk, int h, long long q0, int T, int before,
+                                          int wl, int wpi, int bar, int mark_pid, int mark_k) {
+    const int NQ = T * (a.d.n_heads / a.d.n_kv);
+    const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
+    if (R <= 1) return attn_body<F16, 1>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
+    if (R == 2) return attn_body<F16, 2>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
+    if (R <= 4) return attn_body<F16, 4>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
+    return attn_body<F16, 8>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -1032,24 +1049,42 @@ __device__ __noinline__ void phase_combine(const KCtx& c) {
         combine_task(c.a, it / (nh * 4), (it / 4) % nh, it % 4, c.n_chunks);
 }
 
-// D: O projection + residual.  F: down projection + residual.
+// D: O projection + residual.  F: down projection + residual.  The residual
+// values of the warp's first item are read before the weight work, so the
+// epilogue does not wait for them.
 template <bool kLow>
 __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* cur, int pid, bool down) {
     const MegaArgs& a = c.a;
     const int K = down ? a.d.ffn : a.d.n_heads * kHeadDim, H = a.d.hidden, T = c.T;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
+    float xr[4] = {0.f, 0.f, 0.f, 0.f};
+    if (warp < pi.count) {
+        const int item = pi.first + warp * gridDim.x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int row = g + (k >> 1) * 8;
+            if (row < T) xr[k] = __ldcg(a.x + (size_t)row * H + item * kTileRows + 2 * t + (k & 1));
+        }
+    }
     uint8_t* act_q = c.region;
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
     load_act_smem(down ? a.act2_q : a.act_q, down ? a.act2_d : a.act_d, K, act_q, act_d);
     mark(a.timeline, pid, 0);
-    const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     return weight_phase<kLow>(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
-                            for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
-                                float* o = a.x + (size_t)row * H + item * kTileRows + col;
-                                *o = __ldcg(o) + v;
-                            });
+                            const float4 y = sum_slices(part, K / kTileK / 4);
+                            const float yy[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                const int row = g + (k >> 1) * 8;
+                                if (row < T) {
+                                    float* o = a.x + (size_t)row * H + item * kTileRows + 2 * t + (k & 1);
+                                    *o = (j == warp ? xr[k] : __ldcg(o)) + yy[k];
+                                }
+                            }
                         });
 }
 
