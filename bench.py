@@ -47,6 +47,9 @@ WEIGHT_BYTES = 633_233_408
 NORM_BYTES = 262_144
 KV_BYTES_PER_POS = 114_688
 EMBED_BYTES_PER_ROW = 1_088
+# DRAM bytes (read + write) of one k_verify_persistent launch at this workload,
+# from the ncu capture summarised in profiles/k_verify_persistent_kv2048_t8_full.md.
+TRAFFIC_BYTES = 882_363_648
 
 
 def step_bytes(kv_len: int, T: int) -> int:
@@ -265,9 +268,12 @@ def main():
     peak, peak_kind = measured_peaks()
     bytes_step = step_bytes(KV_LEN, T_ROWS)
     achieved = bytes_step / (ms_step / 1e3) / 1e9
-    roofline = {"bound": "hbm", "kernel": "verify step (one CUDA graph)", "achieved": round(achieved, 1),
+    kernel = ("k_verify_persistent (the whole verify step, one launch)" if model.persistent_grid > 0
+              else "verify step (one CUDA graph of kernels)")
+    roofline = {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1),
                 "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                "algorithmic_bytes": bytes_step, "traffic": None}
+                "algorithmic_bytes": bytes_step,
+                "traffic": TRAFFIC_BYTES if model.persistent_grid > 0 else None}
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32 (fp16 KV)", "data": "synthetic", "config": config,

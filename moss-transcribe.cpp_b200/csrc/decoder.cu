@@ -269,9 +269,17 @@ cudaGraphExec_t step_graph(mtb_decoder* d, int mode, bool penalty) {
         launch_step(d->model->dm, d->kv, d->b, mode, penalty, d->stream);
     }
     if (cudaStreamEndCapture(d->stream, &graph) != cudaSuccess || !graph) return nullptr;
+    // Kernel launches per step: the graph's kernel nodes (memset nodes excluded).
     size_t n = 0;
     cudaGraphGetNodes(graph, nullptr, &n);
-    d->launches = int(n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (n) cudaGraphGetNodes(graph, nodes.data(), &n);
+    int kernels = 0;
+    for (size_t i = 0; i < n; ++i) {
+        cudaGraphNodeType type;
+        if (cudaGraphNodeGetType(nodes[i], &type) == cudaSuccess && type == cudaGraphNodeTypeKernel) ++kernels;
+    }
+    d->launches = kernels;
     if (cudaGraphInstantiate(&g, graph, 0) != cudaSuccess) g = nullptr;
     cudaGraphDestroy(graph);
     return g;
