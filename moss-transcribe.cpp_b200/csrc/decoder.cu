@@ -465,8 +465,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         auto& A = d->allocs;
         auto& E = d->error;
         uint8_t* zero_region = nullptr;
-        const size_t n_tickets = size_t(dm.n_layers) * (F / 32), n_head_tickets = size_t(dm.n_layers) * (dm.n_heads + 2 * dm.n_kv);
-        d->mb.zero_bytes = 16 + (n_tickets + n_head_tickets) * 4;
+        d->mb.zero_bytes = 16;
         if (dalloc(A, E, &d->mb.act2_q, size_t(F / 32) * 512) || dalloc(A, E, &d->mb.act2_d, size_t(F / 32) * 16 * 4) ||
             dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
@@ -474,9 +473,10 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         if (std::getenv("MTB_PROFILE") && dalloc(A, E, &d->mb.timeline, (6 * kMaxBarriers + 2 + 256 * kMaxBarriers * 17) * 8)) return bail();
         d->mb.bar = reinterpret_cast<unsigned*>(zero_region);
         d->mb.abort_flag = reinterpret_cast<int*>(zero_region + 4);
-        d->mb.tickets = reinterpret_cast<unsigned*>(zero_region + 16);
-        d->mb.head_tickets = d->mb.tickets + n_tickets;
-        if (dalloc(A, E, &d->mb.qr, size_t(kTMax) * dm.n_heads * kHeadDim * 4)) return bail();
+        // Failure-path test hook (documented in tests/test_gpu_wait_timeout.py): a
+        // barrier CTA 0 never arrives at, and a shorter wait bound.
+        if (const char* sb = std::getenv("MTB_TEST_STALL_BARRIER")) d->mb.stall_barrier = std::atoi(sb);
+        if (const char* wm = std::getenv("MTB_TEST_WAIT_MS")) d->mb.wait_ns = 1000000ull * std::max(1, std::atoi(wm));
         if (dalloc(A, E, &kvb, size_t(n_pages) * d->kv.page_elems * esz) || dalloc(A, E, &pages, size_t(n_pages) * 4) ||
             dalloc(A, E, &b.state, sizeof(StepState)) || dalloc(A, E, &b.ids, size_t(max_new) * 4) ||
             dalloc(A, E, &b.x, size_t(kTMax) * H * 4) || dalloc(A, E, &b.qkv, size_t(kTMax) * (qd + 2 * kd) * 4) ||

@@ -30,13 +30,14 @@ struct MegaBuffers {
     uint8_t* act2_q;     // SwiGLU fragments (K = ffn)
     float* act2_d;
     float2* lm_val;      // [grid][16] LM-head partials
-    unsigned* bar;       // zeroed before every launch, together with abort_flag and tickets
+    unsigned* bar;       // zeroed before every launch, together with abort_flag
     int* abort_flag;
-    unsigned* tickets;   // [n_layers][ffn / 32]
-    unsigned* head_tickets;  // [n_layers][n_heads + 2 n_kv]
-    float* qr;           // [16][n_heads][128] prepared q rows
     size_t zero_bytes;
-    unsigned long long* timeline;  // optional [2 * kMaxBarriers + 2] (MTB_PROFILE=1)
+    unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
+    // Bound on every grid-barrier wait, and a test hook: CTA 0 skips its
+    // arrival at this barrier (-1: never), so the others' waits run out.
+    unsigned long long wait_ns = 2000000000ull;
+    int stall_barrier = -1;
 };
 
 constexpr int kMaxBarriers = 512;

@@ -75,9 +75,9 @@ struct MegaArgs {
     int max_chunks;
     float2* lm_val;  // [grid][16]
     unsigned* bar;   // grid barrier counter, zero at launch
-    unsigned* tickets;  // [n_layers][ffn/32], zero at launch
-    unsigned* head_tickets;  // [n_layers][n_heads + 2 n_kv], zero at launch
     int* abort_flag;
+    unsigned long long wait_ns;  // bound on a grid-barrier wait
+    int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
     unsigned long long* timeline;  // optional: CTA 0's [barrier][arrive, release] in ns
 };
 
@@ -335,7 +335,8 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
         if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
         // Arrive with release semantics (the CTA's writes, ordered before by the
         // named barrier, become visible with it); poll relaxed; acquire once.
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
+        if (!(b == a.stall_barrier && blockIdx.x == 0))
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long t0 = global_ns();
         int status = 0;
         for (unsigned it = 0;; ++it) {
@@ -344,7 +345,7 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
             if (v >= target) break;
             if ((it & 31) == 31) {
                 if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
-                if (global_ns() - t0 > kWaitNs) {
+                if (global_ns() - t0 > a.wait_ns) {
                     atomicExch(a.abort_flag, 1);
                     a.state->error = 2;
                     status = 1;
@@ -1386,10 +1387,10 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     a.max_chunks = b.max_chunks;
     a.lm_val = mb.lm_val;
     a.bar = mb.bar;
-    a.tickets = mb.tickets;
-    a.head_tickets = mb.head_tickets;
     a.abort_flag = mb.abort_flag;
-    cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, tickets, abort flag
+    a.wait_ns = mb.wait_ns;
+    a.stall_barrier = mb.stall_barrier;
+    cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, abort flag
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
