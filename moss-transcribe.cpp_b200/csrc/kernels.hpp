@@ -30,8 +30,9 @@ struct MegaBuffers {
     uint8_t* act2_q;     // SwiGLU fragments (K = ffn)
     float* act2_d;
     float2* lm_val;      // [grid][16] LM-head partials
-    unsigned* bar;       // zeroed before every launch, together with abort_flag
+    unsigned* bar;       // zeroed before every launch, together with abort_flag and head_done
     int* abort_flag;
+    unsigned* head_done; // [n_layers][n_kv] finished attention items per kv head
     size_t zero_bytes;
     unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
     // Bound on every grid-barrier wait, and a test hook: CTA 0 skips its

@@ -75,6 +75,7 @@ struct MegaArgs {
     int max_chunks;
     float2* lm_val;  // [grid][16]
     unsigned* bar;   // grid barrier counter, zero at launch
+    unsigned* head_done;  // [n_layers][n_kv] finished attention items per kv head, zero at launch
     int* abort_flag;
     unsigned long long wait_ns;  // bound on a grid-barrier wait
     int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
@@ -600,9 +601,35 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
 // sequential fmaf chain), then that q8_0 block of the context row.  All of a
 // batch's loads (32 chunks) are issued together, the next batch's while the
 // current one is summed.
-__device__ __noinline__ void combine_task(const MegaArgs& a, int t, int qh, int k, int n_chunks) {
+__device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int qh, int k, int n_chunks) {
     const int lane = threadIdx.x & 31;
     const int G = a.d.n_heads / a.d.n_kv, h = qh / G, qi = t * G + qh % G;
+    // The head's chunk items are counted as they finish (release-add after
+    // their partials); lane 0 waits for all of them (acquire), bounded like a
+    // barrier, and the warp follows it.
+    {
+        int give_up = 0;
+        if (lane == 0) {
+            const unsigned* done = a.head_done + (size_t)l * a.d.n_kv + h;
+            const unsigned long long t0 = global_ns();
+            for (unsigned it = 0;; ++it) {
+                unsigned v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
+                if (v >= (unsigned)n_chunks) break;
+                if ((it & 15) == 15) {
+                    if (*reinterpret_cast<const volatile int*>(a.abort_flag)) { give_up = 1; break; }
+                    if (global_ns() - t0 > a.wait_ns) {
+                        atomicExch(a.abort_flag, 1);
+                        a.state->error = 2;
+                        give_up = 1;
+                        break;
+                    }
+                }
+            }
+        }
+        if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+        __syncwarp();
+    }
     const size_t base = (size_t)h * a.max_chunks * (kTMax * 4) + qi;  // (h, chunk 0, qi)
     const float* po = a.part_o + base * kHeadDim + 32 * k + lane;
     constexpr size_t kStrideO = (size_t)kTMax * 4 * kHeadDim;         // one chunk further
@@ -647,6 +674,7 @@ __device__ __noinline__ void combine_task(const MegaArgs& a, int t, int qh, int 
     const int blk = qh * 4 + k;
     a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o, iq[0]));
     if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[0]));
+    return true;
 }
 
 // Per-head RMSNorm (the 128-thread tree of k_qk_norm_rope_store) and NEOX
@@ -1036,18 +1064,27 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
         ok = ok && good;
         consumer_sync();
         if (threadIdx.x < n_now * pi.slots) mbar_arrive(&c.empty[(pi.slot0 + (long long)j * pi.slots + threadIdx.x) % kRingSlots]);
+        if (threadIdx.x < n_now) {
+            // The items' partials are written (named barrier above): count them
+            // for their heads' merges (release: cumulative over the CTA's stores).
+            const int hh = (pi.first + (j + threadIdx.x) * gridDim.x) % nkv;
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.head_done + (size_t)l * nkv + hh) : "memory");
+        }
         mark(a.timeline, mp, mk + 3);
     }
     return ok;
 }
 
 // C: chunk merge + quantise, one (row, q head, block) per warp, warps
-// numbered across CTAs.
-__device__ __noinline__ void phase_combine(const KCtx& c) {
+// numbered across CTAs; no grid barrier before it: each task waits for its
+// head's attention items only (they finish at different times).
+__device__ __noinline__ bool phase_combine(const KCtx& c, int l) {
     const int nh = c.a.d.n_heads, warp = threadIdx.x >> 5;
     const int n_tasks = c.T * nh * 4;
-    for (int it = blockIdx.x + gridDim.x * warp; it < n_tasks; it += gridDim.x * kConsumerWarps)
-        combine_task(c.a, it / (nh * 4), (it / 4) % nh, it % 4, c.n_chunks);
+    bool ok = true;
+    for (int it = blockIdx.x + gridDim.x * warp; it < n_tasks && ok; it += gridDim.x * kConsumerWarps)
+        ok = combine_task(c.a, l, it / (nh * 4), (it / 4) % nh, it % 4, c.n_chunks);
+    return ok;
 }
 
 // D: O projection + residual.  F: down projection + residual.  The residual
@@ -1246,8 +1283,7 @@ __device__ __noinline__ void run_phases(const KCtx& c) {
         if (!phase_qkv<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
         if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        phase_combine(c);
+        if (!phase_combine(c, l)) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
         if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), false)) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
@@ -1388,9 +1424,10 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     a.lm_val = mb.lm_val;
     a.bar = mb.bar;
     a.abort_flag = mb.abort_flag;
+    a.head_done = mb.head_done;
     a.wait_ns = mb.wait_ns;
     a.stall_barrier = mb.stall_barrier;
-    cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, abort flag
+    cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, abort flag, head counts
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
