@@ -12,6 +12,7 @@
 #include "../../include/mtb_decoder.h"
 #include "gguf.hpp"
 #include "kernels.hpp"
+#include "prefill_tc.hpp"
 
 #include <algorithm>
 #include <cmath>
@@ -52,6 +53,7 @@ struct mtb_decoder {
     KvCache kv{};
     StepBuffers b{};
     MegaBuffers mb{};
+    PrefillBuffers pf{};
     StepState* h_state = nullptr;  // pinned mirror
     float* h_rows = nullptr;       // pinned staging [kTMax][hidden]
     int32_t* h_ids = nullptr;      // pinned [max_new]
@@ -123,7 +125,7 @@ int fail(std::string& err, const std::string& msg) {
 // Upload one q8_0 matrix (ne = [k, n]) through `staging` and repack it into
 // tiles at destination row groups r * stride + offset.
 int upload_q8(mtb_model* m, const GgufFile& f, const std::string& name, int64_t k, int64_t n, uint8_t* staging,
-              uint8_t* dst, int stride, int offset) {
+              uint8_t* dst, int stride, int offset, uint8_t* pf_dst = nullptr, int pf_half = -1) {
     const GgufTensor* t = f.tensor(name);
     if (!t) return fail(m->error, "missing tensor " + name);
     if (t->type != GGML_Q8_0)
@@ -132,6 +134,7 @@ int upload_q8(mtb_model* m, const GgufFile& f, const std::string& name, int64_t 
         return fail(m->error, name + ": unexpected shape");
     MTB_CK(m, cudaMemcpy(staging, t->data, t->nbytes, cudaMemcpyHostToDevice));
     launch_repack_q8(staging, int(n), int(k), dst, stride, offset, nullptr);
+    if (pf_dst) pf_repack(staging, int(n), int(k), pf_half, pf_dst, nullptr);  // the prefill copy
     MTB_CK(m, cudaGetLastError());
     MTB_CK(m, cudaDeviceSynchronize());
     return 0;
@@ -199,23 +202,36 @@ int load_model(mtb_model* m, const char* path) {
         const std::string p = "qwen3.blk." + std::to_string(l) + ".";
         LayerWeights& w = m->layers[size_t(l)];
         uint8_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+        uint8_t *pqkv = nullptr, *po = nullptr, *pgu = nullptr, *pdown = nullptr;
         if (dalloc(m->allocs, m->error, &qkv, tiles_bytes(qd + 2 * kd, H)) ||
             dalloc(m->allocs, m->error, &o, tiles_bytes(H, qd)) ||
             dalloc(m->allocs, m->error, &gu, tiles_bytes(2 * F, H)) ||
-            dalloc(m->allocs, m->error, &down, tiles_bytes(H, F)))
+            dalloc(m->allocs, m->error, &down, tiles_bytes(H, F)) ||
+            dalloc(m->allocs, m->error, &pqkv, pf_weight_bytes(int(qd + 2 * kd), int(H))) ||
+            dalloc(m->allocs, m->error, &po, pf_weight_bytes(int(H), int(qd))) ||
+            dalloc(m->allocs, m->error, &pgu, pf_weight_bytes(int(2 * F), int(H))) ||
+            dalloc(m->allocs, m->error, &pdown, pf_weight_bytes(int(H), int(F))))
             return -1;
-        if (upload_q8(m, f, p + "attn_q.weight", H, qd, staging, qkv, 1, 0) ||
-            upload_q8(m, f, p + "attn_k.weight", H, kd, staging, qkv, 1, int(qd / kTileRows)) ||
-            upload_q8(m, f, p + "attn_v.weight", H, kd, staging, qkv, 1, int((qd + kd) / kTileRows)) ||
-            upload_q8(m, f, p + "attn_o.weight", qd, H, staging, o, 1, 0) ||
-            upload_q8(m, f, p + "ffn_gate.weight", H, F, staging, gu, 2, 0) ||
-            upload_q8(m, f, p + "ffn_up.weight", H, F, staging, gu, 2, 1) ||
-            upload_q8(m, f, p + "ffn_down.weight", F, H, staging, down, 1, 0))
+        // Prefill steps of q, k, v: whole 128-row tiles in that order.
+        const size_t pf_rows_bytes = pf_weight_bytes(128, int(H));
+        if (upload_q8(m, f, p + "attn_q.weight", H, qd, staging, qkv, 1, 0, pqkv) ||
+            upload_q8(m, f, p + "attn_k.weight", H, kd, staging, qkv, 1, int(qd / kTileRows),
+                      pqkv + size_t(qd / 128) * pf_rows_bytes) ||
+            upload_q8(m, f, p + "attn_v.weight", H, kd, staging, qkv, 1, int((qd + kd) / kTileRows),
+                      pqkv + size_t((qd + kd) / 128) * pf_rows_bytes) ||
+            upload_q8(m, f, p + "attn_o.weight", qd, H, staging, o, 1, 0, po) ||
+            upload_q8(m, f, p + "ffn_gate.weight", H, F, staging, gu, 2, 0, pgu, 0) ||
+            upload_q8(m, f, p + "ffn_up.weight", H, F, staging, gu, 2, 1, pgu, 1) ||
+            upload_q8(m, f, p + "ffn_down.weight", F, H, staging, down, 1, 0, pdown))
             return -1;
         w.qkv = qkv;
         w.o = o;
         w.gu = gu;
         w.down = down;
+        w.pf_qkv = pqkv;
+        w.pf_o = po;
+        w.pf_gu = pgu;
+        w.pf_down = pdown;
         if (upload_f32(m, f, p + "attn_norm.weight", H, &w.attn_norm) ||
             upload_f32(m, f, p + "attn_q_norm.weight", kHeadDim, &w.q_norm) ||
             upload_f32(m, f, p + "attn_k_norm.weight", kHeadDim, &w.k_norm) ||
@@ -292,10 +308,58 @@ int run_step(mtb_decoder* d, int mode) {
     return 0;
 }
 
-// Rows [T][hidden] from the host at past..past+T-1 in chunks of kTMax.
+constexpr int kPrefillRows = 512;                  // rows per prefill pass at most
+constexpr size_t kPrefillPartRows = size_t(1) << 19;  // attention partial entries (512 B each) per pass at most
+
+// Rows of the next prefill pass: at most `remaining` and kPrefillRows, a
+// multiple of 16, and few enough that the pass's attention partials fit.
+int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
+    const ModelDims& dm = d->model->dm.dims;
+    const int G = dm.n_heads / dm.n_kv;
+    int P = std::min(remaining, d->pf.max_rows);
+    P -= P % kTMax;
+    while (P > kTMax) {
+        const size_t need = size_t((P + kTMax - 1) / kTMax) * dm.n_kv * size_t((before + P + kPage - 1) / kPage) * (kTMax * G);
+        if (need <= d->pf.part_rows) break;
+        P -= kTMax;
+    }
+    return P;
+}
+
+// Rows [T][hidden] from the host at past..past+T-1: all but the last 1..16 in
+// prefill passes (every layer over up to 512 rows at once, tcgen05
+// projections), the last ones (and the LM head when asked) in steps of kTMax
+// through the verify kernels.  The host's past (h_state) is current on entry.
 int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last) {
     const int H = d->model->dm.dims.hidden;
-    for (int r0 = 0; r0 < T; r0 += kTMax) {
+    int done = 0;
+    if (d->pf.max_rows >= kTMax && T > kTMax) {
+        const int bulk = T - (T % kTMax ? T % kTMax : kTMax);
+        const int past = d->h_state->past;
+        while (done < bulk) {
+            const int P = prefill_pass_rows(d, bulk - done, past + done);
+            if (P < kTMax) return fail(d->error, "prefill pass does not fit its buffers");
+            d->h2d_bytes += (long long)P * H * 4;
+            MTB_CK(d, cudaMemcpyAsync(d->pf.x, rows + size_t(done) * H, size_t(P) * H * sizeof(float),
+                                      cudaMemcpyHostToDevice, d->stream));
+            launch_prefill_pass(d->model->dm, d->kv, d->pf, P, past + done, hidden_out != nullptr, d->stream);
+            launch_rows_begin(d->b, P, d->stream);
+            launch_rows_end(d->b, d->stream);
+            MTB_CK(d, cudaGetLastError());
+            if (hidden_out) {
+                d->d2h_bytes += (long long)P * H * 4;
+                MTB_CK(d, cudaMemcpyAsync(hidden_out + size_t(done) * H, d->pf.hid, size_t(P) * H * sizeof(float),
+                                          cudaMemcpyDeviceToHost, d->stream));
+            }
+            done += P;
+        }
+        int status = 0;
+        MTB_CK(d, cudaMemcpyAsync(&status, d->pf.status, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+        if (status) return fail(d->error, "prefill projection gave up waiting (tcgen05 pipeline timeout)");
+        d->h_state->past = past + done;
+    }
+    for (int r0 = done; r0 < T; r0 += kTMax) {
         const int n = std::min(kTMax, T - r0);
         std::memcpy(d->h_rows, rows + size_t(r0) * H, size_t(n) * H * sizeof(float));
         MTB_CK(d, cudaMemcpyAsync(d->b.x, d->h_rows, size_t(n) * H * sizeof(float), cudaMemcpyHostToDevice, d->stream));
@@ -491,6 +555,20 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
             dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
             return bail();
+        {
+            // Prefill pass buffers: up to kPrefillRows rows per pass.
+            PrefillBuffers& p = d->pf;
+            const int G = dm.n_heads / dm.n_kv;
+            p.max_rows = std::min(kPrefillRows, (max_seq + kTMax - 1) / kTMax * kTMax);
+            const size_t P = size_t(p.max_rows);
+            p.part_rows = std::min(kPrefillPartRows, size_t((P + kTMax - 1) / kTMax) * dm.n_kv * n_pages * kTMax * G);
+            if (dalloc(A, E, &p.x, P * H * 4) || dalloc(A, E, &p.qkv, P * (qd + 2 * kd) * 4) ||
+                dalloc(A, E, &p.attn, P * qd * 4) || dalloc(A, E, &p.gu, P * F * 4) || dalloc(A, E, &p.hid, P * H * 4) ||
+                dalloc(A, E, &p.xq, pf_act_bytes(int(P), kmax)) || dalloc(A, E, &p.xd, P * (kmax / 32) * 4) ||
+                dalloc(A, E, &p.part_o, p.part_rows * kHeadDim * 4) || dalloc(A, E, &p.part_ml, p.part_rows * sizeof(float2)) ||
+                dalloc(A, E, &p.status, 16))
+                return bail();
+        }
         d->kv.base = kvb;
         d->kv.pages = pages;
         std::vector<int32_t> ident(static_cast<size_t>(n_pages));

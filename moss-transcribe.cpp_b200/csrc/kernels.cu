@@ -12,6 +12,7 @@
 // integer block sums, fp32 d_w*d_x scaling) follows ggml's CPU mul_mat as used
 // by src/cpu_projection.cpp:16-37.
 #include "device_common.cuh"
+#include "prefill_tc.hpp"
 
 #include <cuda_fp16.h>
 #include <cfloat>
@@ -313,15 +314,17 @@ __global__ void __launch_bounds__(kThreads) k_quant_rows(const StepState* st, co
 
 // Per-head RMSNorm + NEOX RoPE of q and k (src/qwen3.cpp:104-118), then the
 // KV store of k and v at positions before+t (src/qwen3.cpp:123-140).
-// grid (kTMax, n_heads + n_kv), block 128.
+// grid (rows, n_heads + n_kv), block 128; T_arg < 0: T and before from the
+// step state, else the prefill pass's rows at positions before_arg + t.
 __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st, float* qkv, int n_heads, int n_kv,
                                                             const float* __restrict__ q_norm,
                                                             const float* __restrict__ k_norm, float eps,
-                                                            float theta_scale, KvCache kv, int layer) {
-    const int T = st->T;
+                                                            float theta_scale, KvCache kv, int layer, int T_arg,
+                                                            int before_arg) {
+    const int T = T_arg < 0 ? st->T : T_arg;
     const int row = blockIdx.x, hh = blockIdx.y;
     if (row >= T) return;
-    const int pos = st->before + row;
+    const int pos = (T_arg < 0 ? st->before : before_arg) + row;
     const int ld = (n_heads + 2 * n_kv) * kHeadDim;
     const bool is_q = hh < n_heads;
     float* src = qkv + (size_t)row * ld + (size_t)hh * kHeadDim;
@@ -368,18 +371,27 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
 // Split-KV causal GQA attention, one CTA per (64-position chunk, kv head):
 // scores q.k * 1/sqrt(128) (q.k = even-dim fmaf chain + odd-dim fmaf chain), query row t sees positions < before + t + 1
 // (src/qwen3_decoder.cpp:142-148), chunk-local max / exp-sum / P.V partials.
+// T_arg < 0: the step's rows (state); else a prefill pass of T_arg rows at
+// before_arg.., split into row blocks of 16 (blockIdx.z), each with its own
+// partial buffers (qstride rows per (head, chunk)).
 __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, const float* __restrict__ qkv, int n_heads,
                                                          int n_kv, KvCache kv, int layer, float* part_o,
-                                                         float2* part_ml, int max_chunks) {
-    const int T = st->T;
+                                                         float2* part_ml, int max_chunks, int T_arg, int before_arg,
+                                                         int qstride) {
+    const int rb = blockIdx.z;
+    const int T_all = T_arg < 0 ? st->T : T_arg;
+    const int T = min(kTMax, T_all - kTMax * rb);
     if (T <= 0) return;
-    const int before = st->before;
+    const int before = (T_arg < 0 ? st->before : before_arg) + kTMax * rb;
     const int kv_len = before + T;
     const int c = blockIdx.x, h = blockIdx.y;
     if (c * kPage >= kv_len) return;
     const int G = n_heads / n_kv;
     const int NQ = T * G;
     const int ld = (n_heads + 2 * n_kv) * kHeadDim;
+    qkv += (size_t)kTMax * rb * ld;
+    part_o += (size_t)rb * n_kv * max_chunks * qstride * kHeadDim;
+    part_ml += (size_t)rb * n_kv * max_chunks * qstride;
     extern __shared__ __align__(16) float sm[];
     float* sq = sm;                              // [NQ][128]
     float* sk = sq + kTMax * 4 * kHeadDim;       // [64][129]  (group <= 4)
@@ -427,7 +439,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
         const float l = warp_sum(e0 + e1);
         sp[q * kPage + lane] = e0;
         sp[q * kPage + lane + 32] = e1;
-        if (lane == 0) part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q] = make_float2(m, l);
+        if (lane == 0) part_ml[((size_t)h * max_chunks + c) * qstride + q] = make_float2(m, l);
     }
     __syncthreads();
     for (int i = tid; i < n_pos * kHeadDim; i += kThreads) {
@@ -440,32 +452,37 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
         const float* pr = sp + q * kPage;
         float acc = 0.f;
         for (int p = 0; p < n_pos; ++p) acc = fmaf(pr[p], sk[p * (kHeadDim + 1) + d], acc);
-        part_o[(((size_t)h * max_chunks + c) * (kTMax * 4) + q) * kHeadDim + d] = acc;
+        part_o[(((size_t)h * max_chunks + c) * qstride + q) * kHeadDim + d] = acc;
     }
 }
 
-// Merge the chunk partials of one (row, head): grid (kTMax, n_heads), block 128.
+// Merge the chunk partials of one (row, head): grid (rows, n_heads), block
+// 128; rows and partial buffers as in k_attn_chunk (row blocks of 16).
 __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n_heads, int n_kv,
                                                       const float* part_o, const float2* part_ml, int max_chunks,
-                                                      float* attn_out) {
-    const int T = st->T;
-    const int t = blockIdx.x, head = blockIdx.y;
-    if (t >= T) return;
+                                                      float* attn_out, int T_arg, int before_arg, int qstride) {
+    const int T_all = T_arg < 0 ? st->T : T_arg;
+    const int t_all = blockIdx.x, head = blockIdx.y;
+    if (t_all >= T_all) return;
+    const int rb = t_all / kTMax, t = t_all % kTMax;
+    const int T = min(kTMax, T_all - kTMax * rb);
     const int G = n_heads / n_kv;
     const int h = head / G, q = t * G + head % G;
-    const int kv_len = st->before + T;
+    const int kv_len = (T_arg < 0 ? st->before : before_arg) + kTMax * rb + T;
     const int n_chunks = (kv_len + kPage - 1) / kPage;
+    part_o += (size_t)rb * n_kv * max_chunks * qstride * kHeadDim;
+    part_ml += (size_t)rb * n_kv * max_chunks * qstride;
     float M = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q].x);
+    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, part_ml[((size_t)h * max_chunks + c) * qstride + q].x);
     float L = 0.f, o = 0.f;
     for (int c = 0; c < n_chunks; ++c) {
-        const float2 ml = part_ml[((size_t)h * max_chunks + c) * (kTMax * 4) + q];
+        const float2 ml = part_ml[((size_t)h * max_chunks + c) * qstride + q];
         if (ml.x == -INFINITY) continue;
         const float wgt = exact_expf(ml.x - M);
         L = fmaf(wgt, ml.y, L);
-        o = fmaf(wgt, part_o[(((size_t)h * max_chunks + c) * (kTMax * 4) + q) * kHeadDim + threadIdx.x], o);
+        o = fmaf(wgt, part_o[(((size_t)h * max_chunks + c) * qstride + q) * kHeadDim + threadIdx.x], o);
     }
-    attn_out[(size_t)t * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = o / L;
+    attn_out[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = o / L;
 }
 
 // ------------------------------------------------------------ embed, draft, accept
@@ -775,6 +792,7 @@ cudaError_t configure_kernels() {
     cudaFuncSetAttribute(k_gemv<EPI_SWIGLU, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_gemv<EPI_ARGMAX, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    pf_configure();
     return cudaGetLastError();
 }
 
@@ -793,11 +811,12 @@ static void forward_layers(const DeviceModel& m, const KvCache& kv, const StepBu
             gemv<EPI_STORE, 2>(a, (a.n_rg + 1) / 2, s);
         }
         k_qk_norm_rope_store<<<dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, w.q_norm,
-                                                                             w.k_norm, d.eps, m.theta_scale, kv, l);
+                                                                             w.k_norm, d.eps, m.theta_scale, kv, l, -1, 0);
         k_attn_chunk<<<dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, kv, l,
-                                                                              b.part_o, b.part_ml, b.max_chunks);
+                                                                              b.part_o, b.part_ml, b.max_chunks, -1, 0,
+                                                                              kTMax * 4);
         k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
-                                                              b.max_chunks, b.attn_out);
+                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4);
         k_quant_rows<<<(qd / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, b.attn_out, qd, b.act_q, b.act_d);
         {
             GemvArgs a{w.o, H / kTileRows, qd / kTileK, b.act_q, b.act_d, b.x, H, b.state, nullptr, nullptr};
@@ -816,6 +835,38 @@ static void forward_layers(const DeviceModel& m, const KvCache& kv, const StepBu
     }
     (void)G;
     k_rmsnorm_quant<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, b.act_q, b.act_d, b.hid);
+}
+
+// A prefill pass: the layer sequence of forward_layers over P rows at once,
+// the projections on tcgen05 (prefill_tc.cu), attention as row blocks of 16
+// through the same split-KV kernels (same arithmetic and order).
+void launch_prefill_pass(const DeviceModel& m, const KvCache& kv, const PrefillBuffers& p, int P, int before,
+                         bool want_hidden, cudaStream_t s) {
+    const ModelDims& d = m.dims;
+    const int H = d.hidden, F = d.ffn;
+    const int qd = d.n_heads * kHeadDim, kd = d.n_kv * kHeadDim;
+    const int G = d.n_heads / d.n_kv;
+    const int n_rb = (P + kTMax - 1) / kTMax, max_chunks = (before + P + kPage - 1) / kPage, qstride = kTMax * G;
+    const size_t attn_smem = (size_t)(kTMax * 4 * kHeadDim + kPage * (kHeadDim + 1) + kTMax * 4 * kPage) * sizeof(float);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const LayerWeights& w = m.layers[l];
+        pf_norm_quant(p.x, P, H, w.attn_norm, d.eps, p.xq, p.xd, nullptr, s);
+        pf_gemm(w.pf_qkv, qd + 2 * kd, H, p.xq, p.xd, P, p.qkv, qd + 2 * kd, PF_EPI_STORE, p.status, s);
+        k_qk_norm_rope_store<<<dim3(P, d.n_heads + d.n_kv), 128, 0, s>>>(nullptr, p.qkv, d.n_heads, d.n_kv, w.q_norm,
+                                                                         w.k_norm, d.eps, m.theta_scale, kv, l, P, before);
+        k_attn_chunk<<<dim3(max_chunks, d.n_kv, n_rb), kThreads, attn_smem, s>>>(nullptr, p.qkv, d.n_heads, d.n_kv, kv, l,
+                                                                                  p.part_o, p.part_ml, max_chunks, P,
+                                                                                  before, qstride);
+        k_attn_combine<<<dim3(P, d.n_heads), 128, 0, s>>>(nullptr, d.n_heads, d.n_kv, p.part_o, p.part_ml, max_chunks,
+                                                          p.attn, P, before, qstride);
+        pf_quant(p.attn, P, qd, p.xq, p.xd, s);
+        pf_gemm(w.pf_o, H, qd, p.xq, p.xd, P, p.x, H, PF_EPI_RESID, p.status, s);
+        pf_norm_quant(p.x, P, H, w.ffn_norm, d.eps, p.xq, p.xd, nullptr, s);
+        pf_gemm(w.pf_gu, 2 * F, H, p.xq, p.xd, P, p.gu, F, PF_EPI_SWIGLU, p.status, s);
+        pf_quant(p.gu, P, F, p.xq, p.xd, s);
+        pf_gemm(w.pf_down, H, F, p.xq, p.xd, P, p.x, H, PF_EPI_RESID, p.status, s);
+    }
+    if (want_hidden) pf_norm_quant(p.x, P, H, m.output_norm, d.eps, p.xq, p.xd, p.hid, s);
 }
 
 static void lm_head(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {

@@ -43,6 +43,23 @@ struct MegaBuffers {
 
 constexpr int kMaxBarriers = 512;
 
+// Buffers of a prefill pass (up to max_rows prompt rows through all layers at
+// once, projections on tcgen05).
+struct PrefillBuffers {
+    float* x = nullptr;     // [max_rows][hidden] residual rows
+    float* qkv = nullptr;   // [max_rows][(n_heads + 2 n_kv) * 128]
+    float* attn = nullptr;  // [max_rows][n_heads * 128]
+    float* gu = nullptr;    // [max_rows][ffn]
+    float* hid = nullptr;   // [max_rows][hidden] final-normed rows
+    uint8_t* xq = nullptr;  // activation steps of the widest K
+    float* xd = nullptr;    // [max_rows][K / 32]
+    float* part_o = nullptr;
+    float2* part_ml = nullptr;
+    size_t part_rows = 0;   // capacity of part_ml in (row block, kv head, chunk, query row) entries
+    int max_rows = 0;
+    int* status = nullptr;  // nonzero: a tcgen05 GEMM wait gave up
+};
+
 struct KvCache {
     void* base;              // pages of [n_layers][2][n_kv][kPage][128] elements
     const int32_t* pages;    // logical page -> physical page
@@ -71,6 +88,11 @@ void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, 
 
 // Embedding rows from host-provided float rows instead of token ids
 // (prefill and the run() test entry): copies `rows` into x.
+// One prefill pass: P rows in p.x at positions before .. before + P - 1
+// through every layer (tcgen05 projections); the final-normed rows into p.hid
+// when want_hidden.  The KV cache receives the P positions.
+void launch_prefill_pass(const DeviceModel& m, const KvCache& kv, const PrefillBuffers& p, int P, int before,
+                         bool want_hidden, cudaStream_t s);
 void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, bool lm_head,
                          bool want_logits, cudaStream_t s);
 

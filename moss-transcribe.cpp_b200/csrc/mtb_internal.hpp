@@ -45,6 +45,8 @@ struct LayerWeights {
     const uint8_t* gu;     // tiles, row groups interleaved gate/up
     const uint8_t* down;   // tiles, rows: hidden, K = ffn
     const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
+    // The same matrices as prefill weight steps (tcgen05 operand layout, prefill_tc.cu).
+    const uint8_t *pf_qkv, *pf_o, *pf_gu, *pf_down;
 };
 
 struct ModelDims {
