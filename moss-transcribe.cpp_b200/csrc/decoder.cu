@@ -194,8 +194,17 @@ int load_model(mtb_model* m, const char* path) {
 
     uint8_t* embd = nullptr;
     if (dalloc(m->allocs, m->error, &embd, tiles_bytes(d.vocab, H))) return -1;
-    if (upload_q8(m, f, "token_embd.weight", H, d.vocab, staging, embd, 1, 0)) return -1;
+    // MTB_LM_TCGEN05=1: the persistent step's LM head on tcgen05 (128-row tiles
+    // streamed through the ring).  Off by default: on B200 it measured slower
+    // than the mma.sync LM phase (80 vs 62 us at T = 8), the 16-slot ring holding
+    // one tile at a time.
+    uint8_t* pf_embd = nullptr;
+    if (std::getenv("MTB_LM_TCGEN05") && d.vocab % 128 == 0 &&
+        dalloc(m->allocs, m->error, &pf_embd, pf_weight_bytes(d.vocab, int(H))))
+        return -1;
+    if (upload_q8(m, f, "token_embd.weight", H, d.vocab, staging, embd, 1, 0, pf_embd)) return -1;
     m->dm.embd = embd;
+    m->dm.pf_embd = pf_embd;
     if (upload_f32(m, f, "qwen3.output_norm.weight", H, &m->dm.output_norm)) return -1;
     m->layers.resize(size_t(d.n_layers));
     for (int l = 0; l < d.n_layers; ++l) {

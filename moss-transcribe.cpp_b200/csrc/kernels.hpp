@@ -71,6 +71,7 @@ struct DeviceModel {
     ModelDims dims;
     LayerWeights* layers;    // host array of device pointers
     const uint8_t* embd;     // token_embd tiles (also the tied LM head)
+    const uint8_t* pf_embd;  // token_embd as tcgen05 weight steps (LM head of the persistent step), or null
     const float* output_norm;
     float theta_scale;       // powf(rope_theta, -2/128), computed on the host
 };

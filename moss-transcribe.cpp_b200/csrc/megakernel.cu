@@ -58,6 +58,7 @@ struct MegaArgs {
     ModelDims d;
     const LayerWeights* layers;  // device array
     const uint8_t* embd;
+    const uint8_t* lm_tiles;  // token_embd as tcgen05 weight steps: LM head on the tensor cores, or null
     const float* output_norm;
     float theta_scale;
     KvCache kv;
@@ -195,7 +196,9 @@ struct Schedule {
     bool kv_f16;
     // sizes per streamed phase kind
     int n[6], bytes[6];
-    __device__ void init(const ModelDims& d, int grid_, int cta_, bool kv_f16_, int n_chunks) {
+    bool lm_tc;  // LM head items are 128-row tcgen05 weight tiles (else 8-row mma.sync tiles)
+    __device__ void init(const ModelDims& d, int grid_, int cta_, bool kv_f16_, int n_chunks, bool lm_tc_) {
+        lm_tc = lm_tc_;
         grid = grid_;
         cta = cta_;
         H = d.hidden;
@@ -216,8 +219,8 @@ struct Schedule {
         bytes[W_GU] = 8 * (H / kTileK) * kTileBytes;
         n[W_DOWN] = H / kTileRows;
         bytes[W_DOWN] = (F / kTileK) * kTileBytes;
-        n[W_LM] = V / kTileRows;
-        bytes[W_LM] = (H / kTileK) * kTileBytes;
+        n[W_LM] = lm_tc ? V / 128 : V / kTileRows;
+        bytes[W_LM] = lm_tc ? (H / 64) * kSlotBytes : (H / kTileK) * kTileBytes;
     }
     __device__ int slots_of(int kind) const { return (bytes[kind] + kSlotBytes - 1) / kSlotBytes; }
     __device__ int count_of(int n_items, int rot, int* first) const {
@@ -240,7 +243,7 @@ struct Schedule {
         return pi;
     }
     __device__ const uint8_t* item_src(const LayerWeights* lw, const uint8_t* embd, int kind, int layer, int item) const {
-        if (kind == W_LM) return embd + (size_t)item * bytes[W_LM];
+        if (kind == W_LM) return embd + (size_t)item * bytes[W_LM];  // embd: the LM-head source of this schedule
         const LayerWeights& w = lw[layer];
         switch (kind) {
             case W_QKV: return w.qkv + (size_t)item * bytes[W_QKV];
@@ -301,7 +304,7 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                         bulk_g2s(dst + lane * row_stride, src, unsigned(row_bytes), &full[s]);
                     }
                 } else if (lane == 0) {
-                    const uint8_t* src = sch.item_src(a.layers, a.embd, kind, layer, item);
+                    const uint8_t* src = sch.item_src(a.layers, sch.lm_tc ? a.lm_tiles : a.embd, kind, layer, item);
                     const int off = k * kSlotBytes;
                     const int nbytes = min(kSlotBytes, sch.bytes[kind] - off);
                     mbar_expect_tx(&full[s], unsigned(nbytes));
@@ -399,7 +402,10 @@ __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
 // blocks b = 8k + w: its partial sum runs over k in order (the same tree), the
 // loads are coalesced per warp and all in flight together, and each warp
 // quantises its own blocks from registers.  K = 256 * NK.
-template <int NK>
+// kUmma: the output is the tcgen05 operand layout instead (16 rows x K bytes
+// as 64-K steps of 1024 bytes, core matrix (row group, 16-byte chunk) at
+// (4 group + chunk) * 128, row at +16 row; scales f32 [16][K / 32]).
+template <int NK, bool kUmma = false>
 __device__ __noinline__ void norm_quant_smem(const float* x, const float* __restrict__ wn, float eps, int T,
                                             uint8_t* act_q, float* act_d, double* s_wsum, float* s_scale,
                                             unsigned long long* timeline = nullptr, int pid = 0) {
@@ -464,9 +470,16 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
 #pragma unroll
             for (int k = 0; k < NK; ++k) {
                 const int blk = 8 * k + warp;
-                act_q[(size_t)blk * 512 + frag_offset(t0 + r, lane)] =
-                    (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[r][k], id[r * NK + k]));
-                if (lane == 0) act_d[blk * 16 + t0 + r] = __half2float(__float2half_rn(dd[r * NK + k]));
+                const uint8_t code = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[r][k], id[r * NK + k]));
+                const float dq = __half2float(__float2half_rn(dd[r * NK + k]));
+                if constexpr (kUmma) {
+                    const int row = t0 + r, e = 256 * k + 32 * warp + lane, kk = e % 64;
+                    act_q[(e / 64) * 1024 + ((row / 8) * 4 + kk / 16) * 128 + (row % 8) * 16 + kk % 16] = code;
+                    if (lane == 0) act_d[row * (K / 32) + blk] = dq;
+                } else {
+                    act_q[(size_t)blk * 512 + frag_offset(t0 + r, lane)] = code;
+                    if (lane == 0) act_d[blk * 16 + t0 + r] = dq;
+                }
             }
         }
     }
@@ -960,6 +973,8 @@ struct KCtx {
     float* scale;      // [16]
     float2* cand;      // [8][16]
     int* flag;
+    uint64_t* lm_bars; // [4]: tcgen05 LM head half_full[2], half_free[2]
+    uint32_t* tmem;    // TMEM base address of the tcgen05 LM head
     int T, before, kv_len, n_chunks;
 };
 
@@ -1243,6 +1258,185 @@ __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
     return ok;
 }
 
+// G on the tensor cores: final RMSNorm + quantise into the tcgen05 operand
+// layout; LM-head items are 128-row tiles streamed as 64-K ring slots (one
+// tcgen05 weight step each).  Thread 0 issues one kind::i8 MMA (M 128, N 16,
+// K 32) per q8_0 block into that block's 16 TMEM columns (all blocks of a tile
+// in the 512 columns, two halves so the next tile overlaps the epilogue) and
+// frees each ring slot with tcgen05.commit when its MMAs are done; warps 4-7
+// (TMEM lane quarters 0-3: one vocab row per thread) read the block sums back,
+// evaluate the library's slice-ordered fp32 epilogue per (row, token) and keep
+// the first maximum per token.  Same values and the same first max as the
+// mma.sync path.
+__device__ __forceinline__ uint64_t lm_desc(uint32_t addr) {
+    // K-major, no swizzle: 16-byte K chunks 128 bytes apart, 8-row groups 512 bytes apart, version 1.
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46);
+}
+
+template <int NK, bool kLow>
+__device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid) {
+    const MegaArgs& a = c.a;
+    constexpr int K = 256 * NK, NB = K / 32, STEPS = K / 64, HALF = STEPS / 2, TT = kLow ? 8 : kTMax;
+    constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(16 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t* act_q = c.region;                                          // [STEPS][1024]
+    float* act_d = reinterpret_cast<float*>(c.region + STEPS * 1024);   // [16][NB]
+    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    mark(a.timeline, pid, 0);
+    const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
+    uint64_t* half_full = c.lm_bars;
+    uint64_t* half_free = c.lm_bars + 2;
+    if (tid == 0) {
+        mbar_init(&half_full[0], 1);
+        mbar_init(&half_full[1], 1);
+        mbar_init(&half_free[0], 4);
+        mbar_init(&half_free[1], 4);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    // The activation bytes were written by the generic proxy; the tensor core reads them through the async proxy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(c.tmem)) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    consumer_sync();
+    mark(a.timeline, pid, 1);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *c.tmem;
+    bool ok = true;
+    float best_v[TT];
+    int best_i[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) { best_v[t] = -INFINITY; best_i[t] = 0x7fffffff; }
+    if (tid == 0) {
+        for (int j = 0; j < pi.count && ok; ++j) {
+            const long long q0 = pi.slot0 + (long long)j * pi.slots;
+            for (int ks = 0; ks < STEPS && ok; ++ks) {
+                const int h = ks / HALF;
+                if (ks % HALF == 0 && j > 0 && !mbar_wait(&half_free[h], unsigned((j - 1) & 1), a.abort_flag)) { ok = false; break; }
+                const long long q = q0 + ks;
+                if (!mbar_wait(&c.full[q % kRingSlots], unsigned((q / kRingSlots) & 1), a.abort_flag)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t wslot = smem_addr(c.ring + (size_t)(q % kRingSlots) * kSlotBytes);
+                const uint32_t xstep = smem_addr(act_q + ks * 1024);
+#pragma unroll
+                for (int b = 0; b < 2; ++b) {
+                    const uint32_t d = tmem + (uint32_t)(((2 * ks + b) % NB) * 16);
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n"
+                        ::"r"(d), "l"(lm_desc(wslot + b * 256)), "l"(lm_desc(xstep + b * 256)), "r"(kIdesc), "r"(0),
+                          "r"(0), "r"(0), "r"(0), "r"(0)
+                        : "memory");
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                             ::"r"(smem_addr(&c.empty[q % kRingSlots])) : "memory");
+                if (ks % HALF == HALF - 1)
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                                 ::"r"(smem_addr(&half_full[h])) : "memory");
+            }
+        }
+    } else if (warp >= 4) {
+        const int q4 = warp & 3, r = 32 * q4 + lane;
+        for (int j = 0; j < pi.count && ok; ++j) {
+            const int item = pi.first + j * gridDim.x;
+            const uint8_t* tile = a.lm_tiles + (size_t)item * STEPS * kSlotBytes;
+            float y[TT], acc[TT];  // acc: the open 256-K slice (a slice may span both halves)
+#pragma unroll
+            for (int t = 0; t < TT; ++t) y[t] = acc[t] = 0.f;
+            for (int h = 0; h < 2 && ok; ++h) {
+                // This row's weight scales of the half (fp16 pairs per 64-K step), before the wait.
+                uint32_t wsc[HALF];
+#pragma unroll
+                for (int u = 0; u < HALF; ++u)
+                    wsc[u] = __ldg(reinterpret_cast<const uint32_t*>(tile + (size_t)(h * HALF + u) * kSlotBytes + 8192) + r);
+                int wok = 1;
+                if (lane == 0) wok = mbar_wait(&half_full[h], unsigned(j & 1), a.abort_flag) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, wok, 0)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                static_assert((2 * HALF) % 4 == 0, "blocks of a half in groups of 4");
+#pragma unroll 1
+                for (int b4 = 0; b4 < 2 * HALF; b4 += 4) {
+                    // Four blocks' sums (4 x 16 columns) in one TMEM load.
+                    uint32_t v[64];
+                    const int kb0 = 2 * HALF * h + b4;
+                    const uint32_t ta = tmem + ((uint32_t)(32 * q4) << 16) + (uint32_t)((kb0 % NB) * 16);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,"
+                        "%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+                        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+                          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]),
+                          "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]),
+                          "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]),
+                          "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]),
+                          "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
+                        : "r"(ta));
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int bb = b4 + u, kb = kb0 + u;
+                        const float dw = (bb & 1) ? h2f_hi(wsc[bb / 2]) : h2f_lo(wsc[bb / 2]);
+#pragma unroll
+                        for (int t = 0; t < TT; ++t)
+                            acc[t] = fmaf((float)(int)v[16 * u + t], __fmul_rn(dw, act_d[t * NB + kb]), acc[t]);
+                        if (kb % 8 == 7) {  // a 256-K slice is complete: add it in order
+#pragma unroll
+                            for (int t = 0; t < TT; ++t) {
+                                y[t] = __fadd_rn(y[t], acc[t]);
+                                acc[t] = 0.f;
+                            }
+                        }
+                    }
+                }
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&half_free[h]);
+            }
+            if (!ok) break;
+            if (warp == 4 && j < 12 && lane == 0 && blockIdx.x < 256 && a.timeline)
+                a.timeline[kCtaMarkBase + ((size_t)blockIdx.x * kMaxBarriers + pid) * kCtaMarks + 2 + j] = global_ns();
+            const int col = item * 128 + r;
+#pragma unroll
+            for (int t = 0; t < TT; ++t)
+                if (y[t] > best_v[t] || (y[t] == best_v[t] && col < best_i[t])) { best_v[t] = y[t]; best_i[t] = col; }
+        }
+        if (!ok) consumer_fail(a);
+    }
+    if (!ok && tid == 0) consumer_fail(a);
+    // First max over the warp's rows for each token, then over the warps.
+#pragma unroll
+    for (int t = 0; t < TT; ++t) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v[t], o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i[t], o);
+            if (ov > best_v[t] || (ov == best_v[t] && oi < best_i[t])) { best_v[t] = ov; best_i[t] = oi; }
+        }
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < kTMax; ++t)
+            c.cand[warp * kTMax + t] = t < TT ? make_float2(best_v[t < TT ? t : 0], __int_as_float(best_i[t < TT ? t : 0]))
+                                              : make_float2(-INFINITY, __int_as_float(0x7fffffff));
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    consumer_sync();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    if (tid < kTMax) {
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const float2 cc = c.cand[w * kTMax + tid];
+            const int ci = __float_as_int(cc.y);
+            if (cc.x > bv || (cc.x == bv && ci < bi)) { bv = cc.x; bi = ci; }
+        }
+        a.lm_val[blockIdx.x * kTMax + tid] = make_float2(bv, __int_as_float(bi));
+    }
+    return ok;
+}
+
 // H (CTA 0): first max over the CTA partials, acceptance and rollback.
 __device__ __noinline__ void phase_accept(const KCtx& c) {
     const MegaArgs& a = c.a;
@@ -1292,7 +1486,9 @@ __device__ __noinline__ void run_phases(const KCtx& c) {
         if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), true)) consumer_fail(c.a);
         if (!end_phase(c, &target)) return;
     }
-    if (!phase_lm<kNK, kLow>(c, cur, phase_index(target))) consumer_fail(c.a);
+    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(c, cur, phase_index(target))
+                     : !phase_lm<kNK, kLow>(c, cur, phase_index(target)))
+        consumer_fail(c.a);
     if (!end_phase(c, &target)) return;
     if (blockIdx.x == 0) phase_accept(c);
 }
@@ -1305,6 +1501,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     __shared__ float s_scale[kTMax * 4];
     __shared__ float2 s_cand[kConsumerWarps * kTMax];
     __shared__ int s_flag;
+    __shared__ __align__(8) uint64_t s_lm_bars[4];
+    __shared__ uint32_t s_tmem;
     const int T = args.state->T;
     if (T <= 0) return;
     const int warp = threadIdx.x >> 5;
@@ -1315,7 +1513,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
         c.before = args.state->before;
         c.kv_len = c.before + T;
         c.n_chunks = (c.kv_len + kPage - 1) / kPage;
-        c.sch.init(args.d, gridDim.x, blockIdx.x, args.kv.type == KV_F16, c.n_chunks);
+        c.sch.init(args.d, gridDim.x, blockIdx.x, args.kv.type == KV_F16, c.n_chunks, args.lm_tiles != nullptr);
         c.ring = smem;
         c.region = smem + (size_t)kRingSlots * kSlotBytes;
         c.rope = reinterpret_cast<float*>(c.region + kRegionBytes);
@@ -1325,6 +1523,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
         c.scale = s_scale;
         c.cand = s_cand;
         c.flag = &s_flag;
+        c.lm_bars = s_lm_bars;
+        c.tmem = &s_tmem;
         if (args.timeline && blockIdx.x == 0) {
             args.timeline[kTimelineStart] = global_ns();
             // SM cycles beside the timer (CTA 0, last barrier slot): the clock the step ran at.
@@ -1406,6 +1606,7 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     a.d = m.dims;
     a.layers = layers_dev;
     a.embd = m.embd;
+    a.lm_tiles = m.pf_embd;
     a.output_norm = m.output_norm;
     a.theta_scale = m.theta_scale;
     a.kv = kv;
