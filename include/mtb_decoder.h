@@ -108,6 +108,20 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
                       const mtb_spec_params* params, int32_t* out_ids, int* n_out, mtb_counters* counters,
                       mtb_draft_fn draft, mtb_commit_fn commit, void* user);
 
+/* fuse_embeds (src/generate.cpp:113-177) on the device: row p of out
+ * [seq][hidden] (host) is the dequantised token_embd row of ids[p], except that
+ * the k-th position holding audio_token_id takes audio row k (masked scatter).
+ * Errors as the reference: an id outside [0, vocab), or more audio positions
+ * than audio rows; fewer positions than rows is accepted. */
+int mtb_fuse_embeds(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio, int audio_token_id,
+                    float* out);
+/* mtb_spec_generate from token ids + audio rows: the fused prompt is built on
+ * the device (mtb_fuse_embeds) and prefilled from device memory, so it never
+ * round-trips the host (generate.cpp:229-241 fuse_embeds + greedy_generate). */
+int mtb_spec_generate_ids(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio,
+                          int audio_token_id, int max_new, int eos, const mtb_spec_params* params, int32_t* out_ids,
+                          int* n_out, mtb_counters* counters);
+
 /* Continue from an existing cache: ids[0:n_ids] are the generated ids (the
  * last is the pending seed, not yet in the cache), past the cache length. */
 int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_new, int eos,

@@ -63,6 +63,11 @@ struct mtb_decoder {
     int32_t* scratch_i = nullptr;  // [max_new + 16]
     int* scratch_n = nullptr;
     float* row_buf = nullptr;      // [hidden]
+    // Device fuse_embeds buffers, allocated on first use: fused rows [max_seq][hidden],
+    // ids + audio slots [2][max_seq], audio rows [max_seq][hidden].
+    float* fused_dev = nullptr;
+    int32_t* fuse_ids = nullptr;
+    float* fuse_audio = nullptr;
     cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
     int launches = 0;
     long long h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes this decoder has issued
@@ -339,8 +344,10 @@ int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
 // prefill passes (every layer over up to 512 rows at once, tcgen05
 // projections), the last ones (and the LM head when asked) in steps of kTMax
 // through the verify kernels.  The host's past (h_state) is current on entry.
-int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last) {
+int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last,
+                      bool rows_on_device = false) {
     const int H = d->model->dm.dims.hidden;
+    const cudaMemcpyKind in_kind = rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     int done = 0;
     if (d->pf.max_rows >= kTMax && T > kTMax) {
         const int bulk = T - (T % kTMax ? T % kTMax : kTMax);
@@ -348,9 +355,9 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
         while (done < bulk) {
             const int P = prefill_pass_rows(d, bulk - done, past + done);
             if (P < kTMax) return fail(d->error, "prefill pass does not fit its buffers");
-            d->h2d_bytes += (long long)P * H * 4;
-            MTB_CK(d, cudaMemcpyAsync(d->pf.x, rows + size_t(done) * H, size_t(P) * H * sizeof(float),
-                                      cudaMemcpyHostToDevice, d->stream));
+            if (!rows_on_device) d->h2d_bytes += (long long)P * H * 4;
+            MTB_CK(d, cudaMemcpyAsync(d->pf.x, rows + size_t(done) * H, size_t(P) * H * sizeof(float), in_kind,
+                                      d->stream));
             launch_prefill_pass(d->model->dm, d->kv, d->pf, P, past + done, hidden_out != nullptr, d->stream);
             launch_rows_begin(d->b, P, d->stream);
             launch_rows_end(d->b, d->stream);
@@ -370,8 +377,13 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
     }
     for (int r0 = done; r0 < T; r0 += kTMax) {
         const int n = std::min(kTMax, T - r0);
-        std::memcpy(d->h_rows, rows + size_t(r0) * H, size_t(n) * H * sizeof(float));
-        MTB_CK(d, cudaMemcpyAsync(d->b.x, d->h_rows, size_t(n) * H * sizeof(float), cudaMemcpyHostToDevice, d->stream));
+        if (rows_on_device) {
+            MTB_CK(d, cudaMemcpyAsync(d->b.x, rows + size_t(r0) * H, size_t(n) * H * sizeof(float),
+                                      cudaMemcpyDeviceToDevice, d->stream));
+        } else {
+            std::memcpy(d->h_rows, rows + size_t(r0) * H, size_t(n) * H * sizeof(float));
+            MTB_CK(d, cudaMemcpyAsync(d->b.x, d->h_rows, size_t(n) * H * sizeof(float), cudaMemcpyHostToDevice, d->stream));
+        }
         launch_rows_begin(d->b, n, d->stream);
         const bool last = r0 + n >= T;
         launch_forward_rows(d->model->dm, d->kv, d->b, lm_on_last && last, false, d->stream);
@@ -427,15 +439,53 @@ void clear_progress(StepState& s) {
     s.target_calls = s.drafted_calls = s.proposed = s.accepted = s.target_input_tokens = s.rewinds = 0;
 }
 
-int prefill(mtb_decoder* d, const float* fused, int seq) {
+int prefill(mtb_decoder* d, const float* fused, int seq, bool on_device = false) {
     if (!fused || seq <= 0) return fail(d->error, "empty prompt");
     if (seq + 1 > d->max_seq) return fail(d->error, "prompt exceeds max_seq");
     d->h_state->past = 0;
     clear_progress(*d->h_state);
     if (push_state(d)) return -1;
-    if (forward_host_rows(d, fused, seq, nullptr, true)) return -1;
+    if (forward_host_rows(d, fused, seq, nullptr, true, on_device)) return -1;
     launch_prefill_seed(d->b, d->stream);
     MTB_CK(d, cudaGetLastError());
+    return 0;
+}
+
+// fuse_embeds (src/generate.cpp:113-177) with the rows built on the device:
+// ids are validated and the audio slots counted on the host (the k-th
+// position holding audio_token_id takes audio row k), ids, slots and audio rows
+// are uploaded, and k_fuse_embeds writes the fused rows into fused_dev.
+int fuse_on_device(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio, int audio_token_id) {
+    const ModelDims& dm = d->model->dm.dims;
+    const int H = dm.hidden;
+    if (!ids || seq <= 0) return fail(d->error, "fuse_embeds: empty input_ids");
+    if (seq > d->max_seq) return fail(d->error, "fuse_embeds: input longer than max_seq");
+    if (n_audio < 0 || n_audio > d->max_seq || (n_audio > 0 && !audio)) return fail(d->error, "fuse_embeds: invalid audio rows");
+    std::vector<int32_t> slot(static_cast<size_t>(seq), -1);
+    int k = 0;
+    for (int p = 0; p < seq; ++p) {
+        if (ids[p] < 0 || ids[p] >= dm.vocab)  // generate.cpp:140-146
+            return fail(d->error, "fuse_embeds: input_ids[" + std::to_string(p) + "]=" + std::to_string(ids[p]) +
+                                      " out of range [0," + std::to_string(dm.vocab) + ")");
+        if (ids[p] != audio_token_id) continue;
+        if (k >= n_audio)  // generate.cpp:163-167
+            return fail(d->error, "fuse_embeds: more audio positions than audio rows (n_audio=" + std::to_string(n_audio) + ")");
+        slot[size_t(p)] = k++;
+    }
+    // k < n_audio is allowed (the reference logs a warning and continues).
+    auto& A = d->allocs;
+    if (!d->fused_dev && (dalloc(A, d->error, &d->fused_dev, size_t(d->max_seq) * H * 4) ||
+                          dalloc(A, d->error, &d->fuse_ids, size_t(d->max_seq) * 2 * 4) ||
+                          dalloc(A, d->error, &d->fuse_audio, size_t(d->max_seq) * H * 4)))
+        return -1;
+    d->h2d_bytes += (long long)seq * 8 + (long long)n_audio * H * 4;
+    MTB_CK(d, cudaMemcpyAsync(d->fuse_ids, ids, size_t(seq) * 4, cudaMemcpyHostToDevice, d->stream));
+    MTB_CK(d, cudaMemcpyAsync(d->fuse_ids + d->max_seq, slot.data(), size_t(seq) * 4, cudaMemcpyHostToDevice, d->stream));
+    if (n_audio > 0)
+        MTB_CK(d, cudaMemcpyAsync(d->fuse_audio, audio, size_t(n_audio) * H * 4, cudaMemcpyHostToDevice, d->stream));
+    launch_fuse_embeds(d->model->dm, d->fuse_ids, d->fuse_ids + d->max_seq, seq, d->fuse_audio, d->fused_dev, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    MTB_CK(d, cudaStreamSynchronize(d->stream));  // `slot` is a host temporary
     return 0;
 }
 
@@ -764,6 +814,58 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
             }
             if (refresh(d)) return -1;
         }
+        MTB_CK(d, cudaMemcpyAsync(out_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+        *n_out = s.n_ids;
+        fill_counters(s, counters);
+        return 0;
+    } catch (const std::exception& e) {
+        d->error = e.what();
+        return -1;
+    }
+}
+
+int mtb_fuse_embeds(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio, int audio_token_id,
+                    float* out) {
+    if (!d || !out) return -1;
+    try {
+        cudaSetDevice(d->device);
+        if (fuse_on_device(d, ids, seq, audio, n_audio, audio_token_id)) return -1;
+        const size_t bytes = size_t(seq) * d->model->dm.dims.hidden * 4;
+        d->d2h_bytes += (long long)bytes;
+        MTB_CK(d, cudaMemcpyAsync(out, d->fused_dev, bytes, cudaMemcpyDeviceToHost, d->stream));
+        MTB_CK(d, cudaStreamSynchronize(d->stream));
+        return 0;
+    } catch (const std::exception& e) {
+        d->error = e.what();
+        return -1;
+    }
+}
+
+int mtb_spec_generate_ids(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio,
+                          int audio_token_id, int max_new, int eos, const mtb_spec_params* params, int32_t* out_ids,
+                          int* n_out, mtb_counters* counters) {
+    if (!d || !out_ids || !n_out) return -1;
+    *n_out = 0;
+    try {
+        cudaSetDevice(d->device);
+        if (refresh(d)) return -1;
+        if (set_params(d, max_new, eos, params)) return -1;
+        if (fuse_on_device(d, ids, seq, audio, n_audio, audio_token_id)) return -1;
+        if (prefill(d, d->fused_dev, seq, true)) return -1;
+        StepState& s = *d->h_state;
+        int i = 0;
+        for (;;) {  // device-driven loop, as in mtb_spec_generate without hooks
+            if (run_step(d, 0)) return -1;
+            MTB_CK(d, cudaMemcpyAsync(&d->h_flag[i & 1], &d->b.state->stop, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+            MTB_CK(d, cudaEventRecord(d->ev[i & 1], d->stream));
+            if (i > 0) {
+                MTB_CK(d, cudaEventSynchronize(d->ev[(i - 1) & 1]));
+                if (d->h_flag[(i - 1) & 1] != STOP_NONE) break;
+            }
+            ++i;
+        }
+        if (refresh(d)) return -1;
         MTB_CK(d, cudaMemcpyAsync(out_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
         MTB_CK(d, cudaStreamSynchronize(d->stream));
         *n_out = s.n_ids;

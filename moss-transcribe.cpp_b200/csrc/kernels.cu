@@ -514,6 +514,35 @@ __global__ void k_embed(StepState* st, const uint8_t* __restrict__ embd, int hid
     }
 }
 
+// fuse_embeds on the device (src/generate.cpp:113-177): row p is the q8_0
+// dequant (d * q) of token ids[p] from the token_embd tiles, or, where
+// slot[p] >= 0 (the k-th audio placeholder, slots counted on the host), audio
+// row slot[p].  grid (seq), block 256.
+__global__ void k_fuse_embeds(const int32_t* __restrict__ ids, const int32_t* __restrict__ slot, int seq,
+                              const float* __restrict__ audio, const uint8_t* __restrict__ embd, int hidden,
+                              float* out) {
+    const int p = blockIdx.x;
+    if (p >= seq) return;
+    const int a = slot[p];
+    const int kt_n = hidden / kTileK;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v;
+        if (a >= 0) {
+            v = audio[(size_t)a * hidden + i];
+        } else {
+            const int id = ids[p];  // validated on the host
+            const int rg = id / kTileRows, g = id % kTileRows;
+            const int kt = i / kTileK, blk = (i % kTileK) / 32, cc = i % 32;
+            const uint8_t* tile = embd + ((size_t)rg * kt_n + kt) * kTileBytes;
+            const int t4 = (cc & 15) >> 2, part = cc >> 4;
+            const int8_t q = (int8_t)tile[(g * 4 + t4) * 16 + blk * 8 + part * 4 + (cc & 3)];
+            const unsigned short hb = *reinterpret_cast<const unsigned short*>(tile + 512 + ((g >> 1) * 4 + blk * 2 + (g & 1)) * 2);
+            v = (float)q * __half2float(__ushort_as_half(hb));
+        }
+        out[(size_t)p * hidden + i] = v;
+    }
+}
+
 // n-gram draft over the generated ids (src/cpu_speculative.cpp:45-56): the
 // longest suffix size in [n_min, n_max] with an earlier occurrence, latest
 // occurrence first.  For each end position e < n the common suffix length
@@ -925,6 +954,11 @@ void launch_lm_argmax_rows(const DeviceModel& m, StepState* state, const float* 
                nullptr, m.dims.vocab, state, partials, nullptr};
     gemv<EPI_ARGMAX, 8>(a, lm_blocks, s);
     k_reduce_choices_out<<<1, 512, 0, s>>>(state, partials, lm_blocks, choices);
+}
+
+void launch_fuse_embeds(const DeviceModel& m, const int32_t* ids, const int32_t* slot, int seq, const float* audio,
+                        float* out, cudaStream_t s) {
+    k_fuse_embeds<<<seq, 256, 0, s>>>(ids, slot, seq, audio, m.embd, m.dims.hidden, out);
 }
 
 void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s) { k_rows_begin<<<1, 1, 0, s>>>(b.state, T); }

@@ -89,6 +89,10 @@ void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, 
 
 // Embedding rows from host-provided float rows instead of token ids
 // (prefill and the run() test entry): copies `rows` into x.
+// fuse_embeds on the device: token rows from the token_embd tiles, audio rows
+// where slot[p] >= 0; out [seq][hidden] (device).
+void launch_fuse_embeds(const DeviceModel& m, const int32_t* ids, const int32_t* slot, int seq, const float* audio,
+                        float* out, cudaStream_t s);
 // One prefill pass: P rows in p.x at positions before .. before + P - 1
 // through every layer (tcgen05 projections); the final-normed rows into p.hid
 // when want_hidden.  The KV cache receives the P positions.

@@ -72,6 +72,9 @@ SIGNATURES = {
     "mtb_greedy_generate": (C.c_int, [_vp, _f32p, C.c_int, C.c_int, C.c_int, C.c_float, _i32p, _ip]),
     "mtb_spec_generate": (C.c_int, [_vp, _f32p, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams), _i32p, _ip,
                                     C.POINTER(Counters), DRAFT_FN, COMMIT_FN, _vp]),
+    "mtb_fuse_embeds": (C.c_int, [_vp, _i32p, C.c_int, _f32p, C.c_int, C.c_int, _f32p]),
+    "mtb_spec_generate_ids": (C.c_int, [_vp, _i32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.POINTER(SpecParams), _i32p, _ip, C.POINTER(Counters)]),
     "mtb_resume": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams)]),
     "mtb_spec_step": (C.c_int, [_vp, _i32p, C.c_int, C.POINTER(Counters)]),
     "mtb_spec_step_async": (C.c_int, [_vp, _vp, C.c_int]),
@@ -251,6 +254,29 @@ class Decoder:
         return out[:n.value].tolist(), counters.as_dict()
 
     # -- step-level API --------------------------------------------------------
+    def fuse_embeds(self, ids, audio: np.ndarray, audio_token_id: int) -> np.ndarray:
+        """fuse_embeds (src/generate.cpp:113) with the rows built on the device."""
+        a = _arr_i32(ids)
+        au = np.ascontiguousarray(audio, dtype=np.float32).reshape(-1, self.model.hidden)
+        out = np.zeros((a.size, self.model.hidden), dtype=np.float32)
+        self._check(lib().mtb_fuse_embeds(self.ptr, _i32(a), a.size, _f32(au), au.shape[0], int(audio_token_id),
+                                          _f32(out)), "fuse_embeds")
+        return out
+
+    def spec_generate_ids(self, ids, audio: np.ndarray, audio_token_id: int, max_new: int, eos: int, k_max: int = 4,
+                          n_min: int = 2, n_max: int = 16, penalty: float = 1.0):
+        """Strict speculative generate from ids + audio rows, fused on the device."""
+        a = _arr_i32(ids)
+        au = np.ascontiguousarray(audio, dtype=np.float32).reshape(-1, self.model.hidden)
+        out = np.zeros(max_new, dtype=np.int32)
+        n = C.c_int()
+        counters = Counters()
+        params = SpecParams(k_max, n_min, n_max, penalty)
+        self._check(lib().mtb_spec_generate_ids(self.ptr, _i32(a), a.size, _f32(au), au.shape[0], int(audio_token_id),
+                                                int(max_new), int(eos), C.byref(params), _i32(out), C.byref(n),
+                                                C.byref(counters)), "spec_generate_ids")
+        return out[:n.value].tolist(), counters.as_dict()
+
     def resume(self, ids, past: int, max_new: int, eos: int, k_max=4, n_min=2, n_max=16, penalty=1.0):
         a = _arr_i32(ids)
         params = SpecParams(k_max, n_min, n_max, penalty)
