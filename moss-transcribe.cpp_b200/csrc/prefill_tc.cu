@@ -17,9 +17,11 @@
 //    then 512 bytes of fp16 scales [128 rows][2 blocks].  8704 bytes per step.
 //  * activations, per (32-token tile, 64-K step): 2048 code bytes, the same
 //    core-matrix order over 4 token groups; scales f32 [T][K / 32] apart.
-// Warp roles (192 threads): warp 0 producer (cp.async.bulk into a 4-stage
-// ring), warp 1 TMEM owner + MMA issuer, warps 2-5 epilogue (warp w reads TMEM
-// lanes 32 (w % 4) ..).  Every wait is bounded; a timeout sets `status`.
+// Warp roles (320 threads): warp 0 producer (cp.async.bulk into a 4-stage
+// ring), warp 1 TMEM owner + MMA issuer, warps 2-9 epilogue in two warpgroups
+// of 16 tokens each (warp w reads TMEM lanes 32 (w % 4) ..; pairs of tokens
+// go through one __fmul2_rn and one __ffma2_rn, each half its own chain).
+// Every wait is bounded; a timeout sets `status`.
 #include "device_common.cuh"
 #include "prefill_tc.hpp"
 
@@ -34,7 +36,8 @@ constexpr int kPfStepW = kPfRows * 64;   // code bytes of one 64-K weight step
 constexpr int kPfStepWB = kPfStepW + kPfRows * 2 * 2;  // + fp16 scales
 constexpr int kPfStepX = kPfTok * 64;    // code bytes of one 64-K activation step
 constexpr int kPfStages = 4;
-constexpr int kPfThreads = 192;
+constexpr int kPfThreads = 320;
+constexpr int kPfHalfTok = kPfTok / 2;  // tokens per epilogue warpgroup
 constexpr unsigned long long kPfWaitNs = 2000000000ull;
 constexpr uint32_t kPfIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPfTok >> 3) << 17) |
                               ((uint32_t)(kPfRows >> 4) << 24);  // s32 <- s8 x s8, K-major, M 128, N 32
@@ -85,7 +88,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
     extern __shared__ __align__(1024) uint8_t pf_smem[];
     uint8_t* stage_w = pf_smem;                                         // [stages][8704] (1024-aligned slots below)
     uint8_t* stage_x = pf_smem + kPfStages * 9216;                      // [stages][2048]
-    float* s_dx = reinterpret_cast<float*>(stage_x + kPfStages * kPfStepX);  // [32 tokens][K / 32]
+    float* s_dx = reinterpret_cast<float*>(stage_x + kPfStages * kPfStepX);  // [K / 32][32 tokens]
     __shared__ __align__(8) uint64_t full[kPfStages], empty[kPfStages], slice_full[2], slice_free[2];
     __shared__ uint32_t tmem_base;
     __shared__ float s_up[kPfTok][64];
@@ -101,7 +104,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
         }
         for (int s = 0; s < 2; ++s) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(su32(&slice_full[s])) : "memory");
-            asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(su32(&slice_free[s])) : "memory");
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 8;" ::"r"(su32(&slice_free[s])) : "memory");
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -111,8 +114,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
     }
     // Activation scales of the tile's tokens (tokens past T read as 0).
     for (int i = threadIdx.x; i < kPfTok * nb; i += kPfThreads) {
-        const int t = tt * kPfTok + i / nb;
-        s_dx[i] = t < a.T ? a.xd[(size_t)t * nb + i % nb] : 0.f;
+        const int t = tt * kPfTok + i / nb, kb = i % nb;
+        s_dx[kb * kPfTok + i / nb] = t < a.T ? a.xd[(size_t)t * nb + kb] : 0.f;
     }
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -166,12 +169,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
             }
         }
     } else {
-        // Epilogue: thread = weight row r of the tile (TMEM lane r).
-        const int q = warp & 3;
+        // Epilogue: thread = weight row r of the tile (TMEM lane r), tokens
+        // 16 tg .. 16 tg + 15 of the tile.
+        const int q = warp & 3, tg = (warp - 2) >> 2;
         const int r = 32 * q + lane;
-        float y[kPfTok];
+        float2 y[kPfHalfTok / 2];
 #pragma unroll
-        for (int t = 0; t < kPfTok; ++t) y[t] = 0.f;
+        for (int u = 0; u < kPfHalfTok / 2; ++u) y[u] = make_float2(0.f, 0.f);
         bool ok = true;
         for (int sl = 0; sl < n_slices && ok; ++sl) {
             // This row's 8 weight scales of the slice (fp16 pairs per 64-K step).
@@ -185,35 +189,41 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
             ok = pf_wait(&slice_full[sl % 2], (sl / 2) & 1, a.status);
             if (!ok) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            float acc[kPfTok];
+            float2 acc[kPfHalfTok / 2];
 #pragma unroll
-            for (int t = 0; t < kPfTok; ++t) acc[t] = 0.f;
+            for (int u = 0; u < kPfHalfTok / 2; ++u) acc[u] = make_float2(0.f, 0.f);
 #pragma unroll
             for (int b = 0; b < 8; ++b) {
                 const int kb = 8 * sl + b;
-                uint32_t v[32];
-                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((kb % 16) * kPfTok);
+                uint32_t v[16];
+                const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((kb % 16) * kPfTok + kPfHalfTok * tg);
                 asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                      "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-                      "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-                      "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                      "=r"(v[15])
                     : "r"(ta));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                const float* dx = s_dx + kb;
+                const float2* dx = reinterpret_cast<const float2*>(s_dx + kb * kPfTok + kPfHalfTok * tg);
+                const float2 dw2 = make_float2(dw[b], dw[b]);
 #pragma unroll
-                for (int t = 0; t < kPfTok; ++t)
-                    acc[t] = fmaf((float)(int)v[t], __fmul_rn(dw[b], dx[t * nb]), acc[t]);
+                for (int u = 0; u < kPfHalfTok / 2; ++u) {
+                    const float2 iv = make_float2((float)(int)v[2 * u], (float)(int)v[2 * u + 1]);
+                    acc[u] = __ffma2_rn(iv, __fmul2_rn(dw2, dx[u]), acc[u]);
+                }
             }
             // Columns of this slice may be reused by slice sl + 2.
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(&slice_free[sl % 2])) : "memory");
 #pragma unroll
-            for (int t = 0; t < kPfTok; ++t) y[t] = __fadd_rn(y[t], acc[t]);
+            for (int u = 0; u < kPfHalfTok / 2; ++u) y[u] = __fadd2_rn(y[u], acc[u]);
+        }
+        float yt[kPfHalfTok];
+#pragma unroll
+        for (int u = 0; u < kPfHalfTok / 2; ++u) {
+            yt[2 * u] = y[u].x;
+            yt[2 * u + 1] = y[u].y;
         }
         const int n = nt * kPfRows + r;
         if (a.epi == PF_EPI_SWIGLU) {
@@ -222,30 +232,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
             // warp meets the named barrier, whatever its wait results.
             if (ok && r >= 64)
 #pragma unroll
-                for (int t = 0; t < kPfTok; ++t) s_up[t][r - 64] = y[t];
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (ok) {
-                if (r < 64) {
+                for (int t = 0; t < kPfHalfTok; ++t) s_up[kPfHalfTok * tg + t][r - 64] = yt[t];
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            if (ok && r < 64) {
 #pragma unroll
-                    for (int t = 0; t < kPfTok; ++t) {
-                        const int row = tt * kPfTok + t;
-                        if (row < a.T) {
-                            const float g = y[t];
-                            const float sl = g / (1.0f + exact_expf(-g));
-                            a.y[(size_t)row * a.ldy + nt * 64 + r] = sl * s_up[t][r];
-                        }
+                for (int t = 0; t < kPfHalfTok; ++t) {
+                    const int tl = kPfHalfTok * tg + t, row = tt * kPfTok + tl;
+                    if (row < a.T) {
+                        const float g = yt[t];
+                        const float sw = g / (1.0f + exact_expf(-g));
+                        a.y[(size_t)row * a.ldy + nt * 64 + r] = sw * s_up[tl][r];
                     }
                 }
             }
         } else if (ok) {
-            {
 #pragma unroll
-                for (int t = 0; t < kPfTok; ++t) {
-                    const int row = tt * kPfTok + t;
-                    if (row < a.T) {
-                        float* o = a.y + (size_t)row * a.ldy + n;
-                        *o = a.epi == PF_EPI_RESID ? __fadd_rn(*o, y[t]) : y[t];
-                    }
+            for (int t = 0; t < kPfHalfTok; ++t) {
+                const int row = tt * kPfTok + kPfHalfTok * tg + t;
+                if (row < a.T) {
+                    float* o = a.y + (size_t)row * a.ldy + n;
+                    *o = a.epi == PF_EPI_RESID ? __fadd_rn(*o, yt[t]) : yt[t];
                 }
             }
         }
