@@ -24,6 +24,10 @@
  *   mtb_greedy_choice                    cpu_greedy_choice (src/cpu_speculative.cpp:57-68),
  *                                        evaluated by the device choice kernel
  *   mtb_spec_step / _async, mtb_resume,  one verify step of the loop body
+ *   mtb_spec_prime, mtb_spec_step_group_async, mtb_spec_run_group
+ *                                        the same loop for several recordings at once
+ *                                        (one launch per step; no reference counterpart:
+ *                                        the reference decodes one recording at a time)
  *   mtb_snapshot_save / _restore         (src/cpu_speculative.cpp:118-155)
  *
  * Conventions: every function returns 0 on success or a negative code and
@@ -132,6 +136,22 @@ int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counter
 /* Same, asynchronous on the decoder's stream, proposal from DEVICE memory
  * (NULL -> on-device draft).  Nothing is copied to or from the host. */
 int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft);
+/* Set the decode parameters and prefill the fused rows (the first id is
+ * emitted), without decoding: the start of mtb_spec_generate
+ * (src/cpu_speculative.cpp:86-117), for decoders stepped as a group. */
+int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params);
+/* One verify step of n decoders (1..8) created from the same model, as ONE
+ * persistent launch: each decoder drafts on the device; their rows (seed +
+ * proposals, at most 16 together) are verified against their own KV caches;
+ * each accepts and rolls back on its own.  Proposals beyond the 16 rows are
+ * cut in group order (the accepted ids do not change: verification is strict
+ * greedy; only the proposal counters do).  ds[0] needs the largest max_seq;
+ * no repetition penalty.  Asynchronous: ordered after the work queued on every
+ * member's stream and before the work queued on it later. */
+int mtb_spec_step_group_async(mtb_decoder* const* ds, int n);
+/* Group steps until every member has stopped (max_steps <= 0: no limit),
+ * then synchronous; steps_out = steps launched.  New ids via mtb_read_ids. */
+int mtb_spec_run_group(mtb_decoder* const* ds, int n, int max_steps, int* steps_out);
 /* Device-side copy of the step state and ids (save) and back (restore),
  * asynchronous on the decoder's stream. */
 int mtb_snapshot_save(mtb_decoder* d);

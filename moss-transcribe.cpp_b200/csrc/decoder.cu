@@ -72,6 +72,7 @@ struct mtb_decoder {
     int launches = 0;
     long long h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes this decoder has issued
     cudaEvent_t ev[16] = {};
+    cudaEvent_t group_ev = nullptr;  // orders a group step against this decoder's stream
     std::vector<void*> allocs;
     std::string error;
     ~mtb_decoder() {
@@ -82,6 +83,7 @@ struct mtb_decoder {
                 if (g) cudaGraphExecDestroy(g);
         for (auto& e : ev)
             if (e) cudaEventDestroy(e);
+        if (group_ev) cudaEventDestroy(group_ev);
         for (void* p : allocs) cudaFree(p);
         if (h_state) cudaFreeHost(h_state);
         if (h_rows) cudaFreeHost(h_rows);
@@ -588,7 +590,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         auto& A = d->allocs;
         auto& E = d->error;
         uint8_t* zero_region = nullptr;
-        d->mb.zero_bytes = 16 + size_t(dm.n_layers) * dm.n_kv * 4;
+        d->mb.zero_bytes = 16 + size_t(dm.n_layers) * kMaxStreams * dm.n_kv * 4;
         if (dalloc(A, E, &d->mb.act2_q, size_t(F / 32) * 512) || dalloc(A, E, &d->mb.act2_d, size_t(F / 32) * 16 * 4) ||
             dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
@@ -648,6 +650,10 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         std::memset(d->h_state, 0, sizeof(StepState));
         for (auto& e : d->ev)
             if (cudaEventCreate(&e) != cudaSuccess) { d->error = "event"; return bail(); }
+        if (cudaEventCreateWithFlags(&d->group_ev, cudaEventDisableTiming) != cudaSuccess) {
+            d->error = "event";
+            return bail();
+        }
         d->h_state->max_seq = max_seq;
         d->h_state->max_new = max_new;
         d->h_state->eos = m->eos;
@@ -944,6 +950,110 @@ int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft
     cudaGraphExec_t g = step_graph(d, mode, d->h_state->penalty > 1.f);
     if (!g) return fail(d->error, "could not build the verify-step graph");
     MTB_CK(d, cudaGraphLaunch(g, d->stream));
+    return 0;
+}
+
+int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params) {
+    if (!d || !fused || seq <= 0) return -1;
+    try {
+        cudaSetDevice(d->device);
+        if (refresh(d)) return -1;
+        if (set_params(d, max_new, eos, params)) return -1;
+        return prefill(d, fused, seq);
+    } catch (const std::exception& e) {
+        d->error = e.what();
+        return -1;
+    }
+}
+
+namespace {
+
+// The group's requirements: 1..kMaxStreams distinct decoders of one model
+// (the persistent kernel available, no repetition penalty), one KV type, and
+// attention partial buffers of ds[0] that cover every member's cache.
+int check_group(mtb_decoder* const* ds, int n) {
+    if (!ds || n < 1 || n > kMaxStreams || !ds[0]) {
+        g_error = "a group has 1 to " + std::to_string(kMaxStreams) + " decoders";
+        return -1;
+    }
+    mtb_decoder* d0 = ds[0];
+    if (d0->model->mega_grid <= 0) return fail(d0->error, "group steps need the persistent verify kernel");
+    for (int i = 0; i < n; ++i) {
+        mtb_decoder* di = ds[i];
+        if (!di) return fail(d0->error, "null decoder in the group");
+        for (int j = 0; j < i; ++j)
+            if (ds[j] == di) return fail(d0->error, "a decoder appears twice in the group");
+        if (di->model != d0->model) return fail(d0->error, "group decoders must share one model");
+        if (di->kv_type != d0->kv_type) return fail(d0->error, "group decoders must share one KV type");
+        if (di->b.max_chunks > d0->b.max_chunks)
+            return fail(d0->error, "the first decoder of a group needs the largest max_seq");
+        if (di->h_state->penalty > 1.f) return fail(d0->error, "group steps take no repetition penalty");
+    }
+    return 0;
+}
+
+// The group step on ds[0]'s stream, ordered after every member's queued work
+// and before its later work.
+int group_step(mtb_decoder* const* ds, int n) {
+    mtb_decoder* d0 = ds[0];
+    KvCache kvs[kMaxStreams];
+    StepState* states[kMaxStreams];
+    int32_t* ids[kMaxStreams];
+    for (int i = 1; i < n; ++i) {
+        MTB_CK(d0, cudaEventRecord(ds[i]->group_ev, ds[i]->stream));
+        MTB_CK(d0, cudaStreamWaitEvent(d0->stream, ds[i]->group_ev, 0));
+    }
+    for (int i = 0; i < n; ++i) {
+        launch_draft(ds[i]->b, 0, d0->stream);
+        kvs[i] = ds[i]->kv;
+        states[i] = ds[i]->b.state;
+        ids[i] = ds[i]->b.ids;
+    }
+    const mtb_model* m = d0->model;
+    MTB_CK(d0, launch_step_persistent_group(m->dm, m->layers_dev, kvs, states, ids, n, d0->b, d0->mb, m->mega_grid,
+                                            d0->stream));
+    MTB_CK(d0, cudaEventRecord(d0->group_ev, d0->stream));
+    for (int i = 1; i < n; ++i) MTB_CK(d0, cudaStreamWaitEvent(ds[i]->stream, d0->group_ev, 0));
+    return 0;
+}
+
+}  // namespace
+
+int mtb_spec_step_group_async(mtb_decoder* const* ds, int n) {
+    if (check_group(ds, n)) return -1;
+    cudaSetDevice(ds[0]->device);
+    return group_step(ds, n);
+}
+
+int mtb_spec_run_group(mtb_decoder* const* ds, int n, int max_steps, int* steps_out) {
+    if (steps_out) *steps_out = 0;
+    if (check_group(ds, n)) return -1;
+    mtb_decoder* d0 = ds[0];
+    cudaSetDevice(d0->device);
+    // Device-driven loop: the host reads the members' stop flags one step behind.
+    int i = 0;
+    for (; max_steps <= 0 || i < max_steps; ++i) {
+        if (group_step(ds, n)) return -1;
+        for (int k = 0; k < n; ++k) {
+            MTB_CK(d0, cudaMemcpyAsync(&ds[k]->h_flag[i & 1], &ds[k]->b.state->stop, sizeof(int),
+                                       cudaMemcpyDeviceToHost, d0->stream));
+            ds[k]->d2h_bytes += sizeof(int);
+        }
+        MTB_CK(d0, cudaEventRecord(d0->ev[i & 1], d0->stream));
+        if (i > 0) {
+            MTB_CK(d0, cudaEventSynchronize(d0->ev[(i - 1) & 1]));
+            bool all = true;
+            for (int k = 0; k < n; ++k) all = all && ds[k]->h_flag[(i - 1) & 1] != STOP_NONE;
+            if (all) { ++i; break; }
+        }
+    }
+    MTB_CK(d0, cudaStreamSynchronize(d0->stream));
+    if (steps_out) *steps_out = i;
+    for (int k = 0; k < n; ++k)
+        if (refresh(ds[k])) {
+            if (k) d0->error = ds[k]->error;
+            return -1;
+        }
     return 0;
 }
 

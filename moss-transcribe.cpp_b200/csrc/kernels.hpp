@@ -32,7 +32,7 @@ struct MegaBuffers {
     float2* lm_val;      // [grid][16] LM-head partials
     unsigned* bar;       // zeroed before every launch, together with abort_flag and head_done
     int* abort_flag;
-    unsigned* head_done; // [n_layers][n_kv] finished attention items per kv head
+    unsigned* head_done; // [n_layers][kMaxStreams][n_kv] finished attention items per kv head
     size_t zero_bytes;
     unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
     // Bound on every grid-barrier wait, and a test hook: CTA 0 skips its
@@ -115,6 +115,13 @@ cudaError_t configure_megakernel(int device, int hidden, int* grid_out);
 bool megakernel_supports(const ModelDims& d, int grid);
 cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
                                    const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s);
+// One persistent launch verifying n_streams decoders of the same model (one
+// KV cache, step state and id array each; their drafted rows together at most
+// kTMax, the proposals beyond that cut in stream order), with b's activation
+// buffers and mb's counters.
+cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache* kvs,
+                                         StepState* const* states, int32_t* const* ids, int n_streams,
+                                         const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s);
 // The draft part of a step alone (0: on-device n-gram, 1: host-forced proposal).
 void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s);
 cudaError_t configure_kernels();

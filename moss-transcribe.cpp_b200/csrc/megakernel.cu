@@ -61,9 +61,13 @@ struct MegaArgs {
     const uint8_t* lm_tiles;  // token_embd as tcgen05 weight steps: LM head on the tensor cores, or null
     const float* output_norm;
     float theta_scale;
-    KvCache kv;
-    StepState* state;
-    int32_t* ids;
+    // Streams verified together (one decoder each: its KV cache, step state
+    // and ids).  The step's rows are the streams' rows in stream order; a
+    // single decoder is the one-stream case.
+    int n_streams;
+    KvCache st_kv[kMaxStreams];
+    StepState* st_state[kMaxStreams];
+    int32_t* st_ids[kMaxStreams];
     float* x;        // [16][H]
     float* qkv;      // [16][qd + 2 kd]
     float* gu;       // [16][F]
@@ -76,7 +80,7 @@ struct MegaArgs {
     int max_chunks;
     float2* lm_val;  // [grid][16]
     unsigned* bar;   // grid barrier counter, zero at launch
-    unsigned* head_done;  // [n_layers][n_kv] finished attention items per kv head, zero at launch
+    unsigned* head_done;  // [n_layers][kMaxStreams][n_kv] finished attention items per kv head, zero at launch
     int* abort_flag;
     unsigned long long wait_ns;  // bound on a grid-barrier wait
     int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
@@ -197,8 +201,14 @@ struct Schedule {
     // sizes per streamed phase kind
     int n[6], bytes[6];
     bool lm_tc;  // LM head items are 128-row tcgen05 weight tiles (else 8-row mma.sync tiles)
-    __device__ void init(const ModelDims& d, int grid_, int cta_, bool kv_f16_, int n_chunks, bool lm_tc_) {
+    int n_str;
+    int item0[kMaxStreams + 1];  // first attention item of each stream (items: stream, chunk, kv head)
+    __device__ void init(const ModelDims& d, int grid_, int cta_, bool kv_f16_, const int* chunks, int n_str_,
+                         bool lm_tc_) {
         lm_tc = lm_tc_;
+        n_str = n_str_;
+        item0[0] = 0;
+        for (int i = 0; i < n_str; ++i) item0[i + 1] = item0[i] + chunks[i] * d.n_kv;
         grid = grid_;
         cta = cta_;
         H = d.hidden;
@@ -211,7 +221,7 @@ struct Schedule {
         kd = d.n_kv * kHeadDim;
         n[W_QKV] = (qd + 2 * kd) / kTileRows;
         bytes[W_QKV] = (H / kTileK) * kTileBytes;
-        n[W_ATTN] = n_chunks * d.n_kv;  // (chunk, kv head) items
+        n[W_ATTN] = item0[n_str];  // (stream, chunk, kv head) items
         bytes[W_ATTN] = 2 * (kv_f16 ? KvSlots<true>::kSlotsPerHalf : KvSlots<false>::kSlotsPerHalf) * kSlotBytes;
         n[W_O] = H / kTileRows;
         bytes[W_O] = (qd / kTileK) * kTileBytes;
@@ -223,6 +233,14 @@ struct Schedule {
         bytes[W_LM] = lm_tc ? (H / 64) * kSlotBytes : (H / kTileK) * kTileBytes;
     }
     __device__ int slots_of(int kind) const { return (bytes[kind] + kSlotBytes - 1) / kSlotBytes; }
+    // Attention item -> (stream, chunk, kv head).
+    __device__ void attn_item_of(int item, int* str, int* chunk, int* h) const {
+        int si = 0;
+        while (si + 1 < n_str && item >= item0[si + 1]) ++si;
+        *str = si;
+        *chunk = (item - item0[si]) / nkv;
+        *h = (item - item0[si]) % nkv;
+    }
     __device__ int count_of(int n_items, int rot, int* first) const {
         const int f = ((cta - rot) % grid + grid) % grid;
         *first = f;
@@ -295,12 +313,14 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                 uint8_t* dst = ring + (size_t)s * kSlotBytes;
                 if (kind == W_ATTN) {
                     const int half = slots / 2, which = k / half, r = (k % half) * rps + lane;
-                    const int chunk = item / sch.nkv, h = item % sch.nkv;
+                    int si, chunk, h;
+                    sch.attn_item_of(item, &si, &chunk, &h);
+                    const KvCache& kvs = a.st_kv[si];
                     if (lane == 0) mbar_expect_tx(&full[s], unsigned(rps * row_bytes));
                     __syncwarp();
                     if (lane < rps) {
-                        const long long off = kv_offset(a.kv, sch.nkv, layer, which, h, chunk * kPage + r);
-                        const uint8_t* src = static_cast<const uint8_t*>(a.kv.base) + off * (sch.kv_f16 ? 2 : 4);
+                        const long long off = kv_offset(kvs, sch.nkv, layer, which, h, chunk * kPage + r);
+                        const uint8_t* src = static_cast<const uint8_t*>(kvs.base) + off * (sch.kv_f16 ? 2 : 4);
                         bulk_g2s(dst + lane * row_stride, src, unsigned(row_bytes), &full[s]);
                     }
                 } else if (lane == 0) {
@@ -330,6 +350,11 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
 
 // Grid barrier over the consumer warps of every CTA (the counter only grows;
 // barrier b completes at (b + 1) * grid arrivals).  Returns false on abort.
+// A wait of the step gave up: every stream's state carries the error.
+__device__ __forceinline__ void report_timeout(const MegaArgs& a) {
+    for (int s = 0; s < a.n_streams; ++s) a.st_state[s]->error = 2;
+}
+
 __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
     consumer_sync();
     if (threadIdx.x == 0) {
@@ -351,7 +376,7 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
                 if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
                 if (global_ns() - t0 > a.wait_ns) {
                     atomicExch(a.abort_flag, 1);
-                    a.state->error = 2;
+                    report_timeout(a);
                     status = 1;
                     break;
                 }
@@ -371,7 +396,7 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
 __device__ void consumer_fail(const MegaArgs& a) {
     if ((threadIdx.x & 31) == 0) {
         atomicExch(a.abort_flag, 1);
-        a.state->error = 2;
+        report_timeout(a);
     }
 }
 
@@ -608,13 +633,13 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
     return y;
 }
 
-// Phase C for one (row t, q head qh, 32-dim block k) by one warp, lane =
+// Phase C for one (row t of the step, stream si, q head qh, 32-dim block k) by one warp, lane =
 // dim 32 k + lane: merge of the chunk partials in chunk order (M = max m_c;
 // w_c = exp(m_c - M); L = sum w_c l_c; o = sum w_c o_c / L, each sum one
 // sequential fmaf chain), then that q8_0 block of the context row.  All of a
 // batch's loads (32 chunks) are issued together, the next batch's while the
 // current one is summed.
-__device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int qh, int k, int n_chunks) {
+__device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int si, int qh, int k, int n_chunks) {
     const int lane = threadIdx.x & 31;
     const int G = a.d.n_heads / a.d.n_kv, h = qh / G, qi = t * G + qh % G;
     // The head's chunk items are counted as they finish (release-add after
@@ -623,7 +648,7 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int q
     {
         int give_up = 0;
         if (lane == 0) {
-            const unsigned* done = a.head_done + (size_t)l * a.d.n_kv + h;
+            const unsigned* done = a.head_done + ((size_t)l * kMaxStreams + si) * a.d.n_kv + h;
             const unsigned long long t0 = global_ns();
             for (unsigned it = 0;; ++it) {
                 unsigned v;
@@ -633,7 +658,7 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int q
                     if (*reinterpret_cast<const volatile int*>(a.abort_flag)) { give_up = 1; break; }
                     if (global_ns() - t0 > a.wait_ns) {
                         atomicExch(a.abort_flag, 1);
-                        a.state->error = 2;
+                        report_timeout(a);
                         give_up = 1;
                         break;
                     }
@@ -866,10 +891,13 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 
 // The item with RP >= this warp's query rows (a power of two).  Returns false
 // when a slot wait gave up.
+// The item's stream has T rows from step row row0 on, after `before` cached
+// positions, in cache `kv`.  Its partials are stored under step rows (row0 + t) * G + jh.
 template <bool F16, int RP>
 __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
                                        const float* rope, int l, int chunk, int h, long long q0, int T, int before,
-                                       int wl, int wpi, int bar, int mark_pid, int mark_k) {
+                                       int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
+                                       int mark_k) {
     using KS = KvSlots<F16>;
     const int nh = a.d.n_heads, nkv = a.d.n_kv, G = nh / nkv;
     const int lane = threadIdx.x & 31, nthr = wpi * 32;
@@ -887,7 +915,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
         float x[RP][4];
 #pragma unroll
         for (int rr = 0; rr < RP; ++rr) {
-            const int r = wl + wpi * rr, t = r / G, jh = r % G;
+            const int r = wl + wpi * rr, t = row0 + r / G, jh = r % G;
             const float* src = a.qkv + (size_t)t * ldq + (size_t)(h * G + jh) * kHeadDim;
 #pragma unroll
             for (int q = 0; q < 4; ++q) x[rr][q] = rr < R ? __ldcg(src + 32 * q + lane) : 0.f;
@@ -895,7 +923,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 #pragma unroll
         for (int rr = 0; rr < RP; ++rr) {
             if (rr < R) {
-                const int r = wl + wpi * rr, t = r / G;
+                const int r = wl + wpi * rr, t = row0 + r / G;
                 float o[4];
                 norm_rope_row(x[rr], w.q_norm, a.d.eps, rope + t * 64 * 2, o);
 #pragma unroll
@@ -911,7 +939,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
     {
         const int r_lo = max(before - p0, 0), nr = max(n_pos - r_lo, 0);
         for (int i = wl; i < 2 * nr; i += wpi) {
-            const int which = i / nr, r = r_lo + i % nr, t = p0 + r - before;
+            const int which = i / nr, r = r_lo + i % nr, t = row0 + p0 + r - before;
             const float* src = a.qkv + (size_t)t * ldq + (size_t)(nh + which * nkv + h) * kHeadDim;
             float x[4], o[4];
 #pragma unroll
@@ -922,11 +950,11 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 #pragma unroll
                 for (int q = 0; q < 4; ++q) o[q] = x[q];
             }
-            const long long off = kv_offset(a.kv, nkv, l, which, h, p0 + r);
+            const long long off = kv_offset(kv, nkv, l, which, h, p0 + r);
             uint8_t* row = kv_row<F16>(ring, q0, which, r);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                kv_store(a.kv, off + 32 * q + lane, o[q]);
+                kv_store(kv, off + 32 * q + lane, o[q]);
                 if constexpr (F16)
                     reinterpret_cast<__half*>(row)[32 * q + lane] = __float2half_rn(o[q]);
                 else
@@ -938,7 +966,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
     }
     item_sync(bar, nthr);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 1);
-    const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4);
+    const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4) + (size_t)row0 * G;
     if (R > 0) attn_rows<F16, RP>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 2);
     return ok;
@@ -947,13 +975,17 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 template <bool F16>
 __device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
                                           const float* rope, int l, int chunk, int h, long long q0, int T, int before,
-                                          int wl, int wpi, int bar, int mark_pid, int mark_k) {
+                                          int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
+                                          int mark_k) {
     const int NQ = T * (a.d.n_heads / a.d.n_kv);
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
-    if (R <= 1) return attn_body<F16, 1>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
-    if (R == 2) return attn_body<F16, 2>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
-    if (R <= 4) return attn_body<F16, 4>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
-    return attn_body<F16, 8>(a, ring, full, region, rope, l, chunk, h, q0, T, before, wl, wpi, bar, mark_pid, mark_k);
+#define MTB_ATTN_BODY(RP) \
+    attn_body<F16, RP>(a, ring, full, region, rope, l, chunk, h, q0, T, before, row0, kv, wl, wpi, bar, mark_pid, mark_k)
+    if (R <= 1) return MTB_ATTN_BODY(1);
+    if (R == 2) return MTB_ATTN_BODY(2);
+    if (R <= 4) return MTB_ATTN_BODY(4);
+    return MTB_ATTN_BODY(8);
+#undef MTB_ATTN_BODY
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -975,7 +1007,10 @@ struct KCtx {
     int* flag;
     uint64_t* lm_bars; // [4]: tcgen05 LM head half_full[2], half_free[2]
     uint32_t* tmem;    // TMEM base address of the tcgen05 LM head
-    int T, before, kv_len, n_chunks;
+    int T;             // rows of the step, all streams
+    // Per stream: rows, first step row, cached positions, attention chunks.
+    int s_T[kMaxStreams], s_row0[kMaxStreams], s_before[kMaxStreams], s_chunks[kMaxStreams];
+    int row_stream[kTMax];  // stream of each step row
 };
 
 __device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
@@ -994,7 +1029,8 @@ __device__ __noinline__ void phase_embed(const KCtx& c) {
     const int tid = threadIdx.x, H = a.d.hidden;
     for (int i = tid; i < kTMax * 64; i += kConsumers) {
         const int t = i / 64, k = i % 64;
-        float theta = (float)(c.before + t);
+        const int si = t < c.T ? c.row_stream[t] : 0;
+        float theta = (float)(t < c.T ? c.s_before[si] + t - c.s_row0[si] : t);
         for (int j = 0; j < k; ++j) theta = __fmul_rn(theta, a.theta_scale);
         float sn, cs;
         exact_sincosf(theta, &sn, &cs);
@@ -1002,12 +1038,13 @@ __device__ __noinline__ void phase_embed(const KCtx& c) {
         c.rope[i * 2 + 1] = sn;
     }
     const int kt_n = H / kTileK;
-    StepState* st = a.state;
     for (int i = blockIdx.x * kConsumers + tid; i < kTMax * H; i += gridDim.x * kConsumers) {
         const int row = i / H, col = i % H;
         float v = 0.f;
         if (row < c.T) {
-            int id = st->tokens[row];
+            const int si = c.row_stream[row];
+            StepState* st = a.st_state[si];
+            int id = st->tokens[row - c.s_row0[si]];
             if (id < 0 || id >= a.d.vocab) { st->error = 1; id = 0; }
             const int rg = id / kTileRows, g = id % kTileRows;
             const int kt = col / kTileK, blk = (col % kTileK) / 32, cc = col % 32;
@@ -1067,23 +1104,27 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
     for (int j = 0; j < pi.count; j += 2) {
         const int n_now = min(2, pi.count - j), wpi = kConsumerWarps / n_now;
         const int sub = warp / wpi, wl = warp % wpi;
-        const int item = pi.first + (j + sub) * gridDim.x, chunk = item / nkv, h = item % nkv;
+        const int item = pi.first + (j + sub) * gridDim.x;
+        int si, chunk, h;
+        c.sch.attn_item_of(item, &si, &chunk, &h);
         const long long q0 = pi.slot0 + (long long)(j + sub) * pi.slots;
         uint8_t* region = c.region + sub * kAttnRegion;
         const int mp = j == 0 && sub == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
-                              ? attn_item<true>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.T, c.before,
-                                                wl, wpi, 2 + sub, mp, mk)
-                              : attn_item<false>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.T, c.before,
-                                                 wl, wpi, 2 + sub, mp, mk);
+                              ? attn_item<true>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.s_T[si],
+                                                c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + sub, mp, mk)
+                              : attn_item<false>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.s_T[si],
+                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + sub, mp, mk);
         ok = ok && good;
         consumer_sync();
         if (threadIdx.x < n_now * pi.slots) mbar_arrive(&c.empty[(pi.slot0 + (long long)j * pi.slots + threadIdx.x) % kRingSlots]);
         if (threadIdx.x < n_now) {
             // The items' partials are written (named barrier above): count them
             // for their heads' merges (release: cumulative over the CTA's stores).
-            const int hh = (pi.first + (j + threadIdx.x) * gridDim.x) % nkv;
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.head_done + (size_t)l * nkv + hh) : "memory");
+            int s2, c2, h2;
+            c.sch.attn_item_of(pi.first + (j + threadIdx.x) * gridDim.x, &s2, &c2, &h2);
+            unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + s2) * nkv + h2;
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         }
         mark(a.timeline, mp, mk + 3);
     }
@@ -1097,8 +1138,10 @@ __device__ __noinline__ bool phase_combine(const KCtx& c, int l) {
     const int nh = c.a.d.n_heads, warp = threadIdx.x >> 5;
     const int n_tasks = c.T * nh * 4;
     bool ok = true;
-    for (int it = blockIdx.x + gridDim.x * warp; it < n_tasks && ok; it += gridDim.x * kConsumerWarps)
-        ok = combine_task(c.a, l, it / (nh * 4), (it / 4) % nh, it % 4, c.n_chunks);
+    for (int it = blockIdx.x + gridDim.x * warp; it < n_tasks && ok; it += gridDim.x * kConsumerWarps) {
+        const int t = it / (nh * 4), si = c.row_stream[t];
+        ok = combine_task(c.a, l, t, si, (it / 4) % nh, it % 4, c.s_chunks[si]);
+    }
     return ok;
 }
 
@@ -1440,7 +1483,6 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
 // H (CTA 0): first max over the CTA partials, acceptance and rollback.
 __device__ __noinline__ void phase_accept(const KCtx& c) {
     const MegaArgs& a = c.a;
-    StepState* st = a.state;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int row = warp; row < c.T; row += kConsumerWarps) {
         float bv = -INFINITY;
@@ -1456,10 +1498,22 @@ __device__ __noinline__ void phase_accept(const KCtx& c) {
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        if (lane == 0) st->choice[row] = bi == 0x7fffffff ? 0 : bi;
+        if (lane == 0) {
+            const int si = c.row_stream[row];
+            a.st_state[si]->choice[row - c.s_row0[si]] = bi == 0x7fffffff ? 0 : bi;
+        }
     }
     consumer_sync();
-    if (threadIdx.x == 0) accept_choices(st, a.ids);
+    // One thread per stream.  A stream whose proposals did not all fit the
+    // step's rows verified the first s_T - 1 of them: its proposal count is cut to that.
+    if (threadIdx.x < a.n_streams && c.s_T[threadIdx.x] > 0) {
+        StepState* st = a.st_state[threadIdx.x];
+        if (st->T != c.s_T[threadIdx.x]) {
+            st->T = c.s_T[threadIdx.x];
+            st->n_prop = st->T - 1;
+        }
+        accept_choices(st, a.st_ids[threadIdx.x]);
+    }
     if (a.timeline && threadIdx.x == 0) {
         a.timeline[kTimelineStart + 1] = global_ns();
         a.timeline[kCtaMarkBase + (size_t)(kMaxBarriers - 1) * kCtaMarks + 1] = clock64();
@@ -1503,17 +1557,37 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     __shared__ int s_flag;
     __shared__ __align__(8) uint64_t s_lm_bars[4];
     __shared__ uint32_t s_tmem;
-    const int T = args.state->T;
-    if (T <= 0) return;
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         KCtx& c = s_ctx;
         c.a = args;
-        c.T = T;
-        c.before = args.state->before;
-        c.kv_len = c.before + T;
-        c.n_chunks = (c.kv_len + kPage - 1) / kPage;
-        c.sch.init(args.d, gridDim.x, blockIdx.x, args.kv.type == KV_F16, c.n_chunks, args.lm_tiles != nullptr);
+        // The streams' rows: every active stream (T > 0) keeps its seed row;
+        // the rows left over go to the proposals in stream order, so that
+        // the step never exceeds kTMax rows (every CTA computes the same table).
+        int active = 0;
+        for (int si = 0; si < args.n_streams; ++si) active += args.st_state[si]->T > 0;
+        int spare = kTMax - active, rows = 0;
+        for (int si = 0; si < args.n_streams; ++si) {
+            const StepState* st = args.st_state[si];
+            int T = st->T;
+            if (T > 0) {
+                const int extra = min(T - 1, max(spare, 0));
+                spare -= extra;
+                T = 1 + extra;
+            } else {
+                T = 0;
+            }
+            if (rows + T > kTMax) T = 0;  // more active streams than rows: cannot happen with kMaxStreams <= kTMax
+            c.s_T[si] = T;
+            c.s_row0[si] = rows;
+            c.s_before[si] = st->before;
+            c.s_chunks[si] = T > 0 ? (st->before + T + kPage - 1) / kPage : 0;
+            for (int t = 0; t < T; ++t) c.row_stream[rows + t] = si;
+            rows += T;
+        }
+        c.T = rows;
+        c.sch.init(args.d, gridDim.x, blockIdx.x, args.st_kv[0].type == KV_F16, c.s_chunks, args.n_streams,
+                   args.lm_tiles != nullptr);
         c.ring = smem;
         c.region = smem + (size_t)kRingSlots * kSlotBytes;
         c.rope = reinterpret_cast<float*>(c.region + kRegionBytes);
@@ -1538,6 +1612,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     }
     __syncthreads();
     const KCtx& c = s_ctx;
+    if (c.T <= 0) return;
     if (warp == kConsumerWarps) {
         producer(c.a, c.sch, c.ring, c.full, c.empty);
         return;
@@ -1599,8 +1674,10 @@ bool megakernel_supports(const ModelDims& d, int grid) {
     return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
 }
 
-cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
-                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache* kvs,
+                                         StepState* const* states, int32_t* const* ids, int n_streams,
+                                         const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+    if (n_streams < 1 || n_streams > kMaxStreams) return cudaErrorInvalidValue;
     MegaArgs a{};
     a.timeline = mb.timeline;
     a.d = m.dims;
@@ -1609,9 +1686,12 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     a.lm_tiles = m.pf_embd;
     a.output_norm = m.output_norm;
     a.theta_scale = m.theta_scale;
-    a.kv = kv;
-    a.state = b.state;
-    a.ids = b.ids;
+    a.n_streams = n_streams;
+    for (int i = 0; i < n_streams; ++i) {
+        a.st_kv[i] = kvs[i];
+        a.st_state[i] = states[i];
+        a.st_ids[i] = ids[i];
+    }
     a.x = b.x;
     a.qkv = b.qkv;
     a.gu = b.gu;
@@ -1645,6 +1725,13 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
         case 512: return cudaLaunchKernelEx(&cfg, k_verify_persistent<2>, a);
         default: return cudaLaunchKernelEx(&cfg, k_verify_persistent<4>, a);
     }
+}
+
+cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
+                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+    StepState* state = b.state;
+    int32_t* ids = b.ids;
+    return launch_step_persistent_group(m, layers_dev, &kv, &state, &ids, 1, b, mb, grid, s);
 }
 
 }  // namespace mtb

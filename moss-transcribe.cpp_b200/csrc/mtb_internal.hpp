@@ -13,6 +13,7 @@ constexpr int kTileRows = 8;    // weight rows per tile (the mma N dimension)
 constexpr int kTileK = 64;      // K per tile (two q8_0 blocks)
 constexpr int kTileBytes = 544; // 512 code bytes + 16 fp16 scales = 16 q8_0 blocks
 constexpr int kPage = 64;       // KV positions per page (= attention chunk)
+constexpr int kMaxStreams = 8;  // decoders verified in one persistent launch (their rows share the 16)
 
 enum KvType : int { KV_F32 = 0, KV_F16 = 1 };
 

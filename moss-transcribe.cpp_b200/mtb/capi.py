@@ -78,6 +78,9 @@ SIGNATURES = {
     "mtb_resume": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams)]),
     "mtb_spec_step": (C.c_int, [_vp, _i32p, C.c_int, C.POINTER(Counters)]),
     "mtb_spec_step_async": (C.c_int, [_vp, _vp, C.c_int]),
+    "mtb_spec_prime": (C.c_int, [_vp, _f32p, C.c_int, C.c_int, C.c_int, C.POINTER(SpecParams)]),
+    "mtb_spec_step_group_async": (C.c_int, [C.POINTER(_vp), C.c_int]),
+    "mtb_spec_run_group": (C.c_int, [C.POINTER(_vp), C.c_int, C.c_int, _ip]),
     "mtb_snapshot_save": (C.c_int, [_vp]),
     "mtb_snapshot_restore_async": (C.c_int, [_vp]),
     "mtb_read_ids": (C.c_int, [_vp, _i32p, C.c_int, _ip, C.POINTER(Counters)]),
@@ -340,6 +343,14 @@ class Decoder:
         lib().mtb_transfer_bytes(self.ptr, C.byref(a), C.byref(b))
         return a.value, b.value
 
+    def spec_prime(self, fused: np.ndarray, max_new: int, eos: int, k_max: int = 4, n_min: int = 2, n_max: int = 16,
+                   penalty: float = 1.0):
+        """Parameters + prefill of the fused rows (first id emitted), no decoding."""
+        f = np.ascontiguousarray(fused, dtype=np.float32).reshape(-1, self.model.hidden)
+        params = SpecParams(k_max, n_min, n_max, penalty)
+        self._check(lib().mtb_spec_prime(self.ptr, _f32(f), f.shape[0], int(max_new), int(eos), C.byref(params)),
+                    "spec_prime")
+
     def spec_step_async(self, draft_device_ptr, n_draft: int):
         self._check(lib().mtb_spec_step_async(self.ptr, C.c_void_p(draft_device_ptr), int(n_draft)), "spec_step_async")
 
@@ -356,3 +367,27 @@ class Decoder:
         ms = C.c_float()
         self._check(lib().mtb_event_elapsed_ms(self.ptr, int(a), int(b), C.byref(ms)), "event_elapsed")
         return ms.value
+
+
+def _group(decoders):
+    arr = (_vp * len(decoders))(*[d.ptr for d in decoders])
+    return arr
+
+
+def _group_error(decoders, what):
+    msg = lib().mtb_decoder_error(decoders[0].ptr).decode() if decoders else ""
+    return MtbError(f"{what}: {msg or lib().mtb_global_error().decode()}")
+
+
+def spec_step_group_async(decoders):
+    """One verify step of several decoders of one model as one launch (mtb_spec_step_group_async)."""
+    if lib().mtb_spec_step_group_async(_group(decoders), len(decoders)) != 0:
+        raise _group_error(decoders, "spec_step_group_async")
+
+
+def spec_run_group(decoders, max_steps: int = 0) -> int:
+    """Group steps until every decoder stopped; returns the steps launched (mtb_spec_run_group)."""
+    n = C.c_int()
+    if lib().mtb_spec_run_group(_group(decoders), len(decoders), int(max_steps), C.byref(n)) != 0:
+        raise _group_error(decoders, "spec_run_group")
+    return n.value
