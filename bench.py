@@ -51,6 +51,12 @@ EMBED_BYTES_PER_ROW = 1_088
 # DRAM bytes (read + write) of one k_verify_persistent launch at this workload,
 # from the ncu capture summarised in profiles/k_verify_persistent_kv2048_t8_full.md.
 TRAFFIC_BYTES = 882_363_648
+# configs[4] sample (multi-stream box throughput): recordings of 1500 audio rows
+# (the KV cache they leave, synthetic fp16), decoded with the device n-gram
+# draft at k = 8, on one GPU.
+MS_STREAMS = 8
+MS_KV = 1500
+MS_STEPS = 48
 
 
 def step_bytes(kv_len: int, T: int) -> int:
@@ -280,6 +286,7 @@ def main():
         pf_times.append(time.perf_counter() - t0)
     pf_dec.close()
     pf_s = statistics.median(pf_times)
+    ms_line = multi_stream(model, capi, fixture) if model.persistent_grid > 0 else None
     prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
                "path": "prefill passes (tcgen05 q8_0 projections) + verify kernels for the last rows",
                "timing": "host wall clock around run(), median of 5, host rows in, hidden rows out"}
@@ -297,7 +304,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32 (fp16 KV)", "data": "synthetic", "config": config,
             "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk,
-            "prefill": prefill}
+            "prefill": prefill, "multi_stream": ms_line}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(path, 5)
     if rank == 0:
@@ -307,6 +314,55 @@ def main():
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def multi_stream(model, capi, fixture) -> dict:
+    """configs[4] on one GPU, a bounded sample: MS_STREAMS recordings decoded
+    MS_STEPS verify steps each, (a) one recording at a time (one persistent
+    launch per recording per step) and (b) as one group (one launch per step for
+    all of them: cross-stream batching; the rows beyond 16 are cut in stream
+    order).  Host wall clock around the public calls (mtb_spec_run_group), ids
+    read back; the accepted ids of (a) and (b) are identical by construction
+    and checked here."""
+    V = model.vocab
+    ds = []
+    for i in range(MS_STREAMS):
+        d = capi.Decoder(model, MS_KV + 512, capi.KV_F16, max_new=512)
+        d.fill_synthetic_kv(MS_KV, 2000 + i)
+        ds.append(d)
+    hist = [fixture.lcg_ids(32, V, seed=300 + i).tolist() for i in range(MS_STREAMS)]
+
+    def start():
+        for d, h in zip(ds, hist):
+            d.resume(h, MS_KV, 512, -1, k_max=8, n_min=3, n_max=3)
+
+    def run(groups):
+        start()
+        t0 = time.perf_counter()
+        for g in groups:
+            capi.spec_run_group(g, MS_STEPS)
+        dt = time.perf_counter() - t0
+        out = [d.read_ids() for d in ds]
+        toks = sum(len(ids) - len(h) for (ids, _), h in zip(out, hist))
+        rows = sum(c["target_input_tokens"] for _, c in out)
+        acc = sum(c["accepted"] for _, c in out)
+        return dt, toks, rows, acc, [ids for ids, _ in out]
+
+    run([[d] for d in ds])  # warm-up
+    s_dt, s_toks, s_rows, s_acc, s_ids = run([[d] for d in ds])
+    run([ds])
+    g_dt, g_toks, g_rows, g_acc, g_ids = run([ds])
+    for d in ds:
+        d.close()
+    assert g_ids == s_ids, "group decode differs from single-stream decode"
+    return {"workload": f"configs[4] sample: {MS_STREAMS} recordings, KV {MS_KV} fp16 synthetic each, "
+                        f"{MS_STEPS} verify steps each, device n-gram draft k=8",
+            "single_stream": {"tokens_per_s": round(s_toks / s_dt, 1), "ms_per_launch": round(s_dt * 1e3 / (MS_STREAMS * MS_STEPS), 3),
+                              "tokens": s_toks, "rows": s_rows, "accepted": s_acc},
+            "grouped": {"tokens_per_s": round(g_toks / g_dt, 1), "ms_per_launch": round(g_dt * 1e3 / MS_STEPS, 3),
+                        "tokens": g_toks, "rows": g_rows, "accepted": g_acc},
+            "speedup": round((g_toks / g_dt) / (s_toks / s_dt), 3),
+            "timing": "host wall clock around mtb_spec_run_group, ids read back; same ids in both modes"}
 
 
 def _device_ids(dec, arr: np.ndarray) -> int:

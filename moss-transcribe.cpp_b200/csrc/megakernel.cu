@@ -145,6 +145,16 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
 }
 
+// 16-byte asynchronous copy global -> shared (L2 only), tracked per thread.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// One pending arrival on `b` that lands when this thread's earlier cp.async copies have.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* b) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(b)) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -312,17 +322,25 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
                 uint8_t* dst = ring + (size_t)s * kSlotBytes;
                 if (kind == W_ATTN) {
-                    const int half = slots / 2, which = k / half, r = (k % half) * rps + lane;
+                    // The slot's rps rows (contiguous in the cache page) into
+                    // padded shared rows: 16-byte copies over all lanes, each
+                    // lane's completion one pending arrival on the slot's
+                    // barrier, then the slot's own arrival.  (Many small bulk
+                    // copies would queue in the copy engine: one per row.)
+                    const int half = slots / 2, which = k / half, r0 = (k % half) * rps;
                     int si, chunk, h;
                     sch.attn_item_of(item, &si, &chunk, &h);
                     const KvCache& kvs = a.st_kv[si];
-                    if (lane == 0) mbar_expect_tx(&full[s], unsigned(rps * row_bytes));
-                    __syncwarp();
-                    if (lane < rps) {
-                        const long long off = kv_offset(kvs, sch.nkv, layer, which, h, chunk * kPage + r);
-                        const uint8_t* src = static_cast<const uint8_t*>(kvs.base) + off * (sch.kv_f16 ? 2 : 4);
-                        bulk_g2s(dst + lane * row_stride, src, unsigned(row_bytes), &full[s]);
+                    const long long off = kv_offset(kvs, sch.nkv, layer, which, h, chunk * kPage + r0);
+                    const uint8_t* src = static_cast<const uint8_t*>(kvs.base) + off * (sch.kv_f16 ? 2 : 4);
+                    const int segs = row_bytes / 16;
+                    for (int i = lane; i < rps * segs; i += 32) {
+                        const int rr = i / segs, sg = i % segs;
+                        cp_async16(dst + rr * row_stride + sg * 16, src + (size_t)rr * row_bytes + sg * 16);
                     }
+                    cp_async_arrive(&full[s]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
                 } else if (lane == 0) {
                     const uint8_t* src = sch.item_src(a.layers, sch.lm_tc ? a.lm_tiles : a.embd, kind, layer, item);
                     const int off = k * kSlotBytes;
@@ -334,6 +352,7 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
         }
         items_before += sch.n[kind];
     }
+    asm volatile("cp.async.wait_all;" ::: "memory");
     if (!ok && lane == 0) {
         atomicExch(a.abort_flag, 1);
         // Drain this CTA's copies still in flight before the CTA exits.
@@ -752,7 +771,9 @@ __device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* 
 // sum), and each P.V output (lane's dims 4 lane .. 4 lane + 3) is one
 // sequential fmaf chain over the chunk's positions; the order of
 // k_attn_chunk and the CPU restatement.
-constexpr int kAttnRegion = 32 * kHeadDim * 4 + 32 * kPage * 8;  // q rows + doubled exp weights
+// Scratch of one warp group's item: query rows [rows][128] f32 + doubled exp
+// weights [rows][64] float2, 1 KB per row.
+constexpr int kAttnRowBytes = kHeadDim * 4 + kPage * 8;
 
 __device__ __forceinline__ void item_sync(int bar, int nthr) {
     asm volatile("bar.sync %0, %1;" ::"r"(bar), "r"(nthr) : "memory");
@@ -894,7 +915,7 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 // The item's stream has T rows from step row row0 on, after `before` cached
 // positions, in cache `kv`.  Its partials are stored under step rows (row0 + t) * G + jh.
 template <bool F16, int RP>
-__device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
+__device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
                                        const float* rope, int l, int chunk, int h, long long q0, int T, int before,
                                        int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
                                        int mark_k) {
@@ -903,8 +924,6 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
     const int lane = threadIdx.x & 31, nthr = wpi * 32;
     const int kv_len = before + T, NQ = T * G;
     const int p0 = chunk * kPage, n_pos = min(kPage, kv_len - p0);
-    float* sq = reinterpret_cast<float*>(region);                         // [32][128] query rows
-    float2* sw = reinterpret_cast<float2*>(region + 32 * kHeadDim * 4);   // [32][64] exp weights, doubled
     const LayerWeights& w = a.layers[l];
     const int ldq = (nh + 2 * nkv) * kHeadDim;
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // query rows of this warp
@@ -973,14 +992,14 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 }
 
 template <bool F16>
-__device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, uint8_t* region,
+__device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
                                           const float* rope, int l, int chunk, int h, long long q0, int T, int before,
                                           int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
                                           int mark_k) {
     const int NQ = T * (a.d.n_heads / a.d.n_kv);
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
 #define MTB_ATTN_BODY(RP) \
-    attn_body<F16, RP>(a, ring, full, region, rope, l, chunk, h, q0, T, before, row0, kv, wl, wpi, bar, mark_pid, mark_k)
+    attn_body<F16, RP>(a, ring, full, sq, sw, rope, l, chunk, h, q0, T, before, row0, kv, wl, wpi, bar, mark_pid, mark_k)
     if (R <= 1) return MTB_ATTN_BODY(1);
     if (R == 2) return MTB_ATTN_BODY(2);
     if (R <= 4) return MTB_ATTN_BODY(4);
@@ -1011,6 +1030,7 @@ struct KCtx {
     // Per stream: rows, first step row, cached positions, attention chunks.
     int s_T[kMaxStreams], s_row0[kMaxStreams], s_before[kMaxStreams], s_chunks[kMaxStreams];
     int row_stream[kTMax];  // stream of each step row
+    int attn_wpi;           // warps per attention item: 2 when every stream has <= 2 query rows per kv head (fp16 KV)
 };
 
 __device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
@@ -1094,37 +1114,43 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
                         });
 }
 
-// B: attention items of this CTA in stream order, two at a time (four warps
-// each, named barriers 2 and 3) while two are left, else one over all eight.
+// B: attention items of this CTA in stream order, by independent groups of
+// wpi warps (named barrier 2 + group): group g takes the CTA's items g,
+// g + groups, ... and, as soon as an item is done, releases its ring slots and
+// counts it for its head's merge.  Four groups of two warps when every stream
+// has at most 2 query rows per kv head (four fp16 items fill the ring), else
+// two groups of four.
 __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, int pid) {
     const MegaArgs& a = c.a;
     const PhaseInfo pi = c.sch.take(W_ATTN, &cur[0], &cur[1]);
-    const int nkv = a.d.n_kv, warp = threadIdx.x >> 5;
+    const int nkv = a.d.n_kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int wpi = c.attn_wpi, n_groups = kConsumerWarps / wpi, g = warp / wpi, wl = warp % wpi;
+    const int rows_cap = wpi == 2 ? 4 : 32;
+    uint8_t* scratch = c.region + (size_t)g * rows_cap * kAttnRowBytes;
+    float* sq = reinterpret_cast<float*>(scratch);
+    float2* sw = reinterpret_cast<float2*>(scratch + (size_t)rows_cap * kHeadDim * 4);
     bool ok = true;
-    for (int j = 0; j < pi.count; j += 2) {
-        const int n_now = min(2, pi.count - j), wpi = kConsumerWarps / n_now;
-        const int sub = warp / wpi, wl = warp % wpi;
-        const int item = pi.first + (j + sub) * gridDim.x;
+    for (int j = g; j < pi.count; j += n_groups) {
         int si, chunk, h;
-        c.sch.attn_item_of(item, &si, &chunk, &h);
-        const long long q0 = pi.slot0 + (long long)(j + sub) * pi.slots;
-        uint8_t* region = c.region + sub * kAttnRegion;
-        const int mp = j == 0 && sub == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
+        c.sch.attn_item_of(pi.first + j * gridDim.x, &si, &chunk, &h);
+        const long long q0 = pi.slot0 + (long long)j * pi.slots;
+        const int mp = j == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
-                              ? attn_item<true>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.s_T[si],
-                                                c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + sub, mp, mk)
-                              : attn_item<false>(a, c.ring, c.full, region, c.rope, l, chunk, h, q0, c.s_T[si],
-                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + sub, mp, mk);
+                              ? attn_item<true>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
+                                                c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + g, mp, mk)
+                              : attn_item<false>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
+                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + g, mp, mk);
         ok = ok && good;
-        consumer_sync();
-        if (threadIdx.x < n_now * pi.slots) mbar_arrive(&c.empty[(pi.slot0 + (long long)j * pi.slots + threadIdx.x) % kRingSlots]);
-        if (threadIdx.x < n_now) {
-            // The items' partials are written (named barrier above): count them
-            // for their heads' merges (release: cumulative over the CTA's stores).
-            int s2, c2, h2;
-            c.sch.attn_item_of(pi.first + (j + threadIdx.x) * gridDim.x, &s2, &c2, &h2);
-            unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + s2) * nkv + h2;
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+        // The group is done with the slots and its partials are stored: free
+        // the slots, and count the item for its head's merge (release:
+        // cumulative over the group's stores, ordered by the named barrier).
+        item_sync(2 + g, wpi * 32);
+        if (wl == 0) {
+            if (lane < pi.slots) mbar_arrive(&c.empty[(q0 + lane) % kRingSlots]);
+            if (lane == 0) {
+                unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + si) * nkv + h;
+                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+            }
         }
         mark(a.timeline, mp, mk + 3);
     }
@@ -1586,6 +1612,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
             rows += T;
         }
         c.T = rows;
+        int max_nq = 0;
+        for (int si = 0; si < args.n_streams; ++si) max_nq = max(max_nq, c.s_T[si] * (args.d.n_heads / args.d.n_kv));
+        c.attn_wpi = max_nq <= 4 && args.st_kv[0].type == KV_F16 ? 2 : 4;
         c.sch.init(args.d, gridDim.x, blockIdx.x, args.st_kv[0].type == KV_F16, c.s_chunks, args.n_streams,
                    args.lm_tiles != nullptr);
         c.ring = smem;
@@ -1670,7 +1699,7 @@ bool megakernel_supports(const ModelDims& d, int grid) {
                                            need(qd, d.hidden / kTileRows, qd / 256)),
                                   std::max(need(d.hidden, d.ffn / 32, 8 * d.hidden / 256) + 16 * 32 * 4,
                                            need(d.ffn, d.hidden / kTileRows, d.ffn / 256)));
-    const size_t attn = (size_t)2 * kAttnRegion;  // two items at a time
+    const size_t attn = (size_t)2 * 32 * kAttnRowBytes;  // two groups of up to 32 query rows
     return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
 }
 
