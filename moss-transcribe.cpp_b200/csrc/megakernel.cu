@@ -294,8 +294,8 @@ __device__ __forceinline__ uint8_t* kv_row(uint8_t* ring, long long q0, int whic
 // ------------------------------------------------------------------ producer
 
 // The producer warp: lane 0 waits for free slots and posts the expected bytes;
-// a weight item slot is one bulk copy (lane 0), an attention slot one bulk
-// copy per K/V row (one row per lane, the padded row stride above).
+// a weight item slot is one bulk copy (lane 0), an attention slot 16-byte
+// cp.async copies over all lanes into the padded rows above.
 __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, uint64_t* full, uint64_t* empty) {
     const int lane = threadIdx.x & 31;
     long long q = 0;  // ring slot sequence number
@@ -312,8 +312,17 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
         int first = 0;
         const int cnt = sch.count_of(sch.n[kind], rot, &first);
         const int slots = sch.slots_of(kind);
+        long long lane_off = 0;  // attention: cache offset of item (j & ~31) + lane's K block
         for (int j = 0; j < cnt && ok; ++j) {
             const int item = first + j * sch.grid;
+            if (kind == W_ATTN && (j & 31) == 0 && j + lane < cnt) {
+                // The next 32 items' page-table lookups at once, one per lane
+                // (one at a time they would serialise the copies behind them).
+                int si, chunk, h;
+                sch.attn_item_of(first + (j + lane) * sch.grid, &si, &chunk, &h);
+                lane_off = kv_offset(a.st_kv[si], sch.nkv, layer, 0, h, chunk * kPage);
+            }
+            const long long item_off = __shfl_sync(0xffffffffu, lane_off, j & 31);
             for (int k = 0; k < slots; ++k, ++q) {
                 const int s = int(q % kRingSlots);
                 const long long use = q / kRingSlots;
@@ -325,14 +334,14 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                     // The slot's rps rows (contiguous in the cache page) into
                     // padded shared rows: 16-byte copies over all lanes, each
                     // lane's completion one pending arrival on the slot's
-                    // barrier, then the slot's own arrival.  (Many small bulk
-                    // copies would queue in the copy engine: one per row.)
+                    // barrier, then the slot's own arrival.  (One bulk copy per
+                    // 256-byte row streamed 4x slower under load.)
                     const int half = slots / 2, which = k / half, r0 = (k % half) * rps;
                     int si, chunk, h;
                     sch.attn_item_of(item, &si, &chunk, &h);
-                    const KvCache& kvs = a.st_kv[si];
-                    const long long off = kv_offset(kvs, sch.nkv, layer, which, h, chunk * kPage + r0);
-                    const uint8_t* src = static_cast<const uint8_t*>(kvs.base) + off * (sch.kv_f16 ? 2 : 4);
+                    // Rows of one (layer, K/V, head) page block are contiguous.
+                    const long long off = item_off + ((long long)which * sch.nkv * kPage + r0) * kHeadDim;
+                    const uint8_t* src = static_cast<const uint8_t*>(a.st_kv[si].base) + off * (sch.kv_f16 ? 2 : 4);
                     const int segs = row_bytes / 16;
                     for (int i = lane; i < rps * segs; i += 32) {
                         const int rr = i / segs, sg = i % segs;
