@@ -51,6 +51,7 @@ struct mtb_decoder {
     cudaStream_t stream = nullptr;
     int max_seq = 0, kv_type = 0, max_new = 0;
     KvCache kv{};
+    KvTensorMap kv_map{};  // the cache for the persistent kernel's TMA tiles
     StepBuffers b{};
     MegaBuffers mb{};
     PrefillBuffers pf{};
@@ -275,8 +276,9 @@ int refresh(mtb_decoder* d) {
     MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
     if (d->h_state->error) {
-        d->error = d->h_state->error == 2 ? "verify step gave up waiting (persistent kernel timeout)"
-                                          : "device reported an out-of-range token id";
+        d->error = d->h_state->error == 2   ? "verify step gave up waiting (persistent kernel timeout)"
+                   : d->h_state->error == 3 ? "persistent kernel: shared-memory ring not 1024-byte aligned"
+                                            : "device reported an out-of-range token id";
         return -1;
     }
     return 0;
@@ -296,7 +298,8 @@ cudaGraphExec_t step_graph(mtb_decoder* d, int mode, bool penalty) {
     if (d->model->mega_grid > 0 && !penalty) {
         // Draft, then the whole verify step as one persistent kernel.
         launch_draft(d->b, mode, d->stream);
-        launch_step_persistent(d->model->dm, d->model->layers_dev, d->kv, d->b, d->mb, d->model->mega_grid, d->stream);
+        launch_step_persistent(d->model->dm, d->model->layers_dev, d->kv, d->kv_map, d->b, d->mb, d->model->mega_grid,
+                               d->stream);
     } else {
         launch_step(d->model->dm, d->kv, d->b, mode, penalty, d->stream);
     }
@@ -638,6 +641,10 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             cudaMemset(kvb, 0, size_t(n_pages) * d->kv.page_elems * esz) != cudaSuccess ||
             cudaMemset(b.state, 0, sizeof(StepState)) != cudaSuccess) {
             d->error = "device initialisation failed";
+            return bail();
+        }
+        if (m->mega_grid > 0 && encode_kv_map(d->kv, (long long)n_pages * d->kv.page_elems, &d->kv_map) != cudaSuccess) {
+            d->error = "could not encode the KV cache tensor map";
             return bail();
         }
         if (cudaMallocHost(&d->h_state, sizeof(StepState)) != cudaSuccess ||
@@ -997,6 +1004,7 @@ int check_group(mtb_decoder* const* ds, int n) {
 int group_step(mtb_decoder* const* ds, int n) {
     mtb_decoder* d0 = ds[0];
     KvCache kvs[kMaxStreams];
+    KvTensorMap maps[kMaxStreams];
     StepState* states[kMaxStreams];
     int32_t* ids[kMaxStreams];
     for (int i = 1; i < n; ++i) {
@@ -1006,12 +1014,13 @@ int group_step(mtb_decoder* const* ds, int n) {
     for (int i = 0; i < n; ++i) {
         launch_draft(ds[i]->b, 0, d0->stream);
         kvs[i] = ds[i]->kv;
+        maps[i] = ds[i]->kv_map;
         states[i] = ds[i]->b.state;
         ids[i] = ds[i]->b.ids;
     }
     const mtb_model* m = d0->model;
-    MTB_CK(d0, launch_step_persistent_group(m->dm, m->layers_dev, kvs, states, ids, n, d0->b, d0->mb, m->mega_grid,
-                                            d0->stream));
+    MTB_CK(d0, launch_step_persistent_group(m->dm, m->layers_dev, kvs, maps, states, ids, n, d0->b, d0->mb,
+                                            m->mega_grid, d0->stream));
     MTB_CK(d0, cudaEventRecord(d0->group_ev, d0->stream));
     for (int i = 1; i < n; ++i) MTB_CK(d0, cudaStreamWaitEvent(ds[i]->stream, d0->group_ev, 0));
     return 0;

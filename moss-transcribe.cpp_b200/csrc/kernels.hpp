@@ -113,15 +113,25 @@ int lm_head_blocks(int vocab);
 int megakernel_smem_bytes();
 cudaError_t configure_megakernel(int device, int hidden, int* grid_out);
 bool megakernel_supports(const ModelDims& d, int grid);
+// TMA tensor map of a KV cache (an opaque CUtensorMap, kept by the decoder).
+struct alignas(64) KvTensorMap {
+    unsigned char bytes[128];
+};
+// The map the persistent kernel streams K/V chunk rows with: the cache pool
+// (pool_elems elements from kv.base) as [rows][row bytes], swizzled boxes.
+cudaError_t encode_kv_map(const KvCache& kv, long long pool_elems, KvTensorMap* out);
+
 cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
-                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s);
+                                   const KvTensorMap& map, const StepBuffers& b, const MegaBuffers& mb, int grid,
+                                   cudaStream_t s);
 // One persistent launch verifying n_streams decoders of the same model (one
 // KV cache, step state and id array each; their drafted rows together at most
 // kTMax, the proposals beyond that cut in stream order), with b's activation
 // buffers and mb's counters.
 cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache* kvs,
-                                         StepState* const* states, int32_t* const* ids, int n_streams,
-                                         const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s);
+                                         const KvTensorMap* maps, StepState* const* states, int32_t* const* ids,
+                                         int n_streams, const StepBuffers& b, const MegaBuffers& mb, int grid,
+                                         cudaStream_t s);
 // The draft part of a step alone (0: on-device n-gram, 1: host-forced proposal).
 void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s);
 cudaError_t configure_kernels();

@@ -5,7 +5,7 @@
 // Here every operation is a phase of one kernel, phases are separated by grid
 // barriers, and one producer warp per CTA streams every weight tile the CTA
 // will need (all layers, then the LM head) through a ring of shared-memory
-// slots with cp.async.bulk + mbarriers.  Weights do not depend on the step's
+// slots with cp.async.bulk (weights) and TMA tensor tiles (K/V) + mbarriers.  Weights do not depend on the step's
 // activations, so HBM keeps streaming while the consumer warps wait at
 // barriers; the consumers find their tiles already in shared memory.
 //
@@ -31,9 +31,12 @@
 // a time limit; on expiry the kernel records an error in the step state,
 // raises an abort flag that every other wait watches, drains its own bulk
 // copies and returns.
+#include <cuda.h>
+
 #include "device_common.cuh"
 
 #include <algorithm>
+#include <cstring>
 
 namespace mtb {
 namespace {
@@ -145,16 +148,6 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
 }
 
-// 16-byte asynchronous copy global -> shared (L2 only), tracked per thread.
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
-}
-
-// One pending arrival on `b` that lands when this thread's earlier cp.async copies have.
-__device__ __forceinline__ void cp_async_arrive(uint64_t* b) {
-    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(b)) : "memory");
-}
-
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -172,6 +165,15 @@ __device__ __forceinline__ void mark(unsigned long long* timeline, int b, int k)
     if (k < kCtaMarks) timeline[kCtaMarkBase + ((size_t)blockIdx.x * kMaxBarriers + b) * kCtaMarks + k] = t;
 }
 
+// 2-D TMA tensor tile (box of the map) at coordinates (x, y) into shared
+// memory, completing bytes on mbarrier b.  No multicast.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* b) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(smem_addr(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_addr(b))
+        : "memory");
+}
+
 // ------------------------------------------------------------------ schedule
 
 // Streamed phases in ring order: per layer A (QKV rows), B (the K/V rows of
@@ -182,17 +184,29 @@ __device__ __forceinline__ void mark(unsigned long long* timeline, int b, int k)
 enum WPhase { W_QKV = 0, W_ATTN = 1, W_O = 2, W_GU = 3, W_DOWN = 4, W_LM = 5 };
 constexpr int kLayerPhases = 5;
 
-// An attention item's K and V chunk rows in the ring: 64 rows each, row stride
-// 272 bytes for fp16 (256 + 16: 16-byte reads of 8 consecutive rows hit 8
-// different bank quads) and 528 for f32; 32 or 16 rows per slot, so one item
-// takes 4 (fp16) or 8 (f32) slots: K rows first, then V rows.
+// An attention item's K and V chunk rows in the ring: 64 rows each, 32 (fp16)
+// or 16 (f32) rows per slot, so one item takes 4 (fp16) or 8 (f32) slots: K
+// rows first, then V rows.  A slot holds its rows as 128-byte boxes (bytes
+// [128 b, 128 b + 128) of every row, box after box), each written by one TMA
+// tensor tile copy with the 128-byte swizzle: 16-byte chunk c of row p sits
+// at chunk c ^ (p & 7) of the row's 128 bytes, so 16-byte reads of one chunk
+// of 8 consecutive rows hit 8 different bank quads.  The boxes start at the
+// slot's first 1024-byte boundary (the swizzle's alignment): slots are
+// kSlotBytes = 8.5 KB apart in a 1024-aligned ring, so at +0 (even slots) or
+// +512 (odd slots), and 8 KB of boxes fit either way.
 template <bool F16>
 struct KvSlots {
     static constexpr int kRowBytes = F16 ? 256 : 512;
-    static constexpr int kRowStride = kRowBytes + 16;
     static constexpr int kRowsPerSlot = F16 ? 32 : 16;
     static constexpr int kSlotsPerHalf = kPage / kRowsPerSlot;
+    static constexpr int kBoxBytes = kRowsPerSlot * 128;
+    static constexpr int kBoxes = kRowBytes / 128;
 };
+
+// The K/V boxes of ring slot s.
+__device__ __forceinline__ uint8_t* kv_slot_base(uint8_t* ring, int s) {
+    return ring + (size_t)s * kSlotBytes + (s & 1) * 512;
+}
 
 struct PhaseInfo {
     int n_items;    // items in the phase
@@ -282,29 +296,33 @@ struct Schedule {
     }
 };
 
-// Row r (0..63) of the K (which = 0) or V (which = 1) rows of the attention
-// item whose slots start at sequence number q0.
+// 16-byte chunk c (0 .. kRowBytes / 16 - 1) of row r (0..63) of the K (which
+// = 0) or V (which = 1) rows of the attention item whose slots start at
+// sequence number q0.
 template <bool F16>
-__device__ __forceinline__ uint8_t* kv_row(uint8_t* ring, long long q0, int which, int r) {
+__device__ __forceinline__ uint8_t* kv_chunk(uint8_t* ring, long long q0, int which, int r, int c) {
     using KS = KvSlots<F16>;
     const long long q = q0 + which * KS::kSlotsPerHalf + r / KS::kRowsPerSlot;
-    return ring + (size_t)(q % kRingSlots) * kSlotBytes + (r % KS::kRowsPerSlot) * KS::kRowStride;
+    const int p = r % KS::kRowsPerSlot;
+    return kv_slot_base(ring, int(q % kRingSlots)) + (c >> 3) * KS::kBoxBytes + p * 128 + (((c & 7) ^ (p & 7)) << 4);
 }
 
 // ------------------------------------------------------------------ producer
 
-// The producer warp: lane 0 waits for free slots and posts the expected bytes;
-// a weight item slot is one bulk copy (lane 0), an attention slot 16-byte
-// cp.async copies over all lanes into the padded rows above.
-__device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, uint64_t* full, uint64_t* empty) {
+// The producer warp: lane 0 waits for free slots, posts the expected bytes
+// and issues the copies: a weight item slot is one bulk copy, an attention
+// slot one TMA tile per 128-byte box of its rows (kv_maps[stream]: the
+// stream's cache as [rows][row bytes], box [rows per slot][128], swizzled).
+__device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Schedule& sch, uint8_t* ring,
+                         uint64_t* full, uint64_t* empty) {
     const int lane = threadIdx.x & 31;
     long long q = 0;  // ring slot sequence number
     const int n_phases = sch.L * kLayerPhases + 1;
     bool ok = true;
     long long items_before = 0;
-    const int row_bytes = sch.kv_f16 ? KvSlots<true>::kRowBytes : KvSlots<false>::kRowBytes;
-    const int row_stride = sch.kv_f16 ? KvSlots<true>::kRowStride : KvSlots<false>::kRowStride;
     const int rps = sch.kv_f16 ? KvSlots<true>::kRowsPerSlot : KvSlots<false>::kRowsPerSlot;
+    const int n_box = sch.kv_f16 ? KvSlots<true>::kBoxes : KvSlots<false>::kBoxes;
+    const int box_bytes = sch.kv_f16 ? KvSlots<true>::kBoxBytes : KvSlots<false>::kBoxBytes;
     for (int p = 0; p < n_phases && ok; ++p) {
         const int kind = p < sch.L * kLayerPhases ? p % kLayerPhases : W_LM;
         const int layer = p / kLayerPhases;
@@ -312,7 +330,7 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
         int first = 0;
         const int cnt = sch.count_of(sch.n[kind], rot, &first);
         const int slots = sch.slots_of(kind);
-        long long lane_off = 0;  // attention: cache offset of item (j & ~31) + lane's K block
+        long long lane_row = 0;  // attention: cache row of item (j & ~31) + lane's K block
         for (int j = 0; j < cnt && ok; ++j) {
             const int item = first + j * sch.grid;
             if (kind == W_ATTN && (j & 31) == 0 && j + lane < cnt) {
@@ -320,9 +338,9 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                 // (one at a time they would serialise the copies behind them).
                 int si, chunk, h;
                 sch.attn_item_of(first + (j + lane) * sch.grid, &si, &chunk, &h);
-                lane_off = kv_offset(a.st_kv[si], sch.nkv, layer, 0, h, chunk * kPage);
+                lane_row = kv_offset(a.st_kv[si], sch.nkv, layer, 0, h, chunk * kPage) / kHeadDim;
             }
-            const long long item_off = __shfl_sync(0xffffffffu, lane_off, j & 31);
+            const long long item_row = __shfl_sync(0xffffffffu, lane_row, j & 31);
             for (int k = 0; k < slots; ++k, ++q) {
                 const int s = int(q % kRingSlots);
                 const long long use = q / kRingSlots;
@@ -331,25 +349,17 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
                 if (!__shfl_sync(0xffffffffu, good, 0)) { ok = false; break; }
                 uint8_t* dst = ring + (size_t)s * kSlotBytes;
                 if (kind == W_ATTN) {
-                    // The slot's rps rows (contiguous in the cache page) into
-                    // padded shared rows: 16-byte copies over all lanes, each
-                    // lane's completion one pending arrival on the slot's
-                    // barrier, then the slot's own arrival.  (One bulk copy per
-                    // 256-byte row streamed 4x slower under load.)
-                    const int half = slots / 2, which = k / half, r0 = (k % half) * rps;
-                    int si, chunk, h;
-                    sch.attn_item_of(item, &si, &chunk, &h);
-                    // Rows of one (layer, K/V, head) page block are contiguous.
-                    const long long off = item_off + ((long long)which * sch.nkv * kPage + r0) * kHeadDim;
-                    const uint8_t* src = static_cast<const uint8_t*>(a.st_kv[si].base) + off * (sch.kv_f16 ? 2 : 4);
-                    const int segs = row_bytes / 16;
-                    for (int i = lane; i < rps * segs; i += 32) {
-                        const int rr = i / segs, sg = i % segs;
-                        cp_async16(dst + rr * row_stride + sg * 16, src + (size_t)rr * row_bytes + sg * 16);
+                    if (lane == 0) {
+                        // The slot's rps rows: contiguous rows of one (layer,
+                        // K/V, head) block of the item's cache page.
+                        const int half = slots / 2, which = k / half, r0 = (k % half) * rps;
+                        int si, chunk, h;
+                        sch.attn_item_of(item, &si, &chunk, &h);
+                        const int y = int(item_row + (long long)which * sch.nkv * kPage + r0);
+                        uint8_t* boxes = kv_slot_base(ring, s);
+                        mbar_expect_tx(&full[s], unsigned(n_box * box_bytes));
+                        for (int b = 0; b < n_box; ++b) tma_load_2d(boxes + b * box_bytes, &kv_maps[si], b * 128, y, &full[s]);
                     }
-                    cp_async_arrive(&full[s]);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&full[s]);
                 } else if (lane == 0) {
                     const uint8_t* src = sch.item_src(a.layers, sch.lm_tc ? a.lm_tiles : a.embd, kind, layer, item);
                     const int off = k * kSlotBytes;
@@ -361,7 +371,6 @@ __device__ void producer(const MegaArgs& a, const Schedule& sch, uint8_t* ring, 
         }
         items_before += sch.n[kind];
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
     if (!ok && lane == 0) {
         atomicExch(a.abort_flag, 1);
         // Drain this CTA's copies still in flight before the CTA exits.
@@ -802,14 +811,19 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 #pragma unroll
     for (int rr = 0; rr < R; ++rr) acc[rr][0] = acc[rr][1] = make_float2(0.f, 0.f);
     {
-        const uint8_t* k0 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane);
-        const uint8_t* k1 = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 0, lane + 32);
+        // K rows of positions lane and lane + 32 (row lane % rows-per-slot of
+        // their slots; rows per slot divide 32, so both rows share the swizzle).
+        const int s0 = int(q0 % kRingSlots), pr = lane % KS::kRowsPerSlot, xs = lane & 7;
+        const uint8_t* ka_row = kv_slot_base(const_cast<uint8_t*>(ring), (s0 + lane / KS::kRowsPerSlot) % kRingSlots) + pr * 128;
+        const uint8_t* kb_row =
+            kv_slot_base(const_cast<uint8_t*>(ring), (s0 + (lane + 32) / KS::kRowsPerSlot) % kRingSlots) + pr * 128;
         constexpr int EB = F16 ? 8 : 4;  // dims per 16-byte read
 #pragma unroll 1
         for (int eb = 0; eb < kHeadDim / EB; ++eb) {
             float2 ka[EB / 2], kb[EB / 2];
-            const uint4 ua = *reinterpret_cast<const uint4*>(k0 + eb * 16);
-            const uint4 ub = *reinterpret_cast<const uint4*>(k1 + eb * 16);
+            const int off = (eb >> 3) * KS::kBoxBytes + (((eb & 7) ^ xs) << 4);
+            const uint4 ua = *reinterpret_cast<const uint4*>(ka_row + off);
+            const uint4 ub = *reinterpret_cast<const uint4*>(kb_row + off);
             if constexpr (F16) {
                 const __half2* ha = reinterpret_cast<const __half2*>(&ua);
                 const __half2* hb = reinterpret_cast<const __half2*>(&ub);
@@ -875,16 +889,22 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
             v23 = make_float2(f.z, f.w);
         }
     };
+    // Lane's 8 (fp16) or 16 (f32) bytes of V row p of a slot: chunk cv of
+    // the row, at the swizzled position.
+    const int cv = F16 ? lane >> 1 : lane, cc = cv & 7;
+    const int v_lane = (cv >> 3) * KS::kBoxBytes + (F16 ? (lane & 1) * 8 : 0);
+    const int s0v = int((q0 + KS::kSlotsPerHalf) % kRingSlots);
     for (int sidx = 0; sidx < KS::kSlotsPerHalf; ++sidx) {
         const int pb = sidx * KS::kRowsPerSlot;
-        const uint8_t* vs = kv_row<F16>(const_cast<uint8_t*>(ring), q0, 1, pb) + lane * (F16 ? 8 : 16);
         const int np = min(KS::kRowsPerSlot, n_pos - pb);
+        const uint8_t* vb = kv_slot_base(const_cast<uint8_t*>(ring), (s0v + sidx) % kRingSlots) + v_lane;
+        auto v_at = [&](int p) -> const uint8_t* { return vb + p * 128 + ((cc ^ (p & 7)) << 4); };
         int pr = 0;
 #pragma unroll 1
         for (; pr + 4 <= np; pr += 4) {
             float2 v[4][2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) load_v(vs + (pr + i) * KS::kRowStride, v[i][0], v[i][1]);
+            for (int i = 0; i < 4; ++i) load_v(v_at(pr + i), v[i][0], v[i][1]);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) {
                 const float4* wr = reinterpret_cast<const float4*>(sw + (wl + wpi * rr) * kPage + pb + pr);
@@ -901,7 +921,7 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 #pragma unroll 1
         for (; pr < np; ++pr) {
             float2 v01, v23;
-            load_v(vs + pr * KS::kRowStride, v01, v23);
+            load_v(v_at(pr), v01, v23);
 #pragma unroll
             for (int rr = 0; rr < R; ++rr) {
                 const float2 w = sw[(wl + wpi * rr) * kPage + pb + pr];
@@ -979,14 +999,15 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
                 for (int q = 0; q < 4; ++q) o[q] = x[q];
             }
             const long long off = kv_offset(kv, nkv, l, which, h, p0 + r);
-            uint8_t* row = kv_row<F16>(ring, q0, which, r);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 kv_store(kv, off + 32 * q + lane, o[q]);
+                const int e = 32 * q + lane;  // element of the row
                 if constexpr (F16)
-                    reinterpret_cast<__half*>(row)[32 * q + lane] = __float2half_rn(o[q]);
+                    *reinterpret_cast<__half*>(kv_chunk<true>(ring, q0, which, r, e >> 3) + (e & 7) * 2) =
+                        __float2half_rn(o[q]);
                 else
-                    reinterpret_cast<float*>(row)[32 * q + lane] = o[q];
+                    *reinterpret_cast<float*>(kv_chunk<false>(ring, q0, which, r, e >> 2) + (e & 3) * 4) = o[q];
             }
         }
         // Order these generic-proxy stores before the producer's next bulk copies into the slots.
@@ -1011,8 +1032,7 @@ __device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint
     attn_body<F16, RP>(a, ring, full, sq, sw, rope, l, chunk, h, q0, T, before, row0, kv, wl, wpi, bar, mark_pid, mark_k)
     if (R <= 1) return MTB_ATTN_BODY(1);
     if (R == 2) return MTB_ATTN_BODY(2);
-    if (R <= 4) return MTB_ATTN_BODY(4);
-    return MTB_ATTN_BODY(8);
+    return MTB_ATTN_BODY(4);  // R <= 4: see KCtx::attn_wpi
 #undef MTB_ATTN_BODY
 }
 
@@ -1039,7 +1059,10 @@ struct KCtx {
     // Per stream: rows, first step row, cached positions, attention chunks.
     int s_T[kMaxStreams], s_row0[kMaxStreams], s_before[kMaxStreams], s_chunks[kMaxStreams];
     int row_stream[kTMax];  // stream of each step row
-    int attn_wpi;           // warps per attention item: 2 when every stream has <= 2 query rows per kv head (fp16 KV)
+    // Warps per attention item: 2 when every stream has <= 4 query rows per kv
+    // head (fp16 KV), 8 above 16, else 4 -- so a warp never holds more than 4
+    // query rows (more would raise the whole kernel's register pressure).
+    int attn_wpi;
 };
 
 __device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
@@ -1127,8 +1150,8 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
 // wpi warps (named barrier 2 + group): group g takes the CTA's items g,
 // g + groups, ... and, as soon as an item is done, releases its ring slots and
 // counts it for its head's merge.  Four groups of two warps when every stream
-// has at most 2 query rows per kv head (four fp16 items fill the ring), else
-// two groups of four.
+// has at most 4 query rows per kv head (four fp16 items fill the ring), one of
+// eight above 16 rows, else two groups of four.
 __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, int pid) {
     const MegaArgs& a = c.a;
     const PhaseInfo pi = c.sch.take(W_ATTN, &cur[0], &cur[1]);
@@ -1582,9 +1605,16 @@ __device__ __noinline__ void run_phases(const KCtx& c) {
     if (blockIdx.x == 0) phase_accept(c);
 }
 
+// Tensor maps of the streams' KV caches (a kernel parameter: TMA reads them
+// from parameter space).
+struct KvMaps {
+    CUtensorMap m[kMaxStreams];
+};
+
 template <int kNK>
-__global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs args) {
-    extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(kMegaThreads, 1)
+    k_verify_persistent(MegaArgs args, const __grid_constant__ KvMaps kv_maps) {
+    extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ KCtx s_ctx;
     __shared__ double s_wsum[kConsumerWarps * kTMax];
     __shared__ float s_scale[kTMax * 4];
@@ -1623,7 +1653,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
         c.T = rows;
         int max_nq = 0;
         for (int si = 0; si < args.n_streams; ++si) max_nq = max(max_nq, c.s_T[si] * (args.d.n_heads / args.d.n_kv));
-        c.attn_wpi = max_nq <= 4 && args.st_kv[0].type == KV_F16 ? 2 : 4;
+        c.attn_wpi = max_nq <= 4 && args.st_kv[0].type == KV_F16 ? 2 : max_nq > 16 ? 8 : 4;
         c.sch.init(args.d, gridDim.x, blockIdx.x, args.st_kv[0].type == KV_F16, c.s_chunks, args.n_streams,
                    args.lm_tiles != nullptr);
         c.ring = smem;
@@ -1651,8 +1681,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) k_verify_persistent(MegaArgs 
     __syncthreads();
     const KCtx& c = s_ctx;
     if (c.T <= 0) return;
+    if (smem_addr(smem) & 1023) {  // the K/V boxes need a 1024-aligned ring
+        if (threadIdx.x == 0 && blockIdx.x == 0) args.st_state[0]->error = 3;
+        return;
+    }
     if (warp == kConsumerWarps) {
-        producer(c.a, c.sch, c.ring, c.full, c.empty);
+        producer(c.a, kv_maps.m, c.sch, c.ring, c.full, c.empty);
         return;
     }
     if (c.T <= 8)
@@ -1712,10 +1746,47 @@ bool megakernel_supports(const ModelDims& d, int grid) {
     return worst <= (size_t)kRegionBytes && attn <= (size_t)kRegionBytes;
 }
 
+static_assert(sizeof(KvTensorMap) == sizeof(CUtensorMap) && alignof(KvTensorMap) >= alignof(CUtensorMap),
+              "KvTensorMap holds a CUtensorMap");
+
+cudaError_t encode_kv_map(const KvCache& kv, long long pool_elems, KvTensorMap* out) {
+    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    const bool f16 = kv.type == KV_F16;
+    const int row_bytes = f16 ? KvSlots<true>::kRowBytes : KvSlots<false>::kRowBytes;
+    const int rps = f16 ? KvSlots<true>::kRowsPerSlot : KvSlots<false>::kRowsPerSlot;
+    const long long rows = pool_elems / kHeadDim;
+    if (rows >= (1ll << 31)) return cudaErrorInvalidValue;  // tile row coordinates are int32
+    // The cache as bytes [rows][row_bytes]; a box is [rps rows][128 bytes].
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box[2] = {128, (cuuint32_t)rps}, elem_strides[2] = {1, 1};
+    CUtensorMap map;
+    const CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv.base, dims, strides, box, elem_strides,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    std::memcpy(out, &map, sizeof(map));
+    return cudaSuccess;
+}
+
 cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache* kvs,
-                                         StepState* const* states, int32_t* const* ids, int n_streams,
-                                         const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+                                         const KvTensorMap* maps, StepState* const* states, int32_t* const* ids,
+                                         int n_streams, const StepBuffers& b, const MegaBuffers& mb, int grid,
+                                         cudaStream_t s) {
     if (n_streams < 1 || n_streams > kMaxStreams) return cudaErrorInvalidValue;
+    KvMaps km;
+    std::memset(&km, 0, sizeof(km));
+    for (int i = 0; i < n_streams; ++i) std::memcpy(&km.m[i], &maps[i], sizeof(CUtensorMap));
     MegaArgs a{};
     a.timeline = mb.timeline;
     a.d = m.dims;
@@ -1759,17 +1830,18 @@ cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeight
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     switch (m.dims.hidden) {
-        case 256: return cudaLaunchKernelEx(&cfg, k_verify_persistent<1>, a);
-        case 512: return cudaLaunchKernelEx(&cfg, k_verify_persistent<2>, a);
-        default: return cudaLaunchKernelEx(&cfg, k_verify_persistent<4>, a);
+        case 256: return cudaLaunchKernelEx(&cfg, k_verify_persistent<1>, a, km);
+        case 512: return cudaLaunchKernelEx(&cfg, k_verify_persistent<2>, a, km);
+        default: return cudaLaunchKernelEx(&cfg, k_verify_persistent<4>, a, km);
     }
 }
 
 cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* layers_dev, const KvCache& kv,
-                                   const StepBuffers& b, const MegaBuffers& mb, int grid, cudaStream_t s) {
+                                   const KvTensorMap& map, const StepBuffers& b, const MegaBuffers& mb, int grid,
+                                   cudaStream_t s) {
     StepState* state = b.state;
     int32_t* ids = b.ids;
-    return launch_step_persistent_group(m, layers_dev, &kv, &state, &ids, 1, b, mb, grid, s);
+    return launch_step_persistent_group(m, layers_dev, &kv, &map, &state, &ids, 1, b, mb, grid, s);
 }
 
 }  // namespace mtb

@@ -85,3 +85,38 @@ def test_verify_microbench_step_bit_exact(full_oracle, full_gpu, T):
     assert got == chain[:keep + 2]
     assert c["past_len"] == 2048 + keep + 1
     assert c["rewinds"] == (1 if T > keep + 1 else 0)
+
+
+def test_config4_long_context_step_bit_exact(full_oracle, full_gpu):
+    """configs[3] context length: a 30-minute recording leaves ~27k cached
+    positions (22,500 audio rows + markers + decoded ids).  KV filled to
+    27,000 positions with synthetic fp16 values; one T = 8 verify step (423
+    attention chunks per head) through the persistent kernel: hidden rows bit
+    for bit equal to the oracle, then the accept/rollback of a half-right
+    draft."""
+    KV, T = 27000, 8
+    V = full_oracle.shape.vocab
+    od = oracle.OracleDecoder(full_oracle, KV + 16, kv_fp16=True)
+    gd = capi.Decoder(full_gpu, KV + 16, capi.KV_F16, max_new=16)
+    od.fill_synthetic_kv(KV, 4321)
+    gd.fill_synthetic_kv(KV, 4321)
+    np.testing.assert_array_equal(gd.kv(27, 0, KV - 40, 40), od.kv(27, 0, KV - 40, 40))
+    seed = int(fixture.lcg_ids(1, V, seed=7)[0])
+    keep = (T - 1) // 2
+    chain = [seed]
+    for _ in range(keep + 1):
+        h = od.run(full_oracle.embed([chain[-1]]))
+        chain.append(int(np.argmax(od.logits(h[0]))))
+    draft = chain[1:1 + keep] + [(chain[1 + keep] + 1 + i) % V for i in range(T - 1 - keep)]
+    od.rewind(KV)
+    inputs = [seed] + draft
+    oh = od.run(full_oracle.embed(inputs))
+    gh = gd.run(full_oracle.embed(inputs))
+    np.testing.assert_array_equal(gh, oh)
+    gd.rewind(KV)
+    gd.resume([seed], KV, 16, -1, k_max=15)
+    c = gd.spec_step(draft)
+    got, _ = gd.read_ids()
+    assert c["accepted"] == keep
+    assert got == chain[:keep + 2]
+    assert c["past_len"] == KV + keep + 1
