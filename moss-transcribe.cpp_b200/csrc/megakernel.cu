@@ -946,8 +946,8 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 template <bool F16, int RP>
 __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
                                        const float* rope, int l, int chunk, int h, long long q0, int T, int before,
-                                       int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
-                                       int mark_k) {
+                                       int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
+                                       int mark_pid, int mark_k) {
     using KS = KvSlots<F16>;
     const int nh = a.d.n_heads, nkv = a.d.n_kv, G = nh / nkv;
     const int lane = threadIdx.x & 31, nthr = wpi * 32;
@@ -957,9 +957,10 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
     const int ldq = (nh + 2 * nkv) * kHeadDim;
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // query rows of this warp
     // This warp's query rows: RMSNorm + RoPE of the raw projections (the
-    // same rows in every chunk item of the head; cheaper than a phase).  All
-    // rows' loads are issued first.
-    {
+    // same rows in every chunk item of the head; cheaper than a phase), unless
+    // the group's previous item had the same stream and head (q_cached: each
+    // warp's rows are still in sq).  All rows' loads are issued first.
+    if (!q_cached) {
         float x[RP][4];
 #pragma unroll
         for (int rr = 0; rr < RP; ++rr) {
@@ -1024,12 +1025,13 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 template <bool F16>
 __device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
                                           const float* rope, int l, int chunk, int h, long long q0, int T, int before,
-                                          int row0, const KvCache& kv, int wl, int wpi, int bar, int mark_pid,
-                                          int mark_k) {
+                                          int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
+                                          int mark_pid, int mark_k) {
     const int NQ = T * (a.d.n_heads / a.d.n_kv);
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
 #define MTB_ATTN_BODY(RP) \
-    attn_body<F16, RP>(a, ring, full, sq, sw, rope, l, chunk, h, q0, T, before, row0, kv, wl, wpi, bar, mark_pid, mark_k)
+    attn_body<F16, RP>(a, ring, full, sq, sw, rope, l, chunk, h, q0, T, before, row0, kv, q_cached, wl, wpi, bar, \
+                       mark_pid, mark_k)
     if (R <= 1) return MTB_ATTN_BODY(1);
     if (R == 2) return MTB_ATTN_BODY(2);
     return MTB_ATTN_BODY(4);  // R <= 4: see KCtx::attn_wpi
@@ -1162,16 +1164,21 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
     float* sq = reinterpret_cast<float*>(scratch);
     float2* sw = reinterpret_cast<float2*>(scratch + (size_t)rows_cap * kHeadDim * 4);
     bool ok = true;
+    int prev = -1;  // stream * n_kv + head of the group's previous item
     for (int j = g; j < pi.count; j += n_groups) {
         int si, chunk, h;
         c.sch.attn_item_of(pi.first + j * gridDim.x, &si, &chunk, &h);
+        const bool q_cached = prev == si * nkv + h;
+        prev = si * nkv + h;
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int mp = j == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
                               ? attn_item<true>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
-                                                c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + g, mp, mk)
+                                                c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
+                                                mp, mk)
                               : attn_item<false>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
-                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], wl, wpi, 2 + g, mp, mk);
+                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
+                                                 mp, mk);
         ok = ok && good;
         // The group is done with the slots and its partials are stored: free
         // the slots, and count the item for its head's merge (release:
