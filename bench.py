@@ -50,7 +50,7 @@ KV_BYTES_PER_POS = 114_688
 EMBED_BYTES_PER_ROW = 1_088
 # DRAM bytes (read + write) of one k_verify_persistent launch at this workload,
 # from the ncu capture summarised in profiles/k_verify_persistent_kv2048_t8_full.md.
-TRAFFIC_BYTES = 882_363_648
+TRAFFIC_BYTES = 884_756_480
 # configs[4] sample (multi-stream box throughput): recordings of 1500 audio rows
 # (the KV cache they leave, synthetic fp16), decoded with the device n-gram
 # draft at k = 8, on one GPU.
@@ -183,6 +183,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the prefill / multi_stream / long_context side measurements (profiling runs)")
     args = ap.parse_args()
     rank, local, world, dist, torch = dist_setup(args)
     from mtb import fixture
@@ -275,25 +277,27 @@ def main():
            "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
            "ms_per_step": e2e_s * 1e3 / n_e2e}
 
-    # ---- prefill: the prompt rows of configs[1] (375 audio + 32 text rows)
-    # through the public run() call, host rows in and hidden rows out; every
-    # layer over all rows at once with the projections on tcgen05.
-    pf_dec = capi.Decoder(model, PREFILL_ROWS + 64, capi.KV_F16, max_new=16)
-    pf_rows = np.random.default_rng(5).standard_normal((PREFILL_ROWS, model.hidden)).astype(np.float32)
-    pf_dec.run(pf_rows)
-    pf_times = []
-    for _ in range(5):
-        pf_dec.rewind(0)
-        t0 = time.perf_counter()
+    prefill = ms_line = lc_line = None
+    if not args.no_extras:
+        # ---- prefill: the prompt rows of configs[1] (375 audio + 32 text rows)
+        # through the public run() call, host rows in and hidden rows out; every
+        # layer over all rows at once with the projections on tcgen05.
+        pf_dec = capi.Decoder(model, PREFILL_ROWS + 64, capi.KV_F16, max_new=16)
+        pf_rows = np.random.default_rng(5).standard_normal((PREFILL_ROWS, model.hidden)).astype(np.float32)
         pf_dec.run(pf_rows)
-        pf_times.append(time.perf_counter() - t0)
-    pf_dec.close()
-    pf_s = statistics.median(pf_times)
-    ms_line = multi_stream(model, capi, fixture) if model.persistent_grid > 0 else None
-    lc_line = long_context(model, capi, seed_tok)
-    prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
-               "path": "prefill passes (tcgen05 q8_0 projections) + verify kernels for the last rows",
-               "timing": "host wall clock around run(), median of 5, host rows in, hidden rows out"}
+        pf_times = []
+        for _ in range(5):
+            pf_dec.rewind(0)
+            t0 = time.perf_counter()
+            pf_dec.run(pf_rows)
+            pf_times.append(time.perf_counter() - t0)
+        pf_dec.close()
+        pf_s = statistics.median(pf_times)
+        ms_line = multi_stream(model, capi, fixture) if model.persistent_grid > 0 else None
+        lc_line = long_context(model, capi, seed_tok)
+        prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
+                   "path": "prefill passes (tcgen05 q8_0 projections) + verify kernels for the last rows",
+                   "timing": "host wall clock around run(), median of 5, host rows in, hidden rows out"}
 
     peak, peak_kind = measured_peaks()
     bytes_step = step_bytes(KV_LEN, T_ROWS)
