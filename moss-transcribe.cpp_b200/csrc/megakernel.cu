@@ -945,7 +945,7 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 // positions, in cache `kv`.  Its partials are stored under step rows (row0 + t) * G + jh.
 template <bool F16, int RP>
 __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
-                                       const float* rope, int l, int chunk, int h, long long q0, int T, int before,
+                                       const float* rope, const float* qk_norm, int l, int chunk, int h, long long q0, int T, int before,
                                        int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
                                        int mark_pid, int mark_k) {
     using KS = KvSlots<F16>;
@@ -953,7 +953,6 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
     const int lane = threadIdx.x & 31, nthr = wpi * 32;
     const int kv_len = before + T, NQ = T * G;
     const int p0 = chunk * kPage, n_pos = min(kPage, kv_len - p0);
-    const LayerWeights& w = a.layers[l];
     const int ldq = (nh + 2 * nkv) * kHeadDim;
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;  // query rows of this warp
     // This warp's query rows: RMSNorm + RoPE of the raw projections (the
@@ -974,7 +973,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
             if (rr < R) {
                 const int r = wl + wpi * rr, t = row0 + r / G;
                 float o[4];
-                norm_rope_row(x[rr], w.q_norm, a.d.eps, rope + t * 64 * 2, o);
+                norm_rope_row(x[rr], qk_norm, a.d.eps, rope + t * 64 * 2, o);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) sq[r * kHeadDim + 32 * q + lane] = o[q];
             }
@@ -994,7 +993,7 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 #pragma unroll
             for (int q = 0; q < 4; ++q) x[q] = __ldcg(src + 32 * q + lane);
             if (which == 0) {
-                norm_rope_row(x, w.k_norm, a.d.eps, rope + t * 64 * 2, o);
+                norm_rope_row(x, qk_norm + kHeadDim, a.d.eps, rope + t * 64 * 2, o);
             } else {
 #pragma unroll
                 for (int q = 0; q < 4; ++q) o[q] = x[q];
@@ -1024,13 +1023,13 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 
 template <bool F16>
 __device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
-                                          const float* rope, int l, int chunk, int h, long long q0, int T, int before,
+                                          const float* rope, const float* qk_norm, int l, int chunk, int h, long long q0, int T, int before,
                                           int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
                                           int mark_pid, int mark_k) {
     const int NQ = T * (a.d.n_heads / a.d.n_kv);
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
 #define MTB_ATTN_BODY(RP) \
-    attn_body<F16, RP>(a, ring, full, sq, sw, rope, l, chunk, h, q0, T, before, row0, kv, q_cached, wl, wpi, bar, \
+    attn_body<F16, RP>(a, ring, full, sq, sw, rope, qk_norm, l, chunk, h, q0, T, before, row0, kv, q_cached, wl, wpi, bar, \
                        mark_pid, mark_k)
     if (R <= 1) return MTB_ATTN_BODY(1);
     if (R == 2) return MTB_ATTN_BODY(2);
@@ -1057,6 +1056,7 @@ struct KCtx {
     int* flag;
     uint64_t* lm_bars; // [4]: tcgen05 LM head half_full[2], half_free[2]
     uint32_t* tmem;    // TMEM base address of the tcgen05 LM head
+    float* qk_norm;    // [2][128]: the layer's q_norm and k_norm weights, staged by phase A for B
     int T;             // rows of the step, all streams
     // Per stream: rows, first step row, cached positions, attention chunks.
     int s_T[kMaxStreams], s_row0[kMaxStreams], s_before[kMaxStreams], s_chunks[kMaxStreams];
@@ -1134,7 +1134,14 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
     constexpr int K = 256 * NK;
     uint8_t* act_q = c.region;
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    // The layer's q/k norm weights for phase B, loaded here where the latency
+    // hides behind this phase's work (B would otherwise chase the layer's
+    // pointers and then the weights before its first item could start).
+    const float qkn = threadIdx.x < 2 * kHeadDim
+                          ? __ldg((threadIdx.x < kHeadDim ? w.q_norm : w.k_norm) + (threadIdx.x % kHeadDim))
+                          : 0.f;
     norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, a.timeline, pid);
+    if (threadIdx.x < 2 * kHeadDim) c.qk_norm[threadIdx.x] = qkn;
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
@@ -1173,10 +1180,10 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int mp = j == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
-                              ? attn_item<true>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
+                              ? attn_item<true>(a, c.ring, c.full, sq, sw, c.rope, c.qk_norm, l, chunk, h, q0, c.s_T[si],
                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
                                                 mp, mk)
-                              : attn_item<false>(a, c.ring, c.full, sq, sw, c.rope, l, chunk, h, q0, c.s_T[si],
+                              : attn_item<false>(a, c.ring, c.full, sq, sw, c.rope, c.qk_norm, l, chunk, h, q0, c.s_T[si],
                                                  c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
                                                  mp, mk);
         ok = ok && good;
@@ -1629,6 +1636,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
     __shared__ int s_flag;
     __shared__ __align__(8) uint64_t s_lm_bars[4];
     __shared__ uint32_t s_tmem;
+    __shared__ float s_qk_norm[2 * kHeadDim];
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         KCtx& c = s_ctx;
@@ -1674,6 +1682,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
         c.flag = &s_flag;
         c.lm_bars = s_lm_bars;
         c.tmem = &s_tmem;
+        c.qk_norm = s_qk_norm;
         if (args.timeline && blockIdx.x == 0) {
             args.timeline[kTimelineStart] = global_ns();
             // SM cycles beside the timer (CTA 0, last barrier slot): the clock the step ran at.
