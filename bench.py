@@ -278,7 +278,7 @@ def main():
            "ms_per_step": e2e_s * 1e3 / n_e2e}
 
     prefill = ms_line = lc_line = None
-    if not args.no_extras:
+    if not args.no_extras and world == 1:  # per-GPU side measurements: the N=1 run carries them
         # ---- prefill: the prompt rows of configs[1] (375 audio + 32 text rows)
         # through the public run() call, host rows in and hidden rows out; every
         # layer over all rows at once with the projections on tcgen05.
