@@ -456,6 +456,208 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
     }
 }
 
+// Prefill attention, register-blocked: one (64-position chunk c, kv head h,
+// 64-token tile) per block of 256 threads, the tile's 128 query rows (group 2)
+// against the chunk's K/V rows.  Each thread forms an 8-row x 4-position score
+// tile (rows 8 rg .. 8 rg + 7, positions pg + 16 i) and later an 8-row x 8-dim
+// output tile (dims 2 dg + 32 i, + 1), so every shared-memory load feeds 4 to 8
+// FMAs instead of one.  Each score and each output is the same chain in the
+// same order as k_attn_chunk (even/odd dim chains, then their sum x scale; P.V
+// one chain over the row block's positions), and the partials go to the same
+// places (row blocks of 16 tokens), so k_attn_combine and the results are
+// unchanged bit for bit.  Row strides padded for conflict-free 8-byte reads.
+constexpr int kPfTok = 64;               // tokens per tile
+constexpr int kPfRows = 2 * kPfTok;      // query rows per tile (group 2)
+constexpr int kPfQS = kHeadDim + 2;      // q / K / V row stride (floats)
+constexpr int kPfSS = kPage + 1;         // score row stride (floats)
+constexpr int kPfWS = kPage + 1;         // weight row stride (float2)
+constexpr size_t kPfAttnSmem =
+    (size_t)(kPfRows * kPfQS + kPage * kPfQS + kPfRows * kPfSS) * 4 + (size_t)kPfRows * kPfWS * 8;
+
+__global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qkv, int n_heads, int n_kv, KvCache kv,
+                                                   int layer, float* part_o, float2* part_ml, int max_chunks, int P,
+                                                   int before, int qstride) {
+    const int c = blockIdx.x, h = blockIdx.y, tile = blockIdx.z;
+    const int t0 = tile * kPfTok;                     // first token of the tile (pass-relative)
+    const int n_tok = min(kPfTok, P - t0);
+    const int p0 = c * kPage;
+    if (n_tok <= 0 || p0 > before + t0 + n_tok - 1) return;  // no row of the tile reaches this chunk
+    const int G = 2, ld = (n_heads + 2 * n_kv) * kHeadDim;
+    extern __shared__ __align__(16) float sm[];
+    float* sq = sm;                                   // [128][130] query rows
+    float* skv = sq + kPfRows * kPfQS;                // [64][130] K, then V
+    float* ss = skv + kPage * kPfQS;                  // [128][65] scores
+    float2* sw = reinterpret_cast<float2*>(ss + kPfRows * kPfSS);  // [128][65] exp weights, doubled
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // Staging: every load of a batch is issued before the first store.
+    // q rows: 4096 float4, 16 per thread in two batches.
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * (8 * b + u), r = i >> 5, d4 = i & 31, t = r / G, j = r % G;
+            v[u] = t < n_tok ? __ldcg(reinterpret_cast<const float4*>(qkv + (size_t)(t0 + t) * ld +
+                                                                      (size_t)(h * G + j) * kHeadDim) + d4)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = tid + 256 * (8 * b + u), r = i >> 5, d4 = i & 31;
+            float* dst = sq + r * kPfQS + 4 * d4;
+            *reinterpret_cast<float2*>(dst) = make_float2(v[u].x, v[u].y);
+            *reinterpret_cast<float2*>(dst + 2) = make_float2(v[u].z, v[u].w);
+        }
+    }
+    // K and V rows (64 x 128 contiguous elements each): 16-byte loads, K
+    // stored now, V kept in registers until the scores are done.
+    const long long koff = kv_offset(kv, n_kv, layer, 0, h, p0);
+    const long long voff = kv_offset(kv, n_kv, layer, 1, h, p0);
+    const bool f16 = kv.type == KV_F16;
+    constexpr int kU = kPage * kHeadDim * 4 / 16 / 256;  // 16-byte f32 units per thread (8); fp16 uses half
+    uint4 vreg[kU];
+    {
+        uint4 kreg[kU];
+        const int nu = f16 ? kU / 2 : kU;
+        const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kv.base) + koff * (f16 ? 2 : 4));
+        const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kv.base) + voff * (f16 ? 2 : 4));
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (u < nu) {
+                kreg[u] = __ldcg(ks + tid + 256 * u);
+                vreg[u] = __ldcg(vs + tid + 256 * u);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (u >= nu) continue;
+            const int e0 = (tid + 256 * u) * (f16 ? 8 : 4);  // first element of the unit
+            float* dst = skv + (e0 / kHeadDim) * kPfQS + e0 % kHeadDim;
+            if (f16) {
+                const __half2* hh = reinterpret_cast<const __half2*>(&kreg[u]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) *reinterpret_cast<float2*>(dst + 2 * q) = __half22float2(hh[q]);
+            } else {
+                *reinterpret_cast<float2*>(dst) = make_float2(__uint_as_float(kreg[u].x), __uint_as_float(kreg[u].y));
+                *reinterpret_cast<float2*>(dst + 2) = make_float2(__uint_as_float(kreg[u].z), __uint_as_float(kreg[u].w));
+            }
+        }
+    }
+    __syncthreads();
+    // Scores: thread (rg, pg) = (tid / 16, tid % 16).
+    const int rg = tid >> 4, pg = tid & 15;
+    {
+        float2 acc[8][4];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[r][i] = make_float2(0.f, 0.f);
+        const float* qb = sq + (rg * 8) * kPfQS;
+        const float* kb = skv + pg * kPfQS;
+#pragma unroll 2
+        for (int d = 0; d < kHeadDim; d += 2) {
+            float2 qv[8], kv4[4];
+#pragma unroll
+            for (int r = 0; r < 8; ++r) qv[r] = *reinterpret_cast<const float2*>(qb + r * kPfQS + d);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) kv4[i] = *reinterpret_cast<const float2*>(kb + (16 * i) * kPfQS + d);
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[r][i] = __ffma2_rn(qv[r], kv4[i], acc[r][i]);
+        }
+        const float scale = 1.0f / sqrtf((float)kHeadDim);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            const int row = rg * 8 + r, t = row / G;  // tile-relative token
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int pp = pg + 16 * i;
+                const bool ok = t < n_tok && p0 + pp <= before + t0 + t;
+                ss[row * kPfSS + pp] = ok ? __fmul_rn(__fadd_rn(acc[r][i].x, acc[r][i].y), scale) : -INFINITY;
+            }
+        }
+    }
+    __syncthreads();
+    // V rows over K (all reads of K are done), from the registers loaded above.
+    {
+        const int nu = f16 ? kU / 2 : kU;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (u >= nu) continue;
+            const int e0 = (tid + 256 * u) * (f16 ? 8 : 4);
+            float* dst = skv + (e0 / kHeadDim) * kPfQS + e0 % kHeadDim;
+            if (f16) {
+                const __half2* hh = reinterpret_cast<const __half2*>(&vreg[u]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) *reinterpret_cast<float2*>(dst + 2 * q) = __half22float2(hh[q]);
+            } else {
+                *reinterpret_cast<float2*>(dst) = make_float2(__uint_as_float(vreg[u].x), __uint_as_float(vreg[u].y));
+                *reinterpret_cast<float2*>(dst + 2) = make_float2(__uint_as_float(vreg[u].z), __uint_as_float(vreg[u].w));
+            }
+        }
+    }
+    // Chunk softmax per row, one warp per row (the order of k_attn_chunk).
+    for (int row = warp; row < kPfRows; row += 8) {
+        const float a0 = ss[row * kPfSS + lane], a1 = ss[row * kPfSS + lane + 32];
+        const float m = warp_max(fmaxf(a0, a1));
+        const float e0 = a0 == -INFINITY ? 0.f : exact_expf(a0 - m);
+        const float e1 = a1 == -INFINITY ? 0.f : exact_expf(a1 - m);
+        const float l = warp_sum(e0 + e1);
+        sw[row * kPfWS + lane] = make_float2(e0, e0);
+        sw[row * kPfWS + lane + 32] = make_float2(e1, e1);
+        const int t = row / G, sb = t / kTMax, rb = tile * (kPfTok / kTMax) + sb;
+        const int kv_len = before + kTMax * rb + min(kTMax, P - kTMax * rb);
+        if (lane == 0 && t < n_tok && p0 < kv_len)
+            part_ml[((size_t)rb * n_kv + h) * max_chunks * qstride + (size_t)c * qstride + (t % kTMax) * G + row % G] =
+                make_float2(m, l);
+    }
+    __syncthreads();
+    // P.V: thread (rg, dg) = (tid / 16, tid % 16): rows 8 rg .. 8 rg + 7 (one row
+    // block of 16 tokens), dims 2 dg + 32 i and + 1; positions up to the row
+    // block's key count.
+    {
+        const int dg = pg;
+        const int sb = (rg * 8 / G) / kTMax, rb = tile * (kPfTok / kTMax) + sb;
+        const int T_rb = min(kTMax, P - kTMax * rb);
+        if (T_rb > 0) {
+            const int kv_len = before + kTMax * rb + T_rb;
+            const int n_pos = min(kPage, kv_len - p0);
+            float2 o[8][4];
+#pragma unroll
+            for (int r = 0; r < 8; ++r)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[r][i] = make_float2(0.f, 0.f);
+            const float* vb = skv + 2 * dg;
+            const float2* wb = sw + (rg * 8) * kPfWS;
+#pragma unroll 2
+            for (int pp = 0; pp < n_pos; ++pp) {
+                float2 v[4], w[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) v[i] = *reinterpret_cast<const float2*>(vb + pp * kPfQS + 32 * i);
+#pragma unroll
+                for (int r = 0; r < 8; ++r) w[r] = wb[r * kPfWS + pp];
+#pragma unroll
+                for (int r = 0; r < 8; ++r)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[r][i] = __ffma2_rn(w[r], v[i], o[r][i]);
+            }
+            if (n_pos > 0) {
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    const int row = rg * 8 + r, t = row / G;
+                    if (t >= n_tok) continue;
+                    float* dst = part_o + (((size_t)rb * n_kv + h) * max_chunks * qstride + (size_t)c * qstride +
+                                           (t % kTMax) * G + row % G) * kHeadDim;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        *reinterpret_cast<float2*>(dst + 2 * dg + 32 * i) = o[r][i];
+                }
+            }
+        }
+    }
+}
+
 // Merge the chunk partials of one (row, head): grid (rows, n_heads), block
 // 128; rows and partial buffers as in k_attn_chunk (row blocks of 16).
 __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n_heads, int n_kv,
@@ -821,6 +1023,7 @@ cudaError_t configure_kernels() {
     cudaFuncSetAttribute(k_gemv<EPI_SWIGLU, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_gemv<EPI_ARGMAX, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
+    cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfAttnSmem);
     pf_configure();
     return cudaGetLastError();
 }
@@ -883,9 +1086,12 @@ void launch_prefill_pass(const DeviceModel& m, const KvCache& kv, const PrefillB
         pf_gemm(w.pf_qkv, qd + 2 * kd, H, p.xq, p.xd, P, p.qkv, qd + 2 * kd, PF_EPI_STORE, p.status, s);
         k_qk_norm_rope_store<<<dim3(P, d.n_heads + d.n_kv), 128, 0, s>>>(nullptr, p.qkv, d.n_heads, d.n_kv, w.q_norm,
                                                                          w.k_norm, d.eps, m.theta_scale, kv, l, P, before);
-        k_attn_chunk<<<dim3(max_chunks, d.n_kv, n_rb), kThreads, attn_smem, s>>>(nullptr, p.qkv, d.n_heads, d.n_kv, kv, l,
-                                                                                  p.part_o, p.part_ml, max_chunks, P,
-                                                                                  before, qstride);
+        if (G == 2)
+            k_pf_attn<<<dim3(max_chunks, d.n_kv, (P + kPfTok - 1) / kPfTok), 256, kPfAttnSmem, s>>>(
+                p.qkv, d.n_heads, d.n_kv, kv, l, p.part_o, p.part_ml, max_chunks, P, before, qstride);
+        else
+            k_attn_chunk<<<dim3(max_chunks, d.n_kv, n_rb), kThreads, attn_smem, s>>>(
+                nullptr, p.qkv, d.n_heads, d.n_kv, kv, l, p.part_o, p.part_ml, max_chunks, P, before, qstride);
         k_attn_combine<<<dim3(P, d.n_heads), 128, 0, s>>>(nullptr, d.n_heads, d.n_kv, p.part_o, p.part_ml, max_chunks,
                                                           p.attn, P, before, qstride);
         pf_quant(p.attn, P, qd, p.xq, p.xd, s);
