@@ -659,7 +659,13 @@ __global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qk
 }
 
 // Merge the chunk partials of one (row, head): grid (rows, n_heads), block
-// 128; rows and partial buffers as in k_attn_chunk (row blocks of 16).
+// 128 (one output dim per thread); rows and partial buffers as in k_attn_chunk
+// (row blocks of 16).  M = max over chunks; then, chunk by chunk in order,
+// w = exp(m_c - M), L += w l_c, o += w o_c (one fmaf chain each, chunks with
+// m_c = -inf skipped).  Chunks go in batches of 128: the batch's weights are
+// formed in parallel (one chunk per thread) into shared memory and its
+// partial loads are issued 16 at a time, so the chains wait on arithmetic,
+// not on one load after another.
 __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n_heads, int n_kv,
                                                       const float* part_o, const float2* part_ml, int max_chunks,
                                                       float* attn_out, int T_arg, int before_arg, int qstride) {
@@ -674,15 +680,41 @@ __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n
     const int n_chunks = (kv_len + kPage - 1) / kPage;
     part_o += (size_t)rb * n_kv * max_chunks * qstride * kHeadDim;
     part_ml += (size_t)rb * n_kv * max_chunks * qstride;
+    const float2* ml = part_ml + (size_t)h * max_chunks * qstride + q;  // chunk c at ml[c * qstride]
+    const float* po = part_o + ((size_t)h * max_chunks * qstride + q) * kHeadDim + threadIdx.x;
+    const size_t so = (size_t)qstride * kHeadDim;                       // one chunk further in po
+    __shared__ float s_red[4];
+    __shared__ float2 s_wl[128];  // (w, l) of the batch's chunks; w < 0 marks a skipped chunk
     float M = -INFINITY;
-    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, part_ml[((size_t)h * max_chunks + c) * qstride + q].x);
+    for (int c = threadIdx.x; c < n_chunks; c += 128) M = fmaxf(M, ml[(size_t)c * qstride].x);
+    M = warp_max(M);
+    if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = M;
+    __syncthreads();
+    M = fmaxf(fmaxf(s_red[0], s_red[1]), fmaxf(s_red[2], s_red[3]));
     float L = 0.f, o = 0.f;
-    for (int c = 0; c < n_chunks; ++c) {
-        const float2 ml = part_ml[((size_t)h * max_chunks + c) * qstride + q];
-        if (ml.x == -INFINITY) continue;
-        const float wgt = exact_expf(ml.x - M);
-        L = fmaf(wgt, ml.y, L);
-        o = fmaf(wgt, part_o[(((size_t)h * max_chunks + c) * qstride + q) * kHeadDim + threadIdx.x], o);
+    for (int c0 = 0; c0 < n_chunks; c0 += 128) {
+        const int nb = min(128, n_chunks - c0);
+        __syncthreads();  // the previous batch's weights are consumed
+        if (threadIdx.x < nb) {
+            const float2 v = ml[(size_t)(c0 + threadIdx.x) * qstride];
+            s_wl[threadIdx.x] = v.x == -INFINITY ? make_float2(-1.f, 0.f) : make_float2(exact_expf(v.x - M), v.y);
+        }
+        __syncthreads();
+        for (int u0 = 0; u0 < nb; u0 += 16) {
+            float ov[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) ov[u] = u0 + u < nb ? __ldcg(po + (size_t)(c0 + u0 + u) * so) : 0.f;
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                if (u0 + u < nb) {
+                    const float2 wl = s_wl[u0 + u];
+                    if (wl.x >= 0.f) {
+                        L = fmaf(wl.x, wl.y, L);
+                        o = fmaf(wl.x, ov[u], o);
+                    }
+                }
+            }
+        }
     }
     attn_out[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = o / L;
 }
