@@ -465,16 +465,22 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
 // same order as k_attn_chunk (even/odd dim chains, then their sum x scale; P.V
 // one chain over the row block's positions), and the partials go to the same
 // places (row blocks of 16 tokens), so k_attn_combine and the results are
-// unchanged bit for bit.  Row strides padded for conflict-free 8-byte reads.
+// unchanged bit for bit.  The chunk softmax runs on the score registers: the
+// 16 threads of a row group hold a row's 64 positions as k_attn_chunk's lanes
+// pg and pg + 16 would (positions pg, pg + 32 and pg + 16, pg + 48), so the pair
+// sums, the first butterfly level (within the thread) and the other four
+// (xor 8, 4, 2, 1 across the 16 threads) add the same values in the same order.
+// The exp weights then overwrite the q rows (done with), which keeps a block at
+// ~100 KB of shared memory and two blocks per SM.  Row strides are padded for
+// conflict-free 8-byte reads.
 constexpr int kPfTok = 64;               // tokens per tile
 constexpr int kPfRows = 2 * kPfTok;      // query rows per tile (group 2)
 constexpr int kPfQS = kHeadDim + 2;      // q / K / V row stride (floats)
-constexpr int kPfSS = kPage + 1;         // score row stride (floats)
-constexpr int kPfWS = kPage + 1;         // weight row stride (float2)
-constexpr size_t kPfAttnSmem =
-    (size_t)(kPfRows * kPfQS + kPage * kPfQS + kPfRows * kPfSS) * 4 + (size_t)kPfRows * kPfWS * 8;
+constexpr int kPfWS = kPage + 1;         // weight row stride (float2): rows of weights fit in the q rows
+static_assert(kPfWS * 2 <= kPfQS, "weights reuse the q rows");
+constexpr size_t kPfAttnSmem = (size_t)(kPfRows * kPfQS + kPage * kPfQS) * 4;
 
-__global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qkv, int n_heads, int n_kv, KvCache kv,
+__global__ void __launch_bounds__(256, 2) k_pf_attn(const float* __restrict__ qkv, int n_heads, int n_kv, KvCache kv,
                                                    int layer, float* part_o, float2* part_ml, int max_chunks, int P,
                                                    int before, int qstride) {
     const int c = blockIdx.x, h = blockIdx.y, tile = blockIdx.z;
@@ -484,11 +490,10 @@ __global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qk
     if (n_tok <= 0 || p0 > before + t0 + n_tok - 1) return;  // no row of the tile reaches this chunk
     const int G = 2, ld = (n_heads + 2 * n_kv) * kHeadDim;
     extern __shared__ __align__(16) float sm[];
-    float* sq = sm;                                   // [128][130] query rows
+    float* sq = sm;                                   // [128][130] query rows, then the exp weights
     float* skv = sq + kPfRows * kPfQS;                // [64][130] K, then V
-    float* ss = skv + kPage * kPfQS;                  // [128][65] scores
-    float2* sw = reinterpret_cast<float2*>(ss + kPfRows * kPfSS);  // [128][65] exp weights, doubled
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float2* sw = reinterpret_cast<float2*>(sq);       // [128][65] exp weights, doubled (over the q rows)
+    const int tid = threadIdx.x;
     // Staging: every load of a batch is issued before the first store.
     // q rows: 4096 float4, 16 per thread in two batches.
 #pragma unroll
@@ -509,49 +514,42 @@ __global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qk
             *reinterpret_cast<float2*>(dst + 2) = make_float2(v[u].z, v[u].w);
         }
     }
-    // K and V rows (64 x 128 contiguous elements each): 16-byte loads, K
-    // stored now, V kept in registers until the scores are done.
+    // K rows (64 x 128 contiguous elements): 16-byte loads, converted to f32.
     const long long koff = kv_offset(kv, n_kv, layer, 0, h, p0);
     const long long voff = kv_offset(kv, n_kv, layer, 1, h, p0);
     const bool f16 = kv.type == KV_F16;
-    constexpr int kU = kPage * kHeadDim * 4 / 16 / 256;  // 16-byte f32 units per thread (8); fp16 uses half
-    uint4 vreg[kU];
-    {
-        uint4 kreg[kU];
+    auto stage = [&](long long off) {
+        constexpr int kU = kPage * kHeadDim * 4 / 16 / 256;  // 16-byte f32 units per thread (8); fp16 uses half
         const int nu = f16 ? kU / 2 : kU;
-        const uint4* ks = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kv.base) + koff * (f16 ? 2 : 4));
-        const uint4* vs = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kv.base) + voff * (f16 ? 2 : 4));
+        const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(kv.base) + off * (f16 ? 2 : 4));
+        uint4 reg[kU];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            if (u < nu) {
-                kreg[u] = __ldcg(ks + tid + 256 * u);
-                vreg[u] = __ldcg(vs + tid + 256 * u);
-            }
-        }
+        for (int u = 0; u < kU; ++u)
+            if (u < nu) reg[u] = __ldcg(src + tid + 256 * u);
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
             if (u >= nu) continue;
             const int e0 = (tid + 256 * u) * (f16 ? 8 : 4);  // first element of the unit
             float* dst = skv + (e0 / kHeadDim) * kPfQS + e0 % kHeadDim;
             if (f16) {
-                const __half2* hh = reinterpret_cast<const __half2*>(&kreg[u]);
+                const __half2* hh = reinterpret_cast<const __half2*>(&reg[u]);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) *reinterpret_cast<float2*>(dst + 2 * q) = __half22float2(hh[q]);
             } else {
-                *reinterpret_cast<float2*>(dst) = make_float2(__uint_as_float(kreg[u].x), __uint_as_float(kreg[u].y));
-                *reinterpret_cast<float2*>(dst + 2) = make_float2(__uint_as_float(kreg[u].z), __uint_as_float(kreg[u].w));
+                *reinterpret_cast<float2*>(dst) = make_float2(__uint_as_float(reg[u].x), __uint_as_float(reg[u].y));
+                *reinterpret_cast<float2*>(dst + 2) = make_float2(__uint_as_float(reg[u].z), __uint_as_float(reg[u].w));
             }
         }
-    }
+    };
+    stage(koff);
     __syncthreads();
-    // Scores: thread (rg, pg) = (tid / 16, tid % 16).
     const int rg = tid >> 4, pg = tid & 15;
+    float2 acc[8][4];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[r][i] = make_float2(0.f, 0.f);
     {
-        float2 acc[8][4];
-#pragma unroll
-        for (int r = 0; r < 8; ++r)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) acc[r][i] = make_float2(0.f, 0.f);
         const float* qb = sq + (rg * 8) * kPfQS;
         const float* kb = skv + pg * kPfQS;
 #pragma unroll 2
@@ -566,51 +564,39 @@ __global__ void __launch_bounds__(256, 1) k_pf_attn(const float* __restrict__ qk
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[r][i] = __ffma2_rn(qv[r], kv4[i], acc[r][i]);
         }
+    }
+    __syncthreads();  // q and K rows are done with: the weights and V take their places
+    stage(voff);
+    {
         const float scale = 1.0f / sqrtf((float)kHeadDim);
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
             const int row = rg * 8 + r, t = row / G;  // tile-relative token
+            float sc[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int pp = pg + 16 * i;
                 const bool ok = t < n_tok && p0 + pp <= before + t0 + t;
-                ss[row * kPfSS + pp] = ok ? __fmul_rn(__fadd_rn(acc[r][i].x, acc[r][i].y), scale) : -INFINITY;
+                sc[i] = ok ? __fmul_rn(__fadd_rn(acc[r][i].x, acc[r][i].y), scale) : -INFINITY;
             }
-        }
-    }
-    __syncthreads();
-    // V rows over K (all reads of K are done), from the registers loaded above.
-    {
-        const int nu = f16 ? kU / 2 : kU;
+            float m = fmaxf(fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3]));
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-            if (u >= nu) continue;
-            const int e0 = (tid + 256 * u) * (f16 ? 8 : 4);
-            float* dst = skv + (e0 / kHeadDim) * kPfQS + e0 % kHeadDim;
-            if (f16) {
-                const __half2* hh = reinterpret_cast<const __half2*>(&vreg[u]);
+            for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            float e[4];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) *reinterpret_cast<float2*>(dst + 2 * q) = __half22float2(hh[q]);
-            } else {
-                *reinterpret_cast<float2*>(dst) = make_float2(__uint_as_float(vreg[u].x), __uint_as_float(vreg[u].y));
-                *reinterpret_cast<float2*>(dst + 2) = make_float2(__uint_as_float(vreg[u].z), __uint_as_float(vreg[u].w));
-            }
+            for (int i = 0; i < 4; ++i) e[i] = sc[i] == -INFINITY ? 0.f : exact_expf(sc[i] - m);
+            // k_attn_chunk's lane pg holds positions pg, pg + 32; lane pg + 16 holds pg + 16, pg + 48.
+            float l = (e[0] + e[2]) + (e[1] + e[3]);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sw[row * kPfWS + pg + 16 * i] = make_float2(e[i], e[i]);
+            const int sb = t / kTMax, rb = tile * (kPfTok / kTMax) + sb;
+            const int kv_len = before + kTMax * rb + min(kTMax, P - kTMax * rb);
+            if (pg == 0 && t < n_tok && p0 < kv_len)
+                part_ml[((size_t)rb * n_kv + h) * max_chunks * qstride + (size_t)c * qstride + (t % kTMax) * G +
+                        row % G] = make_float2(m, l);
         }
-    }
-    // Chunk softmax per row, one warp per row (the order of k_attn_chunk).
-    for (int row = warp; row < kPfRows; row += 8) {
-        const float a0 = ss[row * kPfSS + lane], a1 = ss[row * kPfSS + lane + 32];
-        const float m = warp_max(fmaxf(a0, a1));
-        const float e0 = a0 == -INFINITY ? 0.f : exact_expf(a0 - m);
-        const float e1 = a1 == -INFINITY ? 0.f : exact_expf(a1 - m);
-        const float l = warp_sum(e0 + e1);
-        sw[row * kPfWS + lane] = make_float2(e0, e0);
-        sw[row * kPfWS + lane + 32] = make_float2(e1, e1);
-        const int t = row / G, sb = t / kTMax, rb = tile * (kPfTok / kTMax) + sb;
-        const int kv_len = before + kTMax * rb + min(kTMax, P - kTMax * rb);
-        if (lane == 0 && t < n_tok && p0 < kv_len)
-            part_ml[((size_t)rb * n_kv + h) * max_chunks * qstride + (size_t)c * qstride + (t % kTMax) * G + row % G] =
-                make_float2(m, l);
     }
     __syncthreads();
     // P.V: thread (rg, dg) = (tid / 16, tid % 16): rows 8 rg .. 8 rg + 7 (one row
