@@ -74,6 +74,9 @@ struct mtb_decoder {
     long long h2d_bytes = 0, d2h_bytes = 0;  // host<->device bytes this decoder has issued
     cudaEvent_t ev[16] = {};
     cudaEvent_t group_ev = nullptr;  // orders a group step against this decoder's stream
+    // The pinned step-state mirror equals the device state (no device work since
+    // the last read-back or synchronised push): refresh() need not read it again.
+    bool fresh = false;
     std::vector<void*> allocs;
     std::string error;
     ~mtb_decoder() {
@@ -272,6 +275,7 @@ int load_model(mtb_model* m, const char* path) {
 }
 
 int refresh(mtb_decoder* d) {
+    if (d->fresh && d->h_state->error == 0) return 0;
     d->d2h_bytes += sizeof(StepState);
     MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
@@ -281,6 +285,7 @@ int refresh(mtb_decoder* d) {
                                             : "device reported an out-of-range token id";
         return -1;
     }
+    d->fresh = true;
     return 0;
 }
 
@@ -321,6 +326,7 @@ cudaGraphExec_t step_graph(mtb_decoder* d, int mode, bool penalty) {
 }
 
 int run_step(mtb_decoder* d, int mode) {
+    d->fresh = false;  // device work below changes the step state
     cudaGraphExec_t g = step_graph(d, mode, d->h_state->penalty > 1.f);
     if (!g) return fail(d->error, "could not build the verify-step graph: " + std::string(cudaGetErrorString(cudaGetLastError())));
     MTB_CK(d, cudaGraphLaunch(g, d->stream));
@@ -351,6 +357,7 @@ int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
 // through the verify kernels.  The host's past (h_state) is current on entry.
 int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last,
                       bool rows_on_device = false) {
+    d->fresh = false;  // device work below changes the step state
     const int H = d->model->dm.dims.hidden;
     const cudaMemcpyKind in_kind = rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     int done = 0;
@@ -445,6 +452,7 @@ void clear_progress(StepState& s) {
 }
 
 int prefill(mtb_decoder* d, const float* fused, int seq, bool on_device = false) {
+    d->fresh = false;  // device work below changes the step state
     if (!fused || seq <= 0) return fail(d->error, "empty prompt");
     if (seq + 1 > d->max_seq) return fail(d->error, "prompt exceeds max_seq");
     d->h_state->past = 0;
@@ -461,6 +469,7 @@ int prefill(mtb_decoder* d, const float* fused, int seq, bool on_device = false)
 // position holding audio_token_id takes audio row k), ids, slots and audio rows
 // are uploaded, and k_fuse_embeds writes the fused rows into fused_dev.
 int fuse_on_device(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio, int audio_token_id) {
+    d->fresh = false;  // device work below changes the step state
     const ModelDims& dm = d->model->dm.dims;
     const int H = dm.hidden;
     if (!ids || seq <= 0) return fail(d->error, "fuse_embeds: empty input_ids");
@@ -690,6 +699,7 @@ int mtb_decoder_past_len(const mtb_decoder* dc) {
 
 int mtb_decoder_reset(mtb_decoder* d) {
     if (!d) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     if (refresh(d)) return -1;
     d->h_state->past = 0;  // src/qwen3_decoder.cpp:87-89
@@ -701,6 +711,7 @@ int mtb_decoder_reset(mtb_decoder* d) {
 
 int mtb_decoder_rewind(mtb_decoder* d, int position) {
     if (!d) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     if (refresh(d)) return -1;
     if (position < 0 || position > d->h_state->past) return fail(d->error, "invalid rewind");  // cpu_speculative.cpp:40-42
@@ -712,6 +723,7 @@ int mtb_decoder_rewind(mtb_decoder* d, int position) {
 
 int mtb_decoder_run(mtb_decoder* d, const float* embeds, int T, float* hidden_out) {
     if (!d || !embeds || T <= 0) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     if (refresh(d)) return -1;
     if (d->h_state->past + T > d->max_seq) return fail(d->error, "sequence exceeds max_seq");  // qwen3_decoder.cpp:102
@@ -720,9 +732,11 @@ int mtb_decoder_run(mtb_decoder* d, const float* embeds, int T, float* hidden_ou
 
 int mtb_decoder_logits(mtb_decoder* d, const float* hidden_row, float* logits) {
     if (!d || !hidden_row || !logits) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     const ModelDims& dm = d->model->dm.dims;
     if (refresh(d)) return -1;
+    d->fresh = false;
     const int saved_T = d->h_state->T;
     MTB_CK(d, cudaMemcpyAsync(d->row_buf, hidden_row, size_t(dm.hidden) * 4, cudaMemcpyHostToDevice, d->stream));
     const int one = 1;
@@ -754,6 +768,7 @@ int mtb_decoder_kv_read(mtb_decoder* d, int layer, int which, int pos0, int n_po
 
 int mtb_decoder_fill_synthetic_kv(mtb_decoder* d, int n_pos, uint32_t seed) {
     if (!d || n_pos < 0 || n_pos > d->max_seq) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     launch_fill_synthetic_kv(d->model->dm, d->kv, n_pos, seed, d->stream);
     MTB_CK(d, cudaGetLastError());
@@ -768,6 +783,7 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
                       int32_t* out_ids, int* n_out, mtb_counters* counters, mtb_draft_fn draft, mtb_commit_fn commit,
                       void* user) {
     if (!d || !out_ids || !n_out) return -1;
+    d->fresh = false;
     *n_out = 0;
     try {
         cudaSetDevice(d->device);
@@ -841,6 +857,7 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
 int mtb_fuse_embeds(mtb_decoder* d, const int32_t* ids, int seq, const float* audio, int n_audio, int audio_token_id,
                     float* out) {
     if (!d || !out) return -1;
+    d->fresh = false;
     try {
         cudaSetDevice(d->device);
         if (fuse_on_device(d, ids, seq, audio, n_audio, audio_token_id)) return -1;
@@ -859,6 +876,7 @@ int mtb_spec_generate_ids(mtb_decoder* d, const int32_t* ids, int seq, const flo
                           int audio_token_id, int max_new, int eos, const mtb_spec_params* params, int32_t* out_ids,
                           int* n_out, mtb_counters* counters) {
     if (!d || !out_ids || !n_out) return -1;
+    d->fresh = false;
     *n_out = 0;
     try {
         cudaSetDevice(d->device);
@@ -900,6 +918,7 @@ int mtb_greedy_generate(mtb_decoder* d, const float* fused, int seq, int max_new
 int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_new, int eos,
                const mtb_spec_params* params) {
     if (!d || !ids || n_ids <= 0) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     if (refresh(d)) return -1;
     if (set_params(d, max_new, eos, params)) return -1;
@@ -918,6 +937,7 @@ int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_
     MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->h_ids, size_t(n_ids) * 4, cudaMemcpyHostToDevice, d->stream));
     if (push_state(d)) return -1;
     MTB_CK(d, cudaStreamSynchronize(d->stream));
+    d->fresh = true;
     return 0;
 }
 
@@ -938,6 +958,7 @@ int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counter
         if (push_state(d)) return -1;
         mode = 1;
     }
+    d->fresh = false;
     if (run_step(d, mode)) return -1;
     if (refresh(d)) return -1;
     fill_counters(s, counters);
@@ -946,6 +967,7 @@ int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counter
 
 int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft) {
     if (!d) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     int mode = 0;
     if (draft_device) {
@@ -962,6 +984,7 @@ int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft
 
 int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params) {
     if (!d || !fused || seq <= 0) return -1;
+    d->fresh = false;
     try {
         cudaSetDevice(d->device);
         if (refresh(d)) return -1;
@@ -1003,6 +1026,7 @@ int check_group(mtb_decoder* const* ds, int n) {
 // and before its later work.
 int group_step(mtb_decoder* const* ds, int n) {
     mtb_decoder* d0 = ds[0];
+    for (int i = 0; i < n; ++i) ds[i]->fresh = false;
     KvCache kvs[kMaxStreams];
     KvTensorMap maps[kMaxStreams];
     StepState* states[kMaxStreams];
@@ -1077,6 +1101,7 @@ int mtb_snapshot_save(mtb_decoder* d) {
 
 int mtb_snapshot_restore_async(mtb_decoder* d) {
     if (!d) return -1;
+    d->fresh = false;
     cudaSetDevice(d->device);
     MTB_CK(d, cudaMemcpyAsync(d->b.state, d->snap_state, sizeof(StepState), cudaMemcpyDeviceToDevice, d->stream));
     MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->snap_ids, size_t(d->max_new) * 4, cudaMemcpyDeviceToDevice, d->stream));
@@ -1149,6 +1174,7 @@ int mtb_step_kernel_launches(mtb_decoder* d) {
 int mtb_ngram_draft(mtb_decoder* d, const int32_t* history, int n, int maximum, int n_min, int n_max, int32_t* out,
                     int* n_out) {
     if (!d || !out || !n_out || n < 0 || n > d->max_new || (n > 0 && !history)) return -1;
+    d->fresh = false;
     if (n_min < 1 || n_max < n_min) return fail(d->error, "need 1 <= n_min <= n_max");
     cudaSetDevice(d->device);
     if (n > 0) MTB_CK(d, cudaMemcpyAsync(d->scratch_i, history, size_t(n) * 4, cudaMemcpyHostToDevice, d->stream));
@@ -1170,6 +1196,7 @@ int mtb_ngram_draft(mtb_decoder* d, const int32_t* history, int n, int maximum, 
 int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t* history, int n, float penalty,
                       int32_t* choice) {
     if (!d || !raw || !choice || n_raw <= 0 || n < 0 || n > d->max_new || (n > 0 && !history)) return -1;
+    d->fresh = false;
     if (n_raw > d->model->dm.dims.vocab) return fail(d->error, "more logits than the vocabulary");
     cudaSetDevice(d->device);
     MTB_CK(d, cudaMemcpyAsync(d->b.logits, raw, size_t(n_raw) * 4, cudaMemcpyHostToDevice, d->stream));
