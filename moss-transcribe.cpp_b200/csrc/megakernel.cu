@@ -5,13 +5,16 @@
 // Here every operation is a phase of one kernel, phases are separated by grid
 // barriers, and one producer warp per CTA streams every weight tile the CTA
 // will need (all layers, then the LM head) through a ring of shared-memory
-// slots with cp.async.bulk (weights) and TMA tensor tiles (K/V) + mbarriers.  Weights do not depend on the step's
-// activations, so HBM keeps streaming while the consumer warps wait at
-// barriers; the consumers find their tiles already in shared memory.
+// slots with cp.async.bulk (weights) and TMA tensor tiles (K/V) + mbarriers.
+// Weights do not depend on the step's activations, so HBM keeps streaming
+// while the consumer warps wait at barriers; the consumers find their tiles
+// already in shared memory.  One launch may verify several decoders' rows
+// together (a stream table: each stream its own KV cache, positions, draft
+// and acceptance).
 //
 // Phases per layer (src/qwen3.cpp:62-218):
 //   A  RMSNorm + q8_0 quantise (every CTA, into shared memory); QKV rows
-//   B  attention per (64-position chunk, kv head): per-head RMSNorm + RoPE of
+//   B  attention per (stream, 64-position chunk, kv head): per-head RMSNorm + RoPE of
 //      the head's q rows (and of k for the step's new positions, stored to
 //      the KV cache with the new v rows by the item holding them), scores,
 //      chunk softmax, P.V partials; the chunk's K/V rows streamed into the
