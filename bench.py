@@ -57,6 +57,7 @@ TRAFFIC_BYTES = 884_756_480
 MS_STREAMS = 8
 MS_KV = 1500
 MS_STEPS = 48
+MS_NEW = 768  # configs[4]: decoded tokens per recording
 # configs[3] context length: a 30-minute recording leaves ~27k cached positions.
 LC_KV = 27000
 LC_STEPS = 50
@@ -407,6 +408,31 @@ def multi_stream(model, capi, fixture) -> dict:
     for d in ds:
         d.close()
     assert g_ids == s_ids, "group decode differs from single-stream decode"
+
+    # configs[4] end to end on one GPU: each recording's 1500 prompt rows
+    # (synthetic N(0, 1), host rows in) prefilled, then 768 tokens decoded with
+    # the device draft (k = 8), all recordings stepped as one group.  One
+    # recording alone, the same way, for comparison.
+    prompts = [np.random.default_rng(500 + i).standard_normal((MS_KV, model.hidden)).astype(np.float32)
+               for i in range(MS_STREAMS)]
+    es = [capi.Decoder(model, MS_KV + MS_NEW + 64, capi.KV_F16, max_new=MS_NEW) for _ in range(MS_STREAMS)]
+
+    def e2e(group):
+        t0 = time.perf_counter()
+        for d, pr in zip(group, prompts):
+            d.spec_prime(pr, MS_NEW, -1, k_max=8, n_min=3, n_max=3)
+        steps = capi.spec_run_group(group)
+        dt = time.perf_counter() - t0
+        outs = [d.read_ids() for d in group]
+        return dt, steps, sum(len(ids) for ids, _ in outs), sum(c["accepted"] for _, c in outs)
+
+    e2e(es[:1])  # warm-up (graphs, first prefill)
+    one_dt, one_steps, one_toks, one_acc = e2e(es[:1])
+    one_ids = es[0].read_ids()[0]
+    all_dt, all_steps, all_toks, all_acc = e2e(es)
+    assert es[0].read_ids()[0] == one_ids, "a recording decoded in the group differs from it decoded alone"
+    for d in es:
+        d.close()
     return {"workload": f"configs[4] sample: {MS_STREAMS} recordings, KV {MS_KV} fp16 synthetic each, "
                         f"{MS_STEPS} verify steps each, device n-gram draft k=8",
             "single_stream": {"tokens_per_s": round(s_toks / s_dt, 1), "ms_per_launch": round(s_dt * 1e3 / (MS_STREAMS * MS_STEPS), 3),
@@ -414,7 +440,14 @@ def multi_stream(model, capi, fixture) -> dict:
             "grouped": {"tokens_per_s": round(g_toks / g_dt, 1), "ms_per_launch": round(g_dt * 1e3 / MS_STEPS, 3),
                         "tokens": g_toks, "rows": g_rows, "accepted": g_acc},
             "speedup": round((g_toks / g_dt) / (s_toks / s_dt), 3),
-            "timing": "host wall clock around mtb_spec_run_group, ids read back; same ids in both modes"}
+            "timing": "host wall clock around mtb_spec_run_group, ids read back; same ids in both modes",
+            "end_to_end": {"workload": f"configs[4] on one GPU: {MS_STREAMS} recordings x ({MS_KV} prompt rows prefilled "
+                                       f"+ {MS_NEW} tokens decoded, device n-gram draft k=8), one group",
+                           "tokens_per_s": round(all_toks / all_dt, 1), "s": round(all_dt, 3), "steps": all_steps,
+                           "tokens": all_toks, "accepted": all_acc,
+                           "one_recording": {"tokens_per_s": round(one_toks / one_dt, 1), "s": round(one_dt, 3),
+                                             "steps": one_steps, "accepted": one_acc},
+                           "timing": "host wall clock: mtb_spec_prime (prefill) for each + mtb_spec_run_group"}}
 
 
 def _device_ids(dec, arr: np.ndarray) -> int:
