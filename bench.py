@@ -309,7 +309,7 @@ def main():
         prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
                    "long": {"rows": PREFILL_LONG_ROWS, "ms": round(pl_s * 1e3, 1),
                             "rows_per_s": round(PREFILL_LONG_ROWS / pl_s, 1)},
-                   "path": "prefill passes (tcgen05 q8_0 projections) + verify kernels for the last rows",
+                   "path": "prefill passes over every row (tcgen05 q8_0 projections, register-blocked attention); the first token's LM head from the last pass",
                    "timing": "host wall clock around run(), median of 5, host rows in, hidden rows out"}
 
     peak, peak_kind = measured_peaks()

@@ -342,7 +342,7 @@ int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
     const ModelDims& dm = d->model->dm.dims;
     const int G = dm.n_heads / dm.n_kv;
     int P = std::min(remaining, d->pf.max_rows);
-    P -= P % kTMax;
+    if (P < remaining) P -= P % kTMax;  // a pass that leaves rows over ends on a row block
     while (P > kTMax) {
         const size_t need = size_t((P + kTMax - 1) / kTMax) * dm.n_kv * size_t((before + P + kPage - 1) / kPage) * (kTMax * G);
         if (need <= d->pf.part_rows) break;
@@ -351,10 +351,11 @@ int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
     return P;
 }
 
-// Rows [T][hidden] from the host at past..past+T-1: all but the last 1..16 in
-// prefill passes (every layer over up to 512 rows at once, tcgen05
-// projections), the last ones (and the LM head when asked) in steps of kTMax
-// through the verify kernels.  The host's past (h_state) is current on entry.
+// Rows [T][hidden] from the host at past..past+T-1.  More than kTMax rows: all
+// in prefill passes (every layer over up to 512 rows at once, tcgen05
+// projections), the LM head of the last row (when asked) from the last pass's
+// final-normed rows.  At most kTMax rows: one step of the verify kernels.  The
+// host's past (h_state) is current on entry.
 int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last,
                       bool rows_on_device = false) {
     d->fresh = false;  // device work below changes the step state
@@ -362,15 +363,16 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
     const cudaMemcpyKind in_kind = rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     int done = 0;
     if (d->pf.max_rows >= kTMax && T > kTMax) {
-        const int bulk = T - (T % kTMax ? T % kTMax : kTMax);
         const int past = d->h_state->past;
-        while (done < bulk) {
-            const int P = prefill_pass_rows(d, bulk - done, past + done);
-            if (P < kTMax) return fail(d->error, "prefill pass does not fit its buffers");
+        while (done < T) {
+            const int P = prefill_pass_rows(d, T - done, past + done);
+            if (P < 1 || (P < kTMax && done + P < T)) return fail(d->error, "prefill pass does not fit its buffers");
+            const bool last = done + P >= T;
             if (!rows_on_device) d->h2d_bytes += (long long)P * H * 4;
             MTB_CK(d, cudaMemcpyAsync(d->pf.x, rows + size_t(done) * H, size_t(P) * H * sizeof(float), in_kind,
                                       d->stream));
-            launch_prefill_pass(d->model->dm, d->kv, d->pf, P, past + done, hidden_out != nullptr, d->stream);
+            launch_prefill_pass(d->model->dm, d->kv, d->pf, P, past + done,
+                                hidden_out != nullptr || (lm_on_last && last), d->stream);
             launch_rows_begin(d->b, P, d->stream);
             launch_rows_end(d->b, d->stream);
             MTB_CK(d, cudaGetLastError());
@@ -379,6 +381,7 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
                 MTB_CK(d, cudaMemcpyAsync(hidden_out + size_t(done) * H, d->pf.hid, size_t(P) * H * sizeof(float),
                                           cudaMemcpyDeviceToHost, d->stream));
             }
+            if (lm_on_last && last) launch_lm_row(d->model->dm, d->b, d->pf.hid + size_t(P - 1) * H, d->stream);
             done += P;
         }
         int status = 0;

@@ -1192,6 +1192,15 @@ void launch_prefill_seed(const StepBuffers& b, cudaStream_t s) {
     k_prefill_seed<<<1, 512, 0, s>>>(b.state, b.ids, b.lm_val, b.lm_blocks, 0);
 }
 
+void launch_lm_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s) {
+    // One final-normed row as the step's only row: quantised like the verify
+    // path's last RMSNorm output, then the LM head with its first max (lm_val).
+    k_rows_begin<<<1, 1, 0, s>>>(b.state, 1);
+    k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, hidden_row,
+                                                                                        m.dims.hidden, b.act_q, b.act_d);
+    lm_head(m, b, false, s);
+}
+
 void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s) {
     // hidden_row is device memory holding one row; quantise it as row 0 (T is 1 in state).
     k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, hidden_row,

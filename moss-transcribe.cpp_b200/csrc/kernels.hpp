@@ -104,6 +104,9 @@ void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuff
 void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s);
 void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos,
                       float* out, cudaStream_t s);
+// LM head with its first max (b.lm_val) of one final-normed hidden row in
+// device memory, as the step's only row (state T = 1).
+void launch_lm_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s);
 void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s);
 void launch_prefill_seed(const StepBuffers& b, cudaStream_t s);
 
