@@ -62,6 +62,9 @@ MS_NEW = 768  # configs[4]: decoded tokens per recording
 LC_KV = 27000
 LC_STEPS = 50
 PREFILL_LONG_ROWS = 22528  # configs[3]: 60 chunks x 375 audio rows + markers
+F16_CHUNKS = 5  # configs[2]: 5 chunks x 375 audio rows, a marker token per chunk, 64 prompt tokens
+F16_PROMPT_TOKENS = 64
+F16_NEW = 1024
 
 
 def step_bytes(kv_len: int, T: int) -> int:
@@ -279,7 +282,7 @@ def main():
            "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
            "ms_per_step": e2e_s * 1e3 / n_e2e}
 
-    prefill = ms_line = lc_line = None
+    prefill = ms_line = lc_line = f16_line = None
     if not args.no_extras and world == 1:  # per-GPU side measurements: the N=1 run carries them
         # ---- prefill: the prompt rows of configs[1] (375 audio + 32 text rows)
         # through the public run() call, host rows in and hidden rows out; every
@@ -306,6 +309,7 @@ def main():
         pl_dec.close()
         ms_line = multi_stream(model, capi, fixture) if model.persistent_grid > 0 else None
         lc_line = long_context(model, capi, seed_tok)
+        f16_line = f16_recording(capi, fixture, local)
         prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
                    "long": {"rows": PREFILL_LONG_ROWS, "ms": round(pl_s * 1e3, 1),
                             "rows_per_s": round(PREFILL_LONG_ROWS / pl_s, 1)},
@@ -325,7 +329,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32 (fp16 KV)", "data": "synthetic", "config": config,
             "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk,
-            "prefill": prefill, "multi_stream": ms_line, "long_context": lc_line}
+            "prefill": prefill, "multi_stream": ms_line, "long_context": lc_line, "f16_recording": f16_line}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(path, 5)
     if rank == 0:
@@ -448,6 +452,40 @@ def multi_stream(model, capi, fixture) -> dict:
                            "one_recording": {"tokens_per_s": round(one_toks / one_dt, 1), "s": round(one_dt, 3),
                                              "steps": one_steps, "accepted": one_acc},
                            "timing": "host wall clock: mtb_spec_prime (prefill) for each + mtb_spec_run_group"}}
+
+
+def f16_recording(capi, fixture, device: int) -> dict:
+    """configs[2] end to end on one GPU: the F16-weight decoder (random-init
+    N(0, 0.02) like configs[1], stored F16), a 132 s recording's prompt (64
+    prompt tokens, then per chunk a time-marker token and 375 audio rows N(0, 1))
+    fused on the device, prefilled, and 1024 tokens decoded with the device
+    n-gram draft (k = 8) into an fp16 KV cache, all through the public
+    mtb_spec_generate_ids call: host ids and audio rows in, ids out."""
+    shape = fixture.QWEN3_0_6B
+    path = fixture.cached_fixture(shape, seed=0, dtype="f16")
+    model = capi.Model(path, device)
+    rng = np.random.default_rng(132)
+    ids = list(fixture.lcg_ids(F16_PROMPT_TOKENS, shape.vocab, seed=77))
+    markers = fixture.lcg_ids(F16_CHUNKS, shape.vocab, seed=78)
+    for c in range(F16_CHUNKS):
+        ids.append(int(markers[c]))
+        ids.extend([shape.audio_token_id] * 375)
+    ids = np.asarray(ids, dtype=np.int32)
+    audio = rng.standard_normal((F16_CHUNKS * 375, shape.hidden)).astype(np.float32)
+    dec = capi.Decoder(model, len(ids) + F16_NEW + 64, capi.KV_F16, max_new=F16_NEW)
+    dec.spec_generate_ids(ids, audio, shape.audio_token_id, 64, -1, k_max=8)  # warm-up (graphs)
+    dec.rewind(0)
+    t0 = time.perf_counter()
+    out, c = dec.spec_generate_ids(ids, audio, shape.audio_token_id, F16_NEW, -1, k_max=8)
+    dt = time.perf_counter() - t0
+    dec.close()
+    model.close()
+    return {"workload": f"configs[2]: F16 weights, fp16 KV, {len(ids)} prompt rows ({F16_CHUNKS * 375} audio), "
+                        f"{F16_NEW} tokens, device n-gram draft k=8, one recording",
+            "tokens_per_s": round(len(out) / dt, 1), "s": round(dt, 3), "tokens": len(out),
+            "target_calls": c["target_calls"], "accepted": c["accepted"],
+            "path": "F16 GEMV kernels (multi-kernel verify step); the persistent kernel and tcgen05 prefill are q8_0",
+            "timing": "host wall clock around mtb_spec_generate_ids (fuse + prefill + decode), ids read back"}
 
 
 def _device_ids(dec, arr: np.ndarray) -> int:

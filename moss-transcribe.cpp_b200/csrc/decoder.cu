@@ -151,6 +151,16 @@ int upload_q8(mtb_model* m, const GgufFile& f, const std::string& name, int64_t 
     return 0;
 }
 
+// F16 rows [n][k] (ggml layout: k fastest) copied to dst (device) as they are.
+int upload_f16(mtb_model* m, const GgufFile& f, const std::string& name, int64_t k, int64_t n, uint16_t* dst) {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) return fail(m->error, "missing tensor " + name);
+    if (t->type != GGML_F16) return fail(m->error, name + ": an F16 model needs F16 weights throughout");
+    if (t->ne.size() != 2 || t->ne[0] != k || t->ne[1] != n) return fail(m->error, name + ": unexpected shape");
+    MTB_CK(m, cudaMemcpy(dst, t->data, size_t(k) * size_t(n) * 2, cudaMemcpyHostToDevice));
+    return 0;
+}
+
 int upload_f32(mtb_model* m, const GgufFile& f, const std::string& name, int64_t n, const float** out) {
     const GgufTensor* t = f.tensor(name);
     if (!t) return fail(m->error, "missing tensor " + name);
@@ -190,6 +200,52 @@ int load_model(mtb_model* m, const char* path) {
     const int64_t H = d.hidden, F = d.ffn, qd = int64_t(d.n_heads) * kHeadDim, kd = int64_t(d.n_kv) * kHeadDim;
     const GgufTensor* te = f.tensor("token_embd.weight");
     if (!te) return fail(m->error, "missing token_embd.weight");
+    if (te->type == GGML_F16) {
+        // F16 weights: row-major fp16 on the device, the
+        // multi-kernel path with the F16 GEMV kernels; no persistent kernel and
+        // no tcgen05 prefill (both are q8_0 designs).
+        if (std::max(std::max(H, qd), F) > kF16MaxK) return fail(m->error, "F16 model: projection K too large");
+        m->dm.f16 = true;
+        uint16_t* embd16 = nullptr;
+        if (dalloc(m->allocs, m->error, &embd16, size_t(d.vocab) * size_t(H) * 2)) return -1;
+        if (upload_f16(m, f, "token_embd.weight", H, d.vocab, embd16)) return -1;
+        m->dm.h_embd = embd16;
+        if (upload_f32(m, f, "qwen3.output_norm.weight", H, &m->dm.output_norm)) return -1;
+        m->layers.assign(size_t(d.n_layers), LayerWeights{});
+        for (int l = 0; l < d.n_layers; ++l) {
+            const std::string p = "qwen3.blk." + std::to_string(l) + ".";
+            LayerWeights& w = m->layers[size_t(l)];
+            uint16_t *qkv = nullptr, *o = nullptr, *gu = nullptr, *down = nullptr;
+            if (dalloc(m->allocs, m->error, &qkv, size_t(qd + 2 * kd) * size_t(H) * 2) ||
+                dalloc(m->allocs, m->error, &o, size_t(H) * size_t(qd) * 2) ||
+                dalloc(m->allocs, m->error, &gu, size_t(2 * F) * size_t(H) * 2) ||
+                dalloc(m->allocs, m->error, &down, size_t(H) * size_t(F) * 2))
+                return -1;
+            if (upload_f16(m, f, p + "attn_q.weight", H, qd, qkv) ||
+                upload_f16(m, f, p + "attn_k.weight", H, kd, qkv + size_t(qd) * size_t(H)) ||
+                upload_f16(m, f, p + "attn_v.weight", H, kd, qkv + size_t(qd + kd) * size_t(H)) ||
+                upload_f16(m, f, p + "attn_o.weight", qd, H, o) ||
+                upload_f16(m, f, p + "ffn_gate.weight", H, F, gu) ||
+                upload_f16(m, f, p + "ffn_up.weight", H, F, gu + size_t(F) * size_t(H)) ||
+                upload_f16(m, f, p + "ffn_down.weight", F, H, down))
+                return -1;
+            w.h_qkv = qkv;
+            w.h_o = o;
+            w.h_gu = gu;
+            w.h_down = down;
+            if (upload_f32(m, f, p + "attn_norm.weight", H, &w.attn_norm) ||
+                upload_f32(m, f, p + "attn_q_norm.weight", kHeadDim, &w.q_norm) ||
+                upload_f32(m, f, p + "attn_k_norm.weight", kHeadDim, &w.k_norm) ||
+                upload_f32(m, f, p + "ffn_norm.weight", H, &w.ffn_norm))
+                return -1;
+        }
+        m->dm.layers = m->layers.data();
+        m->dm.theta_scale = std::pow(d.theta, -2.0f / float(kHeadDim));
+        MTB_CK(m, configure_kernels());
+        m->mega_grid = 0;
+        MTB_CK(m, cudaDeviceSynchronize());
+        return 0;
+    }
     size_t staging_bytes = te->nbytes;
     for (int l = 0; l < d.n_layers; ++l) {
         for (const char* nm : {"attn_q", "attn_k", "attn_v", "attn_o", "ffn_gate", "ffn_up", "ffn_down"}) {
@@ -601,7 +657,8 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         int32_t* pages = nullptr;
         StepBuffers& b = d->b;
         b.max_chunks = n_pages;
-        b.lm_blocks = lm_head_blocks(dm.vocab);
+        const bool f16 = m->dm.f16;
+        b.lm_blocks = f16 ? (dm.vocab + kF16Outs - 1) / kF16Outs : lm_head_blocks(dm.vocab);
         auto& A = d->allocs;
         auto& E = d->error;
         uint8_t* zero_region = nullptr;
@@ -631,7 +688,9 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
             dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
             return bail();
-        {
+        if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.gu2, size_t(kTMax) * 2 * F * 4)))
+            return bail();
+        if (!f16) {
             // Prefill pass buffers: up to kPrefillRows rows per pass.
             PrefillBuffers& p = d->pf;
             const int G = dm.n_heads / dm.n_kv;

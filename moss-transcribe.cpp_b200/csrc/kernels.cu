@@ -738,6 +738,16 @@ __global__ void k_embed(StepState* st, const uint8_t* __restrict__ embd, int hid
 // dequant (d * q) of token ids[p] from the token_embd tiles, or, where
 // slot[p] >= 0 (the k-th audio placeholder, slots counted on the host), audio
 // row slot[p].  grid (seq), block 256.
+__global__ void k_fuse_embeds_f16(const int32_t* __restrict__ ids, const int32_t* __restrict__ slot, int seq,
+                                  const float* __restrict__ audio, const __half* __restrict__ embd, int hidden,
+                                  float* out) {
+    const int p = blockIdx.x;
+    if (p >= seq) return;
+    const int a = slot[p];
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x)
+        out[(size_t)p * hidden + i] = a >= 0 ? audio[(size_t)a * hidden + i] : __half2float(embd[(size_t)ids[p] * hidden + i]);
+}
+
 __global__ void k_fuse_embeds(const int32_t* __restrict__ ids, const int32_t* __restrict__ slot, int seq,
                               const float* __restrict__ audio, const uint8_t* __restrict__ embd, int hidden,
                               float* out) {
@@ -1034,6 +1044,8 @@ int lm_head_blocks(int vocab) {
     return std::min(148 * 4, (n_rg + 7) / 8);
 }
 
+static void configure_f16_kernels();
+
 cudaError_t configure_kernels() {
     // Dynamic shared memory above 48 KB is opt-in per kernel (current device).
     cudaFuncSetAttribute(k_gemv<EPI_STORE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -1042,12 +1054,245 @@ cudaError_t configure_kernels() {
     cudaFuncSetAttribute(k_gemv<EPI_ARGMAX, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_attn_chunk, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024);
     cudaFuncSetAttribute(k_pf_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPfAttnSmem);
+    configure_f16_kernels();
     pf_configure();
     return cudaGetLastError();
 }
 
+
+// ------------------------------------------------------------ F16 weights
+// Models with F16 weights (configs[2] of the benchmark) run the multi-kernel
+// path with these kernels in place of the q8_0 ones.  ggml's mul_mat with an
+// F16 src0 rounds the activations to fp16 and sums the exact fp16 x fp16
+// products in f32; the order is the one shared with the CPU restatement
+// (orc_mul_mat_f16): each 32-element block one fmaf chain from 0 in ascending
+// order, the blocks of a 256-element slice added in ascending order, then the
+// slices in ascending order.
+
+// RMSNorm of rows < T (the tree of k_rmsnorm_quant) rounded to fp16 (rows >= T
+// zero); `normed` (optional) gets the f32 rows.
+__global__ void __launch_bounds__(kThreads) k_rmsnorm_f16(const StepState* st, const float* __restrict__ x, int K,
+                                                         const float* __restrict__ w, float eps, __half* act,
+                                                         float* normed) {
+    const int row = blockIdx.x;
+    const int T = st->T;
+    if (T <= 0) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ double s_part[kWarps];
+    __shared__ float s_scale;
+    const bool live = row < T;
+    if (live) {
+        double sum = 0.0;
+        for (int i = threadIdx.x; i < K; i += kThreads) {
+            const float v = x[(size_t)row * K + i];
+            sum += (double)(v * v);
+        }
+        sum = warp_sum_d(sum);
+        if (lane == 0) s_part[warp] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            double tot = 0.0;
+            for (int i = 0; i < kWarps; ++i) tot += s_part[i];
+            const float mean = (float)(tot / K);
+            s_scale = 1.0f / sqrtf(mean + eps);
+        }
+        __syncthreads();
+    }
+    const float scale = live ? s_scale : 0.f;
+    for (int i = threadIdx.x; i < K; i += kThreads) {
+        float v = 0.f;
+        if (live) {
+            v = __fmul_rn(__fmul_rn(x[(size_t)row * K + i], scale), w[i]);
+            if (normed) normed[(size_t)row * K + i] = v;
+        }
+        act[(size_t)row * K + i] = __float2half_rn(v);
+    }
+}
+
+// Rows < T of f32 [16][K] rounded to fp16 (rows >= T zero).
+__global__ void k_rows_f16(const StepState* st, const float* __restrict__ src, int K, __half* act) {
+    const int T = st->T;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kTMax * K; i += gridDim.x * blockDim.x)
+        act[i] = __float2half_rn(i / K < T ? src[i] : 0.f);
+}
+
+// silu(gate) * up of gate | up rows [16][2F] (src/qwen3.cpp:193-204, the
+// q8_0 epilogue's expression) rounded to fp16.
+__global__ void k_swiglu_f16(const StepState* st, const float* __restrict__ gu, int F, __half* act) {
+    const int T = st->T;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kTMax * F; i += gridDim.x * blockDim.x) {
+        const int row = i / F, f = i % F;
+        float v = 0.f;
+        if (row < T) {
+            const float g = gu[(size_t)row * 2 * F + f], u = gu[(size_t)row * 2 * F + F + f];
+            const float sl = g / (1.0f + exact_expf(-g));
+            v = sl * u;
+        }
+        act[i] = __float2half_rn(v);
+    }
+}
+
+// Embedding rows of the step's tokens from fp16 token_embd (exact).
+__global__ void k_embed_f16(StepState* st, const __half* __restrict__ embd, int hidden, int vocab, float* x) {
+    const int row = blockIdx.x;
+    const int T = st->T;
+    if (T <= 0) return;
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v = 0.f;
+        if (row < T) {
+            int id = st->tokens[row];
+            if (id < 0 || id >= vocab) {  // ids are validated on the host; never read out of bounds
+                if (i == 0) st->error = 1;
+                id = 0;
+            }
+            v = __half2float(embd[(size_t)id * hidden + i]);
+        }
+        x[(size_t)row * hidden + i] = v;
+    }
+}
+
+// y[t][o] = sum_k act[t][k] W[o][k] for 32 outputs o per block of 256 threads
+// (lane = output), rows t < T.  Warp w takes block w of every 256-element
+// slice: 4 x 16-byte loads of its output's 32 weights, then the block's fmaf
+// chain for all 16 rows (two rows per __ffma2_rn: each component its own
+// chain) from the activations staged in shared memory as f32 [K][16]
+// (broadcast reads).  Block sums meet in shared memory; each thread adds the
+// 8 blocks of a slice in order for its output and rows w, w + 8, and keeps the
+// slice total.  Epilogues: store, residual add, or the first max over the 32
+// outputs per row (plus the logits when asked).
+enum EpiF16 { F16_STORE = 0, F16_RESID = 1, F16_ARGMAX = 2 };
+template <int EPI>
+__global__ void __launch_bounds__(256) k_gemv_f16(const __half* __restrict__ W, int N, int K,
+                                                  const __half* __restrict__ act, const StepState* st, float* out,
+                                                  int ld, float2* lm_val) {
+    const int T = st->T;
+    if (T <= 0) return;
+    extern __shared__ __align__(16) float sm_f16[];
+    float* xs = sm_f16;                    // [K][16]
+    float* bs = xs + (size_t)K * kTMax;    // [8 blocks][16 rows][32 outputs]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < kTMax * K; i += 256) {
+        const int t = i / K, k = i % K;
+        xs[k * kTMax + t] = __half2float(act[i]);
+    }
+    __syncthreads();
+    const int o = blockIdx.x * kF16Outs + lane;
+    float tot[2] = {0.f, 0.f};  // rows warp, warp + 8
+    for (int s0 = 0; s0 < K; s0 += 256) {
+        const int b0 = s0 + 32 * warp;  // this warp's block of the slice
+        float2 acc[kTMax / 2];
+#pragma unroll
+        for (int p = 0; p < kTMax / 2; ++p) acc[p] = make_float2(0.f, 0.f);
+        if (o < N) {
+            const uint4* wp = reinterpret_cast<const uint4*>(W + (size_t)o * K + b0);
+            uint4 wr[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) wr[u] = __ldg(wp + u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const float wj = __half2float(reinterpret_cast<const __half*>(wr)[j]);
+                const float2 w2 = make_float2(wj, wj);
+                const float4* xr = reinterpret_cast<const float4*>(xs + (size_t)(b0 + j) * kTMax);
+#pragma unroll
+                for (int q = 0; q < kTMax / 4; ++q) {
+                    const float4 xv = xr[q];
+                    acc[2 * q] = __ffma2_rn(make_float2(xv.x, xv.y), w2, acc[2 * q]);
+                    acc[2 * q + 1] = __ffma2_rn(make_float2(xv.z, xv.w), w2, acc[2 * q + 1]);
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < kTMax / 2; ++p) {
+            bs[(warp * kTMax + 2 * p) * 32 + lane] = acc[p].x;
+            bs[(warp * kTMax + 2 * p + 1) * 32 + lane] = acc[p].y;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int t = warp + 8 * h;
+            float a = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) a = a + bs[(i * kTMax + t) * 32 + lane];
+            tot[h] = tot[h] + a;
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int t = warp + 8 * h;
+        if (EPI == F16_ARGMAX) {
+            float bv = (t < T && o < N) ? tot[h] : -INFINITY;
+            int bi = (t < T && o < N) ? o : 0x7fffffff;
+            if (out && t < T && o < N) out[(size_t)t * ld + o] = tot[h];
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if (lane == 0) lm_val[(size_t)blockIdx.x * kTMax + t] = make_float2(bv, __int_as_float(bi));
+        } else if (t < T && o < N) {
+            if (EPI == F16_STORE) out[(size_t)t * ld + o] = tot[h];
+            else out[(size_t)t * ld + o] = out[(size_t)t * ld + o] + tot[h];
+        }
+    }
+}
+
+static size_t gemv_f16_smem(int K) { return ((size_t)K * kTMax + 8 * kTMax * 32) * sizeof(float); }
+constexpr int kF16GemvSmemMax = 227 * 1024;  // K <= kF16MaxK: the loader checks F16 models against it
+
+static void configure_f16_kernels() {
+    cudaFuncSetAttribute(k_gemv_f16<F16_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
+    cudaFuncSetAttribute(k_gemv_f16<F16_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
+    cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
+}
+
+template <int EPI>
+static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const StepState* st, float* out, int ld,
+                     float2* lm_val, cudaStream_t s) {
+    k_gemv_f16<EPI><<<(N + kF16Outs - 1) / kF16Outs, 256, gemv_f16_smem(K), s>>>(
+        reinterpret_cast<const __half*>(W), N, K, reinterpret_cast<const __half*>(act), st, out, ld, lm_val);
+}
+
+// forward_layers for F16 weights: the same sequence with fp16 activations.
+static void forward_layers_f16(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, cudaStream_t s) {
+    const ModelDims& d = m.dims;
+    const int H = d.hidden, F = d.ffn;
+    const int qd = d.n_heads * kHeadDim, kd = d.n_kv * kHeadDim;
+    const size_t attn_smem = (size_t)(kTMax * 4 * kHeadDim + kPage * (kHeadDim + 1) + kTMax * 4 * kPage) * sizeof(float);
+    __half* act = reinterpret_cast<__half*>(b.act_h);
+    for (int l = 0; l < d.n_layers; ++l) {
+        const LayerWeights& w = m.layers[l];
+        k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.attn_norm, d.eps, act, nullptr);
+        gemv_f16<F16_STORE>(w.h_qkv, qd + 2 * kd, H, b.act_h, b.state, b.qkv, qd + 2 * kd, nullptr, s);
+        k_qk_norm_rope_store<<<dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, w.q_norm,
+                                                                             w.k_norm, d.eps, m.theta_scale, kv, l, -1, 0);
+        k_attn_chunk<<<dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, kv, l,
+                                                                              b.part_o, b.part_ml, b.max_chunks, -1, 0,
+                                                                              kTMax * 4);
+        k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
+                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4);
+        k_rows_f16<<<64, 256, 0, s>>>(b.state, b.attn_out, qd, act);
+        gemv_f16<F16_RESID>(w.h_o, H, qd, b.act_h, b.state, b.x, H, nullptr, s);
+        k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.ffn_norm, d.eps, act, nullptr);
+        gemv_f16<F16_STORE>(w.h_gu, 2 * F, H, b.act_h, b.state, b.gu2, 2 * F, nullptr, s);
+        k_swiglu_f16<<<96, 256, 0, s>>>(b.state, b.gu2, F, act);
+        gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h, b.state, b.x, H, nullptr, s);
+    }
+    k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, act, b.hid);
+}
+
+static void lm_head_f16(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {
+    gemv_f16<F16_ARGMAX>(m.h_embd, m.dims.vocab, m.dims.hidden, b.act_h, b.state, want_logits ? b.logits : nullptr,
+                         m.dims.vocab, b.lm_val, s);
+}
+
 // Layers, final norm and (optionally) the LM head for the rows in b.x.
 static void forward_layers(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, cudaStream_t s) {
+    if (m.f16) {
+        forward_layers_f16(m, kv, b, s);
+        return;
+    }
     const ModelDims& d = m.dims;
     const int H = d.hidden, F = d.ffn;
     const int qd = d.n_heads * kHeadDim, kd = d.n_kv * kHeadDim;
@@ -1123,6 +1368,10 @@ void launch_prefill_pass(const DeviceModel& m, const KvCache& kv, const PrefillB
 }
 
 static void lm_head(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {
+    if (m.f16) {
+        lm_head_f16(m, b, want_logits, s);
+        return;
+    }
     GemvArgs a{m.embd, m.dims.vocab / kTileRows, m.dims.hidden / kTileK, b.act_q, b.act_d,
                nullptr, m.dims.vocab, b.state, b.lm_val, want_logits ? b.logits : nullptr};
     gemv<EPI_ARGMAX, 8>(a, b.lm_blocks, s);
@@ -1132,7 +1381,11 @@ void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, 
                  cudaStream_t s) {
     if (draft_mode == 0) k_draft<<<1, 256, 0, s>>>(b.state, b.ids);
     else if (draft_mode == 1) k_draft_forced<<<1, 1, 0, s>>>(b.state);
-    k_embed<<<kTMax, 256, 0, s>>>(b.state, m.embd, m.dims.hidden, m.dims.vocab, b.x);
+    if (m.f16)
+        k_embed_f16<<<kTMax, 256, 0, s>>>(b.state, reinterpret_cast<const __half*>(m.h_embd), m.dims.hidden,
+                                          m.dims.vocab, b.x);
+    else
+        k_embed<<<kTMax, 256, 0, s>>>(b.state, m.embd, m.dims.hidden, m.dims.vocab, b.x);
     forward_layers(m, kv, b, s);
     const bool penalty_path = want_logits;
     lm_head(m, b, penalty_path, s);
@@ -1182,7 +1435,11 @@ void launch_lm_argmax_rows(const DeviceModel& m, StepState* state, const float* 
 
 void launch_fuse_embeds(const DeviceModel& m, const int32_t* ids, const int32_t* slot, int seq, const float* audio,
                         float* out, cudaStream_t s) {
-    k_fuse_embeds<<<seq, 256, 0, s>>>(ids, slot, seq, audio, m.embd, m.dims.hidden, out);
+    if (m.f16)
+        k_fuse_embeds_f16<<<seq, 256, 0, s>>>(ids, slot, seq, audio, reinterpret_cast<const __half*>(m.h_embd),
+                                              m.dims.hidden, out);
+    else
+        k_fuse_embeds<<<seq, 256, 0, s>>>(ids, slot, seq, audio, m.embd, m.dims.hidden, out);
 }
 
 void launch_rows_begin(const StepBuffers& b, int T, cudaStream_t s) { k_rows_begin<<<1, 1, 0, s>>>(b.state, T); }
@@ -1196,6 +1453,11 @@ void launch_lm_row(const DeviceModel& m, const StepBuffers& b, const float* hidd
     // One final-normed row as the step's only row: quantised like the verify
     // path's last RMSNorm output, then the LM head with its first max (lm_val).
     k_rows_begin<<<1, 1, 0, s>>>(b.state, 1);
+    if (m.f16) {
+        k_rows_f16<<<64, 256, 0, s>>>(b.state, hidden_row, m.dims.hidden, reinterpret_cast<__half*>(b.act_h));
+        lm_head(m, b, false, s);
+        return;
+    }
     k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, hidden_row,
                                                                                         m.dims.hidden, b.act_q, b.act_d);
     lm_head(m, b, false, s);
@@ -1203,6 +1465,11 @@ void launch_lm_row(const DeviceModel& m, const StepBuffers& b, const float* hidd
 
 void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s) {
     // hidden_row is device memory holding one row; quantise it as row 0 (T is 1 in state).
+    if (m.f16) {
+        k_rows_f16<<<64, 256, 0, s>>>(b.state, hidden_row, m.dims.hidden, reinterpret_cast<__half*>(b.act_h));
+        lm_head(m, b, true, s);
+        return;
+    }
     k_quant_rows<<<(m.dims.hidden / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, hidden_row,
                                                                                         m.dims.hidden, b.act_q, b.act_d);
     lm_head(m, b, true, s);

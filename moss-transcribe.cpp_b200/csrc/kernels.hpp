@@ -21,8 +21,10 @@ struct StepBuffers {
     float2* part_ml;        // (max, sum) per partial
     float2* lm_val;         // LM-head argmax partials (value, index-as-float bits)
     float* logits;          // [kTMax][vocab] (penalty path and tests), may be null
+    uint16_t* act_h;        // F16 models: fp16 activation rows [kTMax][max(hidden, n_heads*128, ffn)]
+    float* gu2;             // F16 models: gate | up rows [kTMax][2 ffn]
     int max_chunks;
-    int lm_blocks;
+    int lm_blocks;          // LM-head partial blocks per row (q8_0: lm_head_blocks; F16: vocab / 32)
 };
 
 // Extra buffers of the persistent verify-step kernel.
@@ -74,7 +76,15 @@ struct DeviceModel {
     const uint8_t* pf_embd;  // token_embd as tcgen05 weight steps (LM head of the persistent step), or null
     const float* output_norm;
     float theta_scale;       // powf(rope_theta, -2/128), computed on the host
+    bool f16;                // F16 weights: h_embd and LayerWeights::h_* instead of the q8_0 tiles
+    const uint16_t* h_embd;  // F16 models: token_embd [vocab][hidden] fp16 (also the tied LM head)
 };
+
+// LM-head partial blocks per row of an F16 model (32 vocab rows per block).
+constexpr int kF16Outs = 32;
+// Largest projection K of an F16 model (its activations staged as f32 [K][16]
+// in one block's shared memory next to 16 KB of block sums, within 227 KB).
+constexpr int kF16MaxK = (227 * 1024 - 8 * 16 * 32 * 4) / (16 * 4);
 
 // q8_0 rows -> tiles (src: raw ggml blocks, n_rows x k).  Destination row group
 // for source row group r is r * rg_stride + rg_offset.

@@ -48,6 +48,8 @@ struct LayerWeights {
     const float *attn_norm, *q_norm, *k_norm, *ffn_norm;
     // The same matrices as prefill weight steps (tcgen05 operand layout, prefill_tc.cu).
     const uint8_t *pf_qkv, *pf_o, *pf_gu, *pf_down;
+    // F16 models instead: row-major fp16 [rows][K], q|k|v and gate|up rows concatenated.
+    const uint16_t *h_qkv, *h_o, *h_gu, *h_down;
 };
 
 struct ModelDims {

@@ -65,6 +65,10 @@ extern "C" int mtb_lm_head_argmax_noalloc(const mtb_model* m, const float* hidde
     int device = 0;
     if (mtb_model_device_view(m, &view, &device) != 0) { g_noalloc_error = "invalid model"; return -1; }
     const DeviceModel& dm = *static_cast<const DeviceModel*>(view);
+    if (dm.f16) {
+        g_noalloc_error = "the no-allocation LM head takes q8_0 models only";
+        return -2;
+    }
     if (T < 1 || T > kTMax) {
         g_noalloc_error = "T must be in [1, 16] (the scratch holds 16 rows)";
         return -2;

@@ -137,16 +137,17 @@ PARITY_SCALES = {"weight_std": 0.06, "embd_std": 0.2}
 
 
 def cached_fixture(shape: DecoderShape = QWEN3_0_6B, seed: int = 0, directory: str | None = None,
-                   parity: bool = False) -> str:
-    """Path of the fixture for (shape, seed[, parity scales]), writing it on first use."""
+                   parity: bool = False, dtype: str = "q8_0") -> str:
+    """Path of the fixture for (shape, seed[, parity scales][, dtype]), writing it on first use."""
     directory = directory or os.environ.get("MTB_FIXTURE_DIR", "/tmp/mtb_fixtures")
     os.makedirs(directory, exist_ok=True)
     tag = "qwen3_0_6b" if shape == QWEN3_0_6B else "tiny" if shape == TINY else \
         "x".join(str(v) for v in asdict(shape).values())
-    path = os.path.join(directory, f"{tag}_seed{seed}{'_parity' if parity else ''}.gguf")
+    suffix = ("_parity" if parity else "") + ("" if dtype == "q8_0" else f"_{dtype}")
+    path = os.path.join(directory, f"{tag}_seed{seed}{suffix}.gguf")
     if not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        write_fixture(tmp, shape, seed, **(PARITY_SCALES if parity else {}))
+        write_fixture(tmp, shape, seed, dtype=dtype, **(PARITY_SCALES if parity else {}))
         os.replace(tmp, path)
     return path
 

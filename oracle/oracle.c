@@ -227,6 +227,44 @@ void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int
     free(xq);
 }
 
+/* ------------------------------------------------------------------ f16 */
+
+/* F16 weights (configs[2] of the benchmark): ggml's mul_mat with an F16 src0
+ * converts src1 to F16 (its vec_dot_type) and accumulates the F16 x F16
+ * products in f32.  The products of two fp16 values are exact in f32; the
+ * order of the sums is the one this oracle and the CUDA kernels share: each
+ * 32-element block one fmaf chain from 0 in ascending order, the blocks of a
+ * 256-element slice added in ascending order, then the slices in ascending
+ * order (the q8_0 dot's slice structure, with the block sum in place of the
+ * integer block sum x scale). */
+static inline float dot_f16(const uint16_t* w, const uint16_t* xh, int k) {
+    float total = 0.0f;
+    for (int s0 = 0; s0 < k; s0 += 256) {
+        float acc = 0.0f;
+        for (int b = s0; b < s0 + 256 && b < k; b += 32) {
+            float bs = 0.0f;
+            for (int j = 0; j < 32; ++j) bs = fmaf(h2f(xh[b + j]), h2f(w[b + j]), bs);
+            acc = acc + bs;
+        }
+        total = total + acc;
+    }
+    return total;
+}
+
+/* ggml_mul_mat(W f16 [n_rows x k], x f32 [T x k]) -> y [T x n_rows]; x is
+ * rounded to fp16 first (round to nearest even). */
+void orc_mul_mat_f16(const void* w_half, int n_rows, int k, const float* x, int T, float* y) {
+    uint16_t* xh = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)k * (size_t)T);
+    for (size_t i = 0; i < (size_t)k * (size_t)T; ++i) xh[i] = f2h(x[i]);
+    const uint16_t* w = (const uint16_t*)w_half;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < n_rows; ++n) {
+        const uint16_t* row = w + (size_t)n * k;
+        for (int t = 0; t < T; ++t) y[(size_t)t * n_rows + n] = dot_f16(row, xh + (size_t)t * k, k);
+    }
+    free(xh);
+}
+
 /* ------------------------------------------------------------- model */
 
 typedef struct {
@@ -236,6 +274,7 @@ typedef struct {
 
 struct orc_model {
     int hidden, n_layers, n_heads, n_kv, head_dim, ffn, vocab;
+    int wtype;  /* ORC_Q8_0 or ORC_F16: token_embd and every projection (set by the first of them) */
     float eps, theta;
     const void* token_embd;
     const float* output_norm;
@@ -270,7 +309,8 @@ void orc_model_free(orc_model* m) {
 int orc_model_set_tensor(orc_model* m, const char* name, const void* data, int type) {
     if (!m || !name || !data) return -1;
     if (!strcmp(name, "token_embd.weight")) {
-        if (type != ORC_Q8_0) return -2;
+        if ((type != ORC_Q8_0 && type != ORC_F16) || (m->wtype && type != m->wtype)) return -2;
+        m->wtype = type;
         m->token_embd = data;
         return 0;
     }
@@ -296,7 +336,8 @@ int orc_model_set_tensor(orc_model* m, const char* name, const void* data, int t
     for (size_t i = 0; i < sizeof(map) / sizeof(map[0]); ++i) {
         if (strcmp(field, map[i].n)) continue;
         if (map[i].q) {
-            if (type != ORC_Q8_0) return -2;
+            if ((type != ORC_Q8_0 && type != ORC_F16) || (m->wtype && type != m->wtype)) return -2;
+            m->wtype = type;
             *map[i].q = data;
         } else {
             if (type != ORC_F32) return -2;
@@ -316,6 +357,14 @@ int orc_model_check(const orc_model* m) {
             return -2 - l;
     }
     return 0;
+}
+
+/* The model's projection: q8_0 or f16 weights. */
+static void mul_mat_w(const orc_model* m, const void* w, int n_rows, int k, const float* x, int T, float* y) {
+    if (m->wtype == ORC_F16)
+        orc_mul_mat_f16(w, n_rows, k, x, T, y);
+    else
+        orc_mul_mat_q8(w, n_rows, k, x, T, y);
 }
 
 /* ------------------------------------------------------------- decoder */
@@ -468,9 +517,9 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     for (int l = 0; l < m->n_layers; ++l) {
         const orc_layer* L = &m->layers[l];
         for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H, 256);
-        orc_mul_mat_q8(L->wq, qd, H, xn, T, q);
-        orc_mul_mat_q8(L->wk, kd, H, xn, T, k);
-        orc_mul_mat_q8(L->wv, kd, H, xn, T, v);
+        mul_mat_w(d->m, L->wq, qd, H, xn, T, q);
+        mul_mat_w(d->m, L->wk, kd, H, xn, T, k);
+        mul_mat_w(d->m, L->wv, kd, H, xn, T, v);
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 float* qh = q + (size_t)t * qd + (size_t)h * hd;
@@ -555,13 +604,13 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
                 free(cm); free(cl); free(co);
             }
         }
-        orc_mul_mat_q8(L->wo, H, qd, o, T, proj);
+        mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
         for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 256);
-        orc_mul_mat_q8(L->wgate, F, H, xn, T, g);
-        orc_mul_mat_q8(L->wup, F, H, xn, T, u);
+        mul_mat_w(d->m, L->wgate, F, H, xn, T, g);
+        mul_mat_w(d->m, L->wup, F, H, xn, T, u);
         for (size_t i = 0; i < (size_t)T * F; ++i) g[i] = silu(g[i]) * u[i];
-        orc_mul_mat_q8(L->wdown, H, F, g, T, proj);
+        mul_mat_w(d->m, L->wdown, H, F, g, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
     }
     for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 256);
@@ -570,14 +619,24 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     return 0;
 }
 
-/* src/qwen3_decoder.cpp:174-206: token_embd (q8_0) @ hidden, one row. */
+/* src/qwen3_decoder.cpp:174-206: token_embd (q8_0 or f16) @ hidden, one row. */
 void orc_decoder_logits(const orc_decoder* d, const float* hidden_row, float* logits) {
-    orc_mul_mat_q8(d->m->token_embd, d->m->vocab, d->m->hidden, hidden_row, 1, logits);
+    mul_mat_w(d->m, d->m->token_embd, d->m->vocab, d->m->hidden, hidden_row, 1, logits);
 }
 
-/* src/generate.cpp:33-66: get_rows / to_float of q8_0 rows: y = d * q. */
+/* src/generate.cpp:33-66: get_rows / to_float of q8_0 rows (y = d * q) or
+ * f16 rows (exact). */
 int orc_embed_rows(const orc_model* m, const int32_t* ids, int n, float* out) {
     if (!m || !ids || n <= 0) return -1;
+    if (m->wtype == ORC_F16) {
+        const uint16_t* tok = (const uint16_t*)m->token_embd;
+        for (int p = 0; p < n; ++p) {
+            if (ids[p] < 0 || ids[p] >= m->vocab) return -2;
+            for (int i = 0; i < m->hidden; ++i)
+                out[(size_t)p * m->hidden + i] = h2f(tok[(size_t)ids[p] * m->hidden + i]);
+        }
+        return 0;
+    }
     const int nb = m->hidden / 32;
     const blk_q8* tok = (const blk_q8*)m->token_embd;
     for (int p = 0; p < n; ++p) {

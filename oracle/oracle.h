@@ -140,6 +140,9 @@ int orc_greedy_generate(orc_decoder* d, const float* fused, int seq, int max_new
 void orc_quantize_act_q8(const float* x, int64_t k, void* out_blocks);
 void orc_quantize_ref_q8(const float* x, int64_t k, void* out_blocks);
 void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int T, float* y);
+/* The same for f16 weights [n_rows x k]: x rounded to fp16, exact products,
+ * 32-element fmaf chains, blocks then 256-element slices added in order. */
+void orc_mul_mat_f16(const void* w_half, int n_rows, int k, const float* x, int T, float* y);
 void orc_set_threads(int n);
 /* The exp / sin / cos the oracle (and the CUDA kernels) evaluate. */
 float orc_expf(float x);

@@ -71,6 +71,7 @@ def lib():
         L.orc_quantize_act_q8.argtypes = [f32p, C.c_int64, vp]
         L.orc_quantize_ref_q8.argtypes = [f32p, C.c_int64, vp]
         L.orc_mul_mat_q8.argtypes = [vp, C.c_int, C.c_int, f32p, C.c_int, f32p]
+        L.orc_mul_mat_f16.argtypes = [vp, C.c_int, C.c_int, f32p, C.c_int, f32p]
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
@@ -120,6 +121,16 @@ def mul_mat_q8(w_raw: np.ndarray, n_rows: int, k: int, x: np.ndarray) -> np.ndar
     y = np.zeros((x.shape[0], n_rows), dtype=np.float32)
     w_raw = np.ascontiguousarray(w_raw)
     lib().orc_mul_mat_q8(w_raw.ctypes.data, n_rows, k, _f32(x), x.shape[0], _f32(y))
+    return y
+
+
+def mul_mat_f16(w: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """y = x @ w.T for fp16 weights w [n_rows, k] in the order orc_mul_mat_f16 fixes."""
+    w = np.ascontiguousarray(w, dtype=np.float16)
+    n_rows, k = w.shape
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, k)
+    y = np.zeros((x.shape[0], n_rows), dtype=np.float32)
+    lib().orc_mul_mat_f16(w.ctypes.data, n_rows, k, _f32(x), x.shape[0], _f32(y))
     return y
 
 

@@ -35,6 +35,19 @@ def tiny_bench_gguf(fixture_dir):
 
 
 @pytest.fixture(scope="session")
+def tiny_f16_gguf(fixture_dir):
+    """The tiny parity model with F16 weights (token_embd and projections)."""
+    from mtb import fixture
+    return fixture.cached_fixture(fixture.TINY, seed=0, directory=fixture_dir, parity=True, dtype="f16")
+
+
+@pytest.fixture(scope="session")
+def tiny_f16_oracle(tiny_f16_gguf):
+    import oracle
+    return oracle.OracleModel(tiny_f16_gguf)
+
+
+@pytest.fixture(scope="session")
 def tiny_oracle(tiny_gguf):
     import oracle
     return oracle.OracleModel(tiny_gguf)

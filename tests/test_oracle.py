@@ -5,7 +5,8 @@ These pin the CPU restatement before it is trusted as the checker:
   - draft() outputs of the reference's replay tool cpu-lab/moss_ngram_audit.py
     (tests/golden/ngram_draft.json, made by tests/golden/make_golden.py);
   - replay() counters of that tool against the oracle's controller;
-  - gguf.quantize (the reference converter's q8_0 quantiser) byte for byte.
+  - gguf.quantize (the reference converter's q8_0 quantiser) byte for byte;
+  - the F16 dot order against a numpy restatement and a float64 product.
 """
 import json
 import os
@@ -90,6 +91,44 @@ def test_mul_mat_integer_part_is_exact(tiny_oracle):
         xq = xb[:, 2:].view(np.int8).astype(np.int64)
         exact = ((wq * xq[None]).sum(-1) * wd * xd[None]).sum(-1)
         np.testing.assert_allclose(y[t], exact, rtol=1e-5, atol=1e-5)
+
+
+def test_mul_mat_f16_order_and_accuracy():
+    """orc_mul_mat_f16: activations rounded to fp16, each 32-element block a
+    chain from 0, blocks then 256-element slices added in order.  A product of
+    two fp16 values is exact in f32, so fmaf(x, w, acc) == acc + x * w in f32
+    and numpy restates the order bit for bit."""
+    rng = np.random.default_rng(3)
+    n, k = 96, 768
+    w = (0.05 * rng.standard_normal((n, k))).astype(np.float16)
+    x = rng.standard_normal((4, k)).astype(np.float32)
+    y = oracle.mul_mat_f16(w, x)
+    xh = x.astype(np.float16).astype(np.float32)
+    wf = w.astype(np.float32)
+    want = np.zeros((4, n), dtype=np.float32)
+    for s0 in range(0, k, 256):
+        acc = np.zeros((4, n), dtype=np.float32)
+        for b in range(s0, s0 + 256, 32):
+            bs = np.zeros((4, n), dtype=np.float32)
+            for j in range(b, b + 32):
+                bs = bs + xh[:, j:j + 1] * wf[None, :, j]
+            acc = acc + bs
+        want = want + acc
+    np.testing.assert_array_equal(y, want)
+    exact = xh.astype(np.float64) @ wf.astype(np.float64).T
+    np.testing.assert_allclose(y, exact, rtol=1e-5, atol=1e-5)
+
+
+def test_f16_model_speculative_equals_serial_greedy(tiny_f16_oracle):
+    m = tiny_f16_oracle
+    rng = np.random.default_rng(5)
+    fused = np.concatenate([(0.2 * rng.standard_normal((24, m.shape.hidden))).astype(np.float32),
+                            m.embed(np.arange(8) * 37 + 11)])
+    d = oracle.OracleDecoder(m, 128)
+    greedy = d.greedy_generate(fused, 40, -1)
+    ids, counters = d.spec_generate(fused, 40, -1, k_max=4)
+    assert ids == greedy and len(ids) == 40
+    assert counters["accepted"] > 0
 
 
 def _prompt(m, n_audio=40, n_text=8):
