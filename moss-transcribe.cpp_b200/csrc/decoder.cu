@@ -151,13 +151,19 @@ int upload_q8(mtb_model* m, const GgufFile& f, const std::string& name, int64_t 
     return 0;
 }
 
-// F16 rows [n][k] (ggml layout: k fastest) copied to dst (device) as they are.
-int upload_f16(mtb_model* m, const GgufFile& f, const std::string& name, int64_t k, int64_t n, uint16_t* dst) {
+// F16 rows [n][k] (ggml layout: k fastest) through `staging` into dst in the
+// tiled layout of the F16 kernels (launch_repack_f16).
+int upload_f16(mtb_model* m, const GgufFile& f, const std::string& name, int64_t k, int64_t n, uint16_t* staging,
+               uint16_t* dst) {
     const GgufTensor* t = f.tensor(name);
     if (!t) return fail(m->error, "missing tensor " + name);
     if (t->type != GGML_F16) return fail(m->error, name + ": an F16 model needs F16 weights throughout");
     if (t->ne.size() != 2 || t->ne[0] != k || t->ne[1] != n) return fail(m->error, name + ": unexpected shape");
-    MTB_CK(m, cudaMemcpy(dst, t->data, size_t(k) * size_t(n) * 2, cudaMemcpyHostToDevice));
+    if (n % 32 || k % 32) return fail(m->error, name + ": F16 matrices need multiples of 32 rows and columns");
+    MTB_CK(m, cudaMemcpy(staging, t->data, size_t(k) * size_t(n) * 2, cudaMemcpyHostToDevice));
+    launch_repack_f16(staging, int(n), int(k), dst, nullptr);
+    MTB_CK(m, cudaGetLastError());
+    MTB_CK(m, cudaDeviceSynchronize());
     return 0;
 }
 
@@ -201,14 +207,19 @@ int load_model(mtb_model* m, const char* path) {
     const GgufTensor* te = f.tensor("token_embd.weight");
     if (!te) return fail(m->error, "missing token_embd.weight");
     if (te->type == GGML_F16) {
-        // F16 weights: row-major fp16 on the device, the
-        // multi-kernel path with the F16 GEMV kernels; no persistent kernel and
-        // no tcgen05 prefill (both are q8_0 designs).
+        // F16 weights: fp16 on the device in the F16 kernels'
+        // tiled layout, the multi-kernel path with the F16 GEMV kernels; no
+        // persistent kernel and no tcgen05 prefill (both are q8_0 designs).
         if (std::max(std::max(H, qd), F) > kF16MaxK) return fail(m->error, "F16 model: projection K too large");
         m->dm.f16 = true;
+        const size_t staging_halves = std::max(size_t(d.vocab) * size_t(H), size_t(std::max(qd, 2 * F)) * size_t(H));
+        uint16_t* stg = nullptr;
+        std::vector<void*> tmp;
+        if (dalloc(tmp, m->error, &stg, std::max(staging_halves, size_t(H) * size_t(F)) * 2)) return -1;
+        struct Guard { std::vector<void*>& v; ~Guard() { for (void* p : v) cudaFree(p); } } guard{tmp};
         uint16_t* embd16 = nullptr;
         if (dalloc(m->allocs, m->error, &embd16, size_t(d.vocab) * size_t(H) * 2)) return -1;
-        if (upload_f16(m, f, "token_embd.weight", H, d.vocab, embd16)) return -1;
+        if (upload_f16(m, f, "token_embd.weight", H, d.vocab, stg, embd16)) return -1;
         m->dm.h_embd = embd16;
         if (upload_f32(m, f, "qwen3.output_norm.weight", H, &m->dm.output_norm)) return -1;
         m->layers.assign(size_t(d.n_layers), LayerWeights{});
@@ -221,13 +232,13 @@ int load_model(mtb_model* m, const char* path) {
                 dalloc(m->allocs, m->error, &gu, size_t(2 * F) * size_t(H) * 2) ||
                 dalloc(m->allocs, m->error, &down, size_t(H) * size_t(F) * 2))
                 return -1;
-            if (upload_f16(m, f, p + "attn_q.weight", H, qd, qkv) ||
-                upload_f16(m, f, p + "attn_k.weight", H, kd, qkv + size_t(qd) * size_t(H)) ||
-                upload_f16(m, f, p + "attn_v.weight", H, kd, qkv + size_t(qd + kd) * size_t(H)) ||
-                upload_f16(m, f, p + "attn_o.weight", qd, H, o) ||
-                upload_f16(m, f, p + "ffn_gate.weight", H, F, gu) ||
-                upload_f16(m, f, p + "ffn_up.weight", H, F, gu + size_t(F) * size_t(H)) ||
-                upload_f16(m, f, p + "ffn_down.weight", F, H, down))
+            if (upload_f16(m, f, p + "attn_q.weight", H, qd, stg, qkv) ||
+                upload_f16(m, f, p + "attn_k.weight", H, kd, stg, qkv + size_t(qd) * size_t(H)) ||
+                upload_f16(m, f, p + "attn_v.weight", H, kd, stg, qkv + size_t(qd + kd) * size_t(H)) ||
+                upload_f16(m, f, p + "attn_o.weight", qd, H, stg, o) ||
+                upload_f16(m, f, p + "ffn_gate.weight", H, F, stg, gu) ||
+                upload_f16(m, f, p + "ffn_up.weight", H, F, stg, gu + size_t(F) * size_t(H)) ||
+                upload_f16(m, f, p + "ffn_down.weight", F, H, stg, down))
                 return -1;
             w.h_qkv = qkv;
             w.h_o = o;
@@ -688,7 +699,9 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
             dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
             return bail();
-        if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.gu2, size_t(kTMax) * 2 * F * 4)))
+        if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.gu2, size_t(kTMax) * 2 * F * 4) ||
+                    dalloc(A, E, &b.f16_part, f16_part_floats(dm) * 4) ||
+                    dalloc(A, E, &b.f16_cnt, size_t(f16_groups_max(dm)) * 4)))
             return bail();
         if (!f16) {
             // Prefill pass buffers: up to kPrefillRows rows per pass.

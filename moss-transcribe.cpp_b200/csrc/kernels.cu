@@ -368,6 +368,106 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
 
 // ------------------------------------------------------------ attention
 
+// 16-byte chunks r[u] (chunk tid + 256 u of n16) of a chunk's contiguous K or
+// V rows [n_pos][128] (fp16 or f32) -> f32 rows [64][129] in shared memory.
+__device__ __forceinline__ void kv_rows_to_smem(const uint4 (&r)[8], int n16, bool f16, float* dst) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int i = threadIdx.x + u * kThreads;
+        if (i >= n16) continue;
+        if (f16) {
+            const __half* hv = reinterpret_cast<const __half*>(&r[u]);
+            const int e0 = i * 8, p = e0 / kHeadDim, d0 = e0 % kHeadDim;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) dst[p * (kHeadDim + 1) + d0 + e] = __half2float(hv[e]);
+        } else {
+            const float* fv = reinterpret_cast<const float*>(&r[u]);
+            const int e0 = i * 4, p = e0 / kHeadDim, d0 = e0 % kHeadDim;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[p * (kHeadDim + 1) + d0 + e] = fv[e];
+        }
+    }
+}
+
+// Scores of k_attn_chunk: thread (position p, row group qg) forms rows qg,
+// qg + 4, ... (at most NR of them) at p, so each K element loaded once feeds
+// every row and the q rows are warp-uniform broadcast reads (16 bytes = two
+// dim pairs).  Per row: the even-dim and odd-dim fmaf chains in dim order,
+// then (even + odd) x scale; masked positions -inf.
+template <int NR>
+__device__ __forceinline__ void attn_scores(const float* sq, const float* sk, float* sp, int NQ, int G, int n_pos,
+                                            int p0, int before, float scale) {
+    static_assert(kThreads == 256 && kPage == 64 && kHeadDim == 128, "thread roles");
+    const int p = threadIdx.x & (kPage - 1), qg = threadIdx.x >> 6;
+    const int nr = (NQ - qg + 3) >> 2;
+    float ae[NR], ao[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) ae[r] = ao[r] = 0.f;
+    if (p < n_pos) {
+        const float* ka = sk + p * (kHeadDim + 1);
+#pragma unroll 2
+        for (int d = 0; d < kHeadDim; d += 4) {
+            const float k0 = ka[d], k1 = ka[d + 1], k2 = ka[d + 2], k3 = ka[d + 3];
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {
+                if (r < nr) {
+                    const float4 qq = *reinterpret_cast<const float4*>(sq + (qg + 4 * r) * kHeadDim + d);
+                    ae[r] = fmaf(qq.x, k0, ae[r]);
+                    ao[r] = fmaf(qq.y, k1, ao[r]);
+                    ae[r] = fmaf(qq.z, k2, ae[r]);
+                    ao[r] = fmaf(qq.w, k3, ao[r]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+        if (r < nr) {
+            const int q = qg + 4 * r, t = q / G;
+            const bool live = p < n_pos && p0 + p < before + t + 1;
+            sp[q * kPage + p] = live ? (ae[r] + ao[r]) * scale : -INFINITY;
+        }
+    }
+}
+
+// P.V of k_attn_chunk: thread (dim d, row group qg) accumulates rows qg,
+// qg + 2, ... (at most NR): each V element loaded once feeds every row, four
+// probabilities per 16-byte broadcast read; each row's chain runs over the
+// positions in order.  po: this (kv head, chunk)'s partial rows [q][128].
+template <int NR>
+__device__ __forceinline__ void attn_pv(const float* sk, const float* sp, int NQ, int n_pos, float* po) {
+    const int d = threadIdx.x & (kHeadDim - 1), qg = threadIdx.x >> 7;
+    const int nr = (NQ - qg + 1) >> 1;
+    float acc[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0.f;
+    const float* vd = sk + d;
+    int p = 0;
+    for (; p + 4 <= n_pos; p += 4) {
+        const float v0 = vd[p * (kHeadDim + 1)], v1 = vd[(p + 1) * (kHeadDim + 1)];
+        const float v2 = vd[(p + 2) * (kHeadDim + 1)], v3 = vd[(p + 3) * (kHeadDim + 1)];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            if (r < nr) {
+                const float4 pp = *reinterpret_cast<const float4*>(sp + (qg + 2 * r) * kPage + p);
+                acc[r] = fmaf(pp.x, v0, acc[r]);
+                acc[r] = fmaf(pp.y, v1, acc[r]);
+                acc[r] = fmaf(pp.z, v2, acc[r]);
+                acc[r] = fmaf(pp.w, v3, acc[r]);
+            }
+        }
+    }
+    for (; p < n_pos; ++p) {
+        const float v0 = vd[p * (kHeadDim + 1)];
+#pragma unroll
+        for (int r = 0; r < NR; ++r)
+            if (r < nr) acc[r] = fmaf(sp[(qg + 2 * r) * kPage + p], v0, acc[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+        if (r < nr) po[(size_t)(qg + 2 * r) * kHeadDim + d] = acc[r];
+}
+
 // Split-KV causal GQA attention, one CTA per (64-position chunk, kv head):
 // scores q.k * 1/sqrt(128) (q.k = even-dim fmaf chain + odd-dim fmaf chain), query row t sees positions < before + t + 1
 // (src/qwen3_decoder.cpp:142-148), chunk-local max / exp-sum / P.V partials.
@@ -397,38 +497,44 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
     float* sk = sq + kTMax * 4 * kHeadDim;       // [64][129]  (group <= 4)
     float* sp = sk + kPage * (kHeadDim + 1);     // [NQ][64]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < NQ * kHeadDim; i += kThreads) {
-        const int q = i / kHeadDim, d = i % kHeadDim;
-        const int t = q / G, j = q % G;
-        sq[i] = qkv[(size_t)t * ld + (size_t)(h * G + j) * kHeadDim + d];
-    }
     const int p0 = c * kPage;
     const int n_pos = min(kPage, kv_len - p0);
-    const long long koff = kv_offset(kv, n_kv, layer, 0, h, p0);
-    const long long voff = kv_offset(kv, n_kv, layer, 1, h, p0);
-    for (int i = tid; i < n_pos * kHeadDim; i += kThreads) {
-        const int p = i / kHeadDim, d = i % kHeadDim;
-        sk[p * (kHeadDim + 1) + d] = kv_load(kv, koff + i);
+    // The chunk's K and V rows are contiguous in their page: all of both are
+    // requested up front as 16-byte loads (V waits in registers until the
+    // scores are done), so the block pays one memory round trip, not one per
+    // loop trip.
+    const bool f16 = kv.type == KV_F16;
+    const int elem = f16 ? 2 : 4;
+    const int n16 = n_pos * kHeadDim * elem / 16;
+    const uint4* kg = reinterpret_cast<const uint4*>(static_cast<const char*>(kv.base) +
+                                                     kv_offset(kv, n_kv, layer, 0, h, p0) * elem);
+    const uint4* vg = reinterpret_cast<const uint4*>(static_cast<const char*>(kv.base) +
+                                                     kv_offset(kv, n_kv, layer, 1, h, p0) * elem);
+    uint4 kr[8], vr[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int i = tid + u * kThreads;
+        if (i < n16) {
+            kr[u] = kg[i];
+            vr[u] = vg[i];
+        }
     }
+    for (int i = tid; i < NQ * kHeadDim / 4; i += kThreads) {
+        const int q = i / (kHeadDim / 4), d = (i % (kHeadDim / 4)) * 4;
+        const int t = q / G, j = q % G;
+        *reinterpret_cast<float4*>(sq + q * kHeadDim + d) =
+            *reinterpret_cast<const float4*>(qkv + (size_t)t * ld + (size_t)(h * G + j) * kHeadDim + d);
+    }
+    kv_rows_to_smem(kr, n16, f16, sk);
     __syncthreads();
     const float scale = 1.0f / sqrtf((float)kHeadDim);
-    for (int i = tid; i < NQ * kPage; i += kThreads) {
-        const int q = i / kPage, p = i % kPage;
-        const int t = q / G;
-        const int pos = p0 + p;
-        float s = -INFINITY;
-        if (p < n_pos && pos < before + t + 1) {
-            const float* qa = sq + q * kHeadDim;
-            const float* ka = sk + p * (kHeadDim + 1);
-            float ae = 0.f, ao = 0.f;  // even and odd dims, then their sum
-#pragma unroll 8
-            for (int d = 0; d < kHeadDim; d += 2) {
-                ae = fmaf(qa[d], ka[d], ae);
-                ao = fmaf(qa[d + 1], ka[d + 1], ao);
-            }
-            s = (ae + ao) * scale;
-        }
-        sp[q * kPage + p] = s;
+    {
+        const int ns = (NQ + 3) >> 2;  // rows per score thread (at most)
+        if (ns <= 1) attn_scores<1>(sq, sk, sp, NQ, G, n_pos, p0, before, scale);
+        else if (ns <= 2) attn_scores<2>(sq, sk, sp, NQ, G, n_pos, p0, before, scale);
+        else if (ns <= 4) attn_scores<4>(sq, sk, sp, NQ, G, n_pos, p0, before, scale);
+        else if (ns <= 8) attn_scores<8>(sq, sk, sp, NQ, G, n_pos, p0, before, scale);
+        else attn_scores<16>(sq, sk, sp, NQ, G, n_pos, p0, before, scale);
     }
     __syncthreads();
     for (int q = warp; q < NQ; q += kWarps) {
@@ -441,19 +547,16 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
         sp[q * kPage + lane + 32] = e1;
         if (lane == 0) part_ml[((size_t)h * max_chunks + c) * qstride + q] = make_float2(m, l);
     }
+    kv_rows_to_smem(vr, n16, f16, sk);  // the K rows are no longer read: the scores are in sp
     __syncthreads();
-    for (int i = tid; i < n_pos * kHeadDim; i += kThreads) {
-        const int p = i / kHeadDim, d = i % kHeadDim;
-        sk[p * (kHeadDim + 1) + d] = kv_load(kv, voff + i);
-    }
-    __syncthreads();
-    for (int i = tid; i < NQ * kHeadDim; i += kThreads) {
-        const int q = i / kHeadDim, d = i % kHeadDim;
-        const float* pr = sp + q * kPage;
-        float acc = 0.f;
-        for (int p = 0; p < n_pos; ++p) acc = fmaf(pr[p], sk[p * (kHeadDim + 1) + d], acc);
-        part_o[(((size_t)h * max_chunks + c) * qstride + q) * kHeadDim + d] = acc;
-    }
+    float* po = part_o + ((size_t)h * max_chunks + c) * qstride * kHeadDim;
+    const int npv = (NQ + 1) >> 1;  // rows per P.V thread (at most)
+    if (npv <= 1) attn_pv<1>(sk, sp, NQ, n_pos, po);
+    else if (npv <= 2) attn_pv<2>(sk, sp, NQ, n_pos, po);
+    else if (npv <= 4) attn_pv<4>(sk, sp, NQ, n_pos, po);
+    else if (npv <= 8) attn_pv<8>(sk, sp, NQ, n_pos, po);
+    else if (npv <= 16) attn_pv<16>(sk, sp, NQ, n_pos, po);
+    else attn_pv<32>(sk, sp, NQ, n_pos, po);
 }
 
 // Prefill attention, register-blocked: one (64-position chunk c, kv head h,
@@ -738,6 +841,26 @@ __global__ void k_embed(StepState* st, const uint8_t* __restrict__ embd, int hid
 // dequant (d * q) of token ids[p] from the token_embd tiles, or, where
 // slot[p] >= 0 (the k-th audio placeholder, slots counted on the host), audio
 // row slot[p].  grid (seq), block 256.
+// F16 weights on the device, tiled for the GEMV's lane-per-output reads: the
+// [n][k] matrix (n a multiple of 32) as tiles of 32 rows x 32 columns, tile
+// (g, kb) at ((g * k/32) + kb) * 1024 halves, inside it column quarter u
+// (8 columns) at u * 256, row o at o * 8, column e at e.  A warp reading one
+// quarter of a tile for its 32 rows reads 512 contiguous bytes.
+__host__ __device__ __forceinline__ size_t f16_tiled_index(size_t row, int col, int k) {
+    return ((row >> 5) * (size_t)(k >> 5) + (size_t)(col >> 5)) * 1024 + (size_t)((col & 31) >> 3) * 256 +
+           (row & 31) * 8 + (col & 7);
+}
+
+// Row-major [n][k] fp16 (src) -> tiled (dst); one thread per 8 columns.
+__global__ void k_repack_f16(const uint4* __restrict__ src, int n, int k, __half* dst) {
+    const size_t chunks = (size_t)n * (k >> 3);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < chunks; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t row = i / (k >> 3);
+        const int col = (int)(i % (k >> 3)) * 8;
+        *reinterpret_cast<uint4*>(dst + f16_tiled_index(row, col, k)) = src[i];
+    }
+}
+
 __global__ void k_fuse_embeds_f16(const int32_t* __restrict__ ids, const int32_t* __restrict__ slot, int seq,
                                   const float* __restrict__ audio, const __half* __restrict__ embd, int hidden,
                                   float* out) {
@@ -745,7 +868,8 @@ __global__ void k_fuse_embeds_f16(const int32_t* __restrict__ ids, const int32_t
     if (p >= seq) return;
     const int a = slot[p];
     for (int i = threadIdx.x; i < hidden; i += blockDim.x)
-        out[(size_t)p * hidden + i] = a >= 0 ? audio[(size_t)a * hidden + i] : __half2float(embd[(size_t)ids[p] * hidden + i]);
+        out[(size_t)p * hidden + i] =
+            a >= 0 ? audio[(size_t)a * hidden + i] : __half2float(embd[f16_tiled_index((size_t)ids[p], i, hidden)]);
 }
 
 __global__ void k_fuse_embeds(const int32_t* __restrict__ ids, const int32_t* __restrict__ slot, int seq,
@@ -1032,6 +1156,10 @@ __global__ void k_kv_gather(KvCache kv, int n_kv, int layer, int which, int pos0
 
 // ============================================================ launchers
 
+void launch_repack_f16(const uint16_t* src, int n, int k, uint16_t* dst, cudaStream_t s) {
+    k_repack_f16<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const uint4*>(src), n, k, reinterpret_cast<__half*>(dst));
+}
+
 void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int rg_stride, int rg_offset,
                       cudaStream_t s) {
     const long long work = (long long)(n_rows / kTileRows) * (k / kTileK) * 32;
@@ -1145,56 +1273,98 @@ __global__ void k_embed_f16(StepState* st, const __half* __restrict__ embd, int 
                 if (i == 0) st->error = 1;
                 id = 0;
             }
-            v = __half2float(embd[(size_t)id * hidden + i]);
+            v = __half2float(embd[f16_tiled_index((size_t)id, i, hidden)]);
         }
         x[(size_t)row * hidden + i] = v;
     }
 }
 
-// y[t][o] = sum_k act[t][k] W[o][k] for 32 outputs o per block of 256 threads
-// (lane = output), rows t < T.  Warp w takes block w of every 256-element
-// slice: 4 x 16-byte loads of its output's 32 weights, then the block's fmaf
-// chain for all 16 rows (two rows per __ffma2_rn: each component its own
-// chain) from the activations staged in shared memory as f32 [K][16]
-// (broadcast reads).  Block sums meet in shared memory; each thread adds the
-// 8 blocks of a slice in order for its output and rows w, w + 8, and keeps the
-// slice total.  Epilogues: store, residual add, or the first max over the 32
-// outputs per row (plus the logits when asked).
+// y[t][o] = sum_k act[t][k] W[o][k], rows t < T.  One block of 256 threads
+// takes 32 outputs (lane = output) and SPB consecutive 256-element slices of
+// K; warp w takes the 32-element block w of each of those slices.  A lane
+// loads its output's 32 weights of every block it takes up front (64 B per
+// block, issued before the activations are staged so both latencies overlap),
+// then runs each block's fmaf chain from 0 for the rows (1, 2, 4, 8 or 16 of
+// them, the power of two at or above T; two rows per __ffma2_rn, each
+// component its own chain) over the activations staged in shared memory as
+// f32 [k][16] (broadcast reads).  The 8 block values of a
+// slice meet in shared memory and thread (row, output) adds them in block
+// order into the slice total.  With SPB equal to the slice count the block
+// adds its slice totals in order and finishes; otherwise (split K: more blocks
+// in flight for the narrow projections) each slice total goes to f16_part and
+// the last block of the 32 outputs to finish (a counter per group, the
+// fence-then-count pattern; no block waits for another) adds the totals of all
+// slices in order.  Epilogues: store, residual add, or the first max over the
+// 32 outputs per row (plus the logits when asked).
 enum EpiF16 { F16_STORE = 0, F16_RESID = 1, F16_ARGMAX = 2 };
+constexpr int kF16MaxSpb = 4;  // slices per block when K is not split
+constexpr int kF16Pad = 8;     // floats of padding after every 32 staged k (conflict-free staging)
+
+__device__ __forceinline__ int f16_xs_idx(int k) { return k * kTMax + (k >> 5) * kF16Pad; }
+
 template <int EPI>
-__global__ void __launch_bounds__(256) k_gemv_f16(const __half* __restrict__ W, int N, int K,
-                                                  const __half* __restrict__ act, const StepState* st, float* out,
-                                                  int ld, float2* lm_val) {
-    const int T = st->T;
-    if (T <= 0) return;
-    extern __shared__ __align__(16) float sm_f16[];
-    float* xs = sm_f16;                    // [K][16]
-    float* bs = xs + (size_t)K * kTMax;    // [8 blocks][16 rows][32 outputs]
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < kTMax * K; i += 256) {
-        const int t = i / K, k = i % K;
-        xs[k * kTMax + t] = __half2float(act[i]);
+__device__ __forceinline__ void f16_epilogue(float v, int t, int T, int o, int N, int g, float* out, int ld,
+                                             float2* lm_val) {
+    if (EPI == F16_ARGMAX) {
+        float bv = (t < T && o < N) ? v : -INFINITY;
+        int bi = (t < T && o < N) ? o : 0x7fffffff;
+        if (out && t < T && o < N) out[(size_t)t * ld + o] = v;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if ((threadIdx.x & 31) == 0) lm_val[(size_t)g * kTMax + t] = make_float2(bv, __int_as_float(bi));
+    } else if (t < T && o < N) {
+        if (EPI == F16_STORE) out[(size_t)t * ld + o] = v;
+        else out[(size_t)t * ld + o] = out[(size_t)t * ld + o] + v;
     }
-    __syncthreads();
-    const int o = blockIdx.x * kF16Outs + lane;
-    float tot[2] = {0.f, 0.f};  // rows warp, warp + 8
-    for (int s0 = 0; s0 < K; s0 += 256) {
-        const int b0 = s0 + 32 * warp;  // this warp's block of the slice
-        float2 acc[kTMax / 2];
+}
+
+// Weights of block `warp` of each of the block's SPB slices for output o (W
+// tiled; N is a multiple of 32, so every group's tiles exist).
+template <int SPB>
+__device__ __forceinline__ void f16_load_weights(const __half* __restrict__ W, int K, int g, int s0,
+                                                 uint4 (&wr)[SPB][4]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-        for (int p = 0; p < kTMax / 2; ++p) acc[p] = make_float2(0.f, 0.f);
-        if (o < N) {
-            const uint4* wp = reinterpret_cast<const uint4*>(W + (size_t)o * K + b0);
-            uint4 wr[4];
+    for (int si = 0; si < SPB; ++si) {
+        // Tile (g, kb) of the tiled layout (f16_tiled_index): quarter u of
+        // lane o's row is 16 bytes at u * 512 + o * 16, contiguous across lanes.
+        const int kb = (s0 + si) * 8 + warp;
+        const uint4* wp = reinterpret_cast<const uint4*>(W + ((size_t)g * (K >> 5) + kb) * 1024) + lane;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) wr[u] = __ldg(wp + u);
+        for (int u = 0; u < 4; ++u) wr[si][u] = __ldg(wp + u * 32);
+    }
+}
+
+template <int RB, int SPB, int EPI>
+__device__ __forceinline__ void gemv_f16_body(int N, int K, int g, int s0, int nsb, int T, const uint4 (&wr)[SPB][4],
+                                              const float* xs, float* bv, float* out, int ld, float2* lm_val,
+                                              float* part, int* cnt) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int o = g * kF16Outs + lane;
+    float tot[2] = {0.f, 0.f};  // rows warp, warp + 8 (this thread's share of the slice sums)
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const float wj = __half2float(reinterpret_cast<const __half*>(wr)[j]);
+    for (int si = 0; si < SPB; ++si) {
+        constexpr int NA = RB < 2 ? 1 : RB / 2;
+        float2 acc[NA];
+#pragma unroll
+        for (int p = 0; p < NA; ++p) acc[p] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const float wj = __half2float(reinterpret_cast<const __half*>(wr[si])[j]);
+            const float* xk = xs + f16_xs_idx(si * 256 + warp * 32 + j);
+            if (RB == 1) {
+                acc[0].x = fmaf(xk[0], wj, acc[0].x);
+            } else if (RB == 2) {
+                acc[0] = __ffma2_rn(*reinterpret_cast<const float2*>(xk), make_float2(wj, wj), acc[0]);
+            } else {
                 const float2 w2 = make_float2(wj, wj);
-                const float4* xr = reinterpret_cast<const float4*>(xs + (size_t)(b0 + j) * kTMax);
+                const float4* xr = reinterpret_cast<const float4*>(xk);
 #pragma unroll
-                for (int q = 0; q < kTMax / 4; ++q) {
+                for (int q = 0; q < RB / 4; ++q) {
                     const float4 xv = xr[q];
                     acc[2 * q] = __ffma2_rn(make_float2(xv.x, xv.y), w2, acc[2 * q]);
                     acc[2 * q + 1] = __ffma2_rn(make_float2(xv.z, xv.w), w2, acc[2 * q + 1]);
@@ -1202,56 +1372,134 @@ __global__ void __launch_bounds__(256) k_gemv_f16(const __half* __restrict__ W, 
             }
         }
 #pragma unroll
-        for (int p = 0; p < kTMax / 2; ++p) {
-            bs[(warp * kTMax + 2 * p) * 32 + lane] = acc[p].x;
-            bs[(warp * kTMax + 2 * p + 1) * 32 + lane] = acc[p].y;
+        for (int p = 0; p < NA; ++p) {
+            bv[(warp * kTMax + 2 * p) * 32 + lane] = acc[p].x;
+            if (RB > 1) bv[(warp * kTMax + 2 * p + 1) * 32 + lane] = acc[p].y;
         }
         __syncthreads();
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int t = warp + 8 * h;
-            float a = 0.f;
+            if (t < RB) {
+                float a = 0.f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) a = a + bs[(i * kTMax + t) * 32 + lane];
-            tot[h] = tot[h] + a;
+                for (int i = 0; i < 8; ++i) a = a + bv[(i * kTMax + t) * 32 + lane];
+                if (nsb == 1) tot[h] = tot[h] + a;
+                else if (o < N) part[((size_t)(s0 + si) * kTMax + t) * N + o] = a;
+            }
         }
+        if (si + 1 < SPB) __syncthreads();
+    }
+    if (nsb > 1) {
+        __shared__ int s_last;
+        __threadfence();
         __syncthreads();
+        if (tid == 0) s_last = atomicAdd(&cnt[g], 1) == nsb - 1;
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+        const int ns = K >> 8;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int t = warp + 8 * h;
+            if (t < RB && o < N) {
+                float a = 0.f;
+                for (int s = 0; s < ns; ++s) a = a + __ldcg(&part[((size_t)s * kTMax + t) * N + o]);
+                tot[h] = a;
+            }
+        }
+        if (tid == 0) cnt[g] = 0;  // ready for the next launch
     }
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-        const int t = warp + 8 * h;
-        if (EPI == F16_ARGMAX) {
-            float bv = (t < T && o < N) ? tot[h] : -INFINITY;
-            int bi = (t < T && o < N) ? o : 0x7fffffff;
-            if (out && t < T && o < N) out[(size_t)t * ld + o] = tot[h];
+    for (int h = 0; h < 2; ++h) f16_epilogue<EPI>(tot[h], warp + 8 * h, T, o, N, g, out, ld, lm_val);
+}
+
+// grid: (N / 32) x (K / 256 / SPB) blocks, flattened; SPB (1 or kF16MaxSpb)
+// divides the slice count.  SPB = 1 holds 16 weight registers (3 blocks per
+// SM), SPB = 4 holds 64 (2 blocks per SM).
+template <int EPI, int SPB>
+__global__ void __launch_bounds__(256, SPB == 1 ? 3 : 2)
+    k_gemv_f16(const __half* __restrict__ W, int N, int K, const __half* __restrict__ act, const StepState* st,
+               float* out, int ld, float2* lm_val, float* part, int* cnt) {
+    const int T = st->T;
+    if (T <= 0) return;
+    extern __shared__ __align__(16) float sm_f16[];
+    const int nsb = (K >> 8) / SPB;
+    const int g = blockIdx.x / nsb, s0 = (blockIdx.x % nsb) * SPB;
+    constexpr int kw = SPB * 256;
+    uint4 wr[SPB][4];
+    f16_load_weights<SPB>(W, K, g, s0, wr);
+    float* xs = sm_f16;                                  // [kw][16] + padding
+    float* bv = xs + kw * kTMax + (kw >> 5) * kF16Pad;  // [8 blocks][16 rows][32 outputs]
+    const int RS = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : T <= 8 ? 8 : kTMax;  // rows staged and computed
+    // Stage rows < RS of act[:, s0*256 .. +kw) as f32: 8 halves per thread,
+    // consecutive groups of RS threads in consecutive 32-k blocks.
+    constexpr int nkb = kw >> 5;
+    for (int i = threadIdx.x; i < RS * (kw >> 3); i += blockDim.x) {
+        const int t = i % RS, q8 = i / RS;
+        const int k0 = (q8 % nkb) * 32 + (q8 / nkb) * 8;
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(act + (size_t)t * K + (size_t)s0 * 256 + k0));
+        const __half* hv = reinterpret_cast<const __half*>(&v);
+        float* dst = xs + f16_xs_idx(k0) + t;
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-            }
-            if (lane == 0) lm_val[(size_t)blockIdx.x * kTMax + t] = make_float2(bv, __int_as_float(bi));
-        } else if (t < T && o < N) {
-            if (EPI == F16_STORE) out[(size_t)t * ld + o] = tot[h];
-            else out[(size_t)t * ld + o] = out[(size_t)t * ld + o] + tot[h];
-        }
+        for (int e = 0; e < 8; ++e) dst[e * kTMax] = __half2float(hv[e]);
+    }
+    __syncthreads();
+    switch (RS) {
+        case 1: gemv_f16_body<1, SPB, EPI>(N, K, g, s0, nsb, T, wr, xs, bv, out, ld, lm_val, part, cnt); break;
+        case 2: gemv_f16_body<2, SPB, EPI>(N, K, g, s0, nsb, T, wr, xs, bv, out, ld, lm_val, part, cnt); break;
+        case 4: gemv_f16_body<4, SPB, EPI>(N, K, g, s0, nsb, T, wr, xs, bv, out, ld, lm_val, part, cnt); break;
+        case 8: gemv_f16_body<8, SPB, EPI>(N, K, g, s0, nsb, T, wr, xs, bv, out, ld, lm_val, part, cnt); break;
+        default: gemv_f16_body<kTMax, SPB, EPI>(N, K, g, s0, nsb, T, wr, xs, bv, out, ld, lm_val, part, cnt);
     }
 }
 
-static size_t gemv_f16_smem(int K) { return ((size_t)K * kTMax + 8 * kTMax * 32) * sizeof(float); }
-constexpr int kF16GemvSmemMax = 227 * 1024;  // K <= kF16MaxK: the loader checks F16 models against it
+static size_t gemv_f16_smem(int spb) {
+    const int kw = spb * 256;
+    return ((size_t)kw * kTMax + (kw >> 5) * kF16Pad + 8 * kTMax * 32) * sizeof(float);
+}
+
+// Slices per block: four whenever they divide K (each block then has 64 KB
+// of weights in flight and K splits at most K / 1024 ways), else one.
+static int f16_spb(int N, int K) {
+    (void)N;
+    return (K >> 8) % kF16MaxSpb == 0 ? kF16MaxSpb : 1;
+}
+
+size_t f16_part_floats(const ModelDims& d) {
+    const int H = d.hidden, F = d.ffn, qd = d.n_heads * kHeadDim, kd = d.n_kv * kHeadDim;
+    const int shapes[5][2] = {{qd + 2 * kd, H}, {H, qd}, {2 * F, H}, {H, F}, {d.vocab, H}};
+    size_t m = 0;
+    for (const auto& sh : shapes)
+        if (f16_spb(sh[0], sh[1]) < (sh[1] >> 8)) m = std::max(m, (size_t)(sh[1] >> 8) * kTMax * (size_t)sh[0]);
+    return std::max<size_t>(m, 1);
+}
+
+int f16_groups_max(const ModelDims& d) {
+    const int n = std::max(std::max(d.n_heads * kHeadDim + 2 * d.n_kv * kHeadDim, d.hidden), std::max(2 * d.ffn, d.vocab));
+    return (n + kF16Outs - 1) / kF16Outs;
+}
 
 static void configure_f16_kernels() {
-    cudaFuncSetAttribute(k_gemv_f16<F16_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
-    cudaFuncSetAttribute(k_gemv_f16<F16_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
-    cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, kF16GemvSmemMax);
+    const int smem = (int)gemv_f16_smem(kF16MaxSpb);
+    cudaFuncSetAttribute(k_gemv_f16<F16_STORE, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_RESID, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 template <int EPI>
-static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const StepState* st, float* out, int ld,
+static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const StepBuffers& b, float* out, int ld,
                      float2* lm_val, cudaStream_t s) {
-    k_gemv_f16<EPI><<<(N + kF16Outs - 1) / kF16Outs, 256, gemv_f16_smem(K), s>>>(
-        reinterpret_cast<const __half*>(W), N, K, reinterpret_cast<const __half*>(act), st, out, ld, lm_val);
+    const int spb = f16_spb(N, K);
+    const int blocks = (N + kF16Outs - 1) / kF16Outs * ((K >> 8) / spb);
+    const __half* w = reinterpret_cast<const __half*>(W);
+    const __half* a = reinterpret_cast<const __half*>(act);
+    if (spb == kF16MaxSpb)
+        k_gemv_f16<EPI, kF16MaxSpb><<<blocks, 256, gemv_f16_smem(spb), s>>>(w, N, K, a, b.state, out, ld, lm_val,
+                                                                          b.f16_part, b.f16_cnt);
+    else
+        k_gemv_f16<EPI, 1><<<blocks, 256, gemv_f16_smem(1), s>>>(w, N, K, a, b.state, out, ld, lm_val, b.f16_part,
+                                                                 b.f16_cnt);
 }
 
 // forward_layers for F16 weights: the same sequence with fp16 activations.
@@ -1264,7 +1512,7 @@ static void forward_layers_f16(const DeviceModel& m, const KvCache& kv, const St
     for (int l = 0; l < d.n_layers; ++l) {
         const LayerWeights& w = m.layers[l];
         k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.attn_norm, d.eps, act, nullptr);
-        gemv_f16<F16_STORE>(w.h_qkv, qd + 2 * kd, H, b.act_h, b.state, b.qkv, qd + 2 * kd, nullptr, s);
+        gemv_f16<F16_STORE>(w.h_qkv, qd + 2 * kd, H, b.act_h, b, b.qkv, qd + 2 * kd, nullptr, s);
         k_qk_norm_rope_store<<<dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, w.q_norm,
                                                                              w.k_norm, d.eps, m.theta_scale, kv, l, -1, 0);
         k_attn_chunk<<<dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, kv, l,
@@ -1273,17 +1521,17 @@ static void forward_layers_f16(const DeviceModel& m, const KvCache& kv, const St
         k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
                                                               b.max_chunks, b.attn_out, -1, 0, kTMax * 4);
         k_rows_f16<<<64, 256, 0, s>>>(b.state, b.attn_out, qd, act);
-        gemv_f16<F16_RESID>(w.h_o, H, qd, b.act_h, b.state, b.x, H, nullptr, s);
+        gemv_f16<F16_RESID>(w.h_o, H, qd, b.act_h, b, b.x, H, nullptr, s);
         k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.ffn_norm, d.eps, act, nullptr);
-        gemv_f16<F16_STORE>(w.h_gu, 2 * F, H, b.act_h, b.state, b.gu2, 2 * F, nullptr, s);
+        gemv_f16<F16_STORE>(w.h_gu, 2 * F, H, b.act_h, b, b.gu2, 2 * F, nullptr, s);
         k_swiglu_f16<<<96, 256, 0, s>>>(b.state, b.gu2, F, act);
-        gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h, b.state, b.x, H, nullptr, s);
+        gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h, b, b.x, H, nullptr, s);
     }
     k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, act, b.hid);
 }
 
 static void lm_head_f16(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {
-    gemv_f16<F16_ARGMAX>(m.h_embd, m.dims.vocab, m.dims.hidden, b.act_h, b.state, want_logits ? b.logits : nullptr,
+    gemv_f16<F16_ARGMAX>(m.h_embd, m.dims.vocab, m.dims.hidden, b.act_h, b, want_logits ? b.logits : nullptr,
                          m.dims.vocab, b.lm_val, s);
 }
 

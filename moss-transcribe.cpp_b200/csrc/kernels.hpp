@@ -23,6 +23,8 @@ struct StepBuffers {
     float* logits;          // [kTMax][vocab] (penalty path and tests), may be null
     uint16_t* act_h;        // F16 models: fp16 activation rows [kTMax][max(hidden, n_heads*128, ffn)]
     float* gu2;             // F16 models: gate | up rows [kTMax][2 ffn]
+    float* f16_part;        // F16 models: per-slice dot totals of split GEMVs (f16_part_floats)
+    int* f16_cnt;           // F16 models: finished slice blocks per 32-output group (zero between launches)
     int max_chunks;
     int lm_blocks;          // LM-head partial blocks per row (q8_0: lm_head_blocks; F16: vocab / 32)
 };
@@ -82,12 +84,18 @@ struct DeviceModel {
 
 // LM-head partial blocks per row of an F16 model (32 vocab rows per block).
 constexpr int kF16Outs = 32;
-// Largest projection K of an F16 model (its activations staged as f32 [K][16]
-// in one block's shared memory next to 16 KB of block sums, within 227 KB).
-constexpr int kF16MaxK = (227 * 1024 - 8 * 16 * 32 * 4) / (16 * 4);
+// Largest projection K of an F16 model.
+constexpr int kF16MaxK = 16384;
+// Scratch of the F16 GEMVs for a model's shapes: floats of StepBuffers::f16_part
+// and ints of StepBuffers::f16_cnt.
+size_t f16_part_floats(const ModelDims& d);
+int f16_groups_max(const ModelDims& d);
 
 // q8_0 rows -> tiles (src: raw ggml blocks, n_rows x k).  Destination row group
 // for source row group r is r * rg_stride + rg_offset.
+// Row-major fp16 [n][k] (n a multiple of 32, k of 32) -> the tiled layout of
+// the F16 GEMVs and embedding lookups.
+void launch_repack_f16(const uint16_t* src, int n, int k, uint16_t* dst, cudaStream_t s);
 void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int rg_stride, int rg_offset,
                       cudaStream_t s);
 

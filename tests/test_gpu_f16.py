@@ -100,3 +100,32 @@ def test_f16_group_step_is_rejected(gpu_f16):
     d = capi.Decoder(gpu_f16, 128, capi.KV_F32, max_new=16)
     with pytest.raises(RuntimeError):
         capi.spec_run_group([d])
+
+
+def test_f16_full_model_prefill_step_and_lm_head_bit_exact():
+    """The Qwen3-0.6B shape with F16 weights (the configs[2] decoder).  Its
+    K of 1024, 2048 and 3072 run the GEMV blocks of four 256-element slices
+    (whole for K = 1024, split two and three ways for the O and down
+    projections); the tiny model's K of 256 and 512 run one-slice blocks.  So
+    this covers them: hidden rows of a prefill and of the verify steps, the
+    last row's logits, ids and counters."""
+    import os
+    from mtb import fixture
+    path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0, dtype="f16")
+    oracle.set_threads(os.cpu_count() or 8)
+    om = oracle.OracleModel(path)
+    gm = capi.Model(path, 0)
+    rng = np.random.default_rng(11)
+    prompt = np.concatenate([rng.standard_normal((20, om.shape.hidden)).astype(np.float32),
+                             om.embed(fixture.lcg_ids(12, om.shape.vocab, seed=4))])
+    od = oracle.OracleDecoder(om, 256)
+    gd = capi.Decoder(gm, 256, capi.KV_F32, max_new=32)
+    oh = od.run(prompt)
+    gh = gd.run(prompt)
+    np.testing.assert_array_equal(gh, oh)
+    np.testing.assert_array_equal(gd.logits_from_hidden(gh[-1]), od.logits(oh[-1]))
+    o_ids, o_c = od.spec_generate(prompt, 12, -1, k_max=8, n_min=3, n_max=3)
+    g_ids, g_c = gd.cpu_speculative_generate(prompt, 12, -1, k_max=8, n_min=3, n_max=3)
+    assert g_ids == o_ids
+    for key in ("target_calls", "proposed", "accepted", "target_input_tokens", "rewinds"):
+        assert g_c[key] == o_c[key], key
