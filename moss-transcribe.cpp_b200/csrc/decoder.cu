@@ -167,6 +167,29 @@ int upload_f16(mtb_model* m, const GgufFile& f, const std::string& name, int64_t
     return 0;
 }
 
+// ffn_gate and ffn_up [F][H] as one [2F][H] matrix, interleaved by 16 rows
+// (gate rows 16 b .. 16 b + 15, then the same up rows), so each 32-row group
+// of the F16 GEMV holds matching gate and up outputs (its SwiGLU epilogue).
+int upload_f16_gate_up(mtb_model* m, const GgufFile& f, const std::string& gate, const std::string& up, int64_t k,
+                       int64_t n, uint16_t* staging, uint16_t* dst) {
+    const GgufTensor* tg = f.tensor(gate);
+    const GgufTensor* tu = f.tensor(up);
+    if (!tg || !tu) return fail(m->error, "missing tensor " + (tg ? up : gate));
+    for (const GgufTensor* t : {tg, tu}) {
+        if (t->type != GGML_F16) return fail(m->error, gate + ": an F16 model needs F16 weights throughout");
+        if (t->ne.size() != 2 || t->ne[0] != k || t->ne[1] != n) return fail(m->error, gate + ": unexpected shape");
+    }
+    if (n % 16 || k % 32) return fail(m->error, gate + ": F16 matrices need multiples of 32 rows and columns");
+    const size_t block = size_t(16) * size_t(k) * 2;  // 16 rows in bytes
+    MTB_CK(m, cudaMemcpy2D(staging, 2 * block, tg->data, block, block, size_t(n / 16), cudaMemcpyHostToDevice));
+    MTB_CK(m, cudaMemcpy2D(reinterpret_cast<char*>(staging) + block, 2 * block, tu->data, block, block, size_t(n / 16),
+                           cudaMemcpyHostToDevice));
+    launch_repack_f16(staging, int(2 * n), int(k), dst, nullptr);
+    MTB_CK(m, cudaGetLastError());
+    MTB_CK(m, cudaDeviceSynchronize());
+    return 0;
+}
+
 int upload_f32(mtb_model* m, const GgufFile& f, const std::string& name, int64_t n, const float** out) {
     const GgufTensor* t = f.tensor(name);
     if (!t) return fail(m->error, "missing tensor " + name);
@@ -236,8 +259,7 @@ int load_model(mtb_model* m, const char* path) {
                 upload_f16(m, f, p + "attn_k.weight", H, kd, stg, qkv + size_t(qd) * size_t(H)) ||
                 upload_f16(m, f, p + "attn_v.weight", H, kd, stg, qkv + size_t(qd + kd) * size_t(H)) ||
                 upload_f16(m, f, p + "attn_o.weight", qd, H, stg, o) ||
-                upload_f16(m, f, p + "ffn_gate.weight", H, F, stg, gu) ||
-                upload_f16(m, f, p + "ffn_up.weight", H, F, stg, gu + size_t(F) * size_t(H)) ||
+                upload_f16_gate_up(m, f, p + "ffn_gate.weight", p + "ffn_up.weight", H, F, stg, gu) ||
                 upload_f16(m, f, p + "ffn_down.weight", F, H, stg, down))
                 return -1;
             w.h_qkv = qkv;
@@ -699,7 +721,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
             dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
             return bail();
-        if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.gu2, size_t(kTMax) * 2 * F * 4) ||
+        if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.act_h2, size_t(kTMax) * F * 2) ||
                     dalloc(A, E, &b.f16_part, f16_part_floats(dm) * 4) ||
                     dalloc(A, E, &b.f16_cnt, size_t(f16_groups_max(dm)) * 4)))
             return bail();

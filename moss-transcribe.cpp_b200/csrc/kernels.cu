@@ -754,13 +754,18 @@ __global__ void __launch_bounds__(256, 2) k_pf_attn(const float* __restrict__ qk
 // m_c = -inf skipped).  Chunks go in batches of 128: the batch's weights are
 // formed in parallel (one chunk per thread) into shared memory and its
 // partial loads are issued 16 at a time, so the chains wait on arithmetic,
-// not on one load after another.
+// not on one load after another.  act_h (F16 models' step path, else null):
+// the merged rows rounded to fp16 as well, rows >= T zero.
 __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n_heads, int n_kv,
                                                       const float* part_o, const float2* part_ml, int max_chunks,
-                                                      float* attn_out, int T_arg, int before_arg, int qstride) {
+                                                      float* attn_out, int T_arg, int before_arg, int qstride,
+                                                      __half* act_h) {
     const int T_all = T_arg < 0 ? st->T : T_arg;
     const int t_all = blockIdx.x, head = blockIdx.y;
-    if (t_all >= T_all) return;
+    if (t_all >= T_all) {
+        if (act_h) act_h[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = __float2half_rn(0.f);
+        return;
+    }
     const int rb = t_all / kTMax, t = t_all % kTMax;
     const int T = min(kTMax, T_all - kTMax * rb);
     const int G = n_heads / n_kv;
@@ -805,7 +810,9 @@ __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n
             }
         }
     }
-    attn_out[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = o / L;
+    const float r = o / L;
+    attn_out[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = r;
+    if (act_h) act_h[(size_t)t_all * n_heads * kHeadDim + (size_t)head * kHeadDim + threadIdx.x] = __float2half_rn(r);
 }
 
 // ------------------------------------------------------------ embed, draft, accept
@@ -1244,22 +1251,6 @@ __global__ void k_rows_f16(const StepState* st, const float* __restrict__ src, i
         act[i] = __float2half_rn(i / K < T ? src[i] : 0.f);
 }
 
-// silu(gate) * up of gate | up rows [16][2F] (src/qwen3.cpp:193-204, the
-// q8_0 epilogue's expression) rounded to fp16.
-__global__ void k_swiglu_f16(const StepState* st, const float* __restrict__ gu, int F, __half* act) {
-    const int T = st->T;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < kTMax * F; i += gridDim.x * blockDim.x) {
-        const int row = i / F, f = i % F;
-        float v = 0.f;
-        if (row < T) {
-            const float g = gu[(size_t)row * 2 * F + f], u = gu[(size_t)row * 2 * F + F + f];
-            const float sl = g / (1.0f + exact_expf(-g));
-            v = sl * u;
-        }
-        act[i] = __float2half_rn(v);
-    }
-}
-
 // Embedding rows of the step's tokens from fp16 token_embd (exact).
 __global__ void k_embed_f16(StepState* st, const __half* __restrict__ embd, int hidden, int vocab, float* x) {
     const int row = blockIdx.x;
@@ -1294,9 +1285,9 @@ __global__ void k_embed_f16(StepState* st, const __half* __restrict__ embd, int 
 // in flight for the narrow projections) each slice total goes to f16_part and
 // the last block of the 32 outputs to finish (a counter per group, the
 // fence-then-count pattern; no block waits for another) adds the totals of all
-// slices in order.  Epilogues: store, residual add, or the first max over the
-// 32 outputs per row (plus the logits when asked).
-enum EpiF16 { F16_STORE = 0, F16_RESID = 1, F16_ARGMAX = 2 };
+// slices in order.  Epilogues: store, residual add, SwiGLU into fp16 rows, or
+// the first max over the 32 outputs per row (plus the logits when asked).
+enum EpiF16 { F16_STORE = 0, F16_RESID = 1, F16_ARGMAX = 2, F16_SWIGLU = 3 };
 constexpr int kF16MaxSpb = 4;  // slices per block when K is not split
 constexpr int kF16Pad = 8;     // floats of padding after every 32 staged k (conflict-free staging)
 
@@ -1316,6 +1307,21 @@ __device__ __forceinline__ void f16_epilogue(float v, int t, int T, int o, int N
             if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
         if ((threadIdx.x & 31) == 0) lm_val[(size_t)g * kTMax + t] = make_float2(bv, __int_as_float(bi));
+    } else if (EPI == F16_SWIGLU) {
+        // Gate | up rows interleaved by 16 (upload): lanes 0-15 hold gate rows
+        // 16 g .., lanes 16-31 the matching up rows.  out is the fp16 [16][ld]
+        // activation of the down projection: silu(gate) * up (the q8_0
+        // epilogue's expression), rows >= T zero.
+        const float u = __shfl_down_sync(0xffffffffu, v, 16);
+        const int i = g * 16 + (threadIdx.x & 31);
+        if ((threadIdx.x & 31) < 16 && i < ld) {
+            float r = 0.f;
+            if (t < T) {
+                const float sl = v / (1.0f + exact_expf(-v));
+                r = sl * u;
+            }
+            reinterpret_cast<__half*>(out)[(size_t)t * ld + i] = __float2half_rn(r);
+        }
     } else if (t < T && o < N) {
         if (EPI == F16_STORE) out[(size_t)t * ld + o] = v;
         else out[(size_t)t * ld + o] = out[(size_t)t * ld + o] + v;
@@ -1485,6 +1491,7 @@ static void configure_f16_kernels() {
     cudaFuncSetAttribute(k_gemv_f16<F16_STORE, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(k_gemv_f16<F16_RESID, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_SWIGLU, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 template <int EPI>
@@ -1519,13 +1526,12 @@ static void forward_layers_f16(const DeviceModel& m, const KvCache& kv, const St
                                                                               b.part_o, b.part_ml, b.max_chunks, -1, 0,
                                                                               kTMax * 4);
         k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
-                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4);
-        k_rows_f16<<<64, 256, 0, s>>>(b.state, b.attn_out, qd, act);
+                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4, act);
         gemv_f16<F16_RESID>(w.h_o, H, qd, b.act_h, b, b.x, H, nullptr, s);
         k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.ffn_norm, d.eps, act, nullptr);
-        gemv_f16<F16_STORE>(w.h_gu, 2 * F, H, b.act_h, b, b.gu2, 2 * F, nullptr, s);
-        k_swiglu_f16<<<96, 256, 0, s>>>(b.state, b.gu2, F, act);
-        gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h, b, b.x, H, nullptr, s);
+        // SwiGLU in the gate | up GEMV's epilogue, into act_h2 (act_h is its input).
+        gemv_f16<F16_SWIGLU>(w.h_gu, 2 * F, H, b.act_h, b, reinterpret_cast<float*>(b.act_h2), F, nullptr, s);
+        gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h2, b, b.x, H, nullptr, s);
     }
     k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, act, b.hid);
 }
@@ -1559,7 +1565,7 @@ static void forward_layers(const DeviceModel& m, const KvCache& kv, const StepBu
                                                                               b.part_o, b.part_ml, b.max_chunks, -1, 0,
                                                                               kTMax * 4);
         k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
-                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4);
+                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4, nullptr);
         k_quant_rows<<<(qd / 32 * kTMax + kWarps - 1) / kWarps, kThreads, 0, s>>>(b.state, b.attn_out, qd, b.act_q, b.act_d);
         {
             GemvArgs a{w.o, H / kTileRows, qd / kTileK, b.act_q, b.act_d, b.x, H, b.state, nullptr, nullptr};
@@ -1604,7 +1610,7 @@ void launch_prefill_pass(const DeviceModel& m, const KvCache& kv, const PrefillB
             k_attn_chunk<<<dim3(max_chunks, d.n_kv, n_rb), kThreads, attn_smem, s>>>(
                 nullptr, p.qkv, d.n_heads, d.n_kv, kv, l, p.part_o, p.part_ml, max_chunks, P, before, qstride);
         k_attn_combine<<<dim3(P, d.n_heads), 128, 0, s>>>(nullptr, d.n_heads, d.n_kv, p.part_o, p.part_ml, max_chunks,
-                                                          p.attn, P, before, qstride);
+                                                          p.attn, P, before, qstride, nullptr);
         pf_quant(p.attn, P, qd, p.xq, p.xd, s);
         pf_gemm(w.pf_o, H, qd, p.xq, p.xd, P, p.x, H, PF_EPI_RESID, p.status, s);
         pf_norm_quant(p.x, P, H, w.ffn_norm, d.eps, p.xq, p.xd, nullptr, s);

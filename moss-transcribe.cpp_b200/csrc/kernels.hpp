@@ -22,7 +22,7 @@ struct StepBuffers {
     float2* lm_val;         // LM-head argmax partials (value, index-as-float bits)
     float* logits;          // [kTMax][vocab] (penalty path and tests), may be null
     uint16_t* act_h;        // F16 models: fp16 activation rows [kTMax][max(hidden, n_heads*128, ffn)]
-    float* gu2;             // F16 models: gate | up rows [kTMax][2 ffn]
+    uint16_t* act_h2;       // F16 models: SwiGLU rows [kTMax][ffn] fp16 (the down projection's input)
     float* f16_part;        // F16 models: per-slice dot totals of split GEMVs (f16_part_floats)
     int* f16_cnt;           // F16 models: finished slice blocks per 32-output group (zero between launches)
     int max_chunks;
