@@ -67,8 +67,15 @@ F16_PROMPT_TOKENS = 64
 F16_NEW = 1024
 
 
-def step_bytes(kv_len: int, T: int) -> int:
-    return WEIGHT_BYTES + NORM_BYTES + kv_len * KV_BYTES_PER_POS + T * KV_BYTES_PER_POS + T * EMBED_BYTES_PER_ROW
+# F16 weights: 28 layers x 15,728,640 weights + the 151936 x 1024
+# LM head, two bytes each; an embedding row is 1024 fp16 values.
+F16_WEIGHT_BYTES = 1_191_968_768
+F16_EMBED_BYTES_PER_ROW = 2_048
+
+
+def step_bytes(kv_len: int, T: int, f16: bool = False) -> int:
+    w, e = (F16_WEIGHT_BYTES, F16_EMBED_BYTES_PER_ROW) if f16 else (WEIGHT_BYTES, EMBED_BYTES_PER_ROW)
+    return w + NORM_BYTES + kv_len * KV_BYTES_PER_POS + T * KV_BYTES_PER_POS + T * e
 
 
 def measured_peaks():
@@ -190,20 +197,29 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the prefill / multi_stream / long_context side measurements (profiling runs)")
+    ap.add_argument("--f16", action="store_true",
+                    help="the same verify-step microbench on the F16-weight decoder of configs[2] "
+                         "(no side measurements, no CPU baseline)")
     args = ap.parse_args()
+    if args.f16:
+        args.no_extras = args.no_cpu_baseline = True
     rank, local, world, dist, torch = dist_setup(args)
     from mtb import fixture
-    path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0)
-    config = {"workload": "configs[1] verify-step microbench: KV 2048 fp16 synthetic, k+1=8, draft matches 3",
-              "model": "Qwen3-0.6B decoder (random-init N(0,0.02), q8_0)", "kv_len": KV_LEN, "k_plus_1": T_ROWS,
-              "tokens_per_step": 4, "l2": "inputs larger than L2 (633 MB of weights streamed per step)",
+    path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0, dtype="f16" if args.f16 else "q8_0")
+    wname = "F16" if args.f16 else "q8_0"
+    config = {"workload": "configs[1] verify-step microbench: KV 2048 fp16 synthetic, k+1=8, draft matches 3"
+                          + (" (configs[2]'s F16 decoder weights)" if args.f16 else ""),
+              "model": f"Qwen3-0.6B decoder (random-init N(0,0.02), {wname})", "kv_len": KV_LEN, "k_plus_1": T_ROWS,
+              "tokens_per_step": 4,
+              "l2": f"inputs larger than L2 ({'1192' if args.f16 else '633'} MB of weights streamed per step)",
               "parallelism": f"replicas x{world}"}
+    metric = METRIC.replace("q8_0", "F16") if args.f16 else METRIC
 
     if args.impl == "reference":
         if rank != 0:
             return
         cb = cpu_baseline(path, max(args.steps, 1))
-        line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": UNIT, "n_gpus": world,
+        line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32", "data": "synthetic", "config": config,
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
@@ -317,7 +333,7 @@ def main():
                    "timing": "host wall clock around run(), median of 5, host rows in, hidden rows out"}
 
     peak, peak_kind = measured_peaks()
-    bytes_step = step_bytes(KV_LEN, T_ROWS)
+    bytes_step = step_bytes(KV_LEN, T_ROWS, args.f16)
     achieved = bytes_step / (ms_step / 1e3) / 1e9
     kernel = ("k_verify_persistent (the whole verify step, one launch)" if model.persistent_grid > 0
               else "verify step (one CUDA graph of kernels)")
@@ -325,9 +341,10 @@ def main():
                 "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "algorithmic_bytes": bytes_step,
                 "traffic": TRAFFIC_BYTES if model.persistent_grid > 0 else None}
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+    line = {"metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "q8_0 x q8_0 -> f32 (fp16 KV)", "data": "synthetic", "config": config,
+            "vs_baseline": None, "dtype": ("f16 x f16 -> f32" if args.f16 else "q8_0 x q8_0 -> f32") + " (fp16 KV)",
+            "data": "synthetic", "config": config,
             "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk,
             "prefill": prefill, "multi_stream": ms_line, "long_context": lc_line, "f16_recording": f16_line}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
