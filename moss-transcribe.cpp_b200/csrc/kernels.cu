@@ -1271,8 +1271,8 @@ __global__ void k_embed_f16(StepState* st, const __half* __restrict__ embd, int 
 }
 
 // y[t][o] = sum_k act[t][k] W[o][k], rows t < T.  One block of 256 threads
-// takes 32 outputs (lane = output) and SPB consecutive 256-element slices of
-// K; warp w takes the 32-element block w of each of those slices.  A lane
+// takes 32 outputs (lane = output) and SPB (1, 2 or 4) consecutive
+// 256-element slices of K; warp w takes the 32-element block w of each of those slices.  A lane
 // loads its output's 32 weights of every block it takes up front (64 B per
 // block, issued before the activations are staged so both latencies overlap),
 // then runs each block's fmaf chain from 0 for the rows (1, 2, 4, 8 or 16 of
@@ -1420,11 +1420,11 @@ __device__ __forceinline__ void gemv_f16_body(int N, int K, int g, int s0, int n
     for (int h = 0; h < 2; ++h) f16_epilogue<EPI>(tot[h], warp + 8 * h, T, o, N, g, out, ld, lm_val);
 }
 
-// grid: (N / 32) x (K / 256 / SPB) blocks, flattened; SPB (1 or kF16MaxSpb)
-// divides the slice count.  SPB = 1 holds 16 weight registers (3 blocks per
-// SM), SPB = 4 holds 64 (2 blocks per SM).
+// grid: (N / 32) x (K / 256 / SPB) blocks, flattened; SPB (1, 2 or 4)
+// divides the slice count.  SPB = 1 and 2 hold 16 and 32 weight registers (3
+// blocks per SM), SPB = 4 holds 64 (2 blocks per SM).
 template <int EPI, int SPB>
-__global__ void __launch_bounds__(256, SPB == 1 ? 3 : 2)
+__global__ void __launch_bounds__(256, SPB == 4 ? 2 : 3)
     k_gemv_f16(const __half* __restrict__ W, int N, int K, const __half* __restrict__ act, const StepState* st,
                float* out, int ld, float2* lm_val, float* part, int* cnt) {
     const int T = st->T;
@@ -1465,11 +1465,14 @@ static size_t gemv_f16_smem(int spb) {
     return ((size_t)kw * kTMax + (kw >> 5) * kF16Pad + 8 * kTMax * 32) * sizeof(float);
 }
 
-// Slices per block: four whenever they divide K (each block then has 64 KB
-// of weights in flight and K splits at most K / 1024 ways), else one.
+// Slices per block: the most of 4, 2, 1 (dividing K / 256) that still gives
+// at least two blocks per SM; measured on the Qwen3-0.6B F16 step, more and
+// shorter blocks beat fewer, longer ones until the grid fills the GPU twice.
 static int f16_spb(int N, int K) {
-    (void)N;
-    return (K >> 8) % kF16MaxSpb == 0 ? kF16MaxSpb : 1;
+    const int ns = K >> 8, groups = (N + kF16Outs - 1) / kF16Outs;
+    for (int spb : {kF16MaxSpb, 2})
+        if (ns % spb == 0 && groups * (ns / spb) >= 2 * 148) return spb;
+    return 1;
 }
 
 size_t f16_part_floats(const ModelDims& d) {
@@ -1486,12 +1489,19 @@ int f16_groups_max(const ModelDims& d) {
     return (n + kF16Outs - 1) / kF16Outs;
 }
 
+template <int SPB>
+static void configure_f16_spb() {
+    const int smem = (int)gemv_f16_smem(SPB);
+    cudaFuncSetAttribute(k_gemv_f16<F16_STORE, SPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_RESID, SPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX, SPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(k_gemv_f16<F16_SWIGLU, SPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
 static void configure_f16_kernels() {
-    const int smem = (int)gemv_f16_smem(kF16MaxSpb);
-    cudaFuncSetAttribute(k_gemv_f16<F16_STORE, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_gemv_f16<F16_RESID, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_gemv_f16<F16_ARGMAX, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    cudaFuncSetAttribute(k_gemv_f16<F16_SWIGLU, kF16MaxSpb>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    configure_f16_spb<1>();
+    configure_f16_spb<2>();
+    configure_f16_spb<kF16MaxSpb>();
 }
 
 template <int EPI>
@@ -1504,6 +1514,9 @@ static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const
     if (spb == kF16MaxSpb)
         k_gemv_f16<EPI, kF16MaxSpb><<<blocks, 256, gemv_f16_smem(spb), s>>>(w, N, K, a, b.state, out, ld, lm_val,
                                                                           b.f16_part, b.f16_cnt);
+    else if (spb == 2)
+        k_gemv_f16<EPI, 2><<<blocks, 256, gemv_f16_smem(2), s>>>(w, N, K, a, b.state, out, ld, lm_val, b.f16_part,
+                                                                 b.f16_cnt);
     else
         k_gemv_f16<EPI, 1><<<blocks, 256, gemv_f16_smem(1), s>>>(w, N, K, a, b.state, out, ld, lm_val, b.f16_part,
                                                                  b.f16_cnt);
