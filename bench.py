@@ -132,7 +132,12 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_setup(args):
+def dist_setup(args=None):
+    """One process per GPU (torchrun's RANK / LOCAL_RANK / WORLD_SIZE): NCCL
+    over the node's GPUs, used only for the barriers around the timed region
+    and the max over ranks of the measured times (replicas: no data-path
+    collective).  MTB_DIST_BACKEND=gloo runs the same host logic on CPU ranks
+    (the multi-rank tests)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -140,10 +145,27 @@ def dist_setup(args):
         import datetime
         import torch
         import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        backend = os.environ.get("MTB_DIST_BACKEND", "nccl")
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
         return rank, local, world, dist, torch
     return rank, local, world, None, None
+
+
+def max_over_ranks(x: float, dist, torch, local: int) -> float:
+    """The largest x over all ranks (a multi-GPU time is its slowest rank's)."""
+    if not dist:
+        return x
+    dev = f"cuda:{local}" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_throughput(world: int, units_per_rank: float, seconds: float) -> float:
+    """Whole-job rate: every rank processed units_per_rank in at most `seconds`."""
+    return world * units_per_rank / seconds
 
 
 def greedy_draft(model_path: str, dec, kv_len: int, T: int, seed_tok: int, vocab: int):
@@ -188,7 +210,7 @@ def cpu_baseline(path: str, steps: int, sample_s: float = 20.0):
                       f"append + {keep + 1} lazy LM-head rows each, median {t * 1e3:.1f} ms"}
 
 
-def main():
+def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
@@ -200,10 +222,12 @@ def main():
     ap.add_argument("--f16", action="store_true",
                     help="the same verify-step microbench on the F16-weight decoder of configs[2] "
                          "(no side measurements, no CPU baseline)")
-    args = ap.parse_args()
+    args = ap.parse_args(argv)
     if args.f16:
         args.no_extras = args.no_cpu_baseline = True
     rank, local, world, dist, torch = dist_setup(args)
+    if args.impl == "reference" and rank != 0:
+        return  # the reference arm runs on rank 0's host cores only
     from mtb import fixture
     path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0, dtype="f16" if args.f16 else "q8_0")
     wname = "F16" if args.f16 else "q8_0"
@@ -216,8 +240,6 @@ def main():
     metric = METRIC.replace("q8_0", "F16") if args.f16 else METRIC
 
     if args.impl == "reference":
-        if rank != 0:
-            return
         cb = cpu_baseline(path, max(args.steps, 1))
         line = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
@@ -265,12 +287,9 @@ def main():
     clk = clocks.stop()
     ids, c = dec.read_ids()
     assert c["accepted"] == keep, c
-    if dist:
-        t = torch.tensor([ms], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(ms, dist, torch, local)
     ms_step = ms / args.steps
-    value = world * args.steps * tokens_per_step / (ms / 1e3)
+    value = job_throughput(world, args.steps * tokens_per_step, ms / 1e3)
 
     # ---- e2e: the public C ABI with host buffers ------------------------------
     h0 = dec.transfer_bytes()
@@ -289,11 +308,8 @@ def main():
         got, _ = dec.read_ids()
     e2e_s = time.perf_counter() - t0
     h1 = dec.transfer_bytes()
-    if dist:
-        t = torch.tensor([e2e_s], device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = {"value": world * n_e2e * tokens_per_step / e2e_s, "unit": UNIT,
+    e2e_s = max_over_ranks(e2e_s, dist, torch, local)
+    e2e = {"value": job_throughput(world, n_e2e * tokens_per_step, e2e_s), "unit": UNIT,
            "h2d_bytes_per_step": (h1[0] - h0[0]) // n_e2e + len(draft) * 4,
            "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
            "ms_per_step": e2e_s * 1e3 / n_e2e}
