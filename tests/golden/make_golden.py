@@ -1,7 +1,7 @@
 """Generate golden draft/replay vectors from the reference's own Python tool.
 
-Run in a container where the reference tree is mounted (its path is the first
-argument, default /root/reference).  It imports
+Run where the reference tree is checked out, with its path as the only
+argument: python tests/golden/make_golden.py <reference checkout>.  It imports
 cpu-lab/moss_ngram_audit.py (draft(), replay()) from the reference and records
 its outputs on seeded histories; the vectors are committed as
 tests/golden/ngram_draft.json and tests/golden/ngram_replay.json so the tests
@@ -14,7 +14,9 @@ import sys
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <reference checkout>")
+    ref = sys.argv[1]
     sys.path.insert(0, os.path.join(ref, "cpu-lab"))
     import moss_ngram_audit as audit  # noqa: E402  (the reference's replay tool)
 
