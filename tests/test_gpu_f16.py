@@ -45,8 +45,10 @@ def test_f16_run_hidden_logits_and_kv_match_oracle(gpu_f16, tiny_f16_oracle, kv)
             np.testing.assert_array_equal(gd.kv(layer, which, 0, prompt.shape[0]), od.kv(layer, which, 0, prompt.shape[0]))
 
 
-@pytest.mark.parametrize("T", [1, 3, 8, 16])
+@pytest.mark.parametrize("T", [1, 2, 3, 4, 8, 16])
 def test_f16_verify_rows_after_prefix(gpu_f16, tiny_f16_oracle, T):
+    """T rows after a 70-row prefix: every row count the F16 GEMV specialises
+    (1, 2, 4, 8, 16 rows) and one in between."""
     m = tiny_f16_oracle
     prompt = _prompt(m, n_rows=62)
     od = oracle.OracleDecoder(m, 256)
