@@ -13,22 +13,22 @@
  *   mtb_decoder_run                      Qwen3Decoder::run / prefill / decode_one
  *                                        (src/qwen3_decoder.cpp:91-172)
  *   mtb_decoder_logits                   Qwen3Decoder::logits_from_hidden (:174-206)
- *   mtb_decoder_rewind / _past_len       CpuSpeculativeDecoder::rewind (src/cpu_speculative.cpp:40-42),
+ *   mtb_decoder_rewind / _past_len       CpuSpeculativeDecoder::rewind (src/cpu_speculative.cpp:22-24),
  *                                        Qwen3Decoder::past_len (src/qwen3_decoder.hpp:55)
  *   mtb_greedy_generate                  greedy_generate serial path (src/generate.cpp:235-326)
- *   mtb_spec_generate                    cpu_speculative_generate (src/cpu_speculative.cpp:86-165)
+ *   mtb_spec_generate                    cpu_speculative_generate (src/cpu_speculative.cpp:68-147)
  *                                        with CpuSpeculativeHooks draft/committed
  *                                        (src/cpu_speculative.hpp:9-15)
- *   mtb_ngram_draft                      cpu_ngram_draft (src/cpu_speculative.cpp:45-56),
+ *   mtb_ngram_draft                      cpu_ngram_draft (src/cpu_speculative.cpp:27-38),
  *                                        evaluated by the device draft kernel
- *   mtb_greedy_choice                    cpu_greedy_choice (src/cpu_speculative.cpp:57-68),
+ *   mtb_greedy_choice                    cpu_greedy_choice (src/cpu_speculative.cpp:39-50),
  *                                        evaluated by the device choice kernel
  *   mtb_spec_step / _async, mtb_resume,  one verify step of the loop body
  *   mtb_spec_prime, mtb_spec_step_group_async, mtb_spec_run_group
  *                                        the same loop for several recordings at once
  *                                        (one launch per step; no reference counterpart:
  *                                        the reference decodes one recording at a time)
- *   mtb_snapshot_save / _restore         (src/cpu_speculative.cpp:118-155)
+ *   mtb_snapshot_save / _restore         (src/cpu_speculative.cpp:100-137)
  *
  * Conventions: every function returns 0 on success or a negative code and
  * sets a per-object error string; no C++ exception crosses the boundary.  One
@@ -52,8 +52,8 @@ enum { MTB_KV_F32 = 0, MTB_KV_F16 = 1 };
 enum { MTB_STOP_NONE = 0, MTB_STOP_EOS = 1, MTB_STOP_LIMIT = 2, MTB_STOP_ERROR = 3 };
 
 /* Draft policy.  The reference policy is k_max 4, n-gram sizes 16..2
- * (src/cpu_speculative.cpp:47,122); penalty is MTD_REPETITION_PENALTY clamped
- * to [1, 1.5] (:103-104). */
+ * (src/cpu_speculative.cpp:29,104); penalty is MTD_REPETITION_PENALTY clamped
+ * to [1, 1.5] (:85-86). */
 typedef struct mtb_spec_params {
     int32_t k_max;   /* proposals per step, 0..15 */
     int32_t n_min;   /* smallest n-gram size, >= 1 */
@@ -61,7 +61,7 @@ typedef struct mtb_spec_params {
     float penalty;   /* repetition penalty over the last 100 ids */
 } mtb_spec_params;
 
-/* Counters of the CPU_SPECULATIVE log line (src/cpu_speculative.cpp:158). */
+/* Counters of the CPU_SPECULATIVE log line (src/cpu_speculative.cpp:140). */
 typedef struct mtb_counters {
     int64_t target_calls, drafted_calls, proposed, accepted, target_input_tokens, rewinds;
     int32_t stop_reason; /* MTB_STOP_* */
@@ -138,7 +138,7 @@ int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counter
 int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft);
 /* Set the decode parameters and prefill the fused rows (the first id is
  * emitted), without decoding: the start of mtb_spec_generate
- * (src/cpu_speculative.cpp:86-117), for decoders stepped as a group. */
+ * (src/cpu_speculative.cpp:68-99), for decoders stepped as a group. */
 int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params);
 /* One verify step of n decoders (1..8) created from the same model, as ONE
  * persistent launch: each decoder drafts on the device; their rows (seed +
@@ -174,6 +174,17 @@ int mtb_step_kernel_launches(mtb_decoder* d);
  * GPU global timer; the profile counterpart of the
  * reference's MTD_PROFILE phase timers (src/cpu_profile.cpp:23-68). */
 int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out);
+/* Test read-back of the last persistent verify step's own outputs (decoder
+ * created with MTB_STEP_CAPTURE=1 in the environment; for a group step, the
+ * group's first decoder): the step's T rows (all streams, stream order) as
+ * final-RMSNorm'd hidden rows hidden_out [T][hidden], each row's LM-head
+ * maximum max_val[T] and its first index max_idx[T], and per stream
+ * (rows, first row) in stream_rows[8][2].  Any output may be NULL. */
+int mtb_step_capture(mtb_decoder* d, float* hidden_out, float* max_val, int32_t* max_idx, int32_t* stream_rows,
+                     int* T_out);
+/* Test hook: NaN into KV positions [pos0, pos0 + n_pos) of every layer (K and
+ * V), to show that a step never reads a cache slot it has not written. */
+int mtb_debug_poison_kv(mtb_decoder* d, int pos0, int n_pos);
 /* Host<->device bytes this decoder has copied so far (both cumulative). */
 int mtb_transfer_bytes(mtb_decoder* d, int64_t* h2d, int64_t* d2h);
 
@@ -201,7 +212,8 @@ int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t
  * device loading this library holds until exit; the first call on a device
  * looks its address up (call it once before any stream capture).  Calls share
  * that array: calls that overlap on the GPU race.  Nothing is allocated: no
- * cudaMalloc, cudaFree or allocating library routine is called. */
+ * cudaMalloc, cudaFree or allocating library routine is called.  The call runs
+ * on the model's device and leaves the caller's current device as it found it. */
 int mtb_lm_head_argmax_noalloc(const mtb_model* m, const float* hidden_rows, int T, int32_t* choices, void* stream);
 const char* mtb_noalloc_error(void);
 

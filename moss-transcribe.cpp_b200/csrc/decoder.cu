@@ -4,7 +4,7 @@
 // Model: GGUF -> q8_0 tiles in HBM (ModelLoader::load + Qwen3Decoder::load,
 // src/model_loader.cpp:21-114, src/qwen3_decoder.cpp:20-85).  Decoder: paged
 // KV cache, device StepState, step buffers and the CUDA graphs of the verify
-// step.  The generation loop (src/cpu_speculative.cpp:86-165) runs on the
+// step.  The generation loop (src/cpu_speculative.cpp:68-147) runs on the
 // device: drafting, the verify forward, the LM-head first max, acceptance and
 // rollback are kernels of one captured graph, and the host only watches the
 // stop flag.  With draft/commit hooks the loop runs one step per host round
@@ -522,7 +522,7 @@ int set_params(mtb_decoder* d, int max_new, int eos, const mtb_spec_params* p) {
     const int nmin = p ? p->n_min : 2, nmax = p ? p->n_max : 16;
     if (nmin < 1 || nmax < nmin) return fail(d->error, "need 1 <= n_min <= n_max");
     float pen = p ? p->penalty : 1.f;
-    pen = std::max(1.f, std::min(1.5f, pen));  // src/cpu_speculative.cpp:104
+    pen = std::max(1.f, std::min(1.5f, pen));  // src/cpu_speculative.cpp:86
     s.max_new = max_new;
     s.eos = eos;
     s.k_max = k;
@@ -701,6 +701,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
             return bail();
         if (std::getenv("MTB_PROFILE") && dalloc(A, E, &d->mb.timeline, (6 * kMaxBarriers + 2 + 256 * kMaxBarriers * 17) * 8)) return bail();
+        if (std::getenv("MTB_STEP_CAPTURE") && dalloc(A, E, &d->mb.capture, step_capture_floats(H) * 4)) return bail();
         d->mb.bar = reinterpret_cast<unsigned*>(zero_region);
         d->mb.abort_flag = reinterpret_cast<int*>(zero_region + 4);
         d->mb.head_done = reinterpret_cast<unsigned*>(zero_region + 16);
@@ -811,7 +812,7 @@ int mtb_decoder_rewind(mtb_decoder* d, int position) {
     d->fresh = false;
     cudaSetDevice(d->device);
     if (refresh(d)) return -1;
-    if (position < 0 || position > d->h_state->past) return fail(d->error, "invalid rewind");  // cpu_speculative.cpp:40-42
+    if (position < 0 || position > d->h_state->past) return fail(d->error, "invalid rewind");  // cpu_speculative.cpp:22-24
     d->h_state->past = position;
     if (push_state(d)) return -1;
     MTB_CK(d, cudaStreamSynchronize(d->stream));
@@ -915,7 +916,7 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
                 }
                 if (run_step(d, mode)) return -1;
                 if (refresh(d)) return -1;
-                // The commit point precedes the next seed (src/cpu_speculative.cpp:154 then :119).
+                // The commit point precedes the next seed (src/cpu_speculative.cpp:136 then :101).
                 if (commit) {
                     MTB_CK(d, cudaMemcpyAsync(d->h_ids, d->b.ids, size_t(s.n_ids) * 4, cudaMemcpyDeviceToHost, d->stream));
                     MTB_CK(d, cudaStreamSynchronize(d->stream));
@@ -1258,6 +1259,40 @@ int mtb_step_timeline(mtb_decoder* d, int64_t* out, int max_out, int* n_out) {
     MTB_CK(d, cudaMemcpyAsync(out, d->mb.timeline, size_t(n) * 8, cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
     *n_out = n;
+    return 0;
+}
+
+int mtb_step_capture(mtb_decoder* d, float* hidden_out, float* max_val, int32_t* max_idx, int32_t* stream_rows,
+                     int* T_out) {
+    if (!d || !T_out) return -1;
+    *T_out = 0;
+    if (!d->mb.capture) return fail(d->error, "set MTB_STEP_CAPTURE=1 before creating the decoder");
+    cudaSetDevice(d->device);
+    const int H = d->model->dm.dims.hidden;
+    std::vector<float> cap(step_capture_floats(H));
+    MTB_CK(d, cudaMemcpyAsync(cap.data(), d->mb.capture, cap.size() * 4, cudaMemcpyDeviceToHost, d->stream));
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    const float* mx = cap.data() + size_t(kTMax) * H;
+    const int32_t* rows = reinterpret_cast<const int32_t*>(mx + 2 * kTMax);
+    const int T = std::max(0, std::min(kTMax, rows[2 * kMaxStreams]));
+    if (hidden_out) std::memcpy(hidden_out, cap.data(), size_t(T) * H * 4);
+    for (int t = 0; t < T; ++t) {
+        if (max_val) max_val[t] = mx[2 * t];
+        if (max_idx) std::memcpy(&max_idx[t], &mx[2 * t + 1], 4);
+    }
+    if (stream_rows) std::memcpy(stream_rows, rows, 2 * kMaxStreams * 4);
+    *T_out = T;
+    return 0;
+}
+
+int mtb_debug_poison_kv(mtb_decoder* d, int pos0, int n_pos) {
+    if (!d) return -1;
+    if (pos0 < 0 || n_pos < 0 || pos0 + n_pos > d->max_seq) return fail(d->error, "poison range outside the cache");
+    if (n_pos == 0) return 0;
+    cudaSetDevice(d->device);
+    launch_poison_kv(d->model->dm, d->kv, pos0, n_pos, d->stream);
+    MTB_CK(d, cudaGetLastError());
+    MTB_CK(d, cudaStreamSynchronize(d->stream));
     return 0;
 }
 

@@ -904,7 +904,7 @@ __global__ void k_fuse_embeds(const int32_t* __restrict__ ids, const int32_t* __
     }
 }
 
-// n-gram draft over the generated ids (src/cpu_speculative.cpp:45-56): the
+// n-gram draft over the generated ids (src/cpu_speculative.cpp:27-38): the
 // longest suffix size in [n_min, n_max] with an earlier occurrence, latest
 // occurrence first.  For each end position e < n the common suffix length
 // c(e) of ids[0:e] and ids[0:n] (capped at n_max) is computed; the answer is
@@ -1004,7 +1004,7 @@ __device__ void reduce_choices(StepState* st, const float2* lm_val, int lm_block
     }
 }
 
-// Strict acceptance and logical rollback (src/cpu_speculative.cpp:142-153),
+// Strict acceptance and logical rollback (src/cpu_speculative.cpp:124-135),
 // then the next seed (the choice of the last kept row, :119).
 __global__ void k_accept(StepState* st, int32_t* ids, const float2* lm_val, int lm_blocks, int choices_ready) {
     if (st->T <= 0) return;
@@ -1023,7 +1023,7 @@ __global__ void k_prefill_seed(StepState* st, int32_t* ids, const float2* lm_val
     emit_id(st, ids, st->seed);
 }
 
-// Penalised first max (src/cpu_speculative.cpp:57-68) of one logits row by a
+// Penalised first max (src/cpu_speculative.cpp:39-50) of one logits row by a
 // CTA of 1024 threads: the recent set is the last 100 of hist[0:n_hist] +
 // extra[0:n_extra]; adjusted values x>0 ? x/p : x*p; the lowest index wins a
 // tie (NaN entries never win).  `bits` is a dynamic shared bitmap of vocab bits.
@@ -1149,6 +1149,21 @@ __global__ void k_fill_synthetic_kv(KvCache kv, int n_layers, int n_kv, int n_po
     }
 }
 
+// Test hook: NaN into positions [pos0, pos0 + n_pos) of every layer, K and V,
+// so that a step which read a cache slot it had not written would carry NaN.
+__global__ void k_poison_kv(KvCache kv, int n_layers, int n_kv, int pos0, int n_pos) {
+    const long long total = (long long)n_layers * 2 * n_kv * n_pos * kHeadDim;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int d = int(i % kHeadDim);
+        long long r = i / kHeadDim;
+        const int pos = pos0 + int(r % n_pos); r /= n_pos;
+        const int head = int(r % n_kv); r /= n_kv;
+        const int which = int(r % 2);
+        const int layer = int(r / 2);
+        kv_store(kv, kv_offset(kv, n_kv, layer, which, head, pos) + d, __int_as_float(0x7fc00000));
+    }
+}
+
 __global__ void k_kv_gather(KvCache kv, int n_kv, int layer, int which, int pos0, int n_pos, float* out) {
     const long long total = (long long)n_pos * n_kv * kHeadDim;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -1176,7 +1191,7 @@ void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int r
 
 int lm_head_blocks(int vocab) {
     const int n_rg = vocab / kTileRows;
-    return std::min(148 * 4, (n_rg + 7) / 8);
+    return std::min(kLmHeadMaxBlocks, (n_rg + 7) / 8);
 }
 
 static void configure_f16_kernels();
@@ -1744,6 +1759,10 @@ void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* 
 
 void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s) {
     k_fill_synthetic_kv<<<148 * 8, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, n_pos, seed);
+}
+
+void launch_poison_kv(const DeviceModel& m, const KvCache& kv, int pos0, int n_pos, cudaStream_t s) {
+    k_poison_kv<<<148 * 4, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, pos0, n_pos);
 }
 
 void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos, float* out,

@@ -39,6 +39,11 @@ struct MegaBuffers {
     unsigned* head_done; // [n_layers][kMaxStreams][n_kv] finished attention items per kv head
     size_t zero_bytes;
     unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
+    // Optional, MTB_STEP_CAPTURE=1 (test read-back of the persistent step's own
+    // outputs, layout: mtb_step_capture): [16][hidden] final-normed rows, [16]
+    // (LM-head maximum, its index as int bits), [kMaxStreams] (rows, first row)
+    // as int bits, then the step's row count.
+    float* capture = nullptr;
     // Bound on every grid-barrier wait, and a test hook: CTA 0 skips its
     // arrival at this barrier (-1: never), so the others' waits run out.
     unsigned long long wait_ns = 2000000000ull;
@@ -46,6 +51,9 @@ struct MegaBuffers {
 };
 
 constexpr int kMaxBarriers = 512;
+
+// Floats of MegaBuffers::capture for a model of this hidden size.
+inline size_t step_capture_floats(int hidden) { return size_t(kTMax) * hidden + 2 * kTMax + 2 * kMaxStreams + 1; }
 
 // Buffers of a prefill pass (up to max_rows prompt rows through all layers at
 // once, projections on tcgen05).
@@ -120,6 +128,7 @@ void launch_forward_rows(const DeviceModel& m, const KvCache& kv, const StepBuff
                          bool want_logits, cudaStream_t s);
 
 void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s);
+void launch_poison_kv(const DeviceModel& m, const KvCache& kv, int pos0, int n_pos, cudaStream_t s);
 void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos,
                       float* out, cudaStream_t s);
 // LM head with its first max (b.lm_val) of one final-normed hidden row in
@@ -128,6 +137,9 @@ void launch_lm_row(const DeviceModel& m, const StepBuffers& b, const float* hidd
 void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* hidden_row, cudaStream_t s);
 void launch_prefill_seed(const StepBuffers& b, cudaStream_t s);
 
+// Upper bound of lm_head_blocks(): four blocks per SM of a 148-SM B200 (the
+// grid is tuned for that part; other SM counts only change the tuning).
+constexpr int kLmHeadMaxBlocks = 148 * 4;
 int lm_head_blocks(int vocab);
 
 // Persistent verify step (megakernel.cu).

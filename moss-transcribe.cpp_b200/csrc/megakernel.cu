@@ -26,7 +26,7 @@
 //      for the down projection by the CTA that computed it
 //   F  down projection + residual
 // then the final RMSNorm, the LM head with a fused first max, and the
-// acceptance / rollback of src/cpu_speculative.cpp:142-153 (CTA 0).
+// acceptance / rollback of src/cpu_speculative.cpp:124-135 (CTA 0).
 //
 // Every operation evaluates the same arithmetic in the same order as the
 // multi-kernel path (kernels.cu) and the CPU restatement, so the results are
@@ -91,6 +91,7 @@ struct MegaArgs {
     unsigned long long wait_ns;  // bound on a grid-barrier wait
     int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
     unsigned long long* timeline;  // optional: CTA 0's [barrier][arrive, release] in ns
+    float* capture;                // optional: the step's final-normed rows and LM-head maxima (test read-back)
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -473,7 +474,8 @@ __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
 template <int NK, bool kUmma = false>
 __device__ __noinline__ void norm_quant_smem(const float* x, const float* __restrict__ wn, float eps, int T,
                                             uint8_t* act_q, float* act_d, double* s_wsum, float* s_scale,
-                                            unsigned long long* timeline = nullptr, int pid = 0) {
+                                            unsigned long long* timeline = nullptr, int pid = 0,
+                                            float* normed_out = nullptr) {
     constexpr int K = 256 * NK;
     constexpr int RG = 8;  // rows per pass (rows are independent; 8 x NK values per lane)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -526,6 +528,7 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
 #pragma unroll
             for (int k = 0; k < NK; ++k) {
                 v[r][k] = t0 + r < T ? __fmul_rn(__fmul_rn(v[r][k], sc), wv[k]) : 0.f;
+                if (normed_out && t0 + r < T) normed_out[(size_t)(t0 + r) * K + 256 * k + 32 * warp + lane] = v[r][k];
                 am[r * NK + k] = warp_absmax(v[r][k]);
             }
         }
@@ -1316,7 +1319,8 @@ __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     uint8_t* act_q = c.region;
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, nullptr, 0,
+                        blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
     float best_v[2] = {-INFINITY, -INFINITY};
@@ -1399,7 +1403,8 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t* act_q = c.region;                                          // [STEPS][1024]
     float* act_d = reinterpret_cast<float*>(c.region + STEPS * 1024);   // [16][NB]
-    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale);
+    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, nullptr, 0,
+                              blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
     uint64_t* half_full = c.lm_bars;
@@ -1576,7 +1581,19 @@ __device__ __noinline__ void phase_accept(const KCtx& c) {
         if (lane == 0) {
             const int si = c.row_stream[row];
             a.st_state[si]->choice[row - c.s_row0[si]] = bi == 0x7fffffff ? 0 : bi;
+            if (a.capture) {
+                float* cap = a.capture + (size_t)kTMax * a.d.hidden;
+                cap[2 * row] = bv;
+                cap[2 * row + 1] = __int_as_float(bi);
+            }
         }
+    }
+    if (a.capture && threadIdx.x < kMaxStreams) {
+        int* cap = reinterpret_cast<int*>(a.capture + (size_t)kTMax * a.d.hidden + 2 * kTMax);
+        const bool on = (int)threadIdx.x < a.n_streams;
+        cap[2 * threadIdx.x] = on ? c.s_T[threadIdx.x] : 0;
+        cap[2 * threadIdx.x + 1] = on ? c.s_row0[threadIdx.x] : 0;
+        if (threadIdx.x == 0) cap[2 * kMaxStreams] = c.T;
     }
     consumer_sync();
     // One thread per stream.  A stream whose proposals did not all fit the
@@ -1808,6 +1825,7 @@ cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeight
     for (int i = 0; i < n_streams; ++i) std::memcpy(&km.m[i], &maps[i], sizeof(CUtensorMap));
     MegaArgs a{};
     a.timeline = mb.timeline;
+    a.capture = mb.capture;
     a.d = m.dims;
     a.layers = layers_dev;
     a.embd = m.embd;

@@ -18,7 +18,8 @@ using namespace mtb;
 
 // Maximum sizes the scratch is laid out for.
 constexpr int kNoAllocMaxHidden = 4096;
-constexpr int kNoAllocMaxBlocks = 148 * 4;  // lm_head_blocks() never exceeds this
+constexpr int kNoAllocMaxBlocks = kLmHeadMaxBlocks;  // lm_head_blocks() never exceeds this
+static_assert(kNoAllocMaxBlocks >= kLmHeadMaxBlocks, "the scratch covers every LM-head grid");
 constexpr size_t kActQBytes = size_t(kNoAllocMaxHidden / 32) * 512;
 constexpr size_t kActDBytes = size_t(kNoAllocMaxHidden / 32) * 16 * sizeof(float);
 constexpr size_t kPartBytes = size_t(kNoAllocMaxBlocks) * 16 * sizeof(float2);
@@ -29,6 +30,20 @@ constexpr size_t kScratchBytes = kStateBytes + kActQBytes + kActDBytes + kPartBy
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 namespace {
+// Makes a device current and puts the caller's current device back when it
+// goes out of scope.
+struct DeviceGuard {
+    int saved = -1;
+    bool enter(int device) {
+        if (cudaGetDevice(&saved) != cudaSuccess) saved = -1;
+        return saved == device || cudaSetDevice(device) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (saved >= 0 && cudaGetDevice(&now) == cudaSuccess && now != saved) cudaSetDevice(saved);
+    }
+};
+
 std::mutex g_setup_mutex;
 void* g_scratch_ptr[64] = {};  // device address of g_noalloc_scratch, per device
 thread_local std::string g_noalloc_error;
@@ -81,10 +96,10 @@ extern "C" int mtb_lm_head_argmax_noalloc(const mtb_model* m, const float* hidde
         g_noalloc_error = "vocabulary exceeds the no-allocation scratch limit";
         return -2;
     }
-    int current = -1;
-    if (cudaGetDevice(&current) != cudaSuccess || current != device) {
-        if (cudaSetDevice(device) != cudaSuccess) { g_noalloc_error = "cudaSetDevice failed"; return -1; }
-    }
+    // The model's device is made current for the call and the caller's
+    // current device is restored on every return path.
+    DeviceGuard guard;
+    if (!guard.enter(device)) { g_noalloc_error = "cudaSetDevice failed"; return -1; }
     unsigned char* base = nullptr;
     if (scratch_for(device, &base) != 0) return -1;
     auto* state = reinterpret_cast<StepState*>(base);

@@ -5,8 +5,8 @@ tests read like the reference's own:
   - Decoder.run / prefill / decode_one / logits_from_hidden / rewind / past_len
     -> Qwen3Decoder (src/qwen3_decoder.hpp:37-60)
   - greedy_generate          -> src/generate.cpp:235
-  - cpu_speculative_generate -> src/cpu_speculative.cpp:86 (hooks: draft, committed)
-  - cpu_ngram_draft / cpu_greedy_choice -> src/cpu_speculative.cpp:45,57
+  - cpu_speculative_generate -> src/cpu_speculative.cpp:68 (hooks: draft, committed)
+  - cpu_ngram_draft / cpu_greedy_choice -> src/cpu_speculative.cpp:27,39
 Every call goes to the CUDA library; there is no Python or CPU fallback, and
 loading fails loudly when the library or a GPU is missing.
 """
@@ -90,6 +90,8 @@ SIGNATURES = {
     "mtb_step_kernel_launches": (C.c_int, [_vp]),
     "mtb_transfer_bytes": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "mtb_step_timeline": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, _ip]),
+    "mtb_step_capture": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _ip]),
+    "mtb_debug_poison_kv": (C.c_int, [_vp, C.c_int, C.c_int]),
     "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
     "mtb_lm_head_argmax_noalloc": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
@@ -337,6 +339,24 @@ class Decoder:
         self.last_arrivals = vals[6 * 512 + 2:6 * 512 + 2 + 256 * 512].reshape(256, 512)
         self.last_cta_marks = vals[6 * 512 + 2 + 256 * 512:].reshape(256, 512, 16)
         return [(vals[2 * b], vals[2 * b + 1]) for b in range(512)], (vals[1024], vals[1025]), marks
+
+    def step_capture(self):
+        """The last persistent step's own outputs (MTB_STEP_CAPTURE=1 when the
+        decoder was created): final-normed rows [T][hidden], LM-head maxima
+        [T], their first indices [T] and the per-stream (rows, first row)."""
+        hid = np.zeros((16, self.model.hidden), dtype=np.float32)
+        mv = np.zeros(16, dtype=np.float32)
+        mi = np.zeros(16, dtype=np.int32)
+        sr = np.zeros((8, 2), dtype=np.int32)
+        n = C.c_int()
+        self._check(lib().mtb_step_capture(self.ptr, hid.ctypes.data, mv.ctypes.data, mi.ctypes.data, sr.ctypes.data,
+                                           C.byref(n)), "step_capture")
+        T = n.value
+        return hid[:T], mv[:T], mi[:T], sr
+
+    def poison_kv(self, pos0: int, n_pos: int):
+        """Test hook: NaN into cache positions [pos0, pos0 + n_pos) of every layer."""
+        self._check(lib().mtb_debug_poison_kv(self.ptr, int(pos0), int(n_pos)), "poison_kv")
 
     def transfer_bytes(self):
         a, b = C.c_int64(), C.c_int64()

@@ -404,7 +404,7 @@ int orc_decoder_past_len(const orc_decoder* d) { return d ? d->past : -1; }
 void orc_decoder_reset(orc_decoder* d) {
     if (d) d->past = 0;
 }
-/* src/cpu_speculative.cpp:40-42 */
+/* src/cpu_speculative.cpp:22-24 */
 int orc_decoder_rewind(orc_decoder* d, int position) {
     if (!d || position < 0 || position > d->past) return -1;
     d->past = position;
@@ -496,6 +496,62 @@ static void rope_neox(float* x, int n_dims, int pos, float base) {
 
 static inline float silu(float x) { return x / (1.0f + orc_expf(-x)); }
 
+/* One query row's attention in this oracle's (and the CUDA kernels') order:
+ * positions j < valid of K and V at kbase + j * stride / vbase + j * stride.
+ * Each score q.k is two sequential fmaf chains (even and odd dims) added;
+ * softmax(s * scale) per 64-position chunk (chunk max m_c, e = exp(s - m_c),
+ * the pair sums e[p] + e[p + 32] then a 32-value xor butterfly for l_c, each
+ * context dim one fmaf chain o_c); the chunks merged with weights exp(m_c - M)
+ * in chunk order, o = sum w_c o_c / sum w_c l_c. */
+static void attn_row_chunked(const float* qh, const float* kbase, const float* vbase, size_t stride, int valid, int hd,
+                             float scale, float* oh) {
+    const int n_chunks = (valid + 63) / 64;
+    float* cm = (float*)malloc(sizeof(float) * (size_t)n_chunks);
+    float* cl = (float*)malloc(sizeof(float) * (size_t)n_chunks);
+    float* co = (float*)malloc(sizeof(float) * (size_t)n_chunks * hd);
+    for (int c = 0; c < n_chunks; ++c) {
+        float sc[64], e[64];
+        float mx = -INFINITY;
+        for (int p = 0; p < 64; ++p) {
+            const int j = c * 64 + p;
+            sc[p] = -INFINITY;
+            if (j < valid) {
+                const float* kj = kbase + (size_t)j * stride;
+                float ae = 0.0f, ao = 0.0f;
+                for (int e2 = 0; e2 < hd; e2 += 2) {
+                    ae = fmaf(qh[e2], kj[e2], ae);
+                    ao = fmaf(qh[e2 + 1], kj[e2 + 1], ao);
+                }
+                sc[p] = (ae + ao) * scale;
+            }
+            mx = fmaxf(mx, sc[p]);
+        }
+        float pair[32];
+        for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : orc_expf(sc[p] - mx);
+        for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
+        cm[c] = mx;
+        cl[c] = warp_tree_sum(pair);
+        const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
+        for (int e2 = 0; e2 < hd; ++e2) {
+            float acc = 0.0f;
+            for (int p = 0; p < n_pos; ++p) acc = fmaf(e[p], (vbase + (size_t)(c * 64 + p) * stride)[e2], acc);
+            co[(size_t)c * hd + e2] = acc;
+        }
+    }
+    float M = -INFINITY;
+    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, cm[c]);
+    for (int e2 = 0; e2 < hd; ++e2) {
+        float Ls = 0.0f, acc = 0.0f;
+        for (int c = 0; c < n_chunks; ++c) {
+            const float wgt = orc_expf(cm[c] - M);
+            Ls = fmaf(wgt, cl[c], Ls);
+            acc = fmaf(wgt, co[(size_t)c * hd + e2], acc);
+        }
+        oh[e2] = acc / Ls;
+    }
+    free(cm); free(cl); free(co);
+}
+
 int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidden) {
     if (!d || !embeds || T <= 0 || d->past + T > d->max_seq) return -1;
     const orc_model* m = d->m;
@@ -552,56 +608,9 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 const int kvh = h / group;
-                const float* qh = q + (size_t)t * qd + (size_t)h * hd;
-                const int valid = past + t + 1;
-                const int n_chunks = (valid + 63) / 64;
-                float* cm = (float*)malloc(sizeof(float) * (size_t)n_chunks);
-                float* cl = (float*)malloc(sizeof(float) * (size_t)n_chunks);
-                float* co = (float*)malloc(sizeof(float) * (size_t)n_chunks * hd);
-                for (int c = 0; c < n_chunks; ++c) {
-                    float sc[64], e[64];
-                    float mx = -INFINITY;
-                    for (int p = 0; p < 64; ++p) {
-                        const int j = c * 64 + p;
-                        sc[p] = -INFINITY;
-                        if (j < valid) {
-                            const float* kj = d->k + kv_index(d, l, j) + (size_t)kvh * hd;
-                            /* two fmaf chains, even and odd dims, then their sum */
-                            float ae = 0.0f, ao = 0.0f;
-                            for (int e2 = 0; e2 < hd; e2 += 2) {
-                                ae = fmaf(qh[e2], kj[e2], ae);
-                                ao = fmaf(qh[e2 + 1], kj[e2 + 1], ao);
-                            }
-                            sc[p] = (ae + ao) * scale;
-                        }
-                        mx = fmaxf(mx, sc[p]);
-                    }
-                    float pair[32];
-                    for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : orc_expf(sc[p] - mx);
-                    for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
-                    cm[c] = mx;
-                    cl[c] = warp_tree_sum(pair);
-                    const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
-                    for (int e2 = 0; e2 < hd; ++e2) {
-                        float acc = 0.0f;
-                        for (int p = 0; p < n_pos; ++p)
-                            acc = fmaf(e[p], (d->v + kv_index(d, l, c * 64 + p) + (size_t)kvh * hd)[e2], acc);
-                        co[(size_t)c * hd + e2] = acc;
-                    }
-                }
-                float M = -INFINITY;
-                for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, cm[c]);
-                float* oh = o + (size_t)t * qd + (size_t)h * hd;
-                for (int e2 = 0; e2 < hd; ++e2) {
-                    float Ls = 0.0f, acc = 0.0f;
-                    for (int c = 0; c < n_chunks; ++c) {
-                        const float wgt = orc_expf(cm[c] - M);
-                        Ls = fmaf(wgt, cl[c], Ls);
-                        acc = fmaf(wgt, co[(size_t)c * hd + e2], acc);
-                    }
-                    oh[e2] = acc / Ls;
-                }
-                free(cm); free(cl); free(co);
+                attn_row_chunked(q + (size_t)t * qd + (size_t)h * hd, d->k + kv_index(d, l, 0) + (size_t)kvh * hd,
+                                 d->v + kv_index(d, l, 0) + (size_t)kvh * hd, (size_t)nkv * hd, past + t + 1, hd, scale,
+                                 o + (size_t)t * qd + (size_t)h * hd);
             }
         }
         mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
@@ -652,7 +661,7 @@ int orc_embed_rows(const orc_model* m, const int32_t* ids, int n, float* out) {
 
 /* ------------------------------------------------------------- controller */
 
-/* src/cpu_speculative.cpp:45-56 with the n-gram range made explicit. */
+/* src/cpu_speculative.cpp:27-38 with the n-gram range made explicit. */
 int orc_ngram_draft(const int32_t* h, int n, int maximum, int n_min, int n_max, int32_t* out) {
     /* n < 3 is the reference's guard for its fixed n_min = 2; n_min + 1 is its
      * generalisation (the loop below needs a suffix plus one earlier token). */
@@ -672,7 +681,7 @@ int orc_ngram_draft(const int32_t* h, int n, int maximum, int n_min, int n_max, 
     return 0;
 }
 
-/* src/cpu_speculative.cpp:57-68: first max with strict >, optional penalty
+/* src/cpu_speculative.cpp:39-50: first max with strict >, optional penalty
  * over the set of the last 100 ids. */
 int orc_greedy_choice(const float* raw, int vocab, const int32_t* h, int n, float penalty) {
     if (vocab <= 0) return -1;
@@ -701,7 +710,7 @@ int orc_greedy_choice(const float* raw, int vocab, const int32_t* h, int n, floa
 
 static float clamp_penalty(float p) { return p < 1.f ? 1.f : (p > 1.5f ? 1.5f : p); }
 
-/* src/cpu_speculative.cpp:86-165 */
+/* src/cpu_speculative.cpp:68-147 */
 int orc_spec_generate(orc_decoder* d, const float* fused, int seq, int max_new, int eos,
                       int k_max, int n_min, int n_max, float penalty,
                       int32_t* out_ids, orc_counters* c,
@@ -807,4 +816,218 @@ int orc_greedy_generate(orc_decoder* d, const float* fused, int seq, int max_new
     }
     free(raw); free(emb); free(h);
     return rc ? -1 : n;
+}
+
+/* ============================================================ reference order
+ *
+ * A second restatement of the decoder, TEST ONLY, in the reference's own
+ * evaluation order rather than the order this oracle shares with the CUDA
+ * kernels.  Its only use is to bound how far that shared order sits from the
+ * reference's arithmetic (tests/test_reference_order.py).  ggml itself is
+ * absent here, so the ggml steps below are restated from its published x86
+ * source at the pinned commit (AVX2 q8_0 dot, AVX-512 f32 dot) and cannot be
+ * checked bit for bit against the reference binary.
+ *
+ *  - rms_norm: float squares added in double in element order
+ *    (ggml_compute_forward_rms_norm_f32), 1/sqrtf(mean + eps), (x*s)*w;
+ *  - q8_0 x q8_0 dot (ggml_vec_dot_q8_0_q8_0, AVX2): eight float lanes, lane j
+ *    the int32 sum of the products of bytes 4j..4j+3 of a block; per block
+ *    lane_j = fmaf(d_w*d_x, (float)isum_j, lane_j); then hsum_float_8;
+ *  - f32 dot (ggml_vec_dot_f32, AVX-512): four 16-lane fmaf accumulators over
+ *    64-element steps, reduced 0+2, 1+3, 0+1, then the lanes 8-by-8, 4, 2, 1;
+ *    the tail of n % 64 elements added in double;
+ *  - attention (src/qwen3.cpp:158-189): scores = K.q over every cached
+ *    position, ggml_soft_max_ext / cpu_decode_softmax (src/cpu_softmax.cpp:29-36):
+ *    s*scale (+ -inf past the causal limit), max, e = expf(s - max) with the sum
+ *    in double, p = e * (float)(1/sum); context = P.V over the valid length
+ *    (src/cpu_context.cpp:29, ggml_vec_dot_f32);
+ *  - RoPE with libm sinf/cosf, SiLU x / (1 + expf(-x)) with libm expf.
+ */
+
+static float ref_hsum8(const float* a) {
+    /* hsum_float_8: high 128 + low 128, movehl, movehdup */
+    float r[4];
+    for (int j = 0; j < 4; ++j) r[j] = a[j + 4] + a[j];
+    const float r0 = r[0] + r[2], r1 = r[1] + r[3];
+    return r0 + r1;
+}
+
+static float ref_dot_q8(const blk_q8* w, const blk_q8* x, int nb) {
+    float acc[8] = {0};
+    for (int b = 0; b < nb; ++b) {
+        const float d = h2f(w[b].d) * h2f(x[b].d);
+        for (int j = 0; j < 8; ++j) {
+            int s = 0;
+            for (int u = 0; u < 4; ++u) s += w[b].qs[4 * j + u] * x[b].qs[4 * j + u];
+            acc[j] = fmaf(d, (float)s, acc[j]);
+        }
+    }
+    return ref_hsum8(acc);
+}
+
+static void ref_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int T, float* y) {
+    const int nb = k / 32;
+    blk_q8* xq = (blk_q8*)malloc(sizeof(blk_q8) * (size_t)nb * (size_t)T);
+    for (int t = 0; t < T; ++t) orc_quantize_act_q8(x + (size_t)t * k, k, xq + (size_t)t * nb);
+    const blk_q8* w = (const blk_q8*)w_blocks;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < n_rows; ++n)
+        for (int t = 0; t < T; ++t) y[(size_t)t * n_rows + n] = ref_dot_q8(w + (size_t)n * nb, xq + (size_t)t * nb, nb);
+    free(xq);
+}
+
+/* ggml_vec_dot_f32 with strided operands (x[i * sx], y[i * sy]). */
+static float ref_dot_f32(int n, const float* x, size_t sx, const float* y, size_t sy) {
+    const int np = n & ~63;
+    float acc[4][16];
+    memset(acc, 0, sizeof(acc));
+    for (int i = 0; i < np; i += 64)
+        for (int j = 0; j < 4; ++j)
+            for (int l = 0; l < 16; ++l) {
+                const int e = i + 16 * j + l;
+                acc[j][l] = fmaf(x[(size_t)e * sx], y[(size_t)e * sy], acc[j][l]);
+            }
+    double sum = 0.0;
+    if (np > 0) {
+        float v[16];
+        for (int l = 0; l < 16; ++l) {
+            const float a = acc[0][l] + acc[2][l], b = acc[1][l] + acc[3][l];
+            v[l] = a + b;
+        }
+        for (int w = 8; w > 0; w >>= 1)
+            for (int l = 0; l < w; ++l) v[l] = v[l] + v[l + w];
+        sum = v[0];
+    }
+    for (int i = np; i < n; ++i) sum += (double)(x[(size_t)i * sx] * y[(size_t)i * sy]);
+    return (float)sum;
+}
+
+static void ref_rms_norm_mul(const float* x, const float* w, int n, float eps, float* y) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / n);
+    const float scale = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; ++i) y[i] = (x[i] * scale) * w[i];
+}
+
+static void ref_rope_neox(float* x, int n_dims, int pos, float base) {
+    const float theta_scale = powf(base, -2.0f / (float)n_dims);
+    float theta = (float)pos;
+    const int half = n_dims / 2;
+    for (int i = 0; i < half; ++i) {
+        const float c = cosf(theta), s = sinf(theta);
+        const float x0 = x[i], x1 = x[i + half];
+        x[i] = x0 * c - x1 * s;
+        x[i + half] = x0 * s + x1 * c;
+        theta *= theta_scale;
+    }
+}
+
+/* One query row's attention in the reference's order: scores over the row
+ * (ggml_vec_dot_f32), s * scale, max, e = expf(s - max) summed in double,
+ * p = e * (float)(1 / sum), then each context dim ggml_vec_dot_f32 of the V
+ * column and p over the valid length.  Positions past `valid` (the causal
+ * mask's -inf) contribute exact zeros and are left out. */
+static void attn_row_ref(const float* qh, const float* kbase, const float* vbase, size_t stride, int valid, int hd,
+                         float scale, float* oh) {
+    float* p = (float*)malloc(sizeof(float) * (size_t)valid);
+    float mx = -INFINITY;
+    for (int j = 0; j < valid; ++j) {
+        p[j] = ref_dot_f32(hd, kbase + (size_t)j * stride, 1, qh, 1) * scale;
+        mx = fmaxf(mx, p[j]);
+    }
+    double sum = 0.0;
+    for (int j = 0; j < valid; ++j) {
+        const float e = expf(p[j] - mx);
+        sum += (double)e;
+        p[j] = e;
+    }
+    const float inv = (float)(1.0 / sum);
+    for (int j = 0; j < valid; ++j) p[j] = p[j] * inv;
+    for (int e2 = 0; e2 < hd; ++e2) oh[e2] = ref_dot_f32(valid, vbase + e2, stride, p, 1);
+    free(p);
+}
+
+/* Test exports of the two orders' building blocks: one attention row over
+ * K, V [valid][hd] (ref_order 0: this oracle's chunked order, 1: the
+ * reference's), and one q8_0 x q8_0 block dot. */
+void orc_attention_row(int ref_order, const float* q, const float* k, const float* v, int valid, int hd, float* out) {
+    const float scale = 1.0f / sqrtf((float)hd);
+    if (ref_order)
+        attn_row_ref(q, k, v, (size_t)hd, valid, hd, scale, out);
+    else
+        attn_row_chunked(q, k, v, (size_t)hd, valid, hd, scale, out);
+}
+
+float orc_dot_q8_blocks(int ref_order, const void* w, const void* x, int nb) {
+    return ref_order ? ref_dot_q8((const blk_q8*)w, (const blk_q8*)x, nb) : dot_q8((const blk_q8*)w, (const blk_q8*)x, nb);
+}
+
+int orc_decoder_run_ref(orc_decoder* d, const float* embeds, int T, float* out_hidden) {
+    if (!d || !embeds || T <= 0 || d->past + T > d->max_seq || d->m->wtype != ORC_Q8_0) return -1;
+    const orc_model* m = d->m;
+    const int H = m->hidden, hd = m->head_dim, nh = m->n_heads, nkv = m->n_kv, F = m->ffn;
+    const int past = d->past, kv = past + T, group = nh / nkv;
+    const int qd = nh * hd, kd = nkv * hd;
+    float* x = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* xn = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* q = (float*)malloc(sizeof(float) * (size_t)T * qd);
+    float* k = (float*)malloc(sizeof(float) * (size_t)T * kd);
+    float* v = (float*)malloc(sizeof(float) * (size_t)T * kd);
+    float* o = (float*)malloc(sizeof(float) * (size_t)T * qd);
+    float* proj = (float*)malloc(sizeof(float) * (size_t)T * H);
+    float* g = (float*)malloc(sizeof(float) * (size_t)T * F);
+    float* u = (float*)malloc(sizeof(float) * (size_t)T * F);
+    memcpy(x, embeds, sizeof(float) * (size_t)T * H);
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int l = 0; l < m->n_layers; ++l) {
+        const orc_layer* L = &m->layers[l];
+        for (int t = 0; t < T; ++t) ref_rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H);
+        ref_mul_mat_q8(L->wq, qd, H, xn, T, q);
+        ref_mul_mat_q8(L->wk, kd, H, xn, T, k);
+        ref_mul_mat_q8(L->wv, kd, H, xn, T, v);
+        for (int t = 0; t < T; ++t) {
+            for (int h = 0; h < nh; ++h) {
+                float* qh = q + (size_t)t * qd + (size_t)h * hd;
+                ref_rms_norm_mul(qh, L->q_norm, hd, m->eps, qh);
+                ref_rope_neox(qh, hd, past + t, m->theta);
+            }
+            for (int h = 0; h < nkv; ++h) {
+                float* kh = k + (size_t)t * kd + (size_t)h * hd;
+                ref_rms_norm_mul(kh, L->k_norm, hd, m->eps, kh);
+                ref_rope_neox(kh, hd, past + t, m->theta);
+            }
+            float* kdst = d->k + kv_index(d, l, past + t);
+            float* vdst = d->v + kv_index(d, l, past + t);
+            for (int i = 0; i < kd; ++i) {
+                kdst[i] = d->kv_fp16 ? round_f16(k[(size_t)t * kd + i]) : k[(size_t)t * kd + i];
+                vdst[i] = d->kv_fp16 ? round_f16(v[(size_t)t * kd + i]) : v[(size_t)t * kd + i];
+            }
+        }
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int t = 0; t < T; ++t) {
+            for (int h = 0; h < nh; ++h) {
+                const int kvh = h / group;
+                attn_row_ref(q + (size_t)t * qd + (size_t)h * hd, d->k + kv_index(d, l, 0) + (size_t)kvh * hd,
+                             d->v + kv_index(d, l, 0) + (size_t)kvh * hd, (size_t)nkv * hd, past + t + 1, hd, scale,
+                             o + (size_t)t * qd + (size_t)h * hd);
+            }
+        }
+        ref_mul_mat_q8(L->wo, H, qd, o, T, proj);
+        for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
+        for (int t = 0; t < T; ++t) ref_rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H);
+        ref_mul_mat_q8(L->wgate, F, H, xn, T, g);
+        ref_mul_mat_q8(L->wup, F, H, xn, T, u);
+        for (size_t i = 0; i < (size_t)T * F; ++i) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+        ref_mul_mat_q8(L->wdown, H, F, g, T, proj);
+        for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
+    }
+    for (int t = 0; t < T; ++t) ref_rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H);
+    d->past = kv;
+    free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u);
+    return 0;
+}
+
+void orc_decoder_logits_ref(const orc_decoder* d, const float* hidden_row, float* logits) {
+    ref_mul_mat_q8(d->m->token_embd, d->m->vocab, d->m->hidden, hidden_row, 1, logits);
 }

@@ -8,9 +8,9 @@
  *
  * What it restates (reference paths are relative to the moss-transcribe.cpp
  * project root):
- *   - src/cpu_speculative.cpp:45-56    n-gram draft (latest match, longest n first)
- *   - src/cpu_speculative.cpp:57-68    greedy choice (first max, recent-100 penalty)
- *   - src/cpu_speculative.cpp:86-165   strict speculative controller, counters,
+ *   - src/cpu_speculative.cpp:27-38    n-gram draft (latest match, longest n first)
+ *   - src/cpu_speculative.cpp:39-50    greedy choice (first max, recent-100 penalty)
+ *   - src/cpu_speculative.cpp:68-147  strict speculative controller, counters,
  *                                      lazy per-row logits, logical rewind
  *   - src/generate.cpp:235-326         serial greedy generate
  *   - src/generate.cpp:33-66           q8_0 row dequant for the embedding lookup
@@ -125,7 +125,7 @@ int orc_embed_rows(const orc_model* m, const int32_t* ids, int n, float* out);
 /* ---- controller ---- */
 int orc_ngram_draft(const int32_t* history, int n, int maximum, int n_min, int n_max, int32_t* out);
 int orc_greedy_choice(const float* raw, int vocab, const int32_t* history, int n, float penalty);
-/* Strict speculative generate (src/cpu_speculative.cpp:86-165) with the draft
+/* Strict speculative generate (src/cpu_speculative.cpp:68-147) with the draft
  * policy made explicit: at most k_max proposals, n-gram sizes n_max..n_min.
  * Returns the number of ids written (including a trailing EOS), -1 on error. */
 int orc_spec_generate(orc_decoder* d, const float* fused, int seq, int max_new, int eos,
@@ -143,6 +143,18 @@ void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int
 /* The same for f16 weights [n_rows x k]: x rounded to fp16, exact products,
  * 32-element fmaf chains, blocks then 256-element slices added in order. */
 void orc_mul_mat_f16(const void* w_half, int n_rows, int k, const float* x, int T, float* y);
+
+/* TEST ONLY: the same decoder in the reference's own evaluation order (ggml's
+ * x86 dot orders, whole-row softmax with the sum in double, P.V over the
+ * valid length, libm expf/sinf/cosf), q8_0 models only.  Used to bound how far
+ * this oracle's evaluation order sits from the reference's arithmetic. */
+int orc_decoder_run_ref(orc_decoder* d, const float* embeds, int T, float* out_hidden);
+void orc_decoder_logits_ref(const orc_decoder* d, const float* hidden_row, float* logits);
+/* TEST ONLY: one attention row over K, V [valid][hd] in this oracle's order
+ * (ref_order 0) or the reference's (1); one q8_0 x q8_0 dot of nb blocks in
+ * either order. */
+void orc_attention_row(int ref_order, const float* q, const float* k, const float* v, int valid, int hd, float* out);
+float orc_dot_q8_blocks(int ref_order, const void* w, const void* x, int nb);
 void orc_set_threads(int n);
 /* The exp / sin / cos the oracle (and the CUDA kernels) evaluate. */
 float orc_expf(float x);

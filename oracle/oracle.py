@@ -15,6 +15,7 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = None
+_NATIVE = False
 
 F32, F16, Q8_0 = 0, 1, 8
 
@@ -36,10 +37,30 @@ def build():
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
 
 
+def use_native():
+    """Load the -march=native build (the timed CPU baseline), compiling it on
+    this host first.  Must run before the first lib() call."""
+    global _NATIVE
+    if _LIB is not None and not _NATIVE:
+        raise RuntimeError("the portable oracle library is already loaded")
+    subprocess.run(["make", "-s", "-C", _HERE, "native"], check=True)
+    _NATIVE = True
+
+
+def host_isa() -> str:
+    """The SIMD extensions of this host that the native build can use."""
+    try:
+        flags = next(l for l in open("/proc/cpuinfo") if l.startswith("flags")).split()
+    except (OSError, StopIteration):
+        return "unknown"
+    want = ["avx2", "fma", "f16c", "avx512f", "avx512bw", "avx512_vnni", "avx_vnni", "avx512_fp16", "amx_int8"]
+    return "+".join(f for f in want if f in flags) or "baseline x86-64"
+
+
 def lib():
     global _LIB
     if _LIB is None:
-        path = os.path.join(_HERE, "liboracle.so")
+        path = os.path.join(_HERE, "liboracle_native.so" if _NATIVE else "liboracle.so")
         if not os.path.exists(path):
             build()
         L = C.CDLL(path)
@@ -57,6 +78,11 @@ def lib():
         L.orc_decoder_rewind.argtypes = [vp, C.c_int]
         L.orc_decoder_run.argtypes = [vp, f32p, C.c_int, f32p]
         L.orc_decoder_logits.argtypes = [vp, f32p, f32p]
+        L.orc_decoder_run_ref.argtypes = [vp, f32p, C.c_int, f32p]
+        L.orc_decoder_logits_ref.argtypes = [vp, f32p, f32p]
+        L.orc_attention_row.argtypes = [C.c_int, f32p, f32p, f32p, C.c_int, C.c_int, f32p]
+        L.orc_dot_q8_blocks.restype = C.c_float
+        L.orc_dot_q8_blocks.argtypes = [C.c_int, vp, vp, C.c_int]
         L.orc_decoder_kv_read.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, f32p]
         L.orc_decoder_kv_write.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, f32p]
         L.orc_decoder_fill_synthetic_kv.argtypes = [vp, C.c_int, C.c_uint32]
@@ -132,6 +158,24 @@ def mul_mat_f16(w: np.ndarray, x: np.ndarray) -> np.ndarray:
     y = np.zeros((x.shape[0], n_rows), dtype=np.float32)
     lib().orc_mul_mat_f16(w.ctypes.data, n_rows, k, _f32(x), x.shape[0], _f32(y))
     return y
+
+
+def attention_row(q: np.ndarray, k: np.ndarray, v: np.ndarray, ref_order: bool) -> np.ndarray:
+    """One query row's attention over K, V [valid][hd]: this oracle's chunked
+    order, or the reference's whole-row order (test only)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    out = np.zeros(q.size, dtype=np.float32)
+    lib().orc_attention_row(int(ref_order), _f32(q), _f32(k), _f32(v), k.shape[0], q.size, _f32(out))
+    return out
+
+
+def dot_q8_blocks(w_blocks: np.ndarray, x_blocks: np.ndarray, ref_order: bool) -> float:
+    """q8_0 x q8_0 dot of two block rows (34-byte blocks) in either order (test only)."""
+    w = np.ascontiguousarray(w_blocks, dtype=np.uint8)
+    x = np.ascontiguousarray(x_blocks, dtype=np.uint8)
+    return float(lib().orc_dot_q8_blocks(int(ref_order), w.ctypes.data, x.ctypes.data, w.size // 34))
 
 
 def ngram_draft(history, maximum: int, n_min: int = 2, n_max: int = 16) -> list[int]:
@@ -222,6 +266,20 @@ class OracleDecoder:
         h = np.ascontiguousarray(hidden_row, dtype=np.float32).ravel()
         out = np.zeros(self.shape.vocab, dtype=np.float32)
         lib().orc_decoder_logits(self.ptr, _f32(h), _f32(out))
+        return out
+
+    def run_ref(self, embeds: np.ndarray) -> np.ndarray:
+        """run() in the reference's own evaluation order (test only; q8_0 models)."""
+        e = np.ascontiguousarray(embeds, dtype=np.float32).reshape(-1, self.shape.hidden)
+        out = np.zeros_like(e)
+        if lib().orc_decoder_run_ref(self.ptr, _f32(e), e.shape[0], _f32(out)):
+            raise RuntimeError("oracle run_ref failed")
+        return out
+
+    def logits_ref(self, hidden_row: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(hidden_row, dtype=np.float32).ravel()
+        out = np.zeros(self.shape.vocab, dtype=np.float32)
+        lib().orc_decoder_logits_ref(self.ptr, _f32(h), _f32(out))
         return out
 
     def kv(self, layer: int, which: int, pos0: int, n: int) -> np.ndarray:
