@@ -60,6 +60,28 @@ constexpr int kArrivalBase = 6 * kMaxBarriers + 2;     // [cta][barrier] arrival
 constexpr int kCtaMarkBase = kArrivalBase + 256 * kMaxBarriers;  // [cta][barrier][16] sub-phase marks
 constexpr int kCtaMarks = 16;
 
+// Shared memory, named at file scope so that every function's accesses
+// compile to shared-window loads and stores (a pointer kept in memory, or a
+// pointer parameter of a non-inlined function, would be a generic address).
+// Dynamic: the ring (kRingSlots slots), the region (activation fragments,
+// slice partials, attention scratch), the RoPE table, the ring's mbarriers.
+extern __shared__ __align__(1024) uint8_t g_smem[];
+__shared__ double g_wsum[kConsumerWarps * kTMax];
+__shared__ float g_scale[kTMax * 4];
+__shared__ float2 g_cand[kConsumerWarps * kTMax];
+__shared__ int g_flag;
+__shared__ __align__(8) uint64_t g_lm_bars[4];  // tcgen05 LM head: half_full[2], half_free[2]
+__shared__ uint32_t g_tmem;                      // TMEM base address of the tcgen05 LM head
+__shared__ float g_qk_norm[2 * kHeadDim];        // the layer's q_norm and k_norm weights, staged by phase A for B
+
+__device__ __forceinline__ uint8_t* s_ring() { return g_smem; }
+__device__ __forceinline__ uint8_t* s_region() { return g_smem + (size_t)kRingSlots * kSlotBytes; }
+__device__ __forceinline__ float* s_rope() { return reinterpret_cast<float*>(g_smem + (size_t)kRingSlots * kSlotBytes + kRegionBytes); }
+__device__ __forceinline__ uint64_t* s_full() {
+    return reinterpret_cast<uint64_t*>(g_smem + (size_t)kRingSlots * kSlotBytes + kRegionBytes + kRopeBytes);
+}
+__device__ __forceinline__ uint64_t* s_empty() { return s_full() + kRingSlots; }
+
 struct MegaArgs {
     ModelDims d;
     const LayerWeights* layers;  // device array
@@ -404,16 +426,17 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
         // Every CTA's arrival, for the skew between CTAs.
         if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
         // Arrive with release semantics (the CTA's writes, ordered before by the
-        // named barrier, become visible with it); poll relaxed; acquire once.
+        // named barrier, become visible with it); poll with acquire loads, so
+        // the load that sees the last arrival orders everything after it.
         if (!(b == a.stall_barrier && blockIdx.x == 0))
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long t0 = global_ns();
         int status = 0;
         for (unsigned it = 0;; ++it) {
             unsigned v;
-            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
             if (v >= target) break;
-            if ((it & 31) == 31) {
+            if ((it & 255) == 255) {
                 if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
                 if (global_ns() - t0 > a.wait_ns) {
                     atomicExch(a.abort_flag, 1);
@@ -423,7 +446,6 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
                 }
             }
         }
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         if (a.timeline && blockIdx.x == 0) a.timeline[2 * b + 1] = global_ns();
         *s_flag = status;
     }
@@ -473,10 +495,15 @@ __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
 // (4 group + chunk) * 128, row at +16 row; scales f32 [16][K / 32]).
 template <int NK, bool kUmma = false>
 __device__ __noinline__ void norm_quant_smem(const float* x, const float* __restrict__ wn, float eps, int T,
-                                            uint8_t* act_q, float* act_d, double* s_wsum, float* s_scale,
                                             unsigned long long* timeline = nullptr, int pid = 0,
                                             float* normed_out = nullptr) {
     constexpr int K = 256 * NK;
+    // Fragments at the region's start, scales after them (K / 32 blocks x 512
+    // bytes, or the tcgen05 layout's K / 64 steps x 1024 bytes: the same size).
+    uint8_t* act_q = s_region();
+    float* act_d = reinterpret_cast<float*>(s_region() + (size_t)K * 16);
+    double* s_wsum = g_wsum;
+    float* s_scale = g_scale;
     constexpr int RG = 8;  // rows per pass (rows are independent; 8 x NK values per lane)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float wv[NK];
@@ -824,7 +851,7 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
         const uint8_t* kb_row =
             kv_slot_base(const_cast<uint8_t*>(ring), (s0 + (lane + 32) / KS::kRowsPerSlot) % kRingSlots) + pr * 128;
         constexpr int EB = F16 ? 8 : 4;  // dims per 16-byte read
-#pragma unroll 1
+#pragma unroll 2
         for (int eb = 0; eb < kHeadDim / EB; ++eb) {
             float2 ka[EB / 2], kb[EB / 2];
             const int off = (eb >> 3) * KS::kBoxBytes + (((eb & 7) ^ xs) << 4);
@@ -950,11 +977,16 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
 // The item's stream has T rows from step row row0 on, after `before` cached
 // positions, in cache `kv`.  Its partials are stored under step rows (row0 + t) * G + jh.
 template <bool F16, int RP>
-__device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
-                                       const float* rope, const float* qk_norm, int l, int chunk, int h, long long q0, int T, int before,
-                                       int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
-                                       int mark_pid, int mark_k) {
+__device__ __noinline__ bool attn_body(const MegaArgs& a, size_t scratch_off, int rows_cap, int l, int chunk, int h,
+                                       long long q0, int T, int before, int row0, const KvCache& kv, bool q_cached, int wl,
+                                       int wpi, int bar, int mark_pid, int mark_k) {
     using KS = KvSlots<F16>;
+    uint8_t* ring = s_ring();
+    uint64_t* full = s_full();
+    const float* rope = s_rope();
+    const float* qk_norm = g_qk_norm;
+    float* sq = reinterpret_cast<float*>(s_region() + scratch_off);
+    float2* sw = reinterpret_cast<float2*>(s_region() + scratch_off + (size_t)rows_cap * kHeadDim * 4);
     const int nh = a.d.n_heads, nkv = a.d.n_kv, G = nh / nkv;
     const int lane = threadIdx.x & 31, nthr = wpi * 32;
     const int kv_len = before + T, NQ = T * G;
@@ -1028,15 +1060,14 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, uint8_t* ring, uint64_
 }
 
 template <bool F16>
-__device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint64_t* full, float* sq, float2* sw,
-                                          const float* rope, const float* qk_norm, int l, int chunk, int h, long long q0, int T, int before,
-                                          int row0, const KvCache& kv, bool q_cached, int wl, int wpi, int bar,
-                                          int mark_pid, int mark_k) {
+__device__ __forceinline__ bool attn_item(const MegaArgs& a, size_t scratch_off, int rows_cap, int l, int chunk, int h,
+                                          long long q0, int T, int before, int row0, const KvCache& kv, bool q_cached,
+                                          int wl, int wpi, int bar, int mark_pid, int mark_k) {
     const int NQ = T * (a.d.n_heads / a.d.n_kv);
     const int R = wl < NQ ? (NQ - 1 - wl) / wpi + 1 : 0;
 #define MTB_ATTN_BODY(RP) \
-    attn_body<F16, RP>(a, ring, full, sq, sw, rope, qk_norm, l, chunk, h, q0, T, before, row0, kv, q_cached, wl, wpi, bar, \
-                       mark_pid, mark_k)
+    attn_body<F16, RP>(a, scratch_off, rows_cap, l, chunk, h, q0, T, before, row0, kv, q_cached, wl, wpi, bar, mark_pid, \
+                       mark_k)
     if (R <= 1) return MTB_ATTN_BODY(1);
     if (R == 2) return MTB_ATTN_BODY(2);
     return MTB_ATTN_BODY(4);  // R <= 4: see KCtx::attn_wpi
@@ -1051,18 +1082,6 @@ __device__ __forceinline__ bool attn_item(const MegaArgs& a, uint8_t* ring, uint
 struct KCtx {
     MegaArgs a;
     Schedule sch;
-    uint8_t* ring;
-    uint8_t* region;   // activation fragments + slice partials / attention scratch
-    float* rope;       // [16][64][cos, sin]
-    uint64_t* full;
-    uint64_t* empty;
-    double* wsum;      // [8][16]
-    float* scale;      // [16]
-    float2* cand;      // [8][16]
-    int* flag;
-    uint64_t* lm_bars; // [4]: tcgen05 LM head half_full[2], half_free[2]
-    uint32_t* tmem;    // TMEM base address of the tcgen05 LM head
-    float* qk_norm;    // [2][128]: the layer's q_norm and k_norm weights, staged by phase A for B
     int T;             // rows of the step, all streams
     // Per stream: rows, first step row, cached positions, attention chunks.
     int s_T[kMaxStreams], s_row0[kMaxStreams], s_before[kMaxStreams], s_chunks[kMaxStreams];
@@ -1073,18 +1092,22 @@ struct KCtx {
     int attn_wpi;
 };
 
+__shared__ KCtx g_ctx;
+
 __device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
 
 // Grid barrier at the end of a phase; false when the step is being aborted.
-__device__ __noinline__ bool end_phase(const KCtx& c, unsigned* target) {
+__device__ __noinline__ bool end_phase(unsigned* target) {
+    const KCtx& c = g_ctx;
     *target += gridDim.x;
-    return grid_barrier(c.a, *target, c.flag);
+    return grid_barrier(c.a, *target, &g_flag);
 }
 
 // RoPE angles of the step's positions (theta advanced by repeated float
 // products, src/qwen3.cpp:109-118), shared by every layer; and the embedding
 // rows of the step's tokens (q8_0 dequant from the token_embd tiles).
-__device__ __noinline__ void phase_embed(const KCtx& c) {
+__device__ __noinline__ void phase_embed() {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const int tid = threadIdx.x, H = a.d.hidden;
     for (int i = tid; i < kTMax * 64; i += kConsumers) {
@@ -1094,8 +1117,8 @@ __device__ __noinline__ void phase_embed(const KCtx& c) {
         for (int j = 0; j < k; ++j) theta = __fmul_rn(theta, a.theta_scale);
         float sn, cs;
         exact_sincosf(theta, &sn, &cs);
-        c.rope[i * 2] = cs;
-        c.rope[i * 2 + 1] = sn;
+        s_rope()[i * 2] = cs;
+        s_rope()[i * 2 + 1] = sn;
     }
     const int kt_n = H / kTileK;
     for (int i = blockIdx.x * kConsumers + tid; i < kTMax * H; i += gridDim.x * kConsumers) {
@@ -1134,11 +1157,12 @@ __device__ __forceinline__ void for_outputs(const float4& y, int T, F f) {
 
 // A: RMSNorm + quantise (every CTA), QKV rows -> qkv.
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int pid) {
+__device__ __noinline__ bool phase_qkv(int l, long long* cur, int pid) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const LayerWeights& w = a.layers[l];
     constexpr int K = 256 * NK;
-    uint8_t* act_q = c.region;
+    uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
     // The layer's q/k norm weights for phase B, loaded here where the latency
     // hides behind this phase's work (B would otherwise chase the layer's
@@ -1146,13 +1170,13 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
     const float qkn = threadIdx.x < 2 * kHeadDim
                           ? __ldg((threadIdx.x < kHeadDim ? w.q_norm : w.k_norm) + (threadIdx.x % kHeadDim))
                           : 0.f;
-    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, a.timeline, pid);
-    if (threadIdx.x < 2 * kHeadDim) c.qk_norm[threadIdx.x] = qkn;
+    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, a.timeline, pid);
+    if (threadIdx.x < 2 * kHeadDim) g_qk_norm[threadIdx.x] = qkn;
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     const int ldq = (a.d.n_heads + 2 * a.d.n_kv) * kHeadDim, T = c.T;
-    return weight_phase<kLow>(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+    return weight_phase<kLow>(pi, 1, K / kTileK, s_ring(), s_full(), s_empty(), reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
                             for_outputs(sum_slices(part, K / kTileK / 4), T, [&](int row, int col, float v) {
@@ -1167,15 +1191,14 @@ __device__ __noinline__ bool phase_qkv(const KCtx& c, int l, long long* cur, int
 // counts it for its head's merge.  Four groups of two warps when every stream
 // has at most 4 query rows per kv head (four fp16 items fill the ring), one of
 // eight above 16 rows, else two groups of four.
-__device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, int pid) {
+__device__ __noinline__ bool phase_attn(int l, long long* cur, int pid) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const PhaseInfo pi = c.sch.take(W_ATTN, &cur[0], &cur[1]);
     const int nkv = a.d.n_kv, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int wpi = c.attn_wpi, n_groups = kConsumerWarps / wpi, g = warp / wpi, wl = warp % wpi;
     const int rows_cap = wpi == 2 ? 4 : 32;
-    uint8_t* scratch = c.region + (size_t)g * rows_cap * kAttnRowBytes;
-    float* sq = reinterpret_cast<float*>(scratch);
-    float2* sw = reinterpret_cast<float2*>(scratch + (size_t)rows_cap * kHeadDim * 4);
+    const size_t scratch_off = (size_t)g * rows_cap * kAttnRowBytes;
     bool ok = true;
     int prev = -1;  // stream * n_kv + head of the group's previous item
     for (int j = g; j < pi.count; j += n_groups) {
@@ -1186,10 +1209,10 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int mp = j == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
         const bool good = c.sch.kv_f16
-                              ? attn_item<true>(a, c.ring, c.full, sq, sw, c.rope, c.qk_norm, l, chunk, h, q0, c.s_T[si],
+                              ? attn_item<true>(a, scratch_off, rows_cap, l, chunk, h, q0, c.s_T[si],
                                                 c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
                                                 mp, mk)
-                              : attn_item<false>(a, c.ring, c.full, sq, sw, c.rope, c.qk_norm, l, chunk, h, q0, c.s_T[si],
+                              : attn_item<false>(a, scratch_off, rows_cap, l, chunk, h, q0, c.s_T[si],
                                                  c.s_before[si], c.s_row0[si], a.st_kv[si], q_cached, wl, wpi, 2 + g,
                                                  mp, mk);
         ok = ok && good;
@@ -1198,7 +1221,7 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
         // cumulative over the group's stores, ordered by the named barrier).
         item_sync(2 + g, wpi * 32);
         if (wl == 0) {
-            if (lane < pi.slots) mbar_arrive(&c.empty[(q0 + lane) % kRingSlots]);
+            if (lane < pi.slots) mbar_arrive(&s_empty()[(q0 + lane) % kRingSlots]);
             if (lane == 0) {
                 unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + si) * nkv + h;
                 asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
@@ -1212,7 +1235,8 @@ __device__ __noinline__ bool phase_attn(const KCtx& c, int l, long long* cur, in
 // C: chunk merge + quantise, one (row, q head, block) per warp, warps
 // numbered across CTAs; no grid barrier before it: each task waits for its
 // head's attention items only (they finish at different times).
-__device__ __noinline__ bool phase_combine(const KCtx& c, int l) {
+__device__ __noinline__ bool phase_combine(int l) {
+    const KCtx& c = g_ctx;
     const int nh = c.a.d.n_heads, warp = threadIdx.x >> 5;
     const int n_tasks = c.T * nh * 4;
     bool ok = true;
@@ -1227,7 +1251,8 @@ __device__ __noinline__ bool phase_combine(const KCtx& c, int l) {
 // values of the warp's first item are read before the weight work, so the
 // epilogue does not wait for them.
 template <bool kLow>
-__device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* cur, int pid, bool down) {
+__device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bool down) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const int K = down ? a.d.ffn : a.d.n_heads * kHeadDim, H = a.d.hidden, T = c.T;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -1241,12 +1266,12 @@ __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* c
             if (row < T) xr[k] = __ldcg(a.x + (size_t)row * H + item * kTileRows + 2 * t + (k & 1));
         }
     }
-    uint8_t* act_q = c.region;
+    uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
     load_act_smem(down ? a.act2_q : a.act_q, down ? a.act2_d : a.act_d, K, act_q, act_d);
     mark(a.timeline, pid, 0);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
-    return weight_phase<kLow>(pi, 1, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q), act_d,
+    return weight_phase<kLow>(pi, 1, K / kTileK, s_ring(), s_full(), s_empty(), reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
                             const float4 y = sum_slices(part, K / kTileK / 4);
@@ -1267,20 +1292,21 @@ __device__ __noinline__ bool phase_proj_resid(const KCtx& c, int l, long long* c
 // (warp k: pair k), then the block's q8_0 quantisation for the down
 // projection (one row per warp at a time) straight from shared memory.
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_gu(const KCtx& c, int l, long long* cur, int pid) {
+__device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const LayerWeights& w = a.layers[l];
     constexpr int K = 256 * NK;
     constexpr int S = K / kTileK / 4;  // slices per row group
     const int T = c.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint8_t* act_q = c.region;
+    uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T, act_q, act_d, c.wsum, c.scale);
+    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_GU, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     float* s_gu = reinterpret_cast<float*>(s_part + (size_t)pi.count * 8 * S * 32);  // [16 rows][32 features]
-    const bool ok = weight_phase<kLow>(pi, 8, K / kTileK, c.ring, c.full, c.empty, reinterpret_cast<const uint4*>(act_q),
+    const bool ok = weight_phase<kLow>(pi, 8, K / kTileK, s_ring(), s_full(), s_empty(), reinterpret_cast<const uint4*>(act_q),
                                        act_d, s_part, a.abort_flag, [](int, const float4*) {});
     const int g = lane >> 2, t = lane & 3;
     for (int j = 0; j < pi.count; ++j) {
@@ -1313,13 +1339,14 @@ __device__ __noinline__ bool phase_gu(const KCtx& c, int l, long long* cur, int 
 
 // G: final RMSNorm + quantise; LM head with the fused first max -> lm_val[cta].
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
+__device__ __noinline__ bool phase_lm(long long* cur, int pid) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     constexpr int K = 256 * NK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-    uint8_t* act_q = c.region;
+    uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, nullptr, 0,
+    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, nullptr, 0,
                         blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
@@ -1330,14 +1357,14 @@ __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
         const int item = pi.first + j * gridDim.x;
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int jw = j / kConsumerWarps;  // this warp's item count so far
-        if (warp == 0 && jw < 7 && slot_wait(c.full, q0, a.abort_flag)) mark(a.timeline, pid, 1 + 2 * jw);
+        if (warp == 0 && jw < 7 && slot_wait(s_full(), q0, a.abort_flag)) mark(a.timeline, pid, 1 + 2 * jw);
         float4 y;
-        if (!item_rows<kLow>(c.ring, c.full, c.empty, q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
+        if (!item_rows<kLow>(s_ring(), s_full(), s_empty(), q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
                        a.abort_flag, &y)) {
             ok = false;
             break;
         }
-        release_item(c.empty, q0, pi.slots);
+        release_item(s_empty(), q0, pi.slots);
         if (warp == 0 && jw < 7) mark(a.timeline, pid, 2 + 2 * jw);
         const float yy[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
@@ -1363,15 +1390,15 @@ __device__ __noinline__ bool phase_lm(const KCtx& c, long long* cur, int pid) {
         }
     }
     if (t == 0) {
-        c.cand[warp * kTMax + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
-        c.cand[warp * kTMax + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
+        g_cand[warp * kTMax + g] = make_float2(best_v[0], __int_as_float(best_i[0]));
+        g_cand[warp * kTMax + g + 8] = make_float2(best_v[1], __int_as_float(best_i[1]));
     }
     consumer_sync();
     if (tid < kTMax) {
         float bv = -INFINITY;
         int bi = 0x7fffffff;
         for (int r = 0; r < kConsumerWarps; ++r) {
-            const float2 cc = c.cand[r * kTMax + tid];
+            const float2 cc = g_cand[r * kTMax + tid];
             const int ci = __float_as_int(cc.y);
             if (cc.x > bv || (cc.x == bv && ci < bi)) { bv = cc.x; bi = ci; }
         }
@@ -1396,19 +1423,20 @@ __device__ __forceinline__ uint64_t lm_desc(uint32_t addr) {
 }
 
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid) {
+__device__ __noinline__ bool phase_lm_tc(long long* cur, int pid) {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     constexpr int K = 256 * NK, NB = K / 32, STEPS = K / 64, HALF = STEPS / 2, TT = kLow ? 8 : kTMax;
     constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(16 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint8_t* act_q = c.region;                                          // [STEPS][1024]
-    float* act_d = reinterpret_cast<float*>(c.region + STEPS * 1024);   // [16][NB]
-    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, act_q, act_d, c.wsum, c.scale, nullptr, 0,
+    uint8_t* act_q = s_region();                                          // [STEPS][1024]
+    float* act_d = reinterpret_cast<float*>(s_region() + STEPS * 1024);   // [16][NB]
+    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, nullptr, 0,
                               blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
-    uint64_t* half_full = c.lm_bars;
-    uint64_t* half_free = c.lm_bars + 2;
+    uint64_t* half_full = g_lm_bars;
+    uint64_t* half_free = g_lm_bars + 2;
     if (tid == 0) {
         mbar_init(&half_full[0], 1);
         mbar_init(&half_full[1], 1);
@@ -1419,13 +1447,13 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
     // The activation bytes were written by the generic proxy; the tensor core reads them through the async proxy.
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(c.tmem)) : "memory");
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_addr(&g_tmem)) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     consumer_sync();
     mark(a.timeline, pid, 1);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tmem = *c.tmem;
+    const uint32_t tmem = g_tmem;
     bool ok = true;
     float best_v[TT];
     int best_i[TT];
@@ -1438,9 +1466,9 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
                 const int h = ks / HALF;
                 if (ks % HALF == 0 && j > 0 && !mbar_wait(&half_free[h], unsigned((j - 1) & 1), a.abort_flag)) { ok = false; break; }
                 const long long q = q0 + ks;
-                if (!mbar_wait(&c.full[q % kRingSlots], unsigned((q / kRingSlots) & 1), a.abort_flag)) { ok = false; break; }
+                if (!mbar_wait(&s_full()[q % kRingSlots], unsigned((q / kRingSlots) & 1), a.abort_flag)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t wslot = smem_addr(c.ring + (size_t)(q % kRingSlots) * kSlotBytes);
+                const uint32_t wslot = smem_addr(s_ring() + (size_t)(q % kRingSlots) * kSlotBytes);
                 const uint32_t xstep = smem_addr(act_q + ks * 1024);
 #pragma unroll
                 for (int b = 0; b < 2; ++b) {
@@ -1453,7 +1481,7 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
                         : "memory");
                 }
                 asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
-                             ::"r"(smem_addr(&c.empty[q % kRingSlots])) : "memory");
+                             ::"r"(smem_addr(&s_empty()[q % kRingSlots])) : "memory");
                 if (ks % HALF == HALF - 1)
                     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                                  ::"r"(smem_addr(&half_full[h])) : "memory");
@@ -1542,7 +1570,7 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
     if (lane == 0)
 #pragma unroll
         for (int t = 0; t < kTMax; ++t)
-            c.cand[warp * kTMax + t] = t < TT ? make_float2(best_v[t < TT ? t : 0], __int_as_float(best_i[t < TT ? t : 0]))
+            g_cand[warp * kTMax + t] = t < TT ? make_float2(best_v[t < TT ? t : 0], __int_as_float(best_i[t < TT ? t : 0]))
                                               : make_float2(-INFINITY, __int_as_float(0x7fffffff));
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     consumer_sync();
@@ -1551,7 +1579,7 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
         float bv = -INFINITY;
         int bi = 0x7fffffff;
         for (int w = 0; w < kConsumerWarps; ++w) {
-            const float2 cc = c.cand[w * kTMax + tid];
+            const float2 cc = g_cand[w * kTMax + tid];
             const int ci = __float_as_int(cc.y);
             if (cc.x > bv || (cc.x == bv && ci < bi)) { bv = cc.x; bi = ci; }
         }
@@ -1561,7 +1589,8 @@ __device__ __noinline__ bool phase_lm_tc(const KCtx& c, long long* cur, int pid)
 }
 
 // H (CTA 0): first max over the CTA partials, acceptance and rollback.
-__device__ __noinline__ void phase_accept(const KCtx& c) {
+__device__ __noinline__ void phase_accept() {
+    const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int row = warp; row < c.T; row += kConsumerWarps) {
@@ -1614,29 +1643,30 @@ __device__ __noinline__ void phase_accept(const KCtx& c) {
 
 // The consumer warps' phase sequence; kLow: the step has at most 8 rows.
 template <int kNK, bool kLow>
-__device__ __noinline__ void run_phases(const KCtx& c) {
+__device__ __noinline__ void run_phases() {
+    const KCtx& c = g_ctx;
     unsigned target = 0;
     long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
-    phase_embed(c);
-    if (!end_phase(c, &target)) return;
+    phase_embed();
+    if (!end_phase(&target)) return;
     for (int l = 0; l < c.a.d.n_layers; ++l) {
-        if (!phase_qkv<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_attn(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!phase_combine(c, l)) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), false)) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_gu<kNK, kLow>(c, l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
-        if (!phase_proj_resid<kLow>(c, l, cur, phase_index(target), true)) consumer_fail(c.a);
-        if (!end_phase(c, &target)) return;
+        if (!phase_qkv<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(&target)) return;
+        if (!phase_attn(l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!phase_combine(l)) consumer_fail(c.a);
+        if (!end_phase(&target)) return;
+        if (!phase_proj_resid<kLow>(l, cur, phase_index(target), false)) consumer_fail(c.a);
+        if (!end_phase(&target)) return;
+        if (!phase_gu<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(&target)) return;
+        if (!phase_proj_resid<kLow>(l, cur, phase_index(target), true)) consumer_fail(c.a);
+        if (!end_phase(&target)) return;
     }
-    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(c, cur, phase_index(target))
-                     : !phase_lm<kNK, kLow>(c, cur, phase_index(target)))
+    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, phase_index(target))
+                     : !phase_lm<kNK, kLow>(cur, phase_index(target)))
         consumer_fail(c.a);
-    if (!end_phase(c, &target)) return;
-    if (blockIdx.x == 0) phase_accept(c);
+    if (!end_phase(&target)) return;
+    if (blockIdx.x == 0) phase_accept();
 }
 
 // Tensor maps of the streams' KV caches (a kernel parameter: TMA reads them
@@ -1648,18 +1678,9 @@ struct KvMaps {
 template <int kNK>
 __global__ void __launch_bounds__(kMegaThreads, 1)
     k_verify_persistent(MegaArgs args, const __grid_constant__ KvMaps kv_maps) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ KCtx s_ctx;
-    __shared__ double s_wsum[kConsumerWarps * kTMax];
-    __shared__ float s_scale[kTMax * 4];
-    __shared__ float2 s_cand[kConsumerWarps * kTMax];
-    __shared__ int s_flag;
-    __shared__ __align__(8) uint64_t s_lm_bars[4];
-    __shared__ uint32_t s_tmem;
-    __shared__ float s_qk_norm[2 * kHeadDim];
     const int warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
-        KCtx& c = s_ctx;
+        KCtx& c = g_ctx;
         c.a = args;
         // The streams' rows: every active stream (T > 0) keeps its seed row;
         // the rows left over go to the proposals in stream order, so that
@@ -1691,44 +1712,32 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
         c.attn_wpi = max_nq <= 4 && args.st_kv[0].type == KV_F16 ? 2 : max_nq > 16 ? 8 : 4;
         c.sch.init(args.d, gridDim.x, blockIdx.x, args.st_kv[0].type == KV_F16, c.s_chunks, args.n_streams,
                    args.lm_tiles != nullptr);
-        c.ring = smem;
-        c.region = smem + (size_t)kRingSlots * kSlotBytes;
-        c.rope = reinterpret_cast<float*>(c.region + kRegionBytes);
-        c.full = reinterpret_cast<uint64_t*>(c.rope + kTMax * 64 * 2);
-        c.empty = c.full + kRingSlots;
-        c.wsum = s_wsum;
-        c.scale = s_scale;
-        c.cand = s_cand;
-        c.flag = &s_flag;
-        c.lm_bars = s_lm_bars;
-        c.tmem = &s_tmem;
-        c.qk_norm = s_qk_norm;
         if (args.timeline && blockIdx.x == 0) {
             args.timeline[kTimelineStart] = global_ns();
             // SM cycles beside the timer (CTA 0, last barrier slot): the clock the step ran at.
             args.timeline[kCtaMarkBase + (size_t)(kMaxBarriers - 1) * kCtaMarks] = clock64();
         }
         for (int s = 0; s < kRingSlots; ++s) {
-            mbar_init(&c.full[s], 1);
-            mbar_init(&c.empty[s], 1);
+            mbar_init(&s_full()[s], 1);
+            mbar_init(&s_empty()[s], 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    const KCtx& c = s_ctx;
+    const KCtx& c = g_ctx;
     if (c.T <= 0) return;
-    if (smem_addr(smem) & 1023) {  // the K/V boxes need a 1024-aligned ring
+    if (smem_addr(g_smem) & 1023) {  // the K/V boxes need a 1024-aligned ring
         if (threadIdx.x == 0 && blockIdx.x == 0) args.st_state[0]->error = 3;
         return;
     }
     if (warp == kConsumerWarps) {
-        producer(c.a, kv_maps.m, c.sch, c.ring, c.full, c.empty);
+        producer(c.a, kv_maps.m, c.sch, s_ring(), s_full(), s_empty());
         return;
     }
     if (c.T <= 8)
-        run_phases<kNK, true>(c);
+        run_phases<kNK, true>();
     else
-        run_phases<kNK, false>(c);
+        run_phases<kNK, false>();
 }
 
 
