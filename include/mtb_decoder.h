@@ -52,8 +52,9 @@ enum { MTB_KV_F32 = 0, MTB_KV_F16 = 1 };
 enum { MTB_STOP_NONE = 0, MTB_STOP_EOS = 1, MTB_STOP_LIMIT = 2, MTB_STOP_ERROR = 3 };
 
 /* Draft policy.  The reference policy is k_max 4, n-gram sizes 16..2
- * (src/cpu_speculative.cpp:29,104); penalty is MTD_REPETITION_PENALTY clamped
- * to [1, 1.5] (:85-86). */
+ * (src/cpu_speculative.cpp:29,104); penalty clamped to [1, 1.5] (:85-86).  A
+ * NULL params pointer selects that policy with the penalty read from
+ * MTD_REPETITION_PENALTY, as the reference does. */
 typedef struct mtb_spec_params {
     int32_t k_max;   /* proposals per step, 0..15 */
     int32_t n_min;   /* smallest n-gram size, >= 1 */
@@ -74,6 +75,22 @@ typedef int (*mtb_draft_fn)(void* user, const int32_t* ids, int n_ids, int budge
 typedef void (*mtb_commit_fn)(void* user, const int32_t* ids, int n_ids, int past_len, int stopped);
 
 int mtb_abi_version(void);
+/* Whether moss_transcribe_capi_transcribe_pcm / _path can return a
+ * transcript from this build: 0 (the audio front end is not part of it; those
+ * calls return NULL with an error).  No counterpart in the reference. */
+int mtb_capi_can_transcribe(void);
+/* The generate entries (mtb_spec_generate, mtb_spec_generate_ids,
+ * mtb_greedy_generate) end by printing the reference's lines
+ * (src/cpu_speculative.cpp:138-145) to stderr as "[mt I] <line>":
+ * BENCH_GENERATION, CPU_PROFILE, CPU_SPECULATIVE and, with
+ * MTD_TRACE_TOKENS=1 in the environment, BENCH_TOKEN_TRACE in chunks of 128
+ * ids.  level 0 silences them, 1 (the default) prints them. */
+void mtb_set_log_level(int level);
+/* The same lines as text (no prefix, '\n' after each) for given results;
+ * needs no GPU.  Returns the full length; out gets at most out_size - 1 bytes
+ * and a terminating 0. */
+int mtb_format_generation_log(const int32_t* ids, int n_ids, int eos, const mtb_counters* counters, int k_max,
+                              double prefill_seconds, double decoder_seconds, int trace, char* out, int out_size);
 /* Returns the error of the last failed call on this thread that had no object. */
 const char* mtb_global_error(void);
 

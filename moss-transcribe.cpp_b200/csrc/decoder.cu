@@ -15,6 +15,7 @@
 #include "prefill_tc.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
@@ -502,6 +503,64 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
     return 0;
 }
 
+int g_log_level = 1;  // 0: silent, 1: the reference's INFO lines (the default)
+
+// The reference's end-of-generation lines (src/cpu_speculative.cpp:138-145),
+// without the "[mt I] " prefix its logger adds.  Embedding, logits, draft and
+// rewind run inside the device step here, so their own times read 0; the
+// decoder time is the whole step loop.
+std::string generation_log(const int32_t* ids, int n, int eos, const mtb_counters& c, int k_max, double prefill_s,
+                           double decoder_s, bool trace) {
+    const char* stop = c.stop_reason == STOP_EOS ? "eos" : c.stop_reason == STOP_LIMIT ? "token_limit" : "error";
+    char buf[512];
+    std::string out;
+    std::snprintf(buf, sizeof(buf), "BENCH_GENERATION tokens=%d stop=%s\n", n, stop);
+    out += buf;
+    std::snprintf(buf, sizeof(buf), "CPU_PROFILE prefill=%.6f embedding=%.6f decoder=%.6f logits=%.6f\n", prefill_s, 0.0,
+                  decoder_s, 0.0);
+    out += buf;
+    std::snprintf(buf, sizeof(buf),
+                  "CPU_SPECULATIVE targetCalls=%lld draftedCalls=%lld proposed=%lld accepted=%lld targetInputTokens=%lld "
+                  "rewinds=%lld draftSeconds=%.9f rewindSeconds=%.9f maximumDraft=%d\n",
+                  (long long)c.target_calls, (long long)c.drafted_calls, (long long)c.proposed, (long long)c.accepted,
+                  (long long)c.target_input_tokens, (long long)c.rewinds, 0.0, 0.0, k_max);
+    out += buf;
+    if (trace) {
+        for (int off = 0; off < n; off += 128) {
+            std::snprintf(buf, sizeof(buf), "BENCH_TOKEN_TRACE eos=%d total=%d offset=%d ids=[", eos, n, off);
+            out += buf;
+            for (int i = off; i < std::min(n, off + 128); ++i) {
+                if (i != off) out += ',';
+                out += std::to_string(ids[i]);
+            }
+            out += "]\n";
+        }
+    }
+    return out;
+}
+
+bool trace_tokens() {
+    const char* t = std::getenv("MTD_TRACE_TOKENS");
+    return t && !std::strcmp(t, "1");
+}
+
+void emit_generation_log(const int32_t* ids, int n, int eos, const mtb_counters& c, int k_max, double prefill_s,
+                         double decoder_s) {
+    if (g_log_level <= 0) return;
+    const std::string lines = generation_log(ids, n, eos, c, k_max, prefill_s, decoder_s, trace_tokens());
+    size_t a = 0;
+    while (a < lines.size()) {
+        const size_t b = lines.find('\n', a);
+        std::fprintf(stderr, "[mt I] %s\n", lines.substr(a, b - a).c_str());
+        a = b + 1;
+    }
+    std::fflush(stderr);
+}
+
+double wall_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
 void fill_counters(const StepState& s, mtb_counters* c) {
     if (!c) return;
     c->target_calls = s.target_calls;
@@ -514,6 +573,14 @@ void fill_counters(const StepState& s, mtb_counters* c) {
     c->past_len = s.past;
 }
 
+// Without explicit parameters the reference policy applies: k 4, n-grams
+// 16..2, and the repetition penalty from MTD_REPETITION_PENALTY (unset: 1),
+// as src/cpu_speculative.cpp:85-86 and :104 read them.
+float env_penalty() {
+    const char* e = std::getenv("MTD_REPETITION_PENALTY");
+    return e ? float(std::atof(e)) : 1.f;
+}
+
 int set_params(mtb_decoder* d, int max_new, int eos, const mtb_spec_params* p) {
     StepState& s = *d->h_state;
     if (max_new <= 0 || max_new > d->max_new) return fail(d->error, "max_new must be in [1, " + std::to_string(d->max_new) + "]");
@@ -521,7 +588,8 @@ int set_params(mtb_decoder* d, int max_new, int eos, const mtb_spec_params* p) {
     if (k < 0 || k > kTMax - 1) return fail(d->error, "k_max must be in [0, 15]");
     const int nmin = p ? p->n_min : 2, nmax = p ? p->n_max : 16;
     if (nmin < 1 || nmax < nmin) return fail(d->error, "need 1 <= n_min <= n_max");
-    float pen = p ? p->penalty : 1.f;
+    float pen = p ? p->penalty : env_penalty();
+    if (!(pen == pen)) pen = 1.f;              // NaN (an unparsable variable reads as 0, clamped below)
     pen = std::max(1.f, std::min(1.5f, pen));  // src/cpu_speculative.cpp:86
     s.max_new = max_new;
     s.eos = eos;
@@ -602,6 +670,22 @@ int fuse_on_device(mtb_decoder* d, const int32_t* ids, int seq, const float* aud
 extern "C" {
 
 int mtb_abi_version(void) { return kAbiVersion; }
+
+void mtb_set_log_level(int level) { g_log_level = level; }
+
+int mtb_format_generation_log(const int32_t* ids, int n_ids, int eos, const mtb_counters* counters, int k_max,
+                              double prefill_seconds, double decoder_seconds, int trace, char* out, int out_size) {
+    if (!counters || n_ids < 0 || (n_ids > 0 && !ids)) return -1;
+    const std::string s = generation_log(ids, n_ids, eos, *counters, k_max, prefill_seconds, decoder_seconds, trace != 0);
+    if (out && out_size > 0) {
+        const size_t m = std::min(s.size(), size_t(out_size - 1));
+        std::memcpy(out, s.data(), m);
+        out[m] = 0;
+    }
+    return int(s.size());
+}
+
+int mtb_capi_can_transcribe(void) { return 0; }
 const char* mtb_global_error(void) { return g_error.c_str(); }
 
 int mtb_model_load(const char* path, int device, mtb_model** out) {
@@ -887,7 +971,9 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
         cudaSetDevice(d->device);
         if (refresh(d)) return -1;
         if (set_params(d, max_new, eos, params)) return -1;
+        const double t0 = wall_s();
         if (prefill(d, fused, seq)) return -1;
+        const double t1 = wall_s();
         StepState& s = *d->h_state;
         const int vocab = d->model->dm.dims.vocab;
         if (draft || commit) {
@@ -945,6 +1031,9 @@ int mtb_spec_generate(mtb_decoder* d, const float* fused, int seq, int max_new, 
         MTB_CK(d, cudaStreamSynchronize(d->stream));
         *n_out = s.n_ids;
         fill_counters(s, counters);
+        mtb_counters c{};
+        fill_counters(s, &c);
+        emit_generation_log(out_ids, s.n_ids, s.eos, c, s.k_max, t1 - t0, wall_s() - t1);
         return 0;
     } catch (const std::exception& e) {
         d->error = e.what();
@@ -980,8 +1069,10 @@ int mtb_spec_generate_ids(mtb_decoder* d, const int32_t* ids, int seq, const flo
         cudaSetDevice(d->device);
         if (refresh(d)) return -1;
         if (set_params(d, max_new, eos, params)) return -1;
+        const double t0 = wall_s();
         if (fuse_on_device(d, ids, seq, audio, n_audio, audio_token_id)) return -1;
         if (prefill(d, d->fused_dev, seq, true)) return -1;
+        const double t1 = wall_s();
         StepState& s = *d->h_state;
         int i = 0;
         for (;;) {  // device-driven loop, as in mtb_spec_generate without hooks
@@ -999,6 +1090,9 @@ int mtb_spec_generate_ids(mtb_decoder* d, const int32_t* ids, int seq, const flo
         MTB_CK(d, cudaStreamSynchronize(d->stream));
         *n_out = s.n_ids;
         fill_counters(s, counters);
+        mtb_counters c{};
+        fill_counters(s, &c);
+        emit_generation_log(out_ids, s.n_ids, s.eos, c, s.k_max, t1 - t0, wall_s() - t1);
         return 0;
     } catch (const std::exception& e) {
         d->error = e.what();

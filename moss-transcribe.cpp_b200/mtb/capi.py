@@ -91,6 +91,10 @@ SIGNATURES = {
     "mtb_transfer_bytes": (C.c_int, [_vp, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]),
     "mtb_step_timeline": (C.c_int, [_vp, C.POINTER(C.c_int64), C.c_int, _ip]),
     "mtb_step_capture": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _ip]),
+    "mtb_capi_can_transcribe": (C.c_int, []),
+    "mtb_set_log_level": (None, [C.c_int]),
+    "mtb_format_generation_log": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_double, C.c_double, C.c_int,
+                                            C.c_char_p, C.c_int]),
     "mtb_debug_poison_kv": (C.c_int, [_vp, C.c_int, C.c_int]),
     "mtb_ngram_draft": (C.c_int, [_vp, _i32p, C.c_int, C.c_int, C.c_int, C.c_int, _i32p, _ip]),
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
@@ -233,9 +237,12 @@ class Decoder:
         return out[:n.value].tolist()
 
     def cpu_speculative_generate(self, fused: np.ndarray, max_new: int, eos: int, k_max: int = 4, n_min: int = 2,
-                                 n_max: int = 16, penalty: float = 1.0, draft=None, committed=None):
+                                 n_max: int = 16, penalty: float = 1.0, draft=None, committed=None,
+                                 reference_policy: bool = False):
         """Strict speculative generate; `draft(ids, budget)` and
-        `committed(ids, past_len, stopped)` are the reference's hooks."""
+        `committed(ids, past_len, stopped)` are the reference's hooks.
+        reference_policy: pass no parameters (k 4, n 16..2, the penalty from
+        MTD_REPETITION_PENALTY), as the reference's own call does."""
         f = np.ascontiguousarray(fused, dtype=np.float32).reshape(-1, self.model.hidden)
         out = np.zeros(max_new, dtype=np.int32)
         n = C.c_int()
@@ -253,7 +260,8 @@ class Decoder:
 
         dfn = DRAFT_FN(_draft) if draft else DRAFT_FN()
         cfn = COMMIT_FN(_commit) if committed else COMMIT_FN()
-        self._check(lib().mtb_spec_generate(self.ptr, _f32(f), f.shape[0], int(max_new), int(eos), C.byref(params),
+        self._check(lib().mtb_spec_generate(self.ptr, _f32(f), f.shape[0], int(max_new), int(eos),
+                                            None if reference_policy else C.byref(params),
                                             _i32(out), C.byref(n), C.byref(counters), dfn, cfn, None),
                     "spec_generate")
         return out[:n.value].tolist(), counters.as_dict()
@@ -387,6 +395,20 @@ class Decoder:
         ms = C.c_float()
         self._check(lib().mtb_event_elapsed_ms(self.ptr, int(a), int(b), C.byref(ms)), "event_elapsed")
         return ms.value
+
+
+def format_generation_log(ids, eos: int, counters: dict, k_max: int, prefill_s: float = 0.0,
+                          decoder_s: float = 0.0, trace: bool = True) -> str:
+    """The reference's end-of-generation lines for given results (no GPU needed)."""
+    a = _arr_i32(ids)
+    c = Counters(*(int(counters[k]) for k in ("target_calls", "drafted_calls", "proposed", "accepted",
+                                                 "target_input_tokens", "rewinds", "stop_reason", "past_len")))
+    n = lib().mtb_format_generation_log(_i32(a) if a.size else None, a.size, int(eos), C.byref(c), int(k_max),
+                                        float(prefill_s), float(decoder_s), int(trace), None, 0)
+    buf = C.create_string_buffer(n + 1)
+    lib().mtb_format_generation_log(_i32(a) if a.size else None, a.size, int(eos), C.byref(c), int(k_max),
+                                    float(prefill_s), float(decoder_s), int(trace), buf, n + 1)
+    return buf.value.decode()
 
 
 def _group(decoders):

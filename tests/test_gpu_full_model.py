@@ -35,7 +35,11 @@ def test_persistent_verify_kernel_is_active(full_gpu):
     assert full_gpu.persistent_grid >= 132
 
 
-def test_config1_prefill_and_speculative_decode_bit_exact(full_oracle, full_gpu):
+@pytest.mark.parametrize("k_max,n_min,n_max", [(8, 3, 3), (4, 2, 16)], ids=["configs0_k8_n3", "reference_k4_n2_16"])
+def test_config1_prefill_and_speculative_decode_bit_exact(full_oracle, full_gpu, k_max, n_min, n_max):
+    """the 407-row prompt (375 audio + 32 text rows) and all 256
+    decoded tokens, with the configs' draft (k 8, n 3) and with the reference
+    policy (k 4, n 16..2, src/cpu_speculative.cpp:29,104)."""
     prompt = fixture.synthetic_prompt(full_oracle.arrays["token_embd.weight"], full_oracle.shape, n_audio=375,
                                       n_text=32)
     od = oracle.OracleDecoder(full_oracle, 1024)
@@ -44,8 +48,9 @@ def test_config1_prefill_and_speculative_decode_bit_exact(full_oracle, full_gpu)
     gh = gd.run(prompt)
     np.testing.assert_array_equal(gh, oh)
     np.testing.assert_array_equal(gd.logits_from_hidden(gh[-1]), od.logits(oh[-1]))
-    o_ids, o_c = od.spec_generate(prompt, 32, -1, k_max=8, n_min=3, n_max=3)
-    g_ids, g_c = gd.cpu_speculative_generate(prompt, 32, -1, k_max=8, n_min=3, n_max=3)
+    o_ids, o_c = od.spec_generate(prompt, 256, -1, k_max=k_max, n_min=n_min, n_max=n_max)
+    g_ids, g_c = gd.cpu_speculative_generate(prompt, 256, -1, k_max=k_max, n_min=n_min, n_max=n_max)
+    assert len(g_ids) == 256
     assert g_ids == o_ids
     for key in ("target_calls", "drafted_calls", "proposed", "accepted", "target_input_tokens", "rewinds"):
         assert g_c[key] == o_c[key], key
@@ -120,3 +125,19 @@ def test_config4_long_context_step_bit_exact(full_oracle, full_gpu):
     assert c["accepted"] == keep
     assert got == chain[:keep + 2]
     assert c["past_len"] == KV + keep + 1
+
+
+def test_reference_capi_loads_and_frees_the_full_model(full_path):
+    """moss_transcribe_capi_load on the Qwen3-0.6B GGUF (the reference's own
+    entry, include/moss_transcribe_capi.h); transcribe returns NULL with the
+    documented error in this build (no audio front end), as
+    mtb_capi_can_transcribe reports."""
+    import ctypes as C
+    L = capi.lib()
+    ctx = L.moss_transcribe_capi_load(full_path.encode())
+    assert ctx, L.mtb_global_error()
+    assert L.mtb_capi_can_transcribe() == 0
+    samples = (C.c_float * 16000)()
+    assert L.moss_transcribe_capi_transcribe_pcm(ctx, samples, 16000, 16000, 0) is None
+    assert b"audio front end" in L.moss_transcribe_capi_last_error(ctx)
+    L.moss_transcribe_capi_free(ctx)
