@@ -15,9 +15,15 @@ device before each step so every step sees the same 2048-position cache.
          (mtb_resume + mtb_spec_step + mtb_read_ids: host->device and
          device->host copies inside the timed region).
 
+Side lines: `recordings` (configs[4] at every N: 64 recordings of 1500 prompt
+rows + 768 decoded tokens, round robin over the ranks, each GPU stepping its
+share in groups of 8 through the public calls), and at N=1 `config0`
+(configs[0] end to end), `prefill`, `multi_stream`, `long_context`,
+`f16_recording`.
+
 `--impl reference` times the CPU restatement of the reference path (the
-oracle: the reference's own ggml build cannot be compiled here) on the same
-workload with all host cores.  Multi-GPU (torchrun): one independent decoder
+oracle, built for the host's own ISA with -march=native: the reference's own
+ggml build cannot be compiled here) on the same workload with all host cores.  Multi-GPU (torchrun): one independent decoder
 replica per GPU, no collective on the data path (weak scaling); rank 0 prints.
 """
 from __future__ import annotations
@@ -48,9 +54,6 @@ WEIGHT_BYTES = 633_233_408
 NORM_BYTES = 262_144
 KV_BYTES_PER_POS = 114_688
 EMBED_BYTES_PER_ROW = 1_088
-# DRAM bytes (read + write) of one k_verify_persistent launch at this workload,
-# from the ncu capture summarised in profiles/k_verify_persistent_kv2048_t8_full.md.
-TRAFFIC_BYTES = 884_756_480
 # configs[4] sample (multi-stream box throughput): recordings of 1500 audio rows
 # (the KV cache they leave, synthetic fp16), decoded with the device n-gram
 # draft at k = 8, on one GPU.
@@ -58,6 +61,8 @@ MS_STREAMS = 8
 MS_KV = 1500
 MS_STEPS = 48
 MS_NEW = 768  # configs[4]: decoded tokens per recording
+MS_RECORDINGS = 64  # configs[4]: recordings on the node, round robin over the GPUs
+CONFIG0_NEW = 256  # configs[0]: decoded tokens after the 407-row prompt
 # configs[3] context length: a 30-minute recording leaves ~27k cached positions.
 LC_KV = 27000
 LC_STEPS = 50
@@ -96,6 +101,8 @@ class ClockSampler:
         self.path = f"/tmp/mtb_clocks_{os.getpid()}.csv"
 
     def start(self):
+        """Start sampling and wait (up to 5 s) for the first sample, so the
+        timed region that follows is covered from its start."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}",
@@ -105,6 +112,15 @@ class ClockSampler:
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 5.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.02)
 
     def stop(self):
         if not self.proc:
@@ -163,6 +179,16 @@ def max_over_ranks(x: float, dist, torch, local: int) -> float:
     return float(t.item())
 
 
+def sum_over_ranks(x: float, dist, torch, local: int) -> float:
+    """The sum of x over all ranks."""
+    if not dist:
+        return x
+    dev = f"cuda:{local}" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def job_throughput(world: int, units_per_rank: float, seconds: float) -> float:
     """Whole-job rate: every rank processed units_per_rank in at most `seconds`."""
     return world * units_per_rank / seconds
@@ -184,6 +210,7 @@ def cpu_baseline(path: str, steps: int, sample_s: float = 20.0):
     """The CPU restatement (oracle) on the same workload, all host cores."""
     import oracle
     from mtb import fixture
+    oracle.use_native()  # -march=native on this host (AVX-512 / VNNI where present)
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     om = oracle.OracleModel(path)
@@ -207,7 +234,12 @@ def cpu_baseline(path: str, steps: int, sample_s: float = 20.0):
     t = statistics.median(times)
     return {"value": (keep + 1) / t, "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"{len(times)} verify steps of T={T_ROWS} at kv {KV_LEN} (fp16-rounded KV), "
-                      f"append + {keep + 1} lazy LM-head rows each, median {t * 1e3:.1f} ms"}
+                      f"append + {keep + 1} lazy LM-head rows each, median {t * 1e3:.1f} ms; "
+                      f"C restatement built -O3 -march=native ({oracle.host_isa()})",
+            "ms_per_step": round(t * 1e3, 2), "isa": oracle.host_isa(),
+            "reference_published_xeon_ms": {"prefix_512_T8": 34.292, "prefix_1024_T8": 40.435,
+                                            "source": "cpu-lab/causal-context.md:86,89 (16-core Xeon Gold 5416S, "
+                                                      "all 8 logit rows)"}}
 
 
 def main(argv=None):
@@ -314,7 +346,9 @@ def main(argv=None):
            "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
            "ms_per_step": e2e_s * 1e3 / n_e2e}
 
-    prefill = ms_line = lc_line = f16_line = None
+    prefill = ms_line = lc_line = f16_line = c0_line = rec_line = None
+    if not args.no_extras and model.persistent_grid > 0:
+        rec_line = recordings_line(model, capi, dist, torch, rank, local, world)
     if not args.no_extras and world == 1:  # per-GPU side measurements: the N=1 run carries them
         # ---- prefill: the prompt rows of configs[1] (375 audio + 32 text rows)
         # through the public run() call, host rows in and hidden rows out; every
@@ -340,6 +374,7 @@ def main(argv=None):
         pl_s = time.perf_counter() - t0
         pl_dec.close()
         ms_line = multi_stream(model, capi, fixture) if model.persistent_grid > 0 else None
+        c0_line = config0(model, capi, fixture)
         lc_line = long_context(model, capi, seed_tok)
         f16_line = f16_recording(capi, fixture, local)
         prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
@@ -356,13 +391,15 @@ def main(argv=None):
     roofline = {"bound": "hbm", "kernel": kernel, "achieved": round(achieved, 1),
                 "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "algorithmic_bytes": bytes_step,
-                "traffic": TRAFFIC_BYTES if model.persistent_grid > 0 else None}
+                # DRAM bytes come from an ncu capture only (profiles/); no number is carried over here.
+                "traffic": None}
     line = {"metric": metric, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": ("f16 x f16 -> f32" if args.f16 else "q8_0 x q8_0 -> f32") + " (fp16 KV)",
             "data": "synthetic", "config": config,
             "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk,
-            "prefill": prefill, "multi_stream": ms_line, "long_context": lc_line, "f16_recording": f16_line}
+            "prefill": prefill, "recordings": rec_line, "config0": c0_line, "multi_stream": ms_line,
+            "long_context": lc_line, "f16_recording": f16_line}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(path, 5)
     if rank == 0:
@@ -372,6 +409,65 @@ def main(argv=None):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def recordings_line(model, capi, dist, torch, rank: int, local: int, world: int) -> dict:
+    """configs[4] at N GPUs: 64 recordings (1500 synthetic N(0, 1) prompt rows +
+    768 decoded tokens each, device n-gram draft k = 8), recording i on rank
+    i mod N, each rank decoding its share in groups of 8 (one persistent launch
+    per group step) through the public calls (mtb_spec_prime,
+    mtb_spec_run_group, mtb_read_ids): host rows in, ids out.  The job's time
+    is its slowest rank's (wall clock around the rank's share, after a barrier);
+    tokens are summed over the ranks."""
+    from mtb import recordings
+    mine = recordings.partition(MS_RECORDINGS, world, rank)
+    recs = [recordings.Recording(np.random.default_rng(700 + i).standard_normal((MS_KV, model.hidden))
+                                 .astype(np.float32), MS_NEW) for i in mine]
+    recordings.decode_recordings(model, recs[:1] if recs else [], k_max=8)  # warm-up (graphs, first prefill)
+    if dist:
+        torch.cuda.synchronize()
+        dist.barrier()
+    t0 = time.perf_counter()
+    outs = recordings.decode_recordings(model, recs, k_max=8)
+    dt = time.perf_counter() - t0
+    toks = sum(len(ids) for ids, _ in outs)
+    acc = sum(c["accepted"] for _, c in outs)
+    worst = max_over_ranks(dt, dist, torch, local)
+    total = sum_over_ranks(float(toks), dist, torch, local)
+    return {"workload": f"configs[4]: {MS_RECORDINGS} recordings x ({MS_KV} prompt rows prefilled + {MS_NEW} tokens, "
+                        f"device n-gram draft k=8), round robin over {world} GPU(s), groups of 8 per launch",
+            "tokens_per_s": round(total / worst, 1), "tokens_per_s_per_gpu": round(total / worst / world, 1),
+            "recordings_per_gpu": len(mine), "tokens": int(total), "s": round(worst, 3), "accepted_rank0": acc,
+            "scaling": "weak per recording, strong per job: the 64 recordings are fixed, split over the GPUs",
+            "timing": "wall clock around each rank's share (prefill + decode, ids read back), max over ranks"}
+
+
+def config0(model, capi, fixture) -> dict:
+    """configs[0] end to end: the 407-row prompt (375 N(0, 1) audio rows between
+    two halves of 32 LCG text ids' embedding rows) prefilled and 256 tokens
+    decoded, with the configs' draft (n = 3, k = 8) and with the reference
+    policy (k = 4, n-grams 16..2), through mtb_spec_generate: host rows in,
+    ids out."""
+    import oracle  # only for the embedding rows of the text ids (the fused prompt's input)
+    om = oracle.OracleModel(fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0))
+    prompt = fixture.synthetic_prompt(om.arrays["token_embd.weight"], om.shape, n_audio=375, n_text=32)
+    del om
+    dec = capi.Decoder(model, prompt.shape[0] + CONFIG0_NEW + 64, capi.KV_F32, max_new=CONFIG0_NEW)
+    capi.lib().mtb_set_log_level(0)
+    out = {}
+    try:
+        for name, (k, n0, n1) in {"k8_n3": (8, 3, 3), "reference_k4_n2_16": (4, 2, 16)}.items():
+            dec.cpu_speculative_generate(prompt, 16, -1, k_max=k, n_min=n0, n_max=n1)  # warm-up
+            t0 = time.perf_counter()
+            ids, c = dec.cpu_speculative_generate(prompt, CONFIG0_NEW, -1, k_max=k, n_min=n0, n_max=n1)
+            dt = time.perf_counter() - t0
+            out[name] = {"tokens_per_s": round(len(ids) / dt, 1), "s": round(dt, 4), "tokens": len(ids),
+                         "target_calls": c["target_calls"], "accepted": c["accepted"]}
+    finally:
+        capi.lib().mtb_set_log_level(1)
+        dec.close()
+    return {"workload": "configs[0]: 407 prompt rows (375 audio + 32 text) prefilled + 256 tokens, F32 KV",
+            **out, "timing": "host wall clock around mtb_spec_generate (prefill + decode), ids read back"}
 
 
 def long_context(model, capi, seed_tok) -> dict:
@@ -446,30 +542,6 @@ def multi_stream(model, capi, fixture) -> dict:
         d.close()
     assert g_ids == s_ids, "group decode differs from single-stream decode"
 
-    # configs[4] end to end on one GPU: each recording's 1500 prompt rows
-    # (synthetic N(0, 1), host rows in) prefilled, then 768 tokens decoded with
-    # the device draft (k = 8), all recordings stepped as one group.  One
-    # recording alone, the same way, for comparison.
-    prompts = [np.random.default_rng(500 + i).standard_normal((MS_KV, model.hidden)).astype(np.float32)
-               for i in range(MS_STREAMS)]
-    es = [capi.Decoder(model, MS_KV + MS_NEW + 64, capi.KV_F16, max_new=MS_NEW) for _ in range(MS_STREAMS)]
-
-    def e2e(group):
-        t0 = time.perf_counter()
-        for d, pr in zip(group, prompts):
-            d.spec_prime(pr, MS_NEW, -1, k_max=8, n_min=3, n_max=3)
-        steps = capi.spec_run_group(group)
-        dt = time.perf_counter() - t0
-        outs = [d.read_ids() for d in group]
-        return dt, steps, sum(len(ids) for ids, _ in outs), sum(c["accepted"] for _, c in outs)
-
-    e2e(es[:1])  # warm-up (graphs, first prefill)
-    one_dt, one_steps, one_toks, one_acc = e2e(es[:1])
-    one_ids = es[0].read_ids()[0]
-    all_dt, all_steps, all_toks, all_acc = e2e(es)
-    assert es[0].read_ids()[0] == one_ids, "a recording decoded in the group differs from it decoded alone"
-    for d in es:
-        d.close()
     return {"workload": f"configs[4] sample: {MS_STREAMS} recordings, KV {MS_KV} fp16 synthetic each, "
                         f"{MS_STEPS} verify steps each, device n-gram draft k=8",
             "single_stream": {"tokens_per_s": round(s_toks / s_dt, 1), "ms_per_launch": round(s_dt * 1e3 / (MS_STREAMS * MS_STEPS), 3),
@@ -477,14 +549,7 @@ def multi_stream(model, capi, fixture) -> dict:
             "grouped": {"tokens_per_s": round(g_toks / g_dt, 1), "ms_per_launch": round(g_dt * 1e3 / MS_STEPS, 3),
                         "tokens": g_toks, "rows": g_rows, "accepted": g_acc},
             "speedup": round((g_toks / g_dt) / (s_toks / s_dt), 3),
-            "timing": "host wall clock around mtb_spec_run_group, ids read back; same ids in both modes",
-            "end_to_end": {"workload": f"configs[4] on one GPU: {MS_STREAMS} recordings x ({MS_KV} prompt rows prefilled "
-                                       f"+ {MS_NEW} tokens decoded, device n-gram draft k=8), one group",
-                           "tokens_per_s": round(all_toks / all_dt, 1), "s": round(all_dt, 3), "steps": all_steps,
-                           "tokens": all_toks, "accepted": all_acc,
-                           "one_recording": {"tokens_per_s": round(one_toks / one_dt, 1), "s": round(one_dt, 3),
-                                             "steps": one_steps, "accepted": one_acc},
-                           "timing": "host wall clock: mtb_spec_prime (prefill) for each + mtb_spec_run_group"}}
+            "timing": "host wall clock around mtb_spec_run_group, ids read back; same ids in both modes"}
 
 
 def f16_recording(capi, fixture, device: int) -> dict:

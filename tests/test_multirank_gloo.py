@@ -38,6 +38,20 @@ def _worker(rank: int, world: int, port: int, mode: str, q):
             dist.barrier()
             dist.destroy_process_group()
             q.put((r, w, worst, rate, ""))
+        elif mode == "partition":  # configs[4]: each rank's round-robin share of the 64 recordings
+            r, local, w, dist, torch = bench.dist_setup()
+            sys.path.insert(0, os.path.join(ROOT, "moss-transcribe.cpp_b200"))
+            from mtb import recordings
+            mine = recordings.partition(bench.MS_RECORDINGS, w, r)
+            shares = [None] * w
+            dist.all_gather_object(shares, mine)
+            t_rank = 1.0 + r  # a rank's own seconds; the job's time is the slowest rank's
+            worst = bench.max_over_ranks(t_rank, dist, torch, local)
+            tokens = bench.MS_NEW * len(mine)
+            total = bench.sum_over_ranks(float(tokens), dist, torch, local)
+            dist.barrier()
+            dist.destroy_process_group()
+            q.put((r, w, worst, total, repr(shares)))
         else:  # the reference arm: rank 0 would time the CPU path, the others leave at once
             out = io.StringIO()
             if rank == 0:
@@ -85,3 +99,18 @@ def test_reference_arm_runs_on_rank_zero_only():
     for rank, world, _, _, out in res:
         assert world == 2, out
     assert res[1][4] == ""  # rank 1 printed nothing and did no work
+
+
+def test_recordings_partition_over_two_gloo_ranks():
+    """configs[4]'s 64 recordings round robin over the ranks: together the
+    shares cover every recording once; the job's tokens are summed over the
+    ranks and its time is the slowest rank's."""
+    import ast
+    res = _run("partition")
+    assert [r[0] for r in res] == [0, 1]
+    for rank, world, worst, total, shares in res:
+        assert world == 2 and worst == pytest.approx(2.0)
+        parts = ast.literal_eval(shares)
+        assert sorted(i for p in parts for i in p) == list(range(64))
+        assert parts[rank] == list(range(rank, 64, 2))
+        assert total == pytest.approx(64 * 768)
