@@ -448,10 +448,11 @@ def config0(model, capi, fixture) -> dict:
     decoded, with the configs' draft (n = 3, k = 8) and with the reference
     policy (k = 4, n-grams 16..2), through mtb_spec_generate: host rows in,
     ids out."""
-    import oracle  # only for the embedding rows of the text ids (the fused prompt's input)
-    om = oracle.OracleModel(fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0))
-    prompt = fixture.synthetic_prompt(om.arrays["token_embd.weight"], om.shape, n_audio=375, n_text=32)
-    del om
+    import gguf  # the text ids' embedding rows come from the GGUF's token_embd (the fused prompt's input)
+    reader = gguf.GGUFReader(fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0))
+    embd = next(np.ascontiguousarray(t.data) for t in reader.tensors if t.name == "token_embd.weight")
+    prompt = fixture.synthetic_prompt(embd, fixture.read_shape(reader), n_audio=375, n_text=32)
+    del reader, embd
     dec = capi.Decoder(model, prompt.shape[0] + CONFIG0_NEW + 64, capi.KV_F32, max_new=CONFIG0_NEW)
     capi.lib().mtb_set_log_level(0)
     out = {}
