@@ -198,15 +198,36 @@ void orc_quantize_ref_q8(const float* x, int64_t k, void* out_blocks) {
  * are then added in ascending order.  ggml's x86 path spreads each block over
  * eight lanes instead; the evaluation order here is the one this oracle and
  * the CUDA kernels share (a difference of float rounding order only). */
+/* Exact int32 sum of the 32 products of one block pair.  With AVX-512 VNNI
+ * (the -march=native build on such a host) it is one u8 x s8 dot of |w| and
+ * sign(w) * x, as ggml's x86 path forms it; integer sums are exact, so the
+ * result is the scalar loop's. */
+#if defined(__AVX512VNNI__) && defined(__AVX512VL__)
+#include <immintrin.h>
+static inline int block_isum(const int8_t* w, const int8_t* x) {
+    const __m256i wv = _mm256_loadu_si256((const __m256i*)w);
+    const __m256i xv = _mm256_loadu_si256((const __m256i*)x);
+    const __m256i p = _mm256_dpbusd_epi32(_mm256_setzero_si256(), _mm256_sign_epi8(wv, wv), _mm256_sign_epi8(xv, wv));
+    __m128i h = _mm_add_epi32(_mm256_castsi256_si128(p), _mm256_extracti128_si256(p, 1));
+    h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0x4e));
+    h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0xb1));
+    return _mm_cvtsi128_si32(h);
+}
+#else
+static inline int block_isum(const int8_t* w, const int8_t* x) {
+    int isum = 0;
+    for (int j = 0; j < 32; ++j) isum += w[j] * x[j];
+    return isum;
+}
+#endif
+
 static inline float dot_q8(const blk_q8* w, const blk_q8* x, int nb) {
     float total = 0.0f;
     for (int s0 = 0; s0 < nb; s0 += 8) {
         float acc = 0.0f;
         for (int b = s0; b < s0 + 8 && b < nb; ++b) {
             const float d = h2f(w[b].d) * h2f(x[b].d);
-            int isum = 0;
-            for (int j = 0; j < 32; ++j) isum += w[b].qs[j] * x[b].qs[j];
-            acc = fmaf((float)isum, d, acc);
+            acc = fmaf((float)block_isum(w[b].qs, x[b].qs), d, acc);
         }
         total = total + acc;
     }
@@ -505,25 +526,32 @@ static inline float silu(float x) { return x / (1.0f + orc_expf(-x)); }
  * in chunk order, o = sum w_c o_c / sum w_c l_c. */
 static void attn_row_chunked(const float* qh, const float* kbase, const float* vbase, size_t stride, int valid, int hd,
                              float scale, float* oh) {
+    /* The loops run position-inner / dim-inner so that the compiler can keep
+     * many independent chains in vector lanes; every chain is still the same
+     * sequence of fmaf operations as described above. */
+    enum { MAXD = 256 };
     const int n_chunks = (valid + 63) / 64;
     float* cm = (float*)malloc(sizeof(float) * (size_t)n_chunks);
     float* cl = (float*)malloc(sizeof(float) * (size_t)n_chunks);
     float* co = (float*)malloc(sizeof(float) * (size_t)n_chunks * hd);
+    float kt[MAXD][64];
+    if (hd > MAXD) abort();
     for (int c = 0; c < n_chunks; ++c) {
-        float sc[64], e[64];
+        const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
+        float sc[64], e[64], ae[64], ao[64];
+        for (int p = 0; p < n_pos; ++p) {
+            const float* kj = kbase + (size_t)(c * 64 + p) * stride;
+            for (int e2 = 0; e2 < hd; ++e2) kt[e2][p] = kj[e2];
+        }
+        for (int p = 0; p < 64; ++p) ae[p] = ao[p] = 0.0f;
+        for (int e2 = 0; e2 < hd; e2 += 2)
+            for (int p = 0; p < n_pos; ++p) {
+                ae[p] = fmaf(qh[e2], kt[e2][p], ae[p]);
+                ao[p] = fmaf(qh[e2 + 1], kt[e2 + 1][p], ao[p]);
+            }
         float mx = -INFINITY;
         for (int p = 0; p < 64; ++p) {
-            const int j = c * 64 + p;
-            sc[p] = -INFINITY;
-            if (j < valid) {
-                const float* kj = kbase + (size_t)j * stride;
-                float ae = 0.0f, ao = 0.0f;
-                for (int e2 = 0; e2 < hd; e2 += 2) {
-                    ae = fmaf(qh[e2], kj[e2], ae);
-                    ao = fmaf(qh[e2 + 1], kj[e2 + 1], ao);
-                }
-                sc[p] = (ae + ao) * scale;
-            }
+            sc[p] = p < n_pos ? (ae[p] + ao[p]) * scale : -INFINITY;
             mx = fmaxf(mx, sc[p]);
         }
         float pair[32];
@@ -531,24 +559,25 @@ static void attn_row_chunked(const float* qh, const float* kbase, const float* v
         for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
         cm[c] = mx;
         cl[c] = warp_tree_sum(pair);
-        const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
-        for (int e2 = 0; e2 < hd; ++e2) {
-            float acc = 0.0f;
-            for (int p = 0; p < n_pos; ++p) acc = fmaf(e[p], (vbase + (size_t)(c * 64 + p) * stride)[e2], acc);
-            co[(size_t)c * hd + e2] = acc;
+        float* oc = co + (size_t)c * hd;
+        for (int e2 = 0; e2 < hd; ++e2) oc[e2] = 0.0f;
+        for (int p = 0; p < n_pos; ++p) {
+            const float* vp = vbase + (size_t)(c * 64 + p) * stride;
+            const float ep = e[p];
+            for (int e2 = 0; e2 < hd; ++e2) oc[e2] = fmaf(ep, vp[e2], oc[e2]);
         }
     }
     float M = -INFINITY;
     for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, cm[c]);
-    for (int e2 = 0; e2 < hd; ++e2) {
-        float Ls = 0.0f, acc = 0.0f;
-        for (int c = 0; c < n_chunks; ++c) {
-            const float wgt = orc_expf(cm[c] - M);
-            Ls = fmaf(wgt, cl[c], Ls);
-            acc = fmaf(wgt, co[(size_t)c * hd + e2], acc);
-        }
-        oh[e2] = acc / Ls;
+    float Ls = 0.0f;
+    for (int e2 = 0; e2 < hd; ++e2) oh[e2] = 0.0f;
+    for (int c = 0; c < n_chunks; ++c) {
+        const float wgt = orc_expf(cm[c] - M);
+        Ls = fmaf(wgt, cl[c], Ls);
+        const float* oc = co + (size_t)c * hd;
+        for (int e2 = 0; e2 < hd; ++e2) oh[e2] = fmaf(wgt, oc[e2], oh[e2]);
     }
+    for (int e2 = 0; e2 < hd; ++e2) oh[e2] = oh[e2] / Ls;
     free(cm); free(cl); free(co);
 }
 
