@@ -330,13 +330,24 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
     float* src = qkv + (size_t)row * ld + (size_t)hh * kHeadDim;
     const float* w = is_q ? q_norm : k_norm;
     const int d = threadIdx.x;
-    __shared__ double s_part[4];
+    __shared__ float s_sq[kHeadDim];
+    __shared__ double s_tot;
     __shared__ float s_y[kHeadDim];
     const float xv = src[d];
-    double sq = warp_sum_d((double)(xv * xv));
-    if ((d & 31) == 0) s_part[d >> 5] = sq;
+    // Sum of squares, the per-head tree: lane i of warp 0 adds the squares of
+    // elements i, i + 32, i + 64, i + 96 in that order in double, then one xor
+    // butterfly over the 32 lanes.
+    s_sq[d] = xv * xv;
     __syncthreads();
-    const double tot = s_part[0] + s_part[1] + s_part[2] + s_part[3];
+    if (d < 32) {
+        double p = 0.0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) p += (double)s_sq[d + 32 * q];
+        p = warp_sum_d(p);
+        if (d == 0) s_tot = p;
+    }
+    __syncthreads();
+    const double tot = s_tot;
     const float mean = (float)(tot / kHeadDim);
     const float scale = 1.0f / sqrtf(mean + eps);
     s_y[d] = __fmul_rn(__fmul_rn(xv, scale), w[d]);

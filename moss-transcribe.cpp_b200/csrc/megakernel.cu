@@ -73,6 +73,7 @@ __shared__ int g_flag;
 __shared__ __align__(8) uint64_t g_lm_bars[4];  // tcgen05 LM head: half_full[2], half_free[2]
 __shared__ uint32_t g_tmem;                      // TMEM base address of the tcgen05 LM head
 __shared__ float g_qk_norm[2 * kHeadDim];        // the layer's q_norm and k_norm weights, staged by phase A for B
+__shared__ float g_q8s[kConsumerWarps * 64];     // per warp: 32 block scales d and 32 inverses (q8_scales_smem)
 
 __device__ __forceinline__ uint8_t* s_ring() { return g_smem; }
 __device__ __forceinline__ uint8_t* s_region() { return g_smem + (size_t)kRingSlots * kSlotBytes; }
@@ -335,6 +336,64 @@ __device__ __forceinline__ uint8_t* kv_chunk(uint8_t* ring, long long q0, int wh
 
 // ------------------------------------------------------------------ producer
 
+// The LM-head phase's copies.  Item j (one slot: 8 vocabulary rows x the
+// whole hidden K) sits in slot (q0 + j) mod kRingSlots and is consumed by
+// consumer warp j mod kConsumerWarps, so each warp alternates between two
+// slots.  Producer lane l < kConsumerWarps refills the slots of warp l: every
+// round each lane probes its next slot without blocking and issues the copy
+// as soon as that slot is free, so one slow warp holds back only its own
+// refills (in ring order, every refill would wait for the slowest warp).
+// Returns false on abort or when no lane made progress for kWaitNs; the
+// lanes then drain their own copies still in flight (bounded by the same
+// limit: a copy outstanding after it is left behind, the step having failed).
+__device__ bool producer_lm(const MegaArgs& a, const Schedule& sch, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                            long long q0, int cnt, int first) {
+    const int lane = threadIdx.x & 31;
+    const bool mine = lane < kConsumerWarps;
+    int j = lane;  // this lane's next item
+    bool ok = true;
+    unsigned long long last = global_ns();
+    for (unsigned round = 0;; ++round) {
+        int issued = 0;
+        if (mine && j < cnt) {
+            const long long q = q0 + j;
+            const int s = int(q % kRingSlots);
+            const long long use = q / kRingSlots;
+            if (use == 0 || mbar_try_wait(&empty[s], unsigned((use - 1) & 1))) {
+                const uint8_t* src = sch.item_src(a.layers, a.embd, W_LM, 0, first + j * sch.grid);
+                const unsigned nbytes = unsigned(sch.bytes[W_LM]);  // one item: at most one slot
+                mbar_expect_tx(&full[s], nbytes);
+                bulk_g2s(ring + (size_t)s * kSlotBytes, src, nbytes, &full[s]);
+                j += kConsumerWarps;
+                issued = 1;
+            }
+        }
+        const unsigned prog = __ballot_sync(0xffffffffu, issued);
+        if (!__any_sync(0xffffffffu, mine && j < cnt)) break;
+        if (prog) {
+            last = global_ns();
+        } else {
+            if ((round & 63) == 63) {
+                if (*reinterpret_cast<const volatile int*>(a.abort_flag) || global_ns() - last > kWaitNs) { ok = false; break; }
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!ok) {
+        if (lane == 0) atomicExch(a.abort_flag, 1);
+        if (mine)
+            for (int k = 1; k <= 2; ++k) {
+                const int jj = j - k * kConsumerWarps;
+                if (jj < 0) break;
+                const long long q = q0 + jj;
+                const unsigned long long t0 = global_ns();
+                while (!mbar_try_wait(&full[q % kRingSlots], unsigned((q / kRingSlots) & 1)) && global_ns() - t0 < kWaitNs) {
+                }
+            }
+    }
+    return ok;
+}
+
 // The producer warp: lane 0 waits for free slots, posts the expected bytes
 // and issues the copies: a weight item slot is one bulk copy, an attention
 // slot one TMA tile per 128-byte box of its rows (kv_maps[stream]: the
@@ -345,6 +404,7 @@ __device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Sc
     long long q = 0;  // ring slot sequence number
     const int n_phases = sch.L * kLayerPhases + 1;
     bool ok = true;
+    bool lm_lanes = false;  // the LM phase ran in producer_lm (which drains its own copies)
     long long items_before = 0;
     const int rps = sch.kv_f16 ? KvSlots<true>::kRowsPerSlot : KvSlots<false>::kRowsPerSlot;
     const int n_box = sch.kv_f16 ? KvSlots<true>::kBoxes : KvSlots<false>::kBoxes;
@@ -356,6 +416,13 @@ __device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Sc
         int first = 0;
         const int cnt = sch.count_of(sch.n[kind], rot, &first);
         const int slots = sch.slots_of(kind);
+        if (kind == W_LM && !sch.lm_tc && slots == 1) {
+            // The LM head is the last phase: its items (one slot each) are
+            // refilled per consumer warp rather than in ring order.
+            lm_lanes = true;
+            ok = producer_lm(a, sch, ring, full, empty, q, cnt, first);
+            break;
+        }
         long long lane_row = 0;  // attention: cache row of item (j & ~31) + lane's K block
         for (int j = 0; j < cnt && ok; ++j) {
             const int item = first + j * sch.grid;
@@ -397,9 +464,11 @@ __device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Sc
         }
         items_before += sch.n[kind];
     }
-    if (!ok && lane == 0) {
+    if (!ok && lane == 0 && !lm_lanes) {
         atomicExch(a.abort_flag, 1);
-        // Drain this CTA's copies still in flight before the CTA exits.
+        // Drain this CTA's copies still in flight before the CTA exits, each
+        // wait bounded by kWaitNs (best effort: a copy still outstanding after
+        // that is left behind; the step has already failed).
         for (long long r = q - 1; r >= 0 && r >= q - kRingSlots; --r) {
             const int s = int(r % kRingSlots);
             const unsigned long long t0 = global_ns();
@@ -483,6 +552,29 @@ __device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
     if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[q % kRingSlots]);
 }
 
+// q8_scales (the same divisions, so the same results) with the 32 results
+// passed back through the warp's 64 floats of g_q8s, read as broadcasts,
+// instead of 64 shuffles: lane i divides for block i.
+template <int N>
+__device__ __forceinline__ void q8_scales_smem(const float (&amax)[N], float (&d)[N], float (&inv)[N]) {
+    static_assert(N <= 32, "one block per lane");
+    const int lane = threadIdx.x & 31;
+    float* buf = g_q8s + (threadIdx.x >> 5) * 64;
+    float mine = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i)
+        if (lane == i) mine = amax[i];
+    buf[lane] = mine / 127.f;
+    buf[32 + lane] = mine != 0.0f ? 127.f / mine : 0.0f;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        d[i] = buf[i];
+        inv[i] = buf[32 + i];
+    }
+    __syncwarp();  // the next call writes buf again
+}
+
 // RMSNorm (the 256-thread tree of k_rmsnorm_quant) and q8_0 quantisation of
 // rows [T][K] of global x into shared fragments (rows >= T are left as they
 // are: every consumer discards the outputs of those rows).
@@ -559,7 +651,7 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
                 am[r * NK + k] = warp_absmax(v[r][k]);
             }
         }
-        q8_scales<NB>(am, dd, id);
+        q8_scales_smem<NB>(am, dd, id);
 #pragma unroll
         for (int r = 0; r < RG; ++r) {
 #pragma unroll
@@ -785,18 +877,23 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int s
     return true;
 }
 
-// Per-head RMSNorm (the 128-thread tree of k_qk_norm_rope_store) and NEOX
-// RoPE of one q or k head row by one warp.  Lane `lane` holds elements
-// lane + 32 q of the row (q = 0..3): quarter q's square sum is one butterfly,
-// the quarters are added in order, and the RoPE pairs (e, e + 64) are
+// Per-head RMSNorm and NEOX RoPE of one q or k head row by one warp.  Lane
+// `lane` holds elements lane + 32 q of the row (q = 0..3).  Sum of squares
+// (the per-head tree shared with k_qk_norm_rope_store and the CPU
+// restatement): each lane adds its four squares in q order in double, then
+// one xor butterfly over the lanes.  The RoPE pairs (e, e + 64) are
 // (lane, lane + 64) and (lane + 32, lane + 96); `rope` = the row's [64][cos, sin].
-__device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* __restrict__ wn, float eps,
-                                              const float* rope, float (&o)[4]) {
-    const int lane = threadIdx.x & 31;
-    double part[4];
+__device__ __forceinline__ double head_square_part(const float (&x)[4]) {
+    double p = 0.0;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) part[q] = warp_sum_d((double)(x[q] * x[q]));
-    const double tot = part[0] + part[1] + part[2] + part[3];
+    for (int q = 0; q < 4; ++q) p += (double)(x[q] * x[q]);
+    return p;
+}
+
+// The row's normalised, rotated elements from its butterfly total `tot`.
+__device__ __forceinline__ void norm_rope_apply(const float (&x)[4], double tot, const float* __restrict__ wn, float eps,
+                                                const float* rope, float (&o)[4]) {
+    const int lane = threadIdx.x & 31;
     const float mean = (float)(tot * (1.0 / kHeadDim));  // exact: 128 is a power of two
     const float scale = 1.0f / sqrtf(mean + eps);
     float y[4];
@@ -809,6 +906,11 @@ __device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* 
         o[q] = __fsub_rn(__fmul_rn(y[q], cs), __fmul_rn(y[q + 2], sn));
         o[q + 2] = __fadd_rn(__fmul_rn(y[q], sn), __fmul_rn(y[q + 2], cs));
     }
+}
+
+__device__ __forceinline__ void norm_rope_row(const float (&x)[4], const float* __restrict__ wn, float eps,
+                                              const float* rope, float (&o)[4]) {
+    norm_rope_apply(x, warp_sum_d(head_square_part(x)), wn, eps, rope, o);
 }
 
 // Attention of one (64-position chunk, kv head h) item (phase B) by `wpi`
@@ -1006,12 +1108,20 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, size_t scratch_off, in
 #pragma unroll
             for (int q = 0; q < 4; ++q) x[rr][q] = rr < R ? __ldcg(src + 32 * q + lane) : 0.f;
         }
+        // The rows' butterflies interleaved (independent chains).
+        double tot[RP];
+#pragma unroll
+        for (int rr = 0; rr < RP; ++rr) tot[rr] = head_square_part(x[rr]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int rr = 0; rr < RP; ++rr) tot[rr] += __shfl_xor_sync(0xffffffffu, tot[rr], o);
 #pragma unroll
         for (int rr = 0; rr < RP; ++rr) {
             if (rr < R) {
                 const int r = wl + wpi * rr, t = row0 + r / G;
                 float o[4];
-                norm_rope_row(x[rr], qk_norm, a.d.eps, rope + t * 64 * 2, o);
+                norm_rope_apply(x[rr], tot[rr], qk_norm, a.d.eps, rope + t * 64 * 2, o);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) sq[r * kHeadDim + 32 * q + lane] = o[q];
             }

@@ -490,8 +490,9 @@ int orc_decoder_fill_synthetic_kv(orc_decoder* d, int n_pos, uint32_t seed) {
 
 /* ggml rms_norm followed by ggml_mul with the weight (src/qwen3.cpp:27-30):
  * float squares summed in double, mean as float, 1/sqrtf(mean + eps), then
- * (x * scale) * w.  `threads` fixes the summation tree (256 for hidden rows,
- * 128 for per-head q/k norms). */
+ * (x * scale) * w.  `threads` fixes the summation tree (256 for hidden rows;
+ * 32 for per-head q/k norms: each of 32 partials adds elements i, i + 32,
+ * i + 64, i + 96 in order, then one butterfly). */
 static void rms_norm_mul(const float* x, const float* w, int n, float eps, float* y, int threads) {
     const double sum = sum_squares_tree(x, n, threads);
     const float mean = (float)(sum / n);
@@ -608,12 +609,12 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 float* qh = q + (size_t)t * qd + (size_t)h * hd;
-                rms_norm_mul(qh, L->q_norm, hd, m->eps, qh, 128);
+                rms_norm_mul(qh, L->q_norm, hd, m->eps, qh, 32);
                 rope_neox(qh, hd, past + t, m->theta);
             }
             for (int h = 0; h < nkv; ++h) {
                 float* kh = k + (size_t)t * kd + (size_t)h * hd;
-                rms_norm_mul(kh, L->k_norm, hd, m->eps, kh, 128);
+                rms_norm_mul(kh, L->k_norm, hd, m->eps, kh, 32);
                 rope_neox(kh, hd, past + t, m->theta);
             }
             /* KV store at past+t (src/qwen3.cpp:123-140). */
