@@ -779,7 +779,9 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         auto& A = d->allocs;
         auto& E = d->error;
         uint8_t* zero_region = nullptr;
-        d->mb.zero_bytes = 16 + size_t(dm.n_layers) * kMaxStreams * dm.n_kv * 4;
+        const size_t head_bytes = size_t(dm.n_layers) * kMaxStreams * dm.n_kv * 4;
+        const size_t pair_bytes = size_t(dm.n_layers) * (dm.n_heads / 2) * 4;
+        d->mb.zero_bytes = 16 + head_bytes + pair_bytes + size_t(dm.n_layers) * (F / 256) * 4;
         if (dalloc(A, E, &d->mb.act2_q, size_t(F / 32) * 512) || dalloc(A, E, &d->mb.act2_d, size_t(F / 32) * 16 * 4) ||
             dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
@@ -789,6 +791,8 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         d->mb.bar = reinterpret_cast<unsigned*>(zero_region);
         d->mb.abort_flag = reinterpret_cast<int*>(zero_region + 4);
         d->mb.head_done = reinterpret_cast<unsigned*>(zero_region + 16);
+        d->mb.pair_done = reinterpret_cast<unsigned*>(zero_region + 16 + head_bytes);
+        d->mb.slice_done = reinterpret_cast<unsigned*>(zero_region + 16 + head_bytes + pair_bytes);
         // Failure-path test hook (documented in tests/test_gpu_wait_timeout.py): a
         // barrier CTA 0 never arrives at, and a shorter wait bound.
         if (const char* sb = std::getenv("MTB_TEST_STALL_BARRIER")) d->mb.stall_barrier = std::atoi(sb);

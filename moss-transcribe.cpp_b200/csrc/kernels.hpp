@@ -37,6 +37,8 @@ struct MegaBuffers {
     unsigned* bar;       // zeroed before every launch, together with abort_flag and head_done
     int* abort_flag;
     unsigned* head_done; // [n_layers][kMaxStreams][n_kv] finished attention items per kv head
+    unsigned* pair_done; // [n_layers][n_heads / 2] merged context blocks per pair of q heads
+    unsigned* slice_done; // [n_layers][ffn / 256] finished gate/up blocks per 256-feature slice
     size_t zero_bytes;
     unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
     // Optional, MTB_STEP_CAPTURE=1 (test read-back of the persistent step's own

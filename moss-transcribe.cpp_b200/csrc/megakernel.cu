@@ -59,6 +59,10 @@ constexpr int kTimelineStart = 2 * kMaxBarriers;       // kernel start / end slo
 constexpr int kArrivalBase = 6 * kMaxBarriers + 2;     // [cta][barrier] arrivals after the marks
 constexpr int kCtaMarkBase = kArrivalBase + 256 * kMaxBarriers;  // [cta][barrier][16] sub-phase marks
 constexpr int kCtaMarks = 16;
+// Timeline indices of the sub-phase marks of D (O) and F (down) of layer l,
+// which have no grid barrier of their own: past every barrier index.
+constexpr int kSubPhaseO = 320;
+constexpr int kSubPhaseDown = 384;
 
 // Shared memory, named at file scope so that every function's accesses
 // compile to shared-window loads and stores (a pointer kept in memory, or a
@@ -110,6 +114,8 @@ struct MegaArgs {
     float2* lm_val;  // [grid][16]
     unsigned* bar;   // grid barrier counter, zero at launch
     unsigned* head_done;  // [n_layers][kMaxStreams][n_kv] finished attention items per kv head, zero at launch
+    unsigned* pair_done;  // [n_layers][n_heads / 2] merged (row, q head, block) tasks per pair of q heads, zero at launch
+    unsigned* slice_done; // [n_layers][ffn / 256] finished gate/up blocks per 256-feature slice, zero at launch
     int* abort_flag;
     unsigned long long wait_ns;  // bound on a grid-barrier wait
     int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
@@ -547,11 +553,6 @@ __device__ __forceinline__ bool slots_wait(uint64_t* full, long long q0, int n, 
     return __all_sync(0xffffffffu, ok) != 0;
 }
 
-__device__ __forceinline__ void slot_release(uint64_t* empty, long long q) {
-    __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[q % kRingSlots]);
-}
-
 // q8_scales (the same divisions, so the same results) with the 32 results
 // passed back through the warp's 64 floats of g_q8s, read as broadcasts,
 // instead of 64 shuffles: lane i divides for block i.
@@ -674,27 +675,21 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
     mark(timeline, pid, 6);
 }
 
-// Copy fragments [K/32][512] + scales [K/32][16] from global into shared
-// memory, every load of a thread issued before the first store.
-__device__ void load_act_smem(const uint8_t* gq, const float* gd, int K, uint8_t* act_q, float* act_d) {
-    const int nb = K / 32;
-    const uint4* src = reinterpret_cast<const uint4*>(gq);
-    uint4* dst = reinterpret_cast<uint4*>(act_q);
-    const int n16 = nb * 32, nd = nb * 16 / 4;  // uint4 of fragments, float4 of scales
-    constexpr int U = 8;
-    for (int base = threadIdx.x; base < n16; base += kConsumers * U) {
-        uint4 r[U];
+// Slice sl (blocks 8 sl .. 8 sl + 7) of the activation fragments [K/32][512]
+// and scales [K/32][16] from global into the same places in shared memory,
+// by one warp (8 x 16 bytes of fragments and 16 bytes of scales per lane).
+__device__ __forceinline__ void load_act_slice(const uint8_t* gq, const float* gd, int sl, uint8_t* act_q, float* act_d) {
+    const int lane = threadIdx.x & 31;
+    const uint4* src = reinterpret_cast<const uint4*>(gq + (size_t)sl * 8 * 512);
+    uint4* dst = reinterpret_cast<uint4*>(act_q + (size_t)sl * 8 * 512);
+    uint4 r[8];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (base + u * kConsumers < n16) r[u] = __ldcg(src + base + u * kConsumers);
+    for (int u = 0; u < 8; ++u) r[u] = __ldcg(src + u * 32 + lane);
+    const float4 dv = __ldcg(reinterpret_cast<const float4*>(gd + (size_t)sl * 8 * 16) + lane);
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-            if (base + u * kConsumers < n16) dst[base + u * kConsumers] = r[u];
-    }
-    const float4* sd = reinterpret_cast<const float4*>(gd);
-    float4* dd = reinterpret_cast<float4*>(act_d);
-    for (int i = threadIdx.x; i < nd; i += kConsumers) dd[i] = __ldcg(sd + i);
-    consumer_sync();
+    for (int u = 0; u < 8; ++u) dst[u * 32 + lane] = r[u];
+    reinterpret_cast<float4*>(act_d + (size_t)sl * 8 * 16)[lane] = dv;
+    __syncwarp();
 }
 
 // One 256-K slice of one row group from shared memory: the slice partial of
@@ -702,14 +697,14 @@ __device__ void load_act_smem(const uint8_t* gq, const float* gd, int K, uint8_t
 // kLow: the step has at most 8 rows, so the outputs of rows 8..15 (the .z/.w
 // components) are not formed.
 template <bool kLow>
-__device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint4* s_act, const float* s_d, int kt0) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+__device__ __forceinline__ float4 slice_partial_regs(const uint4 (&wvs)[4], const uint2 (&svs)[4], const uint4* s_act,
+                                                     const float* s_d, int kt0) {
+    const int lane = threadIdx.x & 31, g = lane >> 2;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-        const uint8_t* tile = slice + u * kTileBytes;
-        const uint4 wv = *reinterpret_cast<const uint4*>(tile + lane * 16);
-        const uint2 sv = *reinterpret_cast<const uint2*>(tile + 512 + t * 8);
+        const uint4 wv = wvs[u];
+        const uint2 sv = svs[u];
         const int kt = kt0 + u;
         int c0[4], c1[4];
         mma_s8(c0, s_act[(2 * kt) * 32 + lane], wv.x, wv.y);
@@ -734,6 +729,47 @@ __device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint
     return make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
+// The same from shared memory (the slice's 4 tiles in a ring slot).
+template <bool kLow>
+__device__ __forceinline__ float4 slice_partial(const uint8_t* slice, const uint4* s_act, const float* s_d, int kt0) {
+    const int lane = threadIdx.x & 31, t = lane & 3;
+    uint4 wv[4];
+    uint2 sv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        wv[u] = *reinterpret_cast<const uint4*>(slice + u * kTileBytes + lane * 16);
+        sv[u] = *reinterpret_cast<const uint2*>(slice + u * kTileBytes + 512 + t * 8);
+    }
+    return slice_partial_regs<kLow>(wv, sv, s_act, s_d, kt0);
+}
+
+// One LM-head item (a row group's KT tiles, all in one ring slot): the lane's
+// tile fragments are read into registers first and the slot is released
+// before the arithmetic, so the producer refills it while this warp computes.
+// Slices are added in order (0 + slice 0 + slice 1 + ...), as in item_rows.
+template <int KT, bool kLow>
+__device__ __forceinline__ float4 item_staged(const uint8_t* slot, uint64_t* empty_bar, const uint4* s_act, const float* s_d) {
+    const int lane = threadIdx.x & 31, t = lane & 3;
+    uint4 wv[KT];
+    uint2 sv[KT];
+#pragma unroll
+    for (int u = 0; u < KT; ++u) {
+        wv[u] = *reinterpret_cast<const uint4*>(slot + u * kTileBytes + lane * 16);
+        sv[u] = *reinterpret_cast<const uint2*>(slot + u * kTileBytes + 512 + t * 8);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty_bar);
+    float4 y = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s4 = 0; s4 < KT / 4; ++s4) {
+        const uint4 w4[4] = {wv[4 * s4], wv[4 * s4 + 1], wv[4 * s4 + 2], wv[4 * s4 + 3]};
+        const uint2 v4[4] = {sv[4 * s4], sv[4 * s4 + 1], sv[4 * s4 + 2], sv[4 * s4 + 3]};
+        const float4 p = slice_partial_regs<kLow>(w4, v4, s_act, s_d, 4 * s4);
+        y.x = y.x + p.x; y.y = y.y + p.y; y.z = y.z + p.z; y.w = y.w + p.w;
+    }
+    return y;
+}
+
 // Outputs of row group `rg_local` (0 or 1 for a gate/up pair) of the item whose
 // slots start at sequence number q0: 0 + slice 0 + slice 1 + ... in order.
 // Waits for and releases the item's ring slots (all of them when `release`).
@@ -754,19 +790,21 @@ __device__ __forceinline__ bool item_rows(const uint8_t* ring, uint64_t* full, u
     return true;
 }
 
-__device__ __forceinline__ void release_item(uint64_t* empty, long long q0, int slots) {
-    for (int k = 0; k < slots; ++k) slot_release(empty, q0 + k);
-}
-
 // A weight phase of this CTA split into (item, row group, 256-K slice) units
 // over the 8 consumer warps; each unit's partial goes to shared memory, then
 // `epi(j, part)` runs once per item (item j's units start at part + j*U*32,
 // row group r's slice s at (r*S + s)*32) and adds the slices in order.  The
 // phase's ring slots are all released after the units (at most 8 per CTA).
-template <bool kLow, typename Epi>
+// `pre(sl)` runs in the unit's warp before slice sl is used (it may wait for
+// that slice's activations and bring them into shared memory); false aborts.
+struct NoPrologue {
+    __device__ bool operator()(int) const { return true; }
+};
+
+template <bool kLow, typename Epi, typename Pre = NoPrologue>
 __device__ __forceinline__ bool weight_phase(const PhaseInfo& pi, int rgs, int kt_n, const uint8_t* ring,
                                              uint64_t* full, uint64_t* empty, const uint4* s_act, const float* s_d,
-                                             float4* s_part, const int* abort_flag, Epi epi) {
+                                             float4* s_part, const int* abort_flag, Epi epi, Pre pre = Pre()) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = kt_n / 4, U = rgs * S;
     const int n_units = pi.count * U;
@@ -775,6 +813,7 @@ __device__ __forceinline__ bool weight_phase(const PhaseInfo& pi, int rgs, int k
         const int j = u / U, r = (u % U) / S, sl = u % S;
         const int off = (r * kt_n + sl * 4) * kTileBytes;
         const long long q = pi.slot0 + (long long)j * pi.slots + off / kSlotBytes;
+        if (!pre(sl)) { ok = false; break; }
         if (!slot_wait(full, q, abort_flag)) { ok = false; break; }
         s_part[u * 32 + lane] = slice_partial<kLow>(ring + (size_t)(q % kRingSlots) * kSlotBytes + off % kSlotBytes, s_act, s_d, sl * 4);
     }
@@ -801,35 +840,40 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
 // sequential fmaf chain), then that q8_0 block of the context row.  All of a
 // batch's loads (32 chunks) are issued together, the next batch's while the
 // current one is summed.
+// Wait (lane 0 polls with acquire loads, the warp follows) until the counter
+// reaches `target`: its producers release-add after their results are stored,
+// so the results are visible to the warp afterwards.  Bounded like a grid
+// barrier; false on abort or timeout.
+__device__ __forceinline__ bool wait_count(const MegaArgs& a, const unsigned* cnt, unsigned target) {
+    int give_up = 0;
+    if ((threadIdx.x & 31) == 0) {
+        const unsigned long long t0 = global_ns();
+        for (unsigned it = 0;; ++it) {
+            unsigned v;
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+            if (v >= target) break;
+            if ((it & 15) == 15) {
+                if (*reinterpret_cast<const volatile int*>(a.abort_flag)) { give_up = 1; break; }
+                if (global_ns() - t0 > a.wait_ns) {
+                    atomicExch(a.abort_flag, 1);
+                    report_timeout(a);
+                    give_up = 1;
+                    break;
+                }
+            }
+        }
+    }
+    give_up = __shfl_sync(0xffffffffu, give_up, 0);
+    __syncwarp();
+    return give_up == 0;
+}
+
 __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int si, int qh, int k, int n_chunks) {
     const int lane = threadIdx.x & 31;
     const int G = a.d.n_heads / a.d.n_kv, h = qh / G, qi = t * G + qh % G;
     // The head's chunk items are counted as they finish (release-add after
-    // their partials); lane 0 waits for all of them (acquire), bounded like a
-    // barrier, and the warp follows it.
-    {
-        int give_up = 0;
-        if (lane == 0) {
-            const unsigned* done = a.head_done + ((size_t)l * kMaxStreams + si) * a.d.n_kv + h;
-            const unsigned long long t0 = global_ns();
-            for (unsigned it = 0;; ++it) {
-                unsigned v;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done) : "memory");
-                if (v >= (unsigned)n_chunks) break;
-                if ((it & 15) == 15) {
-                    if (*reinterpret_cast<const volatile int*>(a.abort_flag)) { give_up = 1; break; }
-                    if (global_ns() - t0 > a.wait_ns) {
-                        atomicExch(a.abort_flag, 1);
-                        report_timeout(a);
-                        give_up = 1;
-                        break;
-                    }
-                }
-            }
-        }
-        if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
-        __syncwarp();
-    }
+    // their partials).
+    if (!wait_count(a, a.head_done + ((size_t)l * kMaxStreams + si) * a.d.n_kv + h, (unsigned)n_chunks)) return false;
     const size_t base = (size_t)h * a.max_chunks * (kTMax * 4) + qi;  // (h, chunk 0, qi)
     const float* po = a.part_o + base * kHeadDim + 32 * k + lane;
     constexpr size_t kStrideO = (size_t)kTMax * 4 * kHeadDim;         // one chunk further
@@ -874,6 +918,13 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int s
     const int blk = qh * 4 + k;
     a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o, iq[0]));
     if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[0]));
+    // The block is stored (every lane's byte, lane 0's scale): count it for
+    // the O projection's 256-K slice of this pair of q heads.
+    __syncwarp();
+    if (lane == 0) {
+        unsigned* cnt = a.pair_done + (size_t)l * (a.d.n_heads / 2) + qh / 2;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+    }
     return true;
 }
 
@@ -1366,6 +1417,12 @@ __device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bo
     const MegaArgs& a = c.a;
     const int K = down ? a.d.ffn : a.d.n_heads * kHeadDim, H = a.d.hidden, T = c.T;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    // No grid barrier before this phase: each unit waits for its own 256-K
+    // slice of the input (O: the merged context of one pair of q heads, 8 T
+    // merge tasks; down: the SwiGLU of 8 gate/up blocks) and brings that slice
+    // into shared memory.  This CTA's earlier phases used the region: all its
+    // warps are done with them first.
+    consumer_sync();
     const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
     float xr[4] = {0.f, 0.f, 0.f, 0.f};
     if (warp < pi.count) {
@@ -1378,9 +1435,17 @@ __device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bo
     }
     uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    load_act_smem(down ? a.act2_q : a.act_q, down ? a.act2_d : a.act_d, K, act_q, act_d);
+    const uint8_t* gq = down ? a.act2_q : a.act_q;
+    const float* gd = down ? a.act2_d : a.act_d;
+    const unsigned* counts = down ? a.slice_done + (size_t)l * (a.d.ffn / 256) : a.pair_done + (size_t)l * (a.d.n_heads / 2);
+    const unsigned need = down ? 8u : 8u * (unsigned)T;
     mark(a.timeline, pid, 0);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
+    auto pre = [&](int sl) {
+        if (!wait_count(a, counts + sl, need)) return false;
+        load_act_slice(gq, gd, sl, act_q, act_d);
+        return true;
+    };
     return weight_phase<kLow>(pi, 1, K / kTileK, s_ring(), s_full(), s_empty(), reinterpret_cast<const uint4*>(act_q), act_d,
                         s_part, a.abort_flag, [&](int j, const float4* part) {
                             const int item = pi.first + j * gridDim.x;
@@ -1394,7 +1459,7 @@ __device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bo
                                     *o = (j == warp ? xr[k] : __ldcg(o)) + yy[k];
                                 }
                             }
-                        });
+                        }, pre);
 }
 
 // E: RMSNorm + quantise; gate/up for one 32-feature block per item (four
@@ -1411,9 +1476,13 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
     const int T = c.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
+    const PhaseInfo pi = c.sch.take(W_GU, &cur[0], &cur[1]);
+    // A CTA without gate/up blocks skips the RMSNorm: it must not read x here,
+    // since the down projection (no grid barrier before it) may be updating x
+    // by then; the CTAs with blocks have read x before any down item ends.
+    if (pi.count == 0) return true;
     norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T);
     mark(a.timeline, pid, 0);
-    const PhaseInfo pi = c.sch.take(W_GU, &cur[0], &cur[1]);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     float* s_gu = reinterpret_cast<float*>(s_part + (size_t)pi.count * 8 * S * 32);  // [16 rows][32 features]
     const bool ok = weight_phase<kLow>(pi, 8, K / kTileK, s_ring(), s_full(), s_empty(), reinterpret_cast<const uint4*>(act_q),
@@ -1443,6 +1512,11 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
             if (lane == 0) a.act2_d[blk * 16 + row] = __half2float(__float2half_rn(dq[0]));
         }
         consumer_sync();
+        // The block's rows are stored (ordered by the barrier): count it for its 256-feature slice.
+        if (threadIdx.x == 0) {
+            unsigned* cnt = a.slice_done + (size_t)l * (a.d.ffn / 256) + blk / 8;
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
+        }
     }
     return ok;
 }
@@ -1467,14 +1541,15 @@ __device__ __noinline__ bool phase_lm(long long* cur, int pid) {
         const int item = pi.first + j * gridDim.x;
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int jw = j / kConsumerWarps;  // this warp's item count so far
-        if (warp == 0 && jw < 7 && slot_wait(s_full(), q0, a.abort_flag)) mark(a.timeline, pid, 1 + 2 * jw);
-        float4 y;
-        if (!item_rows<kLow>(s_ring(), s_full(), s_empty(), q0, K / kTileK, 0, reinterpret_cast<const uint4*>(act_q), act_d,
-                       a.abort_flag, &y)) {
+        if (!slot_wait(s_full(), q0, a.abort_flag)) {
             ok = false;
             break;
         }
-        release_item(s_empty(), q0, pi.slots);
+        if (warp == 0 && jw < 7) mark(a.timeline, pid, 1 + 2 * jw);
+        static_assert((K / kTileK) * kTileBytes <= kSlotBytes, "an LM-head item fits one ring slot");
+        const float4 y = item_staged<K / kTileK, kLow>(s_ring() + (size_t)(q0 % kRingSlots) * kSlotBytes,
+                                                       &s_empty()[q0 % kRingSlots], reinterpret_cast<const uint4*>(act_q),
+                                                       act_d);
         if (warp == 0 && jw < 7) mark(a.timeline, pid, 2 + 2 * jw);
         const float yy[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
@@ -1762,14 +1837,13 @@ __device__ __noinline__ void run_phases() {
     for (int l = 0; l < c.a.d.n_layers; ++l) {
         if (!phase_qkv<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
         if (!end_phase(&target)) return;
+        // B, C and D share one barrier interval (D waits per slice on C), as do E and F.
         if (!phase_attn(l, cur, phase_index(target))) consumer_fail(c.a);
         if (!phase_combine(l)) consumer_fail(c.a);
-        if (!end_phase(&target)) return;
-        if (!phase_proj_resid<kLow>(l, cur, phase_index(target), false)) consumer_fail(c.a);
+        if (!phase_proj_resid<kLow>(l, cur, kSubPhaseO + l, false)) consumer_fail(c.a);
         if (!end_phase(&target)) return;
         if (!phase_gu<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(&target)) return;
-        if (!phase_proj_resid<kLow>(l, cur, phase_index(target), true)) consumer_fail(c.a);
+        if (!phase_proj_resid<kLow>(l, cur, kSubPhaseDown + l, true)) consumer_fail(c.a);
         if (!end_phase(&target)) return;
     }
     if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, phase_index(target))
@@ -1886,7 +1960,8 @@ bool megakernel_supports(const ModelDims& d, int grid) {
     const bool hidden_ok = d.hidden == 256 || d.hidden == 512 || d.hidden == 1024;
     // Query rows are tiled in pairs (T * group must be even for every T).
     if (!hidden_ok || (d.n_heads / d.n_kv) % 2 != 0 || d.n_heads / d.n_kv * kTMax > 32) return false;
-    if (d.ffn % 32 || (d.ffn / kTileRows) % 4) return false;
+    if (d.ffn % 256 || (d.ffn / kTileRows) % 4) return false;  // down slices of 256 features = 8 gate/up blocks
+    if (d.n_heads % 2) return false;                                // O slices of 256 = one pair of q heads
     const int qd = d.n_heads * kHeadDim;
     // Per weight phase: fragments + scales of its K plus 512 bytes per slice
     // unit of the CTA's items must fit the shared region.
@@ -1971,6 +2046,8 @@ cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeight
     a.bar = mb.bar;
     a.abort_flag = mb.abort_flag;
     a.head_done = mb.head_done;
+    a.pair_done = mb.pair_done;
+    a.slice_done = mb.slice_done;
     a.wait_ns = mb.wait_ns;
     a.stall_barrier = mb.stall_barrier;
     cudaError_t e = cudaMemsetAsync(mb.bar, 0, mb.zero_bytes, s);  // barrier counter, abort flag, head counts
