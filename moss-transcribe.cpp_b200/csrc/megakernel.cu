@@ -255,8 +255,9 @@ struct Schedule {
     int grid, cta;
     int qd, kd, H, F, V, L, nkv;
     bool kv_f16;
-    // sizes per streamed phase kind
-    int n[6], bytes[6];
+    // sizes per streamed phase kind, and n's quotient and remainder by the
+    // grid (so a phase's item count and rotation need no division)
+    int n[6], bytes[6], nq[6], nr[6], nslots[6];
     bool lm_tc;  // LM head items are 128-row tcgen05 weight tiles (else 8-row mma.sync tiles)
     int n_str;
     int item0[kMaxStreams + 1];  // first attention item of each stream (items: stream, chunk, kv head)
@@ -288,8 +289,13 @@ struct Schedule {
         bytes[W_DOWN] = (F / kTileK) * kTileBytes;
         n[W_LM] = lm_tc ? V / 128 : V / kTileRows;
         bytes[W_LM] = lm_tc ? (H / 64) * kSlotBytes : (H / kTileK) * kTileBytes;
+        for (int k = 0; k < 6; ++k) {
+            nq[k] = n[k] / grid;
+            nr[k] = n[k] % grid;
+            nslots[k] = (bytes[k] + kSlotBytes - 1) / kSlotBytes;
+        }
     }
-    __device__ int slots_of(int kind) const { return (bytes[kind] + kSlotBytes - 1) / kSlotBytes; }
+    __device__ int slots_of(int kind) const { return nslots[kind]; }
     // Attention item -> (stream, chunk, kv head).
     __device__ void attn_item_of(int item, int* str, int* chunk, int* h) const {
         int si = 0;
@@ -298,22 +304,31 @@ struct Schedule {
         *chunk = (item - item0[si]) / nkv;
         *h = (item - item0[si]) % nkv;
     }
-    __device__ int count_of(int n_items, int rot, int* first) const {
-        const int f = ((cta - rot) % grid + grid) % grid;
+    // Items of phase `kind` for this CTA, with the phase rotated by `rot`
+    // (0 <= rot < grid): the items first, first + grid, ... below n[kind].
+    __device__ int count_of(int kind, int rot, int* first) const {
+        int f = cta - rot;
+        if (f < 0) f += grid;
         *first = f;
-        return f < n_items ? (n_items - 1 - f) / grid + 1 : 0;
+        return nq[kind] + (f < nr[kind] ? 1 : 0);
+    }
+    // The rotation of the phase after one of `kind` with rotation rot.
+    __device__ int next_rot(int kind, int rot) const {
+        int r = rot + nr[kind];
+        return r >= grid ? r - grid : r;
     }
     // Running position in the phase sequence: both the producer and the
-    // consumers advance it phase by phase, so neither recomputes the prefix.
-    __device__ PhaseInfo take(int kind, long long* items_before, long long* slot_next) const {
+    // consumers advance it phase by phase (cursor[0] = the next phase's
+    // rotation, cursor[1] = its first ring slot), so neither recomputes the prefix.
+    __device__ PhaseInfo take(int kind, long long* rot_cursor, long long* slot_next) const {
         PhaseInfo pi{};
         pi.n_items = n[kind];
-        pi.rot = int(*items_before % grid);
+        pi.rot = int(*rot_cursor);
         pi.bytes = bytes[kind];
-        pi.slots = slots_of(kind);
-        pi.count = count_of(pi.n_items, pi.rot, &pi.first);
+        pi.slots = nslots[kind];
+        pi.count = count_of(kind, pi.rot, &pi.first);
         pi.slot0 = *slot_next;
-        *items_before += n[kind];
+        *rot_cursor = next_rot(kind, pi.rot);
         *slot_next += (long long)pi.count * pi.slots;
         return pi;
     }
@@ -411,16 +426,15 @@ __device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Sc
     const int n_phases = sch.L * kLayerPhases + 1;
     bool ok = true;
     bool lm_lanes = false;  // the LM phase ran in producer_lm (which drains its own copies)
-    long long items_before = 0;
+    int rot = 0;  // rotation of the current phase (Schedule::take)
     const int rps = sch.kv_f16 ? KvSlots<true>::kRowsPerSlot : KvSlots<false>::kRowsPerSlot;
     const int n_box = sch.kv_f16 ? KvSlots<true>::kBoxes : KvSlots<false>::kBoxes;
     const int box_bytes = sch.kv_f16 ? KvSlots<true>::kBoxBytes : KvSlots<false>::kBoxBytes;
     for (int p = 0; p < n_phases && ok; ++p) {
         const int kind = p < sch.L * kLayerPhases ? p % kLayerPhases : W_LM;
         const int layer = p / kLayerPhases;
-        const int rot = int(items_before % sch.grid);
         int first = 0;
-        const int cnt = sch.count_of(sch.n[kind], rot, &first);
+        const int cnt = sch.count_of(kind, rot, &first);
         const int slots = sch.slots_of(kind);
         if (kind == W_LM && !sch.lm_tc && slots == 1) {
             // The LM head is the last phase: its items (one slot each) are
@@ -468,7 +482,7 @@ __device__ void producer(const MegaArgs& a, const CUtensorMap* kv_maps, const Sc
                 }
             }
         }
-        items_before += sch.n[kind];
+        rot = sch.next_rot(kind, rot);
     }
     if (!ok && lane == 0 && !lm_lanes) {
         atomicExch(a.abort_flag, 1);
@@ -493,10 +507,9 @@ __device__ __forceinline__ void report_timeout(const MegaArgs& a) {
     for (int s = 0; s < a.n_streams; ++s) a.st_state[s]->error = 2;
 }
 
-__device__ bool grid_barrier(const MegaArgs& a, unsigned target, int* s_flag) {
+__device__ bool grid_barrier(const MegaArgs& a, unsigned target, int b, int* s_flag) {
     consumer_sync();
     if (threadIdx.x == 0) {
-        const int b = int(target / gridDim.x) - 1;
         if (a.timeline && blockIdx.x == 0) a.timeline[2 * b] = global_ns();
         // Every CTA's arrival, for the skew between CTAs.
         if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
@@ -1255,13 +1268,12 @@ struct KCtx {
 
 __shared__ KCtx g_ctx;
 
-__device__ __forceinline__ int phase_index(unsigned target) { return int(target / gridDim.x); }
-
-// Grid barrier at the end of a phase; false when the step is being aborted.
-__device__ __noinline__ bool end_phase(unsigned* target) {
+// Grid barrier at the end of a phase (barrier *nb, whose arrivals complete at
+// *target); false when the step is being aborted.
+__device__ __noinline__ bool end_phase(unsigned* target, int* nb) {
     const KCtx& c = g_ctx;
     *target += gridDim.x;
-    return grid_barrier(c.a, *target, &g_flag);
+    return grid_barrier(c.a, *target, (*nb)++, &g_flag);
 }
 
 // RoPE angles of the step's positions (theta advanced by repeated float
@@ -1390,6 +1402,9 @@ __device__ __noinline__ bool phase_attn(int l, long long* cur, int pid) {
         }
         mark(a.timeline, mp, mk + 3);
     }
+    // Every group is done with its scratch in the region before phase D
+    // (after the merges, with no grid barrier between) loads into it.
+    consumer_sync();
     return ok;
 }
 
@@ -1420,9 +1435,10 @@ __device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bo
     // No grid barrier before this phase: each unit waits for its own 256-K
     // slice of the input (O: the merged context of one pair of q heads, 8 T
     // merge tasks; down: the SwiGLU of 8 gate/up blocks) and brings that slice
-    // into shared memory.  This CTA's earlier phases used the region: all its
-    // warps are done with them first.
-    consumer_sync();
+    // into shared memory.  This CTA's warps are past their own uses of the
+    // region by then: the attention phase ends with a CTA barrier (the merges
+    // use no shared memory), and the gate/up phase's last barrier follows its
+    // last shared-memory read.
     const PhaseInfo pi = c.sch.take(down ? W_DOWN : W_O, &cur[0], &cur[1]);
     float xr[4] = {0.f, 0.f, 0.f, 0.f};
     if (warp < pi.count) {
@@ -1831,25 +1847,26 @@ template <int kNK, bool kLow>
 __device__ __noinline__ void run_phases() {
     const KCtx& c = g_ctx;
     unsigned target = 0;
+    int nb = 0;                 // grid barriers passed (the timeline's phase index)
     long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
     phase_embed();
-    if (!end_phase(&target)) return;
+    if (!end_phase(&target, &nb)) return;
     for (int l = 0; l < c.a.d.n_layers; ++l) {
-        if (!phase_qkv<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
-        if (!end_phase(&target)) return;
+        if (!phase_qkv<kNK, kLow>(l, cur, nb)) consumer_fail(c.a);
+        if (!end_phase(&target, &nb)) return;
         // B, C and D share one barrier interval (D waits per slice on C), as do E and F.
-        if (!phase_attn(l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!phase_attn(l, cur, nb)) consumer_fail(c.a);
         if (!phase_combine(l)) consumer_fail(c.a);
         if (!phase_proj_resid<kLow>(l, cur, kSubPhaseO + l, false)) consumer_fail(c.a);
-        if (!end_phase(&target)) return;
-        if (!phase_gu<kNK, kLow>(l, cur, phase_index(target))) consumer_fail(c.a);
+        if (!end_phase(&target, &nb)) return;
+        if (!phase_gu<kNK, kLow>(l, cur, nb)) consumer_fail(c.a);
         if (!phase_proj_resid<kLow>(l, cur, kSubPhaseDown + l, true)) consumer_fail(c.a);
-        if (!end_phase(&target)) return;
+        if (!end_phase(&target, &nb)) return;
     }
-    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, phase_index(target))
-                     : !phase_lm<kNK, kLow>(cur, phase_index(target)))
+    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, nb)
+                     : !phase_lm<kNK, kLow>(cur, nb))
         consumer_fail(c.a);
-    if (!end_phase(&target)) return;
+    if (!end_phase(&target, &nb)) return;
     if (blockIdx.x == 0) phase_accept();
 }
 
