@@ -56,6 +56,49 @@ __device__ __forceinline__ double warp_sum_d(double v) {
     return v;
 }
 
+// The hidden-row RMSNorm sum of squares (the tree shared by every kernel and
+// the CPU restatement).  Element squares s_i = (double)(x_i * x_i) (the float
+// product, widened); each 32-element block summed pairwise over adjacent
+// pairs, ((s0 + s1) + (s2 + s3)) + ...; lane l's partial the blocks l, l + 32,
+// ... added in that order from 0; the lane partials combined by one xor
+// butterfly.
+__device__ __forceinline__ double block_sum_squares(const float (&v)[32]) {
+    double u[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) u[i] = (double)(v[2 * i] * v[2 * i]) + (double)(v[2 * i + 1] * v[2 * i + 1]);
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) u[i] = u[2 * i] + u[2 * i + 1];
+    return u[0];
+}
+
+// 1 / sqrt(mean(x^2) + eps) of a row of K (a multiple of 32, at most 32 x 64)
+// elements by a block of nthreads >= K / 32 threads (all of them call it):
+// thread b < K / 32 sums block b, warp 0 combines.  s_q holds K / 32 doubles.
+__device__ __forceinline__ float row_rms_scale(const float* row, int K, float eps, double* s_q, float* s_scale) {
+    const int nb = K / 32;
+    if ((int)threadIdx.x < nb) {
+        float v[32];
+        const float4* r4 = reinterpret_cast<const float4*>(row + 32 * threadIdx.x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = r4[i];
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+        s_q[threadIdx.x] = block_sum_squares(v);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        double p = 0.0;
+        for (int b = threadIdx.x; b < nb; b += 32) p += s_q[b];
+        p = warp_sum_d(p);
+        if (threadIdx.x == 0) *s_scale = 1.0f / sqrtf((float)(p / K) + eps);
+    }
+    __syncthreads();
+    return *s_scale;
+}
+
 // amax of |v| over the 32 lanes: non-negative floats order like their bit
 // patterns, so one integer max reduction gives exactly fmaxf's result.
 __device__ __forceinline__ float warp_absmax(float v) {

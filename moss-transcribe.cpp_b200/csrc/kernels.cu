@@ -256,8 +256,9 @@ void gemv(const GemvArgs& a, int grid, cudaStream_t s) {
 
 // ------------------------------------------------------------ norms, quant
 
-// RMSNorm (double sum of float squares, 1/sqrtf(mean+eps), (x*s)*w) of each
-// of the 16 rows, quantised to the fragment order; rows >= T become zero.
+// RMSNorm (double sum of float squares in the hidden-row tree of
+// row_rms_scale, 1/sqrtf(mean+eps), (x*s)*w) of each of the 16 rows,
+// quantised to the fragment order; rows >= T become zero.
 // Optionally stores the normed f32 rows (final norm -> hidden).
 __global__ void __launch_bounds__(kThreads) k_rmsnorm_quant(const StepState* st, const float* __restrict__ x, int K,
                                                             const float* __restrict__ w, float eps,
@@ -266,27 +267,11 @@ __global__ void __launch_bounds__(kThreads) k_rmsnorm_quant(const StepState* st,
     const int T = st->T;
     if (T <= 0) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ double s_part[kWarps];
+    __shared__ double s_q[kThreads];
     __shared__ float s_scale;
     const bool live = row < T;
-    if (live) {
-        double sum = 0.0;
-        for (int i = threadIdx.x; i < K; i += kThreads) {
-            const float v = x[(size_t)row * K + i];
-            sum += (double)(v * v);
-        }
-        sum = warp_sum_d(sum);
-        if (lane == 0) s_part[warp] = sum;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double tot = 0.0;
-            for (int i = 0; i < kWarps; ++i) tot += s_part[i];
-            const float mean = (float)(tot / K);
-            s_scale = 1.0f / sqrtf(mean + eps);
-        }
-        __syncthreads();
-    }
-    const float scale = live ? s_scale : 0.f;
+    // The hidden-row tree (row_rms_scale); the block is uniform in `live`.
+    const float scale = live ? row_rms_scale(x + (size_t)row * K, K, eps, s_q, &s_scale) : 0.f;
     for (int blk = warp; blk < K / 32; blk += kWarps) {
         const int i = blk * 32 + lane;
         float v = 0.f;
@@ -1230,7 +1215,7 @@ cudaError_t configure_kernels() {
 // order, the blocks of a 256-element slice added in ascending order, then the
 // slices in ascending order.
 
-// RMSNorm of rows < T (the tree of k_rmsnorm_quant) rounded to fp16 (rows >= T
+// RMSNorm of rows < T (the tree of row_rms_scale) rounded to fp16 (rows >= T
 // zero); `normed` (optional) gets the f32 rows.
 __global__ void __launch_bounds__(kThreads) k_rmsnorm_f16(const StepState* st, const float* __restrict__ x, int K,
                                                          const float* __restrict__ w, float eps, __half* act,
@@ -1238,28 +1223,11 @@ __global__ void __launch_bounds__(kThreads) k_rmsnorm_f16(const StepState* st, c
     const int row = blockIdx.x;
     const int T = st->T;
     if (T <= 0) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ double s_part[kWarps];
+    __shared__ double s_q[kThreads];
     __shared__ float s_scale;
     const bool live = row < T;
-    if (live) {
-        double sum = 0.0;
-        for (int i = threadIdx.x; i < K; i += kThreads) {
-            const float v = x[(size_t)row * K + i];
-            sum += (double)(v * v);
-        }
-        sum = warp_sum_d(sum);
-        if (lane == 0) s_part[warp] = sum;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            double tot = 0.0;
-            for (int i = 0; i < kWarps; ++i) tot += s_part[i];
-            const float mean = (float)(tot / K);
-            s_scale = 1.0f / sqrtf(mean + eps);
-        }
-        __syncthreads();
-    }
-    const float scale = live ? s_scale : 0.f;
+    // The hidden-row tree (row_rms_scale); the block is uniform in `live`.
+    const float scale = live ? row_rms_scale(x + (size_t)row * K, K, eps, s_q, &s_scale) : 0.f;
     for (int i = threadIdx.x; i < K; i += kThreads) {
         float v = 0.f;
         if (live) {

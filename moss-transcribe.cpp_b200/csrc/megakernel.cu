@@ -70,14 +70,11 @@ constexpr int kSubPhaseDown = 384;
 // Dynamic: the ring (kRingSlots slots), the region (activation fragments,
 // slice partials, attention scratch), the RoPE table, the ring's mbarriers.
 extern __shared__ __align__(1024) uint8_t g_smem[];
-__shared__ double g_wsum[kConsumerWarps * kTMax];
-__shared__ float g_scale[kTMax * 4];
 __shared__ float2 g_cand[kConsumerWarps * kTMax];
 __shared__ int g_flag;
 __shared__ __align__(8) uint64_t g_lm_bars[4];  // tcgen05 LM head: half_full[2], half_free[2]
 __shared__ uint32_t g_tmem;                      // TMEM base address of the tcgen05 LM head
 __shared__ float g_qk_norm[2 * kHeadDim];        // the layer's q_norm and k_norm weights, staged by phase A for B
-__shared__ float g_q8s[kConsumerWarps * 64];     // per warp: 32 block scales d and 32 inverses (q8_scales_smem)
 
 __device__ __forceinline__ uint8_t* s_ring() { return g_smem; }
 __device__ __forceinline__ uint8_t* s_region() { return g_smem + (size_t)kRingSlots * kSlotBytes; }
@@ -188,7 +185,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         : "memory");
 }
 
-__device__ __forceinline__ float ldcg(const float* p) { return __ldcg(p); }
 
 // Sub-phase mark k (0..3) of phase b in the optional timeline (CTA 0, thread 0).
 __device__ __forceinline__ void mark(unsigned long long* timeline, int b, int k) {
@@ -566,36 +562,14 @@ __device__ __forceinline__ bool slots_wait(uint64_t* full, long long q0, int n, 
     return __all_sync(0xffffffffu, ok) != 0;
 }
 
-// q8_scales (the same divisions, so the same results) with the 32 results
-// passed back through the warp's 64 floats of g_q8s, read as broadcasts,
-// instead of 64 shuffles: lane i divides for block i.
-template <int N>
-__device__ __forceinline__ void q8_scales_smem(const float (&amax)[N], float (&d)[N], float (&inv)[N]) {
-    static_assert(N <= 32, "one block per lane");
-    const int lane = threadIdx.x & 31;
-    float* buf = g_q8s + (threadIdx.x >> 5) * 64;
-    float mine = 0.f;
-#pragma unroll
-    for (int i = 0; i < N; ++i)
-        if (lane == i) mine = amax[i];
-    buf[lane] = mine / 127.f;
-    buf[32 + lane] = mine != 0.0f ? 127.f / mine : 0.0f;
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-        d[i] = buf[i];
-        inv[i] = buf[32 + i];
-    }
-    __syncwarp();  // the next call writes buf again
-}
-
-// RMSNorm (the 256-thread tree of k_rmsnorm_quant) and q8_0 quantisation of
+// RMSNorm (the hidden-row tree of row_rms_scale) and q8_0 quantisation of
 // rows [T][K] of global x into shared fragments (rows >= T are left as they
-// are: every consumer discards the outputs of those rows).
-// Thread 32w + lane owns elements 256k + 32w + lane, i.e. lane `lane` of the
-// blocks b = 8k + w: its partial sum runs over k in order (the same tree), the
-// loads are coalesced per warp and all in flight together, and each warp
-// quantises its own blocks from registers.  K = 256 * NK.
+// are: every consumer discards the outputs of those rows), one warp per row:
+// lane l owns block l of the row (elements 32 l .. 32 l + 31, K <= 1024), so
+// the block's square sum, amax and scale need no other lane; one butterfly
+// makes the row's total.  The 32 codes of a (row, block) are 8 words of the
+// fragment; lanes write them in an order rotated by the lane so that a
+// warp's stores spread over the banks.
 // kUmma: the output is the tcgen05 operand layout instead (16 rows x K bytes
 // as 64-K steps of 1024 bytes, core matrix (row group, 16-byte chunk) at
 // (4 group + chunk) * 128, row at +16 row; scales f32 [16][K / 32]).
@@ -604,88 +578,117 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
                                             unsigned long long* timeline = nullptr, int pid = 0,
                                             float* normed_out = nullptr) {
     constexpr int K = 256 * NK;
+    constexpr int NB = K / 32;  // blocks per row: one per lane at most
+    static_assert(NB <= 32, "one block per lane");
+    static_assert((size_t)K * 16 + NB * 64 + (size_t)(kConsumerWarps + 1) * NB * 36 * 4 <= (size_t)kRegionBytes,
+                  "fragments, scales and the staging buffers fit the region");
     // Fragments at the region's start, scales after them (K / 32 blocks x 512
     // bytes, or the tcgen05 layout's K / 64 steps x 1024 bytes: the same size).
     uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(s_region() + (size_t)K * 16);
-    double* s_wsum = g_wsum;
-    float* s_scale = g_scale;
-    constexpr int RG = 8;  // rows per pass (rows are independent; 8 x NK values per lane)
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float wv[NK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool has = lane < NB;
+    // Rows and the norm weights come in with coalesced 16-byte loads and are
+    // turned around through staging buffers after the fragments and scales in
+    // the region (blocks 36 floats apart: the 16-byte writes of 8 lanes and the
+    // block reads of 8 lanes each hit 32 distinct banks): one per warp for its
+    // rows, one shared for the weights.
+    float* stage_all = reinterpret_cast<float*>(s_region() + (size_t)K * 16 + (size_t)NB * 16 * 4);
+    float* stage = stage_all + warp * NB * 36;
+    float* wstage = stage_all + kConsumerWarps * NB * 36;
+    // This warp's first row is requested before the weights' round trip.
+    float4 f[NB / 4];
+    if (warp < T) {
+        const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)warp * K);
 #pragma unroll
-    for (int k = 0; k < NK; ++k) wv[k] = wn[256 * k + 32 * warp + lane];
-    for (int t0 = 0; t0 < kTMax; t0 += RG) {
-        if (t0 >= T) break;  // rows >= T are never read back: the kernels discard their outputs
-        float v[RG][NK];
+        for (int k = 0; k < NB / 4; ++k) f[k] = __ldcg(x4 + 32 * k + lane);
+    }
+    for (int e4 = threadIdx.x; e4 < K / 4; e4 += kConsumers)
+        *reinterpret_cast<float4*>(wstage + (e4 >> 3) * 36 + 4 * (e4 & 7)) = __ldg(reinterpret_cast<const float4*>(wn) + e4);
+    consumer_sync();
+    float wv[32];
+    if (has) {
 #pragma unroll
-        for (int r = 0; r < RG; ++r)
-#pragma unroll
-            for (int k = 0; k < NK; ++k)
-                v[r][k] = t0 + r < T ? ldcg(x + (size_t)(t0 + r) * K + 256 * k + 32 * warp + lane) : 0.f;
-        // Per-row partials, then the rows' butterflies interleaved (independent
-        // chains; each row's tree is the same xor butterfly).
-        double acc[RG];
-#pragma unroll
-        for (int r = 0; r < RG; ++r) {
-            acc[r] = 0.0;
-#pragma unroll
-            for (int k = 0; k < NK; ++k) acc[r] += (double)(v[r][k] * v[r][k]);
-        }
-        if (t0 == 0) mark(timeline, pid, 4);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int r = 0; r < RG; ++r) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], o);
-        if (lane == 0)
-#pragma unroll
-            for (int r = 0; r < RG; ++r)
-                if (t0 + r < T) s_wsum[warp * kTMax + t0 + r] = acc[r];
-        consumer_sync();
-        if (tid < RG && t0 + tid < T) {
-            double tot = 0.0;
-            for (int i = 0; i < kConsumerWarps; ++i) tot += s_wsum[i * kTMax + t0 + tid];
-            const float mean = (float)(tot * (1.0 / K));  // K a power of two: the same as tot / K
-            s_scale[t0 + tid] = 1.0f / sqrtf(mean + eps);
-        }
-        consumer_sync();
-        if (t0 == 0) mark(timeline, pid, 5);
-        // amax per (row, block) by one integer max reduction each; the scale
-        // divisions spread over the lanes (q8_scales).
-        constexpr int NB = RG * NK <= 32 ? RG * NK : 32;
-        static_assert(RG * NK <= 32, "one block per lane");
-        float am[NB], dd[NB], id[NB];
-#pragma unroll
-        for (int r = 0; r < RG; ++r) {
-            const float sc = t0 + r < T ? s_scale[t0 + r] : 0.f;
-#pragma unroll
-            for (int k = 0; k < NK; ++k) {
-                v[r][k] = t0 + r < T ? __fmul_rn(__fmul_rn(v[r][k], sc), wv[k]) : 0.f;
-                if (normed_out && t0 + r < T) normed_out[(size_t)(t0 + r) * K + 256 * k + 32 * warp + lane] = v[r][k];
-                am[r * NK + k] = warp_absmax(v[r][k]);
-            }
-        }
-        q8_scales_smem<NB>(am, dd, id);
-#pragma unroll
-        for (int r = 0; r < RG; ++r) {
-#pragma unroll
-            for (int k = 0; k < NK; ++k) {
-                const int blk = 8 * k + warp;
-                const uint8_t code = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[r][k], id[r * NK + k]));
-                const float dq = __half2float(__float2half_rn(dd[r * NK + k]));
-                if constexpr (kUmma) {
-                    const int row = t0 + r, e = 256 * k + 32 * warp + lane, kk = e % 64;
-                    act_q[(e / 64) * 1024 + ((row / 8) * 4 + kk / 16) * 128 + (row % 8) * 16 + kk % 16] = code;
-                    if (lane == 0) act_d[row * (K / 32) + blk] = dq;
-                } else {
-                    act_q[(size_t)blk * 512 + frag_offset(t0 + r, lane)] = code;
-                    if (lane == 0) act_d[blk * 16 + t0 + r] = dq;
-                }
-            }
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = *reinterpret_cast<const float4*>(wstage + lane * 36 + 4 * i);
+            wv[4 * i] = f.x; wv[4 * i + 1] = f.y; wv[4 * i + 2] = f.z; wv[4 * i + 3] = f.w;
         }
     }
+    for (int row = warp; row < T; row += kConsumerWarps) {
+        float v[32];
+        {
+            if (row != warp) {
+                const float4* x4 = reinterpret_cast<const float4*>(x + (size_t)row * K);
+#pragma unroll
+                for (int k = 0; k < NB / 4; ++k) f[k] = __ldcg(x4 + 32 * k + lane);
+            }
+#pragma unroll
+            for (int k = 0; k < NB / 4; ++k)
+                *reinterpret_cast<float4*>(stage + (4 * k + (lane >> 3)) * 36 + 4 * (lane & 7)) = f[k];
+            __syncwarp();
+            if (has) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float4 g = *reinterpret_cast<const float4*>(stage + lane * 36 + 4 * i);
+                    v[4 * i] = g.x; v[4 * i + 1] = g.y; v[4 * i + 2] = g.z; v[4 * i + 3] = g.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = 0.f;
+            }
+            __syncwarp();  // the buffer is reused by this warp's next row
+        }
+        if (row == warp) mark(timeline, pid, 4);
+        const double tot = warp_sum_d(has ? block_sum_squares(v) : 0.0);
+        const float scale = 1.0f / sqrtf((float)(tot / K) + eps);
+        if (row == warp) mark(timeline, pid, 5);
+        float am = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            v[i] = __fmul_rn(__fmul_rn(v[i], scale), wv[i]);
+            am = fmaxf(am, fabsf(v[i]));
+        }
+        if (has) {
+            if (normed_out) {
+                float4* o4 = reinterpret_cast<float4*>(normed_out + (size_t)row * K + 32 * lane);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
+            const float d = am / 127.f;
+            const float id = am != 0.0f ? 127.f / am : 0.0f;
+            uint32_t word[8];  // codes 4 w .. 4 w + 3 of the block
+#pragma unroll
+            for (int wd = 0; wd < 8; ++wd) {
+                uint32_t pk = 0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    pk |= (uint32_t)(uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[4 * wd + j], id)) << (8 * j);
+                word[wd] = pk;
+            }
+            const float dq = __half2float(__float2half_rn(d));
+#pragma unroll
+            for (int s8 = 0; s8 < 8; ++s8) {
+                const int wd = (s8 + lane) & 7;  // rotated: spreads the warp's stores over the banks
+                uint32_t val = word[0];
+#pragma unroll
+                for (int i = 1; i < 8; ++i)
+                    if (wd == i) val = word[i];
+                if constexpr (kUmma) {
+                    const int e = 32 * lane + 4 * wd, kk = e % 64;
+                    *reinterpret_cast<uint32_t*>(act_q + (e / 64) * 1024 + ((row / 8) * 4 + kk / 16) * 128 + (row % 8) * 16 +
+                                                 kk % 16) = val;
+                } else {
+                    *reinterpret_cast<uint32_t*>(act_q + (size_t)lane * 512 + frag_offset(row, 4 * wd)) = val;
+                }
+            }
+            if constexpr (kUmma)
+                act_d[row * NB + lane] = dq;
+            else
+                act_d[lane * 16 + row] = dq;
+        }
+        if (row == warp) mark(timeline, pid, 6);
+    }
     consumer_sync();
-    mark(timeline, pid, 6);
 }
 
 // Slice sl (blocks 8 sl .. 8 sl + 7) of the activation fragments [K/32][512]

@@ -284,7 +284,7 @@ __global__ void k_pf_repack(const uint8_t* src, int n_src, int K, int half, uint
     }
 }
 
-// RMSNorm (the 256-thread tree of k_rmsnorm_quant) and q8_0 quantisation of
+// RMSNorm (the hidden-row tree of row_rms_scale) and q8_0 quantisation of
 // T rows into activation steps + scales; one CTA per row.
 __global__ void __launch_bounds__(256) k_pf_norm_quant(const float* __restrict__ x, int T, int K,
                                                       const float* __restrict__ w, float eps, uint8_t* xq, float* xd,
@@ -292,23 +292,9 @@ __global__ void __launch_bounds__(256) k_pf_norm_quant(const float* __restrict__
     const int row = blockIdx.x;
     if (row >= T) return;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ double s_part[8];
+    __shared__ double s_q[256];
     __shared__ float s_scale;
-    double sum = 0.0;
-    for (int i = threadIdx.x; i < K; i += 256) {
-        const float v = x[(size_t)row * K + i];
-        sum += (double)(v * v);
-    }
-    sum = warp_sum_d(sum);
-    if (lane == 0) s_part[warp] = sum;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        double tot = 0.0;
-        for (int i = 0; i < 8; ++i) tot += s_part[i];
-        s_scale = 1.0f / sqrtf((float)(tot / K) + eps);
-    }
-    __syncthreads();
-    const float scale = s_scale;
+    const float scale = row_rms_scale(x + (size_t)row * K, K, eps, s_q, &s_scale);
     const int n_steps = K / 64, tt = row / kPfTok, tr = row % kPfTok;
     for (int blk = warp; blk < K / 32; blk += 8) {
         const int i = blk * 32 + lane;

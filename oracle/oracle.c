@@ -144,6 +144,27 @@ static double sum_squares_tree(const float* x, int n, int threads) {
     return tot;
 }
 
+/* The hidden-row sum of squares, in the kernels' tree (row_rms_scale and
+ * block_sum_squares): element squares (float products, widened to double);
+ * each 32-element block summed pairwise over adjacent pairs,
+ * ((s0 + s1) + (s2 + s3)) + ...; lane l's partial the blocks l, l + 32, ...
+ * added in order from 0; the 32 partials combined by one xor butterfly. */
+static double sum_squares_blocks(const float* x, int n) {
+    double part[32];
+    for (int l = 0; l < 32; ++l) part[l] = 0.0;
+    for (int b = 0; b < n / 32; ++b) {
+        double u[16];
+        const float* v = x + 32 * b;
+        for (int i = 0; i < 16; ++i) u[i] = (double)(v[2 * i] * v[2 * i]) + (double)(v[2 * i + 1] * v[2 * i + 1]);
+        for (int w = 8; w >= 1; w >>= 1)
+            for (int i = 0; i < w; ++i) u[i] = u[2 * i] + u[2 * i + 1];
+        part[b % 32] += u[0];
+    }
+    for (int off = 16; off > 0; off >>= 1)
+        for (int i = 0; i < off; ++i) part[i] = part[i] + part[i + off];
+    return part[0];
+}
+
 /* Float xor-butterfly total of 32 values (the kernels' warp sum). */
 static float warp_tree_sum(float* v) {
     for (int off = 16; off > 0; off >>= 1)
@@ -490,11 +511,11 @@ int orc_decoder_fill_synthetic_kv(orc_decoder* d, int n_pos, uint32_t seed) {
 
 /* ggml rms_norm followed by ggml_mul with the weight (src/qwen3.cpp:27-30):
  * float squares summed in double, mean as float, 1/sqrtf(mean + eps), then
- * (x * scale) * w.  `threads` fixes the summation tree (256 for hidden rows;
- * 32 for per-head q/k norms: each of 32 partials adds elements i, i + 32,
- * i + 64, i + 96 in order, then one butterfly). */
+ * (x * scale) * w.  `threads` fixes the summation tree: 0 for hidden rows
+ * (sum_squares_blocks); 32 for per-head q/k norms (each of 32 partials adds
+ * elements i, i + 32, i + 64, i + 96 in order, then one butterfly). */
 static void rms_norm_mul(const float* x, const float* w, int n, float eps, float* y, int threads) {
-    const double sum = sum_squares_tree(x, n, threads);
+    const double sum = threads ? sum_squares_tree(x, n, threads) : sum_squares_blocks(x, n);
     const float mean = (float)(sum / n);
     const float scale = 1.0f / sqrtf(mean + eps);
     for (int i = 0; i < n; ++i) y[i] = (x[i] * scale) * w[i];
@@ -602,7 +623,7 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
 
     for (int l = 0; l < m->n_layers; ++l) {
         const orc_layer* L = &m->layers[l];
-        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H, 256);
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->attn_norm, H, m->eps, xn + (size_t)t * H, 0);
         mul_mat_w(d->m, L->wq, qd, H, xn, T, q);
         mul_mat_w(d->m, L->wk, kd, H, xn, T, k);
         mul_mat_w(d->m, L->wv, kd, H, xn, T, v);
@@ -645,14 +666,14 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         }
         mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
-        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 256);
+        for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 0);
         mul_mat_w(d->m, L->wgate, F, H, xn, T, g);
         mul_mat_w(d->m, L->wup, F, H, xn, T, u);
         for (size_t i = 0; i < (size_t)T * F; ++i) g[i] = silu(g[i]) * u[i];
         mul_mat_w(d->m, L->wdown, H, F, g, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
     }
-    for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 256);
+    for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 0);
     d->past = kv;
     free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u);
     return 0;
