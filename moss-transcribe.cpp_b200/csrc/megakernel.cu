@@ -510,16 +510,20 @@ __device__ bool grid_barrier(const MegaArgs& a, unsigned target, int b, int* s_f
         // Every CTA's arrival, for the skew between CTAs.
         if (a.timeline && b < kMaxBarriers) a.timeline[kArrivalBase + (size_t)blockIdx.x * kMaxBarriers + b] = global_ns();
         // Arrive with release semantics (the CTA's writes, ordered before by the
-        // named barrier, become visible with it); poll with acquire loads, so
-        // the load that sees the last arrival orders everything after it.
+        // named barrier, become visible with it); poll with relaxed loads, then
+        // one acquire load of the completed count orders everything after it
+        // (an acquire on every poll would invalidate the L1 each time).
         if (!(b == a.stall_barrier && blockIdx.x == 0))
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.bar) : "memory");
         const unsigned long long t0 = global_ns();
         int status = 0;
         for (unsigned it = 0;; ++it) {
             unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
-            if (v >= target) break;
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+            if (v >= target) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.bar) : "memory");
+                break;
+            }
             if ((it & 255) == 255) {
                 if (*reinterpret_cast<volatile int*>(a.abort_flag)) { status = 1; break; }
                 if (global_ns() - t0 > a.wait_ns) {
@@ -856,9 +860,10 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
 // sequential fmaf chain), then that q8_0 block of the context row.  All of a
 // batch's loads (32 chunks) are issued together, the next batch's while the
 // current one is summed.
-// Wait (lane 0 polls with acquire loads, the warp follows) until the counter
-// reaches `target`: its producers release-add after their results are stored,
-// so the results are visible to the warp afterwards.  Bounded like a grid
+// Wait (lane 0 polls with relaxed loads and ends with one acquire load, the
+// warp follows) until the counter reaches `target`: its producers release-add
+// after their results are stored, so the results are visible to the warp
+// afterwards.  Bounded like a grid
 // barrier; false on abort or timeout.
 __device__ __forceinline__ bool wait_count(const MegaArgs& a, const unsigned* cnt, unsigned target) {
     int give_up = 0;
@@ -866,8 +871,11 @@ __device__ __forceinline__ bool wait_count(const MegaArgs& a, const unsigned* cn
         const unsigned long long t0 = global_ns();
         for (unsigned it = 0;; ++it) {
             unsigned v;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
-            if (v >= target) break;
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+            if (v >= target) {
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+                break;
+            }
             if ((it & 15) == 15) {
                 if (*reinterpret_cast<const volatile int*>(a.abort_flag)) { give_up = 1; break; }
                 if (global_ns() - t0 > a.wait_ns) {
@@ -1500,7 +1508,7 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
     // since the down projection (no grid barrier before it) may be updating x
     // by then; the CTAs with blocks have read x before any down item ends.
     if (pi.count == 0) return true;
-    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T);
+    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T, a.timeline, pid);
     mark(a.timeline, pid, 0);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     float* s_gu = reinterpret_cast<float*>(s_part + (size_t)pi.count * 8 * S * 32);  // [16 rows][32 features]
@@ -1549,7 +1557,7 @@ __device__ __noinline__ bool phase_lm(long long* cur, int pid) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, nullptr, 0,
+    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, a.timeline, pid,
                         blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
