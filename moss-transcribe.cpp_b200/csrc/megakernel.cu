@@ -1384,11 +1384,24 @@ __device__ __noinline__ bool phase_attn(int l, long long* cur, int pid) {
     const int rows_cap = wpi == 2 ? 4 : 32;
     const size_t scratch_off = (size_t)g * rows_cap * kAttnRowBytes;
     bool ok = true;
-    int prev = -1;  // stream * n_kv + head of the group's previous item
+    int prev = -1;     // stream * n_kv + head of the group's previous item
+    unsigned done = 0;  // the group's finished items of that (stream, head), not yet counted
+    // Count finished items for their head's merge (release: cumulative over
+    // the group's partial stores, ordered by the group's named barrier).  Once
+    // per run of items of one (stream, head), not per item: each release waits
+    // for the group's stores to complete.
+    auto count_done = [&]() {
+        if (done && wl == 0 && lane == 0) {
+            unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + prev / nkv) * nkv + prev % nkv;
+            asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(cnt), "r"(done) : "memory");
+        }
+        done = 0;
+    };
     for (int j = g; j < pi.count; j += n_groups) {
         int si, chunk, h;
         c.sch.attn_item_of(pi.first + j * gridDim.x, &si, &chunk, &h);
         const bool q_cached = prev == si * nkv + h;
+        if (!q_cached) count_done();
         prev = si * nkv + h;
         const long long q0 = pi.slot0 + (long long)j * pi.slots;
         const int mp = j == 0 ? pid : -1, mk = 0;  // marks: slots ready, rows patched, softmax, done
@@ -1401,18 +1414,13 @@ __device__ __noinline__ bool phase_attn(int l, long long* cur, int pid) {
                                                  mp, mk);
         ok = ok && good;
         // The group is done with the slots and its partials are stored: free
-        // the slots, and count the item for its head's merge (release:
-        // cumulative over the group's stores, ordered by the named barrier).
+        // the slots; the item is counted with the run it belongs to.
         item_sync(2 + g, wpi * 32);
-        if (wl == 0) {
-            if (lane < pi.slots) mbar_arrive(&s_empty()[(q0 + lane) % kRingSlots]);
-            if (lane == 0) {
-                unsigned* cnt = a.head_done + ((size_t)l * kMaxStreams + si) * nkv + h;
-                asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
-            }
-        }
+        if (wl == 0 && lane < pi.slots) mbar_arrive(&s_empty()[(q0 + lane) % kRingSlots]);
+        ++done;
         mark(a.timeline, mp, mk + 3);
     }
+    count_done();
     // Every group is done with its scratch in the region before phase D
     // (after the merges, with no grid barrier between) loads into it.
     consumer_sync();
