@@ -254,6 +254,8 @@ def main(argv=None):
     ap.add_argument("--f16", action="store_true",
                     help="the same verify-step microbench on the F16-weight decoder of configs[2] "
                          "(no side measurements, no CPU baseline)")
+    ap.add_argument("--only", choices=["long_context", "recordings", "config0"],
+                    help="run one side measurement alone and print it as one JSON line (profiling runs)")
     args = ap.parse_args(argv)
     if args.f16:
         args.no_extras = args.no_cpu_baseline = True
@@ -283,6 +285,16 @@ def main(argv=None):
 
     from mtb import capi
     model = capi.Model(path, local)
+    if args.only:
+        if args.only == "long_context":
+            line = long_context(model, capi, int(fixture.lcg_ids(1, model.vocab, seed=99)[0]))
+        elif args.only == "recordings":
+            line = recordings_line(model, capi, dist, torch, rank, local, world)
+        else:
+            line = config0(model, capi, fixture)
+        if rank == 0:
+            print(json.dumps({args.only: line}))
+        return
     dec = capi.Decoder(model, KV_LEN + 64, capi.KV_F16, max_new=64)
     dec.fill_synthetic_kv(KV_LEN, KV_SEED)
     V = model.vocab

@@ -48,13 +48,16 @@ extern "C" {
 typedef struct mtb_model mtb_model;
 typedef struct mtb_decoder mtb_decoder;
 
-enum { MTB_KV_F32 = 0, MTB_KV_F16 = 1 };
+/* KV cache element type; MTB_KV_DEFAULT reads MTB_KV_DTYPE ("f16" or "f32",
+ * unset: f32, the reference's cache type, src/qwen3_decoder.cpp:67-75). */
+enum { MTB_KV_DEFAULT = -1, MTB_KV_F32 = 0, MTB_KV_F16 = 1 };
 enum { MTB_STOP_NONE = 0, MTB_STOP_EOS = 1, MTB_STOP_LIMIT = 2, MTB_STOP_ERROR = 3 };
 
 /* Draft policy.  The reference policy is k_max 4, n-gram sizes 16..2
  * (src/cpu_speculative.cpp:29,104); penalty clamped to [1, 1.5] (:85-86).  A
- * NULL params pointer selects that policy with the penalty read from
- * MTD_REPETITION_PENALTY, as the reference does. */
+ * NULL params pointer selects mtb_spec_params_from_env: that policy with the
+ * penalty read from MTD_REPETITION_PENALTY, as the reference does, and k_max /
+ * n_min / n_max overridable by MTB_SPEC_K / MTB_NGRAM_MIN / MTB_NGRAM_MAX. */
 typedef struct mtb_spec_params {
     int32_t k_max;   /* proposals per step, 0..15 */
     int32_t n_min;   /* smallest n-gram size, >= 1 */
@@ -91,6 +94,28 @@ void mtb_set_log_level(int level);
  * and a terminating 0. */
 int mtb_format_generation_log(const int32_t* ids, int n_ids, int eos, const mtb_counters* counters, int k_max,
                               double prefill_seconds, double decoder_seconds, int trace, char* out, int out_size);
+/* The policy a NULL params pointer selects (see mtb_spec_params); needs no
+ * GPU.  Unparsable or out-of-range variables are reported here (-1, with
+ * mtb_global_error) rather than clamped. */
+int mtb_spec_params_from_env(mtb_spec_params* out);
+/* MTB_KV_F32 or MTB_KV_F16 as MTB_KV_DTYPE selects (unset: MTB_KV_F32), -1 for
+ * an unknown value; needs no GPU. */
+int mtb_kv_type_from_env(void);
+/* Test hook (host-side fault injection): the n-th device allocation made by
+ * this library from now on fails as if cudaMalloc had (n = 0: off).  The
+ * failing call returns its error and leaves no allocation behind. */
+void mtb_debug_fail_alloc(int n);
+/* Bounds-check build (libmoss_transcribe_b200_bc.so, -DMTB_BOUNDS_CHECK):
+ * the kernels check cache positions, page-table entries, the attention
+ * partial buffers and step row counts, record the first violated check on the
+ * device and skip or redirect that access (no trap).  _enabled: 1 in that
+ * build, 0 otherwise.  _status: the recorded site on `device` (0 none, 1 a
+ * cache position outside the decoder's pages, 2 a page-table entry outside
+ * the pool, 3 attention chunks beyond the partial buffers, 4 a step beyond 16
+ * rows), then cleared; always 0 in a normal build; -1 if the device cannot be
+ * selected.  Restores the caller's current device. */
+int mtb_bounds_check_enabled(void);
+int mtb_bounds_check_status(int device);
 /* Returns the error of the last failed call on this thread that had no object. */
 const char* mtb_global_error(void);
 

@@ -19,6 +19,9 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstdio>
+#include <atomic>
+#include <climits>
+#include <cstdint>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -109,10 +112,22 @@ struct mtb_decoder {
 
 namespace {
 
+// Allocation fault injection (mtb_debug_fail_alloc): counts down to the
+// allocation that fails.
+std::atomic<int> g_fail_alloc{0};
+
+cudaError_t device_malloc(void** q, size_t bytes) {
+    int n = g_fail_alloc.load();
+    while (n > 0 && !g_fail_alloc.compare_exchange_weak(n, n - 1)) {
+    }
+    if (n == 1) return cudaErrorMemoryAllocation;
+    return cudaMalloc(q, bytes);
+}
+
 template <class T>
 int dalloc(std::vector<void*>& allocs, std::string& err, T** p, size_t bytes) {
     void* q = nullptr;
-    const cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    const cudaError_t e = device_malloc(&q, bytes ? bytes : 16);
     if (e != cudaSuccess) {
         err = "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e);
         return -1;
@@ -581,14 +596,54 @@ float env_penalty() {
     return e ? float(std::atof(e)) : 1.f;
 }
 
+// An integer environment variable: `dflt` when unset; false when it does not
+// parse as a whole decimal integer.
+bool env_int(const char* name, int dflt, int* out) {
+    const char* e = std::getenv(name);
+    if (!e || !*e) {
+        *out = dflt;
+        return true;
+    }
+    char* end = nullptr;
+    const long v = std::strtol(e, &end, 10);
+    if (*end != 0 || v < INT32_MIN || v > INT32_MAX) return false;
+    *out = int(v);
+    return true;
+}
+
+int params_from_env(mtb_spec_params* out, std::string& err) {
+    int k, nmin, nmax;
+    if (!env_int("MTB_SPEC_K", 4, &k) || !env_int("MTB_NGRAM_MIN", 2, &nmin) || !env_int("MTB_NGRAM_MAX", 16, &nmax))
+        return fail(err, "MTB_SPEC_K / MTB_NGRAM_MIN / MTB_NGRAM_MAX must be integers");
+    if (k < 0 || k > kTMax - 1) return fail(err, "MTB_SPEC_K must be in [0, 15]");
+    if (nmin < 1 || nmax < nmin) return fail(err, "need 1 <= MTB_NGRAM_MIN <= MTB_NGRAM_MAX");
+    out->k_max = k;
+    out->n_min = nmin;
+    out->n_max = nmax;
+    out->penalty = env_penalty();
+    return 0;
+}
+
+int kv_type_from_env() {
+    const char* e = std::getenv("MTB_KV_DTYPE");
+    if (!e || !*e || !std::strcmp(e, "f32")) return KV_F32;
+    if (!std::strcmp(e, "f16")) return KV_F16;
+    return -1;
+}
+
 int set_params(mtb_decoder* d, int max_new, int eos, const mtb_spec_params* p) {
     StepState& s = *d->h_state;
     if (max_new <= 0 || max_new > d->max_new) return fail(d->error, "max_new must be in [1, " + std::to_string(d->max_new) + "]");
-    const int k = p ? p->k_max : 4;
+    mtb_spec_params envp;
+    if (!p) {
+        if (params_from_env(&envp, d->error)) return -1;
+        p = &envp;
+    }
+    const int k = p->k_max;
     if (k < 0 || k > kTMax - 1) return fail(d->error, "k_max must be in [0, 15]");
-    const int nmin = p ? p->n_min : 2, nmax = p ? p->n_max : 16;
+    const int nmin = p->n_min, nmax = p->n_max;
     if (nmin < 1 || nmax < nmin) return fail(d->error, "need 1 <= n_min <= n_max");
-    float pen = p ? p->penalty : env_penalty();
+    float pen = p->penalty;
     if (!(pen == pen)) pen = 1.f;              // NaN (an unparsable variable reads as 0, clamped below)
     pen = std::max(1.f, std::min(1.5f, pen));  // src/cpu_speculative.cpp:86
     s.max_new = max_new;
@@ -686,6 +741,34 @@ int mtb_format_generation_log(const int32_t* ids, int n_ids, int eos, const mtb_
 }
 
 int mtb_capi_can_transcribe(void) { return 0; }
+
+int mtb_spec_params_from_env(mtb_spec_params* out) {
+    if (!out) { g_error = "null argument"; return -1; }
+    return params_from_env(out, g_error);
+}
+
+int mtb_kv_type_from_env(void) { return kv_type_from_env(); }
+
+int mtb_bounds_check_enabled(void) {
+#ifdef MTB_BOUNDS_CHECK
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+int mtb_bounds_check_status(int device) {
+    int prev = 0;
+    if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(device) != cudaSuccess) return -1;
+    unsigned site = bc_take_kernels();
+    const unsigned m = bc_take_megakernel(), p = bc_take_prefill();
+    if (!site) site = m;
+    if (!site) site = p;
+    cudaSetDevice(prev);
+    return int(site);
+}
+
+void mtb_debug_fail_alloc(int n) { g_fail_alloc.store(n > 0 ? n : 0); }
 const char* mtb_global_error(void) { return g_error.c_str(); }
 
 int mtb_model_load(const char* path, int device, mtb_model** out) {
@@ -749,6 +832,13 @@ int mtb_model_dims(const mtb_model* m, int32_t* o) {
 int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_decoder** out) {
     if (!m || !out) { g_error = "null argument"; return -1; }
     *out = nullptr;
+    if (kv_type == MTB_KV_DEFAULT) {
+        kv_type = kv_type_from_env();
+        if (kv_type < 0) {
+            g_error = "MTB_KV_DTYPE must be f16 or f32";
+            return -1;
+        }
+    }
     if (max_seq <= 0 || max_new <= 0 || (kv_type != KV_F32 && kv_type != KV_F16)) {
         g_error = "invalid decoder arguments";
         return -1;
@@ -781,7 +871,9 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         uint8_t* zero_region = nullptr;
         const size_t head_bytes = size_t(dm.n_layers) * kMaxStreams * dm.n_kv * 4;
         const size_t pair_bytes = size_t(dm.n_layers) * (dm.n_heads / 2) * 4;
-        d->mb.zero_bytes = 16 + head_bytes + pair_bytes + size_t(dm.n_layers) * (F / 256) * 4;
+        const size_t slice_bytes = size_t(dm.n_layers) * (F / 256) * 4;
+        const size_t mmax_bytes = size_t(dm.n_layers) * dm.n_kv * kTMax * 4 * 4;
+        d->mb.zero_bytes = 16 + head_bytes + pair_bytes + slice_bytes + mmax_bytes;
         if (dalloc(A, E, &d->mb.act2_q, size_t(F / 32) * 512) || dalloc(A, E, &d->mb.act2_d, size_t(F / 32) * 16 * 4) ||
             dalloc(A, E, &d->mb.lm_val, size_t(std::max(m->mega_grid, 1)) * 16 * sizeof(float2)) ||
             dalloc(A, E, &zero_region, d->mb.zero_bytes))
@@ -793,6 +885,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         d->mb.head_done = reinterpret_cast<unsigned*>(zero_region + 16);
         d->mb.pair_done = reinterpret_cast<unsigned*>(zero_region + 16 + head_bytes);
         d->mb.slice_done = reinterpret_cast<unsigned*>(zero_region + 16 + head_bytes + pair_bytes);
+        d->mb.m_max = reinterpret_cast<unsigned*>(zero_region + 16 + head_bytes + pair_bytes + slice_bytes);
         // Failure-path test hook (documented in tests/test_gpu_wait_timeout.py): a
         // barrier CTA 0 never arrives at, and a shorter wait bound.
         if (const char* sb = std::getenv("MTB_TEST_STALL_BARRIER")) d->mb.stall_barrier = std::atoi(sb);
@@ -830,6 +923,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         }
         d->kv.base = kvb;
         d->kv.pages = pages;
+        d->kv.n_pages = n_pages;
         std::vector<int32_t> ident(static_cast<size_t>(n_pages));
         for (int i = 0; i < n_pages; ++i) ident[size_t(i)] = i;
         if (cudaMemcpy(pages, ident.data(), ident.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -943,7 +1037,7 @@ int mtb_decoder_kv_read(mtb_decoder* d, int layer, int which, int pos0, int n_po
     cudaSetDevice(d->device);
     float* tmp = nullptr;
     const size_t bytes = size_t(n_pos) * dm.n_kv * kHeadDim * 4;
-    MTB_CK(d, cudaMalloc(&tmp, bytes ? bytes : 4));
+    MTB_CK(d, device_malloc(reinterpret_cast<void**>(&tmp), bytes ? bytes : 4));
     launch_kv_gather(d->model->dm, d->kv, layer, which, pos0, n_pos, tmp, d->stream);
     cudaError_t e = cudaMemcpyAsync(out, tmp, bytes, cudaMemcpyDeviceToHost, d->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);

@@ -146,8 +146,34 @@ __device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, u
     if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
 }
 
+// Index checks of the bounds-check build: record the first violated site and
+// tell the caller to skip (or redirect) the access.  In a normal build every
+// check is `true` and compiles away.
+#ifdef MTB_BOUNDS_CHECK
+static __device__ unsigned g_bc_site;
+__device__ __forceinline__ bool bc_check(bool ok, unsigned site) {
+    if (!ok) atomicCAS(&g_bc_site, 0u, site);
+    return ok;
+}
+#define MTB_BC_TAKE(fn)                                   \
+    unsigned fn() {                                       \
+        unsigned v = 0, z = 0;                            \
+        cudaMemcpyFromSymbol(&v, g_bc_site, sizeof(v));   \
+        cudaMemcpyToSymbol(g_bc_site, &z, sizeof(z));     \
+        return v;                                         \
+    }
+#else
+__device__ __forceinline__ bool bc_check(bool, unsigned) { return true; }
+#define MTB_BC_TAKE(fn) \
+    unsigned fn() { return 0; }
+#endif
+
 __device__ __forceinline__ long long kv_offset(const KvCache& kv, int n_kv, int layer, int which, int head, int pos) {
+    // Checked build: an out-of-range position or page reads/writes element 0
+    // of the pool instead (and the site is recorded).
+    if (!bc_check(pos >= 0 && pos < kv.n_pages * kPage, BC_KV_POSITION)) return 0;
     const int page = kv.pages[pos / kPage];
+    if (!bc_check(page >= 0 && page < kv.n_pages, BC_KV_PAGE)) return 0;
     return (long long)page * kv.page_elems +
            ((((long long)layer * 2 + which) * n_kv + head) * kPage + (pos % kPage)) * kHeadDim;
 }
@@ -163,16 +189,16 @@ __device__ __forceinline__ void kv_store(const KvCache& kv, long long off, float
 }
 
 
-// Emit one id into the generated stream (src/cpu_speculative.cpp:108-116).
+// Emit one id into the generated stream (src/cpu_speculative.cpp:90-98).
 __device__ __forceinline__ void emit_id(StepState* st, int32_t* ids, int id) {
     ids[st->n_ids++] = id;
     if (id == st->eos) st->stop = STOP_EOS;
     else if (st->n_ids >= st->max_new) st->stop = STOP_LIMIT;
 }
 
-// Strict acceptance and logical rollback (src/cpu_speculative.cpp:142-153)
+// Strict acceptance and logical rollback (src/cpu_speculative.cpp:124-136)
 // given the per-row choices, then the next seed (the choice of the last kept
-// row, :119).  One thread.
+// row, :124-129).  One thread.
 __device__ __forceinline__ void accept_choices(StepState* st, int32_t* ids) {
     const int np = st->n_prop;
     st->target_calls += 1;

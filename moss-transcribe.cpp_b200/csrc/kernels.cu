@@ -482,6 +482,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
     const int kv_len = before + T;
     const int c = blockIdx.x, h = blockIdx.y;
     if (c * kPage >= kv_len) return;
+    if (!bc_check((kv_len + kPage - 1) / kPage <= max_chunks, BC_PARTIALS)) return;
     const int G = n_heads / n_kv;
     const int NQ = T * G;
     const int ld = (n_heads + 2 * n_kv) * kHeadDim;
@@ -948,6 +949,7 @@ __global__ void __launch_bounds__(256) k_draft(StepState* st, const int32_t* __r
         st->tokens[0] = st->seed;
         if (e >= 0) {
             np = min(budget, n - e);
+            if (!bc_check(1 + np <= kTMax, BC_STEP_ROWS)) np = kTMax - 1;
             for (int i = 0; i < np; ++i) st->tokens[1 + i] = ids[e + i];
         }
         st->n_prop = np;
@@ -973,6 +975,7 @@ __global__ void k_draft_forced(StepState* st) {
     int budget = min(st->k_max, st->max_new - st->n_ids);
     budget = max(min(budget, st->max_seq - st->past - 1), 0);
     st->n_prop = max(0, min(st->n_prop, budget));
+    if (!bc_check(1 + st->n_prop <= kTMax, BC_STEP_ROWS)) st->n_prop = kTMax - 1;
     st->tokens[0] = st->seed;
     st->T = 1 + st->n_prop;
     st->before = st->past;
@@ -1748,5 +1751,7 @@ void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int wh
                       cudaStream_t s) {
     k_kv_gather<<<148, 256, 0, s>>>(kv, m.dims.n_kv, layer, which, pos0, n_pos, out);
 }
+
+MTB_BC_TAKE(bc_take_kernels)
 
 }  // namespace mtb

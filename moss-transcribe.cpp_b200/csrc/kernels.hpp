@@ -39,6 +39,7 @@ struct MegaBuffers {
     unsigned* head_done; // [n_layers][kMaxStreams][n_kv] finished attention items per kv head
     unsigned* pair_done; // [n_layers][n_heads / 2] merged context blocks per pair of q heads
     unsigned* slice_done; // [n_layers][ffn / 256] finished gate/up blocks per 256-feature slice
+    unsigned* m_max;     // [n_layers][n_kv][64] running chunk maxima per (kv head, partial row), ordered bits
     size_t zero_bytes;
     unsigned long long* timeline;  // optional, MTB_PROFILE=1 (layout: mtb_step_timeline)
     // Optional, MTB_STEP_CAPTURE=1 (test read-back of the persistent step's own
@@ -79,7 +80,23 @@ struct KvCache {
     const int32_t* pages;    // logical page -> physical page
     int type;                // KvType
     long long page_elems;    // elements per page
+    int n_pages;             // pages in the pool (logical positions < n_pages * kPage)
 };
+
+// Bounds-check build (-DMTB_BOUNDS_CHECK): each compilation unit records the
+// first violated index check here (the site code), skips or redirects the
+// access, and its host reader returns and clears it.  0: nothing violated, or
+// a normal build (the checks compile to nothing).
+enum BcSite : unsigned {
+    BC_NONE = 0,
+    BC_KV_POSITION = 1,  // a cache position outside the decoder's pages
+    BC_KV_PAGE = 2,      // a page-table entry outside the pool
+    BC_PARTIALS = 3,     // attention chunks beyond the partial buffers
+    BC_STEP_ROWS = 4,    // a step's rows beyond kTMax
+};
+unsigned bc_take_kernels();
+unsigned bc_take_megakernel();
+unsigned bc_take_prefill();
 
 struct DeviceModel {
     ModelDims dims;

@@ -113,6 +113,7 @@ struct MegaArgs {
     unsigned* head_done;  // [n_layers][kMaxStreams][n_kv] finished attention items per kv head, zero at launch
     unsigned* pair_done;  // [n_layers][n_heads / 2] merged (row, q head, block) tasks per pair of q heads, zero at launch
     unsigned* slice_done; // [n_layers][ffn / 256] finished gate/up blocks per 256-feature slice, zero at launch
+    unsigned* m_max;      // [n_layers][n_kv][64] running max of the chunk maxima per (kv head, partial row), ordered bits, zero at launch
     int* abort_flag;
     unsigned long long wait_ns;  // bound on a grid-barrier wait
     int stall_barrier;           // test hook: CTA 0 does not arrive at this barrier (-1: off)
@@ -236,6 +237,8 @@ struct KvSlots {
 __device__ __forceinline__ uint8_t* kv_slot_base(uint8_t* ring, int s) {
     return ring + (size_t)s * kSlotBytes + (s & 1) * 512;
 }
+// The same as a byte offset from the ring's start (1024-aligned).
+__device__ __forceinline__ uint32_t kv_slot_off(int s) { return (uint32_t)s * kSlotBytes + (uint32_t)(s & 1) * 512u; }
 
 struct PhaseInfo {
     int n_items;    // items in the phase
@@ -860,6 +863,16 @@ __device__ __forceinline__ float4 sum_slices(const float4* part, int S) {
 // sequential fmaf chain), then that q8_0 block of the context row.  All of a
 // batch's loads (32 chunks) are issued together, the next batch's while the
 // current one is summed.
+// Float <-> unsigned with the same order (0 is below every encoded value),
+// for a running maximum by atomicMax.
+__device__ __forceinline__ unsigned ordered_bits(float f) {
+    const unsigned b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float from_ordered_bits(unsigned u) {
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
+}
+
 // Wait (lane 0 polls with relaxed loads and ends with one acquire load, the
 // warp follows) until the counter reaches `target`: its producers release-add
 // after their results are stored, so the results are visible to the warp
@@ -900,41 +913,45 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int s
     if (!wait_count(a, a.head_done + ((size_t)l * kMaxStreams + si) * a.d.n_kv + h, (unsigned)n_chunks)) return false;
     const size_t base = (size_t)h * a.max_chunks * (kTMax * 4) + qi;  // (h, chunk 0, qi)
     const float* po = a.part_o + base * kHeadDim + 32 * k + lane;
+    const float2* pml = a.part_ml + base;
     constexpr size_t kStrideO = (size_t)kTMax * 4 * kHeadDim;         // one chunk further
-    float ov[32];
+    constexpr size_t kStrideM = (size_t)kTMax * 4;
+    // M = the largest chunk maximum: kept by the attention items (atomicMax).
+    const float M = from_ordered_bits(__ldcg(a.m_max + ((size_t)l * a.d.n_kv + h) * (kTMax * 4) + qi));
+    // Chunks in batches of 32: each lane holds the batch's 32 values of its
+    // dim and the (m, l) of chunk c0 + lane.  Two batches are requested ahead
+    // of the one being summed (the sums are one sequential chain over the
+    // chunks).  Chunks past the end read as weight 0 (m = -inf, l = 0, o = 0),
+    // which adds nothing.
+    auto load_batch = [&](int c0, float (&o)[32], float2& ml) {
 #pragma unroll
-    for (int u = 0; u < 32; ++u) ov[u] = u < n_chunks ? __ldcg(po + u * kStrideO) : 0.f;
-    const float2 ml_first = lane < n_chunks ? __ldcg(&a.part_ml[base + (size_t)lane * (kTMax * 4)])
-                                            : make_float2(-INFINITY, 0.f);
-    float M = ml_first.x;
-    for (int c = lane + 32; c < n_chunks; c += 32) M = fmaxf(M, __ldcg(&a.part_ml[base + (size_t)c * (kTMax * 4)].x));
-    M = warp_max(M);
+        for (int u = 0; u < 32; ++u) o[u] = c0 + u < n_chunks ? __ldcg(po + (size_t)(c0 + u) * kStrideO) : 0.f;
+        ml = c0 + lane < n_chunks ? __ldcg(pml + (size_t)(c0 + lane) * kStrideM) : make_float2(-INFINITY, 0.f);
+    };
+    float ov[32], o1[32];
+    float2 ml0v, ml1v;
+    load_batch(0, ov, ml0v);
+    load_batch(32, o1, ml1v);
     float Ls = 0.f, acc = 0.f;
     for (int c0 = 0; c0 < n_chunks; c0 += 32) {
-        float2 ml = ml_first;
-        if (c0 > 0)
-            ml = c0 + lane < n_chunks ? __ldcg(&a.part_ml[base + (size_t)(c0 + lane) * (kTMax * 4)])
-                                      : make_float2(-INFINITY, 0.f);
-        const float wl = ml.x == -INFINITY ? 0.f : exact_expf(ml.x - M);
-        float nx[32];
+        float o2[32];
+        float2 ml2v;
+        load_batch(c0 + 64, o2, ml2v);
+        const float wl = ml0v.x == -INFINITY ? 0.f : exact_expf(ml0v.x - M);
 #pragma unroll
         for (int u = 0; u < 32; ++u) {
-            const int c = c0 + 32 + u;
-            nx[u] = c < n_chunks ? __ldcg(po + (size_t)c * kStrideO) : 0.f;
-        }
-        const int nc = min(32, n_chunks - c0);
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-            const float mc = __shfl_sync(0xffffffffu, ml.x, u);
-            const float lc = __shfl_sync(0xffffffffu, ml.y, u);
+            const float lc = __shfl_sync(0xffffffffu, ml0v.y, u);
             const float wgt = __shfl_sync(0xffffffffu, wl, u);
-            if (u < nc && mc != -INFINITY) {
-                Ls = fmaf(wgt, lc, Ls);
-                acc = fmaf(wgt, ov[u], acc);
-            }
+            Ls = fmaf(wgt, lc, Ls);
+            acc = fmaf(wgt, ov[u], acc);
         }
 #pragma unroll
-        for (int u = 0; u < 32; ++u) ov[u] = nx[u];
+        for (int u = 0; u < 32; ++u) {
+            ov[u] = o1[u];
+            o1[u] = o2[u];
+        }
+        ml0v = ml1v;
+        ml1v = ml2v;
     }
     const float o = acc / Ls;
     float am[1] = {warp_absmax(o)}, dq[1], iq[1];
@@ -1012,7 +1029,7 @@ __device__ __forceinline__ void item_sync(int bar, int nthr) {
 template <bool F16, int R>
 __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring, long long q0, const float* sq,
                                           float2* sw, int wl, int wpi, int nq, int G, int p0, int n_pos, int before,
-                                          size_t ml0) {
+                                          size_t ml0, unsigned* mrow) {
     using KS = KvSlots<F16>;
     const int lane = threadIdx.x & 31;
     const float attn_scale = 1.0f / sqrtf((float)kHeadDim);
@@ -1080,7 +1097,10 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
         const float lsum = warp_sum(e0 + e1);
         sw[(wl + wpi * rr) * kPage + lane] = make_float2(e0, e0);
         sw[(wl + wpi * rr) * kPage + lane + 32] = make_float2(e1, e1);
-        if (lane == 0 && r < nq) a.part_ml[ml0 + r] = make_float2(m, lsum);
+        if (lane == 0 && r < nq) {
+            a.part_ml[ml0 + r] = make_float2(m, lsum);
+            atomicMax(mrow + r, ordered_bits(m));  // the merge's M, without reading every chunk's m
+        }
     }
     __syncwarp();
     // P.V: o[rr] = {dims 4 lane, 4 lane + 1}, {4 lane + 2, 4 lane + 3}; each
@@ -1107,6 +1127,34 @@ __device__ __forceinline__ void attn_rows(const MegaArgs& a, const uint8_t* ring
     for (int sidx = 0; sidx < KS::kSlotsPerHalf; ++sidx) {
         const int pb = sidx * KS::kRowsPerSlot;
         const int np = min(KS::kRowsPerSlot, n_pos - pb);
+        if constexpr (F16) {
+            if (np == KS::kRowsPerSlot) {
+                // A full slot in blocks of 8 rows: row 8 m + k of the lane's
+                // chunk cv sits at the lane's offset XOR k * 16, + (8 m + k) * 128.
+                const uint32_t vA = kv_slot_off((s0v + sidx) % kRingSlots) + v_lane + ((uint32_t)cc << 4);
+#pragma unroll 1
+                for (int m = 0; m < KS::kRowsPerSlot / 8; ++m) {
+                    const uint32_t vm = vA + m * 1024;
+                    float2 v[8][2];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) load_v(ring + ((vm ^ (k << 4)) + k * 128), v[k][0], v[k][1]);
+#pragma unroll
+                    for (int rr = 0; rr < R; ++rr) {
+                        const float4* w4 = reinterpret_cast<const float4*>(sw + (wl + wpi * rr) * kPage + pb + 8 * m);
+#pragma unroll
+                        for (int k2 = 0; k2 < 4; ++k2) {
+                            const float4 w = w4[k2];
+                            const float2 wa = make_float2(w.x, w.y), wb = make_float2(w.z, w.w);
+                            o[rr][0] = __ffma2_rn(wa, v[2 * k2][0], o[rr][0]);
+                            o[rr][1] = __ffma2_rn(wa, v[2 * k2][1], o[rr][1]);
+                            o[rr][0] = __ffma2_rn(wb, v[2 * k2 + 1][0], o[rr][0]);
+                            o[rr][1] = __ffma2_rn(wb, v[2 * k2 + 1][1], o[rr][1]);
+                        }
+                    }
+                }
+                continue;
+            }
+        }
         const uint8_t* vb = kv_slot_base(const_cast<uint8_t*>(ring), (s0v + sidx) % kRingSlots) + v_lane;
         auto v_at = [&](int p) -> const uint8_t* { return vb + p * 128 + ((cc ^ (p & 7)) << 4); };
         int pr = 0;
@@ -1239,7 +1287,8 @@ __device__ __noinline__ bool attn_body(const MegaArgs& a, size_t scratch_off, in
     item_sync(bar, nthr);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 1);
     const size_t ml0 = ((size_t)h * a.max_chunks + chunk) * (kTMax * 4) + (size_t)row0 * G;
-    if (R > 0) attn_rows<F16, RP>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0);
+    unsigned* mrow = a.m_max + ((size_t)l * nkv + h) * (kTMax * 4) + (size_t)row0 * G;
+    if (R > 0) attn_rows<F16, RP>(a, ring, q0, sq, sw, wl, wpi, NQ, G, p0, n_pos, before, ml0, mrow);
     if (wl == 0) mark(a.timeline, mark_pid, mark_k + 2);
     return ok;
 }
@@ -1919,6 +1968,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1)
                 T = 0;
             }
             if (rows + T > kTMax) T = 0;  // more active streams than rows: cannot happen with kMaxStreams <= kTMax
+            // Checked build: a stream whose chunks exceed the partial buffers is left out.
+            if (T > 0 && !bc_check((st->before + T + kPage - 1) / kPage <= args.max_chunks, BC_PARTIALS)) T = 0;
             c.s_T[si] = T;
             c.s_row0[si] = rows;
             c.s_before[si] = st->before;
@@ -2083,6 +2134,7 @@ cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeight
     a.abort_flag = mb.abort_flag;
     a.head_done = mb.head_done;
     a.pair_done = mb.pair_done;
+    a.m_max = mb.m_max;
     a.slice_done = mb.slice_done;
     a.wait_ns = mb.wait_ns;
     a.stall_barrier = mb.stall_barrier;
@@ -2112,5 +2164,7 @@ cudaError_t launch_step_persistent(const DeviceModel& m, const LayerWeights* lay
     int32_t* ids = b.ids;
     return launch_step_persistent_group(m, layers_dev, &kv, &map, &state, &ids, 1, b, mb, grid, s);
 }
+
+MTB_BC_TAKE(bc_take_megakernel)
 
 }  // namespace mtb

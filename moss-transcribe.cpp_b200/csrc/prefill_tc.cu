@@ -359,4 +359,6 @@ void pf_gemm(const uint8_t* w, int n_rows, int K, const uint8_t* xq, const float
     k_pf_gemm<<<dim3((T + kPfTok - 1) / kPfTok, n_rows / kPfRows), kPfThreads, 120 * 1024, s>>>(a);
 }
 
+MTB_BC_TAKE(bc_take_prefill)
+
 }  // namespace mtb

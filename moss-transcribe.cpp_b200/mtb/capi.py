@@ -18,10 +18,12 @@ import os
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libmoss_transcribe_b200.so")
+# MTB_LIBRARY selects another build of the library (the bounds-check build
+# libmoss_transcribe_b200_bc.so, for instance).
+LIB_PATH = os.environ.get("MTB_LIBRARY") or os.path.join(os.path.dirname(_HERE), "libmoss_transcribe_b200.so")
 _LIB = None
 
-KV_F32, KV_F16 = 0, 1
+KV_DEFAULT, KV_F32, KV_F16 = -1, 0, 1
 STOP_NONE, STOP_EOS, STOP_LIMIT, STOP_ERROR = 0, 1, 2, 3
 
 
@@ -93,6 +95,11 @@ SIGNATURES = {
     "mtb_step_capture": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _ip]),
     "mtb_capi_can_transcribe": (C.c_int, []),
     "mtb_set_log_level": (None, [C.c_int]),
+    "mtb_spec_params_from_env": (C.c_int, [C.POINTER(SpecParams)]),
+    "mtb_kv_type_from_env": (C.c_int, []),
+    "mtb_debug_fail_alloc": (None, [C.c_int]),
+    "mtb_bounds_check_enabled": (C.c_int, []),
+    "mtb_bounds_check_status": (C.c_int, [C.c_int]),
     "mtb_format_generation_log": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_double, C.c_double, C.c_int,
                                             C.c_char_p, C.c_int]),
     "mtb_debug_poison_kv": (C.c_int, [_vp, C.c_int, C.c_int]),
@@ -121,6 +128,26 @@ def lib():
             fn.argtypes = args
         _LIB = L
     return _LIB
+
+
+def spec_params_from_env() -> dict:
+    """The policy a NULL params pointer selects: the reference policy (k 4,
+    n-grams 16..2, penalty from MTD_REPETITION_PENALTY) with MTB_SPEC_K /
+    MTB_NGRAM_MIN / MTB_NGRAM_MAX overrides.  Raises on an invalid variable."""
+    p = SpecParams()
+    if lib().mtb_spec_params_from_env(C.byref(p)) != 0:
+        raise MtbError(lib().mtb_global_error().decode())
+    return {"k_max": p.k_max, "n_min": p.n_min, "n_max": p.n_max, "penalty": p.penalty}
+
+
+def kv_type_from_env() -> int:
+    """KV_F32 or KV_F16 as MTB_KV_DTYPE selects (unset: KV_F32); -1 if unknown."""
+    return lib().mtb_kv_type_from_env()
+
+
+def debug_fail_alloc(n: int) -> None:
+    """Test hook: the n-th device allocation from now on fails (0: off)."""
+    lib().mtb_debug_fail_alloc(int(n))
 
 
 def _f32(a):
