@@ -162,9 +162,11 @@ def dist_setup(args=None):
         import torch
         import torch.distributed as dist
         backend = os.environ.get("MTB_DIST_BACKEND", "nccl")
+        kw = {}
         if backend == "nccl":
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kw["device_id"] = torch.device("cuda", local)  # rank -> GPU stated, not guessed
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
         return rank, local, world, dist, torch
     return rank, local, world, None, None
 
