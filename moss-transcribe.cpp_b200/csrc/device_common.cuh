@@ -146,6 +146,16 @@ __device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, u
     if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
 }
 
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the
+// stream still runs.  pdl_wait() returns once the predecessor has completed
+// and its writes are visible (immediately for a normal launch), so a kernel
+// reads or writes step data only after it; pdl_launch_dependents() lets the
+// next such kernel start its own independent prologue (weight loads).  Every
+// kernel of a programmatic chain calls pdl_wait() before touching step data.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Index checks of the bounds-check build: record the first violated site and
 // tell the caller to skip (or redirect) the access.  In a normal build every
 // check is `true` and compiles away.

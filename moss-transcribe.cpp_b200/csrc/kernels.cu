@@ -16,6 +16,7 @@
 
 #include <cuda_fp16.h>
 #include <cfloat>
+#include <cstdlib>
 #include <cstdio>
 
 namespace mtb {
@@ -306,6 +307,8 @@ __global__ void __launch_bounds__(128) k_qk_norm_rope_store(const StepState* st,
                                                             const float* __restrict__ k_norm, float eps,
                                                             float theta_scale, KvCache kv, int layer, int T_arg,
                                                             int before_arg) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int T = T_arg < 0 ? st->T : T_arg;
     const int row = blockIdx.x, hh = blockIdx.y;
     if (row >= T) return;
@@ -474,6 +477,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_chunk(const StepState* st, co
                                                          int n_kv, KvCache kv, int layer, float* part_o,
                                                          float2* part_ml, int max_chunks, int T_arg, int before_arg,
                                                          int qstride) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int rb = blockIdx.z;
     const int T_all = T_arg < 0 ? st->T : T_arg;
     const int T = min(kTMax, T_all - kTMax * rb);
@@ -757,6 +762,8 @@ __global__ void __launch_bounds__(128) k_attn_combine(const StepState* st, int n
                                                       const float* part_o, const float2* part_ml, int max_chunks,
                                                       float* attn_out, int T_arg, int before_arg, int qstride,
                                                       __half* act_h) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int T_all = T_arg < 0 ? st->T : T_arg;
     const int t_all = blockIdx.x, head = blockIdx.y;
     if (t_all >= T_all) {
@@ -1223,6 +1230,8 @@ cudaError_t configure_kernels() {
 __global__ void __launch_bounds__(kThreads) k_rmsnorm_f16(const StepState* st, const float* __restrict__ x, int K,
                                                          const float* __restrict__ w, float eps, __half* act,
                                                          float* normed) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int row = blockIdx.x;
     const int T = st->T;
     if (T <= 0) return;
@@ -1424,14 +1433,19 @@ template <int EPI, int SPB>
 __global__ void __launch_bounds__(256, SPB == 4 ? 2 : 3)
     k_gemv_f16(const __half* __restrict__ W, int N, int K, const __half* __restrict__ act, const StepState* st,
                float* out, int ld, float2* lm_val, float* part, int* cnt) {
-    const int T = st->T;
-    if (T <= 0) return;
     extern __shared__ __align__(16) float sm_f16[];
     const int nsb = (K >> 8) / SPB;
     const int g = blockIdx.x / nsb, s0 = (blockIdx.x % nsb) * SPB;
     constexpr int kw = SPB * 256;
+    // The weights do not depend on the step: they are requested before the
+    // wait for the previous kernel (programmatic launch), so their HBM latency
+    // overlaps that kernel's tail.
     uint4 wr[SPB][4];
     f16_load_weights<SPB>(W, K, g, s0, wr);
+    pdl_wait();
+    pdl_launch_dependents();
+    const int T = st->T;
+    if (T <= 0) return;
     float* xs = sm_f16;                                  // [kw][16] + padding
     float* bv = xs + kw * kTMax + (kw >> 5) * kF16Pad;  // [8 blocks][16 rows][32 outputs]
     const int RS = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : T <= 8 ? 8 : kTMax;  // rows staged and computed
@@ -1501,6 +1515,30 @@ static void configure_f16_kernels() {
     configure_f16_spb<kF16MaxSpb>();
 }
 
+// Launch with programmatic stream serialization (the F16 step's kernels, each
+// of which calls pdl_wait() before touching step data): the next kernel's
+// launch and weight loads overlap the current one's tail.  MTB_NO_PDL=1 at the
+// first launch turns it off (ordinary stream order).
+static bool pdl_enabled() {
+    static const bool on = !std::getenv("MTB_NO_PDL");
+    return on;
+}
+
+template <typename... KArgs, typename... Args>
+static void launch_chain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 template <int EPI>
 static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const StepBuffers& b, float* out, int ld,
                      float2* lm_val, cudaStream_t s) {
@@ -1508,15 +1546,16 @@ static void gemv_f16(const uint16_t* W, int N, int K, const uint16_t* act, const
     const int blocks = (N + kF16Outs - 1) / kF16Outs * ((K >> 8) / spb);
     const __half* w = reinterpret_cast<const __half*>(W);
     const __half* a = reinterpret_cast<const __half*>(act);
+    const StepState* st = b.state;
     if (spb == kF16MaxSpb)
-        k_gemv_f16<EPI, kF16MaxSpb><<<blocks, 256, gemv_f16_smem(spb), s>>>(w, N, K, a, b.state, out, ld, lm_val,
-                                                                          b.f16_part, b.f16_cnt);
+        launch_chain(k_gemv_f16<EPI, kF16MaxSpb>, blocks, 256, gemv_f16_smem(spb), s, w, N, K, a, st, out, ld, lm_val,
+                     b.f16_part, b.f16_cnt);
     else if (spb == 2)
-        k_gemv_f16<EPI, 2><<<blocks, 256, gemv_f16_smem(2), s>>>(w, N, K, a, b.state, out, ld, lm_val, b.f16_part,
-                                                                 b.f16_cnt);
+        launch_chain(k_gemv_f16<EPI, 2>, blocks, 256, gemv_f16_smem(2), s, w, N, K, a, st, out, ld, lm_val, b.f16_part,
+                     b.f16_cnt);
     else
-        k_gemv_f16<EPI, 1><<<blocks, 256, gemv_f16_smem(1), s>>>(w, N, K, a, b.state, out, ld, lm_val, b.f16_part,
-                                                                 b.f16_cnt);
+        launch_chain(k_gemv_f16<EPI, 1>, blocks, 256, gemv_f16_smem(1), s, w, N, K, a, st, out, ld, lm_val, b.f16_part,
+                     b.f16_cnt);
 }
 
 // forward_layers for F16 weights: the same sequence with fp16 activations.
@@ -1528,22 +1567,21 @@ static void forward_layers_f16(const DeviceModel& m, const KvCache& kv, const St
     __half* act = reinterpret_cast<__half*>(b.act_h);
     for (int l = 0; l < d.n_layers; ++l) {
         const LayerWeights& w = m.layers[l];
-        k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.attn_norm, d.eps, act, nullptr);
+        launch_chain(k_rmsnorm_f16, kTMax, kThreads, 0, s, b.state, b.x, H, w.attn_norm, d.eps, act, (float*)nullptr);
         gemv_f16<F16_STORE>(w.h_qkv, qd + 2 * kd, H, b.act_h, b, b.qkv, qd + 2 * kd, nullptr, s);
-        k_qk_norm_rope_store<<<dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, w.q_norm,
-                                                                             w.k_norm, d.eps, m.theta_scale, kv, l, -1, 0);
-        k_attn_chunk<<<dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s>>>(b.state, b.qkv, d.n_heads, d.n_kv, kv, l,
-                                                                              b.part_o, b.part_ml, b.max_chunks, -1, 0,
-                                                                              kTMax * 4);
-        k_attn_combine<<<dim3(kTMax, d.n_heads), 128, 0, s>>>(b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
-                                                              b.max_chunks, b.attn_out, -1, 0, kTMax * 4, act);
+        launch_chain(k_qk_norm_rope_store, dim3(kTMax, d.n_heads + d.n_kv), 128, 0, s, b.state, b.qkv, d.n_heads, d.n_kv,
+                     w.q_norm, w.k_norm, d.eps, m.theta_scale, kv, l, -1, 0);
+        launch_chain(k_attn_chunk, dim3(b.max_chunks, d.n_kv), kThreads, attn_smem, s, b.state, b.qkv, d.n_heads, d.n_kv,
+                     kv, l, b.part_o, b.part_ml, b.max_chunks, -1, 0, kTMax * 4);
+        launch_chain(k_attn_combine, dim3(kTMax, d.n_heads), 128, 0, s, b.state, d.n_heads, d.n_kv, b.part_o, b.part_ml,
+                     b.max_chunks, b.attn_out, -1, 0, kTMax * 4, act);
         gemv_f16<F16_RESID>(w.h_o, H, qd, b.act_h, b, b.x, H, nullptr, s);
-        k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, w.ffn_norm, d.eps, act, nullptr);
+        launch_chain(k_rmsnorm_f16, kTMax, kThreads, 0, s, b.state, b.x, H, w.ffn_norm, d.eps, act, (float*)nullptr);
         // SwiGLU in the gate | up GEMV's epilogue, into act_h2 (act_h is its input).
         gemv_f16<F16_SWIGLU>(w.h_gu, 2 * F, H, b.act_h, b, reinterpret_cast<float*>(b.act_h2), F, nullptr, s);
         gemv_f16<F16_RESID>(w.h_down, H, F, b.act_h2, b, b.x, H, nullptr, s);
     }
-    k_rmsnorm_f16<<<kTMax, kThreads, 0, s>>>(b.state, b.x, H, m.output_norm, d.eps, act, b.hid);
+    launch_chain(k_rmsnorm_f16, kTMax, kThreads, 0, s, b.state, b.x, H, m.output_norm, d.eps, act, b.hid);
 }
 
 static void lm_head_f16(const DeviceModel& m, const StepBuffers& b, bool want_logits, cudaStream_t s) {
