@@ -135,14 +135,23 @@ __device__ __forceinline__ int frag_offset(int r, int c) {
 }
 
 // q8_0 quantisation of one 32-element block held one element per lane, as
+// The q8_0 code of x (|x| <= 127, or NaN) as the low byte of the returned
+// bits: adding 1.5 * 2^23 rounds x to the nearest integer, ties to even (the
+// sum's unit in the last place is 1), and leaves it in two's complement in
+// the low bits -- the same code as __float2int_rn, without the conversion
+// unit.  NaN gives code 0, as the conversion does.
+__device__ __forceinline__ uint32_t q8_code_bits(float x) {
+    const uint32_t b = __float_as_uint(__fadd_rn(x, 12582912.0f));
+    return x == x ? b : 0u;
+}
+
 // ggml's x86 from_float: d = amax/127 (stored fp16), code = rint(x * 127/amax).
 __device__ __forceinline__ void quantize_block_lane(float v, int row, int blk, uint8_t* act_q, float* act_d) {
     const int lane = threadIdx.x & 31;
     const float amax = warp_absmax(v);
     const float d = amax / 127.f;
     const float id = amax != 0.0f ? 127.f / amax : 0.0f;
-    const int q = __float2int_rn(__fmul_rn(v, id));
-    act_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)q;
+    act_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)q8_code_bits(__fmul_rn(v, id));
     if (lane == 0) act_d[blk * 16 + row] = __half2float(__float2half_rn(d));
 }
 

@@ -26,7 +26,11 @@ __device__ __forceinline__ float exact_expf(float x) {
     // selected at the end; 2^n is applied as (p * 2^a) * 2^b with
     // (a, b) = (n, 0), (1, 127) for n = 128, (n + 64, -64) for n < -126.
     const float xc = fminf(fmaxf(x, -103.972084f), 88.7228317f);
-    const float n = rintf(__fmul_rn(xc, 1.44269502f));
+    // n = rint(xc * log2 e) by the 1.5 * 2^23 add (|n| <= 150: the sum's unit
+    // in the last place is 1, so it rounds to nearest even), and its integer
+    // value from the sum's low bits, with no conversion instructions.
+    const float tm = __fadd_rn(__fmul_rn(xc, 1.44269502f), 12582912.0f);
+    const float n = __fsub_rn(tm, 12582912.0f);
     float r = fmaf(n, -0.693145752f, xc);
     r = fmaf(n, -1.42860677e-6f, r);
     float p = 1.98412701e-4f;
@@ -37,7 +41,7 @@ __device__ __forceinline__ float exact_expf(float x) {
     p = fmaf(p, r, 0.5f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    const int ni = (int)n;
+    const int ni = (int)(__float_as_uint(tm) - 0x4B400000u);
     const int ea = ni > 127 ? 1 : (ni < -126 ? ni + 64 : ni);
     const int eb = ni > 127 ? 127 : (ni < -126 ? -64 : 0);
     const float y = __fmul_rn(__fmul_rn(p, __uint_as_float((unsigned)(ea + 127) << 23)),

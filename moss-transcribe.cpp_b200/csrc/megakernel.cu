@@ -580,8 +580,16 @@ __device__ __forceinline__ bool slots_wait(uint64_t* full, long long q0, int n, 
 // kUmma: the output is the tcgen05 operand layout instead (16 rows x K bytes
 // as 64-K steps of 1024 bytes, core matrix (row group, 16-byte chunk) at
 // (4 group + chunk) * 128, row at +16 row; scales f32 [16][K / 32]).
+// This consumer thread's float4 of a row-norm weight vector (K = 256 NK),
+// requested before the grid barrier that precedes the norm.
+template <int NK>
+__device__ __forceinline__ float4 norm_weights_prefetch(const float* wn) {
+    constexpr int K = 256 * NK;
+    return threadIdx.x < K / 4 ? __ldg(reinterpret_cast<const float4*>(wn) + threadIdx.x) : make_float4(0.f, 0.f, 0.f, 0.f);
+}
+
 template <int NK, bool kUmma = false>
-__device__ __noinline__ void norm_quant_smem(const float* x, const float* __restrict__ wn, float eps, int T,
+__device__ __noinline__ void norm_quant_smem(const float* x, float4 wpre, float eps, int T,
                                             unsigned long long* timeline = nullptr, int pid = 0,
                                             float* normed_out = nullptr) {
     constexpr int K = 256 * NK;
@@ -610,8 +618,12 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
 #pragma unroll
         for (int k = 0; k < NB / 4; ++k) f[k] = __ldcg(x4 + 32 * k + lane);
     }
-    for (int e4 = threadIdx.x; e4 < K / 4; e4 += kConsumers)
-        *reinterpret_cast<float4*>(wstage + (e4 >> 3) * 36 + 4 * (e4 & 7)) = __ldg(reinterpret_cast<const float4*>(wn) + e4);
+    // The norm weights came in before the grid barrier (norm_weights_prefetch):
+    // they do not depend on the step, and after a barrier their HBM round trip
+    // would add to the rows' L2 round trip.
+    static_assert(K / 4 <= kConsumers, "one float4 of norm weights per consumer thread");
+    if (threadIdx.x < K / 4)
+        *reinterpret_cast<float4*>(wstage + (threadIdx.x >> 3) * 36 + 4 * (threadIdx.x & 7)) = wpre;
     consumer_sync();
     float wv[32];
     if (has) {
@@ -666,20 +678,29 @@ __device__ __noinline__ void norm_quant_smem(const float* x, const float* __rest
             uint32_t word[8];  // codes 4 w .. 4 w + 3 of the block
 #pragma unroll
             for (int wd = 0; wd < 8; ++wd) {
-                uint32_t pk = 0;
+                uint32_t b[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    pk |= (uint32_t)(uint8_t)(int8_t)__float2int_rn(__fmul_rn(v[4 * wd + j], id)) << (8 * j);
-                word[wd] = pk;
+                for (int j = 0; j < 4; ++j) b[j] = q8_code_bits(__fmul_rn(v[4 * wd + j], id));
+                word[wd] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
             }
             const float dq = __half2float(__float2half_rn(d));
+            // Words stored in an order rotated by the lane (spreads the warp's
+            // stores over the banks): rotate the array by lane & 7 in three
+            // conditional steps, then store rot[s8] as word (s8 + lane) & 7.
+#pragma unroll
+            for (int k = 1; k < 8; k <<= 1) {
+                if (lane & k) {
+                    uint32_t t[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) t[i] = word[(i + k) & 7];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) word[i] = t[i];
+                }
+            }
 #pragma unroll
             for (int s8 = 0; s8 < 8; ++s8) {
-                const int wd = (s8 + lane) & 7;  // rotated: spreads the warp's stores over the banks
-                uint32_t val = word[0];
-#pragma unroll
-                for (int i = 1; i < 8; ++i)
-                    if (wd == i) val = word[i];
+                const int wd = (s8 + lane) & 7;
+                const uint32_t val = word[s8];
                 if constexpr (kUmma) {
                     const int e = 32 * lane + 4 * wd, kk = e % 64;
                     *reinterpret_cast<uint32_t*>(act_q + (e / 64) * 1024 + ((row / 8) * 4 + kk / 16) * 128 + (row % 8) * 16 +
@@ -957,7 +978,7 @@ __device__ __noinline__ bool combine_task(const MegaArgs& a, int l, int t, int s
     float am[1] = {warp_absmax(o)}, dq[1], iq[1];
     q8_scales<1>(am, dq, iq);
     const int blk = qh * 4 + k;
-    a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(o, iq[0]));
+    a.act_q[(size_t)blk * 512 + frag_offset(t, lane)] = (uint8_t)q8_code_bits(__fmul_rn(o, iq[0]));
     if (lane == 0) a.act_d[blk * 16 + t] = __half2float(__float2half_rn(dq[0]));
     // The block is stored (every lane's byte, lane 0's scale): count it for
     // the O projection's 256-K slice of this pair of q heads.
@@ -1390,7 +1411,7 @@ __device__ __forceinline__ void for_outputs(const float4& y, int T, F f) {
 
 // A: RMSNorm + quantise (every CTA), QKV rows -> qkv.
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_qkv(int l, long long* cur, int pid) {
+__device__ __noinline__ bool phase_qkv(int l, long long* cur, int pid, float4 wpre) {
     const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     const LayerWeights& w = a.layers[l];
@@ -1403,7 +1424,7 @@ __device__ __noinline__ bool phase_qkv(int l, long long* cur, int pid) {
     const float qkn = threadIdx.x < 2 * kHeadDim
                           ? __ldg((threadIdx.x < kHeadDim ? w.q_norm : w.k_norm) + (threadIdx.x % kHeadDim))
                           : 0.f;
-    norm_quant_smem<NK>(a.x, w.attn_norm, a.d.eps, c.T, a.timeline, pid);
+    norm_quant_smem<NK>(a.x, wpre, a.d.eps, c.T, a.timeline, pid);
     if (threadIdx.x < 2 * kHeadDim) g_qk_norm[threadIdx.x] = qkn;
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_QKV, &cur[0], &cur[1]);
@@ -1551,10 +1572,9 @@ __device__ __noinline__ bool phase_proj_resid(int l, long long* cur, int pid, bo
 // (warp k: pair k), then the block's q8_0 quantisation for the down
 // projection (one row per warp at a time) straight from shared memory.
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
+__device__ __noinline__ bool phase_gu(int l, long long* cur, int pid, float4 wpre) {
     const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
-    const LayerWeights& w = a.layers[l];
     constexpr int K = 256 * NK;
     constexpr int S = K / kTileK / 4;  // slices per row group
     const int T = c.T, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1565,7 +1585,7 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
     // since the down projection (no grid barrier before it) may be updating x
     // by then; the CTAs with blocks have read x before any down item ends.
     if (pi.count == 0) return true;
-    norm_quant_smem<NK>(a.x, w.ffn_norm, a.d.eps, T, a.timeline, pid);
+    norm_quant_smem<NK>(a.x, wpre, a.d.eps, T, a.timeline, pid);
     mark(a.timeline, pid, 0);
     float4* s_part = reinterpret_cast<float4*>(act_d + (K / 32) * 16);
     float* s_gu = reinterpret_cast<float*>(s_part + (size_t)pi.count * 8 * S * 32);  // [16 rows][32 features]
@@ -1592,7 +1612,7 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
             const float v = s_gu[row * 32 + lane];
             float am[1] = {warp_absmax(v)}, dq[1], iq[1];
             q8_scales<1>(am, dq, iq);
-            a.act2_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, iq[0]));
+            a.act2_q[(size_t)blk * 512 + frag_offset(row, lane)] = (uint8_t)q8_code_bits(__fmul_rn(v, iq[0]));
             if (lane == 0) a.act2_d[blk * 16 + row] = __half2float(__float2half_rn(dq[0]));
         }
         consumer_sync();
@@ -1607,15 +1627,14 @@ __device__ __noinline__ bool phase_gu(int l, long long* cur, int pid) {
 
 // G: final RMSNorm + quantise; LM head with the fused first max -> lm_val[cta].
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_lm(long long* cur, int pid) {
+__device__ __noinline__ bool phase_lm(long long* cur, int pid, float4 wpre) {
     const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     constexpr int K = 256 * NK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
     uint8_t* act_q = s_region();
     float* act_d = reinterpret_cast<float*>(act_q + (size_t)(K / 32) * 512);
-    norm_quant_smem<NK>(a.x, a.output_norm, a.d.eps, c.T, a.timeline, pid,
-                        blockIdx.x == 0 ? a.capture : nullptr);
+    norm_quant_smem<NK>(a.x, wpre, a.d.eps, c.T, a.timeline, pid, blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
     float best_v[2] = {-INFINITY, -INFINITY};
@@ -1692,7 +1711,7 @@ __device__ __forceinline__ uint64_t lm_desc(uint32_t addr) {
 }
 
 template <int NK, bool kLow>
-__device__ __noinline__ bool phase_lm_tc(long long* cur, int pid) {
+__device__ __noinline__ bool phase_lm_tc(long long* cur, int pid, float4 wpre) {
     const KCtx& c = g_ctx;
     const MegaArgs& a = c.a;
     constexpr int K = 256 * NK, NB = K / 32, STEPS = K / 64, HALF = STEPS / 2, TT = kLow ? 8 : kTMax;
@@ -1700,8 +1719,7 @@ __device__ __noinline__ bool phase_lm_tc(long long* cur, int pid) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint8_t* act_q = s_region();                                          // [STEPS][1024]
     float* act_d = reinterpret_cast<float*>(s_region() + STEPS * 1024);   // [16][NB]
-    norm_quant_smem<NK, true>(a.x, a.output_norm, a.d.eps, c.T, nullptr, 0,
-                              blockIdx.x == 0 ? a.capture : nullptr);
+    norm_quant_smem<NK, true>(a.x, wpre, a.d.eps, c.T, nullptr, 0, blockIdx.x == 0 ? a.capture : nullptr);
     mark(a.timeline, pid, 0);
     const PhaseInfo pi = c.sch.take(W_LM, &cur[0], &cur[1]);
     uint64_t* half_full = g_lm_bars;
@@ -1917,22 +1935,27 @@ __device__ __noinline__ void run_phases() {
     unsigned target = 0;
     int nb = 0;                 // grid barriers passed (the timeline's phase index)
     long long cur[2] = {0, 0};  // schedule cursor (Schedule::take)
+    const int L = c.a.d.n_layers;
     phase_embed();
+    // Each row norm's weights are requested before the barrier in front of it.
+    float4 wpre = norm_weights_prefetch<kNK>(c.a.layers[0].attn_norm);
     if (!end_phase(&target, &nb)) return;
-    for (int l = 0; l < c.a.d.n_layers; ++l) {
-        if (!phase_qkv<kNK, kLow>(l, cur, nb)) consumer_fail(c.a);
+    for (int l = 0; l < L; ++l) {
+        if (!phase_qkv<kNK, kLow>(l, cur, nb, wpre)) consumer_fail(c.a);
         if (!end_phase(&target, &nb)) return;
         // B, C and D share one barrier interval (D waits per slice on C), as do E and F.
         if (!phase_attn(l, cur, nb)) consumer_fail(c.a);
         if (!phase_combine(l)) consumer_fail(c.a);
         if (!phase_proj_resid<kLow>(l, cur, kSubPhaseO + l, false)) consumer_fail(c.a);
+        wpre = norm_weights_prefetch<kNK>(c.a.layers[l].ffn_norm);
         if (!end_phase(&target, &nb)) return;
-        if (!phase_gu<kNK, kLow>(l, cur, nb)) consumer_fail(c.a);
+        if (!phase_gu<kNK, kLow>(l, cur, nb, wpre)) consumer_fail(c.a);
         if (!phase_proj_resid<kLow>(l, cur, kSubPhaseDown + l, true)) consumer_fail(c.a);
+        wpre = norm_weights_prefetch<kNK>(l + 1 < L ? c.a.layers[l + 1].attn_norm : c.a.output_norm);
         if (!end_phase(&target, &nb)) return;
     }
-    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, nb)
-                     : !phase_lm<kNK, kLow>(cur, nb))
+    if (c.a.lm_tiles ? !phase_lm_tc<kNK, kLow>(cur, nb, wpre)
+                     : !phase_lm<kNK, kLow>(cur, nb, wpre))
         consumer_fail(c.a);
     if (!end_phase(&target, &nb)) return;
     if (blockIdx.x == 0) phase_accept();

@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(256) k_pf_norm_quant(const float* __restrict__
         q8_scales<1>(amv, dq, iq);
         const int kk = i % 64;
         xq[((size_t)tt * n_steps + i / 64) * kPfStepX + ((tr / 8) * 4 + kk / 16) * 128 + (tr % 8) * 16 + kk % 16] =
-            (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, iq[0]));
+            (uint8_t)q8_code_bits(__fmul_rn(v, iq[0]));
         if (lane == 0) xd[(size_t)row * (K / 32) + blk] = __half2float(__float2half_rn(dq[0]));
     }
 }
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(256) k_pf_quant(const float* __restrict__ x, i
     q8_scales<1>(amv, dq, iq);
     const int tt = row / kPfTok, tr = row % kPfTok, kk = i % 64;
     xq[((size_t)tt * n_steps + i / 64) * kPfStepX + ((tr / 8) * 4 + kk / 16) * 128 + (tr % 8) * 16 + kk % 16] =
-        (uint8_t)(int8_t)__float2int_rn(__fmul_rn(v, iq[0]));
+        (uint8_t)q8_code_bits(__fmul_rn(v, iq[0]));
     if (lane == 0) xd[(size_t)row * nb + blk] = __half2float(__float2half_rn(dq[0]));
 }
 
