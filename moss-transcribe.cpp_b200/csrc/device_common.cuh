@@ -37,6 +37,13 @@ __device__ __forceinline__ uint2 ld_nc_u2(const uint8_t* p) {
     return v;
 }
 
+// (float)c for |c| < 2^22 (an int8 x int8 block sum of 32 or 64 products is
+// at most 2^20): the int's bits added to those of 1.5 * 2^23, minus 1.5 * 2^23,
+// on the FMA and integer pipes instead of the conversion unit.  Exact.
+__device__ __forceinline__ float small_int_to_float(int c) {
+    return __fsub_rn(__int_as_float(c + 0x4B400000), 12582912.0f);
+}
+
 __device__ __forceinline__ float h2f_lo(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xffffu))); }
 __device__ __forceinline__ float h2f_hi(uint32_t v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
 

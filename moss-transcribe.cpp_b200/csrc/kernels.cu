@@ -143,14 +143,14 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
                     const float w00 = h2f_lo(sv[u].x), w01 = h2f_hi(sv[u].x);  // block 0, rows 2t, 2t+1
                     const float w10 = h2f_lo(sv[u].y), w11 = h2f_hi(sv[u].y);  // block 1
                     // d = dw * dx is exact (two fp16 values); one fmaf per block.
-                    acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
-                    acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
-                    acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
-                    acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
-                    acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
-                    acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
-                    acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
-                    acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+                    acc[0] = fmaf(small_int_to_float(c0[0]), w00 * x0g, acc[0]);
+                    acc[1] = fmaf(small_int_to_float(c0[1]), w01 * x0g, acc[1]);
+                    acc[2] = fmaf(small_int_to_float(c0[2]), w00 * x0h, acc[2]);
+                    acc[3] = fmaf(small_int_to_float(c0[3]), w01 * x0h, acc[3]);
+                    acc[0] = fmaf(small_int_to_float(c1[0]), w10 * x1g, acc[0]);
+                    acc[1] = fmaf(small_int_to_float(c1[1]), w11 * x1g, acc[1]);
+                    acc[2] = fmaf(small_int_to_float(c1[2]), w10 * x1h, acc[2]);
+                    acc[3] = fmaf(small_int_to_float(c1[3]), w11 * x1h, acc[3]);
                 }
             }
             s_part[(r * S + sl) * 32 + lane] = make_float4(acc[0], acc[1], acc[2], acc[3]);

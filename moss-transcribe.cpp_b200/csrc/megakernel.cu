@@ -755,19 +755,19 @@ __device__ __forceinline__ float4 slice_partial_regs(const uint4 (&wvs)[4], cons
         mma_s8(c1, s_act[(2 * kt + 1) * 32 + lane], wv.z, wv.w);
         const float x0g = s_d[(2 * kt) * 16 + g], x1g = s_d[(2 * kt + 1) * 16 + g];
         const float w00 = h2f_lo(sv.x), w01 = h2f_hi(sv.x), w10 = h2f_lo(sv.y), w11 = h2f_hi(sv.y);
-        acc[0] = fmaf((float)c0[0], w00 * x0g, acc[0]);
-        acc[1] = fmaf((float)c0[1], w01 * x0g, acc[1]);
+        acc[0] = fmaf(small_int_to_float(c0[0]), w00 * x0g, acc[0]);
+        acc[1] = fmaf(small_int_to_float(c0[1]), w01 * x0g, acc[1]);
         if (!kLow) {
             const float x0h = s_d[(2 * kt) * 16 + g + 8];
-            acc[2] = fmaf((float)c0[2], w00 * x0h, acc[2]);
-            acc[3] = fmaf((float)c0[3], w01 * x0h, acc[3]);
+            acc[2] = fmaf(small_int_to_float(c0[2]), w00 * x0h, acc[2]);
+            acc[3] = fmaf(small_int_to_float(c0[3]), w01 * x0h, acc[3]);
         }
-        acc[0] = fmaf((float)c1[0], w10 * x1g, acc[0]);
-        acc[1] = fmaf((float)c1[1], w11 * x1g, acc[1]);
+        acc[0] = fmaf(small_int_to_float(c1[0]), w10 * x1g, acc[0]);
+        acc[1] = fmaf(small_int_to_float(c1[1]), w11 * x1g, acc[1]);
         if (!kLow) {
             const float x1h = s_d[(2 * kt + 1) * 16 + g + 8];
-            acc[2] = fmaf((float)c1[2], w10 * x1h, acc[2]);
-            acc[3] = fmaf((float)c1[3], w11 * x1h, acc[3]);
+            acc[2] = fmaf(small_int_to_float(c1[2]), w10 * x1h, acc[2]);
+            acc[3] = fmaf(small_int_to_float(c1[3]), w11 * x1h, acc[3]);
         }
     }
     return make_float4(acc[0], acc[1], acc[2], acc[3]);

@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
                 const float2 dw2 = make_float2(dw[b], dw[b]);
 #pragma unroll
                 for (int u = 0; u < kPfHalfTok / 2; ++u) {
-                    const float2 iv = make_float2((float)(int)v[2 * u], (float)(int)v[2 * u + 1]);
+                    const float2 iv = make_float2(small_int_to_float((int)v[2 * u]), small_int_to_float((int)v[2 * u + 1]));
                     acc[u] = __ffma2_rn(iv, __fmul2_rn(dw2, dx[u]), acc[u]);
                 }
             }
