@@ -1226,7 +1226,9 @@ int mtb_resume(mtb_decoder* d, const int32_t* ids, int n_ids, int past, int max_
     d->h2d_bytes += size_t(n_ids) * 4;
     MTB_CK(d, cudaMemcpyAsync(d->b.ids, d->h_ids, size_t(n_ids) * 4, cudaMemcpyHostToDevice, d->stream));
     if (push_state(d)) return -1;
-    MTB_CK(d, cudaStreamSynchronize(d->stream));
+    // No synchronisation: the host copy of the state is what the device will
+    // hold once the copies run (every later change of it is pushed again, in
+    // stream order), so the next step needs no read-back.
     d->fresh = true;
     return 0;
 }
