@@ -101,6 +101,10 @@ int mtb_spec_params_from_env(mtb_spec_params* out);
 /* MTB_KV_F32 or MTB_KV_F16 as MTB_KV_DTYPE selects (unset: MTB_KV_F32), -1 for
  * an unknown value; needs no GPU. */
 int mtb_kv_type_from_env(void);
+/* 256-K slices per block the F16 GEMV uses for an n x k projection on the
+ * device configured last (1, 2 or 4; -1 for an invalid shape), so tests can
+ * check which block shapes a model's projections reach. */
+int mtb_f16_slices_per_block(int n, int k);
 /* Test hook (host-side fault injection): the n-th device allocation made by
  * this library from now on fails as if cudaMalloc had (n = 0: off).  The
  * failing call returns its error and leaves no allocation behind. */

@@ -749,6 +749,8 @@ int mtb_spec_params_from_env(mtb_spec_params* out) {
 
 int mtb_kv_type_from_env(void) { return kv_type_from_env(); }
 
+int mtb_f16_slices_per_block(int n, int k) { return n > 0 && k > 0 && k % 256 == 0 ? f16_spb(n, k) : -1; }
+
 int mtb_bounds_check_enabled(void) {
 #ifdef MTB_BOUNDS_CHECK
     return 1;

@@ -21,6 +21,10 @@
 
 namespace mtb {
 
+// SMs of the device the kernels were last configured for (configure_kernels,
+// at model load); the grid choices below are made for it.
+static int g_sm_count = 148;
+
 namespace {
 
 using namespace dev;
@@ -1185,24 +1189,26 @@ __global__ void k_kv_gather(KvCache kv, int n_kv, int layer, int which, int pos0
 // ============================================================ launchers
 
 void launch_repack_f16(const uint16_t* src, int n, int k, uint16_t* dst, cudaStream_t s) {
-    k_repack_f16<<<148 * 8, 256, 0, s>>>(reinterpret_cast<const uint4*>(src), n, k, reinterpret_cast<__half*>(dst));
+    k_repack_f16<<<g_sm_count * 8, 256, 0, s>>>(reinterpret_cast<const uint4*>(src), n, k, reinterpret_cast<__half*>(dst));
 }
 
 void launch_repack_q8(const uint8_t* src, int n_rows, int k, uint8_t* dst, int rg_stride, int rg_offset,
                       cudaStream_t s) {
     const long long work = (long long)(n_rows / kTileRows) * (k / kTileK) * 32;
-    const int grid = (int)std::min<long long>((work + 255) / 256, 148LL * 16);
+    const int grid = (int)std::min<long long>((work + 255) / 256, 16LL * g_sm_count);
     k_repack_q8<<<grid, 256, 0, s>>>(src, n_rows, k, dst, rg_stride, rg_offset);
 }
 
 int lm_head_blocks(int vocab) {
     const int n_rg = vocab / kTileRows;
-    return std::min(kLmHeadMaxBlocks, (n_rg + 7) / 8);
+    return std::min(std::min(kLmHeadMaxBlocks, 4 * g_sm_count), (n_rg + 7) / 8);
 }
 
 static void configure_f16_kernels();
 
 cudaError_t configure_kernels() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&g_sm_count, cudaDevAttrMultiProcessorCount, dev);
     // Dynamic shared memory above 48 KB is opt-in per kernel (current device).
     cudaFuncSetAttribute(k_gemv<EPI_STORE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     cudaFuncSetAttribute(k_gemv<EPI_RESID, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -1479,10 +1485,10 @@ static size_t gemv_f16_smem(int spb) {
 // Slices per block: the most of 4, 2, 1 (dividing K / 256) that still gives
 // at least two blocks per SM; measured on the Qwen3-0.6B F16 step, more and
 // shorter blocks beat fewer, longer ones until the grid fills the GPU twice.
-static int f16_spb(int N, int K) {
+int f16_spb(int N, int K) {
     const int ns = K >> 8, groups = (N + kF16Outs - 1) / kF16Outs;
     for (int spb : {kF16MaxSpb, 2})
-        if (ns % spb == 0 && groups * (ns / spb) >= 2 * 148) return spb;
+        if (ns % spb == 0 && groups * (ns / spb) >= 2 * g_sm_count) return spb;
     return 1;
 }
 
@@ -1778,16 +1784,16 @@ void launch_logits_row(const DeviceModel& m, const StepBuffers& b, const float* 
 }
 
 void launch_fill_synthetic_kv(const DeviceModel& m, const KvCache& kv, int n_pos, uint32_t seed, cudaStream_t s) {
-    k_fill_synthetic_kv<<<148 * 8, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, n_pos, seed);
+    k_fill_synthetic_kv<<<g_sm_count * 8, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, n_pos, seed);
 }
 
 void launch_poison_kv(const DeviceModel& m, const KvCache& kv, int pos0, int n_pos, cudaStream_t s) {
-    k_poison_kv<<<148 * 4, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, pos0, n_pos);
+    k_poison_kv<<<g_sm_count * 4, 256, 0, s>>>(kv, m.dims.n_layers, m.dims.n_kv, pos0, n_pos);
 }
 
 void launch_kv_gather(const DeviceModel& m, const KvCache& kv, int layer, int which, int pos0, int n_pos, float* out,
                       cudaStream_t s) {
-    k_kv_gather<<<148, 256, 0, s>>>(kv, m.dims.n_kv, layer, which, pos0, n_pos, out);
+    k_kv_gather<<<g_sm_count, 256, 0, s>>>(kv, m.dims.n_kv, layer, which, pos0, n_pos, out);
 }
 
 MTB_BC_TAKE(bc_take_kernels)

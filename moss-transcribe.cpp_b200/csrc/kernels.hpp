@@ -159,6 +159,8 @@ void launch_prefill_seed(const StepBuffers& b, cudaStream_t s);
 // Upper bound of lm_head_blocks(): four blocks per SM of a 148-SM B200 (the
 // grid is tuned for that part; other SM counts only change the tuning).
 constexpr int kLmHeadMaxBlocks = 148 * 4;
+// Slices of 256 K per block of the F16 GEMV for an N x K projection (1, 2 or 4).
+int f16_spb(int N, int K);
 int lm_head_blocks(int vocab);
 
 // Persistent verify step (megakernel.cu).

@@ -98,6 +98,7 @@ SIGNATURES = {
     "mtb_spec_params_from_env": (C.c_int, [C.POINTER(SpecParams)]),
     "mtb_kv_type_from_env": (C.c_int, []),
     "mtb_debug_fail_alloc": (None, [C.c_int]),
+    "mtb_f16_slices_per_block": (C.c_int, [C.c_int, C.c_int]),
     "mtb_bounds_check_enabled": (C.c_int, []),
     "mtb_bounds_check_status": (C.c_int, [C.c_int]),
     "mtb_format_generation_log": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, C.c_double, C.c_double, C.c_int,

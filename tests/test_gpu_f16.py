@@ -105,18 +105,25 @@ def test_f16_group_step_is_rejected(gpu_f16):
 
 
 def test_f16_full_model_prefill_step_and_lm_head_bit_exact():
-    """The Qwen3-0.6B shape with F16 weights (the configs[2] decoder).  Its
-    K of 1024, 2048 and 3072 run the GEMV blocks of four 256-element slices
-    (whole for K = 1024, split two and three ways for the O and down
-    projections); the tiny model's K of 256 and 512 run one-slice blocks.  So
-    this covers them: hidden rows of a prefill and of the verify steps, the
-    last row's logits, ids and counters."""
+    """The Qwen3-0.6B shape with F16 weights (the configs[2] decoder).  On
+    a 148-SM B200 its projections take every F16 GEMV block shape: QKV, O and
+    down run one 256-element slice per block (the split-K path, each output's
+    slice totals added by the block that finishes last), gate/up two slices and
+    the LM head four (asserted below, so a change of the rule cannot drop one
+    from this test).  Hidden rows of a prefill and of the verify steps, the
+    last row's logits, ids and counters, bit for bit."""
     import os
     from mtb import fixture
     path = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0, dtype="f16")
     oracle.set_threads(os.cpu_count() or 8)
     om = oracle.OracleModel(path)
     gm = capi.Model(path, 0)
+    H, F, V = om.shape.hidden, om.shape.ffn, om.shape.vocab
+    qkv = om.shape.n_heads * 128 + 2 * om.shape.n_kv_heads * 128
+    spb = capi.lib().mtb_f16_slices_per_block
+    shapes = {"qkv": (qkv, H), "o": (H, om.shape.n_heads * 128), "gate_up": (2 * F, H), "down": (H, F), "lm": (V, H)}
+    got = {name: spb(n, k) for name, (n, k) in shapes.items()}
+    assert got == {"qkv": 1, "o": 1, "gate_up": 2, "down": 1, "lm": 4}, got
     rng = np.random.default_rng(11)
     prompt = np.concatenate([rng.standard_normal((20, om.shape.hidden)).astype(np.float32),
                              om.embed(fixture.lcg_ids(12, om.shape.vocab, seed=4))])
