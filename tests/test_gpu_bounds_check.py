@@ -1,7 +1,8 @@
 """The bounds-check build (libmoss_transcribe_b200_bc.so, -DMTB_BOUNDS_CHECK):
-the same parity cases with every cache position, page-table entry, partial
-buffer and step row count checked on the device, run in a child process that
-loads that build; no check may fire and the results stay bit-exact.  The
+the same parity cases (single decoders with both cache types, a group step of
+three decoders, a Qwen3-0.6B verify step) with every cache position,
+page-table entry, partial buffer and step row count checked on the device,
+run in a child process that loads that build; no check may fire and the results stay bit-exact.  The
 checked build stands in for compute-sanitizer, which this pool does not offer."""
 import json
 import os
@@ -37,6 +38,22 @@ for kv in (capi.KV_F32, capi.KV_F16):
     res.append(got == want)
 out["tiny_ids_equal"] = res
 out["status_after_tiny"] = L.mtb_bounds_check_status(0)
+# A group of three decoders (different prompts and caches) stepped as one
+# persistent launch per step, each against its own oracle decoder.
+group_ok = []
+decs = [capi.Decoder(model, 256, capi.KV_F16, max_new=40) for _ in range(3)]
+prompts = [fixture.synthetic_prompt(m.arrays["token_embd.weight"], m.shape, n_audio=30 + 9 * i, n_text=6, seed=20 + i)
+           for i in range(3)]
+for d, pr in zip(decs, prompts):
+    d.spec_prime(pr, 40, -1, k_max=4, n_min=2, n_max=3)
+capi.spec_run_group(decs)
+for d, pr in zip(decs, prompts):
+    od = oracle.OracleDecoder(m, 256, kv_fp16=True)
+    want = od.spec_generate(pr, 40, -1, k_max=4, n_min=2, n_max=3)[0]
+    group_ok.append(d.read_ids()[0] == want)
+    d.close()
+out["group_ids_equal"] = group_ok
+out["status_after_group"] = L.mtb_bounds_check_status(0)
 # Qwen3-0.6B shape: one T = 8 verify step against a 2048-position fp16 cache
 # through the persistent kernel (NaN pages beyond the valid positions).
 full = fixture.cached_fixture(fixture.QWEN3_0_6B, seed=0)
@@ -65,6 +82,8 @@ def test_checked_build_runs_parity_cases_without_violations(tiny_gguf):
     assert out["enabled"] == 1
     assert out["tiny_ids_equal"] == [True, True]
     assert out["status_after_tiny"] == 0
+    assert out["group_ids_equal"] == [True, True, True]
+    assert out["status_after_group"] == 0
     assert out["full_step_rows"] == 8
     assert out["status_after_full"] == 0
 
