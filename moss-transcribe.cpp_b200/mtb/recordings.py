@@ -48,27 +48,31 @@ def decode_recordings(model, recordings: list[Recording], kv_type=None, k_max: i
                       n_max: int = 3, group_size: int = GROUP_MAX):
     """Decode recordings on `model`'s GPU in groups of `group_size`: each
     member prefilled (mtb_spec_prime), then group steps until all stopped
-    (mtb_spec_run_group).  Returns [(ids, counters)] in input order."""
+    (mtb_spec_run_group).  One set of decoders, sized for the largest
+    recording, serves every group (priming resets a decoder), so the caches
+    and step graphs are made once per GPU, not once per group.  Returns
+    [(ids, counters)] in input order."""
     from . import capi
     kv_type = capi.KV_F16 if kv_type is None else kv_type
+    recordings = list(recordings)
+    if not recordings:
+        return []
+    max_seq = max(r.rows.shape[0] + r.max_new for r in recordings) + 64
+    max_new = max(r.max_new for r in recordings)
     out = []
-    for group in groups_of(list(recordings), group_size):
-        # The first decoder of a group needs the largest cache (its step buffers serve all).
-        order = sorted(range(len(group)), key=lambda j: -(group[j].rows.shape[0] + group[j].max_new))
-        decs = [None] * len(group)
-        try:
-            for j in order:
-                r = group[j]
-                decs[j] = capi.Decoder(model, r.rows.shape[0] + r.max_new + 64, kv_type, max_new=r.max_new)
-            for j in order:
-                r = group[j]
-                decs[j].spec_prime(r.rows, r.max_new, r.eos, k_max=k_max, n_min=n_min, n_max=n_max)
-            capi.spec_run_group([decs[j] for j in order])
+    pool = []
+    try:
+        for _ in range(min(group_size, len(recordings))):
+            pool.append(capi.Decoder(model, max_seq, kv_type, max_new=max_new))
+        for group in groups_of(recordings, group_size):
+            decs = pool[:len(group)]
+            for d, r in zip(decs, group):
+                d.spec_prime(r.rows, r.max_new, r.eos, k_max=k_max, n_min=n_min, n_max=n_max)
+            capi.spec_run_group(decs)
             out.extend(d.read_ids() for d in decs)
-        finally:
-            for d in decs:
-                if d is not None:
-                    d.close()
+    finally:
+        for d in pool:
+            d.close()
     return out
 
 
