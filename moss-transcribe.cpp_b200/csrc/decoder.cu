@@ -63,6 +63,7 @@ struct mtb_decoder {
     float* h_rows = nullptr;       // pinned staging [kTMax][hidden]
     int32_t* h_ids = nullptr;      // pinned [max_new]
     int* h_flag = nullptr;         // pinned [2]
+    int* group_flag = nullptr;     // device [2]: a group run's "every member stopped", one per step parity
     StepState* snap_state = nullptr;
     int32_t* snap_ids = nullptr;
     int32_t* scratch_i = nullptr;  // [max_new + 16]
@@ -903,6 +904,7 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
             dalloc(A, E, &b.lm_val, size_t(b.lm_blocks) * 16 * sizeof(float2)) ||
             dalloc(A, E, &b.logits, size_t(kTMax) * dm.vocab * 4) || dalloc(A, E, &d->snap_state, sizeof(StepState)) ||
             dalloc(A, E, &d->snap_ids, size_t(max_new) * 4) || dalloc(A, E, &d->scratch_i, size_t(max_new + 16) * 4) ||
+            dalloc(A, E, &d->group_flag, 2 * sizeof(int)) ||
             dalloc(A, E, &d->scratch_n, 64) || dalloc(A, E, &d->row_buf, size_t(H) * 4))
             return bail();
         if (f16 && (dalloc(A, E, &b.act_h, size_t(kTMax) * kmax * 2) || dalloc(A, E, &b.act_h2, size_t(kTMax) * F * 2) ||
@@ -1357,21 +1359,42 @@ int mtb_spec_run_group(mtb_decoder* const* ds, int n, int max_steps, int* steps_
     if (check_group(ds, n)) return -1;
     mtb_decoder* d0 = ds[0];
     cudaSetDevice(d0->device);
-    // Device-driven loop: the host reads the members' stop flags one step behind.
+    // Device-driven loop on the first member's stream: the members' earlier
+    // work is ordered before it once (events), then each step is two launches
+    // (the members' drafts in one kernel, the verify step) and a one-int flag
+    // copy; the host reads the flag one step behind.  The final
+    // synchronisation orders the members' later work after the loop.
+    for (int k = 1; k < n; ++k) {
+        MTB_CK(d0, cudaEventRecord(ds[k]->group_ev, ds[k]->stream));
+        MTB_CK(d0, cudaStreamWaitEvent(d0->stream, ds[k]->group_ev, 0));
+    }
+    DraftGroup g{};
+    KvCache kvs[kMaxStreams];
+    KvTensorMap maps[kMaxStreams];
+    StepState* states[kMaxStreams];
+    int32_t* idv[kMaxStreams];
+    g.n = n;
+    for (int k = 0; k < n; ++k) {
+        g.st[k] = states[k] = ds[k]->b.state;
+        g.ids[k] = idv[k] = ds[k]->b.ids;
+        kvs[k] = ds[k]->kv;
+        maps[k] = ds[k]->kv_map;
+    }
+    const mtb_model* m = d0->model;
     int i = 0;
     for (; max_steps <= 0 || i < max_steps; ++i) {
-        if (group_step(ds, n)) return -1;
-        for (int k = 0; k < n; ++k) {
-            MTB_CK(d0, cudaMemcpyAsync(&ds[k]->h_flag[i & 1], &ds[k]->b.state->stop, sizeof(int),
-                                       cudaMemcpyDeviceToHost, d0->stream));
-            ds[k]->d2h_bytes += sizeof(int);
-        }
+        for (int k = 0; k < n; ++k) ds[k]->fresh = false;
+        launch_draft_group(g, d0->stream);
+        MTB_CK(d0, launch_step_persistent_group(m->dm, m->layers_dev, kvs, maps, states, idv, n, d0->b, d0->mb,
+                                                m->mega_grid, d0->stream));
+        launch_group_stopped(g, d0->group_flag + (i & 1), d0->stream);
+        MTB_CK(d0, cudaMemcpyAsync(&d0->h_flag[i & 1], d0->group_flag + (i & 1), sizeof(int), cudaMemcpyDeviceToHost,
+                                   d0->stream));
+        d0->d2h_bytes += sizeof(int);
         MTB_CK(d0, cudaEventRecord(d0->ev[i & 1], d0->stream));
         if (i > 0) {
             MTB_CK(d0, cudaEventSynchronize(d0->ev[(i - 1) & 1]));
-            bool all = true;
-            for (int k = 0; k < n; ++k) all = all && ds[k]->h_flag[(i - 1) & 1] != STOP_NONE;
-            if (all) { ++i; break; }
+            if (d0->h_flag[(i - 1) & 1]) { ++i; break; }
         }
     }
     MTB_CK(d0, cudaStreamSynchronize(d0->stream));

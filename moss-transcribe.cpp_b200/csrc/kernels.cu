@@ -946,7 +946,7 @@ __device__ int draft_search(const int32_t* __restrict__ ids, int n, int budget, 
     return best ? (int)(best & 0xffffffffu) : -1;
 }
 
-__global__ void __launch_bounds__(256) k_draft(StepState* st, const int32_t* __restrict__ ids) {
+__device__ __forceinline__ void draft_member(StepState* st, const int32_t* __restrict__ ids) {
     if (st->stop != STOP_NONE) {
         if (threadIdx.x == 0) st->T = 0;
         return;
@@ -967,6 +967,17 @@ __global__ void __launch_bounds__(256) k_draft(StepState* st, const int32_t* __r
         st->T = 1 + np;
         st->before = st->past;
     }
+}
+
+__global__ void __launch_bounds__(256) k_draft(StepState* st, const int32_t* __restrict__ ids) { draft_member(st, ids); }
+
+__global__ void __launch_bounds__(256) k_draft_group(DraftGroup g) { draft_member(g.st[blockIdx.x], g.ids[blockIdx.x]); }
+
+__global__ void k_group_stopped(DraftGroup g, int* flag) {
+    const int k = threadIdx.x;
+    const bool stopped = k >= g.n || g.st[k]->stop != STOP_NONE;
+    const unsigned all = __all_sync(0xffffffffu, stopped);
+    if (k == 0) *flag = all ? 1 : 0;
 }
 
 // The same search on explicit arguments (mtb_ngram_draft).
@@ -1703,6 +1714,10 @@ void launch_step(const DeviceModel& m, const KvCache& kv, const StepBuffers& b, 
     }
     k_accept<<<1, 512, 0, s>>>(b.state, b.ids, b.lm_val, b.lm_blocks, penalty_path ? 1 : 0);
 }
+
+void launch_draft_group(const DraftGroup& g, cudaStream_t s) { k_draft_group<<<g.n, 256, 0, s>>>(g); }
+
+void launch_group_stopped(const DraftGroup& g, int* flag, cudaStream_t s) { k_group_stopped<<<1, 32, 0, s>>>(g, flag); }
 
 void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s) {
     if (draft_mode == 0) k_draft<<<1, 256, 0, s>>>(b.state, b.ids);

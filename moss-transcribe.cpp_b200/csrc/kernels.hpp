@@ -188,6 +188,16 @@ cudaError_t launch_step_persistent_group(const DeviceModel& m, const LayerWeight
                                          cudaStream_t s);
 // The draft part of a step alone (0: on-device n-gram, 1: host-forced proposal).
 void launch_draft(const StepBuffers& b, int draft_mode, cudaStream_t s);
+// The device n-gram drafts of a group's members (one block each, the draft of
+// launch_draft mode 0), and the group's "every member stopped" flag (1 or 0)
+// into *flag: a group step's host work is two launches, not one per member.
+struct DraftGroup {
+    StepState* st[kMaxStreams];
+    const int32_t* ids[kMaxStreams];
+    int n;
+};
+void launch_draft_group(const DraftGroup& g, cudaStream_t s);
+void launch_group_stopped(const DraftGroup& g, int* flag, cudaStream_t s);
 cudaError_t configure_kernels();
 void launch_draft_args(const int32_t* ids, int n, int maximum, int n_min, int n_max, int32_t* out, int* n_out,
                        cudaStream_t s);
