@@ -184,7 +184,11 @@ int mtb_spec_step(mtb_decoder* d, const int32_t* draft, int n_draft, mtb_counter
 int mtb_spec_step_async(mtb_decoder* d, const int32_t* draft_device, int n_draft);
 /* Set the decode parameters and prefill the fused rows (the first id is
  * emitted), without decoding: the start of mtb_spec_generate
- * (src/cpu_speculative.cpp:68-99), for decoders stepped as a group. */
+ * (src/cpu_speculative.cpp:68-99), for decoders stepped as a group.  Returns
+ * once the prefill is queued on the decoder's stream (the rows have been
+ * copied out of `fused`), so the members of a group prefill side by side; a
+ * prefill that fails on the device is reported by the next call that reads
+ * the decoder's state back (mtb_spec_run_group, mtb_read_ids, ...). */
 int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int eos, const mtb_spec_params* params);
 /* One verify step of n decoders (1..8) created from the same model, as ONE
  * persistent launch: each decoder drafts on the device; their rows (seed +

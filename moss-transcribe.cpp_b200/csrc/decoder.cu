@@ -63,6 +63,8 @@ struct mtb_decoder {
     float* h_rows = nullptr;       // pinned staging [kTMax][hidden]
     int32_t* h_ids = nullptr;      // pinned [max_new]
     int* h_flag = nullptr;         // pinned [2]
+    int* h_pf_status = nullptr;    // pinned: a deferred prefill's status word (pf_status_pending)
+    bool pf_status_pending = false;
     int* group_flag = nullptr;     // device [2]: a group run's "every member stopped", one per step parity
     StepState* snap_state = nullptr;
     int32_t* snap_ids = nullptr;
@@ -98,6 +100,7 @@ struct mtb_decoder {
         if (h_rows) cudaFreeHost(h_rows);
         if (h_ids) cudaFreeHost(h_ids);
         if (h_flag) cudaFreeHost(h_flag);
+        if (h_pf_status) cudaFreeHost(h_pf_status);
         if (stream) cudaStreamDestroy(stream);
     }
 };
@@ -385,6 +388,10 @@ int refresh(mtb_decoder* d) {
     d->d2h_bytes += sizeof(StepState);
     MTB_CK(d, cudaMemcpyAsync(d->h_state, d->b.state, sizeof(StepState), cudaMemcpyDeviceToHost, d->stream));
     MTB_CK(d, cudaStreamSynchronize(d->stream));
+    if (d->pf_status_pending) {
+        d->pf_status_pending = false;
+        if (*d->h_pf_status) return fail(d->error, "prefill projection gave up waiting (tcgen05 pipeline timeout)");
+    }
     if (d->h_state->error) {
         d->error = d->h_state->error == 2   ? "verify step gave up waiting (persistent kernel timeout)"
                    : d->h_state->error == 3 ? "persistent kernel: shared-memory ring not 1024-byte aligned"
@@ -463,7 +470,7 @@ int prefill_pass_rows(const mtb_decoder* d, int remaining, int before) {
 // final-normed rows.  At most kTMax rows: one step of the verify kernels.  The
 // host's past (h_state) is current on entry.
 int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_out, bool lm_on_last,
-                      bool rows_on_device = false) {
+                      bool rows_on_device = false, bool defer_status = false) {
     d->fresh = false;  // device work below changes the step state
     const int H = d->model->dm.dims.hidden;
     const cudaMemcpyKind in_kind = rows_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -490,11 +497,21 @@ int forward_host_rows(mtb_decoder* d, const float* rows, int T, float* hidden_ou
             if (lm_on_last && last) launch_lm_row(d->model->dm, d->b, d->pf.hid + size_t(P - 1) * H, d->stream);
             done += P;
         }
-        int status = 0;
-        MTB_CK(d, cudaMemcpyAsync(&status, d->pf.status, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
-        MTB_CK(d, cudaStreamSynchronize(d->stream));
-        if (status) return fail(d->error, "prefill projection gave up waiting (tcgen05 pipeline timeout)");
-        d->h_state->past = past + done;
+        if (defer_status) {
+            // Checked by the next refresh(): the caller does not wait here, so
+            // several decoders' prefills can run side by side on their streams.
+            MTB_CK(d, cudaMemcpyAsync(d->h_pf_status, d->pf.status, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+            d->pf_status_pending = true;
+        } else {
+            int status = 0;
+            MTB_CK(d, cudaMemcpyAsync(&status, d->pf.status, sizeof(int), cudaMemcpyDeviceToHost, d->stream));
+            MTB_CK(d, cudaStreamSynchronize(d->stream));
+            if (status) return fail(d->error, "prefill projection gave up waiting (tcgen05 pipeline timeout)");
+            d->h_state->past = past + done;
+        }
+        // Deferred: the pinned state mirror is not written while its push may
+        // still be pending; the device holds the new past (k_rows_end) and the
+        // mirror is refreshed before any host use (fresh is false).
     }
     for (int r0 = done; r0 < T; r0 += kTMax) {
         const int n = std::min(kTMax, T - r0);
@@ -667,14 +684,14 @@ void clear_progress(StepState& s) {
     s.target_calls = s.drafted_calls = s.proposed = s.accepted = s.target_input_tokens = s.rewinds = 0;
 }
 
-int prefill(mtb_decoder* d, const float* fused, int seq, bool on_device = false) {
+int prefill(mtb_decoder* d, const float* fused, int seq, bool on_device = false, bool defer_status = false) {
     d->fresh = false;  // device work below changes the step state
     if (!fused || seq <= 0) return fail(d->error, "empty prompt");
     if (seq + 1 > d->max_seq) return fail(d->error, "prompt exceeds max_seq");
     d->h_state->past = 0;
     clear_progress(*d->h_state);
     if (push_state(d)) return -1;
-    if (forward_host_rows(d, fused, seq, nullptr, true, on_device)) return -1;
+    if (forward_host_rows(d, fused, seq, nullptr, true, on_device, defer_status)) return -1;
     launch_prefill_seed(d->b, d->stream);
     MTB_CK(d, cudaGetLastError());
     return 0;
@@ -943,7 +960,8 @@ int mtb_decoder_create(mtb_model* m, int max_seq, int kv_type, int max_new, mtb_
         if (cudaMallocHost(&d->h_state, sizeof(StepState)) != cudaSuccess ||
             cudaMallocHost(&d->h_rows, size_t(kTMax) * H * 4) != cudaSuccess ||
             cudaMallocHost(&d->h_ids, size_t(max_new) * 4) != cudaSuccess ||
-            cudaMallocHost(&d->h_flag, 2 * sizeof(int)) != cudaSuccess) {
+            cudaMallocHost(&d->h_flag, 2 * sizeof(int)) != cudaSuccess ||
+            cudaMallocHost(&d->h_pf_status, sizeof(int)) != cudaSuccess) {
             d->error = "pinned host allocation failed";
             return bail();
         }
@@ -1285,7 +1303,9 @@ int mtb_spec_prime(mtb_decoder* d, const float* fused, int seq, int max_new, int
         cudaSetDevice(d->device);
         if (refresh(d)) return -1;
         if (set_params(d, max_new, eos, params)) return -1;
-        return prefill(d, fused, seq);
+        // No wait for the prefill: a group's members prime one after another
+        // and their prefills overlap on their own streams.
+        return prefill(d, fused, seq, false, true);
     } catch (const std::exception& e) {
         d->error = e.what();
         return -1;
