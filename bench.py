@@ -256,7 +256,7 @@ def main(argv=None):
     ap.add_argument("--f16", action="store_true",
                     help="the same verify-step microbench on the F16-weight decoder of configs[2] "
                          "(no side measurements, no CPU baseline)")
-    ap.add_argument("--only", choices=["long_context", "recordings", "config0"],
+    ap.add_argument("--only", choices=["long_context", "recordings", "config0", "audio"],
                     help="run one side measurement alone and print it as one JSON line (profiling runs)")
     args = ap.parse_args(argv)
     if args.f16:
@@ -286,6 +286,11 @@ def main(argv=None):
         return
 
     from mtb import capi
+    if args.only == "audio":
+        line = audio_front_end(capi, fixture, local, cpu=rank == 0 and world == 1 and not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps({args.only: line}))
+        return
     model = capi.Model(path, local)
     if args.only:
         if args.only == "long_context":
@@ -360,7 +365,7 @@ def main(argv=None):
            "d2h_bytes_per_step": (h1[1] - h0[1]) // n_e2e,
            "ms_per_step": e2e_s * 1e3 / n_e2e}
 
-    prefill = ms_line = lc_line = f16_line = c0_line = rec_line = None
+    prefill = ms_line = lc_line = f16_line = c0_line = rec_line = audio_line = None
     if not args.no_extras and model.persistent_grid > 0:
         rec_line = recordings_line(model, capi, dist, torch, rank, local, world)
     if not args.no_extras and world == 1:  # per-GPU side measurements: the N=1 run carries them
@@ -391,6 +396,7 @@ def main(argv=None):
         c0_line = config0(model, capi, fixture)
         lc_line = long_context(model, capi, seed_tok)
         f16_line = f16_recording(capi, fixture, local)
+        audio_line = audio_front_end(capi, fixture, local, cpu=not args.no_cpu_baseline)
         prefill = {"rows": PREFILL_ROWS, "ms": round(pf_s * 1e3, 3), "rows_per_s": round(PREFILL_ROWS / pf_s, 1),
                    "long": {"rows": PREFILL_LONG_ROWS, "ms": round(pl_s * 1e3, 1),
                             "rows_per_s": round(PREFILL_LONG_ROWS / pl_s, 1)},
@@ -413,7 +419,7 @@ def main(argv=None):
             "data": "synthetic", "config": config,
             "roofline": roofline, "e2e": e2e, "gpu_launches": launches * args.steps, "clocks": clk,
             "prefill": prefill, "recordings": rec_line, "config0": c0_line, "multi_stream": ms_line,
-            "long_context": lc_line, "f16_recording": f16_line}
+            "long_context": lc_line, "f16_recording": f16_line, "audio_front_end": audio_line}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(path, 5)
     if rank == 0:
@@ -423,6 +429,55 @@ def main(argv=None):
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def audio_front_end(capi, fixture, device: int, cpu: bool = True) -> dict:
+    """Row (f)4: the audio front end (log-mel, the 24-layer Whisper-Medium
+    encoder, the adaptor) of a random-init GGUF on one GPU, through the public
+    mtb_audio_encode call with host samples in and host rows out: one 30 s
+    chunk (375 rows) and configs[2]'s five chunks (1875 rows).  CPU baseline:
+    the C restatement on one chunk, all host threads."""
+    path = fixture.cached_audio_fixture(fixture.WHISPER_MEDIUM, seed=0)
+    enc = capi.AudioEncoder(path, device)
+    s = fixture.WHISPER_MEDIUM
+    out = {"model": "Whisper-Medium encoder (24 x 1024, 16 heads, ffn 4096) + adaptor -> 1024, random-init q8_0",
+           "timing": "host wall clock around mtb_audio_encode (samples host->device, rows device->host), median of 5; "
+                     "device_ms from CUDA events around the same call"}
+    # Work per chunk: q8_0 linears (int8 ops) and the F32 attention and conv stem (flops).
+    T, d = s.enc_frames, s.d_model
+    lin = 2 * T * (4 * d * d + 2 * d * s.ffn) * s.n_layers
+    att = 2 * 2 * T * T * d * s.n_layers
+    conv = 2 * (s.n_frames * d * 3 * s.n_mels + T * d * 3 * d)
+    for name, n in (("chunk_30s", s.n_samples), ("configs2_150s", 5 * s.n_samples)):
+        x = fixture.synthetic_pcm(n, seed=7)
+        enc.encode(x)
+        walls, devs = [], []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            rows = enc.encode(x)
+            walls.append(time.perf_counter() - t0)
+            devs.append(enc.last_ms())
+        w = statistics.median(walls)
+        chunks = (n + s.n_samples - 1) // s.n_samples
+        out[name] = {"samples": n, "rows": int(rows.shape[0]), "ms": round(w * 1e3, 2),
+                     "device_ms": round(statistics.median(devs), 2), "realtime_x": round(n / 16000 / w, 1),
+                     "rows_per_s": round(rows.shape[0] / w, 1),
+                     "tera_ops_per_s": round(chunks * (lin + att + conv) / (statistics.median(devs) / 1e3) / 1e12, 1)}
+    out["ops_per_chunk"] = {"int8_linear": lin, "f32_attention": att, "f32_conv": conv}
+    enc.close()
+    if cpu:
+        import oracle
+        oracle.use_native()
+        cores = os.cpu_count() or 1
+        oracle.set_threads(cores)
+        oa = oracle.OracleAudio(path)
+        x = fixture.synthetic_pcm(s.n_samples, seed=7)
+        t0 = time.perf_counter()
+        oa.encode(x)
+        t = time.perf_counter() - t0
+        out["cpu_baseline"] = {"ms_per_chunk": round(t * 1e3, 1), "cores": cores, "kind": "port",
+                               "sample": f"one 30 s chunk, C restatement -O3 -march=native ({oracle.host_isa()})"}
+    return out
 
 
 def recordings_line(model, capi, dist, torch, rank: int, local: int, world: int) -> dict:

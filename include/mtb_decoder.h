@@ -267,6 +267,37 @@ int mtb_greedy_choice(mtb_decoder* d, const float* raw, int n_raw, const int32_t
 int mtb_lm_head_argmax_noalloc(const mtb_model* m, const float* hidden_rows, int T, int32_t* choices, void* stream);
 const char* mtb_noalloc_error(void);
 
+/* ---- Audio front end: 16 kHz samples -> the decoder's audio embedding rows ----
+ * Replaces mt::AudioEncoder (src/audio_encoder.hpp:23-34, src/audio_encoder.cpp:16-75):
+ * WhisperMel::compute (src/mel.cpp:153-224), WhisperEncoder::encode
+ * (src/whisper_encoder.cpp:98-207) and AudioAdaptor::apply
+ * (src/audio_adaptor.cpp:39-96), all on the device.  The GGUF is the one the
+ * decoder loads (mtd.audio.*, mtd.feat.*, mel_filters, enc.*, adaptor.*);
+ * the encoder and adaptor linear weights must be q8_0. */
+typedef struct mtb_audio mtb_audio;
+int mtb_audio_load(const char* gguf_path, int device, mtb_audio** out);
+void mtb_audio_free(mtb_audio* a);
+/* The object's last error, or the last load error of this thread for NULL. */
+const char* mtb_audio_error(const mtb_audio* a);
+/* dims[10]: hidden, d_model, n_layers, n_heads, ffn, n_mels, mel frames per
+ * chunk, samples per chunk, encoder frames per chunk, merge size. */
+int mtb_audio_dims(const mtb_audio* a, int32_t* dims);
+/* Sum over 30 s chunks of token_len = (unpadded - 1) / (hop * 2 * merge) + 1:
+ * the rows mtb_audio_encode returns for n_samples samples. */
+int mtb_audio_tokens(const mtb_audio* a, int n_samples);
+/* AudioEncoder::encode: host samples -> host rows out[n_tokens][hidden]
+ * (max_tokens rows available).  Empty input and a too-small output are
+ * errors, as in the reference. */
+int mtb_audio_encode(mtb_audio* a, const float* samples16k, int n_samples, float* out, int max_tokens,
+                     int* n_tokens);
+/* Device time of the last mtb_audio_encode (host copies included), ms. */
+float mtb_audio_last_ms(const mtb_audio* a);
+/* Test read-back of one chunk: mel [n_mels][frames] (after the chunk
+ * normalisation) and the encoder output [encoder frames][d_model] (after the
+ * final LayerNorm, before the trim); n_samples <= samples per chunk (the rest
+ * is zero-padded as in encode); either output may be NULL. */
+int mtb_audio_debug_chunk(mtb_audio* a, const float* samples, int n_samples, float* mel_out, float* enc_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -87,4 +87,31 @@ __device__ __forceinline__ void exact_sincosf(float x, float* s_out, float* c_ou
     *c_out = (float)co;
 }
 
+// erf: the Maclaurin series erf x = (2 / sqrt pi) sum_n (-1)^n x^(2n+1) / (n! (2n+1))
+// in double, every operation rounded separately: t_n = (t_(n-1) * -x^2) * (1 / n),
+// s += t_n * (1 / (2n + 1)) from s = t_0 = x, until the added term is at most
+// 2^-60 of the sum (at most 128 terms), then s * 2/sqrt(pi) rounded to float.
+// |x| >= 4 gives +-1 (erf there rounds to +-1 in float).  The reciprocals are the
+// correctly rounded doubles; the cancellation of the alternating series costs at
+// most ~1e-10 absolute below |x| = 4, so the float result is the correctly rounded
+// one except near ties.
+__device__ __forceinline__ float exact_erff(float xf) {
+    const double x = (double)xf;
+    if (!(fabs(x) < 4.0)) return xf != xf ? xf : (xf > 0.0f ? 1.0f : -1.0f);
+    const double mx2 = __dmul_rn(-x, x);
+    double term = x, sum = x;
+    for (int n = 1; n <= 128; ++n) {
+        term = __dmul_rn(__dmul_rn(term, mx2), __drcp_rn((double)n));
+        const double add = __dmul_rn(term, __drcp_rn((double)(2 * n + 1)));
+        sum = __dadd_rn(sum, add);
+        if (fabs(add) <= fabs(sum) * 8.673617379884035e-19) break;  // 2^-60
+    }
+    return (float)__dmul_rn(sum, 1.1283791670955126);  // 2 / sqrt(pi)
+}
+
+// GELU, erf form (ggml_vec_gelu_erf_f32): (0.5 x)(1 + erf(x / sqrt 2)).
+__device__ __forceinline__ float exact_gelu_erf(float v) {
+    return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, exact_erff(__fmul_rn(v, 0.707106781f))));
+}
+
 }  // namespace mtb

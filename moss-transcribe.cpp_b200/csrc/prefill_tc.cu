@@ -23,6 +23,7 @@
 // go through one __fmul2_rn and one __ffma2_rn, each half its own chain).
 // Every wait is bounded; a timeout sets `status`.
 #include "device_common.cuh"
+#include "exact_math.cuh"
 #include "prefill_tc.hpp"
 
 namespace mtb {
@@ -82,6 +83,7 @@ struct PfArgs {
     float* y;           // output rows [T][ldy]
     int T, K, ldy, epi;
     int* status;
+    const float* bias;  // [n_rows] for the PF_EPI_BIAS* epilogues, else null
 };
 
 __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
@@ -245,6 +247,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) k_pf_gemm(PfArgs a) {
                     }
                 }
             }
+        } else if (ok && a.epi >= PF_EPI_BIAS) {
+            // Linear layers with a bias (ggml_mul_mat then ggml_add): y = acc + b,
+            // then GELU (erf form), SiLU, or the residual add res + (acc + b).
+            const float b = a.bias[n];
+#pragma unroll
+            for (int t = 0; t < kPfHalfTok; ++t) {
+                const int row = tt * kPfTok + kPfHalfTok * tg + t;
+                if (row < a.T) {
+                    float* o = a.y + (size_t)row * a.ldy + n;
+                    const float v = __fadd_rn(yt[t], b);
+                    if (a.epi == PF_EPI_BIAS_GELU)
+                        *o = exact_gelu_erf(v);
+                    else if (a.epi == PF_EPI_BIAS_SILU)
+                        *o = __fdiv_rn(v, __fadd_rn(1.0f, exact_expf(-v)));
+                    else if (a.epi == PF_EPI_BIAS_RESID)
+                        *o = __fadd_rn(*o, v);
+                    else
+                        *o = v;
+                }
+            }
         } else if (ok) {
 #pragma unroll
             for (int t = 0; t < kPfHalfTok; ++t) {
@@ -354,8 +376,14 @@ void pf_quant(const float* x, int T, int K, uint8_t* xq, float* xd, cudaStream_t
 
 void pf_gemm(const uint8_t* w, int n_rows, int K, const uint8_t* xq, const float* xd, int T, float* y, int ldy, int epi,
              int* status, cudaStream_t s) {
-    PfArgs a{w, xq, xd, y, T, K, ldy, epi, status};
+    PfArgs a{w, xq, xd, y, T, K, ldy, epi, status, nullptr};
     // Dynamic shared memory >= 120 KB keeps one CTA per SM.
+    k_pf_gemm<<<dim3((T + kPfTok - 1) / kPfTok, n_rows / kPfRows), kPfThreads, 120 * 1024, s>>>(a);
+}
+
+void pf_gemm_bias(const uint8_t* w, int n_rows, int K, const uint8_t* xq, const float* xd, int T, float* y, int ldy,
+                  int epi, const float* bias, int* status, cudaStream_t s) {
+    PfArgs a{w, xq, xd, y, T, K, ldy, epi, status, bias};
     k_pf_gemm<<<dim3((T + kPfTok - 1) / kPfTok, n_rows / kPfRows), kPfThreads, 120 * 1024, s>>>(a);
 }
 

@@ -8,7 +8,16 @@
 
 namespace mtb {
 
-enum PfEpilogue { PF_EPI_STORE = 0, PF_EPI_RESID = 1, PF_EPI_SWIGLU = 2 };
+enum PfEpilogue {
+    PF_EPI_STORE = 0,
+    PF_EPI_RESID = 1,
+    PF_EPI_SWIGLU = 2,
+    // With a per-row bias (the Whisper encoder and the audio adaptor):
+    PF_EPI_BIAS = 3,        // y = acc + b
+    PF_EPI_BIAS_GELU = 4,   // y = gelu_erf(acc + b)
+    PF_EPI_BIAS_SILU = 5,   // y = silu(acc + b)
+    PF_EPI_BIAS_RESID = 6,  // y = y + (acc + b)
+};
 
 // Bytes of a matrix in prefill weight steps (n_rows a multiple of 128, K of 256).
 size_t pf_weight_bytes(int n_rows, int K);
@@ -26,5 +35,8 @@ void pf_quant(const float* x, int T, int K, uint8_t* xq, float* xd, cudaStream_t
 // y[T][ldy] (=, +=, or SwiGLU into 64-feature groups) from weight steps and activation steps.
 void pf_gemm(const uint8_t* w, int n_rows, int K, const uint8_t* xq, const float* xd, int T, float* y, int ldy, int epi,
              int* status, cudaStream_t s);
+// The same with a bias b[n_rows] and one of the PF_EPI_BIAS* epilogues.
+void pf_gemm_bias(const uint8_t* w, int n_rows, int K, const uint8_t* xq, const float* xd, int T, float* y, int ldy,
+                  int epi, const float* bias, int* status, cudaStream_t s);
 
 }  // namespace mtb

@@ -108,6 +108,14 @@ SIGNATURES = {
     "mtb_greedy_choice": (C.c_int, [_vp, _f32p, C.c_int, _i32p, C.c_int, C.c_float, _i32p]),
     "mtb_lm_head_argmax_noalloc": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
     "mtb_noalloc_error": (C.c_char_p, []),
+    "mtb_audio_load": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(_vp)]),
+    "mtb_audio_free": (None, [_vp]),
+    "mtb_audio_error": (C.c_char_p, [_vp]),
+    "mtb_audio_dims": (C.c_int, [_vp, _i32p]),
+    "mtb_audio_tokens": (C.c_int, [_vp, C.c_int]),
+    "mtb_audio_encode": (C.c_int, [_vp, _f32p, C.c_int, _f32p, C.c_int, _ip]),
+    "mtb_audio_last_ms": (C.c_float, [_vp]),
+    "mtb_audio_debug_chunk": (C.c_int, [_vp, _f32p, C.c_int, _f32p, _f32p]),
 }
 
 
@@ -187,6 +195,58 @@ class Model:
 
     def __del__(self):
         self.close()
+
+
+class AudioEncoder:
+    """The audio front end of a GGUF on one CUDA device: mt::AudioEncoder
+    (src/audio_encoder.hpp:23-34), encode(samples16k) -> rows [n_tokens][hidden]."""
+
+    def __init__(self, gguf_path: str, device: int = 0):
+        L = lib()
+        p = C.c_void_p()
+        if L.mtb_audio_load(gguf_path.encode(), int(device), C.byref(p)) != 0:
+            raise MtbError(f"mtb_audio_load: {L.mtb_audio_error(None).decode()}")
+        self.ptr = p
+        dims = (C.c_int32 * 10)()
+        L.mtb_audio_dims(self.ptr, dims)
+        (self.hidden, self.d_model, self.n_layers, self.n_heads, self.ffn, self.n_mels, self.n_frames,
+         self.chunk_samples, self.enc_frames, self.merge) = list(dims)
+
+    def close(self):
+        if getattr(self, "ptr", None):
+            lib().mtb_audio_free(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise MtbError(f"{what}: {lib().mtb_audio_error(self.ptr).decode()}")
+
+    def tokens(self, n_samples: int) -> int:
+        return lib().mtb_audio_tokens(self.ptr, int(n_samples))
+
+    def encode(self, samples16k: np.ndarray, max_tokens: int | None = None) -> np.ndarray:
+        x = np.ascontiguousarray(samples16k, dtype=np.float32)
+        cap = max(self.tokens(len(x)), 1) if max_tokens is None else max_tokens
+        out = np.zeros((max(cap, 1), self.hidden), dtype=np.float32)
+        n = C.c_int(0)
+        self._check(lib().mtb_audio_encode(self.ptr, _f32(x), int(len(x)), _f32(out), int(cap), C.byref(n)),
+                    "mtb_audio_encode")
+        return out[:n.value]
+
+    def last_ms(self) -> float:
+        return float(lib().mtb_audio_last_ms(self.ptr))
+
+    def debug_chunk(self, chunk: np.ndarray):
+        """(mel [n_mels][frames], encoder output [enc_frames][d_model]) of one chunk."""
+        x = np.ascontiguousarray(chunk, dtype=np.float32)
+        mel = np.zeros((self.n_mels, self.n_frames), dtype=np.float32)
+        enc = np.zeros((self.enc_frames, self.d_model), dtype=np.float32)
+        self._check(lib().mtb_audio_debug_chunk(self.ptr, _f32(x), int(len(x)), _f32(mel), _f32(enc)),
+                    "mtb_audio_debug_chunk")
+        return mel, enc
 
 
 class Decoder:

@@ -196,3 +196,175 @@ def read_shape(reader) -> DecoderShape:
                         rms_eps=float(get("mtd.text.rms_eps", 1e-6)), rope_theta=float(get("mtd.text.rope_theta", 1e6)),
                         eos_token_id=int(get("mtd.eos_token_id", 151645)),
                         audio_token_id=int(get("mtd.audio_token_id", 151671)))
+
+
+# ------------------------------------------------------------------ audio front end
+
+@dataclass(frozen=True)
+class AudioShape:
+    """The audio front end's configuration (src/model_loader.cpp:131-153 keys)."""
+    d_model: int
+    n_layers: int
+    n_heads: int
+    ffn: int
+    hidden: int                 # the decoder's hidden size (adaptor output)
+    n_mels: int = 80
+    n_fft: int = 400
+    hop: int = 160
+    n_samples: int = 480000     # one 30 s chunk at 16 kHz
+    n_frames: int = 3000
+    merge: int = 4
+    adaptor_eps: float = 1e-6
+
+    @property
+    def enc_frames(self) -> int:
+        return (self.n_frames + 2 - 3) // 2 + 1
+
+    def cfg(self):
+        """The oracle's configuration vector (oracle.h: orc_audio_create)."""
+        return [self.n_fft, self.hop, self.n_mels, self.n_samples, self.n_frames, self.d_model, self.n_layers,
+                self.n_heads, self.ffn, self.merge, self.hidden]
+
+
+# Whisper-Medium encoder + the adaptor into Qwen3-0.6B (the MOSS-Transcribe front end).
+WHISPER_MEDIUM = AudioShape(d_model=1024, n_layers=24, n_heads=16, ffn=4096, hidden=1024)
+# The same widths and 30 s chunk with two layers: every kernel shape at full size, fast to check.
+WHISPER_MEDIUM_2L = AudioShape(d_model=1024, n_layers=2, n_heads=16, ffn=4096, hidden=1024)
+# A small front end (2 s chunks, 256 wide) feeding the TINY decoder.
+TINY_AUDIO = AudioShape(d_model=256, n_layers=2, n_heads=4, ffn=1024, hidden=256, n_samples=32000, n_frames=200)
+
+
+def slaney_mel_filters(n_mels: int, n_fft: int, sr: int = 16000) -> np.ndarray:
+    """[n_mels][n_fft / 2 + 1] triangular filters on the Slaney mel scale with
+    Slaney area normalisation (the construction of Whisper's filter bank)."""
+    def hz_to_mel(f):
+        f = np.asarray(f, dtype=np.float64)
+        lin = f / (200.0 / 3)
+        return np.where(f >= 1000.0, 15.0 + np.log(np.maximum(f, 1e-9) / 1000.0) / (np.log(6.4) / 27.0), lin)
+
+    def mel_to_hz(m):
+        m = np.asarray(m, dtype=np.float64)
+        return np.where(m >= 15.0, 1000.0 * np.exp((np.log(6.4) / 27.0) * (m - 15.0)), (200.0 / 3) * m)
+
+    n_bins = n_fft // 2 + 1
+    fft_freqs = np.linspace(0, sr / 2, n_bins)
+    mel_pts = mel_to_hz(np.linspace(hz_to_mel(0.0), hz_to_mel(sr / 2), n_mels + 2))
+    fdiff = np.diff(mel_pts)
+    ramps = mel_pts[:, None] - fft_freqs[None, :]
+    lower = -ramps[:-2] / fdiff[:-1, None]
+    upper = ramps[2:] / fdiff[1:, None]
+    fb = np.maximum(0, np.minimum(lower, upper))
+    fb *= (2.0 / (mel_pts[2:n_mels + 2] - mel_pts[:n_mels]))[:, None]
+    return fb.astype(np.float32)
+
+
+def audio_tensor_specs(s: AudioShape):
+    """(name, numpy shape, kind): 'q' q8_0 linear, 'w' F32 weight N(0, std), 'b' F32 bias,
+    'g' LayerNorm gain (1 + noise), 'p' positional embedding."""
+    d = s.d_model
+    specs = [("enc.conv1.w", (d, s.n_mels, 3), "w"), ("enc.conv1.b", (d,), "b"),
+             ("enc.conv2.w", (d, d, 3), "w"), ("enc.conv2.b", (d,), "b"),
+             ("enc.pos_embd", (s.enc_frames, d), "p")]
+    for i in range(s.n_layers):
+        p = f"enc.blk.{i}."
+        specs += [(p + "attn_ln.w", (d,), "g"), (p + "attn_ln.b", (d,), "b"),
+                  (p + "attn_q.w", (d, d), "q"), (p + "attn_q.b", (d,), "b"),
+                  (p + "attn_k.w", (d, d), "q"),
+                  (p + "attn_v.w", (d, d), "q"), (p + "attn_v.b", (d,), "b"),
+                  (p + "attn_out.w", (d, d), "q"), (p + "attn_out.b", (d,), "b"),
+                  (p + "ffn_ln.w", (d,), "g"), (p + "ffn_ln.b", (d,), "b"),
+                  (p + "ffn_1.w", (s.ffn, d), "q"), (p + "ffn_1.b", (s.ffn,), "b"),
+                  (p + "ffn_2.w", (d, s.ffn), "q"), (p + "ffn_2.b", (d,), "b")]
+    specs += [("enc.ln_post.w", (d,), "g"), ("enc.ln_post.b", (d,), "b"),
+              ("adaptor.fc1.w", (s.hidden, d * s.merge), "q"), ("adaptor.fc1.b", (s.hidden,), "b"),
+              ("adaptor.fc2.w", (s.hidden, s.hidden), "q"), ("adaptor.fc2.b", (s.hidden,), "b"),
+              ("adaptor.ln.w", (s.hidden,), "g"), ("adaptor.ln.b", (s.hidden,), "b")]
+    return specs
+
+
+def write_audio_fixture(path: str, s: AudioShape = WHISPER_MEDIUM, seed: int = 0, weight_std: float = 0.02) -> str:
+    """A random-init audio front end GGUF with the reference converter's names,
+    keys and types (scripts/convert_moss_transcribe_to_gguf.py:46-53, 110-139,
+    224-281): q8_0 encoder/adaptor linears, F32 conv stem, positional
+    embeddings, biases, LayerNorms and Slaney mel filters stored [n_mels][n_bins]."""
+    import gguf
+    rng = np.random.default_rng(seed)
+    w = gguf.GGUFWriter(path, "moss_transcribe")
+    w.add_uint32("mtd.text.hidden", s.hidden)
+    w.add_uint32("mtd.audio.mel_bins", s.n_mels)
+    w.add_uint32("mtd.audio.d_model", s.d_model)
+    w.add_uint32("mtd.audio.n_layers", s.n_layers)
+    w.add_uint32("mtd.audio.n_heads", s.n_heads)
+    w.add_uint32("mtd.audio.ffn", s.ffn)
+    w.add_uint32("mtd.audio.max_src_pos", s.enc_frames)
+    w.add_uint32("mtd.audio_merge_size", s.merge)
+    w.add_uint32("mtd.adaptor_input_dim", s.d_model * s.merge)
+    w.add_float32("mtd.adaptor_norm_eps", s.adaptor_eps)
+    w.add_uint32("mtd.feat.sr", 16000)
+    w.add_uint32("mtd.feat.n_fft", s.n_fft)
+    w.add_uint32("mtd.feat.hop", s.hop)
+    w.add_uint32("mtd.feat.feature_size", s.n_mels)
+    w.add_uint32("mtd.feat.n_samples", s.n_samples)
+    w.add_uint32("mtd.feat.nb_max_frames", s.n_frames)
+    w.add_tensor("mel_filters", slaney_mel_filters(s.n_mels, s.n_fft))
+    for name, shp, kind in audio_tensor_specs(s):
+        if kind == "g":
+            arr = (1.0 + 0.05 * rng.standard_normal(shp, dtype=np.float32)).astype(np.float32)
+        elif kind == "b":
+            arr = (0.02 * rng.standard_normal(shp, dtype=np.float32)).astype(np.float32)
+        elif kind == "p":
+            arr = (0.1 * rng.standard_normal(shp, dtype=np.float32)).astype(np.float32)
+        else:
+            arr = (np.float32(weight_std) * rng.standard_normal(shp, dtype=np.float32)).astype(np.float32)
+        if kind == "q":
+            raw = _quantize_q8_0(arr)
+            w.add_tensor(name, raw, raw_shape=raw.shape, raw_dtype=gguf.GGMLQuantizationType.Q8_0)
+        else:
+            w.add_tensor(name, arr)
+        del arr
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    return path
+
+
+def cached_audio_fixture(s: AudioShape = WHISPER_MEDIUM, seed: int = 0, directory: str | None = None) -> str:
+    directory = directory or os.environ.get("MTB_FIXTURE_DIR", "/tmp/mtb_fixtures")
+    os.makedirs(directory, exist_ok=True)
+    tag = "x".join(str(v) for v in asdict(s).values())
+    path = os.path.join(directory, f"audio_{tag}_seed{seed}.gguf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        write_audio_fixture(tmp, s, seed)
+        os.replace(tmp, path)
+    return path
+
+
+def synthetic_pcm(n: int, seed: int = 3) -> np.ndarray:
+    """Seeded 16 kHz test signal: a few tones with a slow amplitude envelope plus
+    noise, in [-1, 1] (no recording is available)."""
+    rng = np.random.default_rng(seed)
+    t = np.arange(n, dtype=np.float64) / 16000.0
+    x = np.zeros(n)
+    for f, a in zip(rng.uniform(80, 3000, 6), rng.uniform(0.02, 0.15, 6)):
+        x += a * np.sin(2 * np.pi * f * t + rng.uniform(0, 2 * np.pi))
+    x *= 0.6 + 0.4 * np.sin(2 * np.pi * 0.7 * t)
+    x += 0.01 * rng.standard_normal(n)
+    return np.clip(x, -1, 1).astype(np.float32)
+
+
+def read_audio_shape(reader) -> AudioShape:
+    """AudioShape from a GGUFReader's mtd.* metadata (src/model_loader.cpp:131-153)."""
+    def get(key, default):
+        f = reader.fields.get(key)
+        if f is None:
+            return default
+        return f.parts[f.data[0]][0].item()
+    return AudioShape(d_model=int(get("mtd.audio.d_model", 1024)), n_layers=int(get("mtd.audio.n_layers", 24)),
+                      n_heads=int(get("mtd.audio.n_heads", 16)), ffn=int(get("mtd.audio.ffn", 4096)),
+                      hidden=int(get("mtd.text.hidden", 1024)), n_mels=int(get("mtd.feat.feature_size", 80)),
+                      n_fft=int(get("mtd.feat.n_fft", 400)), hop=int(get("mtd.feat.hop", 160)),
+                      n_samples=int(get("mtd.feat.n_samples", 480000)),
+                      n_frames=int(get("mtd.feat.nb_max_frames", 3000)), merge=int(get("mtd.audio_merge_size", 4)),
+                      adaptor_eps=float(get("mtd.adaptor_norm_eps", 1e-6)))

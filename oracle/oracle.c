@@ -1082,3 +1082,422 @@ int orc_decoder_run_ref(orc_decoder* d, const float* embeds, int T, float* out_h
 void orc_decoder_logits_ref(const orc_decoder* d, const float* hidden_row, float* logits) {
     ref_mul_mat_q8(d->m->token_embd, d->m->vocab, d->m->hidden, hidden_row, 1, logits);
 }
+
+/* ============================================================ audio front end
+ * WhisperMel::compute (src/mel.cpp:153-224), WhisperEncoder::encode
+ * (src/whisper_encoder.cpp:98-207), AudioAdaptor::apply
+ * (src/audio_adaptor.cpp:39-96) and AudioEncoder::encode
+ * (src/audio_encoder.cpp:16-75).
+ *
+ * The mel follows the reference's own order exactly (float window and twiddle
+ * tables formed as at src/mel.cpp:31-45, double sums in ascending index,
+ * log10 in double).  The ggml ops of the encoder and adaptor are restated in
+ * the order the CUDA kernels evaluate them (the decoder's convention):
+ *   - conv1d (kernel 3, padding 1) as im2col x F32 weights: one fmaf chain per
+ *     output over j = ic * 3 + k ascending, then + bias, GELU (erf form:
+ *     (0.5 x)(1 + erff(x / sqrt 2)), ggml_vec_gelu_erf_f32);
+ *   - ggml_norm: mean and variance as double sums, 32 strided partials
+ *     (i = l, l + 32, ...) combined by an xor butterfly; y = ((x - mean) *
+ *     (1 / sqrtf(var + eps))) * w + b;
+ *   - q8_0 linears: the decoder's q8_0 dot (dot_q8), then + bias;
+ *   - attention (no mask, scale 1/sqrt(64)): 64-key tiles with a running
+ *     maximum and sum (online softmax; per tile the 4-key partial sums of 16
+ *     lanes combined by an xor butterfly), P.V as one fmaf chain per tile,
+ *     exp = orc_expf, the output divided by the sum at the end.
+ * `ref_order` = 1 evaluates attention in the reference's order instead (whole
+ * row: f32 scores, max, expf, sum in double, scaled by 1/sum, then P.V over
+ * all keys: src/whisper_encoder.cpp:157-166, ggml soft_max_ext), for the
+ * tests that bound the gap between the two orders. */
+
+typedef struct {
+    const float *attn_ln_w, *attn_ln_b, *ffn_ln_w, *ffn_ln_b;
+    const void *q_w, *k_w, *v_w, *o_w, *fc1_w, *fc2_w; /* q8_0 rows */
+    const float *q_b, *v_b, *o_b, *fc1_b, *fc2_b;
+} orc_audio_layer;
+
+struct orc_audio {
+    int n_fft, hop, n_mels, n_bins, n_samples, n_frames, d, n_layers, n_heads, ffn, merge, hidden, enc_T;
+    float ad_eps;
+    int ref_order;
+    float *window, *cos_t, *sin_t; /* [n_bins][n_fft] as in the reference */
+    const float *fb, *conv1_w, *conv1_b, *conv2_w, *conv2_b, *pos, *ln_post_w, *ln_post_b;
+    const void *ad_fc1_w, *ad_fc2_w;
+    const float *ad_fc1_b, *ad_fc2_b, *ad_ln_w, *ad_ln_b;
+    orc_audio_layer* layers;
+};
+
+orc_audio* orc_audio_create(const int* cfg, float adaptor_eps) {
+    orc_audio* a = (orc_audio*)calloc(1, sizeof(orc_audio));
+    a->n_fft = cfg[0], a->hop = cfg[1], a->n_mels = cfg[2], a->n_samples = cfg[3], a->n_frames = cfg[4];
+    a->d = cfg[5], a->n_layers = cfg[6], a->n_heads = cfg[7], a->ffn = cfg[8], a->merge = cfg[9], a->hidden = cfg[10];
+    a->ad_eps = adaptor_eps;
+    a->n_bins = a->n_fft / 2 + 1;
+    a->enc_T = (a->n_frames + 2 - 3) / 2 + 1;
+    if (a->n_fft <= 0 || a->n_mels <= 0 || a->d <= 0 || a->n_heads <= 0 || a->d != a->n_heads * 64 || a->n_layers <= 0) {
+        free(a);
+        return NULL;
+    }
+    a->layers = (orc_audio_layer*)calloc((size_t)a->n_layers, sizeof(orc_audio_layer));
+    a->window = (float*)malloc(sizeof(float) * (size_t)a->n_fft);
+    a->cos_t = (float*)malloc(sizeof(float) * (size_t)a->n_fft * (size_t)a->n_bins);
+    a->sin_t = (float*)malloc(sizeof(float) * (size_t)a->n_fft * (size_t)a->n_bins);
+    for (int n = 0; n < a->n_fft; ++n) a->window[n] = 0.5f * (1.0f - cos(2.0 * M_PI * n / (double)a->n_fft));
+    for (int k = 0; k < a->n_bins; ++k)
+        for (int n = 0; n < a->n_fft; ++n) {
+            const double ang = 2.0 * M_PI * (double)k * (double)n / (double)a->n_fft;
+            a->cos_t[(size_t)k * a->n_fft + n] = (float)cos(ang);
+            a->sin_t[(size_t)k * a->n_fft + n] = (float)sin(ang);
+        }
+    return a;
+}
+
+void orc_audio_free(orc_audio* a) {
+    if (!a) return;
+    free(a->layers);
+    free(a->window);
+    free(a->cos_t);
+    free(a->sin_t);
+    free(a);
+}
+
+void orc_audio_set_ref_order(orc_audio* a, int ref_order) { a->ref_order = ref_order; }
+
+/* Keeps `data` (the caller owns it): F32 arrays, or q8_0 rows for the linears. */
+int orc_audio_set_tensor(orc_audio* a, const char* name, const void* data) {
+    const float* f = (const float*)data;
+    if (!strcmp(name, "mel_filters")) a->fb = f;
+    else if (!strcmp(name, "enc.conv1.w")) a->conv1_w = f;
+    else if (!strcmp(name, "enc.conv1.b")) a->conv1_b = f;
+    else if (!strcmp(name, "enc.conv2.w")) a->conv2_w = f;
+    else if (!strcmp(name, "enc.conv2.b")) a->conv2_b = f;
+    else if (!strcmp(name, "enc.pos_embd")) a->pos = f;
+    else if (!strcmp(name, "enc.ln_post.w")) a->ln_post_w = f;
+    else if (!strcmp(name, "enc.ln_post.b")) a->ln_post_b = f;
+    else if (!strcmp(name, "adaptor.fc1.w")) a->ad_fc1_w = data;
+    else if (!strcmp(name, "adaptor.fc2.w")) a->ad_fc2_w = data;
+    else if (!strcmp(name, "adaptor.fc1.b")) a->ad_fc1_b = f;
+    else if (!strcmp(name, "adaptor.fc2.b")) a->ad_fc2_b = f;
+    else if (!strcmp(name, "adaptor.ln.w")) a->ad_ln_w = f;
+    else if (!strcmp(name, "adaptor.ln.b")) a->ad_ln_b = f;
+    else {
+        int il = -1, off = 0;
+        if (sscanf(name, "enc.blk.%d.%n", &il, &off) != 1 || il < 0 || il >= a->n_layers) return -1;
+        orc_audio_layer* L = &a->layers[il];
+        const char* s = name + off;
+        if (!strcmp(s, "attn_ln.w")) L->attn_ln_w = f;
+        else if (!strcmp(s, "attn_ln.b")) L->attn_ln_b = f;
+        else if (!strcmp(s, "ffn_ln.w")) L->ffn_ln_w = f;
+        else if (!strcmp(s, "ffn_ln.b")) L->ffn_ln_b = f;
+        else if (!strcmp(s, "attn_q.w")) L->q_w = data;
+        else if (!strcmp(s, "attn_k.w")) L->k_w = data;
+        else if (!strcmp(s, "attn_v.w")) L->v_w = data;
+        else if (!strcmp(s, "attn_out.w")) L->o_w = data;
+        else if (!strcmp(s, "ffn_1.w")) L->fc1_w = data;
+        else if (!strcmp(s, "ffn_2.w")) L->fc2_w = data;
+        else if (!strcmp(s, "attn_q.b")) L->q_b = f;
+        else if (!strcmp(s, "attn_v.b")) L->v_b = f;
+        else if (!strcmp(s, "attn_out.b")) L->o_b = f;
+        else if (!strcmp(s, "ffn_1.b")) L->fc1_b = f;
+        else if (!strcmp(s, "ffn_2.b")) L->fc2_b = f;
+        else return -1;
+    }
+    return 0;
+}
+
+/* src/mel.cpp:153-224 (the serial DFT path): reflect padding, window, power
+ * spectrum, mel projection, log10, chunk normalisation.  chunk: n_samples
+ * values (the caller zero-pads, as src/audio_encoder.cpp:53-55 does);
+ * mel: [n_mels][n_frames]. */
+void orc_audio_mel(const orc_audio* a, const float* chunk, float* mel) {
+    const int N = a->n_samples, pad = a->n_fft / 2, nb = a->n_bins, nf = a->n_fft;
+    float* x = (float*)malloc(sizeof(float) * (size_t)(N + 2 * pad));
+    for (int i = 0; i < pad; ++i) x[i] = chunk[pad - i];
+    for (int i = 0; i < N; ++i) x[pad + i] = chunk[i];
+    for (int i = 0; i < pad; ++i) x[pad + N + i] = chunk[N - 2 - i];
+#pragma omp parallel
+    {
+        float* frame = (float*)malloc(sizeof(float) * (size_t)nf);
+        double* power = (double*)malloc(sizeof(double) * (size_t)nb);
+#pragma omp for schedule(static)
+        for (int t = 0; t < a->n_frames; ++t) {
+            const int start = t * a->hop;
+            for (int n = 0; n < nf; ++n) frame[n] = x[start + n] * a->window[n];
+            for (int b = 0; b < nb; ++b) {
+                const float* cr = a->cos_t + (size_t)b * nf;
+                const float* sr = a->sin_t + (size_t)b * nf;
+                double re = 0.0, im = 0.0;
+                for (int n = 0; n < nf; ++n) {
+                    re += (double)frame[n] * cr[n];
+                    im -= (double)frame[n] * sr[n];
+                }
+                power[b] = re * re + im * im;
+            }
+            for (int m = 0; m < a->n_mels; ++m) {
+                const float* row = a->fb + (size_t)m * nb;
+                double acc = 0.0;
+                for (int b = 0; b < nb; ++b) acc += (double)row[b] * power[b];
+                mel[(size_t)m * a->n_frames + t] = (float)log10(acc > 1e-10 ? acc : 1e-10);
+            }
+        }
+        free(frame);
+        free(power);
+    }
+    free(x);
+    const size_t count = (size_t)a->n_mels * (size_t)a->n_frames;
+    float mx = mel[0];
+    for (size_t i = 0; i < count; ++i) mx = mel[i] > mx ? mel[i] : mx;
+    const float floor_v = mx - 8.0f;
+    for (size_t i = 0; i < count; ++i) {
+        const float v = mel[i] > floor_v ? mel[i] : floor_v;
+        mel[i] = (v + 4.0f) / 4.0f;
+    }
+}
+
+/* erf by its Maclaurin series in double (the CUDA kernels' exact_erff, the
+ * same operations in the same order): t_n = (t_(n-1) * -x^2) * (1/n),
+ * s += t_n * (1/(2n+1)) until the term is at most 2^-60 of the sum;
+ * |x| >= 4 gives +-1.  Tested against libm's erf within 1 ulp. */
+float orc_erff(float xf) {
+    const double x = (double)xf;
+    if (!(fabs(x) < 4.0)) return xf != xf ? xf : (xf > 0.0f ? 1.0f : -1.0f);
+    const double mx2 = -x * x;
+    double term = x, sum = x;
+    for (int n = 1; n <= 128; ++n) {
+        term = (term * mx2) * (1.0 / (double)n);
+        const double add = term * (1.0 / (double)(2 * n + 1));
+        sum = sum + add;
+        if (fabs(add) <= fabs(sum) * 8.673617379884035e-19) break;
+    }
+    return (float)(sum * 1.1283791670955126);
+}
+
+/* GELU, erf form (ggml_vec_gelu_erf_f32): (0.5 x)(1 + erf(x / sqrt 2)). */
+static inline float gelu_erf(float v) { return (0.5f * v) * (1.0f + orc_erff(v * 0.707106781f)); }
+
+/* conv1d, kernel 3, padding 1: out[t][oc] = gelu(b + sum_j A[t][j] W[oc][j]) (+ pos[t][oc]). */
+static void conv_gelu(const float* x, int L, int IC, long sp, long sc, int stride, const float* w, const float* b,
+                      const float* pos, int OC, int OL, float* out) {
+    const int J = IC * 3;
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < OL; ++t) {
+        float* col = (float*)malloc(sizeof(float) * (size_t)J);
+        for (int j = 0; j < J; ++j) {
+            const int ic = j / 3, k = j % 3, p = t * stride + k - 1;
+            col[j] = (p >= 0 && p < L) ? x[(long)p * sp + (long)ic * sc] : 0.f;
+        }
+        for (int oc = 0; oc < OC; ++oc) {
+            const float* wr = w + (size_t)oc * J;
+            float acc = 0.f;
+            for (int j = 0; j < J; ++j) acc = fmaf(col[j], wr[j], acc);
+            float g = gelu_erf(acc + b[oc]);
+            if (pos) g = g + pos[(size_t)t * OC + oc];
+            out[(size_t)t * OC + oc] = g;
+        }
+        free(col);
+    }
+}
+
+static double lane_sum_d(double* v) {
+    /* 32 lane partials combined by an xor butterfly (every lane ends equal). */
+    for (int o = 16; o > 0; o >>= 1) {
+        double nv[32];
+        for (int l = 0; l < 32; ++l) nv[l] = v[l] + v[l ^ o];
+        memcpy(v, nv, sizeof(nv));
+    }
+    return v[0];
+}
+
+static void layer_norm_rows(const float* x, int T, int D, const float* w, const float* b, float eps, float* y) {
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < T; ++r) {
+        const float* xr = x + (size_t)r * D;
+        float* yr = y + (size_t)r * D;
+        double p[32];
+        for (int l = 0; l < 32; ++l) {
+            p[l] = 0.0;
+            for (int i = l; i < D; i += 32) p[l] = p[l] + (double)xr[i];
+        }
+        const float mean = (float)(lane_sum_d(p) / D);
+        for (int l = 0; l < 32; ++l) {
+            p[l] = 0.0;
+            for (int i = l; i < D; i += 32) {
+                const float v = xr[i] - mean;
+                p[l] = p[l] + (double)(v * v);
+            }
+        }
+        const float var = (float)(lane_sum_d(p) / D);
+        const float scale = 1.0f / sqrtf(var + eps);
+        for (int i = 0; i < D; ++i) yr[i] = ((xr[i] - mean) * scale) * w[i] + b[i];
+    }
+}
+
+/* y[T][n] (= | += | gelu | silu) of W q8_0 [n x k] . x[T][k] + b. */
+enum { LIN_BIAS = 0, LIN_GELU = 1, LIN_SILU = 2, LIN_RESID = 3 };
+static void linear_q8(const void* w, const float* b, int n, int k, const float* x, int T, float* y, int mode) {
+    float* tmp = (float*)malloc(sizeof(float) * (size_t)T * (size_t)n);
+    orc_mul_mat_q8(w, n, k, x, T, tmp);
+    for (size_t i = 0; i < (size_t)T * (size_t)n; ++i) {
+        const float v = tmp[i] + (b ? b[i % (size_t)n] : 0.0f);
+        if (mode == LIN_GELU) y[i] = gelu_erf(v);
+        else if (mode == LIN_SILU) y[i] = v / (1.0f + orc_expf(-v));
+        else if (mode == LIN_RESID) y[i] = y[i] + v;
+        else y[i] = v;
+    }
+    free(tmp);
+}
+
+/* One head of one query: q, k, v with row stride ld; out[64]. */
+static void enc_attn_row(const float* q, const float* k, const float* v, long ld, int T, int ref_order, float* out) {
+    const float scale = 0.125f;
+    if (ref_order) {
+        float* p = (float*)malloc(sizeof(float) * (size_t)T);
+        float mx = -INFINITY;
+        for (int j = 0; j < T; ++j) {
+            float s = 0.f;
+            for (int i = 0; i < 64; ++i) s += q[i] * k[(long)j * ld + i];
+            p[j] = s * scale;
+            mx = p[j] > mx ? p[j] : mx;
+        }
+        double sum = 0.0;
+        for (int j = 0; j < T; ++j) {
+            p[j] = expf(p[j] - mx);
+            sum += (double)p[j];
+        }
+        const float inv = (float)(1.0 / sum);
+        for (int j = 0; j < T; ++j) p[j] *= inv;
+        for (int i = 0; i < 64; ++i) {
+            float acc = 0.f;
+            for (int j = 0; j < T; ++j) acc += p[j] * v[(long)j * ld + i];
+            out[i] = acc;
+        }
+        free(p);
+        return;
+    }
+    float m = -1e30f, l = 0.f, o[64];
+    for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    for (int k0 = 0; k0 < T; k0 += 64) {
+        float s[64], p[64];
+        float tmax = -1e30f;
+        for (int c = 0; c < 64; ++c) {
+            const int j = k0 + c;
+            if (j < T) {
+                float acc = 0.f;
+                for (int i = 0; i < 64; ++i) acc = fmaf(q[i], k[(long)j * ld + i], acc);
+                s[c] = acc * scale;
+            } else {
+                s[c] = -1e30f;
+            }
+            tmax = s[c] > tmax ? s[c] : tmax;
+        }
+        const float mn = m > tmax ? m : tmax;
+        const float alpha = orc_expf(m - mn);
+        m = mn;
+        /* 16 lanes x 4 keys: lane partials from 0 in key order, then the butterfly. */
+        float part[16];
+        for (int ln = 0; ln < 16; ++ln) {
+            float ps = 0.f;
+            for (int c = 0; c < 4; ++c) {
+                const int kc = 4 * ln + c;
+                p[kc] = k0 + kc < T ? orc_expf(s[kc] - mn) : 0.f;
+                ps = ps + p[kc];
+            }
+            part[ln] = ps;
+        }
+        for (int off = 8; off > 0; off >>= 1) {
+            float np_[16];
+            for (int ln = 0; ln < 16; ++ln) np_[ln] = part[ln] + part[ln ^ off];
+            memcpy(part, np_, sizeof(np_));
+        }
+        l = l * alpha + part[0];
+        for (int i = 0; i < 64; ++i) {
+            float acc = o[i] * alpha;
+            for (int c = 0; c < 64; ++c) {
+                const int j = k0 + c;
+                acc = fmaf(p[c], j < T ? v[(long)j * ld + i] : 0.f, acc);
+            }
+            o[i] = acc;
+        }
+    }
+    const float inv = 1.0f / l;
+    for (int i = 0; i < 64; ++i) out[i] = o[i] * inv;
+}
+
+/* src/whisper_encoder.cpp:98-207: mel [n_mels][n_frames] -> out [enc_T][d]
+ * (after the final LayerNorm). */
+int orc_audio_encoder(const orc_audio* a, const float* mel, float* out) {
+    const int d = a->d, T = a->enc_T, H = a->n_heads;
+    float* c1 = (float*)malloc(sizeof(float) * (size_t)a->n_frames * d);
+    float* h = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* nrm = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* q = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* k = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* v = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* att = (float*)malloc(sizeof(float) * (size_t)T * d);
+    float* f = (float*)malloc(sizeof(float) * (size_t)T * a->ffn);
+    conv_gelu(mel, a->n_frames, a->n_mels, 1, a->n_frames, 1, a->conv1_w, a->conv1_b, NULL, d, a->n_frames, c1);
+    conv_gelu(c1, a->n_frames, d, d, 1, 2, a->conv2_w, a->conv2_b, a->pos, d, T, h);
+    for (int il = 0; il < a->n_layers; ++il) {
+        const orc_audio_layer* L = &a->layers[il];
+        layer_norm_rows(h, T, d, L->attn_ln_w, L->attn_ln_b, 1e-5f, nrm);
+        linear_q8(L->q_w, L->q_b, d, d, nrm, T, q, LIN_BIAS);
+        linear_q8(L->k_w, NULL, d, d, nrm, T, k, LIN_BIAS);
+        linear_q8(L->v_w, L->v_b, d, d, nrm, T, v, LIN_BIAS);
+#pragma omp parallel for schedule(dynamic, 16)
+        for (int idx = 0; idx < H * T; ++idx) {
+            const int hh = idx / T, t = idx % T;
+            enc_attn_row(q + (size_t)t * d + hh * 64, k + hh * 64, v + hh * 64, d, T, a->ref_order,
+                         att + (size_t)t * d + hh * 64);
+        }
+        linear_q8(L->o_w, L->o_b, d, d, att, T, h, LIN_RESID);
+        layer_norm_rows(h, T, d, L->ffn_ln_w, L->ffn_ln_b, 1e-5f, nrm);
+        linear_q8(L->fc1_w, L->fc1_b, a->ffn, d, nrm, T, f, LIN_GELU);
+        linear_q8(L->fc2_w, L->fc2_b, d, a->ffn, f, T, h, LIN_RESID);
+    }
+    layer_norm_rows(h, T, d, a->ln_post_w, a->ln_post_b, 1e-5f, out);
+    free(c1), free(h), free(nrm), free(q), free(k), free(v), free(att), free(f);
+    return 0;
+}
+
+/* src/audio_adaptor.cpp:39-96: enc [frames][d] (frames a multiple of merge)
+ * -> out [frames / merge][hidden]. */
+int orc_audio_adaptor(const orc_audio* a, const float* enc, int frames, float* out) {
+    const int N = frames / a->merge, kin = a->d * a->merge;
+    float* a1 = (float*)malloc(sizeof(float) * (size_t)N * a->hidden);
+    float* a2 = (float*)malloc(sizeof(float) * (size_t)N * a->hidden);
+    linear_q8(a->ad_fc1_w, a->ad_fc1_b, a->hidden, kin, enc, N, a1, LIN_SILU);
+    linear_q8(a->ad_fc2_w, a->ad_fc2_b, a->hidden, a->hidden, a1, N, a2, LIN_BIAS);
+    layer_norm_rows(a2, N, a->hidden, a->ad_ln_w, a->ad_ln_b, a->ad_eps, out);
+    free(a1), free(a2);
+    return N;
+}
+
+/* src/audio_encoder.cpp:16-75: samples -> out [n_tokens][hidden]; returns
+ * n_tokens, or -1 (empty input, output too small). */
+int orc_audio_encode(const orc_audio* a, const float* samples, int n, float* out, int max_tokens) {
+    if (n <= 0) return -1;
+    const int stride = a->hop * 2 * a->merge;
+    int total = 0;
+    for (int off = 0; off < n; off += a->n_samples) {
+        const int unpadded = n - off < a->n_samples ? n - off : a->n_samples;
+        total += (unpadded - 1) / stride + 1;
+    }
+    if (total > max_tokens) return -1;
+    float* enc_all = (float*)malloc(sizeof(float) * (size_t)total * a->merge * a->d);
+    float* chunk = (float*)malloc(sizeof(float) * (size_t)a->n_samples);
+    float* mel = (float*)malloc(sizeof(float) * (size_t)a->n_mels * a->n_frames);
+    float* enc = (float*)malloc(sizeof(float) * (size_t)a->enc_T * a->d);
+    size_t row = 0;
+    for (int off = 0; off < n; off += a->n_samples) {
+        const int unpadded = n - off < a->n_samples ? n - off : a->n_samples;
+        const int trim = ((unpadded - 1) / stride + 1) * a->merge;
+        memset(chunk, 0, sizeof(float) * (size_t)a->n_samples);
+        memcpy(chunk, samples + off, sizeof(float) * (size_t)unpadded);
+        orc_audio_mel(a, chunk, mel);
+        orc_audio_encoder(a, mel, enc);
+        memcpy(enc_all + row * a->d, enc, sizeof(float) * (size_t)trim * a->d);
+        row += (size_t)trim;
+    }
+    const int N = orc_audio_adaptor(a, enc_all, (int)row, out);
+    free(enc_all), free(chunk), free(mel), free(enc);
+    return N;
+}

@@ -158,7 +158,26 @@ float orc_dot_q8_blocks(int ref_order, const void* w, const void* x, int nb);
 void orc_set_threads(int n);
 /* The exp / sin / cos the oracle (and the CUDA kernels) evaluate. */
 float orc_expf(float x);
+/* erf by its Maclaurin series in double (the kernels' exact_erff). */
+float orc_erff(float x);
 void orc_sincosf(float x, float* s, float* c);
+
+/* Audio front end (src/mel.cpp:153-224, src/whisper_encoder.cpp:98-207,
+ * src/audio_adaptor.cpp:39-96, src/audio_encoder.cpp:16-75).  cfg: n_fft, hop,
+ * n_mels, samples per chunk, mel frames per chunk, d_model, n_layers, n_heads,
+ * ffn, merge, hidden.  Tensors are kept by pointer (the caller owns them):
+ * F32 arrays, q8_0 rows for the encoder and adaptor linears.  The mel is in the
+ * reference's own order; the encoder in the CUDA kernels' order (attention in
+ * the reference's order with orc_audio_set_ref_order(a, 1)). */
+typedef struct orc_audio orc_audio;
+orc_audio* orc_audio_create(const int* cfg, float adaptor_eps);
+void orc_audio_free(orc_audio* a);
+void orc_audio_set_ref_order(orc_audio* a, int ref_order);
+int orc_audio_set_tensor(orc_audio* a, const char* name, const void* data);
+void orc_audio_mel(const orc_audio* a, const float* chunk, float* mel);
+int orc_audio_encoder(const orc_audio* a, const float* mel, float* out);
+int orc_audio_adaptor(const orc_audio* a, const float* enc, int frames, float* out);
+int orc_audio_encode(const orc_audio* a, const float* samples, int n, float* out, int max_tokens);
 
 #ifdef __cplusplus
 }

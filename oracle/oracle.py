@@ -101,7 +101,18 @@ def lib():
         L.orc_set_threads.argtypes = [C.c_int]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
+        L.orc_erff.restype = C.c_float
+        L.orc_erff.argtypes = [C.c_float]
         L.orc_sincosf.argtypes = [C.c_float, f32p, f32p]
+        L.orc_audio_create.restype = vp
+        L.orc_audio_create.argtypes = [i32p, C.c_float]
+        L.orc_audio_free.argtypes = [vp]
+        L.orc_audio_set_ref_order.argtypes = [vp, C.c_int]
+        L.orc_audio_set_tensor.argtypes = [vp, C.c_char_p, vp]
+        L.orc_audio_mel.argtypes = [vp, f32p, f32p]
+        L.orc_audio_encoder.argtypes = [vp, f32p, f32p]
+        L.orc_audio_adaptor.argtypes = [vp, f32p, C.c_int, f32p]
+        L.orc_audio_encode.argtypes = [vp, f32p, C.c_int, f32p, C.c_int]
         _LIB = L
     return _LIB
 
@@ -116,6 +127,10 @@ def _i32(a):
 
 def expf(x: float) -> float:
     return lib().orc_expf(float(x))
+
+
+def erff(x: float) -> float:
+    return lib().orc_erff(x)
 
 
 def sincosf(x: float):
@@ -323,3 +338,71 @@ class OracleDecoder:
         if n < 0:
             raise RuntimeError("oracle greedy generate failed")
         return out[:n].tolist()
+
+
+class OracleAudio:
+    """The audio front end of a GGUF attached to the oracle (src/audio_encoder.cpp:16-75):
+    mel (reference order), Whisper encoder and adaptor (the kernels' order, or
+    attention in the reference's order with ref_order=True)."""
+
+    def __init__(self, path: str, ref_order: bool = False):
+        import gguf
+        import sys
+        sys.path.insert(0, os.path.join(os.path.dirname(_HERE), "moss-transcribe.cpp_b200"))
+        from mtb.fixture import read_audio_shape
+        self.reader = gguf.GGUFReader(path)
+        self.shape = s = read_audio_shape(self.reader)
+        cfg = np.asarray(s.cfg(), dtype=np.int32)
+        self.ptr = lib().orc_audio_create(_i32(cfg), s.adaptor_eps)
+        if not self.ptr:
+            raise ValueError("oracle rejected the audio configuration")
+        lib().orc_audio_set_ref_order(self.ptr, int(ref_order))
+        self.arrays = {}
+        for t in self.reader.tensors:
+            if not (t.name == "mel_filters" or t.name.startswith("enc.") or t.name.startswith("adaptor.")):
+                continue
+            arr = np.ascontiguousarray(t.data)
+            if t.name == "mel_filters" and arr.shape != (s.n_mels, s.n_fft // 2 + 1):
+                arr = np.ascontiguousarray(arr.T)
+            self.arrays[t.name] = arr
+            if lib().orc_audio_set_tensor(self.ptr, t.name.encode(), arr.ctypes.data):
+                raise ValueError(f"oracle rejected tensor {t.name}")
+
+    def __del__(self):
+        if getattr(self, "ptr", None):
+            lib().orc_audio_free(self.ptr)
+            self.ptr = None
+
+    def mel(self, chunk: np.ndarray) -> np.ndarray:
+        s = self.shape
+        x = np.zeros(s.n_samples, dtype=np.float32)
+        x[:len(chunk)] = chunk
+        out = np.zeros((s.n_mels, s.n_frames), dtype=np.float32)
+        lib().orc_audio_mel(self.ptr, _f32(x), _f32(out))
+        return out
+
+    def encoder(self, mel: np.ndarray) -> np.ndarray:
+        s = self.shape
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        out = np.zeros((s.enc_frames, s.d_model), dtype=np.float32)
+        lib().orc_audio_encoder(self.ptr, _f32(mel), _f32(out))
+        return out
+
+    def adaptor(self, enc: np.ndarray) -> np.ndarray:
+        s = self.shape
+        enc = np.ascontiguousarray(enc, dtype=np.float32)
+        out = np.zeros((enc.shape[0] // s.merge, s.hidden), dtype=np.float32)
+        lib().orc_audio_adaptor(self.ptr, _f32(enc), int(enc.shape[0]), _f32(out))
+        return out
+
+    def encode(self, samples: np.ndarray) -> np.ndarray:
+        s = self.shape
+        samples = np.ascontiguousarray(samples, dtype=np.float32)
+        stride = s.hop * 2 * s.merge
+        total = sum((min(s.n_samples, len(samples) - off) - 1) // stride + 1
+                    for off in range(0, len(samples), s.n_samples))
+        out = np.zeros((max(total, 1), s.hidden), dtype=np.float32)
+        n = lib().orc_audio_encode(self.ptr, _f32(samples), int(len(samples)), _f32(out), int(total))
+        if n < 0:
+            raise ValueError("AudioEncoder: empty input samples")
+        return out[:n]

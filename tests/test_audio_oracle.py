@@ -1,0 +1,104 @@
+"""The audio front end's CPU restatement (oracle/oracle.c, audio section),
+pinned where the reference gives a way to pin it:
+  * the mel against an independent numpy restatement of WhisperMel::compute
+    (src/mel.cpp:153-224) that takes the spectrum by FFT in double (the
+    reference's own ExperimentalFft transform, pocketfft r2c in double), on the
+    signal kinds of the reference's mel probe (tests/test_mel_cpu.cpp:53-63:
+    zero, noise, impulse, tone, mixed, extreme) -- the reference records no
+    mel values, only the comparison protocol;
+  * token counts and trims of AudioEncoder::encode (src/audio_encoder.cpp:41-66);
+  * the gap between the oracle's attention order (the kernels') and the
+    reference's whole-row order (src/whisper_encoder.cpp:157-166), bounded by
+    the reference's own encoder tolerance (tests/test_whisper_encoder.cpp:29:
+    atol 5e-2).
+No GPU needed."""
+import numpy as np
+import pytest
+
+import oracle
+from mtb import fixture
+
+
+@pytest.fixture(scope="module")
+def tiny_audio(fixture_dir):
+    return fixture.cached_audio_fixture(fixture.TINY_AUDIO, seed=0, directory=fixture_dir)
+
+
+def reference_kinds(n):
+    """The signals of the reference's mel probe (numpy noise in place of mt19937)."""
+    rng = np.random.default_rng(7301)
+    idx = np.arange(n)
+    out = {"zero": np.zeros(n, np.float32), "noise": rng.uniform(-1, 1, n).astype(np.float32)}
+    imp = np.zeros(n, np.float32)
+    imp[[0, 199, 200, min(10000, n - 2), n - 1]] = 1
+    out["impulse"] = imp
+    out["tone"] = np.sin(idx * 0.17278759594743862).astype(np.float32)
+    out["mixed"] = (rng.uniform(-1, 1, n).astype(np.float32) * np.float32(0.1) +
+                    np.sin(idx * 0.06123).astype(np.float32) * np.float32(0.9)).astype(np.float32)
+    out["extreme"] = np.where(idx & 1, -1e12, 1e12).astype(np.float32)
+    return out
+
+
+def mel_numpy_fft(chunk, s: fixture.AudioShape, fb):
+    """WhisperMel::compute with the spectrum by FFT in double."""
+    pad = s.n_fft // 2
+    x = np.concatenate([chunk[1:pad + 1][::-1], chunk, chunk[-pad - 1:-1][::-1]]).astype(np.float32)
+    n = np.arange(s.n_fft)
+    window = (0.5 * (1.0 - np.cos(2.0 * np.pi * n / s.n_fft))).astype(np.float32)
+    frames = np.stack([x[t * s.hop:t * s.hop + s.n_fft] for t in range(s.n_frames)])
+    frames = (frames * window).astype(np.float32).astype(np.float64)
+    power = np.abs(np.fft.rfft(frames, axis=1)) ** 2
+    mel = np.log10(np.maximum(fb.astype(np.float64) @ power.T, 1e-10)).astype(np.float32)
+    mx = mel.max()
+    return ((np.maximum(mel, mx - np.float32(8.0)) + np.float32(4.0)) / np.float32(4.0)).astype(np.float32)
+
+
+def test_mel_matches_fft_restatement_on_reference_signals(tiny_audio):
+    a = oracle.OracleAudio(tiny_audio)
+    s = a.shape
+    fb = a.arrays["mel_filters"]
+    for kind, x in reference_kinds(s.n_samples).items():
+        got = a.mel(x)
+        want = mel_numpy_fft(x, s, fb)
+        assert got.shape == (s.n_mels, s.n_frames)
+        assert np.isfinite(got).all(), kind
+        # Direct DFT vs FFT in double: the power spectra agree to ~1e-12
+        # relative; after log10 and the float cast, within a few float ulps.
+        np.testing.assert_allclose(got, want, atol=2e-6, rtol=0, err_msg=kind)
+
+
+def test_token_counts_and_empty_input(tiny_audio):
+    a = oracle.OracleAudio(tiny_audio)
+    s = a.shape
+    stride = s.hop * 2 * s.merge
+    for n in (1, stride, stride + 1, s.n_samples, s.n_samples + 1, 2 * s.n_samples + 777):
+        x = fixture.synthetic_pcm(n)
+        out = a.encode(x)
+        want = sum((min(s.n_samples, n - off) - 1) // stride + 1 for off in range(0, n, s.n_samples))
+        assert out.shape == (want, s.hidden), n
+        assert np.isfinite(out).all()
+    with pytest.raises(ValueError):
+        a.encode(np.zeros(0, np.float32))
+
+
+def test_attention_order_gap_within_reference_tolerance(tiny_audio):
+    """The oracle's online-softmax order against the reference's whole-row
+    order, through two encoder layers (the q8_0 requantisation between layers
+    amplifies the float rounding differences)."""
+    a = oracle.OracleAudio(tiny_audio)
+    r = oracle.OracleAudio(tiny_audio, ref_order=True)
+    x = fixture.synthetic_pcm(45000)
+    for mel in (a.mel(x[:32000]), a.mel(x[32000:])):
+        gap = np.abs(a.encoder(mel) - r.encoder(mel)).max()
+        assert gap < 5e-2, gap
+
+
+def test_erf_is_correctly_rounded_on_a_grid():
+    """orc_erff (and the kernels' exact_erff, the same operations) against
+    float64 math.erf: within 1 ulp (0.5 ulp measured)."""
+    import math
+    xs = np.concatenate([np.linspace(-4.5, 4.5, 20001), [0.0, -0.0, 1e-30, 3.9999, 4.0, -4.0, 10.0]])
+    for x in xs.astype(np.float32):
+        got = np.float32(oracle.erff(float(x)))
+        ref = math.erf(float(x))
+        assert abs(float(got) - ref) <= float(np.spacing(np.float32(max(abs(ref), 1e-38)))), x
