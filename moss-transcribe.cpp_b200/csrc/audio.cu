@@ -230,7 +230,7 @@ __global__ void __launch_bounds__(256) k_layer_norm(const float* __restrict__ x,
 // scores and dims 4 tx .. 4 tx + 3 of the output.  Online softmax over the key
 // tiles (running maximum and sum per query, the output rescaled when the
 // maximum grows); exp is exact_expf.
-__global__ void __launch_bounds__(256, 2) k_enc_attn(const float* __restrict__ qkv, int T, int d, float scale,
+__global__ void __launch_bounds__(256, 3) k_enc_attn(const float* __restrict__ qkv, int T, int d, float scale,
                                                     float* __restrict__ out) {
     extern __shared__ __align__(16) float at_smem[];
     float* Qs = at_smem;                // [64 dims][kAttPad]: query fastest
@@ -296,14 +296,16 @@ __global__ void __launch_bounds__(256, 2) k_enc_attn(const float* __restrict__ q
             float psum = 0.f;
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-                const float p = k0 + 4 * tx + c < T ? exact_expf(__fsub_rn(s[a][c], mn)) : 0.f;
-                Ps[(4 * tx + c) * kAttPad + 4 * ty + a] = p;
-                psum = __fadd_rn(psum, p);
+                s[a][c] = k0 + 4 * tx + c < T ? exact_expf(__fsub_rn(s[a][c], mn)) : 0.f;  // now p
+                psum = __fadd_rn(psum, s[a][c]);
             }
 #pragma unroll
             for (int off = 8; off > 0; off >>= 1) psum = __fadd_rn(psum, __shfl_xor_sync(0xffffffffu, psum, off));
             l[a] = __fadd_rn(__fmul_rn(l[a], alpha[a]), psum);
         }
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<float4*>(Ps + (4 * tx + c) * kAttPad + 4 * ty) = make_float4(s[0][c], s[1][c], s[2][c], s[3][c]);
         __syncthreads();
 #pragma unroll
         for (int a = 0; a < 4; ++a)

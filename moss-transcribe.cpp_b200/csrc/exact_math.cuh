@@ -95,14 +95,24 @@ __device__ __forceinline__ void exact_sincosf(float x, float* s_out, float* c_ou
 // correctly rounded doubles; the cancellation of the alternating series costs at
 // most ~1e-10 absolute below |x| = 4, so the float result is the correctly rounded
 // one except near ties.
+struct ErfRcpTable {
+    double v[258];  // v[k] = 1 / k, the correctly rounded double (v[0] unused)
+};
+constexpr ErfRcpTable make_erf_rcp_table() {
+    ErfRcpTable t{};
+    for (int k = 1; k < 258; ++k) t.v[k] = 1.0 / k;
+    return t;
+}
+static __constant__ ErfRcpTable c_erf_rcp = make_erf_rcp_table();
+
 __device__ __forceinline__ float exact_erff(float xf) {
     const double x = (double)xf;
     if (!(fabs(x) < 4.0)) return xf != xf ? xf : (xf > 0.0f ? 1.0f : -1.0f);
     const double mx2 = __dmul_rn(-x, x);
     double term = x, sum = x;
     for (int n = 1; n <= 128; ++n) {
-        term = __dmul_rn(__dmul_rn(term, mx2), __drcp_rn((double)n));
-        const double add = __dmul_rn(term, __drcp_rn((double)(2 * n + 1)));
+        term = __dmul_rn(__dmul_rn(term, mx2), c_erf_rcp.v[n]);
+        const double add = __dmul_rn(term, c_erf_rcp.v[2 * n + 1]);
         sum = __dadd_rn(sum, add);
         if (fabs(add) <= fabs(sum) * 8.673617379884035e-19) break;  // 2^-60
     }
