@@ -94,3 +94,30 @@ def test_whisper_medium_width_chunk_and_encode(medium_2l):
     want = orc.encode(x)
     assert got.shape == want.shape == (375 + 125, 1024)
     np.testing.assert_array_equal(got, want)
+
+
+def test_samples_to_ids_matches_oracle_chain(tiny_audio, tiny_gguf, tiny_oracle):
+    """transcribe_pcm16k's device chain without the tokenizer (src/transcribe.cpp:28-56):
+    samples -> audio rows (mtb_audio_encode) -> prompt ids around the audio span ->
+    fuse_embeds and strict speculative decode on the device (mtb_spec_generate_ids),
+    against the oracle's chain on the same samples: rows, ids and counters equal."""
+    audio = capi.AudioEncoder(tiny_audio, 0)
+    orc_audio = oracle.OracleAudio(tiny_audio)
+    shape = tiny_oracle.shape
+    assert audio.hidden == shape.hidden
+    x = fixture.synthetic_pcm(45000, seed=21)
+    rows = audio.encode(x)
+    np.testing.assert_array_equal(rows, orc_audio.encode(x))
+    text = fixture.lcg_ids(12, shape.vocab - 8).tolist()
+    ids = text[:5] + [shape.audio_token_id] * rows.shape[0] + text[5:]
+    eos = shape.eos_token_id
+    model = capi.Model(tiny_gguf, 0)
+    dec = capi.Decoder(model, len(ids) + 64, capi.KV_F32, max_new=48)
+    got_ids, got_c = dec.spec_generate_ids(ids, rows, shape.audio_token_id, 48, eos, k_max=8, n_min=3, n_max=3)
+    fused = tiny_oracle.embed(ids).copy()
+    fused[5:5 + rows.shape[0]] = rows
+    od = oracle.OracleDecoder(tiny_oracle, len(ids) + 64)
+    want_ids, want_c = od.spec_generate(fused, 48, eos, k_max=8, n_min=3, n_max=3)
+    assert got_ids == want_ids
+    for key in ("target_calls", "proposed", "accepted", "rewinds", "target_input_tokens"):
+        assert got_c[key] == want_c[key], key
