@@ -1104,10 +1104,13 @@ void orc_decoder_logits_ref(const orc_decoder* d, const float* hidden_row, float
  *     maximum and sum (online softmax; per tile the 4-key partial sums of 16
  *     lanes combined by an xor butterfly), P.V as one fmaf chain per tile,
  *     exp = orc_expf, the output divided by the sum at the end.
- * `ref_order` = 1 evaluates attention in the reference's order instead (whole
- * row: f32 scores, max, expf, sum in double, scaled by 1/sum, then P.V over
- * all keys: src/whisper_encoder.cpp:157-166, ggml soft_max_ext), for the
- * tests that bound the gap between the two orders. */
+ * `ref_order` = 1 evaluates the encoder and adaptor in the reference's order
+ * instead, for the tests that bound the gap between the two orders: ggml's
+ * x86 dot orders (ref_dot_f32 for the conv im2col rows, the scores and P.V;
+ * ref_mul_mat_q8 for the q8_0 linears), ggml_norm's sequential double sums,
+ * whole-row softmax (max, libm expf, sum in double, scaled by 1/sum:
+ * src/whisper_encoder.cpp:157-166, ggml soft_max_ext), libm erff and expf in
+ * GELU and SiLU. */
 
 typedef struct {
     const float *attn_ln_w, *attn_ln_b, *ffn_ln_w, *ffn_ln_b;
@@ -1276,7 +1279,7 @@ static inline float gelu_erf(float v) { return (0.5f * v) * (1.0f + orc_erff(v *
 
 /* conv1d, kernel 3, padding 1: out[t][oc] = gelu(b + sum_j A[t][j] W[oc][j]) (+ pos[t][oc]). */
 static void conv_gelu(const float* x, int L, int IC, long sp, long sc, int stride, const float* w, const float* b,
-                      const float* pos, int OC, int OL, float* out) {
+                      const float* pos, int OC, int OL, float* out, int ref) {
     const int J = IC * 3;
 #pragma omp parallel for schedule(static)
     for (int t = 0; t < OL; ++t) {
@@ -1288,8 +1291,11 @@ static void conv_gelu(const float* x, int L, int IC, long sp, long sc, int strid
         for (int oc = 0; oc < OC; ++oc) {
             const float* wr = w + (size_t)oc * J;
             float acc = 0.f;
-            for (int j = 0; j < J; ++j) acc = fmaf(col[j], wr[j], acc);
-            float g = gelu_erf(acc + b[oc]);
+            if (ref)
+                acc = ref_dot_f32(J, col, 1, wr, 1);
+            else
+                for (int j = 0; j < J; ++j) acc = fmaf(col[j], wr[j], acc);
+            float g = ref ? (0.5f * (acc + b[oc])) * (1.0f + erff((acc + b[oc]) * 0.707106781f)) : gelu_erf(acc + b[oc]);
             if (pos) g = g + pos[(size_t)t * OC + oc];
             out[(size_t)t * OC + oc] = g;
         }
@@ -1307,11 +1313,26 @@ static double lane_sum_d(double* v) {
     return v[0];
 }
 
-static void layer_norm_rows(const float* x, int T, int D, const float* w, const float* b, float eps, float* y) {
+static void layer_norm_rows(const float* x, int T, int D, const float* w, const float* b, float eps, float* y,
+                            int ref) {
 #pragma omp parallel for schedule(static)
     for (int r = 0; r < T; ++r) {
         const float* xr = x + (size_t)r * D;
         float* yr = y + (size_t)r * D;
+        if (ref) {
+            /* ggml_norm's sequential double sums. */
+            double sum = 0.0;
+            for (int i = 0; i < D; ++i) sum += (double)xr[i];
+            const float mean = (float)(sum / D);
+            double sum2 = 0.0;
+            for (int i = 0; i < D; ++i) {
+                const float v = xr[i] - mean;
+                sum2 += (double)(v * v);
+            }
+            const float scale = 1.0f / sqrtf((float)(sum2 / D) + eps);
+            for (int i = 0; i < D; ++i) yr[i] = ((xr[i] - mean) * scale) * w[i] + b[i];
+            continue;
+        }
         double p[32];
         for (int l = 0; l < 32; ++l) {
             p[l] = 0.0;
@@ -1333,13 +1354,17 @@ static void layer_norm_rows(const float* x, int T, int D, const float* w, const 
 
 /* y[T][n] (= | += | gelu | silu) of W q8_0 [n x k] . x[T][k] + b. */
 enum { LIN_BIAS = 0, LIN_GELU = 1, LIN_SILU = 2, LIN_RESID = 3 };
-static void linear_q8(const void* w, const float* b, int n, int k, const float* x, int T, float* y, int mode) {
+static void linear_q8(const void* w, const float* b, int n, int k, const float* x, int T, float* y, int mode,
+                      int ref) {
     float* tmp = (float*)malloc(sizeof(float) * (size_t)T * (size_t)n);
-    orc_mul_mat_q8(w, n, k, x, T, tmp);
+    if (ref)
+        ref_mul_mat_q8(w, n, k, x, T, tmp);
+    else
+        orc_mul_mat_q8(w, n, k, x, T, tmp);
     for (size_t i = 0; i < (size_t)T * (size_t)n; ++i) {
         const float v = tmp[i] + (b ? b[i % (size_t)n] : 0.0f);
-        if (mode == LIN_GELU) y[i] = gelu_erf(v);
-        else if (mode == LIN_SILU) y[i] = v / (1.0f + orc_expf(-v));
+        if (mode == LIN_GELU) y[i] = ref ? (0.5f * v) * (1.0f + erff(v * 0.707106781f)) : gelu_erf(v);
+        else if (mode == LIN_SILU) y[i] = v / (1.0f + (ref ? expf(-v) : orc_expf(-v)));
         else if (mode == LIN_RESID) y[i] = y[i] + v;
         else y[i] = v;
     }
@@ -1353,9 +1378,7 @@ static void enc_attn_row(const float* q, const float* k, const float* v, long ld
         float* p = (float*)malloc(sizeof(float) * (size_t)T);
         float mx = -INFINITY;
         for (int j = 0; j < T; ++j) {
-            float s = 0.f;
-            for (int i = 0; i < 64; ++i) s += q[i] * k[(long)j * ld + i];
-            p[j] = s * scale;
+            p[j] = ref_dot_f32(64, q, 1, k + (long)j * ld, 1) * scale;
             mx = p[j] > mx ? p[j] : mx;
         }
         double sum = 0.0;
@@ -1365,11 +1388,7 @@ static void enc_attn_row(const float* q, const float* k, const float* v, long ld
         }
         const float inv = (float)(1.0 / sum);
         for (int j = 0; j < T; ++j) p[j] *= inv;
-        for (int i = 0; i < 64; ++i) {
-            float acc = 0.f;
-            for (int j = 0; j < T; ++j) acc += p[j] * v[(long)j * ld + i];
-            out[i] = acc;
-        }
+        for (int i = 0; i < 64; ++i) out[i] = ref_dot_f32(T, v + i, (size_t)ld, p, 1);
         free(p);
         return;
     }
@@ -1434,26 +1453,27 @@ int orc_audio_encoder(const orc_audio* a, const float* mel, float* out) {
     float* v = (float*)malloc(sizeof(float) * (size_t)T * d);
     float* att = (float*)malloc(sizeof(float) * (size_t)T * d);
     float* f = (float*)malloc(sizeof(float) * (size_t)T * a->ffn);
-    conv_gelu(mel, a->n_frames, a->n_mels, 1, a->n_frames, 1, a->conv1_w, a->conv1_b, NULL, d, a->n_frames, c1);
-    conv_gelu(c1, a->n_frames, d, d, 1, 2, a->conv2_w, a->conv2_b, a->pos, d, T, h);
+    const int ref = a->ref_order;
+    conv_gelu(mel, a->n_frames, a->n_mels, 1, a->n_frames, 1, a->conv1_w, a->conv1_b, NULL, d, a->n_frames, c1, ref);
+    conv_gelu(c1, a->n_frames, d, d, 1, 2, a->conv2_w, a->conv2_b, a->pos, d, T, h, ref);
     for (int il = 0; il < a->n_layers; ++il) {
         const orc_audio_layer* L = &a->layers[il];
-        layer_norm_rows(h, T, d, L->attn_ln_w, L->attn_ln_b, 1e-5f, nrm);
-        linear_q8(L->q_w, L->q_b, d, d, nrm, T, q, LIN_BIAS);
-        linear_q8(L->k_w, NULL, d, d, nrm, T, k, LIN_BIAS);
-        linear_q8(L->v_w, L->v_b, d, d, nrm, T, v, LIN_BIAS);
+        layer_norm_rows(h, T, d, L->attn_ln_w, L->attn_ln_b, 1e-5f, nrm, ref);
+        linear_q8(L->q_w, L->q_b, d, d, nrm, T, q, LIN_BIAS, ref);
+        linear_q8(L->k_w, NULL, d, d, nrm, T, k, LIN_BIAS, ref);
+        linear_q8(L->v_w, L->v_b, d, d, nrm, T, v, LIN_BIAS, ref);
 #pragma omp parallel for schedule(dynamic, 16)
         for (int idx = 0; idx < H * T; ++idx) {
             const int hh = idx / T, t = idx % T;
             enc_attn_row(q + (size_t)t * d + hh * 64, k + hh * 64, v + hh * 64, d, T, a->ref_order,
                          att + (size_t)t * d + hh * 64);
         }
-        linear_q8(L->o_w, L->o_b, d, d, att, T, h, LIN_RESID);
-        layer_norm_rows(h, T, d, L->ffn_ln_w, L->ffn_ln_b, 1e-5f, nrm);
-        linear_q8(L->fc1_w, L->fc1_b, a->ffn, d, nrm, T, f, LIN_GELU);
-        linear_q8(L->fc2_w, L->fc2_b, d, a->ffn, f, T, h, LIN_RESID);
+        linear_q8(L->o_w, L->o_b, d, d, att, T, h, LIN_RESID, ref);
+        layer_norm_rows(h, T, d, L->ffn_ln_w, L->ffn_ln_b, 1e-5f, nrm, ref);
+        linear_q8(L->fc1_w, L->fc1_b, a->ffn, d, nrm, T, f, LIN_GELU, ref);
+        linear_q8(L->fc2_w, L->fc2_b, d, a->ffn, f, T, h, LIN_RESID, ref);
     }
-    layer_norm_rows(h, T, d, a->ln_post_w, a->ln_post_b, 1e-5f, out);
+    layer_norm_rows(h, T, d, a->ln_post_w, a->ln_post_b, 1e-5f, out, ref);
     free(c1), free(h), free(nrm), free(q), free(k), free(v), free(att), free(f);
     return 0;
 }
@@ -1464,9 +1484,10 @@ int orc_audio_adaptor(const orc_audio* a, const float* enc, int frames, float* o
     const int N = frames / a->merge, kin = a->d * a->merge;
     float* a1 = (float*)malloc(sizeof(float) * (size_t)N * a->hidden);
     float* a2 = (float*)malloc(sizeof(float) * (size_t)N * a->hidden);
-    linear_q8(a->ad_fc1_w, a->ad_fc1_b, a->hidden, kin, enc, N, a1, LIN_SILU);
-    linear_q8(a->ad_fc2_w, a->ad_fc2_b, a->hidden, a->hidden, a1, N, a2, LIN_BIAS);
-    layer_norm_rows(a2, N, a->hidden, a->ad_ln_w, a->ad_ln_b, a->ad_eps, out);
+    const int ref = a->ref_order;
+    linear_q8(a->ad_fc1_w, a->ad_fc1_b, a->hidden, kin, enc, N, a1, LIN_SILU, ref);
+    linear_q8(a->ad_fc2_w, a->ad_fc2_b, a->hidden, a->hidden, a1, N, a2, LIN_BIAS, ref);
+    layer_norm_rows(a2, N, a->hidden, a->ad_ln_w, a->ad_ln_b, a->ad_eps, out, ref);
     free(a1), free(a2);
     return N;
 }

@@ -167,8 +167,9 @@ void orc_sincosf(float x, float* s, float* c);
  * n_mels, samples per chunk, mel frames per chunk, d_model, n_layers, n_heads,
  * ffn, merge, hidden.  Tensors are kept by pointer (the caller owns them):
  * F32 arrays, q8_0 rows for the encoder and adaptor linears.  The mel is in the
- * reference's own order; the encoder in the CUDA kernels' order (attention in
- * the reference's order with orc_audio_set_ref_order(a, 1)). */
+ * reference's own order; the encoder and adaptor in the CUDA kernels' order (in
+ * the reference's order -- ggml's dot orders, sequential norms, whole-row
+ * softmax, libm exp/erf -- with orc_audio_set_ref_order(a, 1)). */
 typedef struct orc_audio orc_audio;
 orc_audio* orc_audio_create(const int* cfg, float adaptor_eps);
 void orc_audio_free(orc_audio* a);
