@@ -810,10 +810,11 @@ int mtb_audio_encode(mtb_audio* a, const float* samples16k, int n_samples, float
             return -1;
         }
         const long long frames = total * a->merge;
-        if (frames > INT32_MAX / 2 || ensure_frames(a, int(frames))) {
-            if (a->error.empty()) a->error = "audio too long";
+        if (frames > INT32_MAX / 2) {
+            a->error = "audio too long";
             return -1;
         }
+        if (ensure_frames(a, int(frames))) return -1;
         const long long stride = (long long)a->hop * 2 * a->merge;
         AU_CK(cudaEventRecord(a->ev[0], a->stream));
         long long row = 0;
