@@ -1,11 +1,13 @@
 """The audio front end's CPU restatement (oracle/oracle.c, audio section),
 pinned where the reference gives a way to pin it:
+  * the mel against the reference's own recorded probe statistics
+    (cpu-lab/mel-kernel-v1.jsonl, made by tests/test_mel_cpu.cpp of the
+    reference): its serial-DFT mel against an FFT transform of the same samples
+    differs in exactly the recorded number of values by exactly the recorded
+    amounts, on all six probe signals, with the probe's own filters and noise;
   * the mel against an independent numpy restatement of WhisperMel::compute
-    (src/mel.cpp:153-224) that takes the spectrum by FFT in double (the
-    reference's own ExperimentalFft transform, pocketfft r2c in double), on the
-    signal kinds of the reference's mel probe (tests/test_mel_cpu.cpp:53-63:
-    zero, noise, impulse, tone, mixed, extreme) -- the reference records no
-    mel values, only the comparison protocol;
+    (src/mel.cpp:153-224) that takes the spectrum by FFT in double, within
+    2e-6, on the fixture's Slaney filters;
   * token counts and trims of AudioEncoder::encode (src/audio_encoder.cpp:41-66);
   * the gap between the oracle's order (the kernels') and the reference's own
     evaluation order (src/whisper_encoder.cpp:103-203 over ggml's CPU ops),
@@ -109,3 +111,79 @@ def test_erf_is_correctly_rounded_on_a_grid():
         got = np.float32(oracle.erff(float(x)))
         ref = math.erf(float(x))
         assert abs(float(got) - ref) <= float(np.spacing(np.float32(max(abs(ref), 1e-38)))), x
+
+
+def _probe_signals(noise, samples):
+    """The six signals of the reference's mel probe (tests/test_mel_cpu.cpp:53-63)."""
+    n = np.arange(samples)
+    imp = np.zeros(samples, np.float32)
+    imp[[0, 199, 200, 10000, samples - 1]] = 1
+    return {"zero": np.zeros(samples, np.float32), "noise": noise, "impulse": imp,
+            "tone": np.sin(n * 0.17278759594743862).astype(np.float32),
+            # noise(rng) * 0.1f + std::sin(n * 0.06123) * 0.9f: float product, then double sum
+            "mixed": ((noise * np.float32(0.1)).astype(np.float64) +
+                      np.sin(n * 0.06123) * np.float64(np.float32(0.9))).astype(np.float32),
+            "extreme": np.where(n & 1, -1, 1).astype(np.float32) * np.float32(1e12)}
+
+
+def _fft_mel(x, fb, n_frames):
+    """The probe's comparison transform: the same windowed float samples,
+    spectrum by FFT in double, mel sums over bins in order, log10, normalisation."""
+    pad, n_fft, hop = 200, 400, 160
+    xp = np.concatenate([x[1:pad + 1][::-1], x, x[-pad - 1:-1][::-1]])
+    n = np.arange(n_fft)
+    w = (0.5 * (1.0 - np.cos(2.0 * np.pi * n / n_fft))).astype(np.float32)
+    frames = np.stack([xp[t * hop:t * hop + n_fft] for t in range(n_frames)])
+    power = np.abs(np.fft.rfft((frames * w).astype(np.float32).astype(np.float64), axis=1)) ** 2
+    acc = np.zeros((fb.shape[0], n_frames))
+    fb64 = fb.astype(np.float64)
+    for b in range(fb.shape[1]):
+        acc = acc + fb64[:, b:b + 1] * power[:, b][None, :]
+    mel = np.log10(np.maximum(acc, 1e-10)).astype(np.float32)
+    floor_v = np.float32(mel.max() - np.float32(8.0))
+    return ((np.maximum(mel, floor_v) + np.float32(4.0)) / np.float32(4.0)).astype(np.float32)
+
+
+def test_mel_reproduces_reference_probe_records(tmp_path):
+    """Pin of the mel against the reference's own recorded numbers: its probe
+    (tests/test_mel_cpu.cpp) runs the production serial-DFT mel and an FFT
+    transform of the same samples, with synthetic triangular filters, on six
+    signals, and records how many of the 240,000 values differ in their bits
+    and by how much (cpu-lab/mel-kernel-v1.jsonl).  The oracle's mel (and the
+    device mel, equal to it bit for bit) against the same FFT comparison gives
+    the same counts and the same differences, to the last digit recorded."""
+    import ctypes as C
+    import json
+    import os
+    import shutil
+    import subprocess
+    if not shutil.which("g++"):
+        pytest.skip("g++ is needed to draw the probe's std::mt19937 noise")
+    here = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    want = json.load(open(os.path.join(here, "mel_probe_fft_stats.json")))["signals"]
+    exe = tmp_path / "mel_probe_noise"
+    subprocess.run(["g++", "-O2", "-o", str(exe), os.path.join(here, "mel_probe_noise.cpp")], check=True)
+    samples, n_frames, bins, mels = 480000, 3000, 201, 80
+    noise = np.frombuffer(subprocess.run([str(exe)], check=True, capture_output=True).stdout, dtype=np.float32)
+    assert noise.size == samples
+    # The probe's filters: max(0, 1 - |b - (mel + 1) * 2.4f| / 3) in float.
+    b = np.arange(bins, dtype=np.float32)[None, :]
+    m = (np.arange(mels, dtype=np.float32)[:, None] + np.float32(1)) * np.float32(2.4)
+    fb = np.maximum(np.float32(0), np.float32(1) - np.abs(b - m) / np.float32(3)).astype(np.float32)
+    L = oracle.lib()
+    cfg = np.asarray([400, 160, mels, samples, n_frames, 64, 1, 1, 256, 4, 256], dtype=np.int32)
+    a = L.orc_audio_create(cfg.ctypes.data_as(C.POINTER(C.c_int32)), 1e-6)
+    assert a
+    try:
+        assert L.orc_audio_set_tensor(a, b"mel_filters", fb.ctypes.data) == 0
+        for kind, x in _probe_signals(noise, samples).items():
+            got = np.zeros((mels, n_frames), np.float32)
+            L.orc_audio_mel(a, x.ctypes.data_as(C.POINTER(C.c_float)), got.ctypes.data_as(C.POINTER(C.c_float)))
+            fft = _fft_mel(x, fb, n_frames)
+            err = fft.astype(np.float64) - got
+            rec = want[kind]
+            assert int((got.view(np.uint32) != fft.view(np.uint32)).sum()) == rec["floatBitDifferences"], kind
+            assert np.abs(err).max() == pytest.approx(rec["maxAbsError"], rel=1e-9, abs=0), kind
+            assert np.sqrt((err ** 2).mean()) == pytest.approx(rec["rmsError"], rel=1e-9, abs=0), kind
+    finally:
+        L.orc_audio_free(a)
