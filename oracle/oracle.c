@@ -1281,26 +1281,40 @@ static inline float gelu_erf(float v) { return (0.5f * v) * (1.0f + orc_erff(v *
 static void conv_gelu(const float* x, int L, int IC, long sp, long sc, int stride, const float* w, const float* b,
                       const float* pos, int OC, int OL, float* out, int ref) {
     const int J = IC * 3;
+    /* W transposed to [J][OC]: the chains of all output channels advance
+     * together in vector lanes, each still one fmaf chain over j ascending. */
+    float* wt = (float*)malloc(sizeof(float) * (size_t)J * (size_t)OC);
+#pragma omp parallel for schedule(static)
+    for (int j = 0; j < J; ++j)
+        for (int oc = 0; oc < OC; ++oc) wt[(size_t)j * OC + oc] = w[(size_t)oc * J + j];
 #pragma omp parallel for schedule(static)
     for (int t = 0; t < OL; ++t) {
         float* col = (float*)malloc(sizeof(float) * (size_t)J);
+        float* accs = (float*)malloc(sizeof(float) * (size_t)OC);
         for (int j = 0; j < J; ++j) {
             const int ic = j / 3, k = j % 3, p = t * stride + k - 1;
             col[j] = (p >= 0 && p < L) ? x[(long)p * sp + (long)ic * sc] : 0.f;
         }
+        if (!ref) {
+            for (int oc = 0; oc < OC; ++oc) accs[oc] = 0.f;
+            for (int j = 0; j < J; ++j) {
+                const float cj = col[j];
+                const float* wr = wt + (size_t)j * OC;
+                for (int oc = 0; oc < OC; ++oc) accs[oc] = fmaf(cj, wr[oc], accs[oc]);
+            }
+        }
         for (int oc = 0; oc < OC; ++oc) {
             const float* wr = w + (size_t)oc * J;
-            float acc = 0.f;
-            if (ref)
-                acc = ref_dot_f32(J, col, 1, wr, 1);
-            else
-                for (int j = 0; j < J; ++j) acc = fmaf(col[j], wr[j], acc);
+            float acc = accs[oc];
+            if (ref) acc = ref_dot_f32(J, col, 1, wr, 1);
             float g = ref ? (0.5f * (acc + b[oc])) * (1.0f + erff((acc + b[oc]) * 0.707106781f)) : gelu_erf(acc + b[oc]);
             if (pos) g = g + pos[(size_t)t * OC + oc];
             out[(size_t)t * OC + oc] = g;
         }
         free(col);
+        free(accs);
     }
+    free(wt);
 }
 
 static double lane_sum_d(double* v) {
@@ -1361,6 +1375,7 @@ static void linear_q8(const void* w, const float* b, int n, int k, const float* 
         ref_mul_mat_q8(w, n, k, x, T, tmp);
     else
         orc_mul_mat_q8(w, n, k, x, T, tmp);
+#pragma omp parallel for schedule(static)
     for (size_t i = 0; i < (size_t)T * (size_t)n; ++i) {
         const float v = tmp[i] + (b ? b[i % (size_t)n] : 0.0f);
         if (mode == LIN_GELU) y[i] = ref ? (0.5f * v) * (1.0f + erff(v * 0.707106781f)) : gelu_erf(v);
@@ -1371,8 +1386,12 @@ static void linear_q8(const void* w, const float* b, int n, int k, const float* 
     free(tmp);
 }
 
-/* One head of one query: q, k, v with row stride ld; out[64]. */
-static void enc_attn_row(const float* q, const float* k, const float* v, long ld, int T, int ref_order, float* out) {
+/* One head of one query: q, k, v with row stride ld; out[64].  kt: the head's
+ * keys transposed, [64][Tp] (Tp = T rounded up to 64, zero padded), for the
+ * kernels' order: the 64 score chains of a tile advance together in vector
+ * lanes, each one fmaf chain over the dims in order. */
+static void enc_attn_row(const float* q, const float* k, const float* kt, int Tp, const float* v, long ld, int T,
+                         int ref_order, float* out) {
     const float scale = 0.125f;
     if (ref_order) {
         float* p = (float*)malloc(sizeof(float) * (size_t)T);
@@ -1394,18 +1413,18 @@ static void enc_attn_row(const float* q, const float* k, const float* v, long ld
     }
     float m = -1e30f, l = 0.f, o[64];
     for (int i = 0; i < 64; ++i) o[i] = 0.f;
+    static const float zeros[64];
     for (int k0 = 0; k0 < T; k0 += 64) {
-        float s[64], p[64];
+        float s[64], p[64], acc[64];
         float tmax = -1e30f;
+        for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+        for (int i = 0; i < 64; ++i) {
+            const float qi = q[i];
+            const float* kr = kt + (size_t)i * Tp + k0;
+            for (int c = 0; c < 64; ++c) acc[c] = fmaf(qi, kr[c], acc[c]);
+        }
         for (int c = 0; c < 64; ++c) {
-            const int j = k0 + c;
-            if (j < T) {
-                float acc = 0.f;
-                for (int i = 0; i < 64; ++i) acc = fmaf(q[i], k[(long)j * ld + i], acc);
-                s[c] = acc * scale;
-            } else {
-                s[c] = -1e30f;
-            }
+            s[c] = k0 + c < T ? acc[c] * scale : -1e30f;
             tmax = s[c] > tmax ? s[c] : tmax;
         }
         const float mn = m > tmax ? m : tmax;
@@ -1428,13 +1447,11 @@ static void enc_attn_row(const float* q, const float* k, const float* v, long ld
             memcpy(part, np_, sizeof(np_));
         }
         l = l * alpha + part[0];
-        for (int i = 0; i < 64; ++i) {
-            float acc = o[i] * alpha;
-            for (int c = 0; c < 64; ++c) {
-                const int j = k0 + c;
-                acc = fmaf(p[c], j < T ? v[(long)j * ld + i] : 0.f, acc);
-            }
-            o[i] = acc;
+        for (int i = 0; i < 64; ++i) o[i] = o[i] * alpha;
+        for (int c = 0; c < 64; ++c) {
+            const float pc = p[c];
+            const float* vr = k0 + c < T ? v + (long)(k0 + c) * ld : zeros;
+            for (int i = 0; i < 64; ++i) o[i] = fmaf(pc, vr[i], o[i]);
         }
     }
     const float inv = 1.0f / l;
@@ -1453,6 +1470,8 @@ int orc_audio_encoder(const orc_audio* a, const float* mel, float* out) {
     float* v = (float*)malloc(sizeof(float) * (size_t)T * d);
     float* att = (float*)malloc(sizeof(float) * (size_t)T * d);
     float* f = (float*)malloc(sizeof(float) * (size_t)T * a->ffn);
+    const int Tp = (T + 63) / 64 * 64;
+    float* kt = (float*)malloc(sizeof(float) * (size_t)d * Tp);
     const int ref = a->ref_order;
     conv_gelu(mel, a->n_frames, a->n_mels, 1, a->n_frames, 1, a->conv1_w, a->conv1_b, NULL, d, a->n_frames, c1, ref);
     conv_gelu(c1, a->n_frames, d, d, 1, 2, a->conv2_w, a->conv2_b, a->pos, d, T, h, ref);
@@ -1462,11 +1481,16 @@ int orc_audio_encoder(const orc_audio* a, const float* mel, float* out) {
         linear_q8(L->q_w, L->q_b, d, d, nrm, T, q, LIN_BIAS, ref);
         linear_q8(L->k_w, NULL, d, d, nrm, T, k, LIN_BIAS, ref);
         linear_q8(L->v_w, L->v_b, d, d, nrm, T, v, LIN_BIAS, ref);
+#pragma omp parallel for schedule(static)
+        for (int hh = 0; hh < H; ++hh)
+            for (int i = 0; i < 64; ++i)
+                for (int j = 0; j < Tp; ++j)
+                    kt[((size_t)hh * 64 + i) * Tp + j] = j < T ? k[(size_t)j * d + hh * 64 + i] : 0.f;
 #pragma omp parallel for schedule(dynamic, 16)
         for (int idx = 0; idx < H * T; ++idx) {
             const int hh = idx / T, t = idx % T;
-            enc_attn_row(q + (size_t)t * d + hh * 64, k + hh * 64, v + hh * 64, d, T, a->ref_order,
-                         att + (size_t)t * d + hh * 64);
+            enc_attn_row(q + (size_t)t * d + hh * 64, k + hh * 64, kt + (size_t)hh * 64 * Tp, Tp, v + hh * 64, d, T,
+                         a->ref_order, att + (size_t)t * d + hh * 64);
         }
         linear_q8(L->o_w, L->o_b, d, d, att, T, h, LIN_RESID, ref);
         layer_norm_rows(h, T, d, L->ffn_ln_w, L->ffn_ln_b, 1e-5f, nrm, ref);
@@ -1474,7 +1498,7 @@ int orc_audio_encoder(const orc_audio* a, const float* mel, float* out) {
         linear_q8(L->fc2_w, L->fc2_b, d, a->ffn, f, T, h, LIN_RESID, ref);
     }
     layer_norm_rows(h, T, d, a->ln_post_w, a->ln_post_b, 1e-5f, out, ref);
-    free(c1), free(h), free(nrm), free(q), free(k), free(v), free(att), free(f);
+    free(c1), free(h), free(nrm), free(q), free(k), free(v), free(att), free(f), free(kt);
     return 0;
 }
 
