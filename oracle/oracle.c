@@ -58,7 +58,7 @@ static inline float bits_f32(uint32_t u) {
     return f;
 }
 
-float orc_expf(float x) {
+static inline float exp_own(float x) {
     /* x is clamped for the arithmetic and the special cases are selected at
      * the end; 2^n is applied as (p * 2^a) * 2^b with (a, b) = (n, 0),
      * (1, 127) for n = 128, (n + 64, -64) for n < -126. */
@@ -83,6 +83,8 @@ float orc_expf(float x) {
     if (x < -103.972084f) return 0.0f;      /* e^x below half the smallest subnormal */
     return y;
 }
+
+float orc_expf(float x) { return exp_own(x); }
 
 void orc_sincosf(float x, float* s_out, float* c_out) {
     const double xd = (double)x;
@@ -242,6 +244,42 @@ static inline int block_isum(const int8_t* w, const int8_t* x) {
 }
 #endif
 
+#if defined(__AVX512VNNI__) && defined(__AVX512VL__)
+#define ORC_HAVE_DOT_X8 1
+/* dot_q8 of one weight row with 8 activation rows at once (lane t = row t, the
+ * rows x_stride blocks apart): per block the 8 exact integer sums (u8 x s8
+ * dots of |w| and sign(w) * x, then a horizontal-add tree), and lane by lane
+ * the same fmaf(isum, d_w * d_x, acc) per block and slice sums as dot_q8, so
+ * every lane equals dot_q8's result bit for bit (the native build only). */
+static inline void dot_q8_x8(const blk_q8* w, const blk_q8* x, size_t x_stride, int nb, float* out) {
+    __m256 total = _mm256_setzero_ps();
+    for (int s0 = 0; s0 < nb; s0 += 8) {
+        __m256 acc = _mm256_setzero_ps();
+        for (int b = s0; b < s0 + 8 && b < nb; ++b) {
+            const __m256i wv = _mm256_loadu_si256((const __m256i*)w[b].qs);
+            const __m256i wabs = _mm256_sign_epi8(wv, wv);
+            __m256i p[8];
+            float dx[8];
+            for (int t = 0; t < 8; ++t) {
+                const blk_q8* xb = x + (size_t)t * x_stride + b;
+                const __m256i xv = _mm256_loadu_si256((const __m256i*)xb->qs);
+                p[t] = _mm256_dpbusd_epi32(_mm256_setzero_si256(), wabs, _mm256_sign_epi8(xv, wv));
+                dx[t] = h2f(xb->d);
+            }
+            const __m256i s01 = _mm256_hadd_epi32(p[0], p[1]), s23 = _mm256_hadd_epi32(p[2], p[3]);
+            const __m256i s45 = _mm256_hadd_epi32(p[4], p[5]), s67 = _mm256_hadd_epi32(p[6], p[7]);
+            const __m256i q0 = _mm256_hadd_epi32(s01, s23), q1 = _mm256_hadd_epi32(s45, s67);
+            const __m256i isum = _mm256_add_epi32(_mm256_permute2x128_si256(q0, q1, 0x20),
+                                                  _mm256_permute2x128_si256(q0, q1, 0x31));
+            const __m256 d = _mm256_mul_ps(_mm256_set1_ps(h2f(w[b].d)), _mm256_loadu_ps(dx));
+            acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(isum), d, acc);
+        }
+        total = _mm256_add_ps(total, acc);
+    }
+    _mm256_storeu_ps(out, total);
+}
+#endif
+
 static inline float dot_q8(const blk_q8* w, const blk_q8* x, int nb) {
     float total = 0.0f;
     for (int s0 = 0; s0 < nb; s0 += 8) {
@@ -264,7 +302,15 @@ void orc_mul_mat_q8(const void* w_blocks, int n_rows, int k, const float* x, int
 #pragma omp parallel for schedule(static)
     for (int n = 0; n < n_rows; ++n) {
         const blk_q8* row = w + (size_t)n * nb;
-        for (int t = 0; t < T; ++t) y[(size_t)t * n_rows + n] = dot_q8(row, xq + (size_t)t * nb, nb);
+        int t = 0;
+#ifdef ORC_HAVE_DOT_X8
+        for (; t + 8 <= T; t += 8) {
+            float o8[8];
+            dot_q8_x8(row, xq + (size_t)t * nb, (size_t)nb, nb, o8);
+            for (int u = 0; u < 8; ++u) y[(size_t)(t + u) * n_rows + n] = o8[u];
+        }
+#endif
+        for (; t < T; ++t) y[(size_t)t * n_rows + n] = dot_q8(row, xq + (size_t)t * nb, nb);
     }
     free(xq);
 }
@@ -537,7 +583,7 @@ static void rope_neox(float* x, int n_dims, int pos, float base) {
     }
 }
 
-static inline float silu(float x) { return x / (1.0f + orc_expf(-x)); }
+static inline float silu(float x) { return x / (1.0f + exp_own(-x)); }
 
 /* One query row's attention in this oracle's (and the CUDA kernels') order:
  * positions j < valid of K and V at kbase + j * stride / vbase + j * stride.
@@ -547,7 +593,7 @@ static inline float silu(float x) { return x / (1.0f + orc_expf(-x)); }
  * context dim one fmaf chain o_c); the chunks merged with weights exp(m_c - M)
  * in chunk order, o = sum w_c o_c / sum w_c l_c. */
 static void attn_row_chunked(const float* qh, const float* kbase, const float* vbase, size_t stride, int valid, int hd,
-                             float scale, float* oh) {
+                             float scale, float* oh, const float* kT, size_t kt_stride) {
     /* The loops run position-inner / dim-inner so that the compiler can keep
      * many independent chains in vector lanes; every chain is still the same
      * sequence of fmaf operations as described above. */
@@ -561,23 +607,28 @@ static void attn_row_chunked(const float* qh, const float* kbase, const float* v
     for (int c = 0; c < n_chunks; ++c) {
         const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
         float sc[64], e[64], ae[64], ao[64];
-        for (int p = 0; p < n_pos; ++p) {
-            const float* kj = kbase + (size_t)(c * 64 + p) * stride;
-            for (int e2 = 0; e2 < hd; ++e2) kt[e2][p] = kj[e2];
-        }
-        for (int p = 0; p < 64; ++p) ae[p] = ao[p] = 0.0f;
-        for (int e2 = 0; e2 < hd; e2 += 2)
+        if (!kT)
             for (int p = 0; p < n_pos; ++p) {
-                ae[p] = fmaf(qh[e2], kt[e2][p], ae[p]);
-                ao[p] = fmaf(qh[e2 + 1], kt[e2 + 1][p], ao[p]);
+                const float* kj = kbase + (size_t)(c * 64 + p) * stride;
+                for (int e2 = 0; e2 < hd; ++e2) kt[e2][p] = kj[e2];
             }
+        for (int p = 0; p < 64; ++p) ae[p] = ao[p] = 0.0f;
+        for (int e2 = 0; e2 < hd; e2 += 2) {
+            /* K of this chunk by dim: the caller's transposed copy, or the local one. */
+            const float* k0 = kT ? kT + (size_t)e2 * kt_stride + (size_t)c * 64 : kt[e2];
+            const float* k1 = kT ? kT + (size_t)(e2 + 1) * kt_stride + (size_t)c * 64 : kt[e2 + 1];
+            for (int p = 0; p < n_pos; ++p) {
+                ae[p] = fmaf(qh[e2], k0[p], ae[p]);
+                ao[p] = fmaf(qh[e2 + 1], k1[p], ao[p]);
+            }
+        }
         float mx = -INFINITY;
         for (int p = 0; p < 64; ++p) {
             sc[p] = p < n_pos ? (ae[p] + ao[p]) * scale : -INFINITY;
             mx = fmaxf(mx, sc[p]);
         }
         float pair[32];
-        for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : orc_expf(sc[p] - mx);
+        for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : exp_own(sc[p] - mx);
         for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
         cm[c] = mx;
         cl[c] = warp_tree_sum(pair);
@@ -594,7 +645,7 @@ static void attn_row_chunked(const float* qh, const float* kbase, const float* v
     float Ls = 0.0f;
     for (int e2 = 0; e2 < hd; ++e2) oh[e2] = 0.0f;
     for (int c = 0; c < n_chunks; ++c) {
-        const float wgt = orc_expf(cm[c] - M);
+        const float wgt = exp_own(cm[c] - M);
         Ls = fmaf(wgt, cl[c], Ls);
         const float* oc = co + (size_t)c * hd;
         for (int e2 = 0; e2 < hd; ++e2) oh[e2] = fmaf(wgt, oc[e2], oh[e2]);
@@ -618,6 +669,8 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     float* proj = (float*)malloc(sizeof(float) * (size_t)T * H);
     float* g = (float*)malloc(sizeof(float) * (size_t)T * F);
     float* u = (float*)malloc(sizeof(float) * (size_t)T * F);
+    const int kvp = (kv + 63) / 64 * 64;
+    float* kT = (float*)malloc(sizeof(float) * (size_t)kd * kvp);
     memcpy(x, embeds, sizeof(float) * (size_t)T * H);
     const float scale = 1.0f / sqrtf((float)hd);
 
@@ -655,13 +708,22 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
          * and context o_c) and the chunks are merged with weights
          * exp(m_c - M); the same function as one softmax over the row, in the
          * evaluation order shared with the CUDA kernels. */
+        /* K transposed once per layer and KV head ([kv head][dim][position]),
+         * shared by every row and query head of the group. */
+        const float* kl = d->k + kv_index(d, l, 0);
+#pragma omp parallel for collapse(2) schedule(static)
+        for (int h = 0; h < nkv; ++h)
+            for (int e2 = 0; e2 < hd; ++e2) {
+                float* dst = kT + ((size_t)h * hd + e2) * kvp;
+                for (int p = 0; p < kv; ++p) dst[p] = kl[(size_t)p * kd + (size_t)h * hd + e2];
+            }
 #pragma omp parallel for collapse(2) schedule(static)
         for (int t = 0; t < T; ++t) {
             for (int h = 0; h < nh; ++h) {
                 const int kvh = h / group;
                 attn_row_chunked(q + (size_t)t * qd + (size_t)h * hd, d->k + kv_index(d, l, 0) + (size_t)kvh * hd,
                                  d->v + kv_index(d, l, 0) + (size_t)kvh * hd, (size_t)nkv * hd, past + t + 1, hd, scale,
-                                 o + (size_t)t * qd + (size_t)h * hd);
+                                 o + (size_t)t * qd + (size_t)h * hd, kT + (size_t)kvh * hd * kvp, kvp);
             }
         }
         mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
@@ -675,7 +737,7 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     }
     for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 0);
     d->past = kv;
-    free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u);
+    free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u); free(kT);
     return 0;
 }
 
@@ -1007,7 +1069,7 @@ void orc_attention_row(int ref_order, const float* q, const float* k, const floa
     if (ref_order)
         attn_row_ref(q, k, v, (size_t)hd, valid, hd, scale, out);
     else
-        attn_row_chunked(q, k, v, (size_t)hd, valid, hd, scale, out);
+        attn_row_chunked(q, k, v, (size_t)hd, valid, hd, scale, out, NULL, 0);
 }
 
 float orc_dot_q8_blocks(int ref_order, const void* w, const void* x, int nb) {
@@ -1379,7 +1441,7 @@ static void linear_q8(const void* w, const float* b, int n, int k, const float* 
     for (size_t i = 0; i < (size_t)T * (size_t)n; ++i) {
         const float v = tmp[i] + (b ? b[i % (size_t)n] : 0.0f);
         if (mode == LIN_GELU) y[i] = ref ? (0.5f * v) * (1.0f + erff(v * 0.707106781f)) : gelu_erf(v);
-        else if (mode == LIN_SILU) y[i] = v / (1.0f + (ref ? expf(-v) : orc_expf(-v)));
+        else if (mode == LIN_SILU) y[i] = v / (1.0f + (ref ? expf(-v) : exp_own(-v)));
         else if (mode == LIN_RESID) y[i] = y[i] + v;
         else y[i] = v;
     }
@@ -1428,7 +1490,7 @@ static void enc_attn_row(const float* q, const float* k, const float* kt, int Tp
             tmax = s[c] > tmax ? s[c] : tmax;
         }
         const float mn = m > tmax ? m : tmax;
-        const float alpha = orc_expf(m - mn);
+        const float alpha = exp_own(m - mn);
         m = mn;
         /* 16 lanes x 4 keys: lane partials from 0 in key order, then the butterfly. */
         float part[16];
@@ -1436,7 +1498,7 @@ static void enc_attn_row(const float* q, const float* k, const float* kt, int Tp
             float ps = 0.f;
             for (int c = 0; c < 4; ++c) {
                 const int kc = 4 * ln + c;
-                p[kc] = k0 + kc < T ? orc_expf(s[kc] - mn) : 0.f;
+                p[kc] = k0 + kc < T ? exp_own(s[kc] - mn) : 0.f;
                 ps = ps + p[kc];
             }
             part[ln] = ps;
