@@ -592,6 +592,56 @@ static inline float silu(float x) { return x / (1.0f + exp_own(-x)); }
  * the pair sums e[p] + e[p + 32] then a 32-value xor butterfly for l_c, each
  * context dim one fmaf chain o_c); the chunks merged with weights exp(m_c - M)
  * in chunk order, o = sum w_c o_c / sum w_c l_c. */
+/* One 64-position chunk c of one attention row, from K transposed [dim][kt_stride]
+ * and V rows `stride` apart: the chunk maximum, the chunk sum (pair sums, then
+ * the 32-lane tree) and the unnormalised context, exactly as attn_row_chunked
+ * computes them for that chunk. */
+static void attn_chunk_stats(const float* restrict qh, const float* restrict kT, size_t kt_stride,
+                             const float* restrict vbase, size_t stride, int valid, int hd, float scale, int c,
+                             float* restrict cm, float* restrict cl, float* restrict oc) {
+    const int n_pos = valid - c * 64 < 64 ? valid - c * 64 : 64;
+    float sc[64], e[64], ae[64], ao[64], pair[32];
+    for (int p = 0; p < 64; ++p) ae[p] = ao[p] = 0.0f;
+    for (int e2 = 0; e2 < hd; e2 += 2) {
+        const float* k0 = kT + (size_t)e2 * kt_stride + (size_t)c * 64;
+        const float* k1 = kT + (size_t)(e2 + 1) * kt_stride + (size_t)c * 64;
+        for (int p = 0; p < n_pos; ++p) {
+            ae[p] = fmaf(qh[e2], k0[p], ae[p]);
+            ao[p] = fmaf(qh[e2 + 1], k1[p], ao[p]);
+        }
+    }
+    float mx = -INFINITY;
+    for (int p = 0; p < 64; ++p) {
+        sc[p] = p < n_pos ? (ae[p] + ao[p]) * scale : -INFINITY;
+        mx = fmaxf(mx, sc[p]);
+    }
+    for (int p = 0; p < 64; ++p) e[p] = sc[p] == -INFINITY ? 0.0f : exp_own(sc[p] - mx);
+    for (int p = 0; p < 32; ++p) pair[p] = e[p] + e[p + 32];
+    *cm = mx;
+    *cl = warp_tree_sum(pair);
+    for (int e2 = 0; e2 < hd; ++e2) oc[e2] = 0.0f;
+    for (int p = 0; p < n_pos; ++p) {
+        const float* vp = vbase + (size_t)(c * 64 + p) * stride;
+        const float ep = e[p];
+        for (int e2 = 0; e2 < hd; ++e2) oc[e2] = fmaf(ep, vp[e2], oc[e2]);
+    }
+}
+
+/* The merge of attn_row_chunked: weights exp(m_c - M) in chunk order. */
+static void attn_merge_chunks(const float* cm, const float* cl, const float* co, int n_chunks, int hd, float* oh) {
+    float M = -INFINITY;
+    for (int c = 0; c < n_chunks; ++c) M = fmaxf(M, cm[c]);
+    float Ls = 0.0f;
+    for (int e2 = 0; e2 < hd; ++e2) oh[e2] = 0.0f;
+    for (int c = 0; c < n_chunks; ++c) {
+        const float wgt = exp_own(cm[c] - M);
+        Ls = fmaf(wgt, cl[c], Ls);
+        const float* oc = co + (size_t)c * hd;
+        for (int e2 = 0; e2 < hd; ++e2) oh[e2] = fmaf(wgt, oc[e2], oh[e2]);
+    }
+    for (int e2 = 0; e2 < hd; ++e2) oh[e2] = oh[e2] / Ls;
+}
+
 static void attn_row_chunked(const float* qh, const float* kbase, const float* vbase, size_t stride, int valid, int hd,
                              float scale, float* oh, const float* kT, size_t kt_stride) {
     /* The loops run position-inner / dim-inner so that the compiler can keep
@@ -671,6 +721,10 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     float* u = (float*)malloc(sizeof(float) * (size_t)T * F);
     const int kvp = (kv + 63) / 64 * 64;
     float* kT = (float*)malloc(sizeof(float) * (size_t)kd * kvp);
+    const int max_chunks = kvp / 64;
+    float* a_cm = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks);
+    float* a_cl = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks);
+    float* a_co = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks * hd);
     memcpy(x, embeds, sizeof(float) * (size_t)T * H);
     const float scale = 1.0f / sqrtf((float)hd);
 
@@ -713,19 +767,39 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         const float* kl = d->k + kv_index(d, l, 0);
 #pragma omp parallel for collapse(2) schedule(static)
         for (int h = 0; h < nkv; ++h)
-            for (int e2 = 0; e2 < hd; ++e2) {
-                float* dst = kT + ((size_t)h * hd + e2) * kvp;
-                for (int p = 0; p < kv; ++p) dst[p] = kl[(size_t)p * kd + (size_t)h * hd + e2];
+            for (int p0 = 0; p0 < kv; p0 += 64) {  /* 64 positions x hd dims at a time (cache-resident) */
+                const int p1 = p0 + 64 < kv ? p0 + 64 : kv;
+                for (int e2 = 0; e2 < hd; ++e2) {
+                    float* dst = kT + ((size_t)h * hd + e2) * kvp;
+                    for (int p = p0; p < p1; ++p) dst[p] = kl[(size_t)p * kd + (size_t)h * hd + e2];
+                }
             }
+        /* The chunk statistics of every row and head, one (KV head, chunk) per
+         * work item: its K and V rows are read once for all rows and query heads
+         * of the group.  Then each row's chunks are merged in order.  The same
+         * operations as attn_row_chunked, row by row. */
+        const float* vl = d->v + kv_index(d, l, 0);
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+        for (int kvh = 0; kvh < nkv; ++kvh)
+            for (int c = 0; c < max_chunks; ++c)
+                for (int t = 0; t < T; ++t) {
+                    const int valid = past + t + 1;
+                    if (c * 64 >= valid) continue;
+                    for (int h = kvh * group; h < (kvh + 1) * group; ++h) {
+                        const size_t it = (size_t)t * nh + h;
+                        attn_chunk_stats(q + (size_t)t * qd + (size_t)h * hd, kT + (size_t)kvh * hd * kvp, kvp,
+                                         vl + (size_t)kvh * hd, (size_t)kd, valid, hd, scale, c,
+                                         a_cm + it * max_chunks + c, a_cl + it * max_chunks + c,
+                                         a_co + (it * max_chunks + c) * hd);
+                    }
+                }
 #pragma omp parallel for collapse(2) schedule(static)
-        for (int t = 0; t < T; ++t) {
+        for (int t = 0; t < T; ++t)
             for (int h = 0; h < nh; ++h) {
-                const int kvh = h / group;
-                attn_row_chunked(q + (size_t)t * qd + (size_t)h * hd, d->k + kv_index(d, l, 0) + (size_t)kvh * hd,
-                                 d->v + kv_index(d, l, 0) + (size_t)kvh * hd, (size_t)nkv * hd, past + t + 1, hd, scale,
-                                 o + (size_t)t * qd + (size_t)h * hd, kT + (size_t)kvh * hd * kvp, kvp);
+                const size_t it = (size_t)t * nh + h;
+                attn_merge_chunks(a_cm + it * max_chunks, a_cl + it * max_chunks, a_co + it * max_chunks * hd,
+                                  (past + t + 1 + 63) / 64, hd, o + (size_t)t * qd + (size_t)h * hd);
             }
-        }
         mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
         for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 0);
@@ -738,6 +812,7 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, m->output_norm, H, m->eps, out_hidden + (size_t)t * H, 0);
     d->past = kv;
     free(x); free(xn); free(q); free(k); free(v); free(o); free(proj); free(g); free(u); free(kT);
+    free(a_cm); free(a_cl); free(a_co);
     return 0;
 }
 
