@@ -9,12 +9,13 @@
  *   - errors are reported through moss_transcribe_capi_last_error;
  *   - no C++ exception crosses the boundary.
  *
- * This library holds the decoder hot path only (strict speculative decoding on
- * a B200).  The audio front end the transcribe entries need (WAV decoding, log
- * mel, Whisper encoder, adaptor, tokenizer) is not part of it: the transcribe
- * entries return NULL with a last-error that says so, and callers that own a
- * front end hand fused prompt embeddings to mtb_spec_generate
- * (include/mtb_decoder.h) instead.
+ * This library holds the decoder hot path (strict speculative decoding on a
+ * B200) and the audio front end before it (log mel, Whisper encoder, adaptor:
+ * mtb_audio_encode in include/mtb_decoder.h).  WAV decoding and the tokenizer
+ * (prompt ids, transcript text) are not part of it, so the transcribe entries
+ * return NULL with a last-error that says so; callers that own a tokenizer
+ * encode the audio with mtb_audio_encode and decode prompt ids + audio rows
+ * with mtb_spec_generate_ids (or fused rows with mtb_spec_generate).
  */
 #ifndef MOSS_TRANSCRIBE_CAPI_H
 #define MOSS_TRANSCRIBE_CAPI_H

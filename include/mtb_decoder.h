@@ -79,8 +79,9 @@ typedef void (*mtb_commit_fn)(void* user, const int32_t* ids, int n_ids, int pas
 
 int mtb_abi_version(void);
 /* Whether moss_transcribe_capi_transcribe_pcm / _path can return a
- * transcript from this build: 0 (the audio front end is not part of it; those
- * calls return NULL with an error).  No counterpart in the reference. */
+ * transcript from this build: 0 (WAV decoding and the tokenizer are not part
+ * of it; those calls return NULL with an error).  No counterpart in the
+ * reference. */
 int mtb_capi_can_transcribe(void);
 /* The generate entries (mtb_spec_generate, mtb_spec_generate_ids,
  * mtb_greedy_generate) end by printing the reference's lines

@@ -17,8 +17,9 @@ struct moss_transcribe_ctx {
 
 namespace {
 const char kNoFrontEnd[] =
-    "the audio front end (WAV decoding, log-mel, Whisper encoder, adaptor, tokenizer) is not part of "
-    "libmoss_transcribe_b200: pass fused prompt embeddings to mtb_spec_generate";
+    "a transcript needs WAV decoding and the tokenizer (prompt ids, transcript text), which are not part of "
+    "libmoss_transcribe_b200: run the audio front end with mtb_audio_encode and decode prompt ids + audio rows "
+    "with mtb_spec_generate_ids";
 }
 
 extern "C" int moss_transcribe_capi_abi_version(void) { return 1; }

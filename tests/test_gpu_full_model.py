@@ -130,7 +130,8 @@ def test_config4_long_context_step_bit_exact(full_oracle, full_gpu):
 def test_reference_capi_loads_and_frees_the_full_model(full_path):
     """moss_transcribe_capi_load on the Qwen3-0.6B GGUF (the reference's own
     entry, include/moss_transcribe_capi.h); transcribe returns NULL with the
-    documented error in this build (no audio front end), as
+    documented error in this build (no tokenizer; the audio front end and the
+    decoder are the mtb_audio_* / mtb_spec_generate_ids entries), as
     mtb_capi_can_transcribe reports."""
     import ctypes as C
     L = capi.lib()
@@ -139,5 +140,6 @@ def test_reference_capi_loads_and_frees_the_full_model(full_path):
     assert L.mtb_capi_can_transcribe() == 0
     samples = (C.c_float * 16000)()
     assert L.moss_transcribe_capi_transcribe_pcm(ctx, samples, 16000, 16000, 0) is None
-    assert b"audio front end" in L.moss_transcribe_capi_last_error(ctx)
+    err = L.moss_transcribe_capi_last_error(ctx)
+    assert b"tokenizer" in err and b"mtb_audio_encode" in err, err
     L.moss_transcribe_capi_free(ctx)
