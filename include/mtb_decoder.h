@@ -29,6 +29,8 @@
  *                                        (one launch per step; no reference counterpart:
  *                                        the reference decodes one recording at a time)
  *   mtb_snapshot_save / _restore         (src/cpu_speculative.cpp:100-137)
+ *   mtb_audio_load / _encode / _free     AudioEncoder (src/audio_encoder.cpp:16-75): WhisperMel,
+ *                                        WhisperEncoder, AudioAdaptor on the device
  *
  * Conventions: every function returns 0 on success or a negative code and
  * sets a per-object error string; no C++ exception crosses the boundary.  One
