@@ -722,9 +722,15 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
     const int kvp = (kv + 63) / 64 * 64;
     float* kT = (float*)malloc(sizeof(float) * (size_t)kd * kvp);
     const int max_chunks = kvp / 64;
-    float* a_cm = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks);
-    float* a_cl = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks);
-    float* a_co = (float*)malloc(sizeof(float) * (size_t)T * nh * max_chunks * hd);
+    const size_t row_stats = (size_t)nh * max_chunks * (hd + 2) * sizeof(float);
+#ifndef ORC_ATTN_STATS_BYTES
+#define ORC_ATTN_STATS_BYTES ((size_t)256 * 1024 * 1024)
+#endif
+    int tb = (int)(ORC_ATTN_STATS_BYTES / row_stats);
+    tb = tb < 1 ? 1 : (tb > T ? T : tb);
+    float* a_cm = (float*)malloc(sizeof(float) * (size_t)tb * nh * max_chunks);
+    float* a_cl = (float*)malloc(sizeof(float) * (size_t)tb * nh * max_chunks);
+    float* a_co = (float*)malloc(sizeof(float) * (size_t)tb * nh * max_chunks * hd);
     memcpy(x, embeds, sizeof(float) * (size_t)T * H);
     const float scale = 1.0f / sqrtf((float)hd);
 
@@ -777,29 +783,34 @@ int orc_decoder_run(orc_decoder* d, const float* embeds, int T, float* out_hidde
         /* The chunk statistics of every row and head, one (KV head, chunk) per
          * work item: its K and V rows are read once for all rows and query heads
          * of the group.  Then each row's chunks are merged in order.  The same
-         * operations as attn_row_chunked, row by row. */
+         * operations as attn_row_chunked, row by row.  Rows go in blocks of tb
+         * (the statistics of a block stay below ~256 MB for long prompts). */
         const float* vl = d->v + kv_index(d, l, 0);
+        for (int t0 = 0; t0 < T; t0 += tb) {
+            const int t1 = t0 + tb < T ? t0 + tb : T;
+            const int n_chunks_blk = (past + t1 + 63) / 64;
 #pragma omp parallel for collapse(2) schedule(dynamic, 1)
-        for (int kvh = 0; kvh < nkv; ++kvh)
-            for (int c = 0; c < max_chunks; ++c)
-                for (int t = 0; t < T; ++t) {
-                    const int valid = past + t + 1;
-                    if (c * 64 >= valid) continue;
-                    for (int h = kvh * group; h < (kvh + 1) * group; ++h) {
-                        const size_t it = (size_t)t * nh + h;
-                        attn_chunk_stats(q + (size_t)t * qd + (size_t)h * hd, kT + (size_t)kvh * hd * kvp, kvp,
-                                         vl + (size_t)kvh * hd, (size_t)kd, valid, hd, scale, c,
-                                         a_cm + it * max_chunks + c, a_cl + it * max_chunks + c,
-                                         a_co + (it * max_chunks + c) * hd);
+            for (int kvh = 0; kvh < nkv; ++kvh)
+                for (int c = 0; c < n_chunks_blk; ++c)
+                    for (int t = t0; t < t1; ++t) {
+                        const int valid = past + t + 1;
+                        if (c * 64 >= valid) continue;
+                        for (int h = kvh * group; h < (kvh + 1) * group; ++h) {
+                            const size_t it = (size_t)(t - t0) * nh + h;
+                            attn_chunk_stats(q + (size_t)t * qd + (size_t)h * hd, kT + (size_t)kvh * hd * kvp, kvp,
+                                             vl + (size_t)kvh * hd, (size_t)kd, valid, hd, scale, c,
+                                             a_cm + it * max_chunks + c, a_cl + it * max_chunks + c,
+                                             a_co + (it * max_chunks + c) * hd);
+                        }
                     }
-                }
 #pragma omp parallel for collapse(2) schedule(static)
-        for (int t = 0; t < T; ++t)
-            for (int h = 0; h < nh; ++h) {
-                const size_t it = (size_t)t * nh + h;
-                attn_merge_chunks(a_cm + it * max_chunks, a_cl + it * max_chunks, a_co + it * max_chunks * hd,
-                                  (past + t + 1 + 63) / 64, hd, o + (size_t)t * qd + (size_t)h * hd);
-            }
+            for (int t = t0; t < t1; ++t)
+                for (int h = 0; h < nh; ++h) {
+                    const size_t it = (size_t)(t - t0) * nh + h;
+                    attn_merge_chunks(a_cm + it * max_chunks, a_cl + it * max_chunks, a_co + it * max_chunks * hd,
+                                      (past + t + 1 + 63) / 64, hd, o + (size_t)t * qd + (size_t)h * hd);
+                }
+        }
         mul_mat_w(d->m, L->wo, H, qd, o, T, proj);
         for (size_t i = 0; i < (size_t)T * H; ++i) x[i] = x[i] + proj[i];
         for (int t = 0; t < T; ++t) rms_norm_mul(x + (size_t)t * H, L->ffn_norm, H, m->eps, xn + (size_t)t * H, 0);
